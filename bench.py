@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 routed-MoE layer (driver contract: one JSON line on rank 0).
+
+Workload (default): decode B=1 through a stack of 40
+Ornith MoE layers (256 routed experts + 1 shared, H2048/I512, affine-u4 G256
+weights, A8 activations), fresh seeded weights per layer (16.6 GB resident),
+router logits ~N(0,1) per layer and step.  One step = one token through the
+40 layers, each layer's output feeding the next, every layer called through
+`ornith_b200::routed_from_logits` (routing, routed experts, shared expert,
+combine).  Other workloads: --config decode32 (configs[2], logits + per-expert
+bias N(0,0.5)), prefill1120 / prefill8192 (configs[3], A4, 40 weight sets
+cycled so that weights never stay in L2).
+
+Timing: W warm-up steps, then K steps between CUDA events on the launching
+stream, barrier + synchronize on both sides, max over ranks.  Every step reads
+(distinct experts + 1) x 1.62 MB per layer, far more than the 126 MB L2, so no
+explicit flush is needed (config.l2 says so).  `e2e` repeats the measurement
+through the same public operator with host (pinned) inputs copied in and the
+final output copied out inside the timed region.
+
+--impl reference times the reference's own routed source compiled for the CPU
+(oracle/_ref, built by oracle/build_ref.py) on this host's cores on a bounded
+sample of the same workload; rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+import __graft_entry__ as graft  # noqa: E402
+
+METRIC = 'MoE-layer tokens/s & % of HBM/tensor roofline (decode B=1/32, 8K prefill)'
+EXPERT_BYTES = 1_622_016          # w13 codes 1,048,576 + meta 32,768 + w2 codes 524,288 + meta 16,384
+CONFIGS = {
+    'decode1': dict(T=1, layers=40, bias=0.0, act_bits=8, shared=True, name='decode B=1, 40-layer stack (configs[1])'),
+    'decode32': dict(T=32, layers=40, bias=0.5, act_bits=8, shared=True, name='decode B=32, 40-layer stack (configs[2])'),
+    'prefill1120': dict(T=1120, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 1120 (configs[3])'),
+    'prefill8192': dict(T=8192, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 8192 (configs[3])'),
+}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=20)
+    p.add_argument('--warmup', type=int, default=5)
+    p.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    p.add_argument('--config', default='decode1', choices=sorted(CONFIGS))
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--cpu-seconds', type=float, default=12.0)
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.QUERY}', '--format=csv,noheader,nounits',
+                                          '-i', str(self.index), '-lms', '100'], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=10)
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.lines:
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(n)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': mx, 'reasons': [], 'samples': 0}
+        loaded = sorted(sm)[len(sm) // 4:] or sm
+        return {'sm_mhz': statistics.median(loaded), 'sm_max_mhz': mx, 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# device workload
+# ---------------------------------------------------------------------------
+def device_bank(torch, gen, dev, experts, N, K):
+    codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (experts, N // 32, K // 256, 32, 32), dtype=torch.int32,
+                          device=dev, generator=gen).view(torch.uint32)
+    z = torch.randn((experts, N // 32, K // 256, 32), device=dev, generator=gen)
+    scale = (0.01 * z.abs()).to(torch.float16).clamp_min(2 ** -14)
+    offset = (scale.float() * -8.0).to(torch.float16)
+    meta = ((scale.view(torch.int16).to(torch.int32) & 0xFFFF) | (offset.view(torch.int16).to(torch.int32) << 16))
+    return codes, meta.view(torch.uint32)
+
+
+class Stack:
+    def __init__(self, torch, cfg, dev, seed):
+        self.torch = torch
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        self.layers = []
+        for _ in range(cfg['layers']):
+            g = device_bank(torch, gen, dev, 256, 1024, 2048)
+            d = device_bank(torch, gen, dev, 256, 2048, 512)
+            sg = device_bank(torch, gen, dev, 1, 1024, 2048)
+            sd = device_bank(torch, gen, dev, 1, 2048, 512)
+            gw = (0.02 * torch.randn(2048, device=dev, generator=gen)).to(torch.bfloat16)
+            self.layers.append((g, d, sg, sd, gw))
+        tab = np.load(ROOT / 'tests' / 'golden' / 'shared_math_tables.npz')
+        self.silu = torch.from_numpy(tab['silu_fp32']).to(dev)
+        self.sigmoid = torch.from_numpy(tab['sigmoid_bf16'].view(np.int16)).to(dev).view(torch.bfloat16)
+        self.gen = gen
+
+
+def run(args):
+    import torch
+    import torch.distributed as dist
+    cfg = CONFIGS[args.config]
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=__import__('datetime').timedelta(seconds=120))
+    dev = torch.device('cuda', local)
+    torch.cuda.set_device(dev)
+    graft.load_package()
+    import importlib
+    native = importlib.import_module('ornith_b200.native')
+    lib = native.lib()
+    T, L, bits = cfg['T'], cfg['layers'], cfg['act_bits']
+    stack = Stack(torch, cfg, dev, seed=1234 + rank)
+    steps_total = args.warmup + args.steps
+    # router logits per (step, layer): N(0,1) (+ per-layer per-expert bias)
+    bias = (cfg['bias'] * torch.randn((L, 256), device=dev, generator=stack.gen)) if cfg['bias'] else None
+    n_logit_sets = steps_total if T <= 64 else 1
+    logits = torch.randn((n_logit_sets, L, T, 256), device=dev, generator=stack.gen)
+    if bias is not None:
+        logits += bias[None, :, None, :]
+    x0 = torch.randn((T, 2048), device=dev, generator=stack.gen).to(torch.bfloat16)
+    ws = torch.empty(native.workspace_bytes(T), dtype=torch.uint8, device=dev)
+    outs = [torch.empty((T, 2048), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    shared_out = torch.empty((T, 2048), dtype=torch.bfloat16, device=dev) if cfg['shared'] else None
+    flags = torch.zeros(L, dtype=torch.int32, device=dev)
+
+    def layer_call(l, x, lg, out):
+        (gc, gm), (dc, dm), (sgc, sgm), (sdc, sdm), gw = stack.layers[l]
+        if cfg['shared']:
+            native.routed_from_logits(x, lg, gc, gm, dc, dm, sgc, sgm, sdc, sdm, gw, stack.silu, stack.sigmoid,
+                                      ws, out, shared_out, flags[l:l + 1], T, bits)
+        else:
+            native.routed_from_logits(x, lg, gc, gm, dc, dm, None, None, None, None, None, None, None,
+                                      ws, out, None, flags[l:l + 1], T, bits)
+
+    def step(s, x):
+        lg = logits[s % n_logit_sets]
+        for l in range(L):
+            out = outs[l % 2]
+            layer_call(l, x, lg[l], out)
+            x = out
+        return x
+
+    # algorithmic bytes per step: (distinct experts + 1) * EXPERT_BYTES per layer + activations
+    ids = torch.topk(logits, 8, dim=-1).indices  # [sets, L, T, 8]
+    distinct = []
+    for s in range(n_logit_sets):
+        d = 0
+        for l in range(L):
+            d += int(torch.unique(ids[s, l]).numel()) + (1 if cfg['shared'] else 0)
+        distinct.append(d)
+    act_bytes = L * (2 * T * 4096 + T * 1024)
+
+    def step_bytes(s):
+        return distinct[s % n_logit_sets] * EXPERT_BYTES + act_bytes
+
+    for s in range(args.warmup):
+        step(s, x0)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.ornith_moe_b200_kernel_launches()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record()
+        for s in range(args.warmup, steps_total):
+            step(s, x0)
+        end.record()
+        torch.cuda.synchronize()
+    launches = lib.ornith_moe_b200_kernel_launches() - launches0
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * T * args.steps / (ms / 1e3)
+    bytes_timed = sum(step_bytes(s) for s in range(args.warmup, steps_total)) / args.steps
+
+    # per-layer-call timing (the layer call is the dominant launch group of a step)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    per_layer = []
+    for rep in range(3):
+        x = x0
+        for l in range(L):
+            ev[l][0].record()
+            layer_call(l, x, logits[(args.warmup + rep) % n_logit_sets][l], outs[l % 2])
+            ev[l][1].record()
+            x = outs[l % 2]
+        torch.cuda.synchronize()
+        per_layer += [a.elapsed_time(b) for a, b in ev]
+    layer_ms = statistics.mean(per_layer)
+    layer_bytes = bytes_timed / L
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    peak = peaks.get('hbm_gbs', 6650.0)
+    achieved = layer_bytes / (layer_ms * 1e-3) / 1e9
+
+    # end to end through the public operator, host buffers in and out
+    pin_x = x0.cpu().pin_memory()
+    pin_logits = logits[: min(n_logit_sets, 4)].cpu().pin_memory()
+    pin_out = torch.empty((T, 2048), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x0)
+    lg_dev = torch.empty_like(logits[0])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(args.steps):
+        x_dev.copy_(pin_x, non_blocking=True)
+        lg_dev.copy_(pin_logits[s % pin_logits.shape[0]], non_blocking=True)
+        x = x_dev
+        for l in range(L):
+            layer_call(l, x, lg_dev[l], outs[l % 2])
+            x = outs[l % 2]
+        pin_out.copy_(x, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+    flag_any = int(flags.max().item())
+
+    result = {
+        'metric': METRIC, 'value': round(value, 3), 'unit': 'tokens/s', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms_step, 4),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8',
+        'data': 'synthetic (seeded random-init weights and logits of the configured shapes)',
+        'config': {'workload': cfg['name'], 'tokens_per_step': T, 'layers': L, 'experts': 256, 'top_k': 8,
+                   'hidden': 2048, 'intermediate': 512, 'shared_expert': cfg['shared'],
+                   'weights': 'affine-u4 G256 (scale, offset=-8*scale), N32 storage',
+                   'activations': f'A{bits} per 256-group after H128', 'arith': 'u4 x s8 -> int32 dot, fp32 epilogue',
+                   'parallelism': f'replicas x{world}' if world > 1 else 'single GPU',
+                   'l2': f'inputs larger than L2: {bytes_timed / 1e6:.0f} MB of weights read per step'},
+        'e2e': {'value': round(e2e_value, 3), 'unit': 'tokens/s', 'h2d_bytes_per_step': T * 4096 + L * T * 1024,
+                'd2h_bytes_per_step': T * 4096},
+        'gpu_launches': int(launches),
+        'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
+                     'frac': round(achieved / peak, 4), 'traffic': None,
+                     'kernel': 'one routed_from_logits layer call (all its kernels)',
+                     'algorithmic_bytes_per_launch': int(layer_bytes), 'launch_ms': round(layer_ms, 5),
+                     'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback'},
+        'step_roofline_frac': round(bytes_timed / (ms_step * 1e-3) / 1e9 / peak, 4),
+        'flags_max': flag_any,
+        'clocks': clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result['cpu_baseline'] = cpu_baseline(cfg, args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port for cpu_baseline; compiled reference for --impl reference)
+# ---------------------------------------------------------------------------
+def _cpu_layer(seed=5):
+    graft.load_package()
+    import importlib
+    S = importlib.import_module('ornith_b200.synthetic')
+    return S, S.make_layer(np.random.default_rng(seed))
+
+
+def cpu_baseline(cfg, seconds):
+    from oracle import oracle as O
+    S, layer = _cpu_layer()
+    cores = O.set_threads(os.cpu_count() or 1)
+    tab = np.load(ROOT / 'tests' / 'golden' / 'shared_math_tables.npz')
+    rng = np.random.default_rng(9)
+    T = min(cfg['T'], 64)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 2:
+        x = S.make_tokens(rng, T)
+        logits = rng.standard_normal((T, 256)).astype(np.float32)
+        w, ids = O.route_topk(logits)
+        if cfg['shared']:
+            logit = S.f32_to_bf16_bits(rng.standard_normal(T).astype(np.float32))
+            O.routed_layer_shared(x, w, ids, layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta,
+                                  layer.sgate_codes, layer.sgate_meta, layer.sdown_codes, layer.sdown_meta, logit,
+                                  tab['silu_fp32'], tab['sigmoid_bf16'])
+        else:
+            O.routed_layer(x, w, ids, layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta,
+                           a8=cfg['act_bits'] == 8)
+        n += 1
+    layer_s = (time.perf_counter() - t0) / n
+    tokens_per_s = T / (layer_s * cfg['layers'])
+    return {'value': round(tokens_per_s, 4), 'unit': 'tokens/s', 'cores': cores, 'kind': 'port',
+            'sample': f'{n} single-layer calls of T={T} (oracle C port, OpenMP), scaled to a {cfg["layers"]}-layer step'}
+
+
+def run_reference(args):
+    cfg = CONFIGS[args.config]
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    if not O.reference_available():
+        print(json.dumps({'impl': 'reference', 'unavailable': 'oracle/_ref was not built (needs the reference checkout)'}))
+        return
+    S, layer = _cpu_layer()
+    tab = np.load(ROOT / 'tests' / 'golden' / 'shared_math_tables.npz')
+    rng = np.random.default_rng(10)
+    T = min(cfg['T'], 16 if cfg['shared'] else 64)
+    layers_per_step = 2
+
+    def one():
+        for _ in range(layers_per_step):
+            x = S.make_tokens(rng, T)
+            w, ids = O.route_topk(rng.standard_normal((T, 256)).astype(np.float32))
+            if cfg['shared']:
+                logit = S.f32_to_bf16_bits(rng.standard_normal(T).astype(np.float32))
+                O.ref_routed_shared(x, w, ids, layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta,
+                                    layer.sgate_codes, layer.sgate_meta, layer.sdown_codes, layer.sdown_meta, logit,
+                                    tab['silu_fp32'], tab['sigmoid_bf16'])
+            else:
+                entry = 'ornith_routed_direct_launch' if cfg['act_bits'] == 8 else 'ornith_routed_direct_launch_a4'
+                O.ref_routed(x, w, ids, layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta,
+                             entry=entry)
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    el = time.perf_counter() - t0
+    layer_s = el / (args.steps * layers_per_step)
+    value = T / (layer_s * cfg['layers'])
+    cores = os.cpu_count() or 1
+    sample = (f'{layers_per_step} layer calls of T={T} per step (reference routed_storage source compiled for the CPU '
+              f'with a SIMT shim), scaled to a {cfg["layers"]}-layer step')
+    print(json.dumps({
+        'impl': 'reference', 'metric': METRIC, 'value': round(value, 4), 'unit': 'tokens/s', 'n_gpus': 0,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(el / args.steps * 1e3, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8',
+        'data': 'synthetic', 'config': {'workload': cfg['name'], 'tokens_per_step': T},
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'tokens/s', 'cores': cores, 'kind': 'reference',
+                         'sample': sample},
+        'e2e': {'value': round(value, 4), 'unit': 'tokens/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }), flush=True)
+
+
+if __name__ == '__main__':
+    a = parse()
+    if a.impl == 'reference':
+        run_reference(a)
+    else:
+        run(a)

@@ -1,0 +1,167 @@
+/*
+ * C ABI of the B200 routed mixture-of-experts layer (libornith_moe_b200.so).
+ *
+ * Drop-in for the routed library of ciru-ai/ornith-ciru-halo-agent
+ * (libornith_routed_storage_n32.so, kernels/routed_storage/): the same symbol
+ * names, argument order, layout struct and error behaviour, with CUDA types in
+ * place of HIP ones.  The plugin binds them through ctypes exactly as
+ * plugin-site/ornith_g256/native.py:45-85 and moe_shared.py:135-141 do.
+ *
+ * Fixed shapes: 256 routed experts, top-8, hidden H = 2048, intermediate
+ * I = 512, quantisation group 256, Hadamard block 128.  Weight banks use the
+ * reference's N32 storage (after plugin-site/ornith_g256/method.py:124-158):
+ *   gate_codes  uint32 [256][32][8][32][32]   gate_meta  uint32 [256][32][8][32]
+ *   down_codes  uint32 [256][64][2][32][32]   down_meta  uint32 [256][64][2][32]
+ * Word j of group g for column n holds k = 256g + 8j + d in bits 4d..4d+3 (u4);
+ * each metadata word is fp16 scale (low half) | fp16 offset (high half) and the
+ * weight is scale*code + offset.
+ *
+ * Contract (routed_storage_n32_consumer.cpp:319-351 and the dense contract
+ * kernels/dense_n32/dense_g256_api.h:32-44):
+ *   - every launch is enqueued on `stream`; no allocation, no synchronisation,
+ *     no host reads of device data;
+ *   - the caller owns every buffer; the workspace (size from get_layout) is not
+ *     re-entrant: calls that share it must be ordered on one stream;
+ *   - T == 0 returns success without touching any pointer; bad Tcap/T/bytes,
+ *     null pointers or misaligned pointers return cudaErrorInvalidValue;
+ *     launch failures return the CUDA error;
+ *   - numerical faults are reported through sticky bits OR-ed into *flags_u32
+ *     (never cleared by the library): 1 non-finite input/transform,
+ *     2 invalid activation quantisation, 4 expert id outside [-1, 256),
+ *     8 non-finite projection, 16 non-finite SiLU*up, 32 non-finite or
+ *     overflowing output, 64 a bounded device wait gave up (results incomplete);
+ *   - ids of -1 are padding and skip their slot.
+ * Alignment: workspace 256 B; input, output, codes and metadata 16 B;
+ * route weights, ids and flags 4 B.
+ */
+#ifndef ORNITH_MOE_B200_H
+#define ORNITH_MOE_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORNITH_MOE_B200_EXPORT __attribute__((visibility("default")))
+
+/* Same 15 size_t fields as OrnithRoutedDirectLayout
+ * (kernels/routed_storage/routed_direct_api.h:11-14, native.py:16-20).
+ * workspace_bytes is the size to allocate.  The other fields give the byte
+ * offsets of this library's buffers (gate_low: int8 token activations,
+ * gate_scales/gate_sums: their fp16 scales and int32 sums, middle: fp32
+ * SiLU*up rows, down_low/down_scales/down_sums: quantised middle,
+ * route_out: fp32 per-route down projections, final_f32: fp32 combined sum);
+ * fields with no counterpart here (gate_x, gate_high, gate_y, down_x,
+ * down_high) hold SIZE_MAX. */
+typedef struct OrnithRoutedDirectLayout {
+    size_t workspace_bytes, gate_x, gate_low, gate_high, gate_scales, gate_sums, gate_y;
+    size_t middle, down_x, down_low, down_high, down_scales, down_sums, route_out, final_f32;
+} OrnithRoutedDirectLayout;
+
+/* Replaces ornith_routed_direct_get_layout (routed_storage_n32_consumer.cpp:309-318).
+ * 0 <= Tcap <= 8192. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_direct_get_layout(int Tcap, OrnithRoutedDirectLayout* out);
+
+/* Replaces ornith_routed_direct_launch (routed_storage_n32_consumer.cpp:352-359,
+ * routed_direct_api.h:15-18): A8 activations (int8, +-127) at both projections.
+ * input bf16 [T,2048], route_weights fp32 [T,8], ids int32 [T,8] -> output bf16 [T,2048]. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_direct_launch(
+    const void* input_bf16, const void* route_weights_f32, const void* ids_i32,
+    const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
+    void* workspace, size_t bytes, void* output_bf16, void* flags_u32, int T, int Tcap, cudaStream_t stream);
+
+/* Replaces ornith_routed_direct_launch_a4 (routed_storage_n32_consumer.cpp:360,
+ * routed_direct_api.h:19-24): A4 activations (+-7) at both projections. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_direct_launch_a4(
+    const void* input_bf16, const void* route_weights_f32, const void* ids_i32,
+    const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
+    void* workspace, size_t bytes, void* output_bf16, void* flags_u32, int T, int Tcap, cudaStream_t stream);
+
+/* Replaces ornith_routed_direct_launch_a4_prefill (routed_storage_n32_consumer.cpp:362-370):
+ * A4 when T > 64, A8 otherwise. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_direct_launch_a4_prefill(
+    const void* input_bf16, const void* route_weights_f32, const void* ids_i32,
+    const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
+    void* workspace, size_t bytes, void* output_bf16, void* flags_u32, int T, int Tcap, cudaStream_t stream);
+
+/* Replaces ornith_routed_storage_n32 (routed_storage_n32_consumer.cpp:372): returns 32,
+ * the marker native.py:67-71 checks before using sole N32 storage. */
+ORNITH_MOE_B200_EXPORT int ornith_routed_storage_n32(void);
+
+/* Replaces ornith_routed_prefill_output_tile (routed_storage_n32_consumer.cpp:373):
+ * 32, the production library's A4 prefill output tile.  Informational only. */
+ORNITH_MOE_B200_EXPORT int ornith_routed_prefill_output_tile(void);
+
+/* Replaces ornith_routed_shared_get_layout (routed_storage_n32_consumer.cpp:375-384).
+ * 0 <= Tcap <= 16, as in the reference. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_shared_get_layout(int Tcap, OrnithRoutedDirectLayout* out);
+
+/* Replaces ornith_routed_direct_launch_shared_tables (routed_storage_n32_consumer.cpp:385-401):
+ * the routed layer plus the shared expert as a ninth slot (A8).  Shared banks
+ * have the routed layout with one expert.  shared_logit bf16 [T] (the shared
+ * expert gate logit), shared_silu fp32 [65536] and shared_sigmoid bf16 [65536]
+ * are the tables indexed by bf16 bits (native/shared_math_reference.safetensors).
+ * Shared gate/up and down outputs are rounded to bf16; shared_output bf16 [T,2048]
+ * = bf16(down * sigmoid[logit]) is written separately from output. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_direct_launch_shared_tables(
+    const void* input_bf16, const void* route_weights_f32, const void* ids_i32,
+    const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
+    const void* shared_gate_codes, const void* shared_gate_meta,
+    const void* shared_down_codes, const void* shared_down_meta,
+    const void* shared_logit, const void* shared_silu, const void* shared_sigmoid,
+    void* workspace, size_t bytes, void* output_bf16, void* shared_output_bf16, void* flags_u32,
+    int T, int Tcap, cudaStream_t stream);
+
+/* ABI revision of this library (the counterpart of ornith_dense_g256_abi_version,
+ * kernels/dense_n32/dense_g256_api.h:45).  Returns 1. */
+ORNITH_MOE_B200_EXPORT uint32_t ornith_moe_b200_abi_version(void);
+
+/* Number of kernels this library has enqueued since it was loaded (a host-side
+ * counter, for benchmarks that report how many of this library's kernels ran
+ * in a timed region).  No counterpart in the reference. */
+ORNITH_MOE_B200_EXPORT unsigned long long ornith_moe_b200_kernel_launches(void);
+
+/* Router top-8 with renormalised softmax weights, the role of vLLM's
+ * fused_topk/topk_softmax (vllm/model_executor/layers/fused_moe/router/
+ * fused_topk_router.py:69-102) for renormalize=True.  logits fp32 [T,256] ->
+ * weights fp32 [T,8], ids int32 [T,8].  Slot order: descending logit, lower
+ * expert index first on ties; weights = softmax over the eight selected logits
+ * using the reference's portable exp.  Non-finite logits are never selected
+ * (flag 1); unfilled slots get id -1 and weight 0.  0 <= T <= 8192. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_route_topk(
+    const void* logits_f32, int T, void* weights_f32, void* ids_i32, void* flags_u32, cudaStream_t stream);
+
+/* The MoE layer from router logits (the north-star operator: hidden states,
+ * router logits, top-8, packed weights and scales in, combined hidden states
+ * out).  Runs route_topk into the workspace, then the routed layer; when the
+ * four shared banks are given it also runs the shared expert as a ninth slot
+ * with logit = bf16(sum_k x[t,k]*shared_gate_weight[k]) in fp32 and writes
+ * shared_output.  act_bits: 8 (A8), 4 (A4) or 0 (A4 when T > 64, else A8).
+ * Shared-expert calls require act_bits 8 or 0 with T <= 64. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_launch_from_logits(
+    const void* input_bf16, const void* logits_f32,
+    const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
+    const void* shared_gate_codes, const void* shared_gate_meta,
+    const void* shared_down_codes, const void* shared_down_meta,
+    const void* shared_gate_weight_bf16, const void* shared_silu, const void* shared_sigmoid,
+    void* workspace, size_t bytes, void* output_bf16, void* shared_output_bf16, void* flags_u32,
+    int T, int Tcap, int act_bits, cudaStream_t stream);
+
+/* Workspace size for ornith_moe_b200_launch_from_logits (0 <= Tcap <= 8192). */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes);
+
+/* One-time repack of the reference checkpoint's N16 banks into N32 storage
+ * (plugin-site/ornith_g256/method.py:124-158, prepare_n32_weights):
+ * codes [E][N/16][K/256][32][16] -> [E][N/32][K/256][32][32], metadata
+ * [E][N/16][K/256][16] -> [E][N/32][K/256][32].  N a multiple of 32, K of 256.
+ * Source and destination must not overlap. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_repack_n16_to_n32(
+    const void* codes_n16, const void* meta_n16, void* codes_n32, void* meta_n32,
+    int experts, int N, int K, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

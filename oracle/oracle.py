@@ -1,0 +1,251 @@
+"""ctypes front-end of the CPU oracle (test infrastructure only).
+
+Two checkers live here:
+  * `liboracle.so`, the C restatement of the reference's routed-MoE arithmetic
+    (oracle/ornith_oracle.c);
+  * the reference's own HIP sources compiled for the CPU (oracle/build_ref.py),
+    called through the reference's exported C ABI
+    (kernels/routed_storage/routed_direct_api.h:13-33,
+    routed_storage_n32_consumer.cpp:309-401).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may
+import this module.  The product path never does.
+"""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / '_build' / 'liboracle.so'
+REF_DIR = HERE / '_ref'
+
+E, TOP, H, I, G = 256, 8, 2048, 512, 256
+
+_lib = None
+_refs = {}
+
+
+def build():
+    """Compile liboracle.so (and the reference libraries when the reference checkout exists)."""
+    subprocess.run(['make', '-s', '-C', str(HERE)], check=True)
+    from . import build_ref  # noqa: WPS433
+    ref = Path(build_ref.os.environ.get('ORNITH_REFERENCE', '/root/reference'))
+    if (ref / 'kernels').is_dir():
+        build_ref.build(ref)
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            subprocess.run(['make', '-s', '-C', str(HERE)], check=True)
+        _lib = C.CDLL(str(LIB_PATH))
+        _lib.orc_bf16_rne.restype = C.c_uint16
+        _lib.orc_bf16_rne.argtypes = [C.c_float]
+        _lib.orc_f32_to_half_rne.restype = C.c_uint16
+        _lib.orc_f32_to_half_rne.argtypes = [C.c_float]
+        _lib.orc_half_to_f32.restype = C.c_float
+        _lib.orc_half_to_f32.argtypes = [C.c_uint16]
+        _lib.orc_portable_exp.restype = C.c_float
+        _lib.orc_portable_exp.argtypes = [C.c_float]
+        _lib.orc_silu.restype = C.c_float
+        _lib.orc_silu.argtypes = [C.c_float]
+        _lib.orc_set_threads.restype = C.c_int
+        _lib.orc_set_threads.argtypes = [C.c_int]
+        for name in ('orc_routed_layer', 'orc_routed_layer_shared'):
+            getattr(_lib, name).restype = C.c_int
+    return _lib
+
+
+def set_threads(n):
+    return lib().orc_set_threads(int(n))
+
+
+def _c(a, dtype):
+    a = np.ascontiguousarray(a)
+    if a.dtype != dtype:
+        raise TypeError(f'expected {dtype}, got {a.dtype}')
+    return a
+
+
+def _banks(gate_codes, gate_meta, down_codes, down_meta):
+    return [_c(gate_codes, np.uint32), _c(gate_meta, np.uint32), _c(down_codes, np.uint32), _c(down_meta, np.uint32)]
+
+
+def routed_layer(x_bits, weights, ids, gate_codes, gate_meta, down_codes, down_meta, a8=True):
+    """Routed layer; x_bits uint16 bf16 bits [T,2048].  Returns (out bf16 bits, out fp32, flags)."""
+    x_bits = _c(x_bits, np.uint16)
+    weights = _c(weights, np.float32)
+    ids = _c(ids, np.int32)
+    T = x_bits.shape[0]
+    banks = _banks(gate_codes, gate_meta, down_codes, down_meta)
+    out = np.zeros((T, H), np.uint16)
+    out_f32 = np.zeros((T, H), np.float32)
+    flags = np.zeros(1, np.uint32)
+    rc = lib().orc_routed_layer(_p(x_bits), _p(weights), _p(ids), C.c_int(T), *[_p(b) for b in banks],
+                                C.c_int(1 if a8 else 0), _p(out), _p(out_f32), _p(flags))
+    if rc:
+        raise MemoryError('oracle allocation failed')
+    return out, out_f32, int(flags[0])
+
+
+def routed_layer_shared(x_bits, weights, ids, gate_codes, gate_meta, down_codes, down_meta,
+                        sgate_codes, sgate_meta, sdown_codes, sdown_meta, logit_bits, silu_table, sigmoid_bits):
+    """Routed layer + fused shared slot (A8).  Returns (out, shared_out, out_f32, flags)."""
+    x_bits = _c(x_bits, np.uint16)
+    T = x_bits.shape[0]
+    args = [x_bits, _c(weights, np.float32), _c(ids, np.int32)]
+    banks = _banks(gate_codes, gate_meta, down_codes, down_meta) + _banks(sgate_codes, sgate_meta, sdown_codes, sdown_meta)
+    tables = [_c(logit_bits, np.uint16), _c(silu_table, np.float32), _c(sigmoid_bits, np.uint16)]
+    out = np.zeros((T, H), np.uint16)
+    shared = np.zeros((T, H), np.uint16)
+    out_f32 = np.zeros((T, H), np.float32)
+    flags = np.zeros(1, np.uint32)
+    rc = lib().orc_routed_layer_shared(_p(args[0]), _p(args[1]), _p(args[2]), C.c_int(T),
+                                       *[_p(b) for b in banks], *[_p(t) for t in tables],
+                                       _p(out), _p(shared), _p(out_f32), _p(flags))
+    if rc:
+        raise MemoryError('oracle allocation failed')
+    return out, shared, out_f32, int(flags[0])
+
+
+def route_topk(logits):
+    logits = _c(logits, np.float32)
+    T = logits.shape[0]
+    w = np.zeros((T, TOP), np.float32)
+    ids = np.zeros((T, TOP), np.int32)
+    lib().orc_route_topk(_p(logits), C.c_int(T), _p(w), _p(ids))
+    return w, ids
+
+
+def router_logits(x_bits, w_bits):
+    x_bits, w_bits = _c(x_bits, np.uint16), _c(w_bits, np.uint16)
+    out = np.zeros((x_bits.shape[0], E), np.float32)
+    lib().orc_router_logits(_p(x_bits), _p(w_bits), C.c_int(x_bits.shape[0]), _p(out))
+    return out
+
+
+def transform_tokens(x_bits, ids=None):
+    x_bits = _c(x_bits, np.uint16)
+    T = x_bits.shape[0]
+    y = np.zeros((T, H), np.float32)
+    flags = np.zeros(1, np.uint32)
+    lib().orc_transform_tokens(_p(x_bits), None if ids is None else _p(_c(ids, np.int32)), C.c_int(T), _p(y), _p(flags))
+    return y, int(flags[0])
+
+
+def quantize_rows(y, a8=True):
+    y = _c(y, np.float32)
+    rows, K = y.shape
+    q = np.zeros((rows, K), np.int8)
+    scales = np.zeros((rows, K // G), np.uint16)
+    sums = np.zeros((rows, K // G), np.int32)
+    flags = np.zeros(1, np.uint32)
+    lib().orc_quantize_rows(_p(y), C.c_int(rows), C.c_int(K), C.c_int(1 if a8 else 0), _p(q), _p(scales), _p(sums), _p(flags))
+    return q, scales, sums, int(flags[0])
+
+
+def wht128(v):
+    v = _c(v, np.float32)
+    out = np.zeros(128, np.float32)
+    lib().orc_wht128(_p(v), _p(out))
+    return out
+
+
+def fp32_reference_layer(x_bits, weights, ids, gate_codes, gate_meta, down_codes, down_meta):
+    x_bits = _c(x_bits, np.uint16)
+    T = x_bits.shape[0]
+    out = np.zeros((T, H), np.float32)
+    banks = _banks(gate_codes, gate_meta, down_codes, down_meta)
+    lib().orc_fp32_reference_layer(_p(x_bits), _p(_c(weights, np.float32)), _p(_c(ids, np.int32)), C.c_int(T),
+                                   *[_p(b) for b in banks], _p(out))
+    return out
+
+
+def repack_n16_to_n32(codes16, meta16, N, K):
+    codes16, meta16 = _c(codes16, np.uint32), _c(meta16, np.uint32)
+    Ex = codes16.shape[0]
+    codes32 = np.zeros((Ex, N // 32, K // G, 32, 32), np.uint32)
+    meta32 = np.zeros((Ex, N // 32, K // G, 32), np.uint32)
+    lib().orc_repack_n16_to_n32(_p(codes16), _p(meta16), C.c_int(Ex), C.c_int(N), C.c_int(K), _p(codes32), _p(meta32))
+    return codes32, meta32
+
+
+# ---------------------------------------------------------------------------
+# The reference's own source, compiled for the CPU (oracle/_ref).
+# ---------------------------------------------------------------------------
+
+class RoutedLayout(C.Structure):
+    """OrnithRoutedDirectLayout, kernels/routed_storage/routed_direct_api.h:11-14."""
+    _fields_ = [(n, C.c_size_t) for n in
+                ('workspace_bytes', 'gate_x', 'gate_low', 'gate_high', 'gate_scales',
+                 'gate_sums', 'gate_y', 'middle', 'down_x', 'down_low', 'down_high',
+                 'down_scales', 'down_sums', 'route_out', 'final_f32')]
+
+
+def reference_available(name='routed_storage_n32'):
+    return (REF_DIR / f'libref_{name}.so').exists()
+
+
+def ref_lib(name='routed_storage_n32'):
+    if name not in _refs:
+        path = REF_DIR / f'libref_{name}.so'
+        if not path.exists():
+            raise FileNotFoundError(f'{path} not built (python oracle/build_ref.py in the build container)')
+        _refs[name] = C.CDLL(str(path))
+    return _refs[name]
+
+
+def ref_routed(x_bits, weights, ids, gate_codes, gate_meta, down_codes, down_meta, entry='ornith_routed_direct_launch',
+               Tcap=None, library='routed_storage_n32'):
+    """Run the compiled reference entry point.  Returns (out bf16 bits, final fp32 diagnostic, flags, status)."""
+    L = ref_lib(library)
+    x_bits = _c(x_bits, np.uint16)
+    T = x_bits.shape[0]
+    Tcap = T if Tcap is None else Tcap
+    layout = RoutedLayout()
+    L.ornith_routed_direct_get_layout.restype = C.c_int
+    st = L.ornith_routed_direct_get_layout(C.c_int(Tcap), C.byref(layout))
+    if st:
+        return None, None, None, st
+    ws = np.zeros(max(layout.workspace_bytes, 1), np.uint8)
+    out = np.zeros((max(T, 1), H), np.uint16)
+    flags = np.zeros(1, np.uint32)
+    banks = _banks(gate_codes, gate_meta, down_codes, down_meta)
+    fn = getattr(L, entry)
+    fn.restype = C.c_int
+    st = fn(_p(x_bits), _p(_c(weights, np.float32)), _p(_c(ids, np.int32)), *[_p(b) for b in banks],
+            _p(ws), C.c_size_t(ws.size), _p(out), _p(flags), C.c_int(T), C.c_int(Tcap), None)
+    final = ws[layout.final_f32:layout.final_f32 + T * H * 4].view(np.float32).reshape(T, H).copy() if T else None
+    return out[:T], final, int(flags[0]), st
+
+
+def ref_routed_shared(x_bits, weights, ids, gate_codes, gate_meta, down_codes, down_meta,
+                      sgate_codes, sgate_meta, sdown_codes, sdown_meta, logit_bits, silu_table, sigmoid_bits, Tcap=16):
+    """ornith_routed_direct_launch_shared_tables of the compiled reference."""
+    L = ref_lib('routed_storage_n32')
+    x_bits = _c(x_bits, np.uint16)
+    T = x_bits.shape[0]
+    layout = RoutedLayout()
+    L.ornith_routed_shared_get_layout.restype = C.c_int
+    st = L.ornith_routed_shared_get_layout(C.c_int(Tcap), C.byref(layout))
+    if st:
+        return None, None, None, st
+    ws = np.zeros(layout.workspace_bytes, np.uint8)
+    out = np.zeros((T, H), np.uint16)
+    shared = np.zeros((T, H), np.uint16)
+    flags = np.zeros(1, np.uint32)
+    banks = _banks(gate_codes, gate_meta, down_codes, down_meta) + _banks(sgate_codes, sgate_meta, sdown_codes, sdown_meta)
+    tables = [_c(logit_bits, np.uint16), _c(silu_table, np.float32), _c(sigmoid_bits, np.uint16)]
+    fn = L.ornith_routed_direct_launch_shared_tables
+    fn.restype = C.c_int
+    st = fn(_p(x_bits), _p(_c(weights, np.float32)), _p(_c(ids, np.int32)), *[_p(b) for b in banks],
+            *[_p(t) for t in tables], _p(ws), C.c_size_t(ws.size), _p(out), _p(shared), _p(flags),
+            C.c_int(T), C.c_int(Tcap), None)
+    return out, shared, int(flags[0]), st

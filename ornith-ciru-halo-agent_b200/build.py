@@ -1,0 +1,42 @@
+"""Build libornith_moe_b200.so in-tree with nvcc for sm_100a.
+
+The library is pure CUDA C++ behind a C ABI (include/ornith_moe_b200.h): no
+torch types cross the boundary.  -fmad=false keeps every fp32 step of the
+reference's fixed-order arithmetic un-contracted.
+"""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / 'csrc'
+LIB = HERE / 'libornith_moe_b200.so'
+SOURCES = ['moe_api.cu', 'moe_generic.cu']
+NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
+FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-lineinfo', '-O3', '-std=c++17',
+         '-fmad=false', '-Xcompiler', '-fPIC,-fvisibility=hidden', '-shared', '-rdc=false',
+         f'-I{HERE.parent / "include"}']
+
+
+def stale():
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob('*.cuh')) + list((HERE.parent / 'include').glob('*.h'))
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build(force=False, verbose=False):
+    if not force and not stale():
+        return LIB
+    cmd = [NVCC, *FLAGS, *[str(CSRC / s) for s in SOURCES], '-o', str(LIB)]
+    if verbose:
+        cmd.insert(1, '-Xptxas=-v')
+    subprocess.run(cmd, check=True)
+    return LIB
+
+
+if __name__ == '__main__':
+    build(force=True, verbose='-v' in sys.argv)
+    print(LIB)

@@ -1,0 +1,399 @@
+// C-ABI entry points of libornith_moe_b200.so (declared in include/ornith_moe_b200.h).
+//
+// Argument validation and return codes mirror the reference's routed library
+// (kernels/routed_storage/routed_storage_n32_consumer.cpp:309-401): bad
+// Tcap/T/bytes or null pointers give cudaErrorInvalidValue, T == 0 succeeds
+// without touching any pointer, launch errors are returned as CUDA errors.
+// Alignment is checked as the dense library does (dense_g256_consumer.cpp:256-262).
+#include <stdint.h>
+
+#include <atomic>
+
+#include "../../include/ornith_moe_b200.h"
+#include "moe_layer.cuh"
+
+using namespace ornith;
+
+namespace ornith {
+static std::atomic<unsigned long long> g_launches{0};
+void count_launches(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n), std::memory_order_relaxed); }
+}  // namespace ornith
+
+namespace {
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Top-8 routing, one warp per token (see ornith_moe_b200_route_topk).
+// Lane l holds logits l, l+32, ..., l+224; each of 8 rounds takes the warp-wide
+// maximum among the finite, unselected logits, lower index first on ties.
+__global__ __launch_bounds__(256) void route_topk_kernel(const float* logits, int T, float* weights,
+                                                         int32_t* ids, uint32_t* flags) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const float* l = logits + size_t(warp) * kE;
+    float v[8];
+    bool ok[8];
+    uint32_t f = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[i] = l[lane + 32 * i];
+        ok[i] = isfinite(v[i]);
+        if (!ok[i]) f |= kFlagNonfiniteInput;
+    }
+    float sel_v[kTop];
+    int sel_i[kTop];
+#pragma unroll
+    for (int s = 0; s < kTop; ++s) {
+        float bv = 0.f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            int idx = lane + 32 * i;
+            if (ok[i] && (bi == 0x7fffffff || v[i] > bv)) {
+                bv = v[i];
+                bi = idx;
+            }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, d);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+            bool take = oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi));
+            if (take) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        sel_v[s] = bv;
+        sel_i[s] = bi == 0x7fffffff ? -1 : bi;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (lane + 32 * i == bi) ok[i] = false;
+    }
+    if (lane == 0) {
+        float ex[kTop], sum = 0.f;
+        const float m = sel_i[0] >= 0 ? sel_v[0] : 0.f;
+#pragma unroll
+        for (int s = 0; s < kTop; ++s) {
+            ex[s] = sel_i[s] >= 0 ? portable_exp(__fsub_rn(sel_v[s], m)) : 0.f;
+            sum = __fadd_rn(sum, ex[s]);
+        }
+#pragma unroll
+        for (int s = 0; s < kTop; ++s) {
+            ids[size_t(warp) * kTop + s] = sel_i[s];
+            weights[size_t(warp) * kTop + s] = sel_i[s] >= 0 ? __fdiv_rn(ex[s], sum) : 0.f;
+        }
+        if (f) atomicOr(flags, f);
+    }
+}
+
+// Shared-expert gate logit bf16(sum_k x[t,k]*w[k]) with fp32 products and sums:
+// lane partial sums over k = lane + 32i (i ascending), then an xor tree.
+__global__ __launch_bounds__(256) void shared_logit_kernel(const uint16_t* x, const uint16_t* w, int T, uint16_t* logit) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    float acc = 0.f;
+    for (int i = 0; i < kH / 32; ++i) {
+        int k = lane + 32 * i;
+        acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(x[size_t(warp) * kH + k]), bf16_to_f32(w[k])));
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    if (lane == 0) logit[warp] = bf16_rne(acc);
+}
+
+// N16 -> N32 bank repack (method.py:142-147).  One thread per destination word.
+__global__ void repack_codes_kernel(const uint32_t* src, uint32_t* dst, int E, int N, int groups) {
+    const size_t total = size_t(E) * (N / 32) * groups * 32 * 32;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        size_t rem = i;
+        const int col = int(rem % 32); rem /= 32;
+        const int j = int(rem % 32); rem /= 32;
+        const int g = int(rem % groups); rem /= groups;
+        const int t2 = int(rem % (N / 32)); rem /= (N / 32);
+        const size_t e = rem;
+        const int half = col / 16, l = col % 16;
+        dst[i] = src[((((e * (N / 16) + 2 * t2 + half) * groups + g) * 32 + j) * 16) + l];
+    }
+}
+__global__ void repack_meta_kernel(const uint32_t* src, uint32_t* dst, int E, int N, int groups) {
+    const size_t total = size_t(E) * (N / 32) * groups * 32;
+    for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        size_t rem = i;
+        const int col = int(rem % 32); rem /= 32;
+        const int g = int(rem % groups); rem /= groups;
+        const int t2 = int(rem % (N / 32)); rem /= (N / 32);
+        const size_t e = rem;
+        const int half = col / 16, l = col % 16;
+        dst[i] = src[(((e * (N / 16) + 2 * t2 + half) * groups + g) * 16) + l];
+    }
+}
+
+void fill_layout(int Tcap, OrnithRoutedDirectLayout* out) {
+    const Workspace w = workspace_layout(Tcap);
+    OrnithRoutedDirectLayout l;
+    l.workspace_bytes = w.bytes;
+    l.gate_x = SIZE_MAX;
+    l.gate_low = w.xq;
+    l.gate_high = SIZE_MAX;
+    l.gate_scales = w.xs;
+    l.gate_sums = w.xsum;
+    l.gate_y = SIZE_MAX;
+    l.middle = w.middle;
+    l.down_x = SIZE_MAX;
+    l.down_low = w.mq;
+    l.down_high = SIZE_MAX;
+    l.down_scales = w.ms;
+    l.down_sums = w.msum;
+    l.route_out = w.route_out;
+    l.final_f32 = w.final_f32;
+    *out = l;
+}
+
+cudaError_t run_layer(const LayerArgs& a, cudaStream_t stream) {
+    return launch_generic(a, stream);
+}
+
+cudaError_t routed_launch(int act_bits, const void* input, const void* weights, const void* ids,
+                          const void* gate_codes, const void* gate_meta, const void* down_codes,
+                          const void* down_meta, void* workspace, size_t bytes, void* output, void* flags,
+                          int T, int Tcap, cudaStream_t stream) {
+    if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap) return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes) return cudaErrorInvalidValue;
+    if (!T) return cudaSuccess;
+    if (!input || !weights || !ids || !gate_codes || !gate_meta || !down_codes || !down_meta || !workspace ||
+        !output || !flags)
+        return cudaErrorInvalidValue;
+    if (!aligned(input, 16) || !aligned(output, 16) || !aligned(gate_codes, 16) || !aligned(gate_meta, 16) ||
+        !aligned(down_codes, 16) || !aligned(down_meta, 16) || !aligned(workspace, 256) || !aligned(weights, 4) ||
+        !aligned(ids, 4) || !aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    LayerArgs a{};
+    a.x = static_cast<const uint16_t*>(input);
+    a.weights = static_cast<const float*>(weights);
+    a.ids = static_cast<const int32_t*>(ids);
+    a.gate_codes = static_cast<const uint32_t*>(gate_codes);
+    a.gate_meta = static_cast<const uint32_t*>(gate_meta);
+    a.down_codes = static_cast<const uint32_t*>(down_codes);
+    a.down_meta = static_cast<const uint32_t*>(down_meta);
+    a.out = static_cast<uint16_t*>(output);
+    a.flags = static_cast<uint32_t*>(flags);
+    a.ws = static_cast<uint8_t*>(workspace);
+    a.L = w;
+    a.T = T;
+    a.a8 = act_bits == 8;
+    return run_layer(a, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+cudaError_t ornith_routed_direct_get_layout(int Tcap, OrnithRoutedDirectLayout* out) {
+    if (!out || Tcap < 0 || Tcap > kTcapMax) return cudaErrorInvalidValue;
+    fill_layout(Tcap, out);
+    return cudaSuccess;
+}
+
+cudaError_t ornith_routed_direct_launch(const void* input, const void* weights, const void* ids, const void* gate_codes,
+                                        const void* gate_meta, const void* down_codes, const void* down_meta,
+                                        void* workspace, size_t bytes, void* output, void* flags, int T, int Tcap,
+                                        cudaStream_t stream) {
+    return routed_launch(8, input, weights, ids, gate_codes, gate_meta, down_codes, down_meta, workspace, bytes,
+                         output, flags, T, Tcap, stream);
+}
+
+cudaError_t ornith_routed_direct_launch_a4(const void* input, const void* weights, const void* ids,
+                                           const void* gate_codes, const void* gate_meta, const void* down_codes,
+                                           const void* down_meta, void* workspace, size_t bytes, void* output,
+                                           void* flags, int T, int Tcap, cudaStream_t stream) {
+    return routed_launch(4, input, weights, ids, gate_codes, gate_meta, down_codes, down_meta, workspace, bytes,
+                         output, flags, T, Tcap, stream);
+}
+
+cudaError_t ornith_routed_direct_launch_a4_prefill(const void* input, const void* weights, const void* ids,
+                                                   const void* gate_codes, const void* gate_meta,
+                                                   const void* down_codes, const void* down_meta, void* workspace,
+                                                   size_t bytes, void* output, void* flags, int T, int Tcap,
+                                                   cudaStream_t stream) {
+    return routed_launch(T > 64 ? 4 : 8, input, weights, ids, gate_codes, gate_meta, down_codes, down_meta,
+                         workspace, bytes, output, flags, T, Tcap, stream);
+}
+
+int ornith_routed_storage_n32(void) { return 32; }
+int ornith_routed_prefill_output_tile(void) { return 32; }
+
+cudaError_t ornith_routed_shared_get_layout(int Tcap, OrnithRoutedDirectLayout* out) {
+    if (!out || Tcap < 0 || Tcap > 16) return cudaErrorInvalidValue;
+    fill_layout(Tcap, out);
+    return cudaSuccess;
+}
+
+cudaError_t ornith_routed_direct_launch_shared_tables(
+    const void* input, const void* weights, const void* ids, const void* gate_codes, const void* gate_meta,
+    const void* down_codes, const void* down_meta, const void* shared_gate_codes, const void* shared_gate_meta,
+    const void* shared_down_codes, const void* shared_down_meta, const void* shared_logit, const void* shared_silu,
+    const void* shared_sigmoid, void* workspace, size_t bytes, void* output, void* shared_output, void* flags, int T,
+    int Tcap, cudaStream_t stream) {
+    if (Tcap < 0 || Tcap > 16 || T < 0 || T > Tcap) return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes) return cudaErrorInvalidValue;
+    if (!T) return cudaSuccess;
+    if (!input || !weights || !ids || !gate_codes || !gate_meta || !down_codes || !down_meta || !shared_gate_codes ||
+        !shared_gate_meta || !shared_down_codes || !shared_down_meta || !shared_logit || !shared_silu ||
+        !shared_sigmoid || !workspace || !output || !shared_output || !flags)
+        return cudaErrorInvalidValue;
+    if (!aligned(input, 16) || !aligned(output, 16) || !aligned(shared_output, 16) || !aligned(gate_codes, 16) ||
+        !aligned(gate_meta, 16) || !aligned(down_codes, 16) || !aligned(down_meta, 16) ||
+        !aligned(shared_gate_codes, 16) || !aligned(shared_gate_meta, 16) || !aligned(shared_down_codes, 16) ||
+        !aligned(shared_down_meta, 16) || !aligned(workspace, 256) || !aligned(weights, 4) || !aligned(ids, 4) ||
+        !aligned(flags, 4) || !aligned(shared_silu, 4) || !aligned(shared_logit, 2) || !aligned(shared_sigmoid, 2))
+        return cudaErrorInvalidValue;
+    LayerArgs a{};
+    a.x = static_cast<const uint16_t*>(input);
+    a.weights = static_cast<const float*>(weights);
+    a.ids = static_cast<const int32_t*>(ids);
+    a.gate_codes = static_cast<const uint32_t*>(gate_codes);
+    a.gate_meta = static_cast<const uint32_t*>(gate_meta);
+    a.down_codes = static_cast<const uint32_t*>(down_codes);
+    a.down_meta = static_cast<const uint32_t*>(down_meta);
+    a.sgate_codes = static_cast<const uint32_t*>(shared_gate_codes);
+    a.sgate_meta = static_cast<const uint32_t*>(shared_gate_meta);
+    a.sdown_codes = static_cast<const uint32_t*>(shared_down_codes);
+    a.sdown_meta = static_cast<const uint32_t*>(shared_down_meta);
+    a.shared_logit = static_cast<const uint16_t*>(shared_logit);
+    a.silu_table = static_cast<const float*>(shared_silu);
+    a.sigmoid_table = static_cast<const uint16_t*>(shared_sigmoid);
+    a.out = static_cast<uint16_t*>(output);
+    a.shared_out = static_cast<uint16_t*>(shared_output);
+    a.flags = static_cast<uint32_t*>(flags);
+    a.ws = static_cast<uint8_t*>(workspace);
+    a.L = w;
+    a.T = T;
+    a.a8 = 1;
+    a.shared = 1;
+    a.shared_all_live = 1;
+    return run_layer(a, stream);
+}
+
+uint32_t ornith_moe_b200_abi_version(void) { return 1; }
+
+unsigned long long ornith_moe_b200_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+cudaError_t ornith_moe_b200_route_topk(const void* logits, int T, void* weights, void* ids, void* flags,
+                                       cudaStream_t stream) {
+    if (T < 0 || T > kTcapMax) return cudaErrorInvalidValue;
+    if (!T) return cudaSuccess;
+    if (!logits || !weights || !ids || !flags || !aligned(logits, 4) || !aligned(weights, 4) || !aligned(ids, 4) ||
+        !aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    count_launches(1);
+    route_topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(static_cast<const float*>(logits), T,
+                                                        static_cast<float*>(weights), static_cast<int32_t*>(ids),
+                                                        static_cast<uint32_t*>(flags));
+    return cudaGetLastError();
+}
+
+cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes) {
+    if (!workspace_bytes || Tcap < 0 || Tcap > kTcapMax) return cudaErrorInvalidValue;
+    *workspace_bytes = workspace_layout(Tcap).bytes;
+    return cudaSuccess;
+}
+
+cudaError_t ornith_moe_b200_launch_from_logits(
+    const void* input, const void* logits, const void* gate_codes, const void* gate_meta, const void* down_codes,
+    const void* down_meta, const void* shared_gate_codes, const void* shared_gate_meta, const void* shared_down_codes,
+    const void* shared_down_meta, const void* shared_gate_weight, const void* shared_silu, const void* shared_sigmoid,
+    void* workspace, size_t bytes, void* output, void* shared_output, void* flags, int T, int Tcap, int act_bits,
+    cudaStream_t stream) {
+    if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap) return cudaErrorInvalidValue;
+    if (act_bits != 0 && act_bits != 4 && act_bits != 8) return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes) return cudaErrorInvalidValue;
+    const bool shared = shared_gate_codes || shared_gate_meta || shared_down_codes || shared_down_meta;
+    if (!T) return cudaSuccess;
+    if (!input || !logits || !gate_codes || !gate_meta || !down_codes || !down_meta || !workspace || !output || !flags)
+        return cudaErrorInvalidValue;
+    if (shared && (!shared_gate_codes || !shared_gate_meta || !shared_down_codes || !shared_down_meta ||
+                   !shared_gate_weight || !shared_silu || !shared_sigmoid || !shared_output))
+        return cudaErrorInvalidValue;
+    const int bits = act_bits == 0 ? (T > 64 ? 4 : 8) : act_bits;
+    if (shared && (bits != 8 || T > 64)) return cudaErrorInvalidValue;
+    if (!aligned(input, 16) || !aligned(output, 16) || !aligned(gate_codes, 16) || !aligned(gate_meta, 16) ||
+        !aligned(down_codes, 16) || !aligned(down_meta, 16) || !aligned(workspace, 256) || !aligned(logits, 4) ||
+        !aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    if (shared && (!aligned(shared_output, 16) || !aligned(shared_gate_codes, 16) || !aligned(shared_gate_meta, 16) ||
+                   !aligned(shared_down_codes, 16) || !aligned(shared_down_meta, 16) ||
+                   !aligned(shared_gate_weight, 2) || !aligned(shared_silu, 4) || !aligned(shared_sigmoid, 2)))
+        return cudaErrorInvalidValue;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* tw = reinterpret_cast<float*>(ws + w.topk_w);
+    int32_t* tid = reinterpret_cast<int32_t*>(ws + w.topk_ids);
+    count_launches(1);
+    route_topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(static_cast<const float*>(logits), T, tw, tid,
+                                                        static_cast<uint32_t*>(flags));
+    cudaError_t s = cudaGetLastError();
+    if (s != cudaSuccess) return s;
+    LayerArgs a{};
+    a.x = static_cast<const uint16_t*>(input);
+    a.weights = tw;
+    a.ids = tid;
+    a.gate_codes = static_cast<const uint32_t*>(gate_codes);
+    a.gate_meta = static_cast<const uint32_t*>(gate_meta);
+    a.down_codes = static_cast<const uint32_t*>(down_codes);
+    a.down_meta = static_cast<const uint32_t*>(down_meta);
+    a.out = static_cast<uint16_t*>(output);
+    a.flags = static_cast<uint32_t*>(flags);
+    a.ws = ws;
+    a.L = w;
+    a.T = T;
+    a.a8 = bits == 8;
+    if (shared) {
+        uint16_t* logit = reinterpret_cast<uint16_t*>(ws + w.logit);
+        count_launches(1);
+        shared_logit_kernel<<<(T + 7) / 8, 256, 0, stream>>>(a.x, static_cast<const uint16_t*>(shared_gate_weight), T,
+                                                             logit);
+        s = cudaGetLastError();
+        if (s != cudaSuccess) return s;
+        a.sgate_codes = static_cast<const uint32_t*>(shared_gate_codes);
+        a.sgate_meta = static_cast<const uint32_t*>(shared_gate_meta);
+        a.sdown_codes = static_cast<const uint32_t*>(shared_down_codes);
+        a.sdown_meta = static_cast<const uint32_t*>(shared_down_meta);
+        a.shared_logit = logit;
+        a.silu_table = static_cast<const float*>(shared_silu);
+        a.sigmoid_table = static_cast<const uint16_t*>(shared_sigmoid);
+        a.shared_out = static_cast<uint16_t*>(shared_output);
+        a.shared = 1;
+        a.shared_all_live = 1;
+    }
+    return run_layer(a, stream);
+}
+
+cudaError_t ornith_moe_b200_repack_n16_to_n32(const void* codes_n16, const void* meta_n16, void* codes_n32,
+                                              void* meta_n32, int experts, int N, int K, cudaStream_t stream) {
+    if (experts <= 0 || N <= 0 || N % 32 || K <= 0 || K % kG) return cudaErrorInvalidValue;
+    if (!codes_n16 || !meta_n16 || !codes_n32 || !meta_n32 || !aligned(codes_n16, 4) || !aligned(meta_n16, 4) ||
+        !aligned(codes_n32, 4) || !aligned(meta_n32, 4))
+        return cudaErrorInvalidValue;
+    const size_t code_bytes = size_t(experts) * N * K / 2, meta_bytes = size_t(experts) * N * (K / kG) * 4;
+    auto overlap = [](const void* a, size_t na, const void* b, size_t nb) {
+        uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+        return x < y + nb && y < x + na;
+    };
+    if (overlap(codes_n16, code_bytes, codes_n32, code_bytes) || overlap(meta_n16, meta_bytes, meta_n32, meta_bytes) ||
+        overlap(codes_n32, code_bytes, meta_n32, meta_bytes))
+        return cudaErrorInvalidValue;
+    const int groups = K / kG;
+    count_launches(2);
+    repack_codes_kernel<<<1184, 256, 0, stream>>>(static_cast<const uint32_t*>(codes_n16),
+                                                  static_cast<uint32_t*>(codes_n32), experts, N, groups);
+    cudaError_t s = cudaGetLastError();
+    if (s != cudaSuccess) return s;
+    repack_meta_kernel<<<296, 256, 0, stream>>>(static_cast<const uint32_t*>(meta_n16), static_cast<uint32_t*>(meta_n32),
+                                                experts, N, groups);
+    return cudaGetLastError();
+}
+
+}  // extern "C"

@@ -1,0 +1,227 @@
+// Shared device helpers of the B200 routed-MoE layer (sm_100a).
+//
+// The arithmetic here restates, operation for operation, the fixed-order
+// integer/fp32 pipeline of the reference's routed library
+// (kernels/routed_storage/routed_storage_n32_consumer.cpp of
+// ciru-ai/ornith-ciru-halo-agent) so that results are bit-identical:
+//   * bf16 round-to-nearest-even                     (:17-21)
+//   * 128-point Walsh-Hadamard butterfly x 0x3db504f3 (:22-43)
+//   * per-256-group A8/A4 activation quantisation      (:44-76)
+//   * per-group projection epilogue                    (:152-158)
+//   * SiLU with the reference's portable exp           (:168-175, portable_exp.h:6-25)
+// The library is compiled with -fmad=false so no fp32 step is contracted.
+//
+// Data layout choices that are B200-specific (not the reference's):
+//   * activations are int8 (one byte per element, 2048 B per token row), with
+//     each 8-element block stored as [q0 q2 q4 q6 | q1 q3 q5 q7] so that the
+//     even and odd nibbles of one packed weight word, masked to bytes, meet
+//     their activations in two __dp4a instructions;
+//   * one warp quantises one 256-group: lane l owns elements 8l..8l+7, the
+//     Hadamard steps 1,2,4 stay in registers and steps 8..64 are xor shuffles.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ornith {
+
+constexpr int kE = 256, kTop = 8, kH = 2048, kI = 512, kG = 256;
+constexpr int kTcapMax = 8192;
+constexpr float kInvSqrt128 = 0x1.6a09e6p-4f;  // 0x3db504f3
+
+// Sticky error bits (routed_storage_n32_consumer.cpp:33,51,58,86,115,174,183).
+enum : uint32_t {
+    kFlagNonfiniteInput = 1,
+    kFlagInvalidActivation = 2,
+    kFlagInvalidId = 4,
+    kFlagNonfiniteProjection = 8,
+    kFlagNonfiniteMiddle = 16,
+    kFlagNonfiniteOutput = 32,
+    kFlagWaitTimeout = 64,  // a bounded device wait gave up; results are incomplete
+};
+
+__device__ __forceinline__ uint16_t bf16_rne(float value) {
+    uint32_t bits = __float_as_uint(value);
+    if ((bits & 0x7fffffffu) > 0x7f800000u) return uint16_t((bits >> 16) | 0x40u);
+    return uint16_t((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
+}
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+__device__ __forceinline__ float bf16_round_f32(float v) { return bf16_to_f32(bf16_rne(v)); }
+
+// The reference's deterministic exponential (portable_exp.h:6-25): Cody-Waite
+// reduction n = rint(x*log2 e), two-part ln2, degree-8 Taylor in Horner form
+// evaluated without FMA, then ldexp.
+__device__ __forceinline__ float portable_exp(float x) {
+    if (isnan(x)) return x;
+    if (x <= -104.f) return 0.f;
+    if (x >= 89.f) return __int_as_float(0x7f800000);
+    const float n_float = rintf(__fmul_rn(x, 0x1.715476p+0f));
+    const int n = static_cast<int>(n_float);
+    const float high = __fmul_rn(n_float, 0x1.62e400p-1f);
+    const float low = __fmul_rn(n_float, 0x1.7f7d1cp-20f);
+    const float r = __fsub_rn(__fsub_rn(x, high), low);
+    float p = 0x1.a01a02p-16f;
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.a01a02p-13f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.6c16c2p-10f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.111112p-7f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.555556p-5f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.555556p-3f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1p-1f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1p+0f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1p+0f);
+    return ldexpf(p, n);
+}
+
+// Routed SiLU*up (middle_kernel): (g / (1 + exp(-g))) * up, IEEE division.
+__device__ __forceinline__ float silu_mul(float g, float up) {
+    float denominator = __fadd_rn(1.f, portable_exp(-g));
+    return __fmul_rn(__fdiv_rn(g, denominator), up);
+}
+
+// One projection epilogue step for a 256-group:
+// value + (w_scale*(sa*dot) + w_offset*(sa*sum)).
+__device__ __forceinline__ float group_term(float sa, int dot, int sum, uint32_t meta) {
+    float scaled_dot = __fmul_rn(sa, float(dot));
+    float scaled_sum = __fmul_rn(sa, float(sum));
+    float w_scale = __half2float(__ushort_as_half(uint16_t(meta & 0xffffu)));
+    float w_offset = __half2float(__ushort_as_half(uint16_t(meta >> 16)));
+    return __fadd_rn(__fmul_rn(w_scale, scaled_dot), __fmul_rn(w_offset, scaled_sum));
+}
+
+// In-register 128-point Hadamard over a half-warp: lane l (0..15 within its
+// half) holds elements 8l..8l+7 of one 128-block.  Stage order and operand
+// order are those of the reference's shared-memory butterfly.
+__device__ __forceinline__ void wht128_halfwarp(float (&e)[8], int lane) {
+#pragma unroll
+    for (int step = 1; step < 8; step *= 2) {
+        float n[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            int lo = s & ~step;
+            n[s] = (s & step) ? __fsub_rn(e[lo], e[lo + step]) : __fadd_rn(e[lo], e[lo + step]);
+        }
+#pragma unroll
+        for (int s = 0; s < 8; ++s) e[s] = n[s];
+    }
+#pragma unroll
+    for (int lstep = 1; lstep < 16; lstep *= 2) {
+        const bool upper = (lane & lstep) != 0;
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            float other = __shfl_xor_sync(0xffffffffu, e[s], lstep);
+            e[s] = upper ? __fsub_rn(other, e[s]) : __fadd_rn(e[s], other);
+        }
+    }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) e[s] = __fmul_rn(e[s], kInvSqrt128);
+}
+
+// Quantise one 256-group held by a warp (8 elements per lane, already
+// Hadamard-transformed).  Writes the permuted int8 words for lane l's 8
+// elements (word pair index l), and returns scale/sum through lane 0.
+// routed_storage_n32_consumer.cpp:44-76.
+template <int QMAX>
+__device__ __forceinline__ void quantize_group_warp(const float (&t)[8], int lane, uint2* q_out,
+                                                    __half* scale_out, int32_t* sum_out, uint32_t& flags) {
+    float v[8], absmax = 0.f;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        bool finite = isfinite(t[s]);
+        if (!finite) flags |= kFlagInvalidActivation;
+        v[s] = finite ? t[s] : 0.f;
+        absmax = fmaxf(absmax, fabsf(v[s]));
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) absmax = fmaxf(absmax, __shfl_xor_sync(0xffffffffu, absmax, d));
+    float raw = __fdiv_rn(absmax, float(QMAX));
+    bool valid = isfinite(raw) && raw <= 65504.f;
+    if (!valid) flags |= kFlagInvalidActivation;
+    const bool zero = absmax == 0.f || !valid;
+    __half scale = __float2half_rn(zero ? 1.f : fmaxf(raw, 0x1p-14f));
+    float sf = __half2float(scale);
+    int q[8], sum = 0;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        int qi = zero ? 0 : __float2int_rn(__fdiv_rn(v[s], sf));
+        qi = qi < -QMAX ? -QMAX : (qi > QMAX ? QMAX : qi);
+        q[s] = qi;
+        sum += qi;
+    }
+    uint32_t even = (uint32_t(q[0]) & 0xffu) | ((uint32_t(q[2]) & 0xffu) << 8) |
+                    ((uint32_t(q[4]) & 0xffu) << 16) | ((uint32_t(q[6]) & 0xffu) << 24);
+    uint32_t odd = (uint32_t(q[1]) & 0xffu) | ((uint32_t(q[3]) & 0xffu) << 8) |
+                   ((uint32_t(q[5]) & 0xffu) << 16) | ((uint32_t(q[7]) & 0xffu) << 24);
+    q_out[lane] = make_uint2(even, odd);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    if (lane == 0) {
+        *scale_out = scale;
+        *sum_out = sum;
+    }
+}
+
+// Integer dot of one packed weight word (8 u4 codes, k = 8j+d at bits 4d) with
+// its 8 activations in the permuted [even | odd] int8 layout.
+__device__ __forceinline__ int dot8(uint32_t w, uint2 a, int acc) {
+    int lo = int(w & 0x0f0f0f0fu);
+    int hi = int((w >> 4) & 0x0f0f0f0fu);
+    acc = __dp4a(lo, int(a.x), acc);
+    return __dp4a(hi, int(a.y), acc);
+}
+
+__device__ __forceinline__ bool id_valid(int id) { return id >= 0 && id < kE; }
+
+// ---------------------------------------------------------------------------
+// PTX wrappers: mbarriers and bulk (non-tensor) global->shared copies.
+// No cluster multicast anywhere in this library.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bulk copy global -> this CTA's shared memory, completing on `bar`.
+// dst/src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded waits: every spin in this library gives up after about a second,
+// raises kFlagWaitTimeout and lets the kernel wind down.
+constexpr uint32_t kSpinLimit = 1u << 23;
+
+}  // namespace ornith

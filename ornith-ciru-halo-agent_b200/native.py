@@ -1,0 +1,247 @@
+"""ctypes binding of libornith_moe_b200.so and the torch custom operators.
+
+Mirrors the reference plugin's binding (plugin-site/ornith_g256/native.py):
+  * `configure(settings, capacity)` checks the routed activation settings the
+    way native.py:28-44 does and selects the launch symbol
+    (`ornith_routed_direct_launch`, `_a4` or `_a4_prefill`);
+  * `ornith_b200::routed_out` has the argument order, validation and mutation
+    set of `ornith_g256::routed_out` (native.py:156-186), including the
+    per-phase segmentation of mixed prefill/decode batches;
+  * `ornith_b200::routed_shared_out` is the fused shared-slot launch that
+    moe_shared.py:130-174 drives;
+  * `ornith_b200::routed_from_logits` is the north-star operator (hidden
+    states + router logits -> combined hidden states).
+All launches go to the caller's current CUDA stream.  There is no CPU
+fallback: every operator raises if the CUDA library is missing.
+"""
+import ctypes as C
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / 'libornith_moe_b200.so'
+
+_lib = None
+_PHASE_SEGMENTS = ()
+_SETTINGS = {'launch': 'ornith_routed_direct_launch'}
+
+
+class RoutedLayout(C.Structure):
+    """OrnithRoutedDirectLayout (include/ornith_moe_b200.h; reference native.py:16-20)."""
+    _fields_ = [(n, C.c_size_t) for n in
+                ('workspace_bytes', 'gate_x', 'gate_low', 'gate_high', 'gate_scales',
+                 'gate_sums', 'gate_y', 'middle', 'down_x', 'down_low', 'down_high',
+                 'down_scales', 'down_sums', 'route_out', 'final_f32')]
+
+
+_LAUNCH_ARGS = [C.c_void_p] * 8 + [C.c_size_t] + [C.c_void_p] * 2 + [C.c_int] * 2 + [C.c_void_p]
+SIGNATURES = {
+    'ornith_routed_direct_get_layout': ([C.c_int, C.POINTER(RoutedLayout)], C.c_int),
+    'ornith_routed_direct_launch': (_LAUNCH_ARGS, C.c_int),
+    'ornith_routed_direct_launch_a4': (_LAUNCH_ARGS, C.c_int),
+    'ornith_routed_direct_launch_a4_prefill': (_LAUNCH_ARGS, C.c_int),
+    'ornith_routed_storage_n32': ([], C.c_int),
+    'ornith_routed_prefill_output_tile': ([], C.c_int),
+    'ornith_routed_shared_get_layout': ([C.c_int, C.POINTER(RoutedLayout)], C.c_int),
+    'ornith_routed_direct_launch_shared_tables': (
+        [C.c_void_p] * 15 + [C.c_size_t] + [C.c_void_p] * 3 + [C.c_int] * 2 + [C.c_void_p], C.c_int),
+    'ornith_moe_b200_abi_version': ([], C.c_uint32),
+    'ornith_moe_b200_kernel_launches': ([], C.c_ulonglong),
+    'ornith_moe_b200_route_topk': ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
+    'ornith_moe_b200_launch_from_logits': (
+        [C.c_void_p] * 14 + [C.c_size_t] + [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
+    'ornith_moe_b200_get_layout': ([C.c_int, C.POINTER(C.c_size_t)], C.c_int),
+    'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
+}
+
+
+def lib():
+    """Load the CUDA library (raises if it was not built: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f'{LIB_PATH} is missing: build it with `python {HERE / "build.py"}` '
+                               '(or __graft_entry__.build()); the MoE operators have no CPU fallback')
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes, fn.restype = args, res
+        if handle.ornith_routed_storage_n32() != 32:
+            raise RuntimeError('Sole N32 storage requires the full N32 consumer')
+        _lib = handle
+    return _lib
+
+
+def ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else C.c_void_p(0)
+
+
+def stream(x):
+    return C.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+
+
+def check(status, operation):
+    if status:
+        raise RuntimeError(f'{operation} failed with native status {status}')
+
+
+def get_layout(capacity):
+    layout = RoutedLayout()
+    check(lib().ornith_routed_direct_get_layout(capacity, C.byref(layout)), 'routed layout')
+    return layout
+
+
+def workspace_bytes(capacity):
+    n = C.c_size_t()
+    check(lib().ornith_moe_b200_get_layout(capacity, C.byref(n)), 'layout')
+    return max(n.value, get_layout(capacity).workspace_bytes)
+
+
+def configure(settings, capacity):
+    """Select the routed launch symbol from the plugin settings (native.py:28-44)
+    and return the workspace bytes for `capacity` rows."""
+    bits = settings.get('routed_activation_bits', 8)
+    prefill_bits = settings.get('routed_prefill_activation_bits', 8)
+    if bits not in (4, 8) or prefill_bits not in (4, 8):
+        raise ValueError('G256 routed activation bits must be 4 or 8')
+    if bits == prefill_bits == 4:
+        raise ValueError('Choose either global routed A4 or prefill-only routed A4')
+    suffix = '_a4' if bits == 4 else '_a4_prefill' if prefill_bits == 4 else ''
+    _SETTINGS['launch'] = 'ornith_routed_direct_launch' + suffix
+    return workspace_bytes(capacity)
+
+
+def set_phase_segments(segments):
+    """Mixed prefill/decode segmentation (phase_dispatch.py:13-34): a tuple of
+    (start, end, prefill) row ranges; prefill segments use A4, decode ones A8."""
+    global _PHASE_SEGMENTS
+    _PHASE_SEGMENTS = tuple((int(a), int(b), bool(p)) for a, b, p in segments)
+
+
+def validate(x, out, capacity, k):
+    if (x.ndim != 2 or x.shape[1] != k or not 0 <= x.shape[0] <= capacity
+            or x.dtype != torch.bfloat16 or x.device.type != 'cuda'
+            or out.dtype != x.dtype or out.device != x.device
+            or not x.is_contiguous() or not out.is_contiguous()):
+        raise ValueError('Native G256 requires contiguous BF16 input/output within capacity')
+
+
+def _validate_routes(x, routes, ids):
+    if (routes.dtype != torch.float32 or ids.dtype != torch.int32
+            or routes.shape != (x.shape[0], 8) or ids.shape != routes.shape
+            or routes.device != x.device or ids.device != x.device
+            or not routes.is_contiguous() or not ids.is_contiguous()):
+        raise ValueError('G256 routed input requires FP32 weights and INT32 IDs [T,8]')
+
+
+def _routed_launch(symbol, x, routes, ids, gate, gate_meta, down, down_meta, workspace, out, flags, capacity):
+    validate(x, out, capacity, 2048)
+    _validate_routes(x, routes, ids)
+    fn = getattr(lib(), symbol)
+    check(fn(*[ptr(t) for t in (x, routes, ids, gate, gate_meta, down, down_meta, workspace)],
+             workspace.numel(), ptr(out), ptr(flags), x.shape[0], capacity, stream(x)), 'G256 ' + symbol)
+
+
+@torch.library.custom_op('ornith_b200::routed_out', mutates_args={'workspace', 'out', 'flags'}, device_types='cuda')
+def routed_out(x: torch.Tensor, routes: torch.Tensor, ids: torch.Tensor,
+               gate: torch.Tensor, gate_meta: torch.Tensor, down: torch.Tensor, down_meta: torch.Tensor,
+               workspace: torch.Tensor, out: torch.Tensor, flags: torch.Tensor, capacity: int) -> None:
+    if _PHASE_SEGMENTS and x.shape[0] >= _PHASE_SEGMENTS[-1][1]:
+        segments = list(_PHASE_SEGMENTS)
+        if segments[-1][1] < x.shape[0]:
+            segments.append((segments[-1][1], x.shape[0], True))
+        for start, end, prefill in segments:
+            symbol = 'ornith_routed_direct_launch_a4' if prefill else 'ornith_routed_direct_launch'
+            _routed_launch(symbol, x[start:end], routes[start:end], ids[start:end], gate, gate_meta, down,
+                           down_meta, workspace, out[start:end], flags, capacity)
+        return
+    _routed_launch(_SETTINGS['launch'], x, routes, ids, gate, gate_meta, down, down_meta, workspace, out, flags,
+                   capacity)
+
+
+@routed_out.register_fake
+def _routed_fake(x, routes, ids, gate, gate_meta, down, down_meta, workspace, out, flags, capacity):
+    return None
+
+
+@torch.library.custom_op('ornith_b200::routed_shared_out',
+                         mutates_args={'workspace', 'out', 'shared_out', 'flags'}, device_types='cuda')
+def routed_shared_out(x: torch.Tensor, routes: torch.Tensor, ids: torch.Tensor,
+                      gate: torch.Tensor, gate_meta: torch.Tensor, down: torch.Tensor, down_meta: torch.Tensor,
+                      shared_gate: torch.Tensor, shared_gate_meta: torch.Tensor,
+                      shared_down: torch.Tensor, shared_down_meta: torch.Tensor,
+                      logit: torch.Tensor, silu_table: torch.Tensor, sigmoid_table: torch.Tensor,
+                      workspace: torch.Tensor, out: torch.Tensor, shared_out: torch.Tensor,
+                      flags: torch.Tensor, capacity: int) -> None:
+    validate(x, out, capacity, 2048)
+    validate(x, shared_out, capacity, 2048)
+    _validate_routes(x, routes, ids)
+    if (silu_table.dtype != torch.float32 or sigmoid_table.dtype != torch.bfloat16
+            or silu_table.shape != (65536,) or sigmoid_table.shape != (65536,)
+            or logit.dtype != torch.bfloat16 or logit.numel() != x.shape[0]):
+        raise ValueError('Invalid shared reference table geometry')
+    check(lib().ornith_routed_direct_launch_shared_tables(
+        *[ptr(t) for t in (x, routes, ids, gate, gate_meta, down, down_meta, shared_gate, shared_gate_meta,
+                           shared_down, shared_down_meta, logit, silu_table, sigmoid_table, workspace)],
+        workspace.numel(), ptr(out), ptr(shared_out), ptr(flags), x.shape[0], capacity, stream(x)),
+        'G256 routed shared')
+
+
+@routed_shared_out.register_fake
+def _routed_shared_fake(x, routes, ids, gate, gate_meta, down, down_meta, shared_gate, shared_gate_meta,
+                        shared_down, shared_down_meta, logit, silu_table, sigmoid_table, workspace, out,
+                        shared_out, flags, capacity):
+    return None
+
+
+@torch.library.custom_op('ornith_b200::route_topk', mutates_args={'weights', 'ids', 'flags'}, device_types='cuda')
+def route_topk(logits: torch.Tensor, weights: torch.Tensor, ids: torch.Tensor, flags: torch.Tensor) -> None:
+    if (logits.dtype != torch.float32 or logits.ndim != 2 or logits.shape[1] != 256 or not logits.is_contiguous()
+            or weights.shape != (logits.shape[0], 8) or ids.shape != weights.shape
+            or weights.dtype != torch.float32 or ids.dtype != torch.int32):
+        raise ValueError('route_topk requires FP32 logits [T,256] and [T,8] outputs')
+    check(lib().ornith_moe_b200_route_topk(ptr(logits), logits.shape[0], ptr(weights), ptr(ids), ptr(flags),
+                                           stream(logits)), 'route_topk')
+
+
+@route_topk.register_fake
+def _route_topk_fake(logits, weights, ids, flags):
+    return None
+
+
+@torch.library.custom_op('ornith_b200::routed_from_logits',
+                         mutates_args={'workspace', 'out', 'shared_out', 'flags'}, device_types='cuda')
+def routed_from_logits(x: torch.Tensor, logits: torch.Tensor,
+                       gate: torch.Tensor, gate_meta: torch.Tensor, down: torch.Tensor, down_meta: torch.Tensor,
+                       shared_gate: torch.Tensor | None, shared_gate_meta: torch.Tensor | None,
+                       shared_down: torch.Tensor | None, shared_down_meta: torch.Tensor | None,
+                       shared_gate_weight: torch.Tensor | None, silu_table: torch.Tensor | None,
+                       sigmoid_table: torch.Tensor | None, workspace: torch.Tensor, out: torch.Tensor,
+                       shared_out: torch.Tensor | None, flags: torch.Tensor, capacity: int, act_bits: int) -> None:
+    validate(x, out, capacity, 2048)
+    if logits.dtype != torch.float32 or logits.shape != (x.shape[0], 256) or not logits.is_contiguous():
+        raise ValueError('routed_from_logits requires FP32 router logits [T,256]')
+    check(lib().ornith_moe_b200_launch_from_logits(
+        *[ptr(t) for t in (x, logits, gate, gate_meta, down, down_meta, shared_gate, shared_gate_meta,
+                           shared_down, shared_down_meta, shared_gate_weight, silu_table, sigmoid_table,
+                           workspace)],
+        workspace.numel(), ptr(out), ptr(shared_out), ptr(flags), x.shape[0], capacity, act_bits, stream(x)),
+        'routed_from_logits')
+
+
+@routed_from_logits.register_fake
+def _routed_from_logits_fake(x, logits, gate, gate_meta, down, down_meta, shared_gate, shared_gate_meta,
+                             shared_down, shared_down_meta, shared_gate_weight, silu_table, sigmoid_table,
+                             workspace, out, shared_out, flags, capacity, act_bits):
+    return None
+
+
+def repack_n16_to_n32(codes16, meta16, N, K):
+    """Device repack of checkpoint N16 banks to N32 storage (method.py:124-158)."""
+    e = codes16.shape[0]
+    codes32 = torch.empty((e, N // 32, K // 256, 32, 32), dtype=torch.uint32, device=codes16.device)
+    meta32 = torch.empty((e, N // 32, K // 256, 32), dtype=torch.uint32, device=codes16.device)
+    check(lib().ornith_moe_b200_repack_n16_to_n32(ptr(codes16.contiguous()), ptr(meta16.contiguous()),
+                                                  ptr(codes32), ptr(meta32), e, N, K, stream(codes16)), 'repack')
+    return codes32, meta32

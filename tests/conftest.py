@@ -1,0 +1,58 @@
+"""Shared fixtures.  GPU tests carry @pytest.mark.gpu; everything else runs on CPU."""
+import importlib
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+import __graft_entry__ as graft  # noqa: E402
+
+graft.load_package()
+GOLDEN = ROOT / 'tests' / 'golden'
+
+
+def pytest_configure(config):
+    config.addinivalue_line('markers', 'gpu: needs a CUDA device (B200)')
+
+
+@pytest.fixture(scope='session')
+def S():
+    return importlib.import_module('ornith_b200.synthetic')
+
+
+@pytest.fixture(scope='session')
+def O():
+    from oracle import oracle
+    return oracle
+
+
+@pytest.fixture(scope='session')
+def native():
+    return importlib.import_module('ornith_b200.native')
+
+
+@pytest.fixture(scope='session')
+def golden():
+    return np.load(GOLDEN / 'routed_reference_outputs.npz')
+
+
+@pytest.fixture(scope='session')
+def tables():
+    return np.load(GOLDEN / 'shared_math_tables.npz')
+
+
+@pytest.fixture(scope='session')
+def make_golden():
+    spec = importlib.util.spec_from_file_location('make_golden', GOLDEN / 'make_golden.py')
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.fixture(scope='session')
+def layer1(S):
+    """The layer every golden case uses (seed 1)."""
+    return S.make_layer(np.random.default_rng(1))

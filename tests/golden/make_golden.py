@@ -1,0 +1,146 @@
+"""Regenerate the committed golden fixtures (run in the build container only).
+
+  shared_math_tables.npz
+      The reference's pinned SiLU fp32 / sigmoid bf16 tables for every bf16
+      bit pattern (native/shared_math_reference.safetensors), copied after
+      checking the sha256 recorded in native/shared_math_reference.json.
+  routed_reference_outputs.npz
+      Outputs of the reference's own routed library (kernels/routed_storage/,
+      compiled for the CPU by oracle/build_ref.py) on seeded synthetic cases.
+      Inputs are not stored: each case is regenerated from its seed by the
+      synthetic generator, and the sha256 of the regenerated inputs is stored
+      so that generator drift is detected.
+
+Usage: python tests/golden/make_golden.py [--reference /path/to/reference]
+"""
+import argparse
+import hashlib
+import importlib.util
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+from oracle import oracle as O  # noqa: E402
+
+OUT = Path(__file__).resolve().parent
+
+
+def _synthetic():
+    spec = importlib.util.spec_from_file_location('ornith_synthetic', ROOT / 'ornith-ciru-halo-agent_b200' / 'synthetic.py')
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+# (name, layer seed, case seed, T, pad fraction, hot experts with +6 bias, entry, special)
+CASES = [
+    ('t1_a8', 1, 11, 1, 0.0, 0, 'ornith_routed_direct_launch', ''),
+    ('t3_a8_pad', 1, 12, 3, 0.2, 0, 'ornith_routed_direct_launch', ''),
+    ('t8_a4', 1, 13, 8, 0.1, 0, 'ornith_routed_direct_launch_a4', ''),
+    ('t16_a8', 1, 14, 16, 0.1, 0, 'ornith_routed_direct_launch', ''),
+    ('t17_a8_grouped', 1, 15, 17, 0.05, 12, 'ornith_routed_direct_launch', ''),
+    ('t33_a4_grouped', 1, 16, 33, 0.05, 12, 'ornith_routed_direct_launch_a4', ''),
+    ('t65_a4prefill', 1, 17, 65, 0.05, 24, 'ornith_routed_direct_launch_a4_prefill', ''),
+    ('t5_a8_edges', 1, 18, 5, 0.0, 0, 'ornith_routed_direct_launch', 'edges'),
+]
+
+
+def make_case(S, layer, case_seed, T, pad, hot, special):
+    rng = np.random.default_rng(case_seed)
+    x = S.make_tokens(rng, T)
+    bias = None
+    if hot:
+        bias = np.zeros(S.E, np.float32)
+        bias[:hot] = 6.0
+    w, ids = S.random_routes(rng, T, pad_fraction=pad, bias=bias)
+    if special == 'edges':
+        # token 0: all-zero row (zero groups -> scale 1); token 1: one huge
+        # element saturating its group; token 2: all ids padded (-1) -> zero
+        # output; token 3: one invalid id 300 (flag 4) and one -5 (flag 4);
+        # token 4: a NaN input element (flags 1/2 and propagation).
+        x[0, :] = 0
+        x[1, 7] = S.f32_to_bf16_bits(np.array([3.0e4], np.float32))[0]
+        ids[2, :] = -1
+        ids[3, 2] = 300
+        ids[3, 5] = -5
+        x[4, 100] = 0x7FC0
+    return x, w, ids
+
+
+def digest(*arrays):
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument('--reference', default='/root/reference')
+    args = parser.parse_args()
+    ref = Path(args.reference)
+    import torch
+    from safetensors.torch import load_file
+
+    tables_path = ref / 'native' / 'shared_math_reference.safetensors'
+    receipt = json.loads((ref / 'native' / 'shared_math_reference.json').read_text())
+    sha = hashlib.sha256(tables_path.read_bytes()).hexdigest()
+    if sha != receipt['sha256']:
+        raise SystemExit('shared math table sha256 differs from the reference receipt')
+    t = load_file(str(tables_path))
+    silu = t['silu_fp32'].numpy()
+    sigmoid = t['sigmoid_bf16'].view(torch.int16).numpy().view(np.uint16)
+    np.savez_compressed(OUT / 'shared_math_tables.npz', silu_fp32=silu, sigmoid_bf16=sigmoid,
+                        source_sha256=np.array(sha))
+
+    S = _synthetic()
+    layer = S.make_layer(np.random.default_rng(1))
+    banks = (layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta)
+    sbanks = (layer.sgate_codes, layer.sgate_meta, layer.sdown_codes, layer.sdown_meta)
+    store = {'layer_seed': np.array(1), 'layer_sha256': np.array(digest(*banks, *sbanks, layer.shared_gate_w))}
+    for name, _, case_seed, T, pad, hot, entry, special in CASES:
+        x, w, ids = make_case(S, layer, case_seed, T, pad, hot, special)
+        out, final, flags, st = O.ref_routed(x, w, ids, *banks, entry=entry)
+        assert st == 0, (name, st)
+        store[f'{name}/inputs_sha256'] = np.array(digest(x, w, ids))
+        store[f'{name}/out'] = out
+        if T <= 5:
+            store[f'{name}/final_f32'] = final
+        store[f'{name}/flags'] = np.array(flags, np.uint32)
+        print(name, 'flags', flags)
+    # fused shared slot (T <= 16) with the reference's tables
+    for name, case_seed, T in (('shared_t1', 21, 1), ('shared_t7', 22, 7), ('shared_t16', 23, 16)):
+        x, w, ids = make_case(S, layer, case_seed, T, 0.1, 0, '')
+        logit = S.f32_to_bf16_bits(np.random.default_rng(case_seed + 100).standard_normal(T).astype(np.float32))
+        out, shared, flags, st = O.ref_routed_shared(x, w, ids, *banks, *sbanks, logit, silu, sigmoid)
+        assert st == 0
+        store[f'{name}/inputs_sha256'] = np.array(digest(x, w, ids, logit))
+        store[f'{name}/out'] = out
+        store[f'{name}/shared_out'] = shared
+        store[f'{name}/flags'] = np.array(flags, np.uint32)
+        print(name, 'flags', flags)
+    # configuration 1 of the benchmark: T=4, router linear, seed 0
+    x, router, l1 = S.config1(0)
+    logits = O.router_logits(x, router)
+    w, ids = O.route_topk(logits)
+    b1 = (l1.gate_codes, l1.gate_meta, l1.down_codes, l1.down_meta)
+    store['config1/layer_sha256'] = np.array(digest(*b1, l1.sgate_codes, l1.sgate_meta, l1.sdown_codes,
+                                                    l1.sdown_meta, l1.shared_gate_w))
+    store['config1/logits'] = logits
+    store['config1/ids'] = ids
+    store['config1/weights'] = w
+    for entry, key in (('ornith_routed_direct_launch', 'a8'), ('ornith_routed_direct_launch_a4', 'a4')):
+        out, final, flags, st = O.ref_routed(x, w, ids, *b1, entry=entry)
+        assert st == 0
+        store[f'config1/out_{key}'] = out
+        store[f'config1/flags_{key}'] = np.array(flags, np.uint32)
+    np.savez_compressed(OUT / 'routed_reference_outputs.npz', **store)
+    print('wrote', OUT / 'routed_reference_outputs.npz')
+
+
+if __name__ == '__main__':
+    main()

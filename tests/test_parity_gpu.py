@@ -1,0 +1,236 @@
+"""GPU parity: the CUDA path through the C ABI against the golden vectors
+(outputs of the reference's own routed source) and the CPU oracle.
+Bit-exact for outputs, fp32 diagnostics, ids, routing weights and flags."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device('cuda:0')
+
+
+def dev(a):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).to(DEV).view(torch.bfloat16)
+    if a.dtype == np.uint32:
+        return torch.from_numpy(a.view(np.int32)).to(DEV).view(torch.uint32)
+    return torch.from_numpy(a).to(DEV)
+
+
+def host_bits(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+class Bank:
+    def __init__(self, layer):
+        self.routed = [dev(b) for b in (layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta)]
+        self.shared = [dev(b) for b in (layer.sgate_codes, layer.sgate_meta, layer.sdown_codes, layer.sdown_meta)]
+        self.np_routed = (layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta)
+        self.np_shared = (layer.sgate_codes, layer.sgate_meta, layer.sdown_codes, layer.sdown_meta)
+        self.gate_w = layer.shared_gate_w
+
+
+@pytest.fixture(scope='module')
+def bank1(layer1):
+    return Bank(layer1)
+
+
+def run_entry(native, symbol, x, w, ids, bank, Tcap=None):
+    T = x.shape[0]
+    Tcap = T if Tcap is None else Tcap
+    ws = torch.empty(native.get_layout(Tcap).workspace_bytes, dtype=torch.uint8, device=DEV)
+    out = torch.full((max(T, 1), 2048), -1, dtype=torch.int16, device=DEV).view(torch.bfloat16)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    fn = getattr(native.lib(), symbol)
+    st = fn(*[native.ptr(t) for t in (dev(x), dev(w), dev(ids), *bank.routed, ws)], ws.numel(),
+            native.ptr(out), native.ptr(flags), T, Tcap, native.stream(out))
+    torch.cuda.synchronize()
+    assert st == 0
+    layout = native.get_layout(Tcap)
+    final = ws[layout.final_f32:layout.final_f32 + T * 2048 * 4].view(torch.float32).view(T, 2048).cpu().numpy()
+    return host_bits(out)[:T], final, int(flags.item())
+
+
+def test_golden_cases_bit_exact(native, golden, layer1, bank1, make_golden, S):
+    for name, _, seed, T, pad, hot, entry, special in make_golden.CASES:
+        x, w, ids = make_golden.make_case(S, layer1, seed, T, pad, hot, special)
+        out, final, flags = run_entry(native, entry, x, w, ids, bank1)
+        np.testing.assert_array_equal(out, golden[f'{name}/out'], err_msg=name)
+        assert flags == int(golden[f'{name}/flags']), name
+        if f'{name}/final_f32' in golden:
+            np.testing.assert_array_equal(final.view(np.uint32), golden[f'{name}/final_f32'].view(np.uint32))
+
+
+@pytest.mark.parametrize('T', [1, 2, 4, 5, 8, 13, 16, 17, 24, 31, 32, 33, 48, 64, 65, 100, 256])
+@pytest.mark.parametrize('a8', [True, False])
+def test_random_batches_vs_oracle(native, layer1, bank1, S, O, T, a8):
+    rng = np.random.default_rng(1000 + T + (7 if a8 else 0))
+    x = S.make_tokens(rng, T)
+    bias = np.zeros(256, np.float32)
+    bias[rng.integers(0, 256, 6)] = 3.0
+    w, ids = S.random_routes(rng, T, pad_fraction=0.08, bias=bias)
+    ref, ref_f32, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=a8)
+    symbol = 'ornith_routed_direct_launch' if a8 else 'ornith_routed_direct_launch_a4'
+    out, final, flags = run_entry(native, symbol, x, w, ids, bank1, Tcap=T + 3)
+    np.testing.assert_array_equal(out, ref)
+    np.testing.assert_array_equal(final.view(np.uint32), ref_f32.view(np.uint32))
+    assert flags == ref_flags
+
+
+def test_a4_prefill_switches_at_64(native, layer1, bank1, S, O):
+    for T, a8 in ((64, True), (65, False)):
+        rng = np.random.default_rng(T)
+        x = S.make_tokens(rng, T)
+        w, ids = S.random_routes(rng, T)
+        ref, _, _ = O.routed_layer(x, w, ids, *bank1.np_routed, a8=a8)
+        out, _, _ = run_entry(native, 'ornith_routed_direct_launch_a4_prefill', x, w, ids, bank1)
+        np.testing.assert_array_equal(out, ref)
+
+
+def test_shared_slot_golden(native, golden, layer1, bank1, make_golden, S, tables):
+    silu, sigmoid = dev(tables['silu_fp32']), dev(tables['sigmoid_bf16'])
+    for name, seed, T in (('shared_t1', 21, 1), ('shared_t7', 22, 7), ('shared_t16', 23, 16)):
+        x, w, ids = make_golden.make_case(S, layer1, seed, T, 0.1, 0, '')
+        logit = S.f32_to_bf16_bits(np.random.default_rng(seed + 100).standard_normal(T).astype(np.float32))
+        ws = torch.empty(native.get_layout(16).workspace_bytes, dtype=torch.uint8, device=DEV)
+        out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+        shared = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+        flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+        native.routed_shared_out(dev(x), dev(w), dev(ids), *bank1.routed, *bank1.shared, dev(logit), silu,
+                                 sigmoid, ws, out, shared, flags, 16)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(host_bits(out), golden[f'{name}/out'])
+        np.testing.assert_array_equal(host_bits(shared), golden[f'{name}/shared_out'])
+        assert int(flags.item()) == int(golden[f'{name}/flags'])
+
+
+def test_route_topk_bit_exact(native, O):
+    rng = np.random.default_rng(3)
+    logits = rng.standard_normal((777, 256)).astype(np.float32)
+    logits[0, 10] = logits[0, 20] = 9.0
+    logits[1, :] = -np.inf
+    logits[1, 5] = 1.0
+    logits[2, 7] = np.nan
+    w_ref, ids_ref = O.route_topk(logits)
+    w = torch.empty((777, 8), dtype=torch.float32, device=DEV)
+    ids = torch.empty((777, 8), dtype=torch.int32, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    native.route_topk(dev(logits), w, ids, flags)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref)
+    np.testing.assert_array_equal(w.cpu().numpy().view(np.uint32), w_ref.view(np.uint32))
+    assert int(flags.item()) == 1
+
+
+def test_config1_from_logits(native, golden, S):
+    x, router, l1 = S.config1(0)
+    bank = Bank(l1)
+    logits = golden['config1/logits']
+    T = 4
+    for key, bits in (('a8', 8), ('a4', 4)):
+        ws = torch.empty(native.workspace_bytes(T), dtype=torch.uint8, device=DEV)
+        out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+        flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+        native.routed_from_logits(dev(x), dev(logits), *bank.routed, None, None, None, None, None, None, None,
+                                  ws, out, None, flags, T, bits)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(host_bits(out), golden[f'config1/out_{key}'])
+        assert int(flags.item()) == int(golden[f'config1/flags_{key}'])
+
+
+def shared_logit_like_device(x_bits, w_bits):
+    """The device's fixed-order fp32 logit: lane partial sums over k = lane + 32i,
+    then an xor tree over the 32 lanes, rounded to bf16."""
+    from ornith_b200.synthetic import bf16_bits_to_f32, f32_to_bf16_bits
+    x = bf16_bits_to_f32(x_bits).reshape(-1, 2048)
+    w = bf16_bits_to_f32(w_bits)
+    out = []
+    for row in x:
+        lanes = np.zeros(32, np.float32)
+        for i in range(64):
+            k = np.arange(32) + 32 * i
+            lanes = (lanes + (row[k] * w[k]).astype(np.float32)).astype(np.float32)
+        d = 16
+        while d:
+            lanes = (lanes + lanes[np.arange(32) ^ d]).astype(np.float32)
+            d >>= 1
+        out.append(lanes[0])
+    return f32_to_bf16_bits(np.array(out, np.float32))
+
+
+@pytest.mark.parametrize('T', [1, 6, 16, 40])
+def test_from_logits_with_shared_expert(native, layer1, bank1, S, O, tables, T):
+    rng = np.random.default_rng(50 + T)
+    x = S.make_tokens(rng, T)
+    logits = rng.standard_normal((T, 256)).astype(np.float32)
+    w, ids = O.route_topk(logits)
+    logit = shared_logit_like_device(x, bank1.gate_w)
+    ref, ref_sh, _, ref_flags = O.routed_layer_shared(x, w, ids, *bank1.np_routed, *bank1.np_shared, logit,
+                                                      tables['silu_fp32'], tables['sigmoid_bf16'])
+    ws = torch.empty(native.workspace_bytes(T), dtype=torch.uint8, device=DEV)
+    out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    shared = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    native.routed_from_logits(dev(x), dev(logits), *bank1.routed, *bank1.shared, dev(bank1.gate_w),
+                              dev(tables['silu_fp32']), dev(tables['sigmoid_bf16']), ws, out, shared, flags, T, 0)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host_bits(out), ref)
+    np.testing.assert_array_equal(host_bits(shared), ref_sh)
+    assert int(flags.item()) == ref_flags
+
+
+def test_flags_and_edges_vs_oracle(native, layer1, bank1, S, O):
+    rng = np.random.default_rng(77)
+    T = 6
+    x = S.make_tokens(rng, T)
+    w, ids = S.random_routes(rng, T)
+    x[0, 5] = 0x7F80            # +inf input
+    x[1, :] = 0                 # zero row
+    ids[2, :] = -1              # dead token
+    ids[3, 1] = 256             # invalid id (flag 4)
+    x[4, :256] = 0x7F00         # huge values: bf16 1.7e38 -> invalid activation scale (flag 2)
+    for a8, symbol in ((True, 'ornith_routed_direct_launch'), (False, 'ornith_routed_direct_launch_a4')):
+        ref, ref_f32, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=a8)
+        out, final, flags = run_entry(native, symbol, x, w, ids, bank1)
+        np.testing.assert_array_equal(out, ref)
+        assert flags == ref_flags and flags & 4 and flags & 1
+
+
+def test_prefill_1120_sampled_tokens(native, layer1, bank1, S, O):
+    """Chunked-prefill shape: tokens are independent, so 48 sampled tokens of
+    the full 1120-row call are checked against the oracle run on just them."""
+    rng = np.random.default_rng(1120)
+    T = 1120
+    x = S.make_tokens(rng, T)
+    w, ids = S.random_routes(rng, T)
+    out, _, flags = run_entry(native, 'ornith_routed_direct_launch_a4_prefill', x, w, ids, bank1)
+    pick = np.sort(rng.choice(T, 48, replace=False))
+    ref, _, ref_flags = O.routed_layer(x[pick], w[pick], ids[pick], *bank1.np_routed, a8=False)
+    np.testing.assert_array_equal(out[pick], ref)
+    assert flags == 0 == ref_flags
+
+
+def test_repack_on_device(native):
+    rng = np.random.default_rng(9)
+    N, K = 1024, 2048
+    c32 = rng.integers(0, 2 ** 32, (3, N // 32, K // 256, 32, 32), dtype=np.uint32)
+    m32 = rng.integers(0, 2 ** 32, (3, N // 32, K // 256, 32), dtype=np.uint32)
+    c16 = np.ascontiguousarray(c32.reshape(3, N // 32, K // 256, 32, 2, 16).transpose(0, 1, 4, 2, 3, 5))
+    m16 = np.ascontiguousarray(m32.reshape(3, N // 32, K // 256, 2, 16).transpose(0, 1, 3, 2, 4))
+    rc, rm = native.repack_n16_to_n32(dev(c16.reshape(3, N // 16, K // 256, 32, 16)),
+                                      dev(m16.reshape(3, N // 16, K // 256, 16)), N, K)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(rc.view(torch.int32).cpu().numpy().view(np.uint32), c32)
+    np.testing.assert_array_equal(rm.view(torch.int32).cpu().numpy().view(np.uint32), m32)
+
+
+def test_repeat_calls_deterministic(native, layer1, bank1, S):
+    rng = np.random.default_rng(11)
+    x = S.make_tokens(rng, 32)
+    w, ids = S.random_routes(rng, 32)
+    a = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
+    b = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
+    np.testing.assert_array_equal(a[0], b[0])
