@@ -5,7 +5,8 @@ Workload (default): decode B=1 through a stack of 40
 Ornith MoE layers (256 routed experts + 1 shared, H2048/I512, affine-u4 G256
 weights, A8 activations), fresh seeded weights per layer (16.6 GB resident),
 router logits ~N(0,1) per layer and step.  One step = one token through the
-40 layers, each layer's output feeding the next, every layer called through
+40 independent layers (each takes the step's token rows as input), every
+layer called through
 `ornith_b200::routed_from_logits` (routing, routed experts, shared expert,
 combine).  Other workloads: --config decode32 (configs[2], logits + per-expert
 bias N(0,0.5)), prefill1120 / prefill8192 (configs[3], A4, 40 weight sets
@@ -56,6 +57,8 @@ def parse():
     p.add_argument('--config', default='decode1', choices=sorted(CONFIGS))
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
+    p.add_argument('--layers', type=int, default=None,
+                   help='override the layer count (small cases for profiler captures)')
     return p.parse_args()
 
 
@@ -144,7 +147,9 @@ class Stack:
 def run(args):
     import torch
     import torch.distributed as dist
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg['layers'] = args.layers
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
@@ -184,10 +189,8 @@ def run(args):
     def step(s, x):
         lg = logits[s % n_logit_sets]
         for l in range(L):
-            out = outs[l % 2]
-            layer_call(l, x, lg[l], out)
-            x = out
-        return x
+            layer_call(l, x, lg[l], outs[l % 2])
+        return outs[(L - 1) % 2]
 
     # algorithmic bytes per step: (distinct experts + 1) * EXPERT_BYTES per layer + activations
     ids = torch.topk(logits, 8, dim=-1).indices  # [sets, L, T, 8]
@@ -230,12 +233,10 @@ def run(args):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
     per_layer = []
     for rep in range(3):
-        x = x0
         for l in range(L):
             ev[l][0].record()
-            layer_call(l, x, logits[(args.warmup + rep) % n_logit_sets][l], outs[l % 2])
+            layer_call(l, x0, logits[(args.warmup + rep) % n_logit_sets][l], outs[l % 2])
             ev[l][1].record()
-            x = outs[l % 2]
         torch.cuda.synchronize()
         per_layer += [a.elapsed_time(b) for a, b in ev]
     layer_ms = statistics.mean(per_layer)
@@ -258,11 +259,9 @@ def run(args):
     for s in range(args.steps):
         x_dev.copy_(pin_x, non_blocking=True)
         lg_dev.copy_(pin_logits[s % pin_logits.shape[0]], non_blocking=True)
-        x = x_dev
         for l in range(L):
-            layer_call(l, x, lg_dev[l], outs[l % 2])
-            x = outs[l % 2]
-        pin_out.copy_(x, non_blocking=True)
+            layer_call(l, x_dev, lg_dev[l], outs[l % 2])
+        pin_out.copy_(outs[(L - 1) % 2], non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)

@@ -8,6 +8,8 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 
 #include "../../include/ornith_moe_b200.h"
 #include "moe_layer.cuh"
@@ -150,7 +152,13 @@ void fill_layout(int Tcap, OrnithRoutedDirectLayout* out) {
     *out = l;
 }
 
+// Path selection: the fused persistent kernel for decode batches, the
+// multi-kernel path otherwise.  ORNITH_MOE_B200_PATH=generic forces the
+// multi-kernel path (used by the tests to check both paths).
 cudaError_t run_layer(const LayerArgs& a, cudaStream_t stream) {
+    const char* path = getenv("ORNITH_MOE_B200_PATH");
+    const bool force_generic = path && strcmp(path, "generic") == 0;
+    if (!force_generic && decode_supported(a.T)) return launch_decode(a, stream);
     return launch_generic(a, stream);
 }
 

@@ -68,6 +68,7 @@ void count_launches(int n);
 cudaError_t launch_generic(const LayerArgs& a, cudaStream_t stream);
 // Fused persistent path for decode batches (T <= kDecodeMaxT).
 constexpr int kDecodeMaxT = 32;
+bool decode_supported(int T);
 cudaError_t launch_decode(const LayerArgs& a, cudaStream_t stream);
 
 }  // namespace ornith

@@ -234,3 +234,66 @@ def test_repeat_calls_deterministic(native, layer1, bank1, S):
     a = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
     b = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
     np.testing.assert_array_equal(a[0], b[0])
+
+
+@pytest.mark.parametrize('T', [1, 3, 8, 32])
+def test_multi_kernel_path_matches_fused(native, layer1, bank1, S, O, T, monkeypatch):
+    """Decode batches run the fused persistent kernel; the multi-kernel path
+    (forced through the environment) must give the same bits."""
+    rng = np.random.default_rng(300 + T)
+    x = S.make_tokens(rng, T)
+    w, ids = S.random_routes(rng, T, pad_fraction=0.1)
+    fused = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
+    monkeypatch.setenv('ORNITH_MOE_B200_PATH', 'generic')
+    multi = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
+    ref, _, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=True)
+    np.testing.assert_array_equal(fused[0], ref)
+    np.testing.assert_array_equal(multi[0], ref)
+    assert fused[2] == multi[2] == ref_flags
+
+
+@pytest.mark.parametrize('T', [5, 32])
+def test_duplicate_expert_ids(native, layer1, bank1, S, O, T):
+    """Collisions: the same expert several times in one token.  At T=32 one
+    expert receives 96 routes, beyond the fused kernel's register budget."""
+    rng = np.random.default_rng(400 + T)
+    x = S.make_tokens(rng, T)
+    w, ids = S.random_routes(rng, T)
+    ids[:, 1] = ids[:, 0]
+    ids[:, 2:4] = 17
+    for a8, symbol in ((True, 'ornith_routed_direct_launch'), (False, 'ornith_routed_direct_launch_a4')):
+        ref, ref_f32, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=a8)
+        out, final, flags = run_entry(native, symbol, x, w, ids, bank1)
+        np.testing.assert_array_equal(out, ref)
+        np.testing.assert_array_equal(final.view(np.uint32), ref_f32.view(np.uint32))
+        assert flags == ref_flags
+
+
+def test_all_slots_padded(native, layer1, bank1, S):
+    rng = np.random.default_rng(5)
+    x = S.make_tokens(rng, 4)
+    w = np.ones((4, 8), np.float32)
+    ids = -np.ones((4, 8), np.int32)
+    out, final, flags = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
+    assert not out.any() and not final.any() and flags == 0
+
+
+def test_shared_slot_with_all_routed_padded(native, layer1, bank1, S, O, tables):
+    T = 3
+    rng = np.random.default_rng(6)
+    x = S.make_tokens(rng, T)
+    w = np.ones((T, 8), np.float32)
+    ids = -np.ones((T, 8), np.int32)
+    logit = S.f32_to_bf16_bits(rng.standard_normal(T).astype(np.float32))
+    ref, ref_sh, _, ref_flags = O.routed_layer_shared(x, w, ids, *bank1.np_routed, *bank1.np_shared, logit,
+                                                      tables['silu_fp32'], tables['sigmoid_bf16'])
+    ws = torch.empty(native.get_layout(16).workspace_bytes, dtype=torch.uint8, device=DEV)
+    out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    shared = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    native.routed_shared_out(dev(x), dev(w), dev(ids), *bank1.routed, *bank1.shared, dev(logit),
+                             dev(tables['silu_fp32']), dev(tables['sigmoid_bf16']), ws, out, shared, flags, 16)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host_bits(out), ref)
+    np.testing.assert_array_equal(host_bits(shared), ref_sh)
+    assert int(flags.item()) == ref_flags
