@@ -149,6 +149,17 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_launch_from_logits(
     void* workspace, size_t bytes, void* output_bf16, void* shared_output_bf16, void* flags_u32,
     int T, int Tcap, int act_bits, cudaStream_t stream);
 
+/* Slot-ordered weighted combine from explicit per-route rows: route_out fp32
+ * [T*8][2048] (row 8t+s = slot s of token t), weights fp32 [T,8], ids int32
+ * [T,8] -> output bf16 [T,2048] = bf16(sum over slots with a valid id, in slot
+ * order from +0, of row*weight).  The arithmetic of reduce_slots
+ * (routed_storage_n32_consumer.cpp:176-185); used by the expert-parallel home
+ * rank after the per-slot rows come back from the expert owners.  Flag 32 on
+ * non-finite or overflowing results. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine(
+    const void* route_out_f32, const void* weights_f32, const void* ids_i32, int T,
+    void* output_bf16, void* flags_u32, cudaStream_t stream);
+
 /* Workspace size for ornith_moe_b200_launch_from_logits (0 <= Tcap <= 8192). */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes);
 

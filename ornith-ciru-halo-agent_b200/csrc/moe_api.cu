@@ -131,6 +131,29 @@ __global__ void repack_meta_kernel(const uint32_t* src, uint32_t* dst, int E, in
     }
 }
 
+// Slot-ordered combine from explicit per-route rows (the expert-parallel home
+// rank's final step): out[t,c] = bf16(sum over valid slots s, in slot order,
+// of route_out[8t+s][c] * w[t,s]), starting from +0 (reduce_slots :176-185).
+__global__ __launch_bounds__(256) void combine_rows_kernel(const float* route_out, const float* weights,
+                                                           const int32_t* ids, int T, uint16_t* out, uint32_t* flags) {
+    const size_t index = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint32_t f = 0;
+    if (index < size_t(T) * kH) {
+        const int t = int(index / kH), c = int(index % kH);
+        float sum = 0.f;
+#pragma unroll
+        for (int s = 0; s < kTop; ++s) {
+            const int r = t * kTop + s;
+            if (id_valid(ids[r])) sum = __fadd_rn(sum, __fmul_rn(route_out[size_t(r) * kH + c], weights[r]));
+        }
+        const uint16_t res = bf16_rne(sum);
+        out[index] = res;
+        if (!isfinite(sum) || (res & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
+    }
+    f = __reduce_or_sync(0xffffffffu, f);
+    if (f && (threadIdx.x & 31) == 0) atomicOr(flags, f);
+}
+
 void fill_layout(int Tcap, OrnithRoutedDirectLayout* out) {
     const Workspace w = workspace_layout(Tcap);
     OrnithRoutedDirectLayout l;
@@ -159,6 +182,7 @@ cudaError_t run_layer(const LayerArgs& a, cudaStream_t stream) {
     const char* path = getenv("ORNITH_MOE_B200_PATH");
     const bool force_generic = path && strcmp(path, "generic") == 0;
     if (!force_generic && decode_supported(a.T)) return launch_decode(a, stream);
+    if (!force_generic && a.T > kDecodeMaxT) return launch_prefill(a, stream);
     return launch_generic(a, stream);
 }
 
@@ -300,6 +324,20 @@ cudaError_t ornith_moe_b200_route_topk(const void* logits, int T, void* weights,
     route_topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(static_cast<const float*>(logits), T,
                                                         static_cast<float*>(weights), static_cast<int32_t*>(ids),
                                                         static_cast<uint32_t*>(flags));
+    return cudaGetLastError();
+}
+
+cudaError_t ornith_moe_b200_combine(const void* route_out_f32, const void* weights, const void* ids, int T,
+                                    void* output, void* flags, cudaStream_t stream) {
+    if (T < 0 || T > kTcapMax) return cudaErrorInvalidValue;
+    if (!T) return cudaSuccess;
+    if (!route_out_f32 || !weights || !ids || !output || !flags || !aligned(route_out_f32, 4) ||
+        !aligned(weights, 4) || !aligned(ids, 4) || !aligned(output, 2) || !aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    count_launches(1);
+    combine_rows_kernel<<<(T * kH + 255) / 256, 256, 0, stream>>>(
+        static_cast<const float*>(route_out_f32), static_cast<const float*>(weights), static_cast<const int32_t*>(ids),
+        T, static_cast<uint16_t*>(output), static_cast<uint32_t*>(flags));
     return cudaGetLastError();
 }
 

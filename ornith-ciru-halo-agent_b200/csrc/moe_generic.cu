@@ -36,6 +36,19 @@ Workspace workspace_layout(int Tcap) {
     add(w.topk_w, t * kTop * 4);
     add(w.topk_ids, t * kTop * 4);
     add(w.logit, t * 2);
+    if (Tcap > kDecodeMaxT) {
+        const size_t mt = (rows + 127) / 128 + (kE + 1);
+        add(w.rowpos, rows * 4);
+        add(w.slot_tiles, (kE + 2) * 4);
+        add(w.mtiles, mt * 16);
+        add(w.n_mtiles, 16);
+        add(w.agate, mt * 8 * 32768);
+        add(w.agate_sa, mt * 8 * 128 * 4);
+        add(w.agate_sum, mt * 8 * 128 * 4);
+        add(w.adown, mt * 2 * 32768);
+        add(w.adown_sa, mt * 2 * 128 * 4);
+        add(w.adown_sum, mt * 2 * 128 * 4);
+    }
     w.bytes = cursor;
     return w;
 }
@@ -296,7 +309,7 @@ __global__ __launch_bounds__(256) void combine_kernel(LayerArgs a) {
 }  // namespace
 
 cudaError_t launch_generic(const LayerArgs& a, cudaStream_t stream) {
-    count_launches(6);
+    count_launches(5);
     const int R = a.T * kTop;
     const int rows = R + (a.shared ? a.T : 0);
     plan_kernel<<<1, 1024, 0, stream>>>(a);
@@ -313,9 +326,13 @@ cudaError_t launch_generic(const LayerArgs& a, cudaStream_t stream) {
     ORNITH_CHECK_LAUNCH();
     down_kernel<<<dim3(kH / 32, kE + 1), 256, 0, stream>>>(a);
     ORNITH_CHECK_LAUNCH();
+    return launch_combine(a, stream);
+}
+
+cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream) {
+    count_launches(1);
     combine_kernel<<<(a.T * kH + 255) / 256, 256, 0, stream>>>(a);
-    ORNITH_CHECK_LAUNCH();
-    return cudaSuccess;
+    return cudaGetLastError();
 }
 
 }  // namespace ornith

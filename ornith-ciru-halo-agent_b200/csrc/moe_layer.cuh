@@ -17,6 +17,10 @@ struct Workspace {
     size_t counts, offsets, routes, cursors, active;  // routing plan
     size_t ctrl;                  // counters of the fused kernels
     size_t topk_w, topk_ids, logit;  // router outputs of the from-logits entry point
+    // tensor-core prefill path (only when Tcap > kDecodeMaxT)
+    size_t rowpos, slot_tiles, mtiles, n_mtiles;
+    size_t agate, agate_sa, agate_sum;  // gate activation tiles [MT][8][32 KB] + per-row scale/sum
+    size_t adown, adown_sa, adown_sum;  // down activation tiles [MT][2][32 KB]
     size_t bytes;
 };
 
@@ -66,6 +70,10 @@ void count_launches(int n);
 
 // Multi-kernel path, any T <= 8192.
 cudaError_t launch_generic(const LayerArgs& a, cudaStream_t stream);
+// Slot-ordered combine of route_out into out / shared_out (shared by the paths).
+cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream);
+// Tensor-core prefill path (T > kDecodeMaxT; needs a workspace laid out for Tcap > kDecodeMaxT).
+cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream);
 // Fused persistent path for decode batches (T <= kDecodeMaxT).
 constexpr int kDecodeMaxT = 32;
 bool decode_supported(int T);

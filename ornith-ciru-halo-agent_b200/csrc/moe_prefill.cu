@@ -1,0 +1,676 @@
+// Tensor-core prefill path of the routed-MoE layer (T > 32), sm_100a.
+//
+// Same arithmetic as the reference's grouped path
+// (kernels/routed_storage/routed_storage_n32_prefill.h:43-165): per 256-group
+// exact integer dots, then the fixed fp32 epilogue in ascending group order.
+// B200 schedule:
+//
+//   prefill_plan_kernel   routing plan (slot counts/offsets/route lists, the
+//                         inverse map route -> position) and the list of
+//                         128-route M-tiles per expert slot;
+//   pack_tokens_kernel    Hadamard + quantise each token group once and write
+//                         it into the M-tile of each of its routes, in the
+//                         no-swizzle K-major core-matrix layout tcgen05 reads;
+//   mma_kernel<8, gate>   gate/up grouped GEMM: tcgen05.mma.kind::i8
+//                         (s8 activations x u8 codes -> s32 in TMEM),
+//                         M=128 x N=256 (128 gate + 128 matching up columns),
+//                         fused SiLU*up epilogue -> fp32 middle rows;
+//   pack_middle_kernel    Hadamard + quantise the middle rows into down M-tiles;
+//   mma_kernel<2, down>   down grouped GEMM, N=256 output columns -> route_out;
+//   combine               slot-ordered weighted sum (shared with the
+//                         multi-kernel path).
+//
+// mma_kernel roles (20 warps, one CTA per SM, persistent over tiles):
+//   warp 0      producer: cp.async.bulk of the activation half-tile (16 KB),
+//               the packed u4 codes (8 x 2 KB) and per-group metadata;
+//   warp 1      TMEM allocator and single-thread MMA issuer;
+//   warps 2-3   converters: u4 codes -> u8 core matrices in shared memory;
+//   warps 4-19  four epilogue warpgroups (64 TMEM columns each).
+// K advances in half-groups of 128 through a 3-stage ring.  The int32
+// accumulator of a 256-group is double buffered in TMEM (2 x 256 columns) and
+// pre-filled with the bits of 1.5*2^23, so after the MMAs each cell holds the
+// float 1.5*2^23 + dot exactly (|dot| < 2^22) and float(dot) is one subtraction.
+// Activations use the dp4a byte order [q0 q2 q4 q6 | q1 q3 q5 q7] per 8-block,
+// so unpacking a packed code word is two masks, with no byte shuffles.
+// No TMA or bulk load uses cluster multicast.  Every wait is bounded.
+#include "moe_layer.cuh"
+
+namespace ornith {
+namespace {
+
+constexpr int kMT = 128;                  // routes per M-tile
+constexpr int kNT = 256;                  // B rows (output columns) per tile
+constexpr int kStages = 3;
+constexpr int kABytes = kMT * 128;        // activation half-tile (K = 128)
+constexpr int kBpBytes = kNT * 128 / 2;   // packed codes half-tile
+constexpr int kBuBytes = kNT * 128;       // unpacked codes half-tile
+constexpr int kStageBytes = kABytes + kBpBytes + kBuBytes;
+constexpr int kMetaBytes = kNT * 4 + kMT * 4 + kMT * 4;  // B meta, A scale, A sum
+constexpr int kWarps = 20;
+constexpr int kThreads = kWarps * 32;
+constexpr int kEpiWarps = 16;
+constexpr uint32_t kMagic = 0x4B400000u;  // 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;
+constexpr uint64_t kTimeoutNs = 1000000000ull;
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---- tcgen05 wrappers ----------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// K-major, no-swizzle shared-memory matrix descriptor (sm_100 format, version 1):
+// core matrices of 8 rows x 16 bytes, LBO = byte stride between the two
+// K-adjacent core matrices, SBO = byte stride between 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return uint64_t((addr >> 4) & 0x3FFFu) | (uint64_t((lbo >> 4) & 0x3FFFu) << 16) |
+           (uint64_t((sbo >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46);
+}
+// Instruction descriptor, kind::i8: D s32, A s8 (signed), B u8 (unsigned),
+// both K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (0u << 10) | (uint32_t(kNT >> 3) << 17) | (uint32_t(kMT >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t enable_d) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(enable_d)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(v)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Bounded mbarrier wait; returns false (and raises the abort state) on timeout.
+__device__ bool bwait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* flags) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = now_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort) return false;
+        if (now_ns() - t0 > kTimeoutNs) {
+            atomicOr(flags, kFlagWaitTimeout);
+            *abort = 1;
+            return false;
+        }
+    }
+    return true;
+}
+// Drain wait used on the abort path: lets an issued copy land (bounded).
+__device__ void drain_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = now_ns();
+    while (!mbar_try_wait(bar, parity) && now_ns() - t0 < kTimeoutNs) {
+    }
+}
+
+struct MmaArgs {
+    const uint8_t* atiles;   // [MT][KG][32768] activation tiles
+    const float* asa;        // [MT][KG][128] activation scales
+    const int32_t* asum;     // [MT][KG][128] activation sums
+    const int4* mtiles;      // {slot, first position, rows, 0}
+    const int32_t* n_mtiles;
+    const int32_t* routes;   // position -> route
+    const uint32_t* codes;   // routed bank
+    const uint32_t* meta;
+    const uint32_t* scodes;  // shared bank
+    const uint32_t* smeta;
+    float* out;              // gate: middle [rows][512]; down: route_out [rows][2048]
+    const float* silu_table;
+    uint32_t* flags;
+};
+
+template <int KG, bool GATE>
+__global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
+    constexpr int NUPT = GATE ? 4 : 8;  // N-tiles per M-tile
+    constexpr int K = KG * kG;
+    constexpr int BANK_N = GATE ? 2 * kI : kH;
+    constexpr size_t BANK_CODES = size_t(BANK_N) * K / 8;
+    constexpr size_t BANK_META = size_t(BANK_N) * KG;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* stages = smem;
+    uint8_t* metabuf = smem + kStages * kStageBytes;  // [2][kMetaBytes]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(metabuf + 2 * kMetaBytes);
+    uint64_t* full = bars;                       // [kStages] producer -> converters
+    uint64_t* conv = bars + kStages;             // [kStages] converters -> MMA
+    uint64_t* empty = bars + 2 * kStages;        // [kStages] MMA -> producer
+    uint64_t* meta_full = bars + 3 * kStages;    // [2]
+    uint64_t* meta_empty = meta_full + 2;        // [2]
+    uint64_t* acc_full = meta_empty + 2;         // [2]
+    uint64_t* acc_empty = acc_full + 2;          // [2]
+    uint64_t* drain = acc_empty + 2;             // [1] final MMA completion
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&conv[i], 2);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&meta_full[i], 1);
+            mbar_init(&meta_empty[i], kEpiWarps);
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int n_units = *p.n_mtiles * NUPT;
+
+    auto unit_bank = [&](int unit, const uint32_t*& codes, const uint32_t*& meta) {
+        const int4 mt = p.mtiles[unit / NUPT];
+        const bool shared = mt.x == kE;
+        codes = shared ? p.scodes : p.codes + size_t(mt.x) * BANK_CODES;
+        meta = shared ? p.smeta : p.meta + size_t(mt.x) * BANK_META;
+    };
+    // 32-column bank tile feeding B-tile rows 32i..32i+31 of N-tile nt
+    auto n32_of = [&](int nt, int i) { return GATE ? (i < 4 ? 4 * nt + i : 16 + 4 * nt + (i - 4)) : 8 * nt + i; };
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            int issued = 0, metas = 0;
+            for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
+                const uint32_t *codes, *meta;
+                unit_bank(unit, codes, meta);
+                const int nt = unit % NUPT, tile = unit / NUPT;
+                for (int g = 0; g < KG && !*abort; ++g) {
+                    if (!(metas < 2 || bwait(&meta_empty[metas & 1], uint32_t(metas / 2 - 1) & 1u, abort, p.flags)))
+                        break;
+                    {
+                        const int mb = metas & 1;
+                        uint8_t* m = metabuf + mb * kMetaBytes;
+                        mbar_arrive_expect_tx(&meta_full[mb], kMetaBytes);
+                        for (int i = 0; i < 8; ++i)
+                            bulk_g2s(m + i * 128, meta + (size_t(n32_of(nt, i)) * KG + g) * 32, 128, &meta_full[mb]);
+                        bulk_g2s(m + kNT * 4, p.asa + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
+                        bulk_g2s(m + kNT * 4 + kMT * 4, p.asum + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
+                        ++metas;
+                    }
+                    for (int h = 0; h < 2; ++h) {
+                        const int s = issued % kStages;
+                        if (issued >= kStages &&
+                            !bwait(&empty[s], uint32_t(issued / kStages - 1) & 1u, abort, p.flags))
+                            break;
+                        uint8_t* sA = stages + size_t(s) * kStageBytes;
+                        uint8_t* sBp = sA + kABytes;
+                        mbar_arrive_expect_tx(&full[s], kABytes + kBpBytes);
+                        bulk_g2s(sA, p.atiles + (size_t(tile) * KG + g) * 32768 + h * kABytes, kABytes, &full[s]);
+                        for (int i = 0; i < 8; ++i)
+                            bulk_g2s(sBp + i * 2048, codes + (size_t(n32_of(nt, i)) * KG + g) * 1024 + h * 512, 2048,
+                                     &full[s]);
+                        ++issued;
+                    }
+                }
+            }
+            if (*abort) {
+                // every issued copy lands before the CTA can leave
+                for (int k = issued - kStages; k < issued; ++k)
+                    if (k >= 0) drain_wait(&full[k % kStages], uint32_t(k / kStages) & 1u);
+                for (int k = metas - 2; k < metas; ++k)
+                    if (k >= 0) drain_wait(&meta_full[k & 1], uint32_t(k / 2) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int st = 0, gg = 0;
+            bool any = false;
+            for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
+                for (int g = 0; g < KG && !*abort; ++g, ++gg) {
+                    const int b = gg & 1;
+                    if (!bwait(&acc_empty[b], uint32_t(gg / 2) & 1u, abort, p.flags)) break;
+                    tc_fence_after();
+                    const uint32_t d = tmem + uint32_t(b * kNT);
+                    for (int h = 0; h < 2; ++h, ++st) {
+                        const int s = st % kStages;
+                        if (!bwait(&conv[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
+                        tc_fence_after();
+                        const uint32_t aaddr = smem_addr(stages + size_t(s) * kStageBytes);
+                        const uint32_t baddr = aaddr + kABytes + kBpBytes;
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_i8(d, smem_desc(aaddr + kk * 2 * 2048, 2048, 128),
+                                   smem_desc(baddr + kk * 2 * 4096, 4096, 128), 1u);
+                        mma_commit(&empty[s]);
+                        any = true;
+                    }
+                    mma_commit(&acc_full[b]);
+                }
+            }
+            if (any) {
+                // every MMA issued has finished reading shared memory before the CTA leaves
+                mma_commit(drain);
+                drain_wait(drain, 0);
+            }
+        }
+    } else if (warp < 4) {
+        // ---------------- converters ----------------
+        const int ct = tid - 64;  // 0..63
+        int st = 0;
+        for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
+            for (int g = 0; g < KG && !*abort; ++g) {
+                for (int h = 0; h < 2; ++h, ++st) {
+                    const int s = st % kStages;
+                    if (!bwait(&full[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
+                    const uint32_t* bp = reinterpret_cast<const uint32_t*>(stages + size_t(s) * kStageBytes + kABytes);
+                    uint8_t* bu = stages + size_t(s) * kStageBytes + kABytes + kBpBytes;
+                    // work item (i, q, c): 32-column tile i (8), word pair q (8), column c (32)
+#pragma unroll 4
+                    for (int it = ct; it < 8 * 8 * 32; it += 64) {
+                        const int c = it & 31, q = (it >> 5) & 7, i = it >> 8;
+                        const uint32_t w0 = bp[i * 512 + (2 * q) * 32 + c];
+                        const uint32_t w1 = bp[i * 512 + (2 * q + 1) * 32 + c];
+                        const int n = 32 * i + c;
+                        const uint4 v = make_uint4(w0 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu,
+                                                   (w1 >> 4) & 0x0f0f0f0fu);
+                        *reinterpret_cast<uint4*>(bu + q * 4096 + (n >> 3) * 128 + (n & 7) * 16) = v;
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&conv[s]);
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int ew = warp - 4;                 // 0..15
+        const int wg = ew >> 2;                  // column quarter
+        const int row = 32 * (warp & 3) + lane;  // TMEM lane = tile row
+        const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
+        // column offsets (within a 256-column accumulator) owned by this warpgroup
+        const int c0 = GATE ? 32 * wg : 64 * wg;
+        const int c1 = GATE ? kMT + 32 * wg : 64 * wg + 32;
+        for (int b = 0; b < 2; ++b) {
+            const uint32_t base = tmem + lane_base + uint32_t(b * kNT);
+            tmem_st16_const(base + c0, kMagic);
+            tmem_st16_const(base + c0 + 16, kMagic);
+            tmem_st16_const(base + c1, kMagic);
+            tmem_st16_const(base + c1 + 16, kMagic);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&acc_empty[0]);
+            mbar_arrive(&acc_empty[1]);
+        }
+        uint32_t f = 0;
+        int gg = 0;
+        for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
+            const int4 mt = p.mtiles[unit / NUPT];
+            const int nt = unit % NUPT;
+            float acc[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            bool ok = true;
+            for (int g = 0; g < KG; ++g, ++gg) {
+                const int b = gg & 1;
+                if (!bwait(&meta_full[b], uint32_t(gg / 2) & 1u, abort, p.flags) ||
+                    !bwait(&acc_full[b], uint32_t(gg / 2) & 1u, abort, p.flags)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t* bm = reinterpret_cast<const uint32_t*>(metabuf + b * kMetaBytes);
+                const float sa = reinterpret_cast<const float*>(metabuf + b * kMetaBytes + kNT * 4)[row];
+                const int ssumi = reinterpret_cast<const int32_t*>(metabuf + b * kMetaBytes + kNT * 4 + kMT * 4)[row];
+                const float ssum = __fmul_rn(sa, float(ssumi));
+                const uint32_t base = tmem + lane_base + uint32_t(b * kNT);
+#pragma unroll
+                for (int part = 0; part < 4; ++part) {
+                    const int col = (part < 2 ? c0 : c1) + 16 * (part & 1);
+                    uint32_t r[16];
+                    tmem_ld16(base + col, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const uint32_t mw = bm[col + i];
+                        const float fd = __fsub_rn(__uint_as_float(r[i]), kMagicF);
+                        const float scaled_dot = __fmul_rn(sa, fd);
+                        const float product =
+                            __fmul_rn(__half2float(__ushort_as_half(uint16_t(mw & 0xffffu))), scaled_dot);
+                        const float correction = __fmul_rn(__half2float(__ushort_as_half(uint16_t(mw >> 16))), ssum);
+                        acc[part * 16 + i] = __fadd_rn(acc[part * 16 + i], __fadd_rn(product, correction));
+                    }
+                    tmem_st16_const(base + col, kMagic);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&acc_empty[b]);
+                    mbar_arrive(&meta_empty[b]);
+                }
+            }
+            if (!ok) break;
+            if (row < mt.z) {
+                const int route = p.routes[mt.y + row];
+                const bool shared = mt.x == kE;
+                if (GATE) {
+                    float* dst = p.out + size_t(route) * kI + kMT * nt + 32 * wg;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float v[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            float gv = acc[i + j], uv = acc[32 + i + j], value;
+                            if (shared) {
+                                gv = bf16_round_f32(gv);
+                                uv = bf16_round_f32(uv);
+                                if (!isfinite(gv) || !isfinite(uv)) f |= kFlagNonfiniteProjection;
+                                value = bf16_round_f32(__fmul_rn(p.silu_table[__float_as_uint(gv) >> 16], uv));
+                            } else {
+                                if (!isfinite(gv) || !isfinite(uv)) f |= kFlagNonfiniteProjection;
+                                value = silu_mul(gv, uv);
+                            }
+                            if (!isfinite(value)) f |= kFlagNonfiniteMiddle;
+                            v[j] = value;
+                        }
+                        *reinterpret_cast<float4*>(dst + i) = make_float4(v[0], v[1], v[2], v[3]);
+                    }
+                } else {
+                    float* dst = p.out + size_t(route) * kH + kNT * nt + 64 * wg;
+#pragma unroll
+                    for (int i = 0; i < 64; i += 4) {
+                        float v[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            v[j] = shared ? bf16_round_f32(acc[i + j]) : acc[i + j];
+                            if (!isfinite(v[j])) f |= kFlagNonfiniteProjection;
+                        }
+                        *reinterpret_cast<float4*>(dst + i) = make_float4(v[0], v[1], v[2], v[3]);
+                    }
+                }
+            }
+        }
+        f = __reduce_or_sync(0xffffffffu, f);
+        if (f && lane == 0) atomicOr(p.flags, f);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// Routing plan for the tensor-core path, one CTA.  Positions are grouped by
+// expert slot (slot 256 = shared expert rows R..R+T-1); rowpos is the inverse
+// map; every slot's positions are cut into 128-route M-tiles.
+__global__ __launch_bounds__(1024) void prefill_plan_kernel(LayerArgs a) {
+    __shared__ int counts[kE + 1], offsets[kE + 2], tile_base[kE + 2];
+    const int R = a.T * kTop;
+    for (int e = threadIdx.x; e <= kE; e += blockDim.x) counts[e] = 0;
+    __syncthreads();
+    uint32_t f = 0;
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int e = a.ids[r];
+        if (id_valid(e)) atomicAdd(&counts[e], 1);
+        else if (e != -1) f |= kFlagInvalidId;
+    }
+    f = __reduce_or_sync(0xffffffffu, f);
+    if (f && (threadIdx.x & 31) == 0) atomicOr(a.flags, f);
+    __syncthreads();
+    int4* mtiles = ws_at<int4>(a, a.L.mtiles);
+    if (threadIdx.x == 0) {
+        counts[kE] = a.shared ? a.T : 0;
+        int total = 0, tiles = 0;
+        for (int e = 0; e <= kE; ++e) {
+            offsets[e] = total;
+            tile_base[e] = tiles;
+            for (int m = 0; m < counts[e]; m += kMT) mtiles[tiles++] = make_int4(e, total + m, min(kMT, counts[e] - m), 0);
+            total += counts[e];
+        }
+        offsets[kE + 1] = total;
+        tile_base[kE + 1] = tiles;
+        *ws_at<int32_t>(a, a.L.n_mtiles) = tiles;
+    }
+    __syncthreads();
+    int32_t* g_offsets = ws_at<int32_t>(a, a.L.offsets);
+    int32_t* g_tiles = ws_at<int32_t>(a, a.L.slot_tiles);
+    for (int e = threadIdx.x; e <= kE + 1; e += blockDim.x) {
+        g_offsets[e] = offsets[e];
+        g_tiles[e] = tile_base[e];
+    }
+    int32_t* routes = ws_at<int32_t>(a, a.L.routes);
+    int32_t* rowpos = ws_at<int32_t>(a, a.L.rowpos);
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        const int e = a.ids[r];
+        if (id_valid(e)) {
+            const int pos = offsets[e] + atomicAdd(&counts[e], -1) - 1;
+            routes[pos] = r;
+            rowpos[r] = pos;
+        }
+    }
+    if (a.shared)
+        for (int t = threadIdx.x; t < a.T; t += blockDim.x) {
+            routes[offsets[kE] + t] = R + t;
+            rowpos[R + t] = offsets[kE] + t;
+        }
+}
+
+// Tile and row of a route position inside an activation tile set.
+__device__ __forceinline__ void tile_row(const LayerArgs& a, int slot, int pos, int& tile, int& row) {
+    const int m = pos - ws_at<int32_t>(a, a.L.offsets)[slot];
+    tile = ws_at<int32_t>(a, a.L.slot_tiles)[slot] + m / kMT;
+    row = m % kMT;
+}
+// Byte offset of lane l's 8 activation bytes (K-chunk l/2, half l&1) of `row`
+// inside one 256-group of a tile: [chunk 16][row/8 16][row%8 8][16 bytes].
+__device__ __forceinline__ size_t core_offset(int row, int lane) {
+    return size_t(lane >> 1) * 2048 + (row >> 3) * 128 + (row & 7) * 16 + (lane & 1) * 8;
+}
+
+// Token Hadamard + quantise, scattered to the gate activation tiles of every
+// route of the token.  One warp per (token, 256-group).
+template <int QMAX>
+__global__ __launch_bounds__(256) void pack_tokens_kernel(LayerArgs a) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= a.T * 8) return;
+    const int t = warp / 8, g = warp % 8;
+    bool live = a.shared_all_live;
+    if (!live)
+        for (int s = 0; s < kTop; ++s) live |= id_valid(a.ids[t * kTop + s]);
+    if (!live) return;  // no route reads this token
+    const uint4 raw = *reinterpret_cast<const uint4*>(a.x + size_t(t) * kH + g * kG + lane * 8);
+    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+    float e[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        e[2 * i] = __uint_as_float(w4[i] << 16);
+        e[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
+    }
+    uint32_t f = 0;
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
+    wht128_halfwarp(e, lane);
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
+    __shared__ uint2 qbuf[8][32];
+    __shared__ __half sbuf[8];
+    __shared__ int32_t mbuf[8];
+    const int wl = threadIdx.x >> 5;
+    quantize_group_warp<QMAX>(e, lane, qbuf[wl], &sbuf[wl], &mbuf[wl], f);
+    __syncwarp();
+    const uint2 q = qbuf[wl][lane];
+    const float sa = __half2float(sbuf[wl]);
+    const int32_t sum = mbuf[wl];
+    const int R = a.T * kTop;
+    uint8_t* tiles = ws_at<uint8_t>(a, a.L.agate);
+    float* asa = ws_at<float>(a, a.L.agate_sa);
+    int32_t* asum = ws_at<int32_t>(a, a.L.agate_sum);
+    const int32_t* rowpos = ws_at<int32_t>(a, a.L.rowpos);
+    for (int s = 0; s <= kTop; ++s) {
+        int route, slot;
+        if (s < kTop) {
+            route = t * kTop + s;
+            slot = a.ids[route];
+            if (!id_valid(slot)) continue;
+        } else {
+            if (!a.shared) break;
+            route = R + t;
+            slot = kE;
+        }
+        int tile, row;
+        tile_row(a, slot, rowpos[route], tile, row);
+        *reinterpret_cast<uint2*>(tiles + (size_t(tile) * 8 + g) * 32768 + core_offset(row, lane)) = q;
+        if (lane == 0) {
+            asa[(size_t(tile) * 8 + g) * kMT + row] = sa;
+            asum[(size_t(tile) * 8 + g) * kMT + row] = sum;
+        }
+    }
+    f = __reduce_or_sync(0xffffffffu, f);
+    if (f && lane == 0) atomicOr(a.flags, f);
+}
+
+// Middle Hadamard + quantise into the down activation tiles: one warp per
+// (position, 256-group) of the route list.
+template <int QMAX>
+__global__ __launch_bounds__(256) void pack_middle_kernel(LayerArgs a) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int total = ws_at<int32_t>(a, a.L.offsets)[kE + 1];
+    if (warp >= total * 2) return;
+    const int pos = warp >> 1, g = warp & 1;
+    const int route = ws_at<int32_t>(a, a.L.routes)[pos];
+    const int R = a.T * kTop;
+    const int slot = route >= R ? kE : a.ids[route];
+    const float4* src =
+        reinterpret_cast<const float4*>(ws_at<float>(a, a.L.middle) + size_t(route) * kI + g * kG + lane * 8);
+    const float4 v0 = src[0], v1 = src[1];
+    float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    uint32_t f = 0;
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
+    wht128_halfwarp(e, lane);
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
+    int tile, row;
+    tile_row(a, slot, pos, tile, row);
+    __shared__ uint2 qbuf[8][32];
+    __shared__ __half sbuf[8];
+    __shared__ int32_t mbuf[8];
+    const int wl = threadIdx.x >> 5;
+    quantize_group_warp<QMAX>(e, lane, qbuf[wl], &sbuf[wl], &mbuf[wl], f);
+    __syncwarp();
+    *reinterpret_cast<uint2*>(ws_at<uint8_t>(a, a.L.adown) + (size_t(tile) * 2 + g) * 32768 + core_offset(row, lane)) =
+        qbuf[wl][lane];
+    if (lane == 0) {
+        ws_at<float>(a, a.L.adown_sa)[(size_t(tile) * 2 + g) * kMT + row] = __half2float(sbuf[wl]);
+        ws_at<int32_t>(a, a.L.adown_sum)[(size_t(tile) * 2 + g) * kMT + row] = mbuf[wl];
+    }
+    f = __reduce_or_sync(0xffffffffu, f);
+    if (f && lane == 0) atomicOr(a.flags, f);
+}
+
+constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + 2 * kMetaBytes + 64 * 8 + 64;
+
+struct DeviceState {
+    int sms = 0;
+    bool attr = false;
+};
+DeviceState g_state[64];
+
+}  // namespace
+
+cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
+    int device = 0;
+    cudaError_t st = cudaGetDevice(&device);
+    if (st != cudaSuccess) return st;
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    DeviceState& ds = g_state[device];
+    if (!ds.sms && (st = cudaDeviceGetAttribute(&ds.sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+        return st;
+    auto gate = mma_kernel<8, true>;
+    auto down = mma_kernel<2, false>;
+    if (!ds.attr) {
+        if ((st = cudaFuncSetAttribute(gate, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMmaSmem))) != cudaSuccess)
+            return st;
+        if ((st = cudaFuncSetAttribute(down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMmaSmem))) != cudaSuccess)
+            return st;
+        ds.attr = true;
+    }
+    const int T = a.T, R = T * kTop, rows = R + (a.shared ? T : 0);
+    count_launches(5);
+    prefill_plan_kernel<<<1, 1024, 0, stream>>>(a);
+    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    if (a.a8) pack_tokens_kernel<127><<<(T * 8 + 7) / 8, 256, 0, stream>>>(a);
+    else pack_tokens_kernel<7><<<(T * 8 + 7) / 8, 256, 0, stream>>>(a);
+    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    // upper bound of M-tiles (the kernels read the device-side count)
+    const int max_tiles = (rows + kMT - 1) / kMT + (kE + 1);
+    MmaArgs g{};
+    g.atiles = ws_at<uint8_t>(a, a.L.agate);
+    g.asa = ws_at<float>(a, a.L.agate_sa);
+    g.asum = ws_at<int32_t>(a, a.L.agate_sum);
+    g.mtiles = ws_at<int4>(a, a.L.mtiles);
+    g.n_mtiles = ws_at<int32_t>(a, a.L.n_mtiles);
+    g.routes = ws_at<int32_t>(a, a.L.routes);
+    g.codes = a.gate_codes;
+    g.meta = a.gate_meta;
+    g.scodes = a.sgate_codes;
+    g.smeta = a.sgate_meta;
+    g.out = ws_at<float>(a, a.L.middle);
+    g.silu_table = a.silu_table;
+    g.flags = a.flags;
+    gate<<<min(ds.sms, max_tiles * 4), kThreads, kMmaSmem, stream>>>(g);
+    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    const int mid_warps = rows * 2;
+    if (a.a8) pack_middle_kernel<127><<<(mid_warps + 7) / 8, 256, 0, stream>>>(a);
+    else pack_middle_kernel<7><<<(mid_warps + 7) / 8, 256, 0, stream>>>(a);
+    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    MmaArgs d = g;
+    d.atiles = ws_at<uint8_t>(a, a.L.adown);
+    d.asa = ws_at<float>(a, a.L.adown_sa);
+    d.asum = ws_at<int32_t>(a, a.L.adown_sum);
+    d.codes = a.down_codes;
+    d.meta = a.down_meta;
+    d.scodes = a.sdown_codes;
+    d.smeta = a.sdown_meta;
+    d.out = ws_at<float>(a, a.L.route_out);
+    down<<<min(ds.sms, max_tiles * 8), kThreads, kMmaSmem, stream>>>(d);
+    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    return launch_combine(a, stream);
+}
+
+}  // namespace ornith

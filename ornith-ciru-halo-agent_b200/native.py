@@ -52,6 +52,7 @@ SIGNATURES = {
     'ornith_moe_b200_launch_from_logits': (
         [C.c_void_p] * 14 + [C.c_size_t] + [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_moe_b200_get_layout': ([C.c_int, C.POINTER(C.c_size_t)], C.c_int),
+    'ornith_moe_b200_combine': ([C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3, C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
 }
 
@@ -235,6 +236,17 @@ def _routed_from_logits_fake(x, logits, gate, gate_meta, down, down_meta, shared
                              shared_down, shared_down_meta, shared_gate_weight, silu_table, sigmoid_table,
                              workspace, out, shared_out, flags, capacity, act_bits):
     return None
+
+
+def combine_rows(route_rows, weights, ids, out, flags):
+    """Slot-ordered combine of per-route fp32 rows [T*8, 2048] into bf16 out [T, 2048]."""
+    T = ids.shape[0]
+    if (route_rows.dtype != torch.float32 or route_rows.shape != (T * 8, 2048) or not route_rows.is_contiguous()
+            or out.dtype != torch.bfloat16 or out.shape != (T, 2048) or not out.is_contiguous()):
+        raise ValueError('combine_rows requires FP32 rows [T*8,2048] and a BF16 output [T,2048]')
+    _validate_routes(out, weights, ids)
+    check(lib().ornith_moe_b200_combine(ptr(route_rows), ptr(weights), ptr(ids), T, ptr(out), ptr(flags),
+                                        stream(out)), 'combine')
 
 
 def repack_n16_to_n32(codes16, meta16, N, K):

@@ -236,10 +236,11 @@ def test_repeat_calls_deterministic(native, layer1, bank1, S):
     np.testing.assert_array_equal(a[0], b[0])
 
 
-@pytest.mark.parametrize('T', [1, 3, 8, 32])
+@pytest.mark.parametrize('T', [1, 3, 8, 32, 40, 300])
 def test_multi_kernel_path_matches_fused(native, layer1, bank1, S, O, T, monkeypatch):
-    """Decode batches run the fused persistent kernel; the multi-kernel path
-    (forced through the environment) must give the same bits."""
+    """Decode batches run the fused persistent kernel and larger batches the
+    tensor-core path; the multi-kernel CUDA-core path (forced through the
+    environment) must give the same bits as both."""
     rng = np.random.default_rng(300 + T)
     x = S.make_tokens(rng, T)
     w, ids = S.random_routes(rng, T, pad_fraction=0.1)
