@@ -17,7 +17,9 @@ stream, barrier + synchronize on both sides, max over ranks.  Every step reads
 (distinct experts + 1) x 1.62 MB per layer, far more than the 126 MB L2, so no
 explicit flush is needed (config.l2 says so).  `e2e` repeats the measurement
 through the same public operator with host (pinned) inputs copied in and the
-final output copied out inside the timed region.
+final output copied out inside the timed region.  A decode step is captured
+once as a CUDA graph of those operator calls and replayed (as a serving engine
+does); --no-graph times the eager launches.
 
 --impl reference times the reference's own routed source compiled for the CPU
 (oracle/_ref, built by oracle/build_ref.py) on this host's cores on a bounded
@@ -57,6 +59,7 @@ def parse():
     p.add_argument('--config', default='decode1', choices=sorted(CONFIGS))
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
+    p.add_argument('--no-graph', action='store_true', help='time eager launches instead of a captured step')
     p.add_argument('--layers', type=int, default=None,
                    help='override the layer count (small cases for profiler captures)')
     return p.parse_args()
@@ -144,6 +147,15 @@ class Stack:
         self.gen = gen
 
 
+def launches_per_step(lib, step_fn):
+    """Kernels one step enqueues: counted by running the step eagerly once."""
+    import torch
+    n0 = lib.ornith_moe_b200_kernel_launches()
+    step_fn()
+    torch.cuda.synchronize()
+    return lib.ornith_moe_b200_kernel_launches() - n0
+
+
 def run(args):
     import torch
     import torch.distributed as dist
@@ -186,11 +198,16 @@ def run(args):
             native.routed_from_logits(x, lg, gc, gm, dc, dm, None, None, None, None, None, None, None,
                                       ws, out, None, flags[l:l + 1], T, bits)
 
-    def step(s, x):
-        lg = logits[s % n_logit_sets]
+    # static inputs: a step reads its token rows and router logits from these
+    static_logits = logits[0].clone()
+    x_static = x0
+
+    def step_static():
         for l in range(L):
-            layer_call(l, x, lg[l], outs[l % 2])
-        return outs[(L - 1) % 2]
+            layer_call(l, x_static, static_logits[l], outs[l % 2])
+
+    def stage_inputs(s):
+        static_logits.copy_(logits[s % n_logit_sets], non_blocking=True)
 
     # algorithmic bytes per step: (distinct experts + 1) * EXPERT_BYTES per layer + activations
     ids = torch.topk(logits, 8, dim=-1).indices  # [sets, L, T, 8]
@@ -206,7 +223,45 @@ def run(args):
         return distinct[s % n_logit_sets] * EXPERT_BYTES + act_bytes
 
     for s in range(args.warmup):
-        step(s, x0)
+        stage_inputs(s)
+        step_static()
+    torch.cuda.synchronize()
+
+    # Decode steps are captured once as a CUDA graph and replayed (the way a
+    # serving engine runs decode); the layer calls inside are the same C-ABI
+    # launches.  Each replay is preceded by a device copy of that step's logits.
+    graph, graph_error = None, None
+    layer_graphs = []
+    if not args.no_graph:
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                step_static()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step_static()
+            for l in range(L):
+                g1 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g1):
+                    layer_call(l, x_static, static_logits[l], outs[l % 2])
+                layer_graphs.append(g1)
+            torch.cuda.synchronize()
+        except Exception as exc:  # capture unsupported: time the eager launches instead
+            graph, layer_graphs, graph_error = None, [], repr(exc)[:200]
+            torch.cuda.synchronize()
+
+    def run_step(s):
+        stage_inputs(s)
+        if graph is not None:
+            graph.replay()
+        else:
+            step_static()
+
+    for s in range(args.warmup):
+        run_step(s)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -216,10 +271,12 @@ def run(args):
     with ClockSampler(local) as clk:
         start.record()
         for s in range(args.warmup, steps_total):
-            step(s, x0)
+            run_step(s)
         end.record()
         torch.cuda.synchronize()
-    launches = lib.ornith_moe_b200_kernel_launches() - launches0
+    # kernels of this library enqueued per step (graph replays re-run the captured launches)
+    launches = (lib.ornith_moe_b200_kernel_launches() - launches0) if graph is None else \
+        launches_per_step(lib, step_static) * args.steps
     ms = start.elapsed_time(end)
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -229,13 +286,19 @@ def run(args):
     value = world * T * args.steps / (ms / 1e3)
     bytes_timed = sum(step_bytes(s) for s in range(args.warmup, steps_total)) / args.steps
 
-    # per-layer-call timing (the layer call is the dominant launch group of a step)
+    # per-layer timing: each layer call (routing + fused layer kernel) replayed
+    # as its own graph between events, layers in sequence so that weights stream
+    # from HBM as in a step
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
     per_layer = []
     for rep in range(3):
+        stage_inputs(args.warmup + rep)
         for l in range(L):
             ev[l][0].record()
-            layer_call(l, x0, logits[(args.warmup + rep) % n_logit_sets][l], outs[l % 2])
+            if layer_graphs:
+                layer_graphs[l].replay()
+            else:
+                layer_call(l, x_static, static_logits[l], outs[l % 2])
             ev[l][1].record()
         torch.cuda.synchronize()
         per_layer += [a.elapsed_time(b) for a, b in ev]
@@ -245,22 +308,23 @@ def run(args):
     peak = peaks.get('hbm_gbs', 6650.0)
     achieved = layer_bytes / (layer_ms * 1e-3) / 1e9
 
-    # end to end through the public operator, host buffers in and out
+    # end to end through the public operator: pinned host inputs copied in, the
+    # step (graph of the operator's launches) run, the last output copied out
     pin_x = x0.cpu().pin_memory()
     pin_logits = logits[: min(n_logit_sets, 4)].cpu().pin_memory()
     pin_out = torch.empty((T, 2048), dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty_like(x0)
-    lg_dev = torch.empty_like(logits[0])
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for s in range(args.steps):
-        x_dev.copy_(pin_x, non_blocking=True)
-        lg_dev.copy_(pin_logits[s % pin_logits.shape[0]], non_blocking=True)
-        for l in range(L):
-            layer_call(l, x_dev, lg_dev[l], outs[l % 2])
+        x_static.copy_(pin_x, non_blocking=True)
+        static_logits.copy_(pin_logits[s % pin_logits.shape[0]], non_blocking=True)
+        if graph is not None:
+            graph.replay()
+        else:
+            step_static()
         pin_out.copy_(outs[(L - 1) % 2], non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
@@ -293,8 +357,11 @@ def run(args):
                      'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback'},
         'step_roofline_frac': round(bytes_timed / (ms_step * 1e-3) / 1e9 / peak, 4),
         'flags_max': flag_any,
+        'cuda_graph': graph is not None,
         'clocks': clk.summary(),
     }
+    if graph_error:
+        result['cuda_graph_error'] = graph_error
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(cfg, args.cpu_seconds)
     if world > 1:

@@ -67,7 +67,7 @@ struct Smem {
     uint8_t* dbuf;    // [kNCW][kChunk][512]
     float* dscale;    // [kNCW][kChunk][2]
     int* dsum;        // [kNCW][kChunk][2]
-    int* misc;        // [0] abort, [1] issued stages, [2] nact, [3] NA
+    int* misc;        // [0] abort, [1] final issued count, [2] nact, [3] NA, [4] issued so far
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -113,28 +113,42 @@ __device__ __forceinline__ void warp_flag_or(uint32_t* flags, uint32_t f) {
     if (f && (threadIdx.x & 31) == 0) atomicOr(flags, f);
 }
 
-// Raise the abort state (CTA-local and global) and flag 64.
-__device__ __forceinline__ void give_up(const LayerArgs& a, Smem& s, uint32_t* ctrl) {
+// Raise the abort state (CTA-local and global) and flag 64; the first CTA to
+// give up records where (kCtrlGiveUp) for the caller's diagnosis.
+__device__ __forceinline__ void give_up(const LayerArgs& a, Smem& s, uint32_t* ctrl, uint32_t tag, uint32_t x,
+                                        uint32_t y, uint32_t observed) {
     atomicOr(a.flags, kFlagWaitTimeout);
     atomicExch(&s.misc[0], 1);
+    if (atomicCAS(ctrl + kCtrlGiveUp, 0u, tag) == 0u) {
+        ctrl[kCtrlGiveUp + 1] = blockIdx.x;
+        ctrl[kCtrlGiveUp + 2] = threadIdx.x >> 5;
+        ctrl[kCtrlGiveUp + 3] = x;
+        ctrl[kCtrlGiveUp + 4] = y;
+        ctrl[kCtrlGiveUp + 5] = observed;
+    }
     atomicExch(ctrl + kCtrlAbort, 1u);
 }
 
 // Bounded wait for ring stage `st` to be filled.  Returns false when the
 // stage was never issued because the CTA is aborting.
+// Different warps consume different ring stages, so a warp can reach stage st
+// before the slot's previous use (st - nst) has even landed.  An mbarrier
+// parity wait cannot tell phases two apart, so the warp first waits until the
+// producer has published that stage st was issued (misc[4] > st); from then
+// on the slot's barrier is at most one phase behind and the parity is exact.
 __device__ bool wait_stage(const LayerArgs& a, Smem& s, uint32_t* ctrl, int st, int nst) {
     const int slot = st % nst;
     const uint32_t parity = uint32_t(st / nst) & 1u;
+    volatile int* misc = s.misc;
     uint64_t t0 = 0;
     for (int i = 0;; ++i) {
-        if (mbar_try_wait(&s.full[slot], parity)) return true;
-        volatile int* misc = s.misc;
+        if (misc[4] > st && mbar_try_wait(&s.full[slot], parity)) return true;
         if (misc[0] && st >= misc[1]) return false;
         if (i == 0) t0 = now_ns();
         else if ((i & 63) == 0 && now_ns() - t0 > kTimeoutNs) {
-            give_up(a, s, ctrl);
+            give_up(a, s, ctrl, 1u, uint32_t(st), uint32_t(slot), uint32_t(misc[4]));
             // the copy, if it was issued, still lands: wait for it (bounded) before leaving
-            if (st < misc[1]) {
+            if (st < misc[4]) {
                 uint64_t t1 = now_ns();
                 while (!mbar_try_wait(&s.full[slot], parity) && now_ns() - t1 < kTimeoutNs) {
                 }
@@ -156,7 +170,7 @@ __device__ bool wait_counter(const LayerArgs& a, Smem& s, uint32_t* ctrl, const 
                 break;
             }
             if (now_ns() - t0 > kTimeoutNs) {
-                give_up(a, s, ctrl);
+                give_up(a, s, ctrl, 3u, uint32_t(p - ctrl), target, ld_acquire(p));
                 ok = 0;
                 break;
             }
@@ -245,6 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         fence_barrier_init();
         s.misc[0] = 0;
         s.misc[1] = 0x7fffffff;
+        s.misc[4] = 0;  // stages issued so far (published by the producer)
     }
     for (int e = tid; e <= kE; e += kThreads) s.cnt[e] = 0;
     for (int r = tid; r < R; r += kThreads) s.ids[r] = a.ids[r];
@@ -341,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                         }
                     }
                     if (!ok) {
-                        if (!misc[0]) give_up(a, s, ctrl);
+                        if (!misc[0]) give_up(a, s, ctrl, 2u, uint32_t(st), uint32_t(slot), 0u);
                         break;
                     }
                 }
@@ -381,6 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 mbar_arrive_expect_tx(&s.full[slot], kStageBytes);
                 bulk_g2s(dst, codes, 4096, &s.full[slot]);
                 bulk_g2s(dst + 4096, meta, 128, &s.full[slot]);
+                __threadfence_block();
+                misc[4] = st + 1;
             }
             atomicExch(&s.misc[1], st);  // stages actually issued
         }
@@ -750,7 +767,7 @@ cudaError_t launch_decode(const LayerArgs& a, cudaStream_t stream) {
             return st;
         dc.attr_set[which] = true;
     }
-    if ((st = cudaMemsetAsync(a.ws + a.L.ctrl, 0, (kCtrlAbort + 1) * sizeof(uint32_t), stream)) != cudaSuccess)
+    if ((st = cudaMemsetAsync(a.ws + a.L.ctrl, 0, kCtrlClearWords * sizeof(uint32_t), stream)) != cudaSuccess)
         return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(dc.sms);

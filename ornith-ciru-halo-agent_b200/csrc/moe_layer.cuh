@@ -31,6 +31,11 @@ constexpr int kCtrlGateDone = 32;      // [E+1] gate items finished per expert s
 constexpr int kCtrlReady = 320;        // [E+1] middle of the expert slot quantised
 constexpr int kCtrlColDone = 608;      // [64] down items finished per output tile
 constexpr int kCtrlAbort = 700;        // any CTA gave up a bounded wait
+// first bounded wait that gave up: [tag, cta, warp, x, y, observed], tag 1 = ring
+// stage (x = stage, y = slot), 2 = producer slot reuse (x = stage, y = slot),
+// 3 = global counter (x = ctrl word, y = target, observed = last value)
+constexpr int kCtrlGiveUp = 704;
+constexpr int kCtrlClearWords = 712;   // words zeroed before every fused launch
 
 Workspace workspace_layout(int Tcap);
 
