@@ -163,6 +163,23 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine(
 /* Workspace size for ornith_moe_b200_launch_from_logits (0 <= Tcap <= 8192). */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes);
 
+/* ornith_routed_direct_launch (A8) for callers that cannot allocate device
+ * memory: plugins inside frameworks that own every allocation and pass only
+ * inputs and outputs, embedders without access to an allocator at the launch
+ * site, and code that must not call cudaMalloc while others capture the
+ * stream.  No counterpart in the reference.  The scratch is a fixed 1 MiB
+ * array inside this library that every GPU loading the library keeps until
+ * exit; it limits a call to T <= 8 tokens (larger T: cudaErrorInvalidValue).
+ * Every call on a device shares that array, so calls that can overlap on the
+ * GPU race: order them on one stream.  The first call on a device looks up the
+ * array's address and should come before any stream capture.  The library
+ * calls no allocator.  Arguments and results otherwise as
+ * ornith_routed_direct_launch. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_direct_launch_noalloc(
+    const void* input_bf16, const void* route_weights_f32, const void* ids_i32,
+    const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
+    void* output_bf16, void* flags_u32, int T, cudaStream_t stream);
+
 /* One-time repack of the reference checkpoint's N16 banks into N32 storage
  * (plugin-site/ornith_g256/method.py:124-158, prepare_n32_weights):
  * codes [E][N/16][K/256][32][16] -> [E][N/32][K/256][32][32], metadata

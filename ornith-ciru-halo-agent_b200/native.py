@@ -54,6 +54,7 @@ SIGNATURES = {
     'ornith_moe_b200_get_layout': ([C.c_int, C.POINTER(C.c_size_t)], C.c_int),
     'ornith_moe_b200_combine': ([C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3, C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
+    'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
 }
 
 
