@@ -47,6 +47,12 @@ CONFIGS = {
     'decode32': dict(T=32, layers=40, bias=0.5, act_bits=8, shared=True, name='decode B=32, 40-layer stack (configs[2])'),
     'prefill1120': dict(T=1120, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 1120 (configs[3])'),
     'prefill8192': dict(T=8192, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 8192 (configs[3])'),
+    # expert-parallel sweep: total tokens fixed, experts sharded over the ranks
+    'ep_decode256': dict(T=256, layers=40, bias=0.0, act_bits=8, shared=False, ep=True,
+                         name='expert-parallel decode B=256, 40 layers, Zipf(1.2) expert skew (configs[4])'),
+    'ep_prefill8192': dict(T=8192, layers=4, bias=0.0, act_bits=4, shared=False, ep=True,
+                           name='expert-parallel prefill 8192 tokens, Zipf(1.2) expert skew (configs[4]); '
+                                '4 weight sets cycled'),
 }
 
 
@@ -145,6 +151,86 @@ class Stack:
         self.silu = torch.from_numpy(tab['silu_fp32']).to(dev)
         self.sigmoid = torch.from_numpy(tab['sigmoid_bf16'].view(np.int16)).to(dev).view(torch.bfloat16)
         self.gen = gen
+
+
+def run_ep(args):
+    """Expert-parallel step: every rank routes its share of the tokens and runs
+    each layer through ornith_b200.ep (NCCL all-to-all dispatch, local experts,
+    return of the fp32 per-slot rows, slot-ordered combine)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg['layers'] = args.layers
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    os.environ.setdefault('MASTER_ADDR', '127.0.0.1')
+    os.environ.setdefault('MASTER_PORT', '29541')
+    dist.init_process_group('nccl' if world > 1 else 'gloo', rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    graft.load_package()
+    import importlib
+    native = importlib.import_module('ornith_b200.native')
+    ep = importlib.import_module('ornith_b200.ep')
+    S = importlib.import_module('ornith_b200.synthetic')
+    T_total, L, bits = cfg['T'], cfg['layers'], cfg['act_bits']
+    T = T_total // world
+    epr = 256 // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+    layers = []
+    for _ in range(L):
+        g = device_bank(torch, gen, dev, epr, 1024, 2048)
+        d = device_bank(torch, gen, dev, epr, 2048, 512)
+        layers.append(ep.ExpertParallelMoE(None, world, (g[0], g[1], d[0], d[1]), capacity=min(T * world, 8192),
+                                           act_bits=bits))
+    bias = torch.from_numpy(S.zipf_bias(np.random.default_rng(12), 256, 1.2)).to(dev)  # same on every rank
+    logits = torch.randn((L, T, 256), device=dev, generator=gen) + bias
+    x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
+    w = torch.empty((L, T, 8), dtype=torch.float32, device=dev)
+    ids = torch.empty((L, T, 8), dtype=torch.int32, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    for l in range(L):
+        native.route_topk(logits[l], w[l], ids[l], flags)
+
+    def step():
+        for l in range(L):
+            layers[l](x, ids[l], w[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX) if world > 1 else None
+    ms = float(t.item())
+    value = T_total * args.steps / (ms / 1e3)
+    result = {
+        'metric': METRIC, 'value': round(value, 3), 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': round(ms / args.steps, 4), 'higher_is_better': True,
+        'scaling': 'strong', 'vs_baseline': None, 'dtype': 'int8',
+        'data': 'synthetic (seeded random-init weights and logits of the configured shapes)',
+        'config': {'workload': cfg['name'], 'tokens_per_step': T_total, 'tokens_per_rank': T, 'layers': L,
+                   'experts_per_rank': epr, 'parallelism': f'ep{world}',
+                   'exchange': 'NCCL all_to_all_single dispatch + fp32 per-slot return'},
+        'flags': int(flags.item()), 'clocks': clk.summary(),
+    }
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
 
 
 def launches_per_step(lib, step_fn):
@@ -463,5 +549,7 @@ if __name__ == '__main__':
     a = parse()
     if a.impl == 'reference':
         run_reference(a)
+    elif CONFIGS[a.config].get('ep'):
+        run_ep(a)
     else:
         run(a)

@@ -182,6 +182,40 @@ __device__ bool wait_counter(const LayerArgs& a, Smem& s, uint32_t* ctrl, const 
 
 __device__ __forceinline__ int token_of(int route, int R) { return route >= R ? route - R : route / kTop; }
 
+// Exact integer dots of one (tile, group) stage for NRC routes; lane = output
+// column.  Word j of the stage holds this column's codes for k = 8j..8j+7; the
+// even and odd nibbles meet the permuted activation bytes in two __dp4a whose
+// chains are kept apart for instruction-level parallelism (the integer sum is
+// the same in any order).
+template <int NRC>
+__device__ __forceinline__ void stage_dots(const uint32_t* __restrict__ blk, const uint2* const (&act)[8], int lane,
+                                           int (&dot)[8]) {
+    int dl[NRC], dh[NRC];
+#pragma unroll
+    for (int i = 0; i < NRC; ++i) dl[i] = dh[i] = 0;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+        const uint32_t w = blk[j * 32 + lane];
+        const int lo = int(w & 0x0f0f0f0fu), hi = int((w >> 4) & 0x0f0f0f0fu);
+#pragma unroll
+        for (int i = 0; i < NRC; ++i) {
+            const uint2 av = act[i][j];
+            dl[i] = __dp4a(lo, int(av.x), dl[i]);
+            dh[i] = __dp4a(hi, int(av.y), dh[i]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NRC; ++i) dot[i] = dl[i] + dh[i];
+}
+// n routes (1..8): act[i] for i >= n repeats a valid row and its dot is unused.
+__device__ __forceinline__ void stage_dots_n(int n, const uint32_t* blk, const uint2* const (&act)[8], int lane,
+                                             int (&dot)[8]) {
+    if (n == 1) stage_dots<1>(blk, act, lane, dot);
+    else if (n == 2) stage_dots<2>(blk, act, lane, dot);
+    else if (n <= 4) stage_dots<4>(blk, act, lane, dot);
+    else stage_dots<8>(blk, act, lane, dot);
+}
+
 // Transform + quantise one 256-group of one token into the given destination.
 template <int QMAX>
 __device__ void quant_token_group(const LayerArgs& a, int t, int g, int lane, uint2* q, __half* hs, float* fs,
@@ -473,30 +507,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     const uint32_t mw = blk[1024 + lane];
                     const int nchunks = (nr + 7) / 8;
                     for (int c = 0; c < nchunks; ++c) {
+                        const int n = min(8, nr - c * 8);
                         const uint2* act[8];
                         float sa[8];
                         int sm[8], dot[8];
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
-                            const int ri = c * 8 + i < nr ? c * 8 + i : nr - 1;
+                            const int ri = c * 8 + (i < n ? i : n - 1);
                             const int tok = token_of(s.routes[roff + ri], R);
                             act[i] = reinterpret_cast<const uint2*>(s.xq + size_t(tok) * kH + g * kG);
                             sa[i] = s.xs[tok * 8 + g];
                             sm[i] = s.xsum[tok * 8 + g];
-                            dot[i] = 0;
                         }
-#pragma unroll 4
-                        for (int j = 0; j < 32; ++j) {
-                            const uint32_t w = blk[j * 32 + lane];
-                            const int lo = int(w & 0x0f0f0f0fu), hi = int((w >> 4) & 0x0f0f0f0fu);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                if (c * 8 + i < nr) {
-                                    const uint2 av = act[i][j];
-                                    dot[i] = __dp4a(hi, int(av.y), __dp4a(lo, int(av.x), dot[i]));
-                                }
-                            }
-                        }
+                        stage_dots_n(n, blk, act, lane, dot);
                         if (c < kMaxR / 8) {
 #pragma unroll
                             for (int cc = 0; cc < kMaxR / 8; ++cc) {
@@ -642,21 +665,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                         __syncwarp();
                         load_chunk(c);
                     }
-                    int dot[kChunk];
+                    const int n = min(kChunk, nr - c * kChunk);
+                    const uint2* act[8];
 #pragma unroll
-                    for (int i = 0; i < kChunk; ++i) dot[i] = 0;
-#pragma unroll 4
-                    for (int j = 0; j < 32; ++j) {
-                        const uint32_t w = blk[j * 32 + lane];
-                        const int lo = int(w & 0x0f0f0f0fu), hi = int((w >> 4) & 0x0f0f0f0fu);
-#pragma unroll
-                        for (int i = 0; i < kChunk; ++i) {
-                            if (c * kChunk + i < nr) {
-                                const uint2 av = reinterpret_cast<const uint2*>(dbuf + i * 512 + g * kG)[j];
-                                dot[i] = __dp4a(hi, int(av.y), __dp4a(lo, int(av.x), dot[i]));
-                            }
-                        }
-                    }
+                    for (int i = 0; i < 8; ++i)
+                        act[i] = reinterpret_cast<const uint2*>(dbuf + (i < n ? i : n - 1) * 512 + g * kG);
+                    int dot[8];
+                    stage_dots_n(n, blk, act, lane, dot);
                     if (c < kMaxR / kChunk) {
 #pragma unroll
                         for (int cc = 0; cc < kMaxR / kChunk; ++cc) {

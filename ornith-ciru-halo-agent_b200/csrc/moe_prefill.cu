@@ -46,6 +46,7 @@ constexpr int kBpBytes = kNT * 128 / 2;   // packed codes half-tile
 constexpr int kBuBytes = kNT * 128;       // unpacked codes half-tile
 constexpr int kStageBytes = kABytes + kBpBytes + kBuBytes;
 constexpr int kMetaBytes = kNT * 4 + kMT * 4 + kMT * 4;  // B meta, A scale, A sum
+constexpr int kMetaFBytes = kNT * 4 * 2;                   // fp32 column scales then offsets
 constexpr int kWarps = 20;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarps = 16;
@@ -112,6 +113,22 @@ __device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t v) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Named barrier that also ANDs a predicate across the participating threads,
+// so that every thread takes the same exit decision (no thread is ever left
+// waiting at a barrier the others skipped).
+__device__ __forceinline__ bool named_and(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(uint32_t(pred)), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+
 // Bounded mbarrier wait; returns false (and raises the abort state) on timeout.
 __device__ bool bwait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* flags) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -159,7 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* stages = smem;
     uint8_t* metabuf = smem + kStages * kStageBytes;  // [2][kMetaBytes]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(metabuf + 2 * kMetaBytes);
+    float* metaf = reinterpret_cast<float*>(metabuf + 2 * kMetaBytes);  // [2][scales 256 | offsets 256]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(metabuf + 2 * kMetaBytes + 2 * kMetaFBytes);
     uint64_t* full = bars;                       // [kStages] producer -> converters
     uint64_t* conv = bars + kStages;             // [kStages] converters -> MMA
     uint64_t* empty = bars + 2 * kStages;        // [kStages] MMA -> producer
@@ -335,7 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
         }
         uint32_t f = 0;
         int gg = 0;
-        for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
+        const int et = tid - 128;  // 0..511 within the epilogue warps
+        // Every exit from these loops is a collective decision (named_and), so the
+        // 16 warps always pass the same sequence of barrier 1.
+        for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
+            if (!named_and(1, kEpiWarps * 32, !*abort)) break;
             const int4 mt = p.mtiles[unit / NUPT];
             const int nt = unit % NUPT;
             float acc[64];
@@ -344,13 +366,22 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
             bool ok = true;
             for (int g = 0; g < KG; ++g, ++gg) {
                 const int b = gg & 1;
-                if (!bwait(&meta_full[b], uint32_t(gg / 2) & 1u, abort, p.flags) ||
-                    !bwait(&acc_full[b], uint32_t(gg / 2) & 1u, abort, p.flags)) {
-                    ok = false;
-                    break;
+                const bool mine = ok && bwait(&meta_full[b], uint32_t(gg / 2) & 1u, abort, p.flags);
+                // the group's column metadata, converted once for all rows
+                if (mine && et < kNT) {
+                    const uint32_t mw = reinterpret_cast<const uint32_t*>(metabuf + b * kMetaBytes)[et];
+                    metaf[b * 2 * kNT + et] = __half2float(__ushort_as_half(uint16_t(mw & 0xffffu)));
+                    metaf[b * 2 * kNT + kNT + et] = __half2float(__ushort_as_half(uint16_t(mw >> 16)));
+                }
+                ok = named_and(1, kEpiWarps * 32, mine);
+                if (!ok) break;
+                if (!bwait(&acc_full[b], uint32_t(gg / 2) & 1u, abort, p.flags)) {
+                    ok = false;  // voted at the next barrier
+                    continue;
                 }
                 tc_fence_after();
-                const uint32_t* bm = reinterpret_cast<const uint32_t*>(metabuf + b * kMetaBytes);
+                const float* swf = metaf + b * 2 * kNT;
+                const float* offf = swf + kNT;
                 const float sa = reinterpret_cast<const float*>(metabuf + b * kMetaBytes + kNT * 4)[row];
                 const int ssumi = reinterpret_cast<const int32_t*>(metabuf + b * kMetaBytes + kNT * 4 + kMT * 4)[row];
                 const float ssum = __fmul_rn(sa, float(ssumi));
@@ -362,14 +393,18 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                     tmem_ld16(base + col, r);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const uint32_t mw = bm[col + i];
-                        const float fd = __fsub_rn(__uint_as_float(r[i]), kMagicF);
-                        const float scaled_dot = __fmul_rn(sa, fd);
-                        const float product =
-                            __fmul_rn(__half2float(__ushort_as_half(uint16_t(mw & 0xffffu))), scaled_dot);
-                        const float correction = __fmul_rn(__half2float(__ushort_as_half(uint16_t(mw >> 16))), ssum);
-                        acc[part * 16 + i] = __fadd_rn(acc[part * 16 + i], __fadd_rn(product, correction));
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 sw4 = *reinterpret_cast<const float4*>(swf + col + 4 * q);
+                        const float4 of4 = *reinterpret_cast<const float4*>(offf + col + 4 * q);
+                        const float sw[4] = {sw4.x, sw4.y, sw4.z, sw4.w}, of[4] = {of4.x, of4.y, of4.z, of4.w};
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            const int i = 4 * q + h;
+                            const float fd = __fsub_rn(__uint_as_float(r[i]), kMagicF);
+                            const float scaled_dot = __fmul_rn(sa, fd);
+                            const float term = __fadd_rn(__fmul_rn(sw[h], scaled_dot), __fmul_rn(of[h], ssum));
+                            acc[part * 16 + i] = __fadd_rn(acc[part * 16 + i], term);
+                        }
                     }
                     tmem_st16_const(base + col, kMagic);
                 }
@@ -603,7 +638,7 @@ __global__ __launch_bounds__(256) void pack_middle_kernel(LayerArgs a) {
     if (f && lane == 0) atomicOr(a.flags, f);
 }
 
-constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + 2 * kMetaBytes + 64 * 8 + 64;
+constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + 2 * kMetaBytes + 2 * kMetaFBytes + 64 * 8 + 64;
 
 struct DeviceState {
     int sms = 0;

@@ -1,0 +1,91 @@
+"""GPU: expert parallelism over NCCL (needs 2+ GPUs; skipped otherwise).
+
+Two ranks each hold half of the experts and their own tokens; the expert-
+parallel result must equal the single-GPU layer bit for bit.  NVLS is off as
+the pool requires for multi-rank GPU tests."""
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        return s.getsockname()[1]
+
+
+def _bank(gen, experts, N, K, dev):
+    codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (experts, N // 32, K // 256, 32, 32), dtype=torch.int32,
+                          device=dev, generator=gen).view(torch.uint32)
+    z = torch.randn((experts, N // 32, K // 256, 32), device=dev, generator=gen)
+    scale = (0.01 * z.abs()).to(torch.float16).clamp_min(2 ** -14)
+    offset = (scale.float() * -8.0).to(torch.float16)
+    meta = (scale.view(torch.int16).to(torch.int32) & 0xFFFF) | (offset.view(torch.int16).to(torch.int32) << 16)
+    return codes, meta.view(torch.uint32)
+
+
+def _worker(rank, world, port, T, q):
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), NCCL_NVLS_ENABLE='0')
+        torch.cuda.set_device(rank)
+        dev = torch.device('cuda', rank)
+        dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        sys.path.insert(0, str(ROOT))
+        import __graft_entry__ as g
+        g.load_package()
+        from ornith_b200 import ep, native
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(77)                      # identical full banks on every rank
+        gc, gm = _bank(gen, 256, 1024, 2048, dev)
+        dc, dm = _bank(gen, 256, 2048, 512, dev)
+        tok = torch.Generator(device=dev)
+        tok.manual_seed(1000 + rank)             # each rank's own tokens
+        x = torch.randn((T, 2048), device=dev, generator=tok).to(torch.bfloat16)
+        logits = torch.randn((T, 256), device=dev, generator=tok)
+        w = torch.empty((T, 8), dtype=torch.float32, device=dev)
+        ids = torch.empty((T, 8), dtype=torch.int32, device=dev)
+        flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        native.route_topk(logits, w, ids, flags)
+        # single-GPU reference on this rank
+        ws = torch.empty(native.get_layout(T).workspace_bytes, dtype=torch.uint8, device=dev)
+        ref = torch.empty((T, 2048), dtype=torch.bfloat16, device=dev)
+        native.check(native.lib().ornith_routed_direct_launch(
+            *[native.ptr(t) for t in (x, w, ids, gc, gm, dc, dm, ws)], ws.numel(), native.ptr(ref),
+            native.ptr(flags), T, T, native.stream(x)), 'reference layer')
+        epr = 256 // world
+        sl = slice(rank * epr, (rank + 1) * epr)
+        layer = ep.ExpertParallelMoE(None, world, (gc[sl].contiguous(), gm[sl].contiguous(), dc[sl].contiguous(),
+                                                   dm[sl].contiguous()), capacity=T * world)
+        out = layer(x, ids, w)
+        torch.cuda.synchronize()
+        q.put((rank, bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))), int(flags.item()), ''))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:
+        q.put((rank, False, -1, repr(exc)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+@pytest.mark.parametrize('T', [5, 96])
+def test_expert_parallel_matches_single_gpu(T):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, equal, flags, err in results:
+        assert equal and flags == 0, (rank, flags, err)
