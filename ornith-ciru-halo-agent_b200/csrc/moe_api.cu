@@ -32,61 +32,10 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* logits, in
                                                          int32_t* ids, uint32_t* flags) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
-    const float* l = logits + size_t(warp) * kE;
-    float v[8];
-    bool ok[8];
     uint32_t f = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        v[i] = l[lane + 32 * i];
-        ok[i] = isfinite(v[i]);
-        if (!ok[i]) f |= kFlagNonfiniteInput;
-    }
-    float sel_v[kTop];
-    int sel_i[kTop];
-#pragma unroll
-    for (int s = 0; s < kTop; ++s) {
-        float bv = 0.f;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            int idx = lane + 32 * i;
-            if (ok[i] && (bi == 0x7fffffff || v[i] > bv)) {
-                bv = v[i];
-                bi = idx;
-            }
-        }
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, bv, d);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, d);
-            bool take = oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi));
-            if (take) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        sel_v[s] = bv;
-        sel_i[s] = bi == 0x7fffffff ? -1 : bi;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (lane + 32 * i == bi) ok[i] = false;
-    }
-    if (lane == 0) {
-        float ex[kTop], sum = 0.f;
-        const float m = sel_i[0] >= 0 ? sel_v[0] : 0.f;
-#pragma unroll
-        for (int s = 0; s < kTop; ++s) {
-            ex[s] = sel_i[s] >= 0 ? portable_exp(__fsub_rn(sel_v[s], m)) : 0.f;
-            sum = __fadd_rn(sum, ex[s]);
-        }
-#pragma unroll
-        for (int s = 0; s < kTop; ++s) {
-            ids[size_t(warp) * kTop + s] = sel_i[s];
-            weights[size_t(warp) * kTop + s] = sel_i[s] >= 0 ? __fdiv_rn(ex[s], sum) : 0.f;
-        }
-        if (f) atomicOr(flags, f);
-    }
+    route_topk_warp(logits + size_t(warp) * kE, lane, ids + size_t(warp) * kTop, weights + size_t(warp) * kTop, f);
+    f = __reduce_or_sync(0xffffffffu, f);
+    if (f && lane == 0) atomicOr(flags, f);
 }
 
 // Shared-expert gate logit bf16(sum_k x[t,k]*w[k]) with fp32 products and sums:
@@ -94,14 +43,8 @@ __global__ __launch_bounds__(256) void route_topk_kernel(const float* logits, in
 __global__ __launch_bounds__(256) void shared_logit_kernel(const uint16_t* x, const uint16_t* w, int T, uint16_t* logit) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= T) return;
-    float acc = 0.f;
-    for (int i = 0; i < kH / 32; ++i) {
-        int k = lane + 32 * i;
-        acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(x[size_t(warp) * kH + k]), bf16_to_f32(w[k])));
-    }
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
-    if (lane == 0) logit[warp] = bf16_rne(acc);
+    const uint16_t v = shared_logit_warp(x + size_t(warp) * kH, w, lane);
+    if (lane == 0) logit[warp] = v;
 }
 
 // N16 -> N32 bank repack (method.py:142-147).  One thread per destination word.
@@ -178,11 +121,17 @@ void fill_layout(int Tcap, OrnithRoutedDirectLayout* out) {
 // Path selection: the fused persistent kernel for decode batches, the
 // multi-kernel path otherwise.  ORNITH_MOE_B200_PATH=generic forces the
 // multi-kernel path (used by the tests to check both paths).
-cudaError_t run_layer(const LayerArgs& a, cudaStream_t stream) {
+bool force_generic() {
     const char* path = getenv("ORNITH_MOE_B200_PATH");
-    const bool force_generic = path && strcmp(path, "generic") == 0;
-    if (!force_generic && decode_supported(a.T)) return launch_decode(a, stream);
-    if (!force_generic && a.T > kDecodeMaxT) return launch_prefill(a, stream);
+    return path && strcmp(path, "generic") == 0;
+}
+
+// The fused decode kernel serves the call (it also routes from logits itself).
+bool uses_decode(int T) { return !force_generic() && decode_supported(T); }
+
+cudaError_t run_layer(const LayerArgs& a, cudaStream_t stream) {
+    if (uses_decode(a.T)) return launch_decode(a, stream);
+    if (!force_generic() && a.T > kDecodeMaxT) return launch_prefill(a, stream);
     return launch_generic(a, stream);
 }
 
@@ -377,12 +326,24 @@ cudaError_t ornith_moe_b200_launch_from_logits(
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     float* tw = reinterpret_cast<float*>(ws + w.topk_w);
     int32_t* tid = reinterpret_cast<int32_t*>(ws + w.topk_ids);
-    count_launches(1);
-    route_topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(static_cast<const float*>(logits), T, tw, tid,
-                                                        static_cast<uint32_t*>(flags));
-    cudaError_t s = cudaGetLastError();
-    if (s != cudaSuccess) return s;
+    uint16_t* logit = reinterpret_cast<uint16_t*>(ws + w.logit);
+    // decode batches: the fused kernel routes and computes the shared logits
+    // itself (one launch per layer); otherwise two small kernels run first
+    const bool fused = uses_decode(T);
+    cudaError_t s = cudaSuccess;
+    if (!fused) {
+        count_launches(1);
+        route_topk_kernel<<<(T + 7) / 8, 256, 0, stream>>>(static_cast<const float*>(logits), T, tw, tid,
+                                                            static_cast<uint32_t*>(flags));
+        s = cudaGetLastError();
+        if (s != cudaSuccess) return s;
+    }
     LayerArgs a{};
+    if (fused) {
+        a.logits = static_cast<const float*>(logits);
+        a.ids_out = tid;
+        a.weights_out = tw;
+    }
     a.x = static_cast<const uint16_t*>(input);
     a.weights = tw;
     a.ids = tid;
@@ -397,12 +358,16 @@ cudaError_t ornith_moe_b200_launch_from_logits(
     a.T = T;
     a.a8 = bits == 8;
     if (shared) {
-        uint16_t* logit = reinterpret_cast<uint16_t*>(ws + w.logit);
-        count_launches(1);
-        shared_logit_kernel<<<(T + 7) / 8, 256, 0, stream>>>(a.x, static_cast<const uint16_t*>(shared_gate_weight), T,
-                                                             logit);
-        s = cudaGetLastError();
-        if (s != cudaSuccess) return s;
+        if (fused) {
+            a.shared_gate_weight = static_cast<const uint16_t*>(shared_gate_weight);
+            a.logit_out = logit;
+        } else {
+            count_launches(1);
+            shared_logit_kernel<<<(T + 7) / 8, 256, 0, stream>>>(
+                a.x, static_cast<const uint16_t*>(shared_gate_weight), T, logit);
+            s = cudaGetLastError();
+            if (s != cudaSuccess) return s;
+        }
         a.sgate_codes = static_cast<const uint32_t*>(shared_gate_codes);
         a.sgate_meta = static_cast<const uint32_t*>(shared_gate_meta);
         a.sdown_codes = static_cast<const uint32_t*>(shared_down_codes);

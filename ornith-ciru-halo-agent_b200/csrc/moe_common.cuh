@@ -131,18 +131,30 @@ __device__ __forceinline__ void quantize_group_warp(const float (&t)[8], int lan
         v[s] = finite ? t[s] : 0.f;
         absmax = fmaxf(absmax, fabsf(v[s]));
     }
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) absmax = fmaxf(absmax, __shfl_xor_sync(0xffffffffu, absmax, d));
+    // non-negative floats order like their bit patterns: one warp max reduction
+    absmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(absmax)));
     float raw = __fdiv_rn(absmax, float(QMAX));
     bool valid = isfinite(raw) && raw <= 65504.f;
     if (!valid) flags |= kFlagInvalidActivation;
     const bool zero = absmax == 0.f || !valid;
     __half scale = __float2half_rn(zero ? 1.f : fmaxf(raw, 0x1p-14f));
     float sf = __half2float(scale);
+    // q = rint(RN(v / sf)) exactly, mostly without a division: with
+    // r = RN(1/sf) and y = RN(v*r), |y - v/sf| <= 2^-16 and
+    // |RN(v/sf) - v/sf| <= 2^-18 because |v/sf| < 128 (sf is absmax/QMAX
+    // rounded to fp16, or 2^-14 above it).  So y and RN(v/sf) round to the
+    // same integer unless y lies within 2^-15 of a half-integer; only then is
+    // the quotient computed with the IEEE division.
+    const float rcp = __fdiv_rn(1.f, sf);
     int q[8], sum = 0;
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
-        int qi = zero ? 0 : __float2int_rn(__fdiv_rn(v[s], sf));
+        int qi = 0;
+        if (!zero) {
+            const float y = __fmul_rn(v[s], rcp);
+            const float k = rintf(y);
+            qi = __fsub_rn(0.5f, fabsf(__fsub_rn(y, k))) > 0x1p-15f ? int(k) : __float2int_rn(__fdiv_rn(v[s], sf));
+        }
         qi = qi < -QMAX ? -QMAX : (qi > QMAX ? QMAX : qi);
         q[s] = qi;
         sum += qi;
@@ -152,12 +164,25 @@ __device__ __forceinline__ void quantize_group_warp(const float (&t)[8], int lan
     uint32_t odd = (uint32_t(q[1]) & 0xffu) | ((uint32_t(q[3]) & 0xffu) << 8) |
                    ((uint32_t(q[5]) & 0xffu) << 16) | ((uint32_t(q[7]) & 0xffu) << 24);
     q_out[lane] = make_uint2(even, odd);
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    sum = int(__reduce_add_sync(0xffffffffu, uint32_t(sum)));
     if (lane == 0) {
         *scale_out = scale;
         *sum_out = sum;
     }
+}
+
+// Counter updates between CTAs.  red_release_add publishes the caller's
+// earlier writes (and, after a warp or CTA barrier, those of the threads it
+// synchronised with) without waiting for the update to land;
+// atom_add_acq_rel also returns the previous value and acquires what earlier
+// releasers published.
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
 }
 
 // Integer dot of one packed weight word (8 u4 codes, k = 8j+d at bits 4d) with

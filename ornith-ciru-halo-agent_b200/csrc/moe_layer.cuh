@@ -27,15 +27,17 @@ struct Workspace {
 constexpr int kCtrlWords = 2048;
 // ctrl word layout (uint32), zeroed before every fused launch
 constexpr int kCtrlXDone = 0;          // token groups quantised
-constexpr int kCtrlGateDone = 32;      // [E+1] gate items finished per expert slot
-constexpr int kCtrlReady = 320;        // [E+1] middle of the expert slot quantised
-constexpr int kCtrlColDone = 608;      // [64] down items finished per output tile
-constexpr int kCtrlAbort = 700;        // any CTA gave up a bounded wait
+constexpr int kCtrlLogitDone = 1;      // shared-expert logits written (fused routing)
+constexpr int kCtrlRouteDone = 2;      // tokens routed (fused routing spread over CTAs)
+constexpr int kCtrlGateDone = 32;      // [E+1][2] gate-item parts finished per (expert slot, middle half)
+constexpr int kCtrlReady = 576;        // [E+1] middle-quantisation parts finished per expert slot
+constexpr int kCtrlColDone = 864;      // [64] down items finished per output tile
+constexpr int kCtrlAbort = 960;        // any CTA gave up a bounded wait
 // first bounded wait that gave up: [tag, cta, warp, x, y, observed], tag 1 = ring
 // stage (x = stage, y = slot), 2 = producer slot reuse (x = stage, y = slot),
 // 3 = global counter (x = ctrl word, y = target, observed = last value)
-constexpr int kCtrlGiveUp = 704;
-constexpr int kCtrlClearWords = 712;   // words zeroed before every fused launch
+constexpr int kCtrlGiveUp = 964;
+constexpr int kCtrlClearWords = 976;   // words zeroed before every fused launch
 
 Workspace workspace_layout(int Tcap);
 
@@ -58,12 +60,100 @@ struct LayerArgs {
     uint16_t* shared_out;
     uint32_t* flags;
     uint8_t* ws;
+    // fused routing (decode path of the from-logits entry): when `logits` is
+    // set the kernel computes the top-8 ids/weights itself (ids/weights above
+    // are then ignored) and stores them to ids_out/weights_out; when
+    // `shared_gate_weight` is set it also computes the shared-expert logits
+    // into logit_out, which is then what shared_logit points at.
+    const float* logits;
+    const uint16_t* shared_gate_weight;
+    int32_t* ids_out;
+    float* weights_out;
+    uint16_t* logit_out;
     Workspace L;
     int T;
     int a8;
     int shared;
     int shared_all_live;  // shared-slot semantics: every token row is live for the input transform
 };
+
+// Router top-8 of one token by one warp (the role of vLLM's topk_softmax with
+// renormalisation for this layer): the 8 largest finite logits, ties to the
+// lower expert index, softmax over the 8 with the portable exp and a
+// sequential sum.  Lanes 0..7 write ids[s] and weights[s]; a token with fewer
+// than 8 finite logits gets id -1 / weight 0 in the remaining slots.
+// Selection works on order-preserving integer keys (finite logits only, -0
+// folded onto +0 so that equal logits have equal keys) with two warp
+// reductions per round: the largest key, then the lowest index holding it.
+__device__ __forceinline__ uint32_t logit_order_key(float v) {
+    uint32_t b = __float_as_uint(v);
+    if (b == 0x80000000u) b = 0u;
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float logit_from_key(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+// The selection rounds stay a rolled loop: in a decode layer this code runs
+// once per launch, where a short body that stays in the instruction cache
+// beats an unrolled one.
+__device__ __forceinline__ void route_topk_warp(const float* l, int lane, int32_t* ids, float* weights,
+                                                uint32_t& flags) {
+    uint32_t key[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float v = l[lane + 32 * i];
+        const bool ok = isfinite(v);
+        if (!ok) flags |= kFlagNonfiniteInput;
+        key[i] = ok ? logit_order_key(v) : 0u;  // every finite key is >= 0x00800000
+    }
+    float my_v = 0.f;
+    int my_i = -1;
+#pragma unroll 1
+    for (int s = 0; s < kTop; ++s) {
+        const uint32_t lm = max(max(max(key[0], key[1]), max(key[2], key[3])), max(max(key[4], key[5]), max(key[6], key[7])));
+        const uint32_t m = __reduce_max_sync(0xffffffffu, lm);
+        uint32_t li = 0xffffffffu;
+#pragma unroll
+        for (int i = 7; i >= 0; --i)
+            if (m != 0u && key[i] == m) li = uint32_t(lane + 32 * i);
+        const uint32_t idx = __reduce_min_sync(0xffffffffu, li);
+        if (m != 0u) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (uint32_t(lane + 32 * i) == idx) key[i] = 0u;
+        }
+        if (lane == s) {
+            my_i = m != 0u ? int(idx) : -1;
+            my_v = m != 0u ? logit_from_key(m) : 0.f;
+        }
+    }
+    // slot s = lane (lanes 0..7): exp in parallel, the sum in slot order
+    const float top = __shfl_sync(0xffffffffu, my_v, 0);
+    const int top_i = __shfl_sync(0xffffffffu, my_i, 0);
+    const float mx = top_i >= 0 ? top : 0.f;
+    const float ex = (lane < kTop && my_i >= 0) ? portable_exp(__fsub_rn(my_v, mx)) : 0.f;
+    float sum = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < kTop; ++s) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, s));
+    if (lane < kTop) {
+        ids[lane] = my_i;
+        weights[lane] = my_i >= 0 ? __fdiv_rn(ex, sum) : 0.f;
+    }
+}
+
+// Shared-expert gate logit of one token by one warp: fp32 products summed per
+// lane in k order (k = lane + 32i), then an xor-tree across lanes, rounded to
+// bf16.  Every lane returns the bf16 bits.
+__device__ __forceinline__ uint16_t shared_logit_warp(const uint16_t* x, const uint16_t* w, int lane) {
+    float acc = 0.f;
+    for (int i = 0; i < kH / 32; ++i) {
+        const int k = lane + 32 * i;
+        acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(x[k]), bf16_to_f32(w[k])));
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    return bf16_rne(acc);
+}
 
 template <class T>
 __host__ __device__ __forceinline__ T* ws_at(const LayerArgs& a, size_t off) {

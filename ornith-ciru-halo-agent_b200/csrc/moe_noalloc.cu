@@ -15,7 +15,7 @@
 //     process exits;
 //   * every call on a device shares the one array and it keeps the previous
 //     call's contents; the counters that must start at zero are cleared by
-//     each launch itself (cudaMemsetAsync on the caller's stream) and nothing
+//     each launch itself (a clearing kernel on the caller's stream) and nothing
 //     else is assumed to be zero;
 //   * two calls whose work can overlap on the GPU (different streams without
 //     ordering between them, or different host threads) race on the array, so

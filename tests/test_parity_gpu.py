@@ -114,6 +114,11 @@ def test_route_topk_bit_exact(native, O):
     logits[1, :] = -np.inf
     logits[1, 5] = 1.0
     logits[2, 7] = np.nan
+    logits[3, :] = 0.0          # +0 / -0 ties: equal logits, lower index first
+    logits[3, 1::3] = -0.0
+    logits[4, :] = np.nan       # no finite logit: ids -1, weights 0
+    logits[5, :] = -np.inf      # three finite logits
+    logits[5, [200, 3, 77]] = [-1.0, -0.0, 0.0]
     w_ref, ids_ref = O.route_topk(logits)
     w = torch.empty((777, 8), dtype=torch.float32, device=DEV)
     ids = torch.empty((777, 8), dtype=torch.int32, device=DEV)
@@ -139,6 +144,38 @@ def test_config1_from_logits(native, golden, S):
         torch.cuda.synchronize()
         np.testing.assert_array_equal(host_bits(out), golden[f'config1/out_{key}'])
         assert int(flags.item()) == int(golden[f'config1/flags_{key}'])
+
+
+def edge_logits(rng, T):
+    logits = rng.standard_normal((T, 256)).astype(np.float32)
+    logits[0, 10] = logits[0, 20] = logits[0, 30] = 9.0
+    logits[1, :] = 0.0
+    logits[1, ::2] = -0.0
+    logits[2, :] = -np.inf
+    logits[2, [5, 250, 17]] = [0.5, 0.5, -3.0]
+    logits[3, 7] = np.nan
+    logits[3, 8] = np.inf
+    return logits
+
+
+@pytest.mark.parametrize('T', [1, 4, 8, 16, 27, 32])
+def test_fused_routing_edges(native, layer1, bank1, S, O, T):
+    """The decode kernel's own top-8 (from-logits entry, T <= 32) on ties,
+    signed zeros, non-finite logits and tokens with fewer than 8 finite ones."""
+    rng = np.random.default_rng(900 + T)
+    x = S.make_tokens(rng, T)
+    logits = edge_logits(rng, max(T, 4))[:T]
+    w, ids = O.route_topk(logits)
+    ref, _, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=True)
+    ws = torch.empty(native.workspace_bytes(T), dtype=torch.uint8, device=DEV)
+    out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    native.routed_from_logits(dev(x), dev(logits), *bank1.routed, None, None, None, None, None, None, None,
+                              ws, out, None, flags, T, 8)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(host_bits(out), ref)
+    want = ref_flags | (1 if not np.isfinite(logits).all() else 0)
+    assert int(flags.item()) == want
 
 
 def shared_logit_like_device(x_bits, w_bits):
@@ -199,6 +236,26 @@ def test_flags_and_edges_vs_oracle(native, layer1, bank1, S, O):
         assert flags == ref_flags and flags & 4 and flags & 1
 
 
+def test_latency_mode_edges_vs_oracle(native, layer1, bank1, S, O):
+    """Two tokens (the fused kernel's tile-local mode): non-finite and huge
+    inputs, a duplicate expert, padded slots and an invalid id."""
+    rng = np.random.default_rng(78)
+    T = 2
+    x = S.make_tokens(rng, T)
+    w, ids = S.random_routes(rng, T)
+    x[0, 5] = 0x7F80            # +inf input
+    ids[0, 3] = ids[0, 0]       # duplicate expert in one token
+    x[1, :256] = 0x7F00         # huge values: invalid activation scale (flag 2)
+    ids[1, 1] = 256             # invalid id (flag 4)
+    ids[1, 5:] = -1             # padded slots
+    for a8, symbol in ((True, 'ornith_routed_direct_launch'), (False, 'ornith_routed_direct_launch_a4')):
+        ref, ref_f32, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=a8)
+        out, final, flags = run_entry(native, symbol, x, w, ids, bank1)
+        np.testing.assert_array_equal(out, ref)
+        np.testing.assert_array_equal(final.view(np.uint32), ref_f32.view(np.uint32))
+        assert flags == ref_flags and flags & 4 and flags & 1
+
+
 def test_prefill_1120_sampled_tokens(native, layer1, bank1, S, O):
     """Chunked-prefill shape: tokens are independent, so 48 sampled tokens of
     the full 1120-row call are checked against the oracle run on just them."""
@@ -253,7 +310,7 @@ def test_multi_kernel_path_matches_fused(native, layer1, bank1, S, O, T, monkeyp
     assert fused[2] == multi[2] == ref_flags
 
 
-@pytest.mark.parametrize('T', [5, 32])
+@pytest.mark.parametrize('T', [1, 2, 5, 32])
 def test_duplicate_expert_ids(native, layer1, bank1, S, O, T):
     """Collisions: the same expert several times in one token.  At T=32 one
     expert receives 96 routes, beyond the fused kernel's register budget."""
@@ -270,17 +327,18 @@ def test_duplicate_expert_ids(native, layer1, bank1, S, O, T):
         assert flags == ref_flags
 
 
-def test_all_slots_padded(native, layer1, bank1, S):
+@pytest.mark.parametrize('T', [1, 4])
+def test_all_slots_padded(native, layer1, bank1, S, T):
     rng = np.random.default_rng(5)
-    x = S.make_tokens(rng, 4)
-    w = np.ones((4, 8), np.float32)
-    ids = -np.ones((4, 8), np.int32)
+    x = S.make_tokens(rng, T)
+    w = np.ones((T, 8), np.float32)
+    ids = -np.ones((T, 8), np.int32)
     out, final, flags = run_entry(native, 'ornith_routed_direct_launch', x, w, ids, bank1)
     assert not out.any() and not final.any() and flags == 0
 
 
-def test_shared_slot_with_all_routed_padded(native, layer1, bank1, S, O, tables):
-    T = 3
+@pytest.mark.parametrize('T', [1, 3])
+def test_shared_slot_with_all_routed_padded(native, layer1, bank1, S, O, tables, T):
     rng = np.random.default_rng(6)
     x = S.make_tokens(rng, T)
     w = np.ones((T, 8), np.float32)
