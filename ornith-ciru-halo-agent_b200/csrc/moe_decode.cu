@@ -36,8 +36,12 @@
 namespace ornith {
 namespace {
 
-constexpr int kNCW = 8;                       // consumer warps
-constexpr int kThreads = (kNCW + 1) * 32;     // + one producer warp
+constexpr int kNCW = 8;                       // consumer (dot) warps
+constexpr int kEW = 2;                        // epilogue warps (throughput mode)
+constexpr int kProd = kNCW + kEW;             // producer warp
+constexpr int kWarps = kProd + 1;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTChunk = 4;                    // routes per throughput-mode gate unit
 constexpr int kStageBytes = 4096 + 128;       // one (tile, group) block: codes + metadata
 constexpr int kChunk = 8;                     // routes per dot pass
 constexpr uint64_t kTimeoutNs = 1000000000ull;
@@ -45,7 +49,12 @@ constexpr int kRedundantX = 4;                // T <= 4: every CTA quantises all
 constexpr uint32_t kGateTarget = 8 * kNCW;    // GateDone[slot][half]: 8 gate items x 8 warps
 constexpr uint32_t kReadyTarget = 2 * kNCW;   // Ready[slot]: 2 halves x 8 warps
 constexpr int kMaxTasks = 64;                 // middle-quantisation tasks per CTA (one per gate item at most)
-constexpr int kBarConsumers = 1;              // named barrier of the 8 consumer warps; 2..5 = down pairs
+// named barriers: 1 = the 8 consumer warps, 2..5 = down pairs, 6/7 = gate
+// terms ready in buffer 0/1, 8/9 = buffer 0/1 free again, 10 = consumers and
+// epilogue warps, 11 = the two epilogue warps
+constexpr int kBarConsumers = 1;
+constexpr int kBarTermsReady = 6, kBarTermsFree = 8, kBarDotE = 10, kBarE = 11;
+constexpr int kDotEThreads = (kNCW + kEW) * 32;
 constexpr int kMinStages = 18;                // ring stages needed: one gate item plus slack
 constexpr int kTiles = kH / 32;               // 32-column output tiles of a down projection
 // Expert slots with at most this many routes skip the ready handoff: each
@@ -79,19 +88,23 @@ __device__ unsigned long long g_decode_trace[kTraceCtas][kTraceSlots];
 __device__ __forceinline__ void named_barrier(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+__device__ __forceinline__ void named_barrier_arrive(int id, int threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 struct Smem {
     uint8_t* ring;
     uint64_t* full;
     uint64_t* empty;
+    int* last_st;     // [nst] last stage issued into each ring slot (-1: none)
     uint8_t* xq;      // [T][2048] permuted int8
     __half* xs;       // [T][8]
     int* xsum;        // [T][8]
     int* ids;         // [R]
     float* wts;       // [R]
-    int* cnt;         // [E+1] counts, then placement cursors
-    int* off;         // [E+1]
+    int* cnt;         // [E+1] counts, then placement cursors (plan only, inside tbuf)
+    int* off;         // [E+1] (plan only, inside tbuf)
     int* act_e;       // [E+1] expert of active slot k
     int* act_off;     // [E+1]
     int* act_cnt;     // [E+1]
@@ -101,17 +114,20 @@ struct Smem {
     __half* dscale;   // [kNCW][kChunk]
     int* dsum;        // [kNCW][kChunk]
     int* tasks;       // [kMaxTasks] posted middle-quantisation tasks (2*slot + half)
-    uint32_t* xflag;  // [8 kRedundantX] flags of each token group quantised during routing
-    int* wpre;        // [2][E+2] cost prefixes of the slots' gate items and down items (T > 4)
-    int* misc;        // [0] abort, [1] final issued count, [2] nact, [3] NA, [4] issued so far, [5] tasks posted
+    uint32_t* xflag;  // [8 kRedundantX] flags of each token group quantised during routing (plan only, inside tbuf)
+    int* wpre;        // [2][E+2] cost prefixes of the slots' gate items and down items (plan only, inside tbuf)
+    int* misc;        // [0] abort, [1] final issued count, [2] nact, [3] NA, [4] issued so far, [5] tasks posted,
+                      // [6..9] this CTA's gate and down item ranges (throughput mode)
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+static_assert((3 * (kE + 4) + 2 * (kE + 2)) * 4 + 8 * kRedundantX * 4 <= kNCW * 2 * kChunk * 32 * 4,
+              "plan-only arrays must fit inside tbuf");
 
 // Byte offsets of the shared-memory carve for T tokens and nst ring stages.
 struct Carve {
-    size_t ring, full, empty, xq, xs, xsum, ids, wts, cnt, off, act_e, act_off, act_cnt, routes, tbuf, pbuf, dscale,
-        dsum, tasks, xflag, wpre, misc, total;
+    size_t ring, full, empty, last_st, xq, xs, xsum, ids, wts, act_e, act_off, act_cnt, routes, tbuf, pbuf, dscale,
+        dsum, tasks, misc, total;
 };
 __host__ __device__ inline Carve carve(int T, int nst) {
     Carve c{};
@@ -125,13 +141,12 @@ __host__ __device__ inline Carve carve(int T, int nst) {
     add(c.ring, size_t(nst) * kStageBytes, 128);
     add(c.full, size_t(nst) * 8, 8);
     add(c.empty, size_t(nst) * 8, 8);
+    add(c.last_st, size_t(nst) * 4, 4);
     add(c.xq, size_t(T) * kH, 16);
     add(c.xs, size_t(T) * 8 * 2, 16);
     add(c.xsum, size_t(T) * 8 * 4, 16);
     add(c.ids, R * 4 + 4, 16);
     add(c.wts, R * 4 + 4, 16);
-    add(c.cnt, (kE + 1) * 4, 16);
-    add(c.off, (kE + 1) * 4, 16);
     add(c.act_e, (kE + 1) * 4, 16);
     add(c.act_off, (kE + 1) * 4, 16);
     add(c.act_cnt, (kE + 1) * 4, 16);
@@ -141,8 +156,6 @@ __host__ __device__ inline Carve carve(int T, int nst) {
     add(c.dscale, size_t(kNCW) * kChunk * 2, 16);
     add(c.dsum, size_t(kNCW) * kChunk * 4, 16);
     add(c.tasks, kMaxTasks * 4, 16);
-    add(c.xflag, 8 * kRedundantX * 4, 16);
-    add(c.wpre, 2 * (kE + 2) * 4, 16);
     add(c.misc, 16 * 4, 16);
     c.total = align_up(cur, 128);
     return c;
@@ -421,6 +434,152 @@ __device__ __forceinline__ int range_start(const int* W, int NA, int per_slot, i
     return first_item(W, NA, per_slot, int((total * b + G - 1) / G));
 }
 
+// ---- throughput-mode pieces shared by the consumer and epilogue warps ----
+
+constexpr uint32_t kGateTargetThr = 8;   // split (slot, half): one count per gate item
+constexpr uint32_t kReadyTargetThr = 2;  // one count per quantised half
+constexpr int kHeavyTask = 8;            // halves with more routes are quantised by all warps after the items
+// gate terms of unit buffer `buf`, K-group g, role (0 gate, 1 up), route i of the unit
+__device__ __forceinline__ int term_index(int buf, int g, int role, int i, int lane) {
+    return (((buf * 8 + g) * 2 + role) * kTChunk + i) * 32 + lane;
+}
+
+// Quantisation of (slot, half) groups that are too heavy for the epilogue
+// warps: after the gate items, by the consumer and epilogue warps together
+// (warp index cw over kNCW + kEW warps), one ready count per half.
+template <int QMAX>
+__device__ __forceinline__ void deferred_quant_tasks(const LayerArgs& a, Smem& s, uint32_t* ctrl, int cw, int lane,
+                                                     uint32_t& f) {
+    const int nt = min(*static_cast<volatile int*>(&s.misc[5]), kMaxTasks);
+    for (int t = 0; t < nt; ++t) {
+        const int task = s.tasks[t], kk = task >> 1, hh = task & 1;
+        const int nr2 = s.act_cnt[kk], roff2 = s.act_off[kk];
+        for (int q = cw; q < nr2; q += kNCW + kEW) quant_middle_group<QMAX>(a, s.routes[roff2 + q], hh, lane, f);
+        named_barrier(kBarDotE, kDotEThreads);
+        if (cw == 0 && lane == 0) red_release_add(ctrl + kCtrlReady + kk, 1u);
+    }
+}
+
+// Slot-ordered combine (reduce_slots :176-185) of (tile, token) units
+// cw + b*(kNCW+kEW), + G*(kNCW+kEW), ... once the tile's NA down items are counted.
+__device__ __forceinline__ void combine_units(const LayerArgs& a, Smem& s, uint32_t* ctrl, int T, int R, int G, int b,
+                                              int cw, int lane, int NA, uint32_t& f) {
+    const float* route_out = ws_at<float>(a, a.L.route_out);
+    const uint16_t* logit = a.shared_gate_weight ? a.logit_out : a.shared_logit;
+    bool logit_ok = !(a.shared && a.shared_gate_weight);
+    const volatile int* misc = s.misc;
+    for (int u = b * (kNCW + kEW) + cw; u < T * kTiles; u += G * (kNCW + kEW)) {
+        const int tile = u / T, t = u % T;
+        if (misc[0]) break;
+        if (!wait_counter(a.flags, s.misc, ctrl, ctrl + kCtrlColDone + tile, uint32_t(NA))) break;
+        if (!logit_ok) {
+            if (!wait_counter(a.flags, s.misc, ctrl, ctrl + kCtrlLogitDone, uint32_t(T))) break;
+            logit_ok = true;
+        }
+        const int col = tile * 32 + lane;
+        float sum = 0.f;
+#pragma unroll
+        for (int sl = 0; sl < kTop; ++sl) {
+            const int r = t * kTop + sl;
+            if (id_valid(s.ids[r])) sum = __fadd_rn(sum, __fmul_rn(__ldcg(route_out + size_t(r) * kH + col), s.wts[r]));
+        }
+        const uint16_t res = bf16_rne(sum);
+        ws_at<float>(a, a.L.final_f32)[size_t(t) * kH + col] = sum;
+        a.out[size_t(t) * kH + col] = res;
+        if (!isfinite(sum) || (res & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
+        if (a.shared) {
+            const float gate = bf16_to_f32(a.sigmoid_table[__ldcg(logit + t)]);
+            const float sh = __fmul_rn(__ldcg(route_out + size_t(R + t) * kH + col), gate);
+            a.shared_out[size_t(t) * kH + col] = bf16_rne(sh);
+            if (!isfinite(sh)) f |= kFlagNonfiniteOutput;
+        }
+    }
+}
+
+// Epilogue warps of the throughput mode.  For every gate unit (an item's
+// group terms for up to kTChunk routes, in one of two buffers) they sum the
+// eight K-group terms of each route in ascending order, apply SiLU*up and
+// store the middle row, while the consumer warps already compute the next
+// unit; the buffer handshake is a pair of named barriers per buffer (the
+// consumers arrive on "ready" and wait on "free", these warps the reverse),
+// and the consumers never run more than two units ahead.  After an item
+// they count it for its (slot, half) and quantise a completed half.
+template <int QMAX>
+__device__ __forceinline__ void epilogue_warps(const LayerArgs& a, Smem& s, uint32_t* ctrl, int T, int R, int G, int b,
+                                               int warp, int lane, int NA, int gi0, int ng) {
+    const int e = warp - kNCW;
+    uint32_t f = 0;
+    float* const middle = ws_at<float>(a, a.L.middle);
+    const float* tb = s.tbuf;
+    const volatile int* misc = s.misc;
+    int u = 0;
+    for (int item = 0; item < ng; ++item) {
+        const int gi = gi0 + item, k = gi / 16, p = gi % 16, half = p / 8;
+        const int nr = s.act_cnt[k], roff = s.act_off[k];
+        const bool shared = s.act_e[k] == kE;
+        const bool local_half = k * 16 + 8 * half >= gi0 && k * 16 + 8 * half + 8 <= gi0 + ng;
+        const int nch = (nr + kTChunk - 1) / kTChunk;
+        for (int c = 0; c < nch; ++c, ++u) {
+            const int buf = u & 1;
+            named_barrier(kBarTermsReady + buf, kDotEThreads);
+            const int n = min(kTChunk, nr - c * kTChunk);
+            if (!misc[0]) {
+                for (int r = e; r < n; r += kEW) {
+                    float gv = 0.f, uv = 0.f;
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        gv = __fadd_rn(gv, tb[term_index(buf, g, 0, r, lane)]);
+                        uv = __fadd_rn(uv, tb[term_index(buf, g, 1, r, lane)]);
+                    }
+                    float value;
+                    if (shared) {
+                        gv = bf16_round_f32(gv);
+                        uv = bf16_round_f32(uv);
+                        if (!isfinite(gv) || !isfinite(uv)) f |= kFlagNonfiniteProjection;
+                        value = bf16_round_f32(__fmul_rn(a.silu_table[__float_as_uint(gv) >> 16], uv));
+                    } else {
+                        if (!isfinite(gv) || !isfinite(uv)) f |= kFlagNonfiniteProjection;
+                        value = silu_mul(gv, uv);
+                    }
+                    if (!isfinite(value)) f |= kFlagNonfiniteMiddle;
+                    middle[size_t(s.routes[roff + c * kTChunk + r]) * kI + p * 32 + lane] = value;
+                }
+            }
+            named_barrier_arrive(kBarTermsFree + buf, kDotEThreads);
+        }
+        // the item's middle columns are stored (both warps): count it, and
+        // quantise its (slot, half) once all 8 items are in
+        named_barrier(kBarE, kEW * 32);
+        if (e == 0 && lane == 0) {
+            int task = -1;
+            if (local_half) {
+                if (p % 8 == 7) task = 2 * k + half;
+            } else if (atom_add_acq_rel(ctrl + kCtrlGateDone + 2 * k + half, 1u) == kGateTargetThr - 1) {
+                task = 2 * k + half;
+            }
+            if (task >= 0 && nr > kHeavyTask) {
+                const int t = atomicAdd(&s.misc[5], 1);
+                if (t < kMaxTasks) s.tasks[t] = task;
+                task = -1;
+            }
+            s.misc[10] = task;
+        }
+        named_barrier(kBarE, kEW * 32);
+        const int task = misc[10];
+        if (task >= 0 && !misc[0]) {
+            const int kk = task >> 1, hh = task & 1;
+            const int nr2 = s.act_cnt[kk], roff2 = s.act_off[kk];
+            for (int q = e; q < nr2; q += kEW) quant_middle_group<QMAX>(a, s.routes[roff2 + q], hh, lane, f);
+            named_barrier(kBarE, kEW * 32);
+            if (e == 0 && lane == 0) red_release_add(ctrl + kCtrlReady + kk, 1u);
+        }
+    }
+    named_barrier(kBarDotE, kDotEThreads);  // every item counted, heavy halves posted
+    deferred_quant_tasks<QMAX>(a, s, ctrl, warp, lane, f);
+    combine_units(a, s, ctrl, T, R, G, b, warp, lane, NA, f);
+    warp_flag_or(a.flags, f);
+}
+
 template <int QMAX>
 __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerArgs a, const int nst) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -429,13 +588,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     s.ring = smem_raw + cv.ring;
     s.full = reinterpret_cast<uint64_t*>(smem_raw + cv.full);
     s.empty = reinterpret_cast<uint64_t*>(smem_raw + cv.empty);
+    s.last_st = reinterpret_cast<int*>(smem_raw + cv.last_st);
     s.xq = smem_raw + cv.xq;
     s.xs = reinterpret_cast<__half*>(smem_raw + cv.xs);
     s.xsum = reinterpret_cast<int*>(smem_raw + cv.xsum);
     s.ids = reinterpret_cast<int*>(smem_raw + cv.ids);
     s.wts = reinterpret_cast<float*>(smem_raw + cv.wts);
-    s.cnt = reinterpret_cast<int*>(smem_raw + cv.cnt);
-    s.off = reinterpret_cast<int*>(smem_raw + cv.off);
+    // plan-only arrays live inside tbuf, which the items use only after the plan
+    s.cnt = reinterpret_cast<int*>(smem_raw + cv.tbuf);
+    s.off = s.cnt + (kE + 4);
+    s.wpre = s.off + (kE + 4);
+    s.xflag = reinterpret_cast<uint32_t*>(s.wpre + 2 * (kE + 2));
     s.act_e = reinterpret_cast<int*>(smem_raw + cv.act_e);
     s.act_off = reinterpret_cast<int*>(smem_raw + cv.act_off);
     s.act_cnt = reinterpret_cast<int*>(smem_raw + cv.act_cnt);
@@ -445,8 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     s.dscale = reinterpret_cast<__half*>(smem_raw + cv.dscale);
     s.dsum = reinterpret_cast<int*>(smem_raw + cv.dsum);
     s.tasks = reinterpret_cast<int*>(smem_raw + cv.tasks);
-    s.xflag = reinterpret_cast<uint32_t*>(smem_raw + cv.xflag);
-    s.wpre = reinterpret_cast<int*>(smem_raw + cv.wpre);
+
     s.misc = reinterpret_cast<int*>(smem_raw + cv.misc);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -462,6 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         for (int i = 0; i < nst; ++i) {
             mbar_init(&s.full[i], 1);
             mbar_init(&s.empty[i], 1);
+            s.last_st[i] = -1;
         }
         fence_barrier_init();
         s.misc[0] = 0;
@@ -476,8 +639,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     // of every CTA routes token t.  More tokens: CTA t routes token t into
     // the workspace and every CTA reads the result back (one token per CTA
     // beats several tokens per warp).
-    const bool spread_route = a.logits && T > kNCW + 1;
-    const int nroute_warps = a.logits && !spread_route ? min(T, kNCW + 1) : 0;
+    const bool spread_route = a.logits && T > kWarps;
+    const int nroute_warps = a.logits && !spread_route ? min(T, kWarps) : 0;
     {
         uint32_t f = 0;
         if (spread_route) {
@@ -487,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 if (lane == 0) red_release_add(ctrl + kCtrlRouteDone, 1u);
             }
         } else if (a.logits) {
-            for (int t = warp; t < T; t += kNCW + 1)
+            for (int t = warp; t < T; t += kWarps)
                 route_topk_warp(a.logits + size_t(t) * kE, lane, s.ids + t * kTop, s.wts + t * kTop, f);
         } else {
             for (int r = tid; r < R; r += kThreads) {
@@ -530,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     // (into shared memory; a dead token's codes are never read, and its flags
     // are dropped below once the ids are known)
     if (T <= kRedundantX && warp >= nroute_warps) {
-        for (int q = warp - nroute_warps; q < T * 8; q += kNCW + 1 - nroute_warps) {
+        for (int q = warp - nroute_warps; q < T * 8; q += kWarps - nroute_warps) {
             const int t = q / 8, g = q % 8;
             const uint4 raw = *reinterpret_cast<const uint4*>(a.x + size_t(t) * kH + g * kG + lane * 8);
             uint32_t qf = wht_quant<QMAX>(
@@ -699,6 +862,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 run_g += __shfl_sync(0xffffffffu, ig, 31);
                 run_d += __shfl_sync(0xffffffffu, id, 31);
             }
+            __syncwarp();
+            if (lane < 4) {  // this CTA's item ranges, from the prefixes (read nowhere else)
+                const int* W = lane < 2 ? s.wpre : s.wpre + kE + 2;
+                const int per = lane < 2 ? 16 : 64;
+                s.misc[6 + lane] = range_start(W, NAp, per, b + (lane & 1), G);
+            }
         }
     }
     __syncthreads();
@@ -711,12 +880,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     const bool thr = T > kRedundantX;
     int ng, nd, gi0 = 0, dj0 = 0, jstart = 0;
     if (thr) {
-        const int* Wg = s.wpre;
-        const int* Wd = s.wpre + kE + 2;
-        gi0 = range_start(Wg, NA, 16, b, G);
-        ng = range_start(Wg, NA, 16, b + 1, G) - gi0;
-        dj0 = range_start(Wd, NA, 64, b, G);
-        nd = range_start(Wd, NA, 64, b + 1, G) - dj0;
+        gi0 = s.misc[6];
+        ng = s.misc[7] - gi0;
+        dj0 = s.misc[8];
+        nd = s.misc[9] - dj0;
     } else {
         ng = NGI > b ? (NGI - 1 - b) / G + 1 : 0;
         jstart = ((b - NGI) % G + G) % G;
@@ -724,16 +891,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     }
     const int total_stages = 16 * ng + 2 * nd;
 
-    if (warp == kNCW) {
+    if (warp == kProd) {
         // ---- producer ------------------------------------------------------
         // Lanes issue a group of stages in parallel: the 16 stages of one gate
-        // item, or the 8 stages of one batch of four down items.  Lane i
-        // first waits (bounded) until its slot's previous stage was released;
-        // the group is issued only if every lane's slot is free, and lane 0
-        // then publishes the issued count.  Stage st - nst was issued by an
-        // earlier group (groups are at most 16 < nst stages) whose lane had
-        // waited for st - 2 nst, so a slot's empty barrier is never more than
-        // one phase behind and its parity is exact.
+        // item, or the 8 stages of one batch of four down items.  Lane i waits
+        // (bounded) until its slot's previous stage was released and issues
+        // its stage at once, so the next item streams in while the current
+        // one is computed; lane 0 publishes the issued count once the whole
+        // group is out.  Stage st - nst was issued by an earlier group (groups
+        // are at most 16 < nst stages) whose lane had waited for st - 2 nst,
+        // so a slot's empty barrier is never more than one phase behind and
+        // its parity is exact.  Every issued stage is recorded per slot for
+        // the drain at exit.
         volatile int* misc = s.misc;
         int st0 = 0;
         if (lane == 0) DECODE_TRACE(16);
@@ -773,13 +942,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     }
                 }
             }
-            const bool all_ok = __all_sync(0xffffffffu, ok);
-            const bool stop = __any_sync(0xffffffffu, misc[0] != 0);
-            if (!all_ok || stop) {
-                if (lane == 0 && !misc[0]) give_up(a.flags, s.misc, ctrl, 2u, uint32_t(st0), uint32_t(st0 % nst), 0u);
-                break;
-            }
-            if (mine) {
+            if (lane == 0 && st0 == 80) DECODE_TRACE(13);
+            if (mine && ok && !misc[0]) {
                 int k, tile, g;
                 bool gate;
                 if (st < 16 * ng) {
@@ -816,6 +980,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 mbar_arrive_expect_tx(&s.full[slot], kStageBytes);
                 bulk_g2s(dst, codes, 4096, &s.full[slot]);
                 bulk_g2s(dst + 4096, meta, 128, &s.full[slot]);
+                s.last_st[slot] = st;
+            }
+            const bool all_ok = __all_sync(0xffffffffu, ok);
+            const bool stop = __any_sync(0xffffffffu, misc[0] != 0);
+            if (!all_ok || stop) {
+                if (lane == 0 && !misc[0]) give_up(a.flags, s.misc, ctrl, 2u, uint32_t(st0), uint32_t(st0 % nst), 0u);
+                break;
             }
             st0 = min(st0 + gsz, total_stages);
             __syncwarp();
@@ -825,6 +996,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 // observed itself, so no fence is needed here
                 misc[4] = st0;
                 if (st0 <= 16) DECODE_TRACE(17);
+                if (st0 == 96) DECODE_TRACE(15);
             }
         }
         if (lane == 0) {
@@ -833,11 +1005,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         }
     } else if (NA == 0) {
         // every slot padded and no shared expert: the output is zero
-        if (b == 0)
+        if (b == 0 && warp < kNCW)
             for (int i = tid; i < T * kH; i += kNCW * 32) {
                 a.out[i] = 0;
                 ws_at<float>(a, a.L.final_f32)[i] = 0.f;
             }
+    } else if (warp >= kNCW) {
+        // ---- epilogue warps (throughput mode) -------------------------------
+        if (thr) epilogue_warps<QMAX>(a, s, ctrl, T, R, G, b, warp, lane, NA, gi0, ng);
     } else {
         // ---- consumers -----------------------------------------------------
         uint32_t f = 0;
@@ -880,6 +1055,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         int tasks_done = 0;
         float* const tb = s.tbuf;
         float* const middle = ws_at<float>(a, a.L.middle);
+        if (!thr) {
         for (int item = 0; item < ng; ++item) {
             const int gi = thr ? gi0 + item : b + item * G, k = gi / 16, p = gi % 16, half = p / 8;
             // a (slot, half) whose 8 items all lie in this CTA's range is
@@ -892,6 +1068,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
             if (alive && !wait_stage(a.flags, s.misc, s.full, ctrl, stg + 1, nst)) alive = false;
             if (tid == 0 && item == 0) DECODE_TRACE(4);
             if (item == 0) DECODE_TRACE0(18);
+            if (item == 5) DECODE_TRACE0(25);
             const uint32_t* bg = reinterpret_cast<const uint32_t*>(s.ring + size_t(stg % nst) * kStageBytes);
             const uint32_t* bu = reinterpret_cast<const uint32_t*>(s.ring + size_t((stg + 1) % nst) * kStageBytes);
             const uint32_t mwg = alive ? bg[1024 + lane] : 0u, mwu = alive ? bu[1024 + lane] : 0u;
@@ -912,6 +1089,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     int dg[kChunk], du[kChunk];
                     stage_dots2_n(n, bg, bu, act, lane, dg, du);
                     if (item == 0 && c == 0) DECODE_TRACE0(19);
+                    if (item == 5 && c == 0) DECODE_TRACE0(26);
 #pragma unroll
                     for (int i = 0; i < kChunk; ++i) {
                         if (i < n) {
@@ -929,6 +1107,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 }
                 named_barrier(kBarConsumers, kNCW * 32);
                 if (item == 0 && c == 0) DECODE_TRACE0(20);
+                if (item == 5 && c == 0) DECODE_TRACE0(27);
                 // route c*8 + warp: ordered sum of the 8 group terms, SiLU * up
                 const volatile int* misc = s.misc;
                 if (warp < n && !misc[0]) {
@@ -956,6 +1135,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
             // this warp's share of the item is stored: count it; the warp that
             // completes the (slot, half) posts its quantisation to the CTA
             if (item == 0) DECODE_TRACE0(21);
+            if (item == 5) DECODE_TRACE0(28);
             __syncwarp();
             if (local_half) {
                 if (tid == 0 && p % 8 == 7) {
@@ -975,6 +1155,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
             }
             named_barrier(kBarConsumers, kNCW * 32);
             if (tid == 0 && item == 0) DECODE_TRACE(5);
+            if (item == 4) DECODE_TRACE0(29);
+            if (item == 5) DECODE_TRACE0(30);
             const int posted = min(*static_cast<volatile int*>(&s.misc[5]), kMaxTasks);
             // (the poster's acquiring counter update precedes the barrier above)
             for (; tasks_done < posted; ++tasks_done) {
@@ -985,6 +1167,62 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 if (lane == 0) red_release_add(ctrl + kCtrlReady + kk, 1u);
                 if (lane == 0 && warp == 0) DECODE_TRACE(6);
             }
+        }
+        } else {
+            // throughput mode: units of up to kTChunk routes; the group terms
+            // go to alternating buffers for the epilogue warps
+            int u = 0;
+            for (int item = 0; item < ng; ++item) {
+                const int gi = gi0 + item, k = gi / 16;
+                const int nr = s.act_cnt[k], roff = s.act_off[k];
+                const int stg = 16 * item + 2 * warp;  // gate stage; stg + 1 = up stage of the same group
+                if (alive && !wait_stage(a.flags, s.misc, s.full, ctrl, stg, nst)) alive = false;
+                if (alive && !wait_stage(a.flags, s.misc, s.full, ctrl, stg + 1, nst)) alive = false;
+                if (item == 5) DECODE_TRACE0(25);
+                const uint32_t* bg = reinterpret_cast<const uint32_t*>(s.ring + size_t(stg % nst) * kStageBytes);
+                const uint32_t* bu = reinterpret_cast<const uint32_t*>(s.ring + size_t((stg + 1) % nst) * kStageBytes);
+                const uint32_t mwg = alive ? bg[1024 + lane] : 0u, mwu = alive ? bu[1024 + lane] : 0u;
+                const int nch = (nr + kTChunk - 1) / kTChunk;
+                for (int c = 0; c < nch; ++c, ++u) {
+                    const int buf = u & 1;
+                    if (u >= 2) named_barrier(kBarTermsFree + buf, kDotEThreads);  // unit u-2 consumed
+                    const int n = min(kTChunk, nr - c * kTChunk);
+                    if (alive) {
+                        const uint4* act[kChunk];
+                        float sa[kChunk];
+                        int sm[kChunk];
+#pragma unroll
+                        for (int i = 0; i < kChunk; ++i) {
+                            const int tok = token_of(s.routes[roff + c * kTChunk + (i < n ? i : n - 1)], R);
+                            act[i] = reinterpret_cast<const uint4*>(s.xq + size_t(tok) * kH + warp * kG);
+                            sa[i] = __half2float(s.xs[tok * 8 + warp]);
+                            sm[i] = s.xsum[tok * 8 + warp];
+                        }
+                        int dg[kChunk], du[kChunk];
+                        stage_dots2_n(n, bg, bu, act, lane, dg, du);
+                        if (item == 5 && c == 0) DECODE_TRACE0(26);
+#pragma unroll
+                        for (int i = 0; i < kTChunk; ++i) {
+                            if (i < n) {
+                                tb[term_index(buf, warp, 0, i, lane)] = group_term(sa[i], dg[i], sm[i], mwg);
+                                tb[term_index(buf, warp, 1, i, lane)] = group_term(sa[i], du[i], sm[i], mwu);
+                            }
+                        }
+                        if (c == nch - 1) {
+                            __syncwarp();
+                            if (lane == 0) {
+                                mbar_arrive(&s.empty[stg % nst]);
+                                mbar_arrive(&s.empty[(stg + 1) % nst]);
+                            }
+                        }
+                    }
+                    named_barrier_arrive(kBarTermsReady + buf, kDotEThreads);
+                }
+            }
+            // the epilogue warps' last two buffer releases: tbuf is free after these
+            for (int v = u >= 2 ? u - 2 : 0; v < u; ++v) named_barrier(kBarTermsFree + (v & 1), kDotEThreads);
+            named_barrier(kBarDotE, kDotEThreads);  // every item counted, heavy halves posted
+            deferred_quant_tasks<QMAX>(a, s, ctrl, warp, lane, f);
         }
         if (tid == 0) DECODE_TRACE(7);
 
@@ -1139,7 +1377,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 const int nr = s.act_cnt[k], roff = s.act_off[k];
                 const bool shared = s.act_e[k] == kE;
                 const bool cached = nr <= 32;
-                if (warp == 0 && alive && !wait_counter(a.flags, s.misc, ctrl, ctrl + kCtrlReady + k, kReadyTarget))
+                if (warp == 0 && alive && !wait_counter(a.flags, s.misc, ctrl, ctrl + kCtrlReady + k, kReadyTargetThr))
                     alive = false;
                 named_barrier(kBarConsumers, kNCW * 32);  // every warp after warp 0's acquire
                 if (d0 == 0) DECODE_TRACE0(8);
@@ -1158,6 +1396,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     }
                 }
                 named_barrier(kBarConsumers, kNCW * 32);
+                bool run_ok = true;
                 for (int dd = d0 + pair; dd < d1; dd += 4) {
                     const int tile = (dj0 + dd) % 64;
                     const int st = 16 * ng + 2 * dd + g;
@@ -1229,46 +1468,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                         }
                         if (c + 1 < nchunks) named_barrier(2 + pair, 64);  // pbuf is rewritten next
                     }
-                    if (g == 0 && ok) {
-                        __syncwarp();
-                        if (lane == 0) red_release_add(ctrl + kCtrlColDone + tile, 1u);
-                    }
+                    run_ok = run_ok && ok;
+                }
+                // count this pair's tiles of the run: one fence for all of them
+                if (g == 0 && run_ok && d0 + pair < d1) {
+                    __syncwarp();
+                    __threadfence();
+                    for (int i = lane; d0 + pair + 4 * i < d1; i += 32)
+                        red_relaxed_add(ctrl + kCtrlColDone + (dj0 + d0 + pair + 4 * i) % 64, 1u);
                 }
                 named_barrier(kBarConsumers, kNCW * 32);  // the run's activations are replaced next
                 if (d0 == 0) DECODE_TRACE0(9);
                 d0 = d1;
             }
-            // ---- slot-ordered combine (reduce_slots :176-185): warp w of CTA b
-            // takes (tile, token) units b*8 + w, + G*8, ... once the tile's NA
-            // down items are counted
-            const uint16_t* logit = a.shared_gate_weight ? a.logit_out : a.shared_logit;
-            bool logit_ok = !(a.shared && a.shared_gate_weight);
-            for (int u = b * kNCW + warp; u < T * kTiles; u += G * kNCW) {
-                const int tile = u / T, t = u % T;
-                if (!alive) break;
-                if (!wait_counter(a.flags, s.misc, ctrl, ctrl + kCtrlColDone + tile, uint32_t(NA))) break;
-                if (!logit_ok) {
-                    if (!wait_counter(a.flags, s.misc, ctrl, ctrl + kCtrlLogitDone, uint32_t(T))) break;
-                    logit_ok = true;
-                }
-                const int col = tile * 32 + lane;
-                float sum = 0.f;
-#pragma unroll
-                for (int sl = 0; sl < kTop; ++sl) {
-                    const int r = t * kTop + sl;
-                    if (id_valid(s.ids[r])) sum = __fadd_rn(sum, __fmul_rn(__ldcg(route_out + size_t(r) * kH + col), s.wts[r]));
-                }
-                const uint16_t res = bf16_rne(sum);
-                ws_at<float>(a, a.L.final_f32)[size_t(t) * kH + col] = sum;
-                a.out[size_t(t) * kH + col] = res;
-                if (!isfinite(sum) || (res & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
-                if (a.shared) {
-                    const float gate = bf16_to_f32(a.sigmoid_table[__ldcg(logit + t)]);
-                    const float sh = __fmul_rn(__ldcg(route_out + size_t(R + t) * kH + col), gate);
-                    a.shared_out[size_t(t) * kH + col] = bf16_rne(sh);
-                    if (!isfinite(sh)) f |= kFlagNonfiniteOutput;
-                }
-            }
+            combine_units(a, s, ctrl, T, R, G, b, warp, lane, NA, f);
             DECODE_TRACE0(10);
         }
         warp_flag_or(a.flags, f);
@@ -1280,10 +1493,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         DECODE_TRACE(11);
         DECODE_CLOCK(24);
         if (s.misc[0]) {
-            const int issued = s.misc[1] < s.misc[4] ? s.misc[1] : s.misc[4];
             const uint64_t t0 = now_ns();
-            for (int slot = 0; slot < nst && slot < issued; ++slot) {
-                const int last = slot + ((issued - 1 - slot) / nst) * nst;  // last stage issued into this slot
+            for (int slot = 0; slot < nst; ++slot) {
+                const int last = s.last_st[slot];  // last stage issued into this slot
+                if (last < 0) continue;
                 const uint32_t parity = uint32_t(last / nst) & 1u;
                 while (!mbar_try_wait(&s.full[slot], parity) && now_ns() - t0 < kTimeoutNs) {
                 }
