@@ -63,6 +63,7 @@ constexpr int kTiles = kH / 32;               // 32-column output tiles of a dow
 // hot experts of larger batches) are quantised once by the CTA that completes
 // them and released through the ready count.
 constexpr int kSelfQuantMax = 4;
+constexpr int kSplit = 8;   // routes per slot in the throughput plan (heavier experts are split)
 __host__ __device__ inline bool light_slot(int T, int nr) { return T <= 4 && nr <= kSelfQuantMax; }
 
 __device__ __forceinline__ uint64_t now_ns() {
@@ -79,7 +80,9 @@ __device__ unsigned long long g_decode_trace[kTraceCtas][kTraceSlots];
 #define DECODE_TRACE(i) (g_decode_trace[blockIdx.x][i] = clock64())
 #define DECODE_TRACE0(i) (threadIdx.x == 0 ? void(g_decode_trace[blockIdx.x][i] = clock64()) : void(0))
 #define DECODE_CLOCK(i) (g_decode_trace[blockIdx.x][i] = now_ns())
+#define DECODE_VALUE(i, v) (g_decode_trace[blockIdx.x][i] = (unsigned long long)(v))
 #else
+#define DECODE_VALUE(i, v) ((void)0)
 #define DECODE_TRACE(i) ((void)0)
 #define DECODE_TRACE0(i) ((void)0)
 #define DECODE_CLOCK(i) ((void)0)
@@ -105,9 +108,9 @@ struct Smem {
     float* wts;       // [R]
     int* cnt;         // [E+1] counts, then placement cursors (plan only, inside tbuf)
     int* off;         // [E+1] (plan only, inside tbuf)
-    int* act_e;       // [E+1] expert of active slot k
-    int* act_off;     // [E+1]
-    int* act_cnt;     // [E+1]
+    int* act_e;       // [kMaxSlots] expert of active slot k (kE: shared expert)
+    int* act_off;     // [kMaxSlots] first position of the slot's routes
+    int* act_cnt;     // [kMaxSlots] routes of the slot
     int* routes;      // [R+T]
     float* tbuf;      // gate: [kNCW][2][kChunk][32] group terms; down: [kNCW][kChunk][256 B] activations
     float* pbuf;      // [kNCW/2][kChunk][32] second-group terms of the down pairs
@@ -115,13 +118,13 @@ struct Smem {
     int* dsum;        // [kNCW][kChunk]
     int* tasks;       // [kMaxTasks] posted middle-quantisation tasks (2*slot + half)
     uint32_t* xflag;  // [8 kRedundantX] flags of each token group quantised during routing (plan only, inside tbuf)
-    int* wpre;        // [2][E+2] cost prefixes of the slots' gate items and down items (plan only, inside tbuf)
+    int* wpre;        // [2][kMaxSlots+2] cost prefixes of the slots' gate items and down items (plan only, inside tbuf)
     int* misc;        // [0] abort, [1] final issued count, [2] nact, [3] NA, [4] issued so far, [5] tasks posted,
                       // [6..9] this CTA's gate and down item ranges (throughput mode)
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
-static_assert((3 * (kE + 4) + 2 * (kE + 2)) * 4 + 8 * kRedundantX * 4 <= kNCW * 2 * kChunk * 32 * 4,
+static_assert((2 * (kE + 4) + 2 * (kMaxSlots + 2)) * 4 + 8 * kRedundantX * 4 <= kNCW * 2 * kChunk * 32 * 4,
               "plan-only arrays must fit inside tbuf");
 
 // Byte offsets of the shared-memory carve for T tokens and nst ring stages.
@@ -147,9 +150,9 @@ __host__ __device__ inline Carve carve(int T, int nst) {
     add(c.xsum, size_t(T) * 8 * 4, 16);
     add(c.ids, R * 4 + 4, 16);
     add(c.wts, R * 4 + 4, 16);
-    add(c.act_e, (kE + 1) * 4, 16);
-    add(c.act_off, (kE + 1) * 4, 16);
-    add(c.act_cnt, (kE + 1) * 4, 16);
+    add(c.act_e, kMaxSlots * 4, 16);
+    add(c.act_off, kMaxSlots * 4, 16);
+    add(c.act_cnt, kMaxSlots * 4, 16);
     add(c.routes, (R + T) * 4 + 4, 16);
     add(c.tbuf, size_t(kNCW) * 2 * kChunk * 32 * 4, 16);
     add(c.pbuf, size_t(kNCW / 2) * kChunk * 32 * 4, 16);
@@ -413,7 +416,7 @@ __device__ __forceinline__ void quant_middle_group(const LayerArgs& a, int route
 // groups and long runs of one slot's down tiles.  Relative cost of an item of
 // a slot with nr routes: a gate item streams 66 KB and runs 2 x 16 x 8 dp4a
 // per route and lane, a down item streams 8 KB with a fixed per-tile overhead.
-__host__ __device__ inline int gate_cost(int nr) { return 3 + nr; }
+__host__ __device__ inline int gate_cost(int nr) { return 7 + nr; }
 __host__ __device__ inline int down_cost(int nr) { return 8 + nr; }
 // First item (slot-major index, per_slot items per slot) whose cost prefix is
 // at least `target`; W[k] = cost of all items of slots < k, W[NA] = total.
@@ -598,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     s.cnt = reinterpret_cast<int*>(smem_raw + cv.tbuf);
     s.off = s.cnt + (kE + 4);
     s.wpre = s.off + (kE + 4);
-    s.xflag = reinterpret_cast<uint32_t*>(s.wpre + 2 * (kE + 2));
+    s.xflag = reinterpret_cast<uint32_t*>(s.wpre + 2 * (kMaxSlots + 2));
     s.act_e = reinterpret_cast<int*>(smem_raw + cv.act_e);
     s.act_off = reinterpret_cast<int*>(smem_raw + cv.act_off);
     s.act_cnt = reinterpret_cast<int*>(smem_raw + cv.act_cnt);
@@ -783,12 +786,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         __syncthreads();
         if (tid == 0) DECODE_TRACE(14);
         if (warp == 0) {
+            // an expert with more than kSplit routes becomes several slots of
+            // at most kSplit routes (its weights stream once per slot), so that
+            // no item is much heavier than the others
             int c[8], tot = 0, nz = 0;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 c[i] = s.cnt[8 * lane + i];
                 tot += c[i];
-                nz += c[i] > 0;
+                nz += (c[i] + kSplit - 1) / kSplit;
             }
             int it = tot, in = nz;
 #pragma unroll
@@ -805,23 +811,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 const int e = 8 * lane + i;
                 s.off[e] = run;
                 s.cnt[e] = 0;  // from here on: placement cursor
-                if (c[i] > 0) {
+                for (int q = 0; q < c[i]; q += kSplit, ++k) {
                     s.act_e[k] = e;
-                    s.act_off[k] = run;
-                    s.act_cnt[k] = c[i];
-                    ++k;
+                    s.act_off[k] = run + q;
+                    s.act_cnt[k] = min(kSplit, c[i] - q);
                 }
                 run += c[i];
             }
             const int nact = __shfl_sync(0xffffffffu, in, 31), total = __shfl_sync(0xffffffffu, it, 31);
             if (lane == 31) {
-                if (a.shared) {
-                    s.act_e[nact] = kE;
-                    s.act_off[nact] = total;
-                    s.act_cnt[nact] = T;
-                }
+                int na = nact;
+                if (a.shared)
+                    for (int q = 0; q < T; q += kSplit, ++na) {
+                        s.act_e[na] = kE;
+                        s.act_off[na] = total + q;
+                        s.act_cnt[na] = min(kSplit, T - q);
+                    }
                 s.misc[2] = nact;
-                s.misc[3] = nact + (a.shared ? 1 : 0);
+                s.misc[3] = na;
             }
             __syncwarp();
             // routes of each expert in ascending route order (warp-wide match per 32 routes)
@@ -857,14 +864,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 }
                 if (k <= NAp) {
                     s.wpre[k] = run_g + ig - 16 * wg;
-                    s.wpre[kE + 2 + k] = run_d + id - 64 * wd;
+                    s.wpre[kMaxSlots + 2 + k] = run_d + id - 64 * wd;
                 }
                 run_g += __shfl_sync(0xffffffffu, ig, 31);
                 run_d += __shfl_sync(0xffffffffu, id, 31);
             }
             __syncwarp();
             if (lane < 4) {  // this CTA's item ranges, from the prefixes (read nowhere else)
-                const int* W = lane < 2 ? s.wpre : s.wpre + kE + 2;
+                const int* W = lane < 2 ? s.wpre : s.wpre + kMaxSlots + 2;
                 const int per = lane < 2 ? 16 : 64;
                 s.misc[6 + lane] = range_start(W, NAp, per, b + (lane & 1), G);
             }
@@ -890,6 +897,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         nd = NDI > jstart ? (NDI - 1 - jstart) / G + 1 : 0;
     }
     const int total_stages = 16 * ng + 2 * nd;
+    if (tid == 0) {
+        DECODE_VALUE(14, ng);
+        DECODE_VALUE(13, nd);
+        DECODE_VALUE(12, thr ? (s.act_cnt[gi0 / 16] | (s.act_cnt[min(dj0 / 64, NA - 1)] << 16)) : 0);
+    }
 
     if (warp == kProd) {
         // ---- producer ------------------------------------------------------
@@ -905,7 +917,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         // the drain at exit.
         volatile int* misc = s.misc;
         int st0 = 0;
-        if (lane == 0) DECODE_TRACE(16);
         while (st0 < total_stages) {
             if (st0 == 16 * ng && ng > 0) {
                 // the down stages wait until this CTA's last gate stage has landed,
@@ -942,7 +953,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     }
                 }
             }
-            if (lane == 0 && st0 == 80) DECODE_TRACE(13);
             if (mine && ok && !misc[0]) {
                 int k, tile, g;
                 bool gate;
@@ -996,7 +1006,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 // observed itself, so no fence is needed here
                 misc[4] = st0;
                 if (st0 <= 16) DECODE_TRACE(17);
-                if (st0 == 96) DECODE_TRACE(15);
             }
         }
         if (lane == 0) {
@@ -1364,11 +1373,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         } else {
             // ---- down items, throughput mode: per run of one slot's tiles,
             // the slot's middle activations (up to 32 routes) are loaded into
-            // shared memory once; warp pair q takes tiles q, q+4, ... of the
-            // run, one K-group per warp
-            const int pair = warp >> 1, g = warp & 1;
+            // shared memory once; warp w takes tiles w, w+8, ... of the run,
+            // both K-groups, and sums their terms in order itself
             uint8_t* const sact = reinterpret_cast<uint8_t*>(s.tbuf);  // [32 routes][512 B]
-            float* pb = s.pbuf + pair * kChunk * 32;
             float* const route_out = ws_at<float>(a, a.L.route_out);
             uint8_t* dact = reinterpret_cast<uint8_t*>(s.tbuf) + size_t(warp) * kChunk * kG;  // uncached runs
             for (int d0 = 0; d0 < nd;) {
@@ -1397,19 +1404,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 }
                 named_barrier(kBarConsumers, kNCW * 32);
                 bool run_ok = true;
-                for (int dd = d0 + pair; dd < d1; dd += 4) {
+                for (int dd = d0 + warp; dd < d1; dd += kNCW) {
                     const int tile = (dj0 + dd) % 64;
-                    const int st = 16 * ng + 2 * dd + g;
+                    const int st0 = 16 * ng + 2 * dd;  // K-group 0; st0 + 1 = K-group 1
                     bool ok = ok_run && alive;
-                    if (ok && !wait_stage(a.flags, s.misc, s.full, ctrl, st, nst)) ok = false;
+                    if (ok && !wait_stage(a.flags, s.misc, s.full, ctrl, st0, nst)) ok = false;
+                    if (ok && !wait_stage(a.flags, s.misc, s.full, ctrl, st0 + 1, nst)) ok = false;
                     if (!ok) alive = false;
-                    const uint32_t* blk = reinterpret_cast<const uint32_t*>(s.ring + size_t(st % nst) * kStageBytes);
-                    const uint32_t mw = ok ? blk[1024 + lane] : 0u;
-                    const int nchunks = (nr + kChunk - 1) / kChunk;
-                    float term[kChunk];
-                    for (int c = 0; c < nchunks; ++c) {
+                    const uint32_t* blk[2] = {reinterpret_cast<const uint32_t*>(s.ring + size_t(st0 % nst) * kStageBytes),
+                                              reinterpret_cast<const uint32_t*>(s.ring + size_t((st0 + 1) % nst) * kStageBytes)};
+                    const uint32_t mw0 = ok ? blk[0][1024 + lane] : 0u, mw1 = ok ? blk[1][1024 + lane] : 0u;
+                    for (int c = 0; ok && c * kChunk < nr; ++c) {
                         const int n = min(kChunk, nr - c * kChunk);
-                        if (ok) {
+                        float term0[kChunk];
+#pragma unroll 1
+                        for (int g = 0; g < 2; ++g) {
                             const uint4* act[kChunk];
                             float sa[kChunk];
                             int sm[kChunk];
@@ -1422,7 +1431,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                                     sm[i] = s.dsum[ri * 2 + g];
                                 }
                             } else {
-                                __syncwarp();  // the previous chunk's reads of dact are done
+                                __syncwarp();  // earlier reads of dact are done
                                 for (int i = lane; i < n * 16; i += 32) {
                                     const int ri = i / 16, part = i % 16;
                                     const int route = s.routes[roff + c * kChunk + ri];
@@ -1441,46 +1450,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                                 }
                             }
                             int dot[kChunk];
-                            stage_dots1_n(n, blk, act, lane, dot);
+                            stage_dots1_n(n, blk[g], act, lane, dot);
+                            if (g == 0) {
 #pragma unroll
-                            for (int i = 0; i < kChunk; ++i) term[i] = group_term(sa[i], dot[i], sm[i], mw);
-                            if (g == 1) {
+                                for (int i = 0; i < kChunk; ++i) term0[i] = group_term(sa[i], dot[i], sm[i], mw0);
+                            } else if (!misc[0]) {
 #pragma unroll
-                                for (int i = 0; i < kChunk; ++i)
-                                    if (i < n) pb[i * 32 + lane] = term[i];
-                            }
-                            if (c == nchunks - 1) {
-                                __syncwarp();
-                                if (lane == 0) mbar_arrive(&s.empty[st % nst]);
-                            }
-                        }
-                        named_barrier(2 + pair, 64);
-                        if (g == 0 && ok && !misc[0]) {
-#pragma unroll
-                            for (int i = 0; i < kChunk; ++i) {
-                                if (i < n) {
-                                    float v = __fadd_rn(__fadd_rn(0.f, term[i]), pb[i * 32 + lane]);
-                                    if (shared) v = bf16_round_f32(v);
-                                    if (!isfinite(v)) f |= kFlagNonfiniteProjection;
-                                    route_out[size_t(s.routes[roff + c * kChunk + i]) * kH + tile * 32 + lane] = v;
+                                for (int i = 0; i < kChunk; ++i) {
+                                    if (i < n) {
+                                        float v = __fadd_rn(__fadd_rn(0.f, term0[i]), group_term(sa[i], dot[i], sm[i], mw1));
+                                        if (shared) v = bf16_round_f32(v);
+                                        if (!isfinite(v)) f |= kFlagNonfiniteProjection;
+                                        route_out[size_t(s.routes[roff + c * kChunk + i]) * kH + tile * 32 + lane] = v;
+                                    }
                                 }
                             }
                         }
-                        if (c + 1 < nchunks) named_barrier(2 + pair, 64);  // pbuf is rewritten next
+                    }
+                    if (ok) {
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(&s.empty[st0 % nst]);
+                            mbar_arrive(&s.empty[(st0 + 1) % nst]);
+                        }
                     }
                     run_ok = run_ok && ok;
                 }
-                // count this pair's tiles of the run: one fence for all of them
-                if (g == 0 && run_ok && d0 + pair < d1) {
+                // count this warp's tiles of the run: one fence for all of them
+                if (run_ok && d0 + warp < d1) {
                     __syncwarp();
                     __threadfence();
-                    for (int i = lane; d0 + pair + 4 * i < d1; i += 32)
-                        red_relaxed_add(ctrl + kCtrlColDone + (dj0 + d0 + pair + 4 * i) % 64, 1u);
+                    for (int i = lane; d0 + warp + kNCW * i < d1; i += 32)
+                        red_relaxed_add(ctrl + kCtrlColDone + (dj0 + d0 + warp + kNCW * i) % 64, 1u);
                 }
                 named_barrier(kBarConsumers, kNCW * 32);  // the run's activations are replaced next
                 if (d0 == 0) DECODE_TRACE0(9);
                 d0 = d1;
             }
+            DECODE_TRACE0(16);
             combine_units(a, s, ctrl, T, R, G, b, warp, lane, NA, f);
             DECODE_TRACE0(10);
         }

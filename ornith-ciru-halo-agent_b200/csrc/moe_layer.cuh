@@ -29,15 +29,16 @@ constexpr int kCtrlWords = 2048;
 constexpr int kCtrlXDone = 0;          // token groups quantised
 constexpr int kCtrlLogitDone = 1;      // shared-expert logits written (fused routing)
 constexpr int kCtrlRouteDone = 2;      // tokens routed (fused routing spread over CTAs)
-constexpr int kCtrlGateDone = 32;      // [E+1][2] gate-item parts finished per (expert slot, middle half)
-constexpr int kCtrlReady = 576;        // [E+1] middle-quantisation parts finished per expert slot
-constexpr int kCtrlColDone = 864;      // [64] down items finished per output tile
-constexpr int kCtrlAbort = 960;        // any CTA gave up a bounded wait
+constexpr int kMaxSlots = 320;         // expert slots of the fused decode plan (split slots included)
+constexpr int kCtrlGateDone = 32;      // [kMaxSlots][2] gate-item counts per (slot, middle half)
+constexpr int kCtrlReady = 672;        // [kMaxSlots] middle-quantisation counts per slot
+constexpr int kCtrlColDone = 992;      // [64] down items finished per output tile
+constexpr int kCtrlAbort = 1056;       // any CTA gave up a bounded wait
 // first bounded wait that gave up: [tag, cta, warp, x, y, observed], tag 1 = ring
 // stage (x = stage, y = slot), 2 = producer slot reuse (x = stage, y = slot),
 // 3 = global counter (x = ctrl word, y = target, observed = last value)
-constexpr int kCtrlGiveUp = 964;
-constexpr int kCtrlClearWords = 976;   // words zeroed before every fused launch
+constexpr int kCtrlGiveUp = 1060;
+constexpr int kCtrlClearWords = 1072;  // words zeroed before every fused launch
 
 Workspace workspace_layout(int Tcap);
 
