@@ -42,6 +42,17 @@ import __graft_entry__ as graft  # noqa: E402
 
 METRIC = 'MoE-layer tokens/s & % of HBM/tensor roofline (decode B=1/32, 8K prefill)'
 EXPERT_BYTES = 1_622_016          # w13 codes 1,048,576 + meta 32,768 + w2 codes 524,288 + meta 16,384
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture of the same workload (profiles/decode_layer_kernel_decode1.md,
+# profiles/decode_layer_kernel_decode32.md, profiles/prefill_mma_kernel_prefill8192.md).
+NCU_TRAFFIC = {
+    'decode1': {'kernel': 'decode_layer_kernel<127>', 'bytes': 14_737_152},
+    'decode32': {'kernel': 'decode_layer_kernel<127>', 'bytes': 214_940_160 + 5_720_320},
+    'prefill8192': {'kernel': 'mma_kernel<8,1> (gate/up)', 'bytes': 454_199_552 + 119_388_928},
+}
+# int8 multiply-accumulates per valid route of one layer: gate/up 1024x2048 + down 2048x512
+MACS_PER_ROUTE = 3_145_728
+
 CONFIGS = {
     'decode1': dict(T=1, layers=40, bias=0.0, act_bits=8, shared=True, name='decode B=1, 40-layer stack (configs[1])'),
     'decode32': dict(T=32, layers=40, bias=0.5, act_bits=8, shared=True, name='decode B=32, 40-layer stack (configs[2])'),
@@ -393,6 +404,30 @@ def run(args):
     peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
     peak = peaks.get('hbm_gbs', 6650.0)
     achieved = layer_bytes / (layer_ms * 1e-3) / 1e9
+    traffic = NCU_TRAFFIC.get(args.config)
+    hbm_roofline = {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
+                    'frac': round(achieved / peak, 4), 'traffic': traffic['bytes'] if traffic else None,
+                    'kernel': 'one routed_from_logits layer call (all its kernels)',
+                    'algorithmic_bytes_per_launch': int(layer_bytes), 'launch_ms': round(layer_ms, 5),
+                    'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'}
+    if T > 64:
+        # prefill: the grouped int8 GEMMs bound the layer; int8 dense tensor rate is
+        # twice bf16 on B200, and only the bf16 rate is measured on this pool
+        ops = 2.0 * T * 8 * MACS_PER_ROUTE
+        bf16 = peaks.get('bf16_tflops', 1590.0)
+        tops = ops / (layer_ms * 1e-3) / 1e12
+        roofline = {'bound': 'tensor', 'achieved': round(tops, 1), 'peak': round(2 * bf16, 1), 'unit': 'TOP/s',
+                    'frac': round(tops / (2 * bf16), 4), 'traffic': traffic['bytes'] if traffic else None,
+                    'kernel': 'one routed_from_logits layer call (all its kernels)',
+                    'algorithmic_ops_per_launch': ops, 'launch_ms': round(layer_ms, 5),
+                    'peak_source': ('2 x MEASURED_PEAKS.json bf16_tflops (of measured; int8 = 2 x bf16 dense)'
+                                    if peaks else '2 x fallback 1590 TFLOP/s'),
+                    'frac_of_bf16_peak': round(tops / bf16, 4),
+                    'hbm': hbm_roofline}
+    else:
+        roofline = hbm_roofline
+    if traffic:
+        roofline['traffic_kernel'] = traffic['kernel']
 
     # end to end through the public operator: pinned host inputs copied in, the
     # step (graph of the operator's launches) run, the last output copied out
@@ -436,11 +471,7 @@ def run(args):
         'e2e': {'value': round(e2e_value, 3), 'unit': 'tokens/s', 'h2d_bytes_per_step': T * 4096 + L * T * 1024,
                 'd2h_bytes_per_step': T * 4096},
         'gpu_launches': int(launches),
-        'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
-                     'frac': round(achieved / peak, 4), 'traffic': None,
-                     'kernel': 'one routed_from_logits layer call (all its kernels)',
-                     'algorithmic_bytes_per_launch': int(layer_bytes), 'launch_ms': round(layer_ms, 5),
-                     'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback'},
+        'roofline': roofline,
         'step_roofline_frac': round(bytes_timed / (ms_step * 1e-3) / 1e9 / peak, 4),
         'flags_max': flag_any,
         'cuda_graph': graph is not None,
