@@ -42,6 +42,7 @@ Workspace workspace_layout(int Tcap) {
         add(w.slot_tiles, (kE + 2) * 4);
         add(w.mtiles, mt * 16);
         add(w.n_mtiles, 16);
+        add(w.pblock, size_t(2) * kPlanBlocks * (kE + 1) * 4);
         add(w.agate, mt * 8 * 32768);
         add(w.agate_sa, mt * 8 * 128 * 4);
         add(w.agate_sum, mt * 8 * 128 * 4);

@@ -19,6 +19,7 @@ struct Workspace {
     size_t topk_w, topk_ids, logit;  // router outputs of the from-logits entry point
     // tensor-core prefill path (only when Tcap > kDecodeMaxT)
     size_t rowpos, slot_tiles, mtiles, n_mtiles;
+    size_t pblock;                // per-block expert counts, then bases [kPlanBlocks][E+1] (x2)
     size_t agate, agate_sa, agate_sum;  // gate activation tiles [MT][8][32 KB] + per-row scale/sum
     size_t adown, adown_sa, adown_sum;  // down activation tiles [MT][2][32 KB]
     size_t bytes;
@@ -172,6 +173,7 @@ cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream);
 cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream);
 // Fused persistent path for decode batches (T <= kDecodeMaxT).
 constexpr int kDecodeMaxT = 32;
+constexpr int kPlanBlocks = 256;  // most blocks of the prefill routing plan
 bool decode_supported(int T);
 cudaError_t launch_decode(const LayerArgs& a, cudaStream_t stream);
 

@@ -5,9 +5,9 @@
 // exact integer dots, then the fixed fp32 epilogue in ascending group order.
 // B200 schedule:
 //
-//   prefill_plan_kernel   routing plan (slot counts/offsets/route lists, the
-//                         inverse map route -> position) and the list of
-//                         128-route M-tiles per expert slot;
+//   prefill_count/scan/place_kernel  routing plan (slot counts/offsets/route
+//                         lists, the inverse map route -> position) and the
+//                         list of 128-route M-tiles per expert slot;
 //   pack_tokens_kernel    Hadamard + quantise each token group once and write
 //                         it into the M-tile of each of its routes, in the
 //                         no-swizzle K-major core-matrix layout tcgen05 reads;
@@ -466,59 +466,120 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
     if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-// Routing plan for the tensor-core path, one CTA.  Positions are grouped by
-// expert slot (slot 256 = shared expert rows R..R+T-1); rowpos is the inverse
-// map; every slot's positions are cut into 128-route M-tiles.
-__global__ __launch_bounds__(1024) void prefill_plan_kernel(LayerArgs a) {
-    __shared__ int counts[kE + 1], offsets[kE + 2], tile_base[kE + 2];
-    const int R = a.T * kTop;
-    for (int e = threadIdx.x; e <= kE; e += blockDim.x) counts[e] = 0;
+// Routing plan for the tensor-core path, in three launches over blocks of
+// routes: per-block expert counts; one CTA turning them into slot offsets,
+// per-block bases and the list of 128-route M-tiles per slot (slot 256 = the
+// shared expert, rows R..R+T-1); placement of every route at
+// offset + block base + rank within the block.  Routes of one slot may appear
+// in any order (every route's row is computed independently); rowpos is the
+// inverse map.
+__device__ __forceinline__ int plan_chunk(int R, int nblk) { return (R + nblk - 1) / nblk; }
+
+__global__ __launch_bounds__(256) void prefill_count_kernel(LayerArgs a, int nblk) {
+    __shared__ int hist[kE + 1];
+    for (int e = threadIdx.x; e <= kE; e += blockDim.x) hist[e] = 0;
     __syncthreads();
+    const int R = a.T * kTop, chunk = plan_chunk(R, nblk);
+    const int r0 = blockIdx.x * chunk, r1 = min(R, r0 + chunk);
     uint32_t f = 0;
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
         const int e = a.ids[r];
-        if (id_valid(e)) atomicAdd(&counts[e], 1);
+        if (id_valid(e)) atomicAdd(&hist[e], 1);
         else if (e != -1) f |= kFlagInvalidId;
     }
     f = __reduce_or_sync(0xffffffffu, f);
     if (f && (threadIdx.x & 31) == 0) atomicOr(a.flags, f);
     __syncthreads();
-    int4* mtiles = ws_at<int4>(a, a.L.mtiles);
-    if (threadIdx.x == 0) {
-        counts[kE] = a.shared ? a.T : 0;
-        int total = 0, tiles = 0;
-        for (int e = 0; e <= kE; ++e) {
-            offsets[e] = total;
-            tile_base[e] = tiles;
-            for (int m = 0; m < counts[e]; m += kMT) mtiles[tiles++] = make_int4(e, total + m, min(kMT, counts[e] - m), 0);
-            total += counts[e];
+    int* bc = ws_at<int32_t>(a, a.L.pblock) + size_t(blockIdx.x) * (kE + 1);
+    for (int e = threadIdx.x; e <= kE; e += blockDim.x) bc[e] = hist[e];
+}
+
+__global__ __launch_bounds__(1024) void prefill_scan_kernel(LayerArgs a, int nblk) {
+    __shared__ int warp_tot[32][2];
+    const int e = threadIdx.x, lane = e & 31, w = e >> 5;
+    const int* bc = ws_at<int32_t>(a, a.L.pblock);
+    int* bb = ws_at<int32_t>(a, a.L.pblock) + size_t(kPlanBlocks) * (kE + 1);
+    int c = 0;
+    if (e < kE) {
+        for (int blk = 0; blk < nblk; ++blk) {
+            bb[size_t(blk) * (kE + 1) + e] = c;  // this block's base inside expert e's run
+            c += bc[size_t(blk) * (kE + 1) + e];
         }
-        offsets[kE + 1] = total;
-        tile_base[kE + 1] = tiles;
-        *ws_at<int32_t>(a, a.L.n_mtiles) = tiles;
+    } else if (e == kE) {
+        c = a.shared ? a.T : 0;
+    }
+    const int t = e <= kE ? (c + kMT - 1) / kMT : 0;
+    // exclusive scans of counts and tile counts over the 257 slots
+    int ic = c, it = t;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int uc = __shfl_up_sync(0xffffffffu, ic, d), ut = __shfl_up_sync(0xffffffffu, it, d);
+        if (lane >= d) {
+            ic += uc;
+            it += ut;
+        }
+    }
+    if (lane == 31) {
+        warp_tot[w][0] = ic;
+        warp_tot[w][1] = it;
     }
     __syncthreads();
+    if (w == 0) {
+        int vc = warp_tot[lane][0], vt = warp_tot[lane][1];
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int uc = __shfl_up_sync(0xffffffffu, vc, d), ut = __shfl_up_sync(0xffffffffu, vt, d);
+            if (lane >= d) {
+                vc += uc;
+                vt += ut;
+            }
+        }
+        warp_tot[lane][0] = vc;  // inclusive over warps
+        warp_tot[lane][1] = vt;
+    }
+    __syncthreads();
+    const int before_c = (w ? warp_tot[w - 1][0] : 0) + ic - c;
+    const int before_t = (w ? warp_tot[w - 1][1] : 0) + it - t;
     int32_t* g_offsets = ws_at<int32_t>(a, a.L.offsets);
     int32_t* g_tiles = ws_at<int32_t>(a, a.L.slot_tiles);
-    for (int e = threadIdx.x; e <= kE + 1; e += blockDim.x) {
-        g_offsets[e] = offsets[e];
-        g_tiles[e] = tile_base[e];
+    int4* mtiles = ws_at<int4>(a, a.L.mtiles);
+    if (e <= kE) {
+        g_offsets[e] = before_c;
+        g_tiles[e] = before_t;
+        for (int m = 0; m * kMT < c; ++m) mtiles[before_t + m] = make_int4(e, before_c + m * kMT, min(kMT, c - m * kMT), 0);
+        if (e == kE) {
+            g_offsets[kE + 1] = before_c + c;
+            g_tiles[kE + 1] = before_t + t;
+            *ws_at<int32_t>(a, a.L.n_mtiles) = before_t + t;
+        }
     }
+}
+
+__global__ __launch_bounds__(256) void prefill_place_kernel(LayerArgs a, int nblk) {
+    __shared__ int base[kE + 1];
+    const int R = a.T * kTop, chunk = plan_chunk(R, nblk);
+    const int r0 = blockIdx.x * chunk, r1 = min(R, r0 + chunk);
+    const int32_t* g_offsets = ws_at<int32_t>(a, a.L.offsets);
+    const int* bb = ws_at<int32_t>(a, a.L.pblock) + size_t(kPlanBlocks) * (kE + 1) + size_t(blockIdx.x) * (kE + 1);
+    for (int e = threadIdx.x; e < kE; e += blockDim.x) base[e] = g_offsets[e] + bb[e];
+    __syncthreads();
     int32_t* routes = ws_at<int32_t>(a, a.L.routes);
     int32_t* rowpos = ws_at<int32_t>(a, a.L.rowpos);
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
         const int e = a.ids[r];
         if (id_valid(e)) {
-            const int pos = offsets[e] + atomicAdd(&counts[e], -1) - 1;
+            const int pos = atomicAdd(&base[e], 1);
             routes[pos] = r;
             rowpos[r] = pos;
         }
     }
-    if (a.shared)
+    if (a.shared && blockIdx.x == 0) {
+        const int sh = g_offsets[kE];
         for (int t = threadIdx.x; t < a.T; t += blockDim.x) {
-            routes[offsets[kE] + t] = R + t;
-            rowpos[R + t] = offsets[kE] + t;
+            routes[sh + t] = R + t;
+            rowpos[R + t] = sh + t;
         }
+    }
 }
 
 // Tile and row of a route position inside an activation tile set.
@@ -666,8 +727,11 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
         ds.attr = true;
     }
     const int T = a.T, R = T * kTop, rows = R + (a.shared ? T : 0);
-    count_launches(5);
-    prefill_plan_kernel<<<1, 1024, 0, stream>>>(a);
+    const int nblk = min(kPlanBlocks, max(1, (R + 255) / 256));
+    count_launches(7);
+    prefill_count_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
+    prefill_scan_kernel<<<1, 1024, 0, stream>>>(a, nblk);
+    prefill_place_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
     if ((st = cudaGetLastError()) != cudaSuccess) return st;
     if (a.a8) pack_tokens_kernel<127><<<(T * 8 + 7) / 8, 256, 0, stream>>>(a);
     else pack_tokens_kernel<7><<<(T * 8 + 7) / 8, 256, 0, stream>>>(a);
