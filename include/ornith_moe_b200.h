@@ -160,6 +160,16 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine(
     const void* route_out_f32, const void* weights_f32, const void* ids_i32, int T,
     void* output_bf16, void* flags_u32, cudaStream_t stream);
 
+/* The same combine from gathered rows: rows fp32 [n][2048] holds only the
+ * per-slot rows that exist, and row_index int32 [T,8] gives the row of slot s
+ * of token t (ignored where the id is -1 padding; a valid id whose index is
+ * outside [0, n) raises flag 4 and contributes nothing).  Saves the expert-
+ * parallel home rank from scattering the returned rows into a dense
+ * [T*8][2048] buffer.  No counterpart in the reference. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine_gathered(
+    const void* rows_f32, int n_rows, const void* row_index_i32, const void* weights_f32, const void* ids_i32,
+    int T, void* output_bf16, void* flags_u32, cudaStream_t stream);
+
 /* Workspace size for ornith_moe_b200_launch_from_logits (0 <= Tcap <= 8192). */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes);
 

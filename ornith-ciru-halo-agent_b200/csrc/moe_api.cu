@@ -47,6 +47,35 @@ __global__ __launch_bounds__(256) void shared_logit_kernel(const uint16_t* x, co
     if (lane == 0) logit[warp] = v;
 }
 
+// combine_rows_kernel with the per-slot rows gathered: row_index[8t+s] is the
+// row of slot s of token t in `rows` (n rows).
+__global__ __launch_bounds__(256) void combine_gathered_kernel(const float* rows, int n, const int32_t* row_index,
+                                                               const float* weights, const int32_t* ids, int T,
+                                                               uint16_t* out, uint32_t* flags) {
+    const size_t index = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint32_t f = 0;
+    if (index < size_t(T) * kH) {
+        const int t = int(index / kH), c = int(index % kH);
+        float sum = 0.f;
+#pragma unroll
+        for (int s = 0; s < kTop; ++s) {
+            const int r = t * kTop + s;
+            if (!id_valid(ids[r])) continue;
+            const int row = row_index[r];
+            if (row < 0 || row >= n) {
+                f |= kFlagInvalidId;
+                continue;
+            }
+            sum = __fadd_rn(sum, __fmul_rn(rows[size_t(row) * kH + c], weights[r]));
+        }
+        const uint16_t res = bf16_rne(sum);
+        out[index] = res;
+        if (!isfinite(sum) || (res & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
+    }
+    f = __reduce_or_sync(0xffffffffu, f);
+    if (f && (threadIdx.x & 31) == 0) atomicOr(flags, f);
+}
+
 // N16 -> N32 bank repack (method.py:142-147).  One thread per destination word.
 __global__ void repack_codes_kernel(const uint32_t* src, uint32_t* dst, int E, int N, int groups) {
     const size_t total = size_t(E) * (N / 32) * groups * 32 * 32;
@@ -287,6 +316,23 @@ cudaError_t ornith_moe_b200_combine(const void* route_out_f32, const void* weigh
     combine_rows_kernel<<<(T * kH + 255) / 256, 256, 0, stream>>>(
         static_cast<const float*>(route_out_f32), static_cast<const float*>(weights), static_cast<const int32_t*>(ids),
         T, static_cast<uint16_t*>(output), static_cast<uint32_t*>(flags));
+    return cudaGetLastError();
+}
+
+cudaError_t ornith_moe_b200_combine_gathered(const void* rows_f32, int n_rows, const void* row_index_i32,
+                                             const void* weights, const void* ids, int T, void* output, void* flags,
+                                             cudaStream_t stream) {
+    if (T < 0 || T > kTcapMax || n_rows < 0) return cudaErrorInvalidValue;
+    if (!T) return cudaSuccess;
+    if ((!rows_f32 && n_rows) || !row_index_i32 || !weights || !ids || !output || !flags ||
+        !aligned(rows_f32, 4) || !aligned(row_index_i32, 4) || !aligned(weights, 4) || !aligned(ids, 4) ||
+        !aligned(output, 2) || !aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    count_launches(1);
+    combine_gathered_kernel<<<(T * kH + 255) / 256, 256, 0, stream>>>(
+        static_cast<const float*>(rows_f32), n_rows, static_cast<const int32_t*>(row_index_i32),
+        static_cast<const float*>(weights), static_cast<const int32_t*>(ids), T, static_cast<uint16_t*>(output),
+        static_cast<uint32_t*>(flags));
     return cudaGetLastError();
 }
 

@@ -15,7 +15,9 @@ for its own tokens.  One layer call on every rank, for the rank's own tokens:
      per-route down projections of the valid slots are kept;
   5. return exchange of those rows, one per (token, slot) owned by d;
   6. home combine: slot-ordered weighted sum into bf16 with the same
-     arithmetic as the single-GPU layer, so the result is bit-identical to it.
+     arithmetic as the single-GPU layer, so the result is bit-identical to it;
+     it reads the returned rows where they arrived, through a (token, slot)
+     -> row index, instead of scattering them into a dense [8T, 2048] buffer.
 
 These collectives are the layer's only exchange.  Every rank takes the same
 collective steps in the same order, zero-sized messages included.
@@ -88,28 +90,26 @@ def return_rows(group, world, plan, ids_recv, recv_counts, route_rows):
     return got
 
 
-def assemble_route_rows(T, plan, got):
-    """Place the returned rows at route index 8*token + slot (zeros elsewhere)."""
-    rows = torch.zeros((T * TOP, H), dtype=torch.float32, device=got.device)
-    tok = plan.token_index.unsqueeze(1).expand(-1, TOP)
-    slot = torch.arange(TOP, device=got.device).unsqueeze(0).expand_as(tok)
-    dest = (tok * TOP + slot)[plan.slot_mask]
-    rows[dest] = got
-    return rows
+def route_row_index(T, plan, device):
+    """int32 [T, 8]: the row of `got` (return_rows) holding slot s of token t,
+    -1 for slots no rank returned (padding ids)."""
+    idx = torch.full((T, TOP), -1, dtype=torch.int32, device=device)
+    k, s = plan.slot_mask.nonzero(as_tuple=True)  # the order of return_rows
+    idx[plan.token_index[k], s] = torch.arange(k.numel(), dtype=torch.int32, device=device)
+    return idx
 
 
 def ep_layer(group, world, x, ids, weights, compute, combine):
     """One expert-parallel layer call.
 
     compute(x_recv, ids_recv) -> fp32 [n_recv, 8, 2048] per-slot rows for this
-    rank's experts; combine(rows [T*8, 2048], weights, ids) -> output.  Both
-    are injected so that the host logic also runs on CPU ranks."""
+    rank's experts; combine(rows [n, 2048], row_index [T, 8], weights, ids) ->
+    output.  Both are injected so that the host logic also runs on CPU ranks."""
     plan = build_dispatch(ids, world)
     x_recv, ids_recv, recv_counts = exchange_rows(group, world, plan, x)
     route_rows = compute(x_recv, ids_recv)
     got = return_rows(group, world, plan, ids_recv, recv_counts, route_rows)
-    rows = assemble_route_rows(x.shape[0], plan, got)
-    return combine(rows, weights, ids)
+    return combine(got, route_row_index(x.shape[0], plan, got.device), weights, ids)
 
 
 class ExpertParallelMoE:
@@ -147,9 +147,9 @@ class ExpertParallelMoE:
         off = self.layout.route_out
         return self.workspace[off:off + n * TOP * H * 4].view(torch.float32).view(n, TOP, H)
 
-    def combine(self, rows, weights, ids):
+    def combine(self, rows, row_index, weights, ids):
         out = torch.empty((ids.shape[0], H), dtype=torch.bfloat16, device=rows.device)
-        self.native.combine_rows(rows, weights, ids, out, self.flags)
+        self.native.combine_gathered(rows, row_index, weights, ids, out, self.flags)
         return out
 
     def __call__(self, x, ids, weights):

@@ -53,6 +53,8 @@ SIGNATURES = {
         [C.c_void_p] * 14 + [C.c_size_t] + [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_moe_b200_get_layout': ([C.c_int, C.POINTER(C.c_size_t)], C.c_int),
     'ornith_moe_b200_combine': ([C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3, C.c_int),
+    'ornith_moe_b200_combine_gathered': ([C.c_void_p, C.c_int] + [C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3,
+                                         C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
 }
@@ -248,6 +250,19 @@ def combine_rows(route_rows, weights, ids, out, flags):
     _validate_routes(out, weights, ids)
     check(lib().ornith_moe_b200_combine(ptr(route_rows), ptr(weights), ptr(ids), T, ptr(out), ptr(flags),
                                         stream(out)), 'combine')
+
+
+def combine_gathered(rows, row_index, weights, ids, out, flags):
+    """Slot-ordered combine from gathered fp32 rows [n, 2048]; row_index int32 [T, 8]
+    names the row of each valid slot."""
+    T = ids.shape[0]
+    if (rows.dtype != torch.float32 or rows.dim() != 2 or rows.shape[1] != 2048 or not rows.is_contiguous()
+            or row_index.dtype != torch.int32 or row_index.shape != (T, 8) or not row_index.is_contiguous()
+            or out.dtype != torch.bfloat16 or out.shape != (T, 2048) or not out.is_contiguous()):
+        raise ValueError('combine_gathered requires FP32 rows [n,2048], INT32 row_index [T,8], BF16 out [T,2048]')
+    _validate_routes(out, weights, ids)
+    check(lib().ornith_moe_b200_combine_gathered(ptr(rows), rows.shape[0], ptr(row_index), ptr(weights), ptr(ids), T,
+                                                 ptr(out), ptr(flags), stream(out)), 'combine_gathered')
 
 
 def repack_n16_to_n32(codes16, meta16, N, K):

@@ -34,6 +34,16 @@ def fake_combine(rows, weights, ids):
     return out
 
 
+def fake_combine_gathered(rows, row_index, weights, ids):
+    """The same sum, reading slot s of token t from rows[row_index[t, s]]."""
+    T = ids.shape[0]
+    dense = torch.zeros((T, TOP, H), dtype=torch.float32)
+    have = row_index >= 0
+    dense[have] = rows[row_index[have].long()]
+    assert bool(((ids >= 0) <= have).all()), 'a valid slot came back without a row'
+    return fake_combine(dense.view(T * TOP, H), weights, ids)
+
+
 def _port():
     with socket.socket() as s:
         s.bind(('127.0.0.1', 0))
@@ -66,7 +76,7 @@ def _worker(rank, world, port, T, seed, q):
         def compute(xr, ir):
             return fake_rows(xr, ir, rank * epr) if xr.shape[0] else torch.zeros((0, TOP, H))
 
-        out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine)
+        out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered)
         ref = fake_combine(fake_rows(x, ids, 0).view(T * TOP, H), weights, ids)
         q.put((rank, bool(torch.equal(out, ref)), ''))
         dist.barrier()

@@ -356,3 +356,43 @@ def test_shared_slot_with_all_routed_padded(native, layer1, bank1, S, O, tables,
     np.testing.assert_array_equal(host_bits(out), ref)
     np.testing.assert_array_equal(host_bits(shared), ref_sh)
     assert int(flags.item()) == ref_flags
+
+
+@pytest.mark.parametrize('T', [1, 7, 64])
+def test_combine_gathered_matches_dense_combine(native, S, T):
+    """The expert-parallel home combine reads returned rows through a (token, slot)
+    index; it must give the dense per-route combine's bits, and flag a valid slot
+    whose row index is out of range."""
+    rng = np.random.default_rng(11 + T)
+    ids = rng.integers(0, 128, (T, 8)).astype(np.int32)
+    ids[rng.random((T, 8)) < 0.2] = -1
+    w = rng.random((T, 8)).astype(np.float32)
+    valid = ids >= 0
+    n = int(valid.sum())
+    order = rng.permutation(n)
+    row_index = -np.ones((T, 8), np.int32)
+    row_index[valid] = order
+    rows = rng.standard_normal((n + 3, 2048)).astype(np.float32)
+    dense = np.zeros((T * 8, 2048), np.float32)
+    dense[valid.reshape(-1)] = rows[order]
+    ref = np.zeros((T, 2048), np.float32)
+    for s in range(8):
+        ref = np.where(valid[:, s:s + 1], (ref + dense.reshape(T, 8, 2048)[:, s] * w[:, s:s + 1]).astype(np.float32),
+                       ref)
+    ref_bits = S.f32_to_bf16_bits(ref)
+    wd, idd = dev(w), dev(ids)
+    out_g = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    out_d = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    native.combine_gathered(dev(rows), dev(row_index), wd, idd, out_g, flags)
+    native.combine_rows(dev(dense), wd, idd, out_d, flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == 0
+    np.testing.assert_array_equal(host_bits(out_g), ref_bits)
+    np.testing.assert_array_equal(host_bits(out_d), ref_bits)
+    bad = row_index.copy()
+    t, s = np.argwhere(valid)[0]
+    bad[t, s] = n + 3
+    native.combine_gathered(dev(rows), dev(bad), wd, idd, out_g, flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) & 4
