@@ -52,7 +52,9 @@ extern "C" {
  * offsets of this library's buffers (gate_low: int8 token activations,
  * gate_scales/gate_sums: their fp16 scales and int32 sums, middle: fp32
  * SiLU*up rows, down_low/down_scales/down_sums: quantised middle,
- * route_out: fp32 per-route down projections, final_f32: fp32 combined sum);
+ * route_out: fp32 per-route down projections, final_f32: fp32 combined sum;
+ * for T > 32 the rows of middle and route_out are in expert-slot order, see
+ * ornith_moe_b200_gather_route_rows);
  * fields with no counterpart here (gate_x, gate_high, gate_y, down_x,
  * down_high) hold SIZE_MAX. */
 typedef struct OrnithRoutedDirectLayout {
@@ -169,6 +171,18 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine(
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine_gathered(
     const void* rows_f32, int n_rows, const void* row_index_i32, const void* weights_f32, const void* ids_i32,
     int T, void* output_bf16, void* flags_u32, cudaStream_t stream);
+
+/* Copies the fp32 down projections of n routes out of a workspace after a
+ * layer call of T tokens on it (capacity Tcap): row i of rows fp32 [n][2048]
+ * is the projection of route route_index[i] (8*token + slot, a slot with a
+ * valid id).  The layer keeps these rows in route order for T <= 32 and in
+ * expert-slot order on the tensor-core path, where this reads them through
+ * its route -> row map.  A route index outside [0, 8T) raises flag 4 and
+ * gives a zero row.  Used by the expert-parallel return exchange; no
+ * counterpart in the reference. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_gather_route_rows(
+    const void* workspace, size_t bytes, int T, int Tcap, const void* route_index_i32, int n, void* rows_f32,
+    void* flags_u32, cudaStream_t stream);
 
 /* Workspace size for ornith_moe_b200_launch_from_logits (0 <= Tcap <= 8192). */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes);

@@ -19,6 +19,11 @@ using namespace ornith;
 namespace ornith {
 static std::atomic<unsigned long long> g_launches{0};
 void count_launches(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n), std::memory_order_relaxed); }
+static bool generic_forced() {
+    const char* path = getenv("ORNITH_MOE_B200_PATH");
+    return path && strcmp(path, "generic") == 0;
+}
+bool rows_by_position(int T) { return !generic_forced() && T > kDecodeMaxT; }
 }  // namespace ornith
 
 namespace {
@@ -74,6 +79,26 @@ __global__ __launch_bounds__(256) void combine_gathered_kernel(const float* rows
     }
     f = __reduce_or_sync(0xffffffffu, f);
     if (f && (threadIdx.x & 31) == 0) atomicOr(flags, f);
+}
+
+// Copies route rows out of route_out (through rowpos on the tensor-core
+// path).  One CTA per row, 256 threads x 8 floats.
+__global__ __launch_bounds__(256) void gather_route_rows_kernel(const float* route_out, const int32_t* rowpos,
+                                                                const int32_t* route_index, int R, int rows,
+                                                                float* dst, uint32_t* flags) {
+    const int i = blockIdx.x;
+    const int r = route_index[i];
+    int row = -1;
+    if (r >= 0 && r < R) row = rowpos ? rowpos[r] : r;
+    float4* d = reinterpret_cast<float4*>(dst + size_t(i) * kH) + threadIdx.x * 2;
+    if (row < 0 || row >= rows) {
+        d[0] = d[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (threadIdx.x == 0) atomicOr(flags, kFlagInvalidId);
+        return;
+    }
+    const float4* src = reinterpret_cast<const float4*>(route_out + size_t(row) * kH) + threadIdx.x * 2;
+    d[0] = __ldcs(src);
+    d[1] = __ldcs(src + 1);
 }
 
 // N16 -> N32 bank repack (method.py:142-147).  One thread per destination word.
@@ -150,17 +175,14 @@ void fill_layout(int Tcap, OrnithRoutedDirectLayout* out) {
 // Path selection: the fused persistent kernel for decode batches, the
 // multi-kernel path otherwise.  ORNITH_MOE_B200_PATH=generic forces the
 // multi-kernel path (used by the tests to check both paths).
-bool force_generic() {
-    const char* path = getenv("ORNITH_MOE_B200_PATH");
-    return path && strcmp(path, "generic") == 0;
-}
+bool force_generic() { return generic_forced(); }
 
 // The fused decode kernel serves the call (it also routes from logits itself).
 bool uses_decode(int T) { return !force_generic() && decode_supported(T); }
 
 cudaError_t run_layer(const LayerArgs& a, cudaStream_t stream) {
     if (uses_decode(a.T)) return launch_decode(a, stream);
-    if (!force_generic() && a.T > kDecodeMaxT) return launch_prefill(a, stream);
+    if (rows_by_position(a.T)) return launch_prefill(a, stream);
     return launch_generic(a, stream);
 }
 
@@ -333,6 +355,26 @@ cudaError_t ornith_moe_b200_combine_gathered(const void* rows_f32, int n_rows, c
         static_cast<const float*>(rows_f32), n_rows, static_cast<const int32_t*>(row_index_i32),
         static_cast<const float*>(weights), static_cast<const int32_t*>(ids), T, static_cast<uint16_t*>(output),
         static_cast<uint32_t*>(flags));
+    return cudaGetLastError();
+}
+
+cudaError_t ornith_moe_b200_gather_route_rows(const void* workspace, size_t bytes, int T, int Tcap,
+                                             const void* route_index_i32, int n, void* rows_f32, void* flags,
+                                             cudaStream_t stream) {
+    if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap || n < 0) return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes) return cudaErrorInvalidValue;
+    if (!n) return cudaSuccess;
+    if (!workspace || !route_index_i32 || !rows_f32 || !flags || !aligned(workspace, 256) ||
+        !aligned(route_index_i32, 4) || !aligned(rows_f32, 16) || !aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+    const int32_t* rowpos = rows_by_position(T) ? reinterpret_cast<const int32_t*>(ws + w.rowpos) : nullptr;
+    count_launches(1);
+    gather_route_rows_kernel<<<n, 256, 0, stream>>>(reinterpret_cast<const float*>(ws + w.route_out), rowpos,
+                                                    static_cast<const int32_t*>(route_index_i32), T * kTop,
+                                                    T * (kTop + 1), static_cast<float*>(rows_f32),
+                                                    static_cast<uint32_t*>(flags));
     return cudaGetLastError();
 }
 

@@ -50,16 +50,20 @@ __device__ __forceinline__ float bf16_round_f32(float v) { return bf16_to_f32(bf
 
 // The reference's deterministic exponential (portable_exp.h:6-25): Cody-Waite
 // reduction n = rint(x*log2 e), two-part ln2, degree-8 Taylor in Horner form
-// evaluated without FMA, then ldexp.
+// evaluated without FMA, then ldexp.  Written without branches so that many
+// independent evaluations interleave: the same steps run on x clamped into
+// [-104, 89] and the special cases (NaN, x <= -104 -> 0, x >= 89 -> inf) are
+// selected at the end.  ldexp(p, n) is two power-of-two scalings: p lies in
+// [0.7, 1.42] and n in [-150, 128], so p * 2^(n>>1) is exact (normal) and the
+// second product rounds once, which is the correctly rounded p * 2^n that
+// ldexpf returns.
 __device__ __forceinline__ float portable_exp(float x) {
-    if (isnan(x)) return x;
-    if (x <= -104.f) return 0.f;
-    if (x >= 89.f) return __int_as_float(0x7f800000);
-    const float n_float = rintf(__fmul_rn(x, 0x1.715476p+0f));
+    const float xc = fminf(fmaxf(x, -104.f), 89.f);
+    const float n_float = rintf(__fmul_rn(xc, 0x1.715476p+0f));
     const int n = static_cast<int>(n_float);
     const float high = __fmul_rn(n_float, 0x1.62e400p-1f);
     const float low = __fmul_rn(n_float, 0x1.7f7d1cp-20f);
-    const float r = __fsub_rn(__fsub_rn(x, high), low);
+    const float r = __fsub_rn(__fsub_rn(xc, high), low);
     float p = 0x1.a01a02p-16f;
     p = __fadd_rn(__fmul_rn(p, r), 0x1.a01a02p-13f);
     p = __fadd_rn(__fmul_rn(p, r), 0x1.6c16c2p-10f);
@@ -69,7 +73,38 @@ __device__ __forceinline__ float portable_exp(float x) {
     p = __fadd_rn(__fmul_rn(p, r), 0x1p-1f);
     p = __fadd_rn(__fmul_rn(p, r), 0x1p+0f);
     p = __fadd_rn(__fmul_rn(p, r), 0x1p+0f);
-    return ldexpf(p, n);
+    const int n1 = n >> 1, n2 = n - n1;
+    float res = __fmul_rn(__fmul_rn(p, __int_as_float((n1 + 127) << 23)), __int_as_float((n2 + 127) << 23));
+    res = x >= 89.f ? __int_as_float(0x7f800000) : res;
+    res = x <= -104.f ? 0.f : res;
+    return isnan(x) ? x : res;
+}
+
+// g / d rounded to nearest even, for the SiLU denominator d = 1 + exp(-g) >= 1,
+// without a call on the common path.  Markstein's FMA-based method (P. W.
+// Markstein, IBM J. Res. Dev. 34(1), 1990): one Newton step on the hardware
+// reciprocal estimate, q0 = g*y, one FMA correction q1 = q0 + (g - d*q0)*y.
+// q1 is then checked exactly: r1 = g - d*q1 is exact by FMA when q1 is within
+// one ulp, and q1 is the correctly rounded quotient iff |r1| < d*ulp(q1)/2
+// when q1 is not a power of two (both neighbours one ulp away).  *ok is false
+// where that check cannot confirm q1 (powers of two, zero or tiny quotients,
+// d >= 2^24, |g| >= 2^64, non-finite operands); the caller then divides with
+// __fdiv_rn.  Checked against __fdiv_rn for every fp32 g with
+// d = 1 + portable_exp(-g).
+__device__ __forceinline__ float div_rn_ge1(float g, float d, bool& ok) {
+    float y0;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(d));
+    const float e = __fmaf_rn(-d, y0, 1.f);
+    const float y1 = __fmaf_rn(y0, e, y0);
+    const float q0 = __fmul_rn(g, y1);
+    const float r0 = __fmaf_rn(-d, q0, g);
+    const float q1 = __fmaf_rn(r0, y1, q0);
+    const float r1 = __fmaf_rn(-d, q1, g);
+    const uint32_t qb = __float_as_uint(q1);
+    const float half_ulp = __uint_as_float((qb & 0x7f800000u) - (24u << 23));
+    ok = d < 16777216.f && fabsf(g) < 0x1p64f && fabsf(q1) >= 0x1p-100f && (qb & 0x7fffffu) != 0u &&
+         fabsf(r1) < __fmul_rn(d, half_ulp);
+    return q1;
 }
 
 // Routed SiLU*up (middle_kernel): (g / (1 + exp(-g))) * up, IEEE division.

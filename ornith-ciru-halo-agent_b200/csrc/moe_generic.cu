@@ -275,17 +275,22 @@ __global__ __launch_bounds__(256) void down_kernel(LayerArgs a) {
 }
 
 // Slot-ordered weighted combine (reduce_slots :176-185, reduce_slots_shared :296-306).
+// BY_POSITION: the rows of route_out are in slot-position order (the
+// tensor-core path) and rowpos maps a route to its row.
+template <bool BY_POSITION>
 __global__ __launch_bounds__(256) void combine_kernel(LayerArgs a) {
     const size_t index = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
     uint32_t f = 0;
     if (index < size_t(a.T) * kH) {
         const int t = int(index / kH), c = int(index % kH);
         const float* route_out = ws_at<float>(a, a.L.route_out);
+        const int32_t* rowpos = BY_POSITION ? ws_at<int32_t>(a, a.L.rowpos) : nullptr;
+        auto row_of = [&](int r) { return size_t(BY_POSITION ? rowpos[r] : r); };
         float sum = 0.f;
 #pragma unroll
         for (int s = 0; s < kTop; ++s) {
             const int r = t * kTop + s;
-            if (id_valid(a.ids[r])) sum = __fadd_rn(sum, __fmul_rn(route_out[size_t(r) * kH + c], a.weights[r]));
+            if (id_valid(a.ids[r])) sum = __fadd_rn(sum, __fmul_rn(route_out[row_of(r) * kH + c], a.weights[r]));
         }
         uint16_t result = bf16_rne(sum);
         ws_at<float>(a, a.L.final_f32)[index] = sum;
@@ -293,7 +298,7 @@ __global__ __launch_bounds__(256) void combine_kernel(LayerArgs a) {
         if (!isfinite(sum) || (result & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
         if (a.shared) {
             float gate = bf16_to_f32(a.sigmoid_table[a.shared_logit[t]]);
-            float sh = __fmul_rn(route_out[size_t(a.T * kTop + t) * kH + c], gate);
+            float sh = __fmul_rn(route_out[row_of(a.T * kTop + t) * kH + c], gate);
             a.shared_out[index] = bf16_rne(sh);
             if (!isfinite(sh)) f |= kFlagNonfiniteOutput;
         }
@@ -330,9 +335,18 @@ cudaError_t launch_generic(const LayerArgs& a, cudaStream_t stream) {
     return launch_combine(a, stream);
 }
 
-cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream) {
+cudaError_t launch_quant_tokens(const LayerArgs& a, cudaStream_t stream) {
     count_launches(1);
-    combine_kernel<<<(a.T * kH + 255) / 256, 256, 0, stream>>>(a);
+    const int tok_warps = a.T * (kH / kG);
+    if (a.a8) quant_tokens_kernel<127><<<(tok_warps + 7) / 8, 256, 0, stream>>>(a);
+    else quant_tokens_kernel<7><<<(tok_warps + 7) / 8, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream, bool by_position) {
+    count_launches(1);
+    if (by_position) combine_kernel<true><<<(a.T * kH + 255) / 256, 256, 0, stream>>>(a);
+    else combine_kernel<false><<<(a.T * kH + 255) / 256, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -7,7 +7,10 @@ namespace ornith {
 
 // Workspace of one layer call, all offsets 256-byte aligned.  Rows of the
 // intermediate buffers are "routes": r < R = 8T are routed slots (token r/8,
-// slot r%8), r = R + t is the shared expert's row for token t.
+// slot r%8), r = R + t is the shared expert's row for token t.  On the
+// tensor-core path (rows_by_position) the rows of middle and route_out are in
+// slot-position order instead, so that one 128-route M-tile writes one
+// contiguous block; rowpos[r] is then the row of route r.
 struct Workspace {
     size_t xq, xs, xsum;          // token activations: int8 [T,2048] (permuted), fp16 [T,8], i32 [T,8]
     size_t middle;                // fp32 [R+T, 512] SiLU*up
@@ -168,7 +171,12 @@ void count_launches(int n);
 // Multi-kernel path, any T <= 8192.
 cudaError_t launch_generic(const LayerArgs& a, cudaStream_t stream);
 // Slot-ordered combine of route_out into out / shared_out (shared by the paths).
-cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream);
+cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream, bool by_position = false);
+// Hadamard + quantise every token group once into xq / xs / xsum.
+cudaError_t launch_quant_tokens(const LayerArgs& a, cudaStream_t stream);
+// True when a layer call of T tokens runs the tensor-core path, whose middle
+// and route_out rows are in slot-position order (see Workspace).
+bool rows_by_position(int T);
 // Tensor-core prefill path (T > kDecodeMaxT; needs a workspace laid out for Tcap > kDecodeMaxT).
 cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream);
 // Fused persistent path for decode batches (T <= kDecodeMaxT).

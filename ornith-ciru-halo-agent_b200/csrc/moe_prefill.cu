@@ -8,9 +8,9 @@
 //   prefill_count/scan/place_kernel  routing plan (slot counts/offsets/route
 //                         lists, the inverse map route -> position) and the
 //                         list of 128-route M-tiles per expert slot;
-//   pack_tokens_kernel    Hadamard + quantise each token group once and write
-//                         it into the M-tile of each of its routes, in the
-//                         no-swizzle K-major core-matrix layout tcgen05 reads;
+//   quant_tokens_kernel   Hadamard + quantise each token group once (xq);
+//   pack_gather_kernel    copy each M-tile's token rows into the no-swizzle
+//                         K-major core-matrix layout tcgen05 reads;
 //   mma_kernel<8, gate>   gate/up grouped GEMM: tcgen05.mma.kind::i8
 //                         (s8 activations x u8 codes -> s32 in TMEM),
 //                         M=128 x N=256 (128 gate + 128 matching up columns),
@@ -18,7 +18,10 @@
 //   pack_middle_kernel    Hadamard + quantise the middle rows into down M-tiles;
 //   mma_kernel<2, down>   down grouped GEMM, N=256 output columns -> route_out;
 //   combine               slot-ordered weighted sum (shared with the
-//                         multi-kernel path).
+//                         multi-kernel path), reading rows through rowpos.
+// middle and route_out rows are in slot-position order: the 128 rows of an
+// M-tile are one contiguous block, so the epilogue's row stores stay inside
+// it instead of scattering over the whole buffer (one TLB reach per tile).
 //
 // mma_kernel roles (20 warps, one CTA per SM, persistent over tiles):
 //   warp 0      producer: cp.async.bulk of the activation half-tile (16 KB),
@@ -47,6 +50,7 @@ constexpr int kBuBytes = kNT * 128;       // unpacked codes half-tile
 constexpr int kStageBytes = kABytes + kBpBytes + kBuBytes;
 constexpr int kMetaBytes = kNT * 4 + kMT * 4 + kMT * 4;  // B meta, A scale, A sum
 constexpr int kMetaFBytes = kNT * 4 * 2;                   // fp32 column scales then offsets
+constexpr int kMetaSlots = 4;  // metadata ring: the producer runs up to 4 groups ahead of the epilogue
 constexpr int kWarps = 20;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarps = 16;
@@ -59,6 +63,19 @@ __device__ __forceinline__ uint64_t now_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+
+// Per-role timestamps of a few CTAs (clock64), compiled in only with
+// -DORNITH_PREFILL_TRACE; the default build has none.
+#ifdef ORNITH_PREFILL_TRACE
+constexpr int kPTraceCtas = 4, kPTraceKinds = 10, kPTraceLen = 256;
+__device__ unsigned long long g_prefill_trace[2][kPTraceCtas][kPTraceKinds][kPTraceLen];
+#define PREFILL_TRACE(kind, idx)                                                                         \
+    ((blockIdx.x % 37 == 0 && blockIdx.x / 37 < kPTraceCtas && (idx) < kPTraceLen)                      \
+         ? void(g_prefill_trace[GATE ? 0 : 1][blockIdx.x / 37][kind][idx] = clock64())                  \
+         : void(0))
+#else
+#define PREFILL_TRACE(kind, idx) ((void)0)
+#endif
 
 // ---- tcgen05 wrappers ----------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -150,18 +167,41 @@ __device__ void drain_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// 8 x 8 transpose of float4 chunks inside each group of eight lanes: chunk r
+// of lane 8a + j ends in chunk j of lane 8a + r.  Three butterfly stages; at
+// stage d every chunk whose index differs from the lane in bit d trades
+// places with the partner lane's chunk of index r ^ d.
+__device__ __forceinline__ void transpose8(float4 (&c)[8], int lane) {
+#pragma unroll
+    for (int d = 1; d < 8; d <<= 1) {
+        const bool hi = (lane & d) != 0;
+#pragma unroll
+        for (int r0 = 0; r0 < 8; ++r0) {
+            if (r0 & d) continue;
+            const int r1 = r0 | d;
+            const float4 send = hi ? c[r0] : c[r1];
+            float4 recv;
+            recv.x = __shfl_xor_sync(0xffffffffu, send.x, d);
+            recv.y = __shfl_xor_sync(0xffffffffu, send.y, d);
+            recv.z = __shfl_xor_sync(0xffffffffu, send.z, d);
+            recv.w = __shfl_xor_sync(0xffffffffu, send.w, d);
+            if (hi) c[r0] = recv;
+            else c[r1] = recv;
+        }
+    }
+}
+
 struct MmaArgs {
     const uint8_t* atiles;   // [MT][KG][32768] activation tiles
     const float* asa;        // [MT][KG][128] activation scales
     const int32_t* asum;     // [MT][KG][128] activation sums
     const int4* mtiles;      // {slot, first position, rows, 0}
     const int32_t* n_mtiles;
-    const int32_t* routes;   // position -> route
     const uint32_t* codes;   // routed bank
     const uint32_t* meta;
     const uint32_t* scodes;  // shared bank
     const uint32_t* smeta;
-    float* out;              // gate: middle [rows][512]; down: route_out [rows][2048]
+    float* out;              // gate: middle [positions][512]; down: route_out [positions][2048]
     const float* silu_table;
     uint32_t* flags;
 };
@@ -175,15 +215,15 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
     constexpr size_t BANK_META = size_t(BANK_N) * KG;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* stages = smem;
-    uint8_t* metabuf = smem + kStages * kStageBytes;  // [2][kMetaBytes]
-    float* metaf = reinterpret_cast<float*>(metabuf + 2 * kMetaBytes);  // [2][scales 256 | offsets 256]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(metabuf + 2 * kMetaBytes + 2 * kMetaFBytes);
+    uint8_t* metabuf = smem + kStages * kStageBytes;  // [kMetaSlots][kMetaBytes]
+    float* metaf = reinterpret_cast<float*>(metabuf + kMetaSlots * kMetaBytes);  // [2][scales 256 | offsets 256]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(metabuf + kMetaSlots * kMetaBytes + 2 * kMetaFBytes);
     uint64_t* full = bars;                       // [kStages] producer -> converters
     uint64_t* conv = bars + kStages;             // [kStages] converters -> MMA
     uint64_t* empty = bars + 2 * kStages;        // [kStages] MMA -> producer
-    uint64_t* meta_full = bars + 3 * kStages;    // [2]
-    uint64_t* meta_empty = meta_full + 2;        // [2]
-    uint64_t* acc_full = meta_empty + 2;         // [2]
+    uint64_t* meta_full = bars + 3 * kStages;    // [kMetaSlots]
+    uint64_t* meta_empty = meta_full + kMetaSlots;  // [kMetaSlots]
+    uint64_t* acc_full = meta_empty + kMetaSlots;   // [2]
     uint64_t* acc_empty = acc_full + 2;          // [2]
     uint64_t* drain = acc_empty + 2;             // [1] final MMA completion
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -196,9 +236,11 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
             mbar_init(&conv[i], 2);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kMetaSlots; ++i) {
             mbar_init(&meta_full[i], 1);
             mbar_init(&meta_empty[i], kEpiWarps);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], kEpiWarps);
         }
@@ -212,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int n_units = *p.n_mtiles * NUPT;
+    if (tid == 0) PREFILL_TRACE(9, 0);
 
     auto unit_bank = [&](int unit, const uint32_t*& codes, const uint32_t*& meta) {
         const int4 mt = p.mtiles[unit / NUPT];
@@ -231,16 +274,18 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 unit_bank(unit, codes, meta);
                 const int nt = unit % NUPT, tile = unit / NUPT;
                 for (int g = 0; g < KG && !*abort; ++g) {
-                    if (!(metas < 2 || bwait(&meta_empty[metas & 1], uint32_t(metas / 2 - 1) & 1u, abort, p.flags)))
+                    if (!(metas < kMetaSlots || bwait(&meta_empty[metas % kMetaSlots],
+                                                      uint32_t(metas / kMetaSlots - 1) & 1u, abort, p.flags)))
                         break;
                     {
-                        const int mb = metas & 1;
+                        const int mb = metas % kMetaSlots;
                         uint8_t* m = metabuf + mb * kMetaBytes;
                         mbar_arrive_expect_tx(&meta_full[mb], kMetaBytes);
                         for (int i = 0; i < 8; ++i)
                             bulk_g2s(m + i * 128, meta + (size_t(n32_of(nt, i)) * KG + g) * 32, 128, &meta_full[mb]);
                         bulk_g2s(m + kNT * 4, p.asa + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
                         bulk_g2s(m + kNT * 4 + kMT * 4, p.asum + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
+                        PREFILL_TRACE(0, metas);
                         ++metas;
                     }
                     for (int h = 0; h < 2; ++h) {
@@ -255,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         for (int i = 0; i < 8; ++i)
                             bulk_g2s(sBp + i * 2048, codes + (size_t(n32_of(nt, i)) * KG + g) * 1024 + h * 512, 2048,
                                      &full[s]);
+                        PREFILL_TRACE(1, issued);
                         ++issued;
                     }
                 }
@@ -263,8 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 // every issued copy lands before the CTA can leave
                 for (int k = issued - kStages; k < issued; ++k)
                     if (k >= 0) drain_wait(&full[k % kStages], uint32_t(k / kStages) & 1u);
-                for (int k = metas - 2; k < metas; ++k)
-                    if (k >= 0) drain_wait(&meta_full[k & 1], uint32_t(k / 2) & 1u);
+                for (int k = metas - kMetaSlots; k < metas; ++k)
+                    if (k >= 0) drain_wait(&meta_full[k % kMetaSlots], uint32_t(k / kMetaSlots) & 1u);
             }
         }
     } else if (warp == 1) {
@@ -277,11 +323,13 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                     const int b = gg & 1;
                     if (!bwait(&acc_empty[b], uint32_t(gg / 2) & 1u, abort, p.flags)) break;
                     tc_fence_after();
+                    PREFILL_TRACE(4, gg);
                     const uint32_t d = tmem + uint32_t(b * kNT);
                     for (int h = 0; h < 2; ++h, ++st) {
                         const int s = st % kStages;
                         if (!bwait(&conv[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
                         tc_fence_after();
+                        PREFILL_TRACE(5, st);
                         const uint32_t aaddr = smem_addr(stages + size_t(s) * kStageBytes);
                         const uint32_t baddr = aaddr + kABytes + kBpBytes;
 #pragma unroll
@@ -302,29 +350,43 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
         }
     } else if (warp < 4) {
         // ---------------- converters ----------------
-        const int ct = tid - 64;  // 0..63
+        const int cw = warp - 2;  // converter warp 0..1
         int st = 0;
         for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
             for (int g = 0; g < KG && !*abort; ++g) {
                 for (int h = 0; h < 2; ++h, ++st) {
                     const int s = st % kStages;
                     if (!bwait(&full[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
-                    const uint32_t* bp = reinterpret_cast<const uint32_t*>(stages + size_t(s) * kStageBytes + kABytes);
-                    uint8_t* bu = stages + size_t(s) * kStageBytes + kABytes + kBpBytes;
-                    // work item (i, q, c): 32-column tile i (8), word pair q (8), column c (32)
-#pragma unroll 4
-                    for (int it = ct; it < 8 * 8 * 32; it += 64) {
-                        const int c = it & 31, q = (it >> 5) & 7, i = it >> 8;
-                        const uint32_t w0 = bp[i * 512 + (2 * q) * 32 + c];
-                        const uint32_t w1 = bp[i * 512 + (2 * q + 1) * 32 + c];
-                        const int n = 32 * i + c;
-                        const uint4 v = make_uint4(w0 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu,
-                                                   (w1 >> 4) & 0x0f0f0f0fu);
-                        *reinterpret_cast<uint4*>(bu + q * 4096 + (n >> 3) * 128 + (n & 7) * 16) = v;
+                    if (warp == 2 && lane == 0) PREFILL_TRACE(2, st);
+                    // Work item (i, q, c): 32-column tile i (8), word pair q (8),
+                    // column c = lane; converter warp cw takes the pairs
+                    // q = cw + 2*qq.  Packed word j of column c of tile i is
+                    // bp[512 i + 32 j + c]; column n = 32 i + c of the K-major
+                    // core-matrix layout takes pair q at byte
+                    // 4096 q + 128 (n >> 3) + 16 (n & 7).  Every offset below
+                    // is a compile-time constant from two per-thread bases.
+                    const uint32_t* bp = reinterpret_cast<const uint32_t*>(stages + size_t(s) * kStageBytes + kABytes) +
+                                         lane + 64 * cw;
+                    uint8_t* bu = stages + size_t(s) * kStageBytes + kABytes + kBpBytes + cw * 4096 + (lane >> 3) * 128 +
+                                  (lane & 7) * 16;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        uint32_t w[8];
+#pragma unroll
+                        for (int qq = 0; qq < 4; ++qq) {
+                            w[2 * qq] = bp[i * 512 + qq * 128];
+                            w[2 * qq + 1] = bp[i * 512 + qq * 128 + 32];
+                        }
+#pragma unroll
+                        for (int qq = 0; qq < 4; ++qq)
+                            *reinterpret_cast<uint4*>(bu + qq * 8192 + i * 512) =
+                                make_uint4(w[2 * qq] & 0x0f0f0f0fu, (w[2 * qq] >> 4) & 0x0f0f0f0fu,
+                                           w[2 * qq + 1] & 0x0f0f0f0fu, (w[2 * qq + 1] >> 4) & 0x0f0f0f0fu);
                     }
                     fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&conv[s]);
+                    if (warp == 2 && lane == 0) PREFILL_TRACE(3, st);
                 }
             }
         }
@@ -353,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
         }
         uint32_t f = 0;
         int gg = 0;
+        int un = 0;  // units done (trace index)
         const int et = tid - 128;  // 0..511 within the epilogue warps
         // Every exit from these loops is a collective decision (named_and), so the
         // 16 warps always pass the same sequence of barrier 1.
@@ -366,24 +429,28 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
             bool ok = true;
             for (int g = 0; g < KG; ++g, ++gg) {
                 const int b = gg & 1;
-                const bool mine = ok && bwait(&meta_full[b], uint32_t(gg / 2) & 1u, abort, p.flags);
+                const int ms = gg % kMetaSlots;
+                const uint8_t* mslot = metabuf + ms * kMetaBytes;
+                const bool mine = ok && bwait(&meta_full[ms], uint32_t(gg / kMetaSlots) & 1u, abort, p.flags);
                 // the group's column metadata, converted once for all rows
                 if (mine && et < kNT) {
-                    const uint32_t mw = reinterpret_cast<const uint32_t*>(metabuf + b * kMetaBytes)[et];
+                    const uint32_t mw = reinterpret_cast<const uint32_t*>(mslot)[et];
                     metaf[b * 2 * kNT + et] = __half2float(__ushort_as_half(uint16_t(mw & 0xffffu)));
                     metaf[b * 2 * kNT + kNT + et] = __half2float(__ushort_as_half(uint16_t(mw >> 16)));
                 }
                 ok = named_and(1, kEpiWarps * 32, mine);
                 if (!ok) break;
+                if (ew == 0 && lane == 0) PREFILL_TRACE(6, gg);
                 if (!bwait(&acc_full[b], uint32_t(gg / 2) & 1u, abort, p.flags)) {
                     ok = false;  // voted at the next barrier
                     continue;
                 }
                 tc_fence_after();
+                if (ew == 0 && lane == 0) PREFILL_TRACE(7, gg);
                 const float* swf = metaf + b * 2 * kNT;
                 const float* offf = swf + kNT;
-                const float sa = reinterpret_cast<const float*>(metabuf + b * kMetaBytes + kNT * 4)[row];
-                const int ssumi = reinterpret_cast<const int32_t*>(metabuf + b * kMetaBytes + kNT * 4 + kMT * 4)[row];
+                const float sa = reinterpret_cast<const float*>(mslot + kNT * 4)[row];
+                const int ssumi = reinterpret_cast<const int32_t*>(mslot + kNT * 4 + kMT * 4)[row];
                 const float ssum = __fmul_rn(sa, float(ssumi));
                 const uint32_t base = tmem + lane_base + uint32_t(b * kNT);
 #pragma unroll
@@ -413,50 +480,94 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&acc_empty[b]);
-                    mbar_arrive(&meta_empty[b]);
+                    mbar_arrive(&meta_empty[ms]);
                 }
+                if (ew == 0 && lane == 0) PREFILL_TRACE(8, gg);
             }
             if (!ok) break;
-            if (row < mt.z) {
-                const int route = p.routes[mt.y + row];
-                const bool shared = mt.x == kE;
-                if (GATE) {
-                    float* dst = p.out + size_t(route) * kI + kMT * nt + 32 * wg;
+            if (ew == 0 && lane == 0) PREFILL_TRACE(9, 2 + 4 * un);
+            // Unit results, written as whole 128-byte lines: the eight float4
+            // chunks of a lane are transposed across its group of eight lanes,
+            // so that store m of lane 8a + j writes chunk j of tile row
+            // rbase + m.  Flags count only the tile's real rows.
+            const bool valid = row < mt.z;
+            const bool shared = mt.x == kE;
+            const int rbase = 32 * (warp & 3) + 8 * (lane >> 3), jc = lane & 7;
+            float4 c[8];
+            if (GATE) {
+                if (shared) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
+                    for (int k = 0; k < 8; ++k) {
                         float v[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            float gv = acc[i + j], uv = acc[32 + i + j], value;
-                            if (shared) {
-                                gv = bf16_round_f32(gv);
-                                uv = bf16_round_f32(uv);
-                                if (!isfinite(gv) || !isfinite(uv)) f |= kFlagNonfiniteProjection;
-                                value = bf16_round_f32(__fmul_rn(p.silu_table[__float_as_uint(gv) >> 16], uv));
-                            } else {
-                                if (!isfinite(gv) || !isfinite(uv)) f |= kFlagNonfiniteProjection;
-                                value = silu_mul(gv, uv);
-                            }
-                            if (!isfinite(value)) f |= kFlagNonfiniteMiddle;
-                            v[j] = value;
+                            const float gv = bf16_round_f32(acc[4 * k + j]), uv = bf16_round_f32(acc[32 + 4 * k + j]);
+                            if (valid && (!isfinite(gv) || !isfinite(uv))) f |= kFlagNonfiniteProjection;
+                            v[j] = bf16_round_f32(__fmul_rn(p.silu_table[__float_as_uint(gv) >> 16], uv));
+                            if (valid && !isfinite(v[j])) f |= kFlagNonfiniteMiddle;
                         }
-                        *reinterpret_cast<float4*>(dst + i) = make_float4(v[0], v[1], v[2], v[3]);
+                        c[k] = make_float4(v[0], v[1], v[2], v[3]);
                     }
                 } else {
-                    float* dst = p.out + size_t(route) * kH + kNT * nt + 64 * wg;
+                    // silu_mul in batches of 8: the eight exponentials and
+                    // divisions are independent straight-line chains and
+                    // interleave; the rare quotients the fast division cannot
+                    // confirm are redone with __fdiv_rn
 #pragma unroll
-                    for (int i = 0; i < 64; i += 4) {
+                    for (int i = 0; i < 32; i += 8) {
+                        float d[8], q[8], v[8];
+                        bool ok[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) d[j] = __fadd_rn(1.f, portable_exp(-acc[i + j]));
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) q[j] = div_rn_ge1(acc[i + j], d[j], ok[j]);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            if (!ok[j]) q[j] = __fdiv_rn(acc[i + j], d[j]);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float gv = acc[i + j], uv = acc[32 + i + j];
+                            if (valid && (!isfinite(gv) || !isfinite(uv))) f |= kFlagNonfiniteProjection;
+                            v[j] = __fmul_rn(q[j], uv);
+                            if (valid && !isfinite(v[j])) f |= kFlagNonfiniteMiddle;
+                        }
+                        c[i / 4] = make_float4(v[0], v[1], v[2], v[3]);
+                        c[i / 4 + 1] = make_float4(v[4], v[5], v[6], v[7]);
+                    }
+                }
+                if (ew == 0 && lane == 0) PREFILL_TRACE(9, 3 + 4 * un);
+                transpose8(c, lane);
+                if (ew == 0 && lane == 0) PREFILL_TRACE(9, 4 + 4 * un);
+                float* dst = p.out + size_t(mt.y + rbase) * kI + kMT * nt + 32 * wg + 4 * jc;
+#pragma unroll
+                for (int m = 0; m < 8; ++m)
+                    if (rbase + m < mt.z) *reinterpret_cast<float4*>(dst + size_t(m) * kI) = c[m];
+            } else {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
                         float v[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            v[j] = shared ? bf16_round_f32(acc[i + j]) : acc[i + j];
-                            if (!isfinite(v[j])) f |= kFlagNonfiniteProjection;
+                            v[j] = shared ? bf16_round_f32(acc[32 * h + 4 * k + j]) : acc[32 * h + 4 * k + j];
+                            if (valid && !isfinite(v[j])) f |= kFlagNonfiniteProjection;
                         }
-                        *reinterpret_cast<float4*>(dst + i) = make_float4(v[0], v[1], v[2], v[3]);
+                        c[k] = make_float4(v[0], v[1], v[2], v[3]);
                     }
+                    if (ew == 0 && lane == 0 && h == 0) PREFILL_TRACE(9, 3 + 4 * un);
+                    transpose8(c, lane);
+                    if (ew == 0 && lane == 0 && h == 0) PREFILL_TRACE(9, 4 + 4 * un);
+                    float* dst = p.out + size_t(mt.y + rbase) * kH + kNT * nt + 64 * wg + 32 * h + 4 * jc;
+#pragma unroll
+                    for (int m = 0; m < 8; ++m)
+                        if (rbase + m < mt.z) *reinterpret_cast<float4*>(dst + size_t(m) * kH) = c[m];
                 }
             }
+            if (ew == 0 && lane == 0) PREFILL_TRACE(9, 5 + 4 * un);
+            ++un;
         }
+        if (ew == 0 && lane == 0) PREFILL_TRACE(9, 1);
         f = __reduce_or_sync(0xffffffffu, f);
         if (f && lane == 0) atomicOr(p.flags, f);
     }
@@ -594,68 +705,34 @@ __device__ __forceinline__ size_t core_offset(int row, int lane) {
     return size_t(lane >> 1) * 2048 + (row >> 3) * 128 + (row & 7) * 16 + (lane & 1) * 8;
 }
 
-// Token Hadamard + quantise, scattered to the gate activation tiles of every
-// route of the token.  One warp per (token, 256-group).
-template <int QMAX>
-__global__ __launch_bounds__(256) void pack_tokens_kernel(LayerArgs a) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= a.T * 8) return;
-    const int t = warp / 8, g = warp % 8;
-    bool live = a.shared_all_live;
-    if (!live)
-        for (int s = 0; s < kTop; ++s) live |= id_valid(a.ids[t * kTop + s]);
-    if (!live) return;  // no route reads this token
-    const uint4 raw = *reinterpret_cast<const uint4*>(a.x + size_t(t) * kH + g * kG + lane * 8);
-    const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-    float e[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        e[2 * i] = __uint_as_float(w4[i] << 16);
-        e[2 * i + 1] = __uint_as_float(w4[i] & 0xffff0000u);
-    }
-    uint32_t f = 0;
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
-    wht128_halfwarp(e, lane);
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
-    __shared__ uint2 qbuf[8][32];
-    __shared__ __half sbuf[8];
-    __shared__ int32_t mbuf[8];
-    const int wl = threadIdx.x >> 5;
-    quantize_group_warp<QMAX>(e, lane, qbuf[wl], &sbuf[wl], &mbuf[wl], f);
-    __syncwarp();
-    const uint2 q = qbuf[wl][lane];
-    const float sa = __half2float(sbuf[wl]);
-    const int32_t sum = mbuf[wl];
+// Gate activation tiles from the quantised tokens (xq, xs, xsum, written once
+// per token by the token quantisation kernel): one CTA per (M-tile, 256-group)
+// copies the 128 rows' 256 bytes into the tile's K-major core-matrix layout
+// [chunk 16][row 128][16 bytes].  Thread = (row, chunk pair): its loads read
+// 16 bytes of one token row (L2-resident), its stores are contiguous across
+// the warp, so the 32 KB tile is written in whole lines.
+__global__ __launch_bounds__(256) void pack_gather_kernel(LayerArgs a) {
+    const int tile = blockIdx.x >> 3, g = blockIdx.x & 7;
+    if (tile >= *ws_at<int32_t>(a, a.L.n_mtiles)) return;
+    const int4 mt = ws_at<int4>(a, a.L.mtiles)[tile];
+    const int row = threadIdx.x & 127;
+    if (row >= mt.z) return;
     const int R = a.T * kTop;
-    uint8_t* tiles = ws_at<uint8_t>(a, a.L.agate);
-    float* asa = ws_at<float>(a, a.L.agate_sa);
-    int32_t* asum = ws_at<int32_t>(a, a.L.agate_sum);
-    const int32_t* rowpos = ws_at<int32_t>(a, a.L.rowpos);
-    for (int s = 0; s <= kTop; ++s) {
-        int route, slot;
-        if (s < kTop) {
-            route = t * kTop + s;
-            slot = a.ids[route];
-            if (!id_valid(slot)) continue;
-        } else {
-            if (!a.shared) break;
-            route = R + t;
-            slot = kE;
-        }
-        int tile, row;
-        tile_row(a, slot, rowpos[route], tile, row);
-        *reinterpret_cast<uint2*>(tiles + (size_t(tile) * 8 + g) * 32768 + core_offset(row, lane)) = q;
-        if (lane == 0) {
-            asa[(size_t(tile) * 8 + g) * kMT + row] = sa;
-            asum[(size_t(tile) * 8 + g) * kMT + row] = sum;
-        }
+    const int route = ws_at<int32_t>(a, a.L.routes)[mt.y + row];
+    const int t = route >= R ? route - R : route / kTop;
+    const uint4* src = reinterpret_cast<const uint4*>(ws_at<uint8_t>(a, a.L.xq) + size_t(t) * kH + g * kG);
+    uint4* dst = reinterpret_cast<uint4*>(ws_at<uint8_t>(a, a.L.agate) + (size_t(tile) * 8 + g) * 32768) + row;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int chunk = (threadIdx.x >> 7) + 2 * k;
+        dst[chunk * kMT] = __ldcg(src + chunk);
     }
-    f = __reduce_or_sync(0xffffffffu, f);
-    if (f && lane == 0) atomicOr(a.flags, f);
+    if (threadIdx.x < kMT) {
+        ws_at<float>(a, a.L.agate_sa)[(size_t(tile) * 8 + g) * kMT + row] =
+            __half2float(ws_at<__half>(a, a.L.xs)[t * (kH / kG) + g]);
+        ws_at<int32_t>(a, a.L.agate_sum)[(size_t(tile) * 8 + g) * kMT + row] =
+            ws_at<int32_t>(a, a.L.xsum)[t * (kH / kG) + g];
+    }
 }
 
 // Middle Hadamard + quantise into the down activation tiles: one warp per
@@ -670,7 +747,7 @@ __global__ __launch_bounds__(256) void pack_middle_kernel(LayerArgs a) {
     const int R = a.T * kTop;
     const int slot = route >= R ? kE : a.ids[route];
     const float4* src =
-        reinterpret_cast<const float4*>(ws_at<float>(a, a.L.middle) + size_t(route) * kI + g * kG + lane * 8);
+        reinterpret_cast<const float4*>(ws_at<float>(a, a.L.middle) + size_t(pos) * kI + g * kG + lane * 8);
     const float4 v0 = src[0], v1 = src[1];
     float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     uint32_t f = 0;
@@ -699,7 +776,7 @@ __global__ __launch_bounds__(256) void pack_middle_kernel(LayerArgs a) {
     if (f && lane == 0) atomicOr(a.flags, f);
 }
 
-constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + 2 * kMetaBytes + 2 * kMetaFBytes + 64 * 8 + 64;
+constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + kMetaSlots * kMetaBytes + 2 * kMetaFBytes + 64 * 8 + 64;
 
 struct DeviceState {
     int sms = 0;
@@ -708,6 +785,13 @@ struct DeviceState {
 DeviceState g_state[64];
 
 }  // namespace
+
+#ifdef ORNITH_PREFILL_TRACE
+// Copies the role timestamps of the last gate and down launches.
+extern "C" __attribute__((visibility("default"))) int ornith_moe_b200_prefill_trace(void* dst) {
+    return int(cudaMemcpyFromSymbol(dst, g_prefill_trace, sizeof(g_prefill_trace)));
+}
+#endif
 
 cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     int device = 0;
@@ -728,23 +812,22 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     }
     const int T = a.T, R = T * kTop, rows = R + (a.shared ? T : 0);
     const int nblk = min(kPlanBlocks, max(1, (R + 255) / 256));
-    count_launches(7);
+    count_launches(7);  // plan x3, gather, gate, middle, down; quantisation and combine count their own
     prefill_count_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
     prefill_scan_kernel<<<1, 1024, 0, stream>>>(a, nblk);
     prefill_place_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
     if ((st = cudaGetLastError()) != cudaSuccess) return st;
-    if (a.a8) pack_tokens_kernel<127><<<(T * 8 + 7) / 8, 256, 0, stream>>>(a);
-    else pack_tokens_kernel<7><<<(T * 8 + 7) / 8, 256, 0, stream>>>(a);
-    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    if ((st = launch_quant_tokens(a, stream)) != cudaSuccess) return st;
     // upper bound of M-tiles (the kernels read the device-side count)
     const int max_tiles = (rows + kMT - 1) / kMT + (kE + 1);
+    pack_gather_kernel<<<max_tiles * 8, 256, 0, stream>>>(a);
+    if ((st = cudaGetLastError()) != cudaSuccess) return st;
     MmaArgs g{};
     g.atiles = ws_at<uint8_t>(a, a.L.agate);
     g.asa = ws_at<float>(a, a.L.agate_sa);
     g.asum = ws_at<int32_t>(a, a.L.agate_sum);
     g.mtiles = ws_at<int4>(a, a.L.mtiles);
     g.n_mtiles = ws_at<int32_t>(a, a.L.n_mtiles);
-    g.routes = ws_at<int32_t>(a, a.L.routes);
     g.codes = a.gate_codes;
     g.meta = a.gate_meta;
     g.scodes = a.sgate_codes;
@@ -769,7 +852,7 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     d.out = ws_at<float>(a, a.L.route_out);
     down<<<min(ds.sms, max_tiles * 8), kThreads, kMmaSmem, stream>>>(d);
     if ((st = cudaGetLastError()) != cudaSuccess) return st;
-    return launch_combine(a, stream);
+    return launch_combine(a, stream, true);
 }
 
 }  // namespace ornith

@@ -12,7 +12,7 @@ for its own tokens.  One layer call on every rank, for the rank's own tokens:
   3. exchange: counts, then token rows (bf16 pairs carried as int32) and local
      ids (all_to_all_single; NCCL on GPUs, gloo on CPU);
   4. expert compute on the received rows with the local banks; the fp32
-     per-route down projections of the valid slots are kept;
+     down projections of the valid slots are gathered in (token, slot) order;
   5. return exchange of those rows, one per (token, slot) owned by d;
   6. home combine: slot-ordered weighted sum into bf16 with the same
      arithmetic as the single-GPU layer, so the result is bit-identical to it;
@@ -75,17 +75,16 @@ def exchange_rows(group, world, plan, x):
     return x_recv.view(x.dtype), ids_recv, recv_counts
 
 
-def return_rows(group, world, plan, ids_recv, recv_counts, route_rows):
+def return_rows(group, world, plan, ids_recv, recv_counts, out_rows):
     """Send every (token, slot) row computed here back to the token's home rank.
 
-    route_rows: fp32 [n_recv, 8, 2048] per received token and slot.  Only the
-    slots with a valid local id travel, in (token, slot) order.  Returns the
-    home-side fp32 rows [n_sent_slots, 2048] in the order of plan.slot_mask."""
+    out_rows: fp32 [n_valid, 2048], one row per received slot with a valid
+    local id, in (token, slot) order.  Returns the home-side fp32 rows
+    [n_sent_slots, 2048] in the order of plan.slot_mask."""
     valid = ids_recv >= 0
-    out_rows = route_rows[valid].contiguous()  # (token, slot) order
     back_counts = [int(v.sum()) for v in torch.split(valid.sum(dim=1), recv_counts)]
     home_counts = [int(m.sum()) for m in torch.split(plan.slot_mask, plan.send_counts)]
-    got = torch.empty((sum(home_counts), H), dtype=torch.float32, device=route_rows.device)
+    got = torch.empty((sum(home_counts), H), dtype=torch.float32, device=out_rows.device)
     _a2a(group, got, out_rows, home_counts, back_counts)
     return got
 
@@ -102,13 +101,14 @@ def route_row_index(T, plan, device):
 def ep_layer(group, world, x, ids, weights, compute, combine):
     """One expert-parallel layer call.
 
-    compute(x_recv, ids_recv) -> fp32 [n_recv, 8, 2048] per-slot rows for this
-    rank's experts; combine(rows [n, 2048], row_index [T, 8], weights, ids) ->
-    output.  Both are injected so that the host logic also runs on CPU ranks."""
+    compute(x_recv, ids_recv) -> fp32 [n_valid, 2048]: the rows of the received
+    slots with a valid id, in (token, slot) order; combine(rows [n, 2048],
+    row_index [T, 8], weights, ids) -> output.  Both are injected so that the
+    host logic also runs on CPU ranks."""
     plan = build_dispatch(ids, world)
     x_recv, ids_recv, recv_counts = exchange_rows(group, world, plan, x)
-    route_rows = compute(x_recv, ids_recv)
-    got = return_rows(group, world, plan, ids_recv, recv_counts, route_rows)
+    out_rows = compute(x_recv, ids_recv)
+    got = return_rows(group, world, plan, ids_recv, recv_counts, out_rows)
     return combine(got, route_row_index(x.shape[0], plan, got.device), weights, ids)
 
 
@@ -144,8 +144,10 @@ class ExpertParallelMoE:
                                                       self.workspace)],
                             self.workspace.numel(), native.ptr(self._scratch_out), native.ptr(self.flags), n,
                             self.capacity, native.stream(x_recv)), 'expert-parallel compute')
-        off = self.layout.route_out
-        return self.workspace[off:off + n * TOP * H * 4].view(torch.float32).view(n, TOP, H)
+        sel = (ids_recv >= 0).view(-1).nonzero().flatten().to(torch.int32)  # (token, slot) order
+        rows = torch.empty((sel.numel(), H), dtype=torch.float32, device=x_recv.device)
+        native.gather_route_rows(self.workspace, n, self.capacity, sel, rows, self.flags)
+        return rows
 
     def combine(self, rows, row_index, weights, ids):
         out = torch.empty((ids.shape[0], H), dtype=torch.bfloat16, device=rows.device)

@@ -55,6 +55,8 @@ SIGNATURES = {
     'ornith_moe_b200_combine': ([C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3, C.c_int),
     'ornith_moe_b200_combine_gathered': ([C.c_void_p, C.c_int] + [C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3,
                                          C.c_int),
+    'ornith_moe_b200_gather_route_rows': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_int]
+                                          + [C.c_void_p] * 3, C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
 }
@@ -263,6 +265,17 @@ def combine_gathered(rows, row_index, weights, ids, out, flags):
     _validate_routes(out, weights, ids)
     check(lib().ornith_moe_b200_combine_gathered(ptr(rows), rows.shape[0], ptr(row_index), ptr(weights), ptr(ids), T,
                                                  ptr(out), ptr(flags), stream(out)), 'combine_gathered')
+
+
+def gather_route_rows(workspace, T, capacity, route_index, rows, flags):
+    """fp32 down projections of the routes route_index (8*token + slot) of the
+    last layer call of T tokens on `workspace`, into rows [n, 2048]."""
+    n = route_index.numel()
+    if (route_index.dtype != torch.int32 or not route_index.is_contiguous() or rows.dtype != torch.float32
+            or rows.shape != (n, 2048) or not rows.is_contiguous()):
+        raise ValueError('gather_route_rows requires INT32 route indices [n] and FP32 rows [n,2048]')
+    check(lib().ornith_moe_b200_gather_route_rows(ptr(workspace), workspace.numel(), T, capacity, ptr(route_index), n,
+                                                  ptr(rows), ptr(flags), stream(rows)), 'gather_route_rows')
 
 
 def repack_n16_to_n32(codes16, meta16, N, K):

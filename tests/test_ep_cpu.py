@@ -74,7 +74,7 @@ def _worker(rank, world, port, T, seed, q):
         epr = E // world
 
         def compute(xr, ir):
-            return fake_rows(xr, ir, rank * epr) if xr.shape[0] else torch.zeros((0, TOP, H))
+            return fake_rows(xr, ir, rank * epr)[ir >= 0] if xr.shape[0] else torch.zeros((0, H))
 
         out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered)
         ref = fake_combine(fake_rows(x, ids, 0).view(T * TOP, H), weights, ids)

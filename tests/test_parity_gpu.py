@@ -396,3 +396,32 @@ def test_combine_gathered_matches_dense_combine(native, S, T):
     native.combine_gathered(dev(rows), dev(bad), wd, idd, out_g, flags)
     torch.cuda.synchronize()
     assert int(flags.item()) & 4
+
+
+@pytest.mark.parametrize('T', [5, 96])
+def test_gather_route_rows_across_paths(native, layer1, bank1, S, T, monkeypatch):
+    """gather_route_rows returns the same per-route rows whichever path ran the
+    layer: route order (decode kernel, multi-kernel path) or expert-slot order
+    (tensor-core path, read through its route -> row map)."""
+    rng = np.random.default_rng(900 + T)
+    x = S.make_tokens(rng, T)
+    w, ids = S.random_routes(rng, T, pad_fraction=0.1)
+    sel = torch.from_numpy(np.flatnonzero(ids.reshape(-1) >= 0).astype(np.int32)).to(DEV)
+
+    def rows_after_layer():
+        ws = torch.empty(native.get_layout(T).workspace_bytes, dtype=torch.uint8, device=DEV)
+        out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+        flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+        native.check(native.lib().ornith_routed_direct_launch(
+            *[native.ptr(t) for t in (dev(x), dev(w), dev(ids), *bank1.routed, ws)], ws.numel(), native.ptr(out),
+            native.ptr(flags), T, T, native.stream(out)), 'layer')
+        rows = torch.empty((sel.numel(), 2048), dtype=torch.float32, device=DEV)
+        native.gather_route_rows(ws, T, T, sel, rows, flags)
+        torch.cuda.synchronize()
+        return rows.cpu().numpy(), int(flags.item())
+
+    fast, f1 = rows_after_layer()
+    monkeypatch.setenv('ORNITH_MOE_B200_PATH', 'generic')
+    multi, f2 = rows_after_layer()
+    assert f1 == f2 == 0
+    np.testing.assert_array_equal(fast.view(np.uint32), multi.view(np.uint32))
