@@ -87,7 +87,7 @@ __device__ __forceinline__ float portable_exp(float x) {
 // q1 is then checked exactly: r1 = g - d*q1 is exact by FMA when q1 is within
 // one ulp, and q1 is the correctly rounded quotient iff |r1| < d*ulp(q1)/2
 // when q1 is not a power of two (both neighbours one ulp away).  *ok is false
-// where that check cannot confirm q1 (powers of two, zero or tiny quotients,
+// where that check cannot confirm q1 (powers of two, tiny non-zero quotients,
 // d >= 2^24, |g| >= 2^64, non-finite operands); the caller then divides with
 // __fdiv_rn.  Checked against __fdiv_rn for every fp32 g with
 // d = 1 + portable_exp(-g).
@@ -104,7 +104,10 @@ __device__ __forceinline__ float div_rn_ge1(float g, float d, bool& ok) {
     const float half_ulp = __uint_as_float((qb & 0x7f800000u) - (24u << 23));
     ok = d < 16777216.f && fabsf(g) < 0x1p64f && fabsf(q1) >= 0x1p-100f && (qb & 0x7fffffu) != 0u &&
          fabsf(r1) < __fmul_rn(d, half_ulp);
-    return q1;
+    // a zero dividend gives itself (its sign kept) for every finite d >= 1
+    const bool zero = g == 0.f && d < 16777216.f;
+    ok = ok || zero;
+    return zero ? g : q1;
 }
 
 // Routed SiLU*up (middle_kernel): (g / (1 + exp(-g))) * up, IEEE division.

@@ -275,33 +275,59 @@ __global__ __launch_bounds__(256) void down_kernel(LayerArgs a) {
 }
 
 // Slot-ordered weighted combine (reduce_slots :176-185, reduce_slots_shared :296-306).
+// One CTA per token, eight columns per thread: every slot's row is read as
+// one contiguous 8 KB burst (two float4 per thread, streamed past L1/L2).
 // BY_POSITION: the rows of route_out are in slot-position order (the
 // tensor-core path) and rowpos maps a route to its row.
 template <bool BY_POSITION>
 __global__ __launch_bounds__(256) void combine_kernel(LayerArgs a) {
-    const size_t index = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int t = blockIdx.x, c = threadIdx.x * 8;
+    const float* route_out = ws_at<float>(a, a.L.route_out);
+    const int32_t* rowpos = BY_POSITION ? ws_at<int32_t>(a, a.L.rowpos) : nullptr;
+    auto row_ptr = [&](int r) {
+        return reinterpret_cast<const float4*>(route_out + size_t(BY_POSITION ? rowpos[r] : r) * kH + c);
+    };
     uint32_t f = 0;
-    if (index < size_t(a.T) * kH) {
-        const int t = int(index / kH), c = int(index % kH);
-        const float* route_out = ws_at<float>(a, a.L.route_out);
-        const int32_t* rowpos = BY_POSITION ? ws_at<int32_t>(a, a.L.rowpos) : nullptr;
-        auto row_of = [&](int r) { return size_t(BY_POSITION ? rowpos[r] : r); };
-        float sum = 0.f;
+    float sum[8];
 #pragma unroll
-        for (int s = 0; s < kTop; ++s) {
-            const int r = t * kTop + s;
-            if (id_valid(a.ids[r])) sum = __fadd_rn(sum, __fmul_rn(route_out[row_of(r) * kH + c], a.weights[r]));
+    for (int j = 0; j < 8; ++j) sum[j] = 0.f;
+#pragma unroll
+    for (int s = 0; s < kTop; ++s) {
+        const int r = t * kTop + s;
+        if (!id_valid(a.ids[r])) continue;
+        const float w = a.weights[r];
+        const float4* src = row_ptr(r);
+        const float4 v0 = __ldcs(src), v1 = __ldcs(src + 1);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sum[j] = __fadd_rn(sum[j], __fmul_rn(v[j], w));
+    }
+    const size_t index = size_t(t) * kH + c;
+    uint32_t packed[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const uint16_t lo = bf16_rne(sum[j]), hi = bf16_rne(sum[j + 1]);
+        if (!isfinite(sum[j]) || (lo & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
+        if (!isfinite(sum[j + 1]) || (hi & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
+        packed[j / 2] = uint32_t(lo) | (uint32_t(hi) << 16);
+    }
+    float4* fin = reinterpret_cast<float4*>(ws_at<float>(a, a.L.final_f32) + index);
+    fin[0] = make_float4(sum[0], sum[1], sum[2], sum[3]);
+    fin[1] = make_float4(sum[4], sum[5], sum[6], sum[7]);
+    *reinterpret_cast<uint4*>(a.out + index) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    if (a.shared) {
+        const float gate = bf16_to_f32(a.sigmoid_table[a.shared_logit[t]]);
+        const float4* src = row_ptr(a.T * kTop + t);
+        const float4 v0 = __ldcs(src), v1 = __ldcs(src + 1);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t sp[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            const float s0 = __fmul_rn(v[j], gate), s1 = __fmul_rn(v[j + 1], gate);
+            if (!isfinite(s0) || !isfinite(s1)) f |= kFlagNonfiniteOutput;
+            sp[j / 2] = uint32_t(bf16_rne(s0)) | (uint32_t(bf16_rne(s1)) << 16);
         }
-        uint16_t result = bf16_rne(sum);
-        ws_at<float>(a, a.L.final_f32)[index] = sum;
-        a.out[index] = result;
-        if (!isfinite(sum) || (result & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
-        if (a.shared) {
-            float gate = bf16_to_f32(a.sigmoid_table[a.shared_logit[t]]);
-            float sh = __fmul_rn(route_out[row_of(a.T * kTop + t) * kH + c], gate);
-            a.shared_out[index] = bf16_rne(sh);
-            if (!isfinite(sh)) f |= kFlagNonfiniteOutput;
-        }
+        *reinterpret_cast<uint4*>(a.shared_out + index) = make_uint4(sp[0], sp[1], sp[2], sp[3]);
     }
     flag_or(a.flags, f);
 }
@@ -345,8 +371,8 @@ cudaError_t launch_quant_tokens(const LayerArgs& a, cudaStream_t stream) {
 
 cudaError_t launch_combine(const LayerArgs& a, cudaStream_t stream, bool by_position) {
     count_launches(1);
-    if (by_position) combine_kernel<true><<<(a.T * kH + 255) / 256, 256, 0, stream>>>(a);
-    else combine_kernel<false><<<(a.T * kH + 255) / 256, 256, 0, stream>>>(a);
+    if (by_position) combine_kernel<true><<<a.T, 256, 0, stream>>>(a);
+    else combine_kernel<false><<<a.T, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -23,12 +23,14 @@
 // M-tile are one contiguous block, so the epilogue's row stores stay inside
 // it instead of scattering over the whole buffer (one TLB reach per tile).
 //
-// mma_kernel roles (20 warps, one CTA per SM, persistent over tiles):
+// mma_kernel roles (24 warps, one CTA per SM, persistent over tiles):
 //   warp 0      producer: cp.async.bulk of the activation half-tile (16 KB),
 //               the packed u4 codes (8 x 2 KB) and per-group metadata;
 //   warp 1      TMEM allocator and single-thread MMA issuer;
-//   warps 2-3   converters: u4 codes -> u8 core matrices in shared memory;
-//   warps 4-19  four epilogue warpgroups (64 TMEM columns each).
+//   warps 2-5   converters: u4 codes -> u8 core matrices in shared memory;
+//   warps 6-7   idle (they complete the second setup warpgroup);
+//   warps 8-23  four epilogue warpgroups (64 TMEM columns each), which take
+//               the registers the setup warpgroups give up (setmaxnreg).
 // K advances in half-groups of 128 through a 3-stage ring.  The int32
 // accumulator of a 256-group is double buffered in TMEM (2 x 256 columns) and
 // pre-filled with the bits of 1.5*2^23, so after the MMAs each cell holds the
@@ -51,9 +53,17 @@ constexpr int kStageBytes = kABytes + kBpBytes + kBuBytes;
 constexpr int kMetaBytes = kNT * 4 + kMT * 4 + kMT * 4;  // B meta, A scale, A sum
 constexpr int kMetaFBytes = kNT * 4 * 2;                   // fp32 column scales then offsets
 constexpr int kMetaSlots = 4;  // metadata ring: the producer runs up to 4 groups ahead of the epilogue
-constexpr int kWarps = 20;
+constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarps = 16;
+constexpr int kEpiFirst = 8;    // epilogue warps 8..23 (warpgroups 2..5)
+constexpr int kConvWarps = 4;   // converter warps 2..5, one per scheduler
+// Register split (setmaxnreg, per warpgroup): the two setup warpgroups drop to
+// kRegsSetup, the four epilogue warpgroups rise to kRegsEpi.  The sum must not
+// exceed what the CTA was launched with (kThreads x kRegsLaunch), which the
+// launcher checks against the compiled count before the first launch.
+constexpr int kRegsSetup = 48, kRegsEpi = 96, kRegsLaunch = 80;
+static_assert(2 * 128 * kRegsSetup + 4 * 128 * kRegsEpi <= kThreads * kRegsLaunch, "register split");
 constexpr uint32_t kMagic = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 constexpr uint64_t kTimeoutNs = 1000000000ull;
@@ -67,7 +77,7 @@ __device__ __forceinline__ uint64_t now_ns() {
 // Per-role timestamps of a few CTAs (clock64), compiled in only with
 // -DORNITH_PREFILL_TRACE; the default build has none.
 #ifdef ORNITH_PREFILL_TRACE
-constexpr int kPTraceCtas = 4, kPTraceKinds = 10, kPTraceLen = 256;
+constexpr int kPTraceCtas = 4, kPTraceKinds = 11, kPTraceLen = 256;
 __device__ unsigned long long g_prefill_trace[2][kPTraceCtas][kPTraceKinds][kPTraceLen];
 #define PREFILL_TRACE(kind, idx)                                                                         \
     ((blockIdx.x % 37 == 0 && blockIdx.x / 37 < kPTraceCtas && (idx) < kPTraceLen)                      \
@@ -233,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&conv[i], 2);
+            mbar_init(&conv[i], kConvWarps);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < kMetaSlots; ++i) {
@@ -265,134 +275,138 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
     // 32-column bank tile feeding B-tile rows 32i..32i+31 of N-tile nt
     auto n32_of = [&](int nt, int i) { return GATE ? (i < 4 ? 4 * nt + i : 16 + 4 * nt + (i - 4)) : 8 * nt + i; };
 
-    if (warp == 0) {
-        // ---------------- producer ----------------
-        if (lane == 0) {
-            int issued = 0, metas = 0;
-            for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
-                const uint32_t *codes, *meta;
-                unit_bank(unit, codes, meta);
-                const int nt = unit % NUPT, tile = unit / NUPT;
-                for (int g = 0; g < KG && !*abort; ++g) {
-                    if (!(metas < kMetaSlots || bwait(&meta_empty[metas % kMetaSlots],
-                                                      uint32_t(metas / kMetaSlots - 1) & 1u, abort, p.flags)))
-                        break;
-                    {
-                        const int mb = metas % kMetaSlots;
-                        uint8_t* m = metabuf + mb * kMetaBytes;
-                        mbar_arrive_expect_tx(&meta_full[mb], kMetaBytes);
-                        for (int i = 0; i < 8; ++i)
-                            bulk_g2s(m + i * 128, meta + (size_t(n32_of(nt, i)) * KG + g) * 32, 128, &meta_full[mb]);
-                        bulk_g2s(m + kNT * 4, p.asa + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
-                        bulk_g2s(m + kNT * 4 + kMT * 4, p.asum + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
-                        PREFILL_TRACE(0, metas);
-                        ++metas;
-                    }
-                    for (int h = 0; h < 2; ++h) {
-                        const int s = issued % kStages;
-                        if (issued >= kStages &&
-                            !bwait(&empty[s], uint32_t(issued / kStages - 1) & 1u, abort, p.flags))
+    if (warp < kEpiFirst) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsSetup));
+        if (warp == 0) {
+            // ---------------- producer ----------------
+            if (lane == 0) {
+                int issued = 0, metas = 0;
+                for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
+                    const uint32_t *codes, *meta;
+                    unit_bank(unit, codes, meta);
+                    const int nt = unit % NUPT, tile = unit / NUPT;
+                    for (int g = 0; g < KG && !*abort; ++g) {
+                        if (!(metas < kMetaSlots || bwait(&meta_empty[metas % kMetaSlots],
+                                                          uint32_t(metas / kMetaSlots - 1) & 1u, abort, p.flags)))
                             break;
-                        uint8_t* sA = stages + size_t(s) * kStageBytes;
-                        uint8_t* sBp = sA + kABytes;
-                        mbar_arrive_expect_tx(&full[s], kABytes + kBpBytes);
-                        bulk_g2s(sA, p.atiles + (size_t(tile) * KG + g) * 32768 + h * kABytes, kABytes, &full[s]);
-                        for (int i = 0; i < 8; ++i)
-                            bulk_g2s(sBp + i * 2048, codes + (size_t(n32_of(nt, i)) * KG + g) * 1024 + h * 512, 2048,
-                                     &full[s]);
-                        PREFILL_TRACE(1, issued);
-                        ++issued;
+                        {
+                            const int mb = metas % kMetaSlots;
+                            uint8_t* m = metabuf + mb * kMetaBytes;
+                            mbar_arrive_expect_tx(&meta_full[mb], kMetaBytes);
+                            for (int i = 0; i < 8; ++i)
+                                bulk_g2s(m + i * 128, meta + (size_t(n32_of(nt, i)) * KG + g) * 32, 128, &meta_full[mb]);
+                            bulk_g2s(m + kNT * 4, p.asa + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
+                            bulk_g2s(m + kNT * 4 + kMT * 4, p.asum + (size_t(tile) * KG + g) * kMT, kMT * 4, &meta_full[mb]);
+                            PREFILL_TRACE(0, metas);
+                            ++metas;
+                        }
+                        for (int h = 0; h < 2; ++h) {
+                            const int s = issued % kStages;
+                            if (issued >= kStages &&
+                                !bwait(&empty[s], uint32_t(issued / kStages - 1) & 1u, abort, p.flags))
+                                break;
+                            uint8_t* sA = stages + size_t(s) * kStageBytes;
+                            uint8_t* sBp = sA + kABytes;
+                            mbar_arrive_expect_tx(&full[s], kABytes + kBpBytes);
+                            bulk_g2s(sA, p.atiles + (size_t(tile) * KG + g) * 32768 + h * kABytes, kABytes, &full[s]);
+                            for (int i = 0; i < 8; ++i)
+                                bulk_g2s(sBp + i * 2048, codes + (size_t(n32_of(nt, i)) * KG + g) * 1024 + h * 512, 2048,
+                                         &full[s]);
+                            PREFILL_TRACE(1, issued);
+                            ++issued;
+                        }
                     }
                 }
+                if (*abort) {
+                    // every issued copy lands before the CTA can leave
+                    for (int k = issued - kStages; k < issued; ++k)
+                        if (k >= 0) drain_wait(&full[k % kStages], uint32_t(k / kStages) & 1u);
+                    for (int k = metas - kMetaSlots; k < metas; ++k)
+                        if (k >= 0) drain_wait(&meta_full[k % kMetaSlots], uint32_t(k / kMetaSlots) & 1u);
+                }
             }
-            if (*abort) {
-                // every issued copy lands before the CTA can leave
-                for (int k = issued - kStages; k < issued; ++k)
-                    if (k >= 0) drain_wait(&full[k % kStages], uint32_t(k / kStages) & 1u);
-                for (int k = metas - kMetaSlots; k < metas; ++k)
-                    if (k >= 0) drain_wait(&meta_full[k % kMetaSlots], uint32_t(k / kMetaSlots) & 1u);
+        } else if (warp == 1) {
+            // ---------------- MMA issuer ----------------
+            if (lane == 0) {
+                int st = 0, gg = 0;
+                bool any = false;
+                for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
+                    for (int g = 0; g < KG && !*abort; ++g, ++gg) {
+                        const int b = gg & 1;
+                        if (!bwait(&acc_empty[b], uint32_t(gg / 2) & 1u, abort, p.flags)) break;
+                        tc_fence_after();
+                        PREFILL_TRACE(4, gg);
+                        const uint32_t d = tmem + uint32_t(b * kNT);
+                        for (int h = 0; h < 2; ++h, ++st) {
+                            const int s = st % kStages;
+                            if (!bwait(&conv[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
+                            tc_fence_after();
+                            PREFILL_TRACE(5, st);
+                            const uint32_t aaddr = smem_addr(stages + size_t(s) * kStageBytes);
+                            const uint32_t baddr = aaddr + kABytes + kBpBytes;
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+                                mma_i8(d, smem_desc(aaddr + kk * 2 * 2048, 2048, 128),
+                                       smem_desc(baddr + kk * 2 * 4096, 4096, 128), 1u);
+                            mma_commit(&empty[s]);
+                            any = true;
+                        }
+                        mma_commit(&acc_full[b]);
+                    }
+                }
+                if (any) {
+                    // every MMA issued has finished reading shared memory before the CTA leaves
+                    mma_commit(drain);
+                    drain_wait(drain, 0);
+                }
             }
-        }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            int st = 0, gg = 0;
-            bool any = false;
+        } else if (warp < 2 + kConvWarps) {
+            // ---------------- converters ----------------
+            const int cw = warp - 2;  // converter warp 0..3
+            int st = 0;
             for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
-                for (int g = 0; g < KG && !*abort; ++g, ++gg) {
-                    const int b = gg & 1;
-                    if (!bwait(&acc_empty[b], uint32_t(gg / 2) & 1u, abort, p.flags)) break;
-                    tc_fence_after();
-                    PREFILL_TRACE(4, gg);
-                    const uint32_t d = tmem + uint32_t(b * kNT);
+                for (int g = 0; g < KG && !*abort; ++g) {
                     for (int h = 0; h < 2; ++h, ++st) {
                         const int s = st % kStages;
-                        if (!bwait(&conv[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
-                        tc_fence_after();
-                        PREFILL_TRACE(5, st);
-                        const uint32_t aaddr = smem_addr(stages + size_t(s) * kStageBytes);
-                        const uint32_t baddr = aaddr + kABytes + kBpBytes;
+                        if (!bwait(&full[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
+                        if (warp == 2 && lane == 0) PREFILL_TRACE(2, st);
+                        // Work item (i, q, c): 32-column tile i (8), word pair q (8),
+                        // column c = lane; converter warp cw takes the pairs
+                        // q = cw + 4*qq.  Packed word j of column c of tile i is
+                        // bp[512 i + 32 j + c]; column n = 32 i + c of the K-major
+                        // core-matrix layout takes pair q at byte
+                        // 4096 q + 128 (n >> 3) + 16 (n & 7).  Every offset below
+                        // is a compile-time constant from two per-thread bases.
+                        const uint32_t* bp = reinterpret_cast<const uint32_t*>(stages + size_t(s) * kStageBytes + kABytes) +
+                                             lane + 64 * cw;
+                        uint8_t* bu = stages + size_t(s) * kStageBytes + kABytes + kBpBytes + cw * 4096 + (lane >> 3) * 128 +
+                                      (lane & 7) * 16;
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)
-                            mma_i8(d, smem_desc(aaddr + kk * 2 * 2048, 2048, 128),
-                                   smem_desc(baddr + kk * 2 * 4096, 4096, 128), 1u);
-                        mma_commit(&empty[s]);
-                        any = true;
-                    }
-                    mma_commit(&acc_full[b]);
-                }
-            }
-            if (any) {
-                // every MMA issued has finished reading shared memory before the CTA leaves
-                mma_commit(drain);
-                drain_wait(drain, 0);
-            }
-        }
-    } else if (warp < 4) {
-        // ---------------- converters ----------------
-        const int cw = warp - 2;  // converter warp 0..1
-        int st = 0;
-        for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
-            for (int g = 0; g < KG && !*abort; ++g) {
-                for (int h = 0; h < 2; ++h, ++st) {
-                    const int s = st % kStages;
-                    if (!bwait(&full[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
-                    if (warp == 2 && lane == 0) PREFILL_TRACE(2, st);
-                    // Work item (i, q, c): 32-column tile i (8), word pair q (8),
-                    // column c = lane; converter warp cw takes the pairs
-                    // q = cw + 2*qq.  Packed word j of column c of tile i is
-                    // bp[512 i + 32 j + c]; column n = 32 i + c of the K-major
-                    // core-matrix layout takes pair q at byte
-                    // 4096 q + 128 (n >> 3) + 16 (n & 7).  Every offset below
-                    // is a compile-time constant from two per-thread bases.
-                    const uint32_t* bp = reinterpret_cast<const uint32_t*>(stages + size_t(s) * kStageBytes + kABytes) +
-                                         lane + 64 * cw;
-                    uint8_t* bu = stages + size_t(s) * kStageBytes + kABytes + kBpBytes + cw * 4096 + (lane >> 3) * 128 +
-                                  (lane & 7) * 16;
+                        for (int i = 0; i < 8; ++i) {
+                            uint32_t w[4];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        uint32_t w[8];
+                            for (int qq = 0; qq < 2; ++qq) {
+                                w[2 * qq] = bp[i * 512 + qq * 256];
+                                w[2 * qq + 1] = bp[i * 512 + qq * 256 + 32];
+                            }
 #pragma unroll
-                        for (int qq = 0; qq < 4; ++qq) {
-                            w[2 * qq] = bp[i * 512 + qq * 128];
-                            w[2 * qq + 1] = bp[i * 512 + qq * 128 + 32];
+                            for (int qq = 0; qq < 2; ++qq)
+                                *reinterpret_cast<uint4*>(bu + qq * 16384 + i * 512) =
+                                    make_uint4(w[2 * qq] & 0x0f0f0f0fu, (w[2 * qq] >> 4) & 0x0f0f0f0fu,
+                                               w[2 * qq + 1] & 0x0f0f0f0fu, (w[2 * qq + 1] >> 4) & 0x0f0f0f0fu);
                         }
-#pragma unroll
-                        for (int qq = 0; qq < 4; ++qq)
-                            *reinterpret_cast<uint4*>(bu + qq * 8192 + i * 512) =
-                                make_uint4(w[2 * qq] & 0x0f0f0f0fu, (w[2 * qq] >> 4) & 0x0f0f0f0fu,
-                                           w[2 * qq + 1] & 0x0f0f0f0fu, (w[2 * qq + 1] >> 4) & 0x0f0f0f0fu);
+                        fence_proxy_async();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&conv[s]);
+                        if (warp == 2 && lane == 0) PREFILL_TRACE(3, st);
                     }
-                    fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&conv[s]);
-                    if (warp == 2 && lane == 0) PREFILL_TRACE(3, st);
                 }
             }
         }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpi));
         // ---------------- epilogue ----------------
-        const int ew = warp - 4;                 // 0..15
+        const int ew = warp - kEpiFirst;         // 0..15
         const int wg = ew >> 2;                  // column quarter
         const int row = 32 * (warp & 3) + lane;  // TMEM lane = tile row
         const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
@@ -416,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
         uint32_t f = 0;
         int gg = 0;
         int un = 0;  // units done (trace index)
-        const int et = tid - 128;  // 0..511 within the epilogue warps
+        const int et = tid - kEpiFirst * 32;  // 0..511 within the epilogue warps
         // Every exit from these loops is a collective decision (named_and), so the
         // 16 warps always pass the same sequence of barrier 1.
         for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
@@ -515,15 +529,19 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                     // confirm are redone with __fdiv_rn
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
-                        float d[8], q[8], v[8];
+                        // rows past the tile's end hold stale sums: they take
+                        // g = 1 so that they never reach the slow division
+                        float gs[8], d[8], q[8], v[8];
                         bool ok[8];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) d[j] = __fadd_rn(1.f, portable_exp(-acc[i + j]));
+                        for (int j = 0; j < 8; ++j) gs[j] = valid ? acc[i + j] : 1.f;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) q[j] = div_rn_ge1(acc[i + j], d[j], ok[j]);
+                        for (int j = 0; j < 8; ++j) d[j] = __fadd_rn(1.f, portable_exp(-gs[j]));
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) q[j] = div_rn_ge1(gs[j], d[j], ok[j]);
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
-                            if (!ok[j]) q[j] = __fdiv_rn(acc[i + j], d[j]);
+                            if (!ok[j]) q[j] = __fdiv_rn(gs[j], d[j]);
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const float gv = acc[i + j], uv = acc[32 + i + j];
@@ -565,6 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 }
             }
             if (ew == 0 && lane == 0) PREFILL_TRACE(9, 5 + 4 * un);
+            if (lane == 0) PREFILL_TRACE(10, 16 * un + ew);
             ++un;
         }
         if (ew == 0 && lane == 0) PREFILL_TRACE(9, 1);
@@ -693,87 +712,116 @@ __global__ __launch_bounds__(256) void prefill_place_kernel(LayerArgs a, int nbl
     }
 }
 
-// Tile and row of a route position inside an activation tile set.
-__device__ __forceinline__ void tile_row(const LayerArgs& a, int slot, int pos, int& tile, int& row) {
-    const int m = pos - ws_at<int32_t>(a, a.L.offsets)[slot];
-    tile = ws_at<int32_t>(a, a.L.slot_tiles)[slot] + m / kMT;
-    row = m % kMT;
+// Shared-memory image of one 32 KB activation tile group: the K-major
+// core-matrix layout [chunk 16][row 128][16 bytes] with the row rotated by
+// the chunk, so that the 16 chunks of one row (written together) and
+// consecutive rows of one chunk (read together) both spread over all banks.
+__device__ __forceinline__ uint32_t tile_slot(int chunk, int row) {
+    return uint32_t(chunk) * 2048u + uint32_t((row + chunk) & (kMT - 1)) * 16u;
 }
-// Byte offset of lane l's 8 activation bytes (K-chunk l/2, half l&1) of `row`
-// inside one 256-group of a tile: [chunk 16][row/8 16][row%8 8][16 bytes].
-__device__ __forceinline__ size_t core_offset(int row, int lane) {
-    return size_t(lane >> 1) * 2048 + (row >> 3) * 128 + (row & 7) * 16 + (lane & 1) * 8;
+// Copies the shared-memory tile image to its global tile in whole lines.
+__device__ __forceinline__ void store_tile(const uint8_t* img, uint8_t* dst) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int idx = k * 256 + threadIdx.x;  // chunk * 128 + row
+        reinterpret_cast<uint4*>(dst)[idx] = *reinterpret_cast<const uint4*>(img + tile_slot(idx >> 7, idx & 127));
+    }
 }
 
 // Gate activation tiles from the quantised tokens (xq, xs, xsum, written once
 // per token by the token quantisation kernel): one CTA per (M-tile, 256-group)
-// copies the 128 rows' 256 bytes into the tile's K-major core-matrix layout
-// [chunk 16][row 128][16 bytes].  Thread = (row, chunk pair): its loads read
-// 16 bytes of one token row (L2-resident), its stores are contiguous across
-// the warp, so the 32 KB tile is written in whole lines.
+// reads its 128 token rows whole (16 threads x 16 bytes per row), rearranges
+// them in shared memory and writes the 32 KB tile in whole lines.  Rows past
+// the tile's end are zero.
 __global__ __launch_bounds__(256) void pack_gather_kernel(LayerArgs a) {
+    __shared__ __align__(16) uint8_t img[32768];
     const int tile = blockIdx.x >> 3, g = blockIdx.x & 7;
     if (tile >= *ws_at<int32_t>(a, a.L.n_mtiles)) return;
     const int4 mt = ws_at<int4>(a, a.L.mtiles)[tile];
-    const int row = threadIdx.x & 127;
-    if (row >= mt.z) return;
     const int R = a.T * kTop;
-    const int route = ws_at<int32_t>(a, a.L.routes)[mt.y + row];
-    const int t = route >= R ? route - R : route / kTop;
-    const uint4* src = reinterpret_cast<const uint4*>(ws_at<uint8_t>(a, a.L.xq) + size_t(t) * kH + g * kG);
-    uint4* dst = reinterpret_cast<uint4*>(ws_at<uint8_t>(a, a.L.agate) + (size_t(tile) * 8 + g) * 32768) + row;
+    const int32_t* routes = ws_at<int32_t>(a, a.L.routes) + mt.y;
+    const uint8_t* xq = ws_at<uint8_t>(a, a.L.xq) + g * kG;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const int chunk = (threadIdx.x >> 7) + 2 * k;
-        dst[chunk * kMT] = __ldcg(src + chunk);
+        const int idx = k * 256 + threadIdx.x;  // row * 16 + chunk
+        const int row = idx >> 4, chunk = idx & 15;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row < mt.z) {
+            const int route = routes[row];
+            const int t = route >= R ? route - R : route / kTop;
+            v = __ldcg(reinterpret_cast<const uint4*>(xq + size_t(t) * kH) + chunk);
+        }
+        *reinterpret_cast<uint4*>(img + tile_slot(chunk, row)) = v;
     }
     if (threadIdx.x < kMT) {
-        ws_at<float>(a, a.L.agate_sa)[(size_t(tile) * 8 + g) * kMT + row] =
-            __half2float(ws_at<__half>(a, a.L.xs)[t * (kH / kG) + g]);
-        ws_at<int32_t>(a, a.L.agate_sum)[(size_t(tile) * 8 + g) * kMT + row] =
-            ws_at<int32_t>(a, a.L.xsum)[t * (kH / kG) + g];
+        const int row = threadIdx.x;
+        float sa = 0.f;
+        int32_t sum = 0;
+        if (row < mt.z) {
+            const int route = routes[row];
+            const int t = route >= R ? route - R : route / kTop;
+            sa = __half2float(ws_at<__half>(a, a.L.xs)[t * (kH / kG) + g]);
+            sum = ws_at<int32_t>(a, a.L.xsum)[t * (kH / kG) + g];
+        }
+        ws_at<float>(a, a.L.agate_sa)[(size_t(tile) * 8 + g) * kMT + row] = sa;
+        ws_at<int32_t>(a, a.L.agate_sum)[(size_t(tile) * 8 + g) * kMT + row] = sum;
     }
+    __syncthreads();
+    store_tile(img, ws_at<uint8_t>(a, a.L.agate) + (size_t(tile) * 8 + g) * 32768);
 }
 
-// Middle Hadamard + quantise into the down activation tiles: one warp per
-// (position, 256-group) of the route list.
+// Middle Hadamard + quantise into the down activation tiles: one CTA per
+// eight consecutive rows of an (M-tile, 256-group), one warp per row (read
+// whole from the slot-ordered middle buffer).  The eight quantised rows meet
+// in shared memory and leave as 16 whole 128-byte lines (one per K-chunk).
+// Rows past the tile's end are zero.
 template <int QMAX>
 __global__ __launch_bounds__(256) void pack_middle_kernel(LayerArgs a) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int total = ws_at<int32_t>(a, a.L.offsets)[kE + 1];
-    if (warp >= total * 2) return;
-    const int pos = warp >> 1, g = warp & 1;
-    const int route = ws_at<int32_t>(a, a.L.routes)[pos];
-    const int R = a.T * kTop;
-    const int slot = route >= R ? kE : a.ids[route];
-    const float4* src =
-        reinterpret_cast<const float4*>(ws_at<float>(a, a.L.middle) + size_t(pos) * kI + g * kG + lane * 8);
-    const float4 v0 = src[0], v1 = src[1];
-    float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    uint32_t f = 0;
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
-    wht128_halfwarp(e, lane);
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-        if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
-    int tile, row;
-    tile_row(a, slot, pos, tile, row);
+    __shared__ __align__(16) uint2 img[16][8][2];  // [chunk][row][half]
     __shared__ uint2 qbuf[8][32];
     __shared__ __half sbuf[8];
     __shared__ int32_t mbuf[8];
-    const int wl = threadIdx.x >> 5;
-    quantize_group_warp<QMAX>(e, lane, qbuf[wl], &sbuf[wl], &mbuf[wl], f);
-    __syncwarp();
-    *reinterpret_cast<uint2*>(ws_at<uint8_t>(a, a.L.adown) + (size_t(tile) * 2 + g) * 32768 + core_offset(row, lane)) =
-        qbuf[wl][lane];
-    if (lane == 0) {
-        ws_at<float>(a, a.L.adown_sa)[(size_t(tile) * 2 + g) * kMT + row] = __half2float(sbuf[wl]);
-        ws_at<int32_t>(a, a.L.adown_sum)[(size_t(tile) * 2 + g) * kMT + row] = mbuf[wl];
+    const int tile = blockIdx.x >> 5, g = (blockIdx.x >> 4) & 1, r0 = (blockIdx.x & 15) * 8;
+    if (tile >= *ws_at<int32_t>(a, a.L.n_mtiles)) return;
+    const int4 mt = ws_at<int4>(a, a.L.mtiles)[tile];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = r0 + warp;
+    float* tsa = ws_at<float>(a, a.L.adown_sa) + (size_t(tile) * 2 + g) * kMT;
+    int32_t* tsum = ws_at<int32_t>(a, a.L.adown_sum) + (size_t(tile) * 2 + g) * kMT;
+    uint32_t f = 0;
+    if (row < mt.z) {
+        const float4* src =
+            reinterpret_cast<const float4*>(ws_at<float>(a, a.L.middle) + size_t(mt.y + row) * kI + g * kG + lane * 8);
+        const float4 v0 = __ldcs(src), v1 = __ldcs(src + 1);
+        float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+            if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
+        wht128_halfwarp(e, lane);
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+            if (!isfinite(e[s])) f |= kFlagNonfiniteInput;
+        quantize_group_warp<QMAX>(e, lane, qbuf[warp], &sbuf[warp], &mbuf[warp], f);
+        __syncwarp();
+        img[lane >> 1][warp][lane & 1] = qbuf[warp][lane];
+        if (lane == 0) {
+            tsa[row] = __half2float(sbuf[warp]);
+            tsum[row] = mbuf[warp];
+        }
+    } else {
+        img[lane >> 1][warp][lane & 1] = make_uint2(0u, 0u);
+        if (lane == 0) {
+            tsa[row] = 0.f;
+            tsum[row] = 0;
+        }
     }
     f = __reduce_or_sync(0xffffffffu, f);
     if (f && lane == 0) atomicOr(a.flags, f);
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const int chunk = threadIdx.x >> 3, ri = threadIdx.x & 7;
+        uint8_t* dst = ws_at<uint8_t>(a, a.L.adown) + (size_t(tile) * 2 + g) * 32768 + chunk * 2048 + (r0 + ri) * 16;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(&img[chunk][ri][0]);
+    }
 }
 
 constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + kMetaSlots * kMetaBytes + 2 * kMetaFBytes + 64 * 8 + 64;
@@ -808,6 +856,13 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
             return st;
         if ((st = cudaFuncSetAttribute(down, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kMmaSmem))) != cudaSuccess)
             return st;
+        // setmaxnreg.inc waits for registers the CTA does not have if the
+        // kernel was compiled with fewer launch registers than the split assumes
+        for (const void* k : {reinterpret_cast<const void*>(gate), reinterpret_cast<const void*>(down)}) {
+            cudaFuncAttributes fa;
+            if ((st = cudaFuncGetAttributes(&fa, k)) != cudaSuccess) return st;
+            if (fa.numRegs < kRegsLaunch || fa.maxThreadsPerBlock < kThreads) return cudaErrorInvalidConfiguration;
+        }
         ds.attr = true;
     }
     const int T = a.T, R = T * kTop, rows = R + (a.shared ? T : 0);
@@ -837,9 +892,8 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     g.flags = a.flags;
     gate<<<min(ds.sms, max_tiles * 4), kThreads, kMmaSmem, stream>>>(g);
     if ((st = cudaGetLastError()) != cudaSuccess) return st;
-    const int mid_warps = rows * 2;
-    if (a.a8) pack_middle_kernel<127><<<(mid_warps + 7) / 8, 256, 0, stream>>>(a);
-    else pack_middle_kernel<7><<<(mid_warps + 7) / 8, 256, 0, stream>>>(a);
+    if (a.a8) pack_middle_kernel<127><<<max_tiles * 32, 256, 0, stream>>>(a);
+    else pack_middle_kernel<7><<<max_tiles * 32, 256, 0, stream>>>(a);
     if ((st = cudaGetLastError()) != cudaSuccess) return st;
     MmaArgs d = g;
     d.atiles = ws_at<uint8_t>(a, a.L.adown);
