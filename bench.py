@@ -59,9 +59,9 @@ CONFIGS = {
     'prefill1120': dict(T=1120, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 1120 (configs[3])'),
     'prefill8192': dict(T=8192, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 8192 (configs[3])'),
     # expert-parallel sweep: total tokens fixed, experts sharded over the ranks
-    'ep_decode256': dict(T=256, layers=40, bias=0.0, act_bits=8, shared=False, ep=True,
+    'ep_decode256': dict(T=256, layers=40, bias=0.0, act_bits=8, shared=False, ep=True, exchange='fixed',
                          name='expert-parallel decode B=256, 40 layers, Zipf(1.2) expert skew (configs[4])'),
-    'ep_prefill8192': dict(T=8192, layers=4, bias=0.0, act_bits=4, shared=False, ep=True,
+    'ep_prefill8192': dict(T=8192, layers=4, bias=0.0, act_bits=4, shared=False, ep=True, exchange='compact',
                            name='expert-parallel prefill 8192 tokens, Zipf(1.2) expert skew (configs[4]); '
                                 '4 weight sets cycled'),
 }
@@ -198,7 +198,7 @@ def run_ep(args):
         g = device_bank(torch, gen, dev, epr, 1024, 2048)
         d = device_bank(torch, gen, dev, epr, 2048, 512)
         layers.append(ep.ExpertParallelMoE(None, world, (g[0], g[1], d[0], d[1]), capacity=min(T * world, 8192),
-                                           act_bits=bits))
+                                           act_bits=bits, exchange=cfg['exchange']))
     bias = torch.from_numpy(S.zipf_bias(np.random.default_rng(12), 256, 1.2)).to(dev)  # same on every rank
     logits = torch.randn((L, T, 256), device=dev, generator=gen) + bias
     x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
@@ -235,7 +235,9 @@ def run_ep(args):
         'data': 'synthetic (seeded random-init weights and logits of the configured shapes)',
         'config': {'workload': cfg['name'], 'tokens_per_step': T_total, 'tokens_per_rank': T, 'layers': L,
                    'experts_per_rank': epr, 'parallelism': f'ep{world}',
-                   'exchange': 'NCCL all_to_all_single dispatch + fp32 per-slot return'},
+                   'exchange': ('NCCL all_gather of token rows + equal-block all_to_all of fp32 per-slot rows '
+                                '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
+                                'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)')},
         'flags': int(flags.item()), 'clocks': clk.summary(),
     }
     dist.barrier()

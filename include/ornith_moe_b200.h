@@ -184,6 +184,14 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_gather_route_rows(
     const void* workspace, size_t bytes, int T, int Tcap, const void* route_index_i32, int n, void* rows_f32,
     void* flags_u32, cudaStream_t stream);
 
+/* Route-ordered copy of the same projections: rows fp32 [8T][2048] receives
+ * row r for every route r with a valid id of the last layer call of T tokens
+ * on the workspace; rows of padding slots hold unspecified values.  Used by the
+ * expert-parallel exchange with fixed-size blocks; no counterpart in the
+ * reference. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_scatter_route_rows(
+    const void* workspace, size_t bytes, int T, int Tcap, void* rows_f32, cudaStream_t stream);
+
 /* Workspace size for ornith_moe_b200_launch_from_logits (0 <= Tcap <= 8192). */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes);
 

@@ -101,6 +101,23 @@ __global__ __launch_bounds__(256) void gather_route_rows_kernel(const float* rou
     d[1] = __ldcs(src + 1);
 }
 
+// Route-ordered copy of route_out: CTA p copies the row at position p (the
+// route routes[p] on the tensor-core path, route p otherwise) to rows[route].
+__global__ __launch_bounds__(256) void scatter_route_rows_kernel(const float* route_out, const int32_t* routes,
+                                                                 const int32_t* n_positions, int R, float* dst) {
+    const int p = blockIdx.x;
+    int r = p;
+    if (routes) {
+        if (p >= *n_positions) return;
+        r = routes[p];
+    }
+    if (r < 0 || r >= R) return;  // the shared expert's rows
+    const float4* src = reinterpret_cast<const float4*>(route_out + size_t(p) * kH) + threadIdx.x * 2;
+    float4* d = reinterpret_cast<float4*>(dst + size_t(r) * kH) + threadIdx.x * 2;
+    d[0] = __ldcs(src);
+    d[1] = __ldcs(src + 1);
+}
+
 // N16 -> N32 bank repack (method.py:142-147).  One thread per destination word.
 __global__ void repack_codes_kernel(const uint32_t* src, uint32_t* dst, int E, int N, int groups) {
     const size_t total = size_t(E) * (N / 32) * groups * 32 * 32;
@@ -375,6 +392,25 @@ cudaError_t ornith_moe_b200_gather_route_rows(const void* workspace, size_t byte
                                                     static_cast<const int32_t*>(route_index_i32), T * kTop,
                                                     T * (kTop + 1), static_cast<float*>(rows_f32),
                                                     static_cast<uint32_t*>(flags));
+    return cudaGetLastError();
+}
+
+cudaError_t ornith_moe_b200_scatter_route_rows(const void* workspace, size_t bytes, int T, int Tcap, void* rows_f32,
+                                              cudaStream_t stream) {
+    if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap) return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes) return cudaErrorInvalidValue;
+    if (!T) return cudaSuccess;
+    if (!workspace || !rows_f32 || !aligned(workspace, 256) || !aligned(rows_f32, 16)) return cudaErrorInvalidValue;
+    const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+    const bool by_position = rows_by_position(T);
+    count_launches(1);
+    // positions: routed rows first, the shared expert's rows (if any) last
+    scatter_route_rows_kernel<<<T * (kTop + (by_position ? 1 : 0)), 256, 0, stream>>>(
+        reinterpret_cast<const float*>(ws + w.route_out),
+        by_position ? reinterpret_cast<const int32_t*>(ws + w.routes) : nullptr,
+        by_position ? reinterpret_cast<const int32_t*>(ws + w.offsets) + kE + 1 : nullptr, T * kTop,
+        static_cast<float*>(rows_f32));
     return cudaGetLastError();
 }
 

@@ -3,21 +3,30 @@
 The reference runs one rank and refuses EP (plugin-site/ornith_g256/moe_base.py:34-39);
 this module adds it.  Rank r of n owns routed experts
 [r*256/n, (r+1)*256/n); the shared expert is replicated and runs on each rank
-for its own tokens.  One layer call on every rank, for the rank's own tokens:
+for its own tokens.  One layer call on every rank, for the rank's own tokens,
+in one of two exchange modes.
 
-  1. route: top-8 ids and weights of the local tokens;
-  2. dispatch plan: for every destination rank d, the local tokens with at
+compact (any batch; ranks may hold different token counts):
+  1. dispatch plan: for every destination rank d, the local tokens with at
      least one expert on d (deduplicated per (token, rank)), with their eight
      ids rewritten to d's local expert numbers (-1 for slots owned elsewhere);
-  3. exchange: counts, then token rows (bf16 pairs carried as int32) and local
-     ids (all_to_all_single; NCCL on GPUs, gloo on CPU);
-  4. expert compute on the received rows with the local banks; the fp32
+  2. exchange: counts, then token rows (bf16 pairs carried as int32) and local
+     ids (all_to_all_single with variable splits; NCCL on GPUs, gloo on CPU);
+  3. expert compute on the received rows with the local banks; the fp32
      down projections of the valid slots are gathered in (token, slot) order;
-  5. return exchange of those rows, one per (token, slot) owned by d;
-  6. home combine: slot-ordered weighted sum into bf16 with the same
-     arithmetic as the single-GPU layer, so the result is bit-identical to it;
-     it reads the returned rows where they arrived, through a (token, slot)
-     -> row index, instead of scattering them into a dense [8T, 2048] buffer.
+  4. return exchange of those rows, one per (token, slot) owned by d;
+  5. home combine: slot-ordered weighted sum into bf16 with the same
+     arithmetic as the single-GPU layer, so the result is bit-identical to it.
+     It reads the returned rows where they arrived, through a (token, slot)
+     -> row index built on the device.
+
+fixed (small batches, the same token count on every rank): no counts and no
+host synchronisation.  Every rank gathers every rank's token rows
+(all_gather) and receives, per source rank, the eight ids of each of its
+tokens in local numbering (-1 where another rank owns the slot).  The expert
+compute returns the route-ordered [T, 8, 2048] block of each source rank,
+padding slots included, and one all_to_all of equal blocks brings them home;
+the row index of slot s of token t is (owner * T + t) * 8 + s.
 
 These collectives are the layer's only exchange.  Every rank takes the same
 collective steps in the same order, zero-sized messages included.
@@ -33,26 +42,31 @@ E, TOP, H = 256, 8, 2048
 @dataclass
 class DispatchPlan:
     send_counts: list          # tokens sent to each rank
+    home_counts: list          # (token, slot) rows each rank sends back
     token_index: torch.Tensor  # [sum(send_counts)] local token of each sent row, grouped by rank
     local_ids: torch.Tensor    # [sum(send_counts), 8] ids in the destination's numbering, -1 elsewhere
     slot_mask: torch.Tensor    # [sum(send_counts), 8] True where the slot is owned by the destination
 
 
-def build_dispatch(ids, world, experts_per_rank=None):
-    """Group each token's slots by owning rank (pure tensor logic, any device)."""
+def owners(ids, world, experts_per_rank=None):
     epr = experts_per_rank or E // world
-    owner = torch.where(ids >= 0, torch.div(ids, epr, rounding_mode='floor'), torch.full_like(ids, -1))
-    counts, tokens, lids, masks = [], [], [], []
-    for d in range(world):
-        m = owner == d
-        tok = m.any(dim=1).nonzero().flatten()
-        mk = m[tok]
-        lid = torch.where(mk, ids[tok] - d * epr, torch.full_like(ids[tok], -1))
-        counts.append(int(tok.numel()))
-        tokens.append(tok)
-        lids.append(lid)
-        masks.append(mk)
-    return DispatchPlan(counts, torch.cat(tokens), torch.cat(lids).to(torch.int32).contiguous(), torch.cat(masks))
+    return torch.where(ids >= 0, torch.div(ids, epr, rounding_mode='floor'), torch.full_like(ids, -1)), epr
+
+
+def build_dispatch(ids, world, experts_per_rank=None):
+    """Group each token's slots by owning rank (pure tensor logic, any device;
+    one host synchronisation for the split sizes)."""
+    owner, epr = owners(ids, world, experts_per_rank)
+    dest = torch.arange(world, device=ids.device).view(-1, 1, 1)
+    mask = owner.unsqueeze(0) == dest                      # [world, T, 8]
+    sent = mask.any(dim=2).nonzero()                       # (d, t), grouped by d, t ascending
+    d, tok = sent[:, 0], sent[:, 1]
+    slot_mask = mask[d, tok]
+    local = torch.where(slot_mask, ids[tok] - (d * epr).unsqueeze(1), torch.full_like(slot_mask, -1, dtype=ids.dtype))
+    counts = torch.stack([torch.bincount(d, minlength=world),
+                          torch.zeros(world, dtype=torch.int64, device=ids.device).index_add_(
+                              0, d, slot_mask.sum(dim=1))]).tolist()
+    return DispatchPlan(counts[0], counts[1], tok, local.to(torch.int32).contiguous(), slot_mask)
 
 
 def _a2a(group, out, inp, out_splits, in_splits):
@@ -75,31 +89,41 @@ def exchange_rows(group, world, plan, x):
     return x_recv.view(x.dtype), ids_recv, recv_counts
 
 
-def return_rows(group, world, plan, ids_recv, recv_counts, out_rows):
+def valid_counts(ids_recv, recv_counts):
+    """(token, slot) rows with a valid local id, per source rank (host ints)."""
+    src = torch.repeat_interleave(torch.arange(len(recv_counts), device=ids_recv.device),
+                                  torch.tensor(recv_counts, device=ids_recv.device), output_size=ids_recv.shape[0])
+    per = torch.zeros(len(recv_counts), dtype=torch.int64, device=ids_recv.device)
+    return per.index_add_(0, src, (ids_recv >= 0).sum(dim=1)).tolist()
+
+
+def return_rows(group, world, plan, back_counts, out_rows):
     """Send every (token, slot) row computed here back to the token's home rank.
 
     out_rows: fp32 [n_valid, 2048], one row per received slot with a valid
-    local id, in (token, slot) order.  Returns the home-side fp32 rows
-    [n_sent_slots, 2048] in the order of plan.slot_mask."""
-    valid = ids_recv >= 0
-    back_counts = [int(v.sum()) for v in torch.split(valid.sum(dim=1), recv_counts)]
-    home_counts = [int(m.sum()) for m in torch.split(plan.slot_mask, plan.send_counts)]
-    got = torch.empty((sum(home_counts), H), dtype=torch.float32, device=out_rows.device)
-    _a2a(group, got, out_rows, home_counts, back_counts)
+    local id, in (token, slot) order; back_counts: those rows per source rank.
+    Returns the home-side fp32 rows [n_sent_slots, 2048] in the order of
+    plan.slot_mask."""
+    got = torch.empty((sum(plan.home_counts), H), dtype=torch.float32, device=out_rows.device)
+    _a2a(group, got, out_rows, plan.home_counts, back_counts)
     return got
 
 
 def route_row_index(T, plan, device):
     """int32 [T, 8]: the row of `got` (return_rows) holding slot s of token t,
-    -1 for slots no rank returned (padding ids)."""
+    -1 for slots no rank returned (padding ids).  No host synchronisation:
+    rows arrive in slot_mask order, so the row of a masked entry is the count
+    of masked entries before it; each slot has one owner, so the per-token
+    maximum over destinations picks it."""
+    flat = plan.slot_mask.reshape(-1).to(torch.int32)
+    dense = torch.where(plan.slot_mask, (torch.cumsum(flat, 0, dtype=torch.int32) - 1).view_as(plan.slot_mask),
+                        torch.full_like(plan.slot_mask, -1, dtype=torch.int32))
     idx = torch.full((T, TOP), -1, dtype=torch.int32, device=device)
-    k, s = plan.slot_mask.nonzero(as_tuple=True)  # the order of return_rows
-    idx[plan.token_index[k], s] = torch.arange(k.numel(), dtype=torch.int32, device=device)
-    return idx
+    return idx.scatter_reduce_(0, plan.token_index.view(-1, 1).expand(-1, TOP), dense, 'amax')
 
 
 def ep_layer(group, world, x, ids, weights, compute, combine):
-    """One expert-parallel layer call.
+    """One expert-parallel layer call, compact exchange.
 
     compute(x_recv, ids_recv) -> fp32 [n_valid, 2048]: the rows of the received
     slots with a valid id, in (token, slot) order; combine(rows [n, 2048],
@@ -107,9 +131,33 @@ def ep_layer(group, world, x, ids, weights, compute, combine):
     host logic also runs on CPU ranks."""
     plan = build_dispatch(ids, world)
     x_recv, ids_recv, recv_counts = exchange_rows(group, world, plan, x)
+    back_counts = valid_counts(ids_recv, recv_counts)
     out_rows = compute(x_recv, ids_recv)
-    got = return_rows(group, world, plan, ids_recv, recv_counts, out_rows)
+    got = return_rows(group, world, plan, back_counts, out_rows)
     return combine(got, route_row_index(x.shape[0], plan, got.device), weights, ids)
+
+
+def ep_layer_fixed(group, world, x, ids, weights, compute_block, combine):
+    """One expert-parallel layer call, fixed-size exchange (same T on every rank).
+
+    compute_block(x_all [world*T, 2048], ids_all [world*T, 8]) -> fp32
+    [world*T, 8, 2048], route-ordered (padding slots unspecified)."""
+    T = x.shape[0]
+    owner, epr = owners(ids, world)
+    dest = torch.arange(world, device=ids.device).view(-1, 1, 1)
+    local = torch.where(owner.unsqueeze(0) == dest, ids.unsqueeze(0) - dest * epr,
+                        torch.full_like(owner.unsqueeze(0), -1)).to(torch.int32).contiguous()   # [world, T, 8]
+    x_all = torch.empty((world * T, H // 2), dtype=torch.int32, device=x.device)
+    dist.all_gather_into_tensor(x_all, x.contiguous().view(torch.int32), group=group)
+    ids_all = torch.empty_like(local)
+    dist.all_to_all_single(ids_all, local, group=group)
+    rows = compute_block(x_all.view(x.dtype), ids_all.view(world * T, TOP))
+    got = torch.empty_like(rows)
+    dist.all_to_all_single(got, rows, group=group)        # block d: rank d's rows for my tokens
+    t = torch.arange(T, device=ids.device, dtype=torch.int32).view(-1, 1)
+    s = torch.arange(TOP, device=ids.device, dtype=torch.int32).view(1, -1)
+    row_index = torch.where(owner >= 0, (owner.to(torch.int32) * T + t) * TOP + s, torch.full_like(owner, -1))
+    return combine(got.view(world * T * TOP, H), row_index.to(torch.int32).contiguous(), weights, ids)
 
 
 class ExpertParallelMoE:
@@ -117,14 +165,19 @@ class ExpertParallelMoE:
 
     banks: (gate_codes, gate_meta, down_codes, down_meta) of the local experts
     only ([256/world, ...] each).  capacity: the largest number of token rows
-    one rank may receive (world * local tokens at most)."""
+    one rank may receive (world * local tokens at most).  exchange: 'compact'
+    (variable splits, any token counts) or 'fixed' (equal blocks, no host
+    synchronisation; every rank must call with the same token count)."""
 
-    def __init__(self, group, world, banks, capacity, act_bits=8):
+    def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact'):
         from . import native
+        if exchange not in ('compact', 'fixed'):
+            raise ValueError(f'unknown exchange mode {exchange!r}')
         self.native = native
         self.group, self.world = group, world
         self.banks = banks
         self.capacity = int(capacity)
+        self.exchange = exchange
         self.symbol = 'ornith_routed_direct_launch' if act_bits == 8 else 'ornith_routed_direct_launch_a4'
         dev = banks[0].device
         self.layout = native.get_layout(self.capacity)
@@ -133,21 +186,31 @@ class ExpertParallelMoE:
         self._ones = torch.ones((self.capacity, TOP), dtype=torch.float32, device=dev)
         self._scratch_out = torch.empty((self.capacity, H), dtype=torch.bfloat16, device=dev)
 
-    def compute(self, x_recv, ids_recv):
+    def _layer(self, x_recv, ids_recv):
         n = x_recv.shape[0]
         if n > self.capacity:
             raise ValueError(f'expert-parallel receive of {n} rows exceeds capacity {self.capacity}')
-        native = self.native
         if n:
+            native = self.native
             fn = getattr(native.lib(), self.symbol)
             native.check(fn(*[native.ptr(t) for t in (x_recv.contiguous(), self._ones[:n], ids_recv, *self.banks,
                                                       self.workspace)],
                             self.workspace.numel(), native.ptr(self._scratch_out), native.ptr(self.flags), n,
                             self.capacity, native.stream(x_recv)), 'expert-parallel compute')
+        return n
+
+    def compute(self, x_recv, ids_recv):
+        n = self._layer(x_recv, ids_recv)
         sel = (ids_recv >= 0).view(-1).nonzero().flatten().to(torch.int32)  # (token, slot) order
         rows = torch.empty((sel.numel(), H), dtype=torch.float32, device=x_recv.device)
-        native.gather_route_rows(self.workspace, n, self.capacity, sel, rows, self.flags)
+        self.native.gather_route_rows(self.workspace, n, self.capacity, sel, rows, self.flags)
         return rows
+
+    def compute_block(self, x_all, ids_all):
+        n = self._layer(x_all, ids_all)
+        rows = torch.empty((n * TOP, H), dtype=torch.float32, device=x_all.device)
+        self.native.scatter_route_rows(self.workspace, n, self.capacity, rows)
+        return rows.view(n, TOP, H)
 
     def combine(self, rows, row_index, weights, ids):
         out = torch.empty((ids.shape[0], H), dtype=torch.bfloat16, device=rows.device)
@@ -155,4 +218,6 @@ class ExpertParallelMoE:
         return out
 
     def __call__(self, x, ids, weights):
+        if self.exchange == 'fixed':
+            return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine)
         return ep_layer(self.group, self.world, x, ids, weights, self.compute, self.combine)

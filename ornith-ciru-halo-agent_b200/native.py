@@ -57,6 +57,8 @@ SIGNATURES = {
                                          C.c_int),
     'ornith_moe_b200_gather_route_rows': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_int]
                                           + [C.c_void_p] * 3, C.c_int),
+    'ornith_moe_b200_scatter_route_rows': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_void_p],
+                                           C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
 }
@@ -276,6 +278,15 @@ def gather_route_rows(workspace, T, capacity, route_index, rows, flags):
         raise ValueError('gather_route_rows requires INT32 route indices [n] and FP32 rows [n,2048]')
     check(lib().ornith_moe_b200_gather_route_rows(ptr(workspace), workspace.numel(), T, capacity, ptr(route_index), n,
                                                   ptr(rows), ptr(flags), stream(rows)), 'gather_route_rows')
+
+
+def scatter_route_rows(workspace, T, capacity, rows):
+    """Route-ordered fp32 down projections [8T, 2048] of the last layer call of
+    T tokens on `workspace` (rows of padding slots hold unspecified values)."""
+    if rows.dtype != torch.float32 or rows.shape != (T * 8, 2048) or not rows.is_contiguous():
+        raise ValueError('scatter_route_rows requires FP32 rows [8T,2048]')
+    check(lib().ornith_moe_b200_scatter_route_rows(ptr(workspace), workspace.numel(), T, capacity, ptr(rows),
+                                                   stream(rows)), 'scatter_route_rows')
 
 
 def repack_n16_to_n32(codes16, meta16, N, K):

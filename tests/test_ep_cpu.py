@@ -61,7 +61,7 @@ def _inputs(rank, T, seed):
     return x, ids, weights
 
 
-def _worker(rank, world, port, T, seed, q):
+def _worker(rank, world, port, T, seed, q, mode):
     try:
         os.environ['MASTER_ADDR'] = '127.0.0.1'
         os.environ['MASTER_PORT'] = str(port)
@@ -76,7 +76,13 @@ def _worker(rank, world, port, T, seed, q):
         def compute(xr, ir):
             return fake_rows(xr, ir, rank * epr)[ir >= 0] if xr.shape[0] else torch.zeros((0, H))
 
-        out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered)
+        def compute_block(xa, ia):
+            return fake_rows(xa, ia, rank * epr)
+
+        if mode == 'fixed':
+            out = ep.ep_layer_fixed(None, world, x, ids, weights, compute_block, fake_combine_gathered)
+        else:
+            out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered)
         ref = fake_combine(fake_rows(x, ids, 0).view(T * TOP, H), weights, ids)
         q.put((rank, bool(torch.equal(out, ref)), ''))
         dist.barrier()
@@ -85,12 +91,13 @@ def _worker(rank, world, port, T, seed, q):
         q.put((rank, False, repr(exc)))
 
 
+@pytest.mark.parametrize('mode', ['compact', 'fixed'])
 @pytest.mark.parametrize('world,T', [(2, 16), (4, 9)])
-def test_ep_dispatch_combine_matches_single_rank(world, T):
+def test_ep_dispatch_combine_matches_single_rank(world, T, mode):
     ctx = mp.get_context('spawn')
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, T, 1234, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, 1234, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=180) for _ in range(world)]

@@ -31,7 +31,7 @@ def _bank(gen, experts, N, K, dev):
     return codes, meta.view(torch.uint32)
 
 
-def _worker(rank, world, port, T, q):
+def _worker(rank, world, port, T, q, mode):
     try:
         import datetime
         import torch.distributed as dist
@@ -64,7 +64,7 @@ def _worker(rank, world, port, T, q):
         epr = 256 // world
         sl = slice(rank * epr, (rank + 1) * epr)
         layer = ep.ExpertParallelMoE(None, world, (gc[sl].contiguous(), gm[sl].contiguous(), dc[sl].contiguous(),
-                                                   dm[sl].contiguous()), capacity=T * world)
+                                                   dm[sl].contiguous()), capacity=T * world, exchange=mode)
         out = layer(x, ids, w)
         torch.cuda.synchronize()
         q.put((rank, bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))), int(flags.item()), ''))
@@ -75,13 +75,14 @@ def _worker(rank, world, port, T, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+@pytest.mark.parametrize('mode', ['compact', 'fixed'])
 @pytest.mark.parametrize('T', [5, 96])
-def test_expert_parallel_matches_single_gpu(T):
+def test_expert_parallel_matches_single_gpu(T, mode):
     import torch.multiprocessing as mp
     ctx = mp.get_context('spawn')
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in range(2)]

@@ -400,9 +400,10 @@ def test_combine_gathered_matches_dense_combine(native, S, T):
 
 @pytest.mark.parametrize('T', [5, 96])
 def test_gather_route_rows_across_paths(native, layer1, bank1, S, T, monkeypatch):
-    """gather_route_rows returns the same per-route rows whichever path ran the
-    layer: route order (decode kernel, multi-kernel path) or expert-slot order
-    (tensor-core path, read through its route -> row map)."""
+    """gather_route_rows and scatter_route_rows return the same per-route rows
+    whichever path ran the layer: route order (decode kernel, multi-kernel
+    path) or expert-slot order (tensor-core path, read through its route ->
+    row map)."""
     rng = np.random.default_rng(900 + T)
     x = S.make_tokens(rng, T)
     w, ids = S.random_routes(rng, T, pad_fraction=0.1)
@@ -417,11 +418,15 @@ def test_gather_route_rows_across_paths(native, layer1, bank1, S, T, monkeypatch
             native.ptr(flags), T, T, native.stream(out)), 'layer')
         rows = torch.empty((sel.numel(), 2048), dtype=torch.float32, device=DEV)
         native.gather_route_rows(ws, T, T, sel, rows, flags)
+        dense = torch.zeros((T * 8, 2048), dtype=torch.float32, device=DEV)
+        native.scatter_route_rows(ws, T, T, dense)
         torch.cuda.synchronize()
-        return rows.cpu().numpy(), int(flags.item())
+        return rows.cpu().numpy(), dense[sel.long()].cpu().numpy(), int(flags.item())
 
-    fast, f1 = rows_after_layer()
+    fast, fast_dense, f1 = rows_after_layer()
     monkeypatch.setenv('ORNITH_MOE_B200_PATH', 'generic')
-    multi, f2 = rows_after_layer()
+    multi, multi_dense, f2 = rows_after_layer()
     assert f1 == f2 == 0
     np.testing.assert_array_equal(fast.view(np.uint32), multi.view(np.uint32))
+    np.testing.assert_array_equal(fast_dense.view(np.uint32), fast.view(np.uint32))
+    np.testing.assert_array_equal(multi_dense.view(np.uint32), multi.view(np.uint32))
