@@ -215,6 +215,25 @@ def run_ep(args):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # The fixed-block exchange has no host synchronisation, so the whole step
+    # (collectives included) is captured once and replayed.
+    graph = None
+    if cfg['exchange'] == 'fixed' and not args.no_graph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph.replay()
+        torch.cuda.synchronize()
+        step = graph.replay
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -238,9 +257,12 @@ def run_ep(args):
                    'exchange': ('NCCL all_gather of token rows + equal-block all_to_all of fp32 per-slot rows '
                                 '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
                                 'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)')},
-        'flags': int(flags.item()), 'clocks': clk.summary(),
+        'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': graph is not None,
     }
     dist.barrier()
+    step = None
+    graph = None  # a graph holding NCCL calls is released before the process group
+    torch.cuda.synchronize()
     dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
