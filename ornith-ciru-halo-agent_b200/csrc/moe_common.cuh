@@ -110,6 +110,37 @@ __device__ __forceinline__ float div_rn_ge1(float g, float d, bool& ok) {
     return zero ? g : q1;
 }
 
+// The SiLU quotient g / (1 + portable_exp(-g)) for |g| < 80, the common case,
+// in about half the instructions of the general form: the exponent argument is
+// inside portable_exp's range, so its range selects drop out and ldexp is one
+// exact product (n in [-116, 116], p * 2^n normal); the division is
+// div_rn_ge1.  *ok is false outside |g| < 80 or where div_rn_ge1 cannot confirm
+// the quotient; the caller then uses the general form.  Checked against the
+// general form on the GPU for every fp32 g.
+__device__ __forceinline__ float silu_quotient_fast(float g, bool& ok) {
+    const float x = -g;
+    const float n_float = rintf(__fmul_rn(x, 0x1.715476p+0f));
+    const int n = static_cast<int>(n_float);
+    const float high = __fmul_rn(n_float, 0x1.62e400p-1f);
+    const float low = __fmul_rn(n_float, 0x1.7f7d1cp-20f);
+    const float r = __fsub_rn(__fsub_rn(x, high), low);
+    float p = 0x1.a01a02p-16f;
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.a01a02p-13f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.6c16c2p-10f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.111112p-7f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.555556p-5f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1.555556p-3f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1p-1f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1p+0f);
+    p = __fadd_rn(__fmul_rn(p, r), 0x1p+0f);
+    const float e = __fmul_rn(p, __int_as_float((n + 127) << 23));
+    const float d = __fadd_rn(1.f, e);
+    bool dok;
+    const float q = div_rn_ge1(g, d, dok);
+    ok = dok && fabsf(g) < 80.f;
+    return q;
+}
+
 // Routed SiLU*up (middle_kernel): (g / (1 + exp(-g))) * up, IEEE division.
 __device__ __forceinline__ float silu_mul(float g, float up) {
     float denominator = __fadd_rn(1.f, portable_exp(-g));
@@ -256,6 +287,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// try_wait that may suspend the thread for up to hint_ns until the phase
+// completes (instead of returning at once), so waiting warps stop taking issue
+// slots from the working ones.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;

@@ -67,6 +67,7 @@ static_assert(2 * 128 * kRegsSetup + 4 * 128 * kRegsEpi <= kThreads * kRegsLaunc
 constexpr uint32_t kMagic = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 constexpr uint64_t kTimeoutNs = 1000000000ull;
+constexpr uint32_t kSuspendNs = 20000;  // longest suspension of one wait attempt
 
 __device__ __forceinline__ uint64_t now_ns() {
     uint64_t t;
@@ -77,14 +78,20 @@ __device__ __forceinline__ uint64_t now_ns() {
 // Per-role timestamps of a few CTAs (clock64), compiled in only with
 // -DORNITH_PREFILL_TRACE; the default build has none.
 #ifdef ORNITH_PREFILL_TRACE
-constexpr int kPTraceCtas = 4, kPTraceKinds = 11, kPTraceLen = 256;
+constexpr int kPTraceCtas = 4, kPTraceKinds = 12, kPTraceLen = 256;
 __device__ unsigned long long g_prefill_trace[2][kPTraceCtas][kPTraceKinds][kPTraceLen];
 #define PREFILL_TRACE(kind, idx)                                                                         \
     ((blockIdx.x % 37 == 0 && blockIdx.x / 37 < kPTraceCtas && (idx) < kPTraceLen)                      \
          ? void(g_prefill_trace[GATE ? 0 : 1][blockIdx.x / 37][kind][idx] = clock64())                  \
          : void(0))
+// spin iterations of the bounded waits, per warp (kind 11)
+#define PREFILL_SPINS(n)                                                                                 \
+    ((blockIdx.x % 37 == 0 && blockIdx.x / 37 < kPTraceCtas)                                           \
+         ? void(atomicAdd(&g_prefill_trace[0][blockIdx.x / 37][11][threadIdx.x >> 5], (unsigned long long)(n))) \
+         : void(0))
 #else
 #define PREFILL_TRACE(kind, idx) ((void)0)
+#define PREFILL_SPINS(n) ((void)0)
 #endif
 
 // ---- tcgen05 wrappers ----------------------------------------------------
@@ -160,7 +167,9 @@ __device__ __forceinline__ bool named_and(int id, int threads, bool pred) {
 __device__ bool bwait(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* flags) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = now_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    unsigned spins = 0;
+    while (!mbar_try_wait_suspend(bar, parity, kSuspendNs)) {
+        ++spins;
         if (*abort) return false;
         if (now_ns() - t0 > kTimeoutNs) {
             atomicOr(flags, kFlagWaitTimeout);
@@ -168,6 +177,7 @@ __device__ bool bwait(uint64_t* bar, uint32_t parity, volatile int* abort, uint3
             return false;
         }
     }
+    if ((threadIdx.x & 31) == 0) PREFILL_SPINS(spins + 1);
     return true;
 }
 // Drain wait used on the abort path: lets an issued copy land (bounded).
@@ -523,25 +533,22 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         c[k] = make_float4(v[0], v[1], v[2], v[3]);
                     }
                 } else {
-                    // silu_mul in batches of 8: the eight exponentials and
-                    // divisions are independent straight-line chains and
-                    // interleave; the rare quotients the fast division cannot
-                    // confirm are redone with __fdiv_rn
+                    // silu_mul in batches of 8: the eight quotients are
+                    // independent straight-line chains and interleave; the rare
+                    // ones the fast form cannot confirm take the general form
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
                         // rows past the tile's end hold stale sums: they take
                         // g = 1 so that they never reach the slow division
-                        float gs[8], d[8], q[8], v[8];
+                        float gs[8], q[8], v[8];
                         bool ok[8];
 #pragma unroll
                         for (int j = 0; j < 8; ++j) gs[j] = valid ? acc[i + j] : 1.f;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) d[j] = __fadd_rn(1.f, portable_exp(-gs[j]));
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) q[j] = div_rn_ge1(gs[j], d[j], ok[j]);
+                        for (int j = 0; j < 8; ++j) q[j] = silu_quotient_fast(gs[j], ok[j]);
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
-                            if (!ok[j]) q[j] = __fdiv_rn(gs[j], d[j]);
+                            if (!ok[j]) q[j] = __fdiv_rn(gs[j], __fadd_rn(1.f, portable_exp(-gs[j])));
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const float gv = acc[i + j], uv = acc[32 + i + j];
