@@ -77,6 +77,8 @@ def parse():
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
     p.add_argument('--no-graph', action='store_true', help='time eager launches instead of a captured step')
+    p.add_argument('--placement', choices=['balanced', 'contiguous'], default='balanced',
+                   help='expert placement of the expert-parallel configs')
     p.add_argument('--layers', type=int, default=None,
                    help='override the layer count (small cases for profiler captures)')
     return p.parse_args()
@@ -193,13 +195,20 @@ def run_ep(args):
     epr = 256 // world
     gen = torch.Generator(device=dev)
     gen.manual_seed(4321 + rank)
+    bias = torch.from_numpy(S.zipf_bias(np.random.default_rng(12), 256, 1.2)).to(dev)  # same on every rank
+    # expert placement balanced by routed load, from a calibration batch drawn
+    # from the same distribution (identical on every rank); each rank's random
+    # banks stand for the experts the placement gives it
+    calib = torch.randn((4096, 256), generator=torch.Generator().manual_seed(999)) + bias.cpu()
+    loads = torch.bincount(torch.topk(calib, 8, dim=1).indices.flatten(), minlength=256)
+    placement = ep.balanced_placement(loads, world, dev) if args.placement == 'balanced' else \
+        ep.contiguous_placement(world, dev)
     layers = []
     for _ in range(L):
         g = device_bank(torch, gen, dev, epr, 1024, 2048)
         d = device_bank(torch, gen, dev, epr, 2048, 512)
         layers.append(ep.ExpertParallelMoE(None, world, (g[0], g[1], d[0], d[1]), capacity=min(T * world, 8192),
-                                           act_bits=bits, exchange=cfg['exchange']))
-    bias = torch.from_numpy(S.zipf_bias(np.random.default_rng(12), 256, 1.2)).to(dev)  # same on every rank
+                                           act_bits=bits, exchange=cfg['exchange'], placement=placement))
     logits = torch.randn((L, T, 256), device=dev, generator=gen) + bias
     x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
     w = torch.empty((L, T, 8), dtype=torch.float32, device=dev)
@@ -254,6 +263,8 @@ def run_ep(args):
         'data': 'synthetic (seeded random-init weights and logits of the configured shapes)',
         'config': {'workload': cfg['name'], 'tokens_per_step': T_total, 'tokens_per_rank': T, 'layers': L,
                    'experts_per_rank': epr, 'parallelism': f'ep{world}',
+                   'placement': ('balanced by routed load of a 4096-token calibration batch'
+                                 if args.placement == 'balanced' else 'contiguous ranges'),
                    'exchange': ('NCCL all_gather of token rows + equal-block all_to_all of fp32 per-slot rows '
                                 '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
                                 'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)')},

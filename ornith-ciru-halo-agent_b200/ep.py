@@ -1,10 +1,11 @@
 """Expert parallelism for the routed-MoE layer over torch.distributed.
 
 The reference runs one rank and refuses EP (plugin-site/ornith_g256/moe_base.py:34-39);
-this module adds it.  Rank r of n owns routed experts
-[r*256/n, (r+1)*256/n); the shared expert is replicated and runs on each rank
-for its own tokens.  One layer call on every rank, for the rank's own tokens,
-in one of two exchange modes.
+this module adds it.  Every rank owns 256/n routed experts: by default rank r
+owns [r*256/n, (r+1)*256/n); a Placement can assign them by routed load
+instead (balanced_placement).  The shared expert is replicated and runs on
+each rank for its own tokens.  One layer call on every rank, for the rank's own
+tokens, in one of two exchange modes.
 
 compact (any batch; ranks may hold different token counts):
   1. dispatch plan: for every destination rank d, the local tokens with at
@@ -40,6 +41,51 @@ E, TOP, H = 256, 8, 2048
 
 
 @dataclass
+class Placement:
+    """Which rank holds each routed expert, and at which index of its banks."""
+    rank: torch.Tensor   # int64 [256]
+    local: torch.Tensor  # int64 [256]
+
+    def experts_of(self, r):
+        """Global expert ids held by rank r, in bank order."""
+        mine = (self.rank == r).nonzero().flatten()
+        return mine[torch.argsort(self.local[mine])].tolist()
+
+
+def contiguous_placement(world, device=None):
+    e = torch.arange(E, device=device)
+    epr = E // world
+    return Placement(torch.div(e, epr, rounding_mode='floor'), e % epr)
+
+
+def balanced_placement(counts, world, device=None):
+    """Equal expert counts per rank, routed load balanced greedily: experts in
+    decreasing load go to the least-loaded rank that still has room (ties to the
+    lower rank, so every rank computes the same placement from the same counts)."""
+    counts = [float(c) for c in torch.as_tensor(counts).flatten().tolist()]
+    if len(counts) != E or E % world:
+        raise ValueError('balanced_placement needs 256 expert loads and a world size dividing 256')
+    epr = E // world
+    load, fill = [0.0] * world, [0] * world
+    rank, local = [0] * E, [0] * E
+    for e in sorted(range(E), key=lambda i: (-counts[i], i)):
+        r = min((r for r in range(world) if fill[r] < epr), key=lambda r: (load[r], r))
+        rank[e], local[e] = r, fill[r]
+        load[r] += counts[e]
+        fill[r] += 1
+    return Placement(torch.tensor(rank, device=device), torch.tensor(local, device=device))
+
+
+def map_ids(ids, placement):
+    """(owning rank, index in the owner's banks) of every slot; -1 for padding."""
+    valid = ids >= 0
+    e = ids.clamp(min=0).long()
+    neg = torch.full_like(ids, -1)
+    return (torch.where(valid, placement.rank[e].to(ids.dtype), neg),
+            torch.where(valid, placement.local[e].to(ids.dtype), neg))
+
+
+@dataclass
 class DispatchPlan:
     send_counts: list          # tokens sent to each rank
     home_counts: list          # (token, slot) rows each rank sends back
@@ -48,21 +94,17 @@ class DispatchPlan:
     slot_mask: torch.Tensor    # [sum(send_counts), 8] True where the slot is owned by the destination
 
 
-def owners(ids, world, experts_per_rank=None):
-    epr = experts_per_rank or E // world
-    return torch.where(ids >= 0, torch.div(ids, epr, rounding_mode='floor'), torch.full_like(ids, -1)), epr
-
-
-def build_dispatch(ids, world, experts_per_rank=None):
+def build_dispatch(ids, world, placement=None):
     """Group each token's slots by owning rank (pure tensor logic, any device;
     one host synchronisation for the split sizes)."""
-    owner, epr = owners(ids, world, experts_per_rank)
+    placement = placement or contiguous_placement(world, ids.device)
+    owner, lid = map_ids(ids, placement)
     dest = torch.arange(world, device=ids.device).view(-1, 1, 1)
     mask = owner.unsqueeze(0) == dest                      # [world, T, 8]
     sent = mask.any(dim=2).nonzero()                       # (d, t), grouped by d, t ascending
     d, tok = sent[:, 0], sent[:, 1]
     slot_mask = mask[d, tok]
-    local = torch.where(slot_mask, ids[tok] - (d * epr).unsqueeze(1), torch.full_like(slot_mask, -1, dtype=ids.dtype))
+    local = torch.where(slot_mask, lid[tok], torch.full_like(slot_mask, -1, dtype=ids.dtype))
     counts = torch.stack([torch.bincount(d, minlength=world),
                           torch.zeros(world, dtype=torch.int64, device=ids.device).index_add_(
                               0, d, slot_mask.sum(dim=1))]).tolist()
@@ -122,14 +164,14 @@ def route_row_index(T, plan, device):
     return idx.scatter_reduce_(0, plan.token_index.view(-1, 1).expand(-1, TOP), dense, 'amax')
 
 
-def ep_layer(group, world, x, ids, weights, compute, combine):
+def ep_layer(group, world, x, ids, weights, compute, combine, placement=None):
     """One expert-parallel layer call, compact exchange.
 
     compute(x_recv, ids_recv) -> fp32 [n_valid, 2048]: the rows of the received
     slots with a valid id, in (token, slot) order; combine(rows [n, 2048],
     row_index [T, 8], weights, ids) -> output.  Both are injected so that the
     host logic also runs on CPU ranks."""
-    plan = build_dispatch(ids, world)
+    plan = build_dispatch(ids, world, placement)
     x_recv, ids_recv, recv_counts = exchange_rows(group, world, plan, x)
     back_counts = valid_counts(ids_recv, recv_counts)
     out_rows = compute(x_recv, ids_recv)
@@ -137,15 +179,16 @@ def ep_layer(group, world, x, ids, weights, compute, combine):
     return combine(got, route_row_index(x.shape[0], plan, got.device), weights, ids)
 
 
-def ep_layer_fixed(group, world, x, ids, weights, compute_block, combine):
+def ep_layer_fixed(group, world, x, ids, weights, compute_block, combine, placement=None):
     """One expert-parallel layer call, fixed-size exchange (same T on every rank).
 
     compute_block(x_all [world*T, 2048], ids_all [world*T, 8]) -> fp32
     [world*T, 8, 2048], route-ordered (padding slots unspecified)."""
     T = x.shape[0]
-    owner, epr = owners(ids, world)
+    placement = placement or contiguous_placement(world, ids.device)
+    owner, lid = map_ids(ids, placement)
     dest = torch.arange(world, device=ids.device).view(-1, 1, 1)
-    local = torch.where(owner.unsqueeze(0) == dest, ids.unsqueeze(0) - dest * epr,
+    local = torch.where(owner.unsqueeze(0) == dest, lid.unsqueeze(0),
                         torch.full_like(owner.unsqueeze(0), -1)).to(torch.int32).contiguous()   # [world, T, 8]
     x_all = torch.empty((world * T, H // 2), dtype=torch.int32, device=x.device)
     dist.all_gather_into_tensor(x_all, x.contiguous().view(torch.int32), group=group)
@@ -164,12 +207,14 @@ class ExpertParallelMoE:
     """GPU expert-parallel layer over NCCL with this library's kernels.
 
     banks: (gate_codes, gate_meta, down_codes, down_meta) of the local experts
-    only ([256/world, ...] each).  capacity: the largest number of token rows
+    only ([256/world, ...] each, in the placement's bank order:
+    placement.experts_of(rank)).  capacity: the largest number of token rows
     one rank may receive (world * local tokens at most).  exchange: 'compact'
     (variable splits, any token counts) or 'fixed' (equal blocks, no host
-    synchronisation; every rank must call with the same token count)."""
+    synchronisation; every rank must call with the same token count).
+    placement: the same on every rank; contiguous ranges by default."""
 
-    def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact'):
+    def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact', placement=None):
         from . import native
         if exchange not in ('compact', 'fixed'):
             raise ValueError(f'unknown exchange mode {exchange!r}')
@@ -178,6 +223,7 @@ class ExpertParallelMoE:
         self.banks = banks
         self.capacity = int(capacity)
         self.exchange = exchange
+        self.placement = placement or contiguous_placement(world, banks[0].device)
         self.symbol = 'ornith_routed_direct_launch' if act_bits == 8 else 'ornith_routed_direct_launch_a4'
         dev = banks[0].device
         self.layout = native.get_layout(self.capacity)
@@ -219,5 +265,6 @@ class ExpertParallelMoE:
 
     def __call__(self, x, ids, weights):
         if self.exchange == 'fixed':
-            return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine)
-        return ep_layer(self.group, self.world, x, ids, weights, self.compute, self.combine)
+            return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine,
+                                  self.placement)
+        return ep_layer(self.group, self.world, x, ids, weights, self.compute, self.combine, self.placement)

@@ -17,10 +17,11 @@ ROOT = Path(__file__).resolve().parents[1]
 E, TOP, H = 256, 8, 2048
 
 
-def fake_rows(x, ids_local, rank_offset):
-    """Deterministic per-slot rows depending on the token row and the global expert."""
+def fake_rows(x, ids_local, table):
+    """Deterministic per-slot rows depending on the token row and the global
+    expert (table: global expert of each local bank index)."""
     xf = x.float()
-    g = (ids_local + rank_offset).clamp(min=0).float()
+    g = table[ids_local.clamp(min=0).long()].float()
     return (xf.unsqueeze(1) * (g.unsqueeze(2) * 0.01 + 1.0) + g.unsqueeze(2) * 0.5).contiguous()
 
 
@@ -61,7 +62,7 @@ def _inputs(rank, T, seed):
     return x, ids, weights
 
 
-def _worker(rank, world, port, T, seed, q, mode):
+def _worker(rank, world, port, T, seed, q, mode, balanced):
     try:
         os.environ['MASTER_ADDR'] = '127.0.0.1'
         os.environ['MASTER_PORT'] = str(port)
@@ -71,19 +72,24 @@ def _worker(rank, world, port, T, seed, q, mode):
         g.load_package()
         from ornith_b200 import ep
         x, ids, weights = _inputs(rank, T, seed)
-        epr = E // world
+        if balanced:  # a load-balanced placement from (identical) skewed loads
+            loads = torch.arange(E, dtype=torch.float64).flip(0) ** 2
+            placement = ep.balanced_placement(loads, world)
+        else:
+            placement = ep.contiguous_placement(world)
+        table = torch.tensor(placement.experts_of(rank))
 
         def compute(xr, ir):
-            return fake_rows(xr, ir, rank * epr)[ir >= 0] if xr.shape[0] else torch.zeros((0, H))
+            return fake_rows(xr, ir, table)[ir >= 0] if xr.shape[0] else torch.zeros((0, H))
 
         def compute_block(xa, ia):
-            return fake_rows(xa, ia, rank * epr)
+            return fake_rows(xa, ia, table)
 
         if mode == 'fixed':
-            out = ep.ep_layer_fixed(None, world, x, ids, weights, compute_block, fake_combine_gathered)
+            out = ep.ep_layer_fixed(None, world, x, ids, weights, compute_block, fake_combine_gathered, placement)
         else:
-            out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered)
-        ref = fake_combine(fake_rows(x, ids, 0).view(T * TOP, H), weights, ids)
+            out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered, placement)
+        ref = fake_combine(fake_rows(x, ids, torch.arange(E)).view(T * TOP, H), weights, ids)
         q.put((rank, bool(torch.equal(out, ref)), ''))
         dist.barrier()
         dist.destroy_process_group()
@@ -91,13 +97,14 @@ def _worker(rank, world, port, T, seed, q, mode):
         q.put((rank, False, repr(exc)))
 
 
+@pytest.mark.parametrize('balanced', [False, True])
 @pytest.mark.parametrize('mode', ['compact', 'fixed'])
 @pytest.mark.parametrize('world,T', [(2, 16), (4, 9)])
-def test_ep_dispatch_combine_matches_single_rank(world, T, mode):
+def test_ep_dispatch_combine_matches_single_rank(world, T, mode, balanced):
     ctx = mp.get_context('spawn')
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, T, 1234, q, mode)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, T, 1234, q, mode, balanced)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=180) for _ in range(world)]
@@ -122,3 +129,20 @@ def test_build_dispatch_groups_by_owner():
     assert plan.local_ids[2].tolist() == [-1, 72, -1, -1, 2, -1, -1, 127]
     assert plan.local_ids[3].tolist() == [1, 0, -1, -1, -1, -1, -1, -1]
     assert int(plan.slot_mask.sum()) == int((ids >= 0).sum())
+
+
+def test_balanced_placement_properties():
+    import __graft_entry__ as g
+    g.load_package()
+    from ornith_b200 import ep
+    loads = torch.rand(E, generator=torch.Generator().manual_seed(3)) ** 4
+    for world in (2, 4, 8):
+        pl = ep.balanced_placement(loads, world)
+        per = [ep.Placement.experts_of(pl, r) for r in range(world)]
+        assert sorted(sum(per, [])) == list(range(E))                   # every expert exactly once
+        assert all(len(x) == E // world for x in per)                   # equal banks
+        assert all(pl.local[e] == i for x in per for i, e in enumerate(x))
+        rank_load = [float(loads[x].sum()) for x in per]
+        contiguous = [float(loads[r * E // world:(r + 1) * E // world].sum()) for r in range(world)]
+        assert max(rank_load) <= max(contiguous) + 1e-9
+        assert max(rank_load) - min(rank_load) <= float(loads.max()) + 1e-9  # greedy bound

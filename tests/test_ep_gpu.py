@@ -31,7 +31,7 @@ def _bank(gen, experts, N, K, dev):
     return codes, meta.view(torch.uint32)
 
 
-def _worker(rank, world, port, T, q, mode):
+def _worker(rank, world, port, T, q, mode, balanced):
     try:
         import datetime
         import torch.distributed as dist
@@ -61,10 +61,17 @@ def _worker(rank, world, port, T, q, mode):
         native.check(native.lib().ornith_routed_direct_launch(
             *[native.ptr(t) for t in (x, w, ids, gc, gm, dc, dm, ws)], ws.numel(), native.ptr(ref),
             native.ptr(flags), T, T, native.stream(x)), 'reference layer')
-        epr = 256 // world
-        sl = slice(rank * epr, (rank + 1) * epr)
-        layer = ep.ExpertParallelMoE(None, world, (gc[sl].contiguous(), gm[sl].contiguous(), dc[sl].contiguous(),
-                                                   dm[sl].contiguous()), capacity=T * world, exchange=mode)
+        if balanced:  # any placement must give the same bits; use a skewed-load one
+            placement = ep.balanced_placement(torch.arange(256, dtype=torch.float64).flip(0) ** 2, world, dev)
+        else:
+            placement = ep.contiguous_placement(world, dev)
+        sl = torch.tensor(placement.experts_of(rank), device=dev)
+
+        def pick(bank):  # this rank's experts, in the placement's bank order
+            return bank.view(torch.int32)[sl].contiguous().view(torch.uint32)
+
+        layer = ep.ExpertParallelMoE(None, world, (pick(gc), pick(gm), pick(dc), pick(dm)), capacity=T * world,
+                                     exchange=mode, placement=placement)
         out = layer(x, ids, w)
         torch.cuda.synchronize()
         q.put((rank, bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))), int(flags.item()), ''))
@@ -75,14 +82,15 @@ def _worker(rank, world, port, T, q, mode):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+@pytest.mark.parametrize('balanced', [False, True])
 @pytest.mark.parametrize('mode', ['compact', 'fixed'])
 @pytest.mark.parametrize('T', [5, 96])
-def test_expert_parallel_matches_single_gpu(T, mode):
+def test_expert_parallel_matches_single_gpu(T, mode, balanced):
     import torch.multiprocessing as mp
     ctx = mp.get_context('spawn')
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, q, mode)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, q, mode, balanced)) for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in range(2)]
