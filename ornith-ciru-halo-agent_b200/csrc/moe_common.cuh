@@ -119,8 +119,12 @@ __device__ __forceinline__ float div_rn_ge1(float g, float d, bool& ok) {
 // general form on the GPU for every fp32 g.
 __device__ __forceinline__ float silu_quotient_fast(float g, bool& ok) {
     const float x = -g;
-    const float n_float = rintf(__fmul_rn(x, 0x1.715476p+0f));
-    const int n = static_cast<int>(n_float);
+    // rint(t) for |t| < 2^22 as (t + 1.5*2^23) - 1.5*2^23 (the addition rounds
+    // to the nearest even integer), and n from the sum's low mantissa bits:
+    // both on the FMA and integer pipes instead of the conversion unit
+    const float shifted = __fadd_rn(__fmul_rn(x, 0x1.715476p+0f), 12582912.f);
+    const float n_float = __fsub_rn(shifted, 12582912.f);
+    const int n = __float_as_int(shifted) - 0x4B400000;
     const float high = __fmul_rn(n_float, 0x1.62e400p-1f);
     const float low = __fmul_rn(n_float, 0x1.7f7d1cp-20f);
     const float r = __fsub_rn(__fsub_rn(x, high), low);
