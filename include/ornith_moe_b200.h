@@ -192,6 +192,26 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_gather_route_rows(
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_scatter_route_rows(
     const void* workspace, size_t bytes, int T, int Tcap, void* rows_f32, cudaStream_t stream);
 
+/* Router logits, the router linear ahead of the operator
+ * (iu4_correctness/gates_projection.py:17-25): input bf16 [T,2048],
+ * router_weight bf16 [256,2048] -> logits fp32 [T,256], each the fp32 sum
+ * over k of f32(x)*f32(w).  The reference's reduction order is unspecified;
+ * these agree with an exact sum to fp32 rounding. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_router_logits(
+    const void* input_bf16, const void* router_weight_bf16, int T, void* logits_f32, cudaStream_t stream);
+
+/* The router linear followed by ornith_moe_b200_launch_from_logits: the
+ * logits are written to logits_f32 [T,256] (caller memory) and routed from
+ * there.  Same workspace, outputs and flags as the from-logits entry. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_launch_from_hidden(
+    const void* input_bf16, const void* router_weight_bf16, void* logits_f32,
+    const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
+    const void* shared_gate_codes, const void* shared_gate_meta,
+    const void* shared_down_codes, const void* shared_down_meta,
+    const void* shared_gate_weight_bf16, const void* shared_silu, const void* shared_sigmoid,
+    void* workspace, size_t bytes, void* output_bf16, void* shared_output_bf16, void* flags_u32,
+    int T, int Tcap, int act_bits, cudaStream_t stream);
+
 /* Workspace size for ornith_moe_b200_launch_from_logits (0 <= Tcap <= 8192). */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes);
 

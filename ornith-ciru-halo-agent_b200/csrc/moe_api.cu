@@ -118,6 +118,40 @@ __global__ __launch_bounds__(256) void scatter_route_rows_kernel(const float* ro
     d[1] = __ldcs(src + 1);
 }
 
+// Router logits (iu4_correctness/gates_projection.py:17-25):
+// logits[t][e] = sum_k f32(x[t][k]) * f32(W[e][k]), fp32.  One warp per expert
+// keeps its 2048 weights in registers (64 per lane: k = 256 j + 8 lane + i)
+// and walks the CTA's tokens; per token a lane accumulates its 64 products
+// with FMA in k order, then an xor tree (16, 8, 4, 2, 1) adds the lanes.  The
+// reference's Triton reduction order is unspecified, so the logits agree to
+// rounding (relative 1e-5), not bit for bit.
+constexpr int kRouterTokens = 64;  // tokens per CTA
+__global__ __launch_bounds__(256) void router_logits_kernel(const uint16_t* x, const uint16_t* w, int T,
+                                                            float* logits) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 8 + warp;
+    const int t0 = blockIdx.y * kRouterTokens, t1 = min(T, t0 + kRouterTokens);
+    uint4 wr[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wr[j] = __ldg(reinterpret_cast<const uint4*>(w + size_t(e) * kH + j * 256 + lane * 8));
+    for (int t = t0; t < t1; ++t) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint4 xr = __ldg(reinterpret_cast<const uint4*>(x + size_t(t) * kH + j * 256 + lane * 8));
+            const uint32_t xv[4] = {xr.x, xr.y, xr.z, xr.w}, wv[4] = {wr[j].x, wr[j].y, wr[j].z, wr[j].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc = __fmaf_rn(__uint_as_float(xv[i] << 16), __uint_as_float(wv[i] << 16), acc);
+                acc = __fmaf_rn(__uint_as_float(xv[i] & 0xffff0000u), __uint_as_float(wv[i] & 0xffff0000u), acc);
+            }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+        if (lane == 0) logits[size_t(t) * kE + e] = acc;
+    }
+}
+
 // N16 -> N32 bank repack (method.py:142-147).  One thread per destination word.
 __global__ void repack_codes_kernel(const uint32_t* src, uint32_t* dst, int E, int N, int groups) {
     const size_t total = size_t(E) * (N / 32) * groups * 32 * 32;
@@ -412,6 +446,35 @@ cudaError_t ornith_moe_b200_scatter_route_rows(const void* workspace, size_t byt
         by_position ? reinterpret_cast<const int32_t*>(ws + w.offsets) + kE + 1 : nullptr, T * kTop,
         static_cast<float*>(rows_f32));
     return cudaGetLastError();
+}
+
+cudaError_t ornith_moe_b200_router_logits(const void* input, const void* router_weight, int T, void* logits,
+                                         cudaStream_t stream) {
+    if (T < 0 || T > kTcapMax) return cudaErrorInvalidValue;
+    if (!T) return cudaSuccess;
+    if (!input || !router_weight || !logits || !aligned(input, 16) || !aligned(router_weight, 16) ||
+        !aligned(logits, 4))
+        return cudaErrorInvalidValue;
+    count_launches(1);
+    router_logits_kernel<<<dim3(kE / 8, (T + kRouterTokens - 1) / kRouterTokens), 256, 0, stream>>>(
+        static_cast<const uint16_t*>(input), static_cast<const uint16_t*>(router_weight), T, static_cast<float*>(logits));
+    return cudaGetLastError();
+}
+
+cudaError_t ornith_moe_b200_launch_from_hidden(
+    const void* input, const void* router_weight, void* logits, const void* gate_codes, const void* gate_meta,
+    const void* down_codes, const void* down_meta, const void* shared_gate_codes, const void* shared_gate_meta,
+    const void* shared_down_codes, const void* shared_down_meta, const void* shared_gate_weight,
+    const void* shared_silu, const void* shared_sigmoid, void* workspace, size_t bytes, void* output,
+    void* shared_output, void* flags, int T, int Tcap, int act_bits, cudaStream_t stream) {
+    if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap) return cudaErrorInvalidValue;
+    cudaError_t st = ornith_moe_b200_router_logits(input, router_weight, T, logits, stream);
+    if (st != cudaSuccess) return st;
+    return ornith_moe_b200_launch_from_logits(input, logits, gate_codes, gate_meta, down_codes, down_meta,
+                                              shared_gate_codes, shared_gate_meta, shared_down_codes,
+                                              shared_down_meta, shared_gate_weight, shared_silu, shared_sigmoid,
+                                              workspace, bytes, output, shared_output, flags, T, Tcap, act_bits,
+                                              stream);
 }
 
 cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* workspace_bytes) {

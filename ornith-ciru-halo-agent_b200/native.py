@@ -52,6 +52,9 @@ SIGNATURES = {
     'ornith_moe_b200_launch_from_logits': (
         [C.c_void_p] * 14 + [C.c_size_t] + [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_moe_b200_get_layout': ([C.c_int, C.POINTER(C.c_size_t)], C.c_int),
+    'ornith_moe_b200_router_logits': ([C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
+    'ornith_moe_b200_launch_from_hidden': (
+        [C.c_void_p] * 15 + [C.c_size_t] + [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_moe_b200_combine': ([C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3, C.c_int),
     'ornith_moe_b200_combine_gathered': ([C.c_void_p, C.c_int] + [C.c_void_p] * 3 + [C.c_int] + [C.c_void_p] * 3,
                                          C.c_int),
@@ -242,6 +245,47 @@ def routed_from_logits(x: torch.Tensor, logits: torch.Tensor,
 def _routed_from_logits_fake(x, logits, gate, gate_meta, down, down_meta, shared_gate, shared_gate_meta,
                              shared_down, shared_down_meta, shared_gate_weight, silu_table, sigmoid_table,
                              workspace, out, shared_out, flags, capacity, act_bits):
+    return None
+
+
+def router_logits(x, router_weight, logits):
+    """Router linear: bf16 x [T,2048] and bf16 W [256,2048] -> fp32 logits [T,256]."""
+    T = x.shape[0]
+    if (x.dtype != torch.bfloat16 or x.shape != (T, 2048) or not x.is_contiguous()
+            or router_weight.dtype != torch.bfloat16 or router_weight.shape != (256, 2048)
+            or not router_weight.is_contiguous() or logits.dtype != torch.float32 or logits.shape != (T, 256)
+            or not logits.is_contiguous()):
+        raise ValueError('router_logits requires BF16 x [T,2048], BF16 W [256,2048] and FP32 logits [T,256]')
+    check(lib().ornith_moe_b200_router_logits(ptr(x), ptr(router_weight), T, ptr(logits), stream(x)), 'router_logits')
+
+
+@torch.library.custom_op('ornith_b200::routed_from_hidden',
+                         mutates_args={'logits', 'workspace', 'out', 'shared_out', 'flags'}, device_types='cuda')
+def routed_from_hidden(x: torch.Tensor, router_weight: torch.Tensor, logits: torch.Tensor,
+                       gate: torch.Tensor, gate_meta: torch.Tensor, down: torch.Tensor, down_meta: torch.Tensor,
+                       shared_gate: torch.Tensor | None, shared_gate_meta: torch.Tensor | None,
+                       shared_down: torch.Tensor | None, shared_down_meta: torch.Tensor | None,
+                       shared_gate_weight: torch.Tensor | None, silu_table: torch.Tensor | None,
+                       sigmoid_table: torch.Tensor | None, workspace: torch.Tensor, out: torch.Tensor,
+                       shared_out: torch.Tensor | None, flags: torch.Tensor, capacity: int, act_bits: int) -> None:
+    """The router linear, then routed_from_logits; `logits` receives the router output."""
+    validate(x, out, capacity, 2048)
+    if (router_weight.dtype != torch.bfloat16 or router_weight.shape != (256, 2048)
+            or not router_weight.is_contiguous() or logits.dtype != torch.float32
+            or logits.shape != (x.shape[0], 256) or not logits.is_contiguous()):
+        raise ValueError('routed_from_hidden requires BF16 router weight [256,2048] and FP32 logits [T,256]')
+    check(lib().ornith_moe_b200_launch_from_hidden(
+        *[ptr(t) for t in (x, router_weight, logits, gate, gate_meta, down, down_meta, shared_gate, shared_gate_meta,
+                           shared_down, shared_down_meta, shared_gate_weight, silu_table, sigmoid_table,
+                           workspace)],
+        workspace.numel(), ptr(out), ptr(shared_out), ptr(flags), x.shape[0], capacity, act_bits, stream(x)),
+        'routed_from_hidden')
+
+
+@routed_from_hidden.register_fake
+def _routed_from_hidden_fake(x, router_weight, logits, gate, gate_meta, down, down_meta, shared_gate,
+                             shared_gate_meta, shared_down, shared_down_meta, shared_gate_weight, silu_table,
+                             sigmoid_table, workspace, out, shared_out, flags, capacity, act_bits):
     return None
 
 

@@ -430,3 +430,46 @@ def test_gather_route_rows_across_paths(native, layer1, bank1, S, T, monkeypatch
     np.testing.assert_array_equal(fast.view(np.uint32), multi.view(np.uint32))
     np.testing.assert_array_equal(fast_dense.view(np.uint32), fast.view(np.uint32))
     np.testing.assert_array_equal(multi_dense.view(np.uint32), multi.view(np.uint32))
+
+
+@pytest.mark.parametrize('T', [1, 4, 33, 300])
+def test_router_logits_vs_oracle(native, S, O, T):
+    """Router linear (gates_projection.py:17-25): fp32 sums whose order the
+    reference leaves unspecified, so agreement is to fp32 rounding (relative
+    1e-5 of the sum of |x*w|), against the oracle's exact (double) sum."""
+    rng = np.random.default_rng(70 + T)
+    x = S.make_tokens(rng, T)
+    w = S.make_router(rng)
+    ref = O.router_logits(x, w)
+    logits = torch.empty((T, 256), dtype=torch.float32, device=DEV)
+    native.router_logits(dev(x), dev(w), logits)
+    torch.cuda.synchronize()
+    got = logits.cpu().numpy()
+    scale = np.abs(S.bf16_bits_to_f32(x)) @ np.abs(S.bf16_bits_to_f32(w)).T
+    assert np.all(np.abs(got - ref) <= 1e-5 * scale + 1e-30)
+
+
+def test_config1_from_hidden(native, golden, S):
+    """Config 1 with the router linear on the GPU: logits within rounding of the
+    reference's, the same top-8 ids as the golden case, and the fused entry
+    equal bit for bit to the from-logits entry fed the same logits."""
+    x, router, l1 = S.config1(0)
+    bank = Bank(l1)
+    T = 4
+    ws = torch.empty(native.workspace_bytes(T), dtype=torch.uint8, device=DEV)
+    out_h = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    out_l = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    logits = torch.empty((T, 256), dtype=torch.float32, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    native.routed_from_hidden(dev(x), dev(router), logits, *bank.routed, None, None, None, None, None, None, None,
+                              ws, out_h, None, flags, T, 8)
+    native.routed_from_logits(dev(x), logits.clone(), *bank.routed, None, None, None, None, None, None, None,
+                              ws, out_l, None, flags, T, 8)
+    torch.cuda.synchronize()
+    ref = golden['config1/logits']
+    got = logits.cpu().numpy()
+    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+    ref_top = np.argsort(-ref, axis=1, kind='stable')[:, :8]
+    got_top = np.argsort(-got, axis=1, kind='stable')[:, :8]
+    np.testing.assert_array_equal(np.sort(got_top, axis=1), np.sort(ref_top, axis=1))
+    np.testing.assert_array_equal(host_bits(out_h), host_bits(out_l))
