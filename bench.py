@@ -79,6 +79,8 @@ def parse():
     p.add_argument('--no-graph', action='store_true', help='time eager launches instead of a captured step')
     p.add_argument('--placement', choices=['balanced', 'contiguous'], default='balanced',
                    help='expert placement of the expert-parallel configs')
+    p.add_argument('--combine', choices=['exact', 'partial'], default='exact',
+                   help='expert-parallel return: per-slot rows (bit-exact) or per-rank fp32 partial sums')
     p.add_argument('--layers', type=int, default=None,
                    help='override the layer count (small cases for profiler captures)')
     return p.parse_args()
@@ -208,7 +210,8 @@ def run_ep(args):
         g = device_bank(torch, gen, dev, epr, 1024, 2048)
         d = device_bank(torch, gen, dev, epr, 2048, 512)
         layers.append(ep.ExpertParallelMoE(None, world, (g[0], g[1], d[0], d[1]), capacity=min(T * world, 8192),
-                                           act_bits=bits, exchange=cfg['exchange'], placement=placement))
+                                           act_bits=bits, exchange=cfg['exchange'], placement=placement,
+                                           combine=args.combine))
     logits = torch.randn((L, T, 256), device=dev, generator=gen) + bias
     x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
     w = torch.empty((L, T, 8), dtype=torch.float32, device=dev)
@@ -265,6 +268,8 @@ def run_ep(args):
                    'experts_per_rank': epr, 'parallelism': f'ep{world}',
                    'placement': ('balanced by routed load of a 4096-token calibration batch'
                                  if args.placement == 'balanced' else 'contiguous ranges'),
+                   'combine': ('per-slot fp32 rows, bit-identical to one GPU' if args.combine == 'exact' else
+                               'per-rank fp32 partial sums, equal to one GPU within fp32 rounding'),
                    'exchange': ('NCCL all_gather of token rows + equal-block all_to_all of fp32 per-slot rows '
                                 '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
                                 'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)')},

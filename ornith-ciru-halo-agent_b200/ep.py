@@ -29,6 +29,14 @@ compute returns the route-ordered [T, 8, 2048] block of each source rank,
 padding slots included, and one all_to_all of equal blocks brings them home;
 the row index of slot s of token t is (owner * T + t) * 8 + s.
 
+Both modes also have a rank-partial combine (combine='partial'): the expert
+rank weights and sums its own slots of each token in slot order (the layer's
+own fp32 combine, before bf16 rounding) and returns one fp32 row per (token,
+rank) instead of one per (token, slot); the home rank adds the ranks' partial
+rows in rank order and rounds to bf16.  The association differs from the
+single-GPU sum, so the result agrees to fp32 rounding (within the north-star
+tolerance) rather than bit for bit, for up to 8x less return traffic.
+
 These collectives are the layer's only exchange.  Every rank takes the same
 collective steps in the same order, zero-sized messages included.
 """
@@ -179,6 +187,44 @@ def ep_layer(group, world, x, ids, weights, compute, combine, placement=None):
     return combine(got, route_row_index(x.shape[0], plan, got.device), weights, ids)
 
 
+def partial_row_index(T, world, token_index, dest, device):
+    """int32 [T, 8] for combine_gathered: column d holds the row of rank d's
+    partial for the token (-1 where the token sent nothing to d); columns
+    >= world are -1.  token_index / dest: token and rank of each returned row,
+    in arrival order."""
+    idx = torch.full((T, TOP), -1, dtype=torch.int32, device=device)
+    idx[token_index, dest] = torch.arange(token_index.numel(), dtype=torch.int32, device=device)
+    return idx
+
+
+def rank_sum(combine, got, row_index, like_weights):
+    """Home-side sum of the ranks' partial rows in rank order, through the
+    slot-ordered combine with unit weights (x * 1 is exact) and the ranks as
+    slots."""
+    ones = torch.ones_like(like_weights)
+    ids = torch.where(row_index >= 0, torch.zeros_like(row_index), torch.full_like(row_index, -1))
+    return combine(got, row_index, ones, ids)
+
+
+def ep_layer_partial(group, world, x, ids, weights, compute_partial, combine, placement=None):
+    """Compact exchange with the rank-partial combine.
+
+    compute_partial(x_recv, ids_recv, w_recv) -> fp32 [n_recv, 2048]: per
+    received token, its routing weights times this rank's projections summed
+    in slot order."""
+    plan = build_dispatch(ids, world, placement)
+    x_recv, ids_recv, recv_counts = exchange_rows(group, world, plan, x)
+    w_send = torch.where(plan.slot_mask, weights[plan.token_index], torch.zeros_like(weights[plan.token_index]))
+    w_recv = torch.empty((sum(recv_counts), TOP), dtype=torch.float32, device=x.device)
+    _a2a(group, w_recv, w_send.contiguous(), recv_counts, plan.send_counts)
+    part = compute_partial(x_recv, ids_recv, w_recv)
+    got = torch.empty((plan.token_index.numel(), H), dtype=torch.float32, device=x.device)
+    _a2a(group, got, part.contiguous(), plan.send_counts, recv_counts)
+    dest = torch.repeat_interleave(torch.arange(world, device=x.device),
+                                   torch.tensor(plan.send_counts, device=x.device), output_size=got.shape[0])
+    return rank_sum(combine, got, partial_row_index(x.shape[0], world, plan.token_index, dest, x.device), weights)
+
+
 def ep_layer_fixed(group, world, x, ids, weights, compute_block, combine, placement=None):
     """One expert-parallel layer call, fixed-size exchange (same T on every rank).
 
@@ -203,6 +249,33 @@ def ep_layer_fixed(group, world, x, ids, weights, compute_block, combine, placem
     return combine(got.view(world * T * TOP, H), row_index.to(torch.int32).contiguous(), weights, ids)
 
 
+def ep_layer_fixed_partial(group, world, x, ids, weights, compute_partial, combine, placement=None):
+    """Fixed-size exchange with the rank-partial combine: one fp32 [T, 2048]
+    block per rank comes home (no host synchronisation)."""
+    T = x.shape[0]
+    placement = placement or contiguous_placement(world, ids.device)
+    owner, lid = map_ids(ids, placement)
+    dest = torch.arange(world, device=ids.device).view(-1, 1, 1)
+    mine = owner.unsqueeze(0) == dest                                                      # [world, T, 8]
+    local = torch.where(mine, lid.unsqueeze(0), torch.full_like(owner.unsqueeze(0), -1)).to(torch.int32).contiguous()
+    w_local = torch.where(mine, weights.unsqueeze(0), torch.zeros_like(weights).unsqueeze(0)).contiguous()
+    x_all = torch.empty((world * T, H // 2), dtype=torch.int32, device=x.device)
+    dist.all_gather_into_tensor(x_all, x.contiguous().view(torch.int32), group=group)
+    ids_all = torch.empty_like(local)
+    dist.all_to_all_single(ids_all, local, group=group)
+    w_all = torch.empty_like(w_local)
+    dist.all_to_all_single(w_all, w_local, group=group)
+    part = compute_partial(x_all.view(x.dtype), ids_all.view(world * T, TOP), w_all.view(world * T, TOP))
+    got = torch.empty_like(part)
+    dist.all_to_all_single(got, part.contiguous(), group=group)    # block d: rank d's partials for my tokens
+    t = torch.arange(T, device=ids.device, dtype=torch.int32).view(-1, 1)
+    d = torch.arange(TOP, device=ids.device, dtype=torch.int32).view(1, -1)
+    has = (mine.any(dim=2).t() if world == TOP else
+           torch.cat([mine.any(dim=2).t(), torch.zeros((T, TOP - world), dtype=torch.bool, device=ids.device)], 1))
+    row_index = torch.where(has, d * T + t, torch.full_like(has, -1, dtype=torch.int32))
+    return rank_sum(combine, got.view(world * T, H), row_index.contiguous(), weights)
+
+
 class ExpertParallelMoE:
     """GPU expert-parallel layer over NCCL with this library's kernels.
 
@@ -212,12 +285,20 @@ class ExpertParallelMoE:
     one rank may receive (world * local tokens at most).  exchange: 'compact'
     (variable splits, any token counts) or 'fixed' (equal blocks, no host
     synchronisation; every rank must call with the same token count).
-    placement: the same on every rank; contiguous ranges by default."""
+    combine: 'exact' (per-slot rows, bit-identical to one GPU) or 'partial'
+    (per-rank partial sums, fp32-rounding agreement).  placement: the same on
+    every rank; contiguous ranges by default."""
 
-    def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact', placement=None):
+    def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact', placement=None,
+                 combine='exact'):
         from . import native
         if exchange not in ('compact', 'fixed'):
             raise ValueError(f'unknown exchange mode {exchange!r}')
+        if combine not in ('exact', 'partial'):
+            raise ValueError(f'unknown combine mode {combine!r}')
+        if combine == 'partial' and world > TOP:
+            raise ValueError('the rank-partial combine supports at most 8 ranks')
+        self.combine_mode = combine
         self.native = native
         self.group, self.world = group, world
         self.banks = banks
@@ -232,14 +313,15 @@ class ExpertParallelMoE:
         self._ones = torch.ones((self.capacity, TOP), dtype=torch.float32, device=dev)
         self._scratch_out = torch.empty((self.capacity, H), dtype=torch.bfloat16, device=dev)
 
-    def _layer(self, x_recv, ids_recv):
+    def _layer(self, x_recv, ids_recv, w_recv=None):
         n = x_recv.shape[0]
         if n > self.capacity:
             raise ValueError(f'expert-parallel receive of {n} rows exceeds capacity {self.capacity}')
         if n:
             native = self.native
             fn = getattr(native.lib(), self.symbol)
-            native.check(fn(*[native.ptr(t) for t in (x_recv.contiguous(), self._ones[:n], ids_recv, *self.banks,
+            w = self._ones[:n] if w_recv is None else w_recv.contiguous()
+            native.check(fn(*[native.ptr(t) for t in (x_recv.contiguous(), w, ids_recv, *self.banks,
                                                       self.workspace)],
                             self.workspace.numel(), native.ptr(self._scratch_out), native.ptr(self.flags), n,
                             self.capacity, native.stream(x_recv)), 'expert-parallel compute')
@@ -258,12 +340,20 @@ class ExpertParallelMoE:
         self.native.scatter_route_rows(self.workspace, n, self.capacity, rows)
         return rows.view(n, TOP, H)
 
+    def compute_partial(self, x_recv, ids_recv, w_recv):
+        n = self._layer(x_recv, ids_recv, w_recv)
+        off = self.layout.final_f32
+        return self.workspace[off:off + n * H * 4].view(torch.float32).view(n, H)
+
     def combine(self, rows, row_index, weights, ids):
         out = torch.empty((ids.shape[0], H), dtype=torch.bfloat16, device=rows.device)
         self.native.combine_gathered(rows, row_index, weights, ids, out, self.flags)
         return out
 
     def __call__(self, x, ids, weights):
+        if self.combine_mode == 'partial':
+            run = ep_layer_fixed_partial if self.exchange == 'fixed' else ep_layer_partial
+            return run(self.group, self.world, x, ids, weights, self.compute_partial, self.combine, self.placement)
         if self.exchange == 'fixed':
             return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine,
                                   self.placement)

@@ -45,6 +45,32 @@ def fake_combine_gathered(rows, row_index, weights, ids):
     return fake_combine(dense.view(T * TOP, H), weights, ids)
 
 
+def fake_partial(x, ids_local, w_local, table):
+    """Slot-ordered weighted sum of one rank's own slots (padding: -1 ids)."""
+    r = fake_rows(x, ids_local, table)
+    out = torch.zeros((x.shape[0], H), dtype=torch.float32)
+    for s in range(TOP):
+        valid = (ids_local[:, s] >= 0).unsqueeze(1)
+        out = torch.where(valid, out + r[:, s] * w_local[:, s:s + 1], out)
+    return out
+
+
+def rank_partial_reference(x, ids, weights, placement, world):
+    """Sum over ranks, in rank order, of each rank's slot-ordered partial."""
+    import __graft_entry__ as g
+    g.load_package()
+    from ornith_b200 import ep
+    owner, lid = ep.map_ids(ids, placement)
+    out = torch.zeros((x.shape[0], H), dtype=torch.float32)
+    for d in range(world):
+        mine = owner == d
+        table = torch.tensor(placement.experts_of(d))
+        part = fake_partial(x, torch.where(mine, lid, torch.full_like(lid, -1)),
+                            torch.where(mine, weights, torch.zeros_like(weights)), table)
+        out = torch.where(mine.any(dim=1, keepdim=True), out + part, out)
+    return out
+
+
 def _port():
     with socket.socket() as s:
         s.bind(('127.0.0.1', 0))
@@ -85,11 +111,23 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
         def compute_block(xa, ia):
             return fake_rows(xa, ia, table)
 
+        def compute_partial(xr, ir, wr):
+            return fake_partial(xr, ir, wr, table) if xr.shape[0] else torch.zeros((0, H))
+
         if mode == 'fixed':
             out = ep.ep_layer_fixed(None, world, x, ids, weights, compute_block, fake_combine_gathered, placement)
-        else:
+        elif mode == 'compact':
             out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered, placement)
-        ref = fake_combine(fake_rows(x, ids, torch.arange(E)).view(T * TOP, H), weights, ids)
+        elif mode == 'fixed_partial':
+            out = ep.ep_layer_fixed_partial(None, world, x, ids, weights, compute_partial, fake_combine_gathered,
+                                            placement)
+        else:
+            out = ep.ep_layer_partial(None, world, x, ids, weights, compute_partial, fake_combine_gathered,
+                                      placement)
+        if mode.endswith('partial'):
+            ref = rank_partial_reference(x, ids, weights, placement, world)
+        else:
+            ref = fake_combine(fake_rows(x, ids, torch.arange(E)).view(T * TOP, H), weights, ids)
         q.put((rank, bool(torch.equal(out, ref)), ''))
         dist.barrier()
         dist.destroy_process_group()
@@ -98,7 +136,7 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
 
 
 @pytest.mark.parametrize('balanced', [False, True])
-@pytest.mark.parametrize('mode', ['compact', 'fixed'])
+@pytest.mark.parametrize('mode', ['compact', 'fixed', 'compact_partial', 'fixed_partial'])
 @pytest.mark.parametrize('world,T', [(2, 16), (4, 9)])
 def test_ep_dispatch_combine_matches_single_rank(world, T, mode, balanced):
     ctx = mp.get_context('spawn')

@@ -31,7 +31,23 @@ def _bank(gen, experts, N, K, dev):
     return codes, meta.view(torch.uint32)
 
 
-def _worker(rank, world, port, T, q, mode, balanced):
+CASES = [  # (exchange, balanced placement, combine)
+    ('compact', False, 'exact'), ('compact', True, 'exact'), ('fixed', False, 'exact'), ('fixed', True, 'exact'),
+    ('compact', True, 'partial'), ('fixed', True, 'partial'),
+]
+
+
+def _close(out, ref):
+    """Rank-partial combine: a different association of the same fp32 sum, so
+    elements with cancellation may differ by more than a bf16 step; the check is
+    the north-star bound (relative L2 <= 1e-3, max-abs <= 2e-2)."""
+    a = out.float()
+    b = ref.float()
+    rel_l2 = float((a - b).norm() / b.norm().clamp_min(1e-30))
+    return rel_l2 <= 1e-3 and float((a - b).abs().max()) <= 2e-2
+
+
+def _worker(rank, world, port, T, q):
     try:
         import datetime
         import torch.distributed as dist
@@ -61,40 +77,48 @@ def _worker(rank, world, port, T, q, mode, balanced):
         native.check(native.lib().ornith_routed_direct_launch(
             *[native.ptr(t) for t in (x, w, ids, gc, gm, dc, dm, ws)], ws.numel(), native.ptr(ref),
             native.ptr(flags), T, T, native.stream(x)), 'reference layer')
-        if balanced:  # any placement must give the same bits; use a skewed-load one
-            placement = ep.balanced_placement(torch.arange(256, dtype=torch.float64).flip(0) ** 2, world, dev)
-        else:
-            placement = ep.contiguous_placement(world, dev)
-        sl = torch.tensor(placement.experts_of(rank), device=dev)
+        results = []
+        for mode, balanced, combine in CASES:
+            if balanced:  # any placement must give the same result; use a skewed-load one
+                placement = ep.balanced_placement(torch.arange(256, dtype=torch.float64).flip(0) ** 2, world, dev)
+            else:
+                placement = ep.contiguous_placement(world, dev)
+            sl = torch.tensor(placement.experts_of(rank), device=dev)
 
-        def pick(bank):  # this rank's experts, in the placement's bank order
-            return bank.view(torch.int32)[sl].contiguous().view(torch.uint32)
+            def pick(bank):  # this rank's experts, in the placement's bank order
+                return bank.view(torch.int32)[sl].contiguous().view(torch.uint32)
 
-        layer = ep.ExpertParallelMoE(None, world, (pick(gc), pick(gm), pick(dc), pick(dm)), capacity=T * world,
-                                     exchange=mode, placement=placement)
-        out = layer(x, ids, w)
-        torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))), int(flags.item()), ''))
+            layer = ep.ExpertParallelMoE(None, world, (pick(gc), pick(gm), pick(dc), pick(dm)), capacity=T * world,
+                                         exchange=mode, placement=placement, combine=combine)
+            out = layer(x, ids, w)
+            torch.cuda.synchronize()
+            ok = (bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))) if combine == 'exact'
+                  else _close(out, ref))
+            results.append(((mode, balanced, combine), ok, int(layer.flags.item())))
+            dist.barrier()
+        q.put((rank, results, int(flags.item()), ''))
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:
-        q.put((rank, False, -1, repr(exc)))
+        q.put((rank, None, -1, repr(exc)))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
-@pytest.mark.parametrize('balanced', [False, True])
-@pytest.mark.parametrize('mode', ['compact', 'fixed'])
 @pytest.mark.parametrize('T', [5, 96])
-def test_expert_parallel_matches_single_gpu(T, mode, balanced):
+def test_expert_parallel_matches_single_gpu(T):
+    """Every exchange mode and placement: bit-identical to the single-GPU layer
+    with the exact combine, within fp32 rounding with the rank-partial one."""
     import torch.multiprocessing as mp
     ctx = mp.get_context('spawn')
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, q, mode, balanced)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = [q.get(timeout=240) for _ in range(2)]
+    results = [q.get(timeout=300) for _ in range(2)]
     for p in procs:
         p.join(timeout=60)
-    for rank, equal, flags, err in results:
-        assert equal and flags == 0, (rank, flags, err)
+    for rank, cases, flags, err in results:
+        assert cases is not None and flags == 0, (rank, flags, err)
+        for case, ok, case_flags in cases:
+            assert ok and case_flags == 0, (rank, case, case_flags)
