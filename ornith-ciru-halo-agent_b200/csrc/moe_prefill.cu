@@ -633,18 +633,45 @@ __global__ __launch_bounds__(256) void prefill_count_kernel(LayerArgs a, int nbl
 
 __global__ __launch_bounds__(1024) void prefill_scan_kernel(LayerArgs a, int nblk) {
     __shared__ int warp_tot[32][2];
+    __shared__ int total[kE];
     const int e = threadIdx.x, lane = e & 31, w = e >> 5;
     const int* bc = ws_at<int32_t>(a, a.L.pblock);
     int* bb = ws_at<int32_t>(a, a.L.pblock) + size_t(kPlanBlocks) * (kE + 1);
-    int c = 0;
-    if (e < kE) {
-        for (int blk = 0; blk < nblk; ++blk) {
-            bb[size_t(blk) * (kE + 1) + e] = c;  // this block's base inside expert e's run
-            c += bc[size_t(blk) * (kE + 1) + e];
+    // Per-block bases inside each expert's run: warp w takes experts w, w+32,
+    // ...; lane l holds the counts of blocks 8l..8l+7 (all loaded before use),
+    // a serial prefix over those and a warp scan over the lanes.
+    static_assert(kPlanBlocks == 256, "eight blocks per lane");
+    for (int ex = w; ex < kE; ex += 32) {
+        int v[8], run = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int blk = 8 * lane + k;
+            v[k] = blk < nblk ? bc[size_t(blk) * (kE + 1) + ex] : 0;
         }
-    } else if (e == kE) {
-        c = a.shared ? a.T : 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c0 = run;
+            run += v[k];
+            v[k] = c0;
+        }
+        int incl = run;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += u;
+        }
+        const int base = incl - run;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int blk = 8 * lane + k;
+            if (blk < nblk) bb[size_t(blk) * (kE + 1) + ex] = base + v[k];
+        }
+        if (lane == 31) total[ex] = incl;
     }
+    __syncthreads();
+    int c = 0;
+    if (e < kE) c = total[e];
+    else if (e == kE) c = a.shared ? a.T : 0;
     const int t = e <= kE ? (c + kMT - 1) / kMT : 0;
     // exclusive scans of counts and tile counts over the 257 slots
     int ic = c, it = t;
