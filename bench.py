@@ -64,6 +64,12 @@ CONFIGS = {
     'ep_prefill8192': dict(T=8192, layers=4, bias=0.0, act_bits=4, shared=False, ep=True, exchange='compact',
                            name='expert-parallel prefill 8192 tokens, Zipf(1.2) expert skew (configs[4]); '
                                 '4 weight sets cycled'),
+    # dense G256 projection (the next row after the MoE layer): QKVZ-shaped
+    # 12288 x 2048 banks, 40 of them so that weights stream from HBM
+    'dense_qkvz1': dict(T=1, layers=40, N=12288, K=2048, dense=True,
+                        name='dense G256 A8 projection N12288 x K2048, 1 row, 40 banks'),
+    'dense_qkvz16': dict(T=16, layers=40, N=12288, K=2048, dense=True,
+                         name='dense G256 A8 projection N12288 x K2048, 16 rows, 40 banks'),
 }
 
 
@@ -282,6 +288,118 @@ def run_ep(args):
     dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def run_dense(args):
+    """Dense G256 projections (ornith_dense_g256_launch, N16 banks): one step =
+    the step's rows through 40 independent banks, captured as one CUDA graph.
+    Roofline: the algorithmic bytes of one launch (codes N*K/2, metadata
+    N*K/64, bf16 rows in and out, the fp32 diagnostic row out) over its
+    CUDA-event time."""
+    import torch
+    cfg = dict(CONFIGS[args.config])
+    if args.layers:
+        cfg['layers'] = args.layers
+    dev = torch.device('cuda', 0)
+    torch.cuda.set_device(dev)
+    graft.load_package()
+    import importlib
+    native = importlib.import_module('ornith_b200.native')
+    lib = native.lib()
+    M, L, N, K = cfg['T'], cfg['layers'], cfg['N'], cfg['K']
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(777)
+    banks = []
+    for _ in range(L):
+        codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (N // 16, K // 256, 32, 16), dtype=torch.int32, device=dev,
+                              generator=gen).view(torch.uint32)
+        z = torch.randn((N // 16, K // 256, 16), device=dev, generator=gen)
+        scale = (0.01 * z.abs()).to(torch.float16).clamp_min(2 ** -14)
+        offset = (scale.float() * -8.0).to(torch.float16)
+        meta = ((scale.view(torch.int16).to(torch.int32) & 0xFFFF) |
+                (offset.view(torch.int16).to(torch.int32) << 16)).view(torch.uint32)
+        banks.append((codes, meta))
+    x = torch.randn((M, K), device=dev, generator=gen).to(torch.bfloat16)
+    outs = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    ws = torch.empty(native.dense_workspace_bytes(M, [(N, K)]), dtype=torch.uint8, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def call(l):
+        native.dense_out(x, banks[l][0], banks[l][1], ws, outs[l % 2], flags, M, N, K, 2, M)
+
+    def step():
+        for l in range(L):
+            call(l)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    launches = launches_per_step(lib, step) * args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    # one launch (quantisation + projection) timed alone, banks in sequence
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    per = []
+    for _ in range(3):
+        for l in range(L):
+            ev[l][0].record()
+            call(l)
+            ev[l][1].record()
+        torch.cuda.synchronize()
+        per += [a.elapsed_time(b) for a, b in ev]
+    launch_ms = statistics.mean(per)
+    algo = N * K // 2 + N * (K // 256) * 4 + M * K * 2 + M * N * 2 + M * N * 4
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    peak = peaks.get('hbm_gbs', 6650.0)
+    achieved = algo / (launch_ms * 1e-3) / 1e9
+    # end to end through the operator: pinned rows in, last output out
+    pin_x = x.cpu().pin_memory()
+    pin_out = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        x.copy_(pin_x, non_blocking=True)
+        graph.replay()
+        pin_out.copy_(outs[(L - 1) % 2], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    print(json.dumps({
+        'metric': 'dense G256 projection rows/s (40-bank step) & % of HBM roofline', 'value': round(
+            M * L * args.steps / (ms / 1e3), 3), 'unit': 'row-projections/s', 'n_gpus': 1, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': round(ms / args.steps, 4), 'higher_is_better': True,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8', 'data': 'synthetic (seeded random banks)',
+        'config': {'workload': cfg['name'], 'rows': M, 'N': N, 'K': K, 'banks': L,
+                   'l2': f'inputs larger than L2: {L * algo / 1e6:.0f} MB per step'},
+        'e2e': {'value': round(M * L * args.steps / (e2e_ms / 1e3), 3), 'unit': 'row-projections/s',
+                'h2d_bytes_per_step': M * K * 2, 'd2h_bytes_per_step': M * N * 2},
+        'gpu_launches': int(launches),
+        'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
+                     'frac': round(achieved / peak, 4), 'traffic': None,
+                     'kernel': 'one dense launch (dense_quant_kernel + dense_project_kernel<16>)',
+                     'algorithmic_bytes_per_launch': algo, 'launch_ms': round(launch_ms, 5),
+                     'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'},
+        'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': True,
+    }), flush=True)
 
 
 def launches_per_step(lib, step_fn):
@@ -574,6 +692,8 @@ def run_reference(args):
     if not O.reference_available():
         print(json.dumps({'impl': 'reference', 'unavailable': 'oracle/_ref was not built (needs the reference checkout)'}))
         return
+    if cfg.get('dense'):
+        return run_reference_dense(args, cfg, O)
     S, layer = _cpu_layer()
     tab = np.load(ROOT / 'tests' / 'golden' / 'shared_math_tables.npz')
     rng = np.random.default_rng(10)
@@ -616,11 +736,47 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_reference_dense(args, cfg, O):
+    """The reference's dense library compiled for the CPU (oracle/_ref), one
+    bank per call, scaled to the 40-bank step."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('ornith_synthetic', ROOT / 'ornith-ciru-halo-agent_b200' / 'synthetic.py')
+    S = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(S)
+    rng = np.random.default_rng(10)
+    M, N, K, L = cfg['T'], cfg['N'], cfg['K'], cfg['layers']
+    codes, meta = S.make_dense_bank(rng, N, K)
+    x = S.make_rows(rng, M, K)
+    calls = 4
+    for _ in range(args.warmup):
+        O.ref_dense(x, codes, meta, N, K)
+    t0 = time.perf_counter()
+    for _ in range(args.steps * calls):
+        O.ref_dense(x, codes, meta, N, K)
+    el = time.perf_counter() - t0
+    call_s = el / (args.steps * calls)
+    value = M / call_s
+    sample = f'{calls} calls per step of one {N}x{K} bank, {M} rows (reference dense source compiled for the CPU)'
+    print(json.dumps({
+        'impl': 'reference', 'metric': 'dense G256 projection rows/s (40-bank step) & % of HBM roofline',
+        'value': round(value, 4), 'unit': 'row-projections/s', 'n_gpus': 0, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': round(call_s * L * 1e3, 3), 'higher_is_better': True,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8', 'data': 'synthetic',
+        'config': {'workload': cfg['name'], 'rows': M},
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'row-projections/s', 'cores': os.cpu_count() or 1,
+                         'kind': 'reference', 'sample': sample},
+        'e2e': {'value': round(value, 4), 'unit': 'row-projections/s', 'h2d_bytes_per_step': 0,
+                'd2h_bytes_per_step': 0},
+    }), flush=True)
+
+
 if __name__ == '__main__':
     a = parse()
     if a.impl == 'reference':
         run_reference(a)
     elif CONFIGS[a.config].get('ep'):
         run_ep(a)
+    elif CONFIGS[a.config].get('dense'):
+        run_dense(a)
     else:
         run(a)

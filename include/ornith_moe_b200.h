@@ -241,6 +241,73 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_repack_n16_to_n32(
     const void* codes_n16, const void* meta_n16, void* codes_n32, void* meta_n32,
     int experts, int N, int K, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Dense G256 projections (Ornith's dense layers): drop-in for the reference's
+ * dense library (kernels/dense_n32/dense_g256_api.h, dense_g256_consumer.cpp),
+ * same symbols, arguments and return codes.  Shapes: N a positive multiple of
+ * 16, at most 12288 (or exactly 248320); K a positive multiple of 256, at most
+ * 8192; 0 <= M <= Mcap <= 8192; bits 8; transform 128.
+ * Banks: codes U32[N/16][K/256][32][16] (word j of group g for column n holds
+ * k = 256g + 8j + d in bits 4d), metadata U32[N/16][K/256][16] = fp16 scale
+ * (low half) | fp16 offset (high half); the N32 entry takes the N32 shadow
+ * U32[N/32][K/256][32][32] / [N/32][K/256][32] (plugin-site/ornith_g256/
+ * dense_n32.py:30-31).  Arithmetic: bf16 -> fp32, H128 x 0x3db504f3, A8 per
+ * 256-group, exact integer dots, per column over ascending groups
+ * value += w_scale*(sa*dot) + w_offset*(sa*sum) without FMA, bf16 RNE.
+ * Flags (sticky, dense_g256_api.h:14-19): 1 non-finite transform input or
+ * output, 2 invalid activation, 4 non-finite projection, 8 bf16 with an
+ * all-ones exponent.  M == 0 returns success without touching a pointer
+ * (the N32 entry rejects it, as the reference does).  Alignment: input 16 B
+ * (the reference asks 2), workspace 256 B, codes, metadata and flags 4 B,
+ * output 2 B; workspace, output and flags must not overlap any other buffer.
+ * ------------------------------------------------------------------------ */
+
+/* Same 7 size_t fields as the reference (dense_g256_api.h:11-13,
+ * native.py:11-13).  Here `low` is the int8 activations [Mcap,K], `scales`
+ * fp16 [Mcap,K/256], `sums` int32 [Mcap,K/256], `projection` the fp32
+ * diagnostic [Mcap,N]; `transformed` and `high` hold SIZE_MAX. */
+typedef struct OrnithDenseG256Layout {
+    size_t workspace_bytes, transformed, low, high, scales, sums, projection;
+} OrnithDenseG256Layout;
+
+/* Replaces ornith_dense_g256_abi_version (dense_g256_api.h:45).  Returns 1. */
+ORNITH_MOE_B200_EXPORT uint32_t ornith_dense_g256_abi_version(void);
+
+/* Replaces ornith_dense_g256_get_layout (dense_g256_api.h:46,
+ * dense_g256_consumer.cpp:162-171). */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_dense_g256_get_layout(int Mcap, int N, int K, int bits,
+                                                                 OrnithDenseG256Layout* out);
+
+/* Replaces ornith_dense_g256_launch (dense_g256_api.h:47-50,
+ * dense_g256_consumer.cpp:172-190): input bf16 [M,K] -> output bf16 [M,N]
+ * from an N16 bank.  geometry 0, 1 or 2 is accepted and gives identical
+ * results (the reference's WMMA/compact job shapes). */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_dense_g256_launch(
+    const void* input_bf16, const void* codes, const void* metadata,
+    void* workspace, size_t workspace_bytes, void* output_bf16, void* flags_u32,
+    int M, int Mcap, int N, int K, int bits, int transform, int geometry, cudaStream_t stream);
+
+/* Replaces ornith_dense_g256_launch_n32 (dense_g256_consumer.cpp:360-379):
+ * the same projection from the N32 shadow bank, 1 <= M <= 16, N a multiple
+ * of 32, geometry 2. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_dense_g256_launch_n32(
+    const void* input_bf16, const void* codes, const void* metadata,
+    void* workspace, size_t workspace_bytes, void* output_bf16, void* flags_u32,
+    int M, int Mcap, int N, int K, int bits, int transform, int geometry, cudaStream_t stream);
+
+/* Replaces ornith_dense_g256_n32_rows (dense_g256_consumer.cpp:380): 16. */
+ORNITH_MOE_B200_EXPORT int ornith_dense_g256_n32_rows(void);
+
+/* Replaces ornith_dense_g256_prepare_bf16 (dense_g256_api.h:51-59,
+ * dense_g256_consumer.cpp:231-247): transformed bf16 [M,K] = bf16(H128(x))
+ * and weights bf16 [N,K] = bf16(scale*code + offset) from the N16 bank, for a
+ * caller-side bf16 GEMM transformed @ weights^T (the reference's prefill path,
+ * native.py:138-149).  No workspace.  Alignment 16 B for input, codes,
+ * transformed and weights. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_dense_g256_prepare_bf16(
+    const void* input_bf16, const void* codes, const void* metadata,
+    void* transformed_bf16, void* weights_bf16, void* flags_u32, int M, int N, int K, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

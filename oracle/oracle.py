@@ -249,3 +249,85 @@ def ref_routed_shared(x_bits, weights, ids, gate_codes, gate_meta, down_codes, d
             *[_p(t) for t in tables], _p(ws), C.c_size_t(ws.size), _p(out), _p(shared), _p(flags),
             C.c_int(T), C.c_int(Tcap), None)
     return out, shared, int(flags[0]), st
+
+
+# ---------------------------------------------------------------------------
+# Dense G256 projection (kernels/dense_n32/, dense_g256_api.h:20-38)
+# ---------------------------------------------------------------------------
+
+def dense_project(x_bits, codes, meta, N, K, width=16):
+    """A8 dense projection of bf16 rows x [M,K] by a bank stored `width` (16 or 32)
+    columns per tile.  Returns (out bf16 bits [M,N], fp32 values [M,N], flags)."""
+    x_bits = _c(x_bits, np.uint16).reshape(-1, K)
+    M = x_bits.shape[0]
+    out = np.zeros((M, N), np.uint16)
+    diag = np.zeros((M, N), np.float32)
+    flags = np.zeros(1, np.uint32)
+    lib().orc_dense_project(_p(x_bits), C.c_int(M), C.c_int(N), C.c_int(K), C.c_int(width),
+                            _p(_c(codes, np.uint32)), _p(_c(meta, np.uint32)), _p(out), _p(diag), _p(flags))
+    return out, diag, int(flags[0])
+
+
+def dense_prepare_bf16(x_bits, codes16, meta16, N, K):
+    """Prefill preparation: (bf16 H128(x) [M,K], bf16 dequantised W [N,K], flags)."""
+    x_bits = _c(x_bits, np.uint16).reshape(-1, K)
+    M = x_bits.shape[0]
+    xt = np.zeros((M, K), np.uint16)
+    w = np.zeros((N, K), np.uint16)
+    flags = np.zeros(1, np.uint32)
+    lib().orc_dense_prepare_bf16(_p(x_bits), C.c_int(M), C.c_int(N), C.c_int(K),
+                                 _p(_c(codes16, np.uint32)), _p(_c(meta16, np.uint32)), _p(xt), _p(w), _p(flags))
+    return xt, w, int(flags[0])
+
+
+def _aligned_bytes(n, alignment=256):
+    """Zeroed uint8 buffer of n bytes starting on an `alignment`-byte boundary."""
+    raw = np.zeros(n + alignment, np.uint8)
+    skip = (-raw.ctypes.data) % alignment
+    return raw[skip:skip + n]
+
+
+class DenseLayout(C.Structure):
+    """OrnithDenseG256Layout, kernels/dense_n32/dense_g256_api.h:11-13."""
+    _fields_ = [(n, C.c_size_t) for n in
+                ('workspace_bytes', 'transformed', 'low', 'high', 'scales', 'sums', 'projection')]
+
+
+def ref_dense(x_bits, codes, meta, N, K, entry='ornith_dense_g256_launch', geometry=2, Mcap=None):
+    """A dense launch of the compiled reference (N16 bank for ornith_dense_g256_launch,
+    N32 bank for ornith_dense_g256_launch_n32).  Returns (out, fp32 projection, flags, status)."""
+    L = ref_lib('dense_n32')
+    x_bits = _c(x_bits, np.uint16).reshape(-1, K)
+    M = x_bits.shape[0]
+    Mcap = M if Mcap is None else Mcap
+    layout = DenseLayout()
+    L.ornith_dense_g256_get_layout.restype = C.c_int
+    st = L.ornith_dense_g256_get_layout(C.c_int(Mcap), C.c_int(N), C.c_int(K), C.c_int(8), C.byref(layout))
+    if st:
+        return None, None, None, st
+    ws = _aligned_bytes(max(layout.workspace_bytes, 256))
+    out = np.zeros((max(M, 1), N), np.uint16)
+    flags = np.zeros(1, np.uint32)
+    fn = getattr(L, entry)
+    fn.restype = C.c_int
+    st = fn(_p(x_bits), _p(_c(codes, np.uint32)), _p(_c(meta, np.uint32)), _p(ws), C.c_size_t(ws.size),
+            _p(out), _p(flags), C.c_int(M), C.c_int(Mcap), C.c_int(N), C.c_int(K), C.c_int(8), C.c_int(128),
+            C.c_int(geometry), None)
+    if st:
+        return None, None, int(flags[0]), st
+    proj = ws[layout.projection:layout.projection + M * N * 4].view(np.float32).reshape(M, N).copy()
+    return out[:M], proj, int(flags[0]), st
+
+
+def ref_dense_prepare_bf16(x_bits, codes16, meta16, N, K):
+    L = ref_lib('dense_n32')
+    x_bits = _c(x_bits, np.uint16).reshape(-1, K)
+    M = x_bits.shape[0]
+    xt = np.zeros((M, K), np.uint16)
+    w = np.zeros((N, K), np.uint16)
+    flags = np.zeros(1, np.uint32)
+    fn = L.ornith_dense_g256_prepare_bf16
+    fn.restype = C.c_int
+    st = fn(_p(x_bits), _p(_c(codes16, np.uint32)), _p(_c(meta16, np.uint32)), _p(xt), _p(w), _p(flags),
+            C.c_int(M), C.c_int(N), C.c_int(K), None)
+    return xt, w, int(flags[0]), st

@@ -646,6 +646,139 @@ void orc_repack_n16_to_n32(const uint32_t* codes16, const uint32_t* meta16, int 
             }
 }
 
+/* ------------------------------------------------------------------------
+ * Dense G256 projection (the reference's dense-layer library,
+ * kernels/dense_n32/dense_g256_api.h:20-38 and dense_g256_consumer.cpp).
+ * Dense flag bits (dense_g256_api.h:14-19): 1 non-finite transform input or
+ * output, 2 invalid activation, 4 non-finite projection, 8 non-finite bf16. */
+enum { ORC_DENSE_NONFINITE_BF16 = 8, ORC_DENSE_NONFINITE_PROJ = 4 };
+
+/* Column n, group g, word j of a dense bank stored `width` columns per tile
+ * (16: codes U32[N/16][K/256][32][16], dense_g256_api.h:27; 32: the N32 shadow
+ * U32[N/32][K/256][32][32], dense_n32.py:30-31). */
+static size_t dense_code_at(int width, int groups, int n, int g, int j) {
+    return (((size_t)(n / width) * groups + g) * 32 + j) * width + (n % width);
+}
+static size_t dense_meta_at(int width, int groups, int n, int g) {
+    return ((size_t)(n / width) * groups + g) * width + (n % width);
+}
+
+/* store() of dense_g256_consumer.cpp:74-79: flag 4 for a non-finite fp32
+ * value, bf16 RNE, flag 8 when the bf16 exponent is all ones. */
+static uint16_t dense_store(float v, uint32_t* f) {
+    if (!isfinite(v)) *f |= ORC_DENSE_NONFINITE_PROJ;
+    uint16_t r = orc_bf16_rne(v);
+    if ((r & 0x7f80u) == 0x7f80u) *f |= ORC_DENSE_NONFINITE_BF16;
+    return r;
+}
+
+/* A8 dense projection out[M,N] = bf16(x[M,K] . W[N,K]^T) in the reference's
+ * arithmetic: per row, bf16 -> fp32, H128 per 128-block (flag 1 on non-finite
+ * input or output, transform :27-39), A8 quantisation per 256-group (quantize
+ * :41-73, flag 2), then per column over ascending groups
+ *   value = value + (w_scale*(sa*dot) + w_offset*(sa*sum))
+ * (compact_projection :116-142, wmma_projection :80-115, compact_projection_n32
+ * :250-272, compact_projection_n32_rows :325-358 all compute this sequence),
+ * stored through dense_store.  diag (may be NULL) receives the fp32 values. */
+void orc_dense_project(const uint16_t* x, int M, int N, int K, int width,
+                       const uint32_t* codes, const uint32_t* meta,
+                       uint16_t* out, float* diag, uint32_t* flags) {
+    const int groups = K / ORC_G;
+    float* y = (float*)malloc(sizeof(float) * (size_t)M * K);
+    int8_t* q = (int8_t*)malloc((size_t)M * K);
+    uint16_t* sc = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)M * groups);
+    int32_t* sums = (int32_t*)malloc(sizeof(int32_t) * (size_t)M * groups);
+    uint32_t f = 0;
+    for (int r = 0; r < M; ++r)
+        for (int b = 0; b < K / 128; ++b) {
+            float in[128];
+            for (int l = 0; l < 128; ++l) {
+                in[l] = orc_bf16_to_f32(x[(size_t)r * K + b * 128 + l]);
+                if (!isfinite(in[l])) f |= ORC_FLAG_NONFINITE_INPUT;
+            }
+            float* o = y + (size_t)r * K + b * 128;
+            orc_wht128(in, o);
+            for (int l = 0; l < 128; ++l) if (!isfinite(o[l])) f |= ORC_FLAG_NONFINITE_INPUT;
+        }
+    orc_quantize_rows(y, M, K, 1, q, sc, sums, &f);
+#pragma omp parallel for reduction(| : f) schedule(static)
+    for (int n = 0; n < N; ++n) {
+        int8_t wc[ORC_G];
+        float* acc = (float*)calloc((size_t)M, sizeof(float));
+        for (int g = 0; g < groups; ++g) {
+            for (int j = 0; j < 32; ++j) {
+                uint32_t w = codes[dense_code_at(width, groups, n, g, j)];
+                for (int d = 0; d < 8; ++d) wc[j * 8 + d] = (int8_t)((w >> (4 * d)) & 15u);
+            }
+            uint32_t mt = meta[dense_meta_at(width, groups, n, g)];
+            float sw = orc_half_to_f32((uint16_t)(mt & 0xffffu)), off = orc_half_to_f32((uint16_t)(mt >> 16));
+            for (int r = 0; r < M; ++r) {
+                const int8_t* qa = q + (size_t)r * K + (size_t)g * ORC_G;
+                int32_t dot = 0;
+                for (int k = 0; k < ORC_G; ++k) dot += (int32_t)wc[k] * (int32_t)qa[k];
+                float sa = orc_half_to_f32(sc[(size_t)r * groups + g]);
+                float scaled_dot = sa * (float)dot, scaled_sum = sa * (float)sums[(size_t)r * groups + g];
+                float product = sw * scaled_dot, correction = off * scaled_sum;
+                acc[r] = acc[r] + (product + correction);
+            }
+        }
+        for (int r = 0; r < M; ++r) {
+            uint32_t lf = 0;
+            out[(size_t)r * N + n] = dense_store(acc[r], &lf);
+            if (diag) diag[(size_t)r * N + n] = acc[r];
+            f |= lf;
+        }
+        free(acc);
+    }
+    *flags |= f;
+    free(y);
+    free(q);
+    free(sc);
+    free(sums);
+}
+
+/* Prefill preparation (ornith_dense_g256_prepare_bf16, dense_g256_consumer.cpp
+ * :192-247): xt[M,K] = bf16(H128(x)) with flag 1 on non-finite input/output
+ * and flag 8 on a bf16 with all-ones exponent; w[N,K] = bf16(scale*code +
+ * offset) from the N16 bank (fp32 product, then sum), flag 8 likewise. */
+void orc_dense_prepare_bf16(const uint16_t* x, int M, int N, int K,
+                            const uint32_t* codes16, const uint32_t* meta16,
+                            uint16_t* xt, uint16_t* w, uint32_t* flags) {
+    const int groups = K / ORC_G;
+    uint32_t f = 0;
+    for (int r = 0; r < M; ++r)
+        for (int b = 0; b < K / 128; ++b) {
+            float in[128], o[128];
+            for (int l = 0; l < 128; ++l) {
+                in[l] = orc_bf16_to_f32(x[(size_t)r * K + b * 128 + l]);
+                if (!isfinite(in[l])) f |= ORC_FLAG_NONFINITE_INPUT;
+            }
+            orc_wht128(in, o);
+            for (int l = 0; l < 128; ++l) {
+                if (!isfinite(o[l])) f |= ORC_FLAG_NONFINITE_INPUT;
+                uint16_t h = orc_bf16_rne(o[l]);
+                if ((h & 0x7f80u) == 0x7f80u) f |= ORC_DENSE_NONFINITE_BF16;
+                xt[(size_t)r * K + b * 128 + l] = h;
+            }
+        }
+#pragma omp parallel for reduction(| : f) schedule(static)
+    for (int n = 0; n < N; ++n)
+        for (int g = 0; g < groups; ++g) {
+            uint32_t mt = meta16[dense_meta_at(16, groups, n, g)];
+            float sw = orc_half_to_f32((uint16_t)(mt & 0xffffu)), off = orc_half_to_f32((uint16_t)(mt >> 16));
+            for (int j = 0; j < 32; ++j) {
+                uint32_t code = codes16[dense_code_at(16, groups, n, g, j)];
+                for (int d = 0; d < 8; ++d) {
+                    float v = sw * (float)((code >> (4 * d)) & 15u) + off;
+                    uint16_t h = orc_bf16_rne(v);
+                    if ((h & 0x7f80u) == 0x7f80u) f |= ORC_DENSE_NONFINITE_BF16;
+                    w[(size_t)n * K + (size_t)g * ORC_G + j * 8 + d] = h;
+                }
+            }
+        }
+    *flags |= f;
+}
+
 int orc_set_threads(int n) {
 #ifdef _OPENMP
     if (n > 0) omp_set_num_threads(n);

@@ -10,7 +10,10 @@ Mirrors the reference plugin's binding (plugin-site/ornith_g256/native.py):
   * `ornith_b200::routed_shared_out` is the fused shared-slot launch that
     moe_shared.py:130-174 drives;
   * `ornith_b200::routed_from_logits` is the north-star operator (hidden
-    states + router logits -> combined hidden states).
+    states + router logits -> combined hidden states);
+  * `ornith_b200::dense_out` has the arguments and the A8 / bf16-prefill
+    split of `ornith_g256::dense_out` (native.py:121-153), and
+    `dense_n32_out` is the one-row N32 shadow launch of dense_n32.py:45-53.
 All launches go to the caller's current CUDA stream.  There is no CPU
 fallback: every operator raises if the CUDA library is missing.
 """
@@ -35,6 +38,13 @@ class RoutedLayout(C.Structure):
                  'down_scales', 'down_sums', 'route_out', 'final_f32')]
 
 
+class DenseLayout(C.Structure):
+    """OrnithDenseG256Layout (include/ornith_moe_b200.h; reference native.py:11-13)."""
+    _fields_ = [(n, C.c_size_t) for n in
+                ('workspace_bytes', 'transformed', 'low', 'high', 'scales', 'sums', 'projection')]
+
+
+_DENSE_ARGS = [C.c_void_p] * 4 + [C.c_size_t] + [C.c_void_p] * 2 + [C.c_int] * 7 + [C.c_void_p]
 _LAUNCH_ARGS = [C.c_void_p] * 8 + [C.c_size_t] + [C.c_void_p] * 2 + [C.c_int] * 2 + [C.c_void_p]
 SIGNATURES = {
     'ornith_routed_direct_get_layout': ([C.c_int, C.POINTER(RoutedLayout)], C.c_int),
@@ -64,6 +74,12 @@ SIGNATURES = {
                                            C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
+    'ornith_dense_g256_abi_version': ([], C.c_uint32),
+    'ornith_dense_g256_get_layout': ([C.c_int] * 4 + [C.POINTER(DenseLayout)], C.c_int),
+    'ornith_dense_g256_launch': (_DENSE_ARGS, C.c_int),
+    'ornith_dense_g256_launch_n32': (_DENSE_ARGS, C.c_int),
+    'ornith_dense_g256_n32_rows': ([], C.c_int),
+    'ornith_dense_g256_prepare_bf16': ([C.c_void_p] * 6 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
 }
 
 
@@ -341,3 +357,83 @@ def repack_n16_to_n32(codes16, meta16, N, K):
     check(lib().ornith_moe_b200_repack_n16_to_n32(ptr(codes16.contiguous()), ptr(meta16.contiguous()),
                                                   ptr(codes32), ptr(meta32), e, N, K, stream(codes16)), 'repack')
     return codes32, meta32
+
+
+# ---------------------------------------------------------------------------
+# Dense G256 projections (reference native.py:121-153, dense_n32.py:37-53)
+# ---------------------------------------------------------------------------
+
+def dense_get_layout(capacity, n, k):
+    layout = DenseLayout()
+    check(lib().ornith_dense_g256_get_layout(capacity, n, k, 8, C.byref(layout)), 'dense layout')
+    return layout
+
+
+def dense_workspace_bytes(capacity, shapes):
+    """Arena bytes for dense calls of up to `capacity` rows over (n, k) shapes:
+    the A8 workspace, or the bf16 prefill buffers [capacity,k] + [n,k]
+    (native.py:87-91)."""
+    sizes = []
+    for n, k in shapes:
+        sizes.append(dense_get_layout(capacity, n, k).workspace_bytes)
+        sizes.append((capacity * k + n * k) * 2)
+    return max(sizes)
+
+
+def _dense_impl(x, codes, metadata, workspace, out, flags, capacity, n, k, geometry, a8_max_rows):
+    validate(x, out, capacity, k)
+    if out.shape != (x.shape[0], n):
+        raise ValueError('Native G256 dense output must be [M, N]')
+    if x.shape[0] > a8_max_rows:
+        # bf16 prefill: transformed x and dequantised W in the arena, then a bf16 GEMM
+        weight_offset = capacity * k * 2
+        if workspace.numel() < weight_offset + n * k * 2:
+            raise ValueError('G256 dense workspace too small for the bf16 prefill path')
+        transformed = workspace[:x.shape[0] * k * 2].view(torch.bfloat16).view(x.shape[0], k)
+        weight = workspace[weight_offset:weight_offset + n * k * 2].view(torch.bfloat16).view(n, k)
+        check(lib().ornith_dense_g256_prepare_bf16(ptr(x), ptr(codes), ptr(metadata), ptr(transformed),
+                                                    ptr(weight), ptr(flags), x.shape[0], n, k, stream(x)),
+              'G256 BF16 prefill preparation')
+        torch.mm(transformed, weight.t(), out=out)
+        return
+    check(lib().ornith_dense_g256_launch(ptr(x), ptr(codes), ptr(metadata), ptr(workspace), workspace.numel(),
+                                         ptr(out), ptr(flags), x.shape[0], capacity, n, k, 8, 128, geometry,
+                                         stream(x)), 'G256 dense')
+
+
+@torch.library.custom_op('ornith_b200::dense_out', mutates_args={'workspace', 'out', 'flags'}, device_types='cuda')
+def dense_out(x: torch.Tensor, codes: torch.Tensor, metadata: torch.Tensor,
+              workspace: torch.Tensor, out: torch.Tensor, flags: torch.Tensor,
+              capacity: int, n: int, k: int, geometry: int, a8_max_rows: int) -> None:
+    """out[M,n] = x[M,k] projected by an N16 G256 bank: A8 for M <= a8_max_rows,
+    else the bf16 prefill path; mixed batches follow the phase segments."""
+    if _PHASE_SEGMENTS and x.shape[0] >= _PHASE_SEGMENTS[-1][1]:
+        for start, end, prefill in _PHASE_SEGMENTS:
+            _dense_impl(x[start:end], codes, metadata, workspace, out[start:end], flags,
+                        capacity, n, k, geometry, 0 if prefill else capacity)
+        end = _PHASE_SEGMENTS[-1][1]
+        if end < x.shape[0]:
+            _dense_impl(x[end:], codes, metadata, workspace, out[end:], flags, capacity, n, k, geometry, 0)
+        return
+    _dense_impl(x, codes, metadata, workspace, out, flags, capacity, n, k, geometry, a8_max_rows)
+
+
+@dense_out.register_fake
+def _dense_fake(x, codes, metadata, workspace, out, flags, capacity, n, k, geometry, a8_max_rows):
+    return None
+
+
+def dense_n32_out(x, codes32, metadata32, workspace, out, flags, capacity, n, k):
+    """A8 projection of 1..16 rows from an N32 shadow bank (dense_n32.py:45-53)."""
+    validate(x, out, capacity, k)
+    check(lib().ornith_dense_g256_launch_n32(ptr(x), ptr(codes32), ptr(metadata32), ptr(workspace),
+                                             workspace.numel(), ptr(out), ptr(flags), x.shape[0], capacity,
+                                             n, k, 8, 128, 2, stream(x)), 'G256 dense N32')
+
+
+def dense_n32_shadow(codes, metadata, n, k):
+    """N32 shadow of an N16 dense bank on the device (dense_n32.py:30-31),
+    through the repack kernel with one bank."""
+    codes32, meta32 = repack_n16_to_n32(codes.reshape(1, n // 16, k // 256, 32, 16),
+                                        metadata.reshape(1, n // 16, k // 256, 16), n, k)
+    return codes32[0], meta32[0]

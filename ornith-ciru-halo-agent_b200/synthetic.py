@@ -52,6 +52,23 @@ def make_bank(rng, experts, N, K):
     return codes, meta
 
 
+def make_dense_bank(rng, N, K):
+    """One dense G256 bank in the reference's N16 storage (dense_g256_api.h:27-29):
+    codes uint32 [N/16, K/256, 32, 16], metadata uint32 [N/16, K/256, 16], with
+    the value distribution of make_bank.  Draw order: codes, then scales."""
+    codes = rng.integers(0, 2 ** 32, size=(N // 16, K // G, 32, 16), dtype=np.uint32)
+    z = rng.standard_normal((N // 16, K // G, 16), dtype=np.float32)
+    scale = np.maximum((np.float32(0.01) * np.abs(z)).astype(np.float16), np.float16(2 ** -14))
+    offset = (scale.astype(np.float32) * np.float32(-8.0)).astype(np.float16)
+    meta = scale.view(np.uint16).astype(np.uint32) | (offset.view(np.uint16).astype(np.uint32) << 16)
+    return codes, meta
+
+
+def make_rows(rng, M, K):
+    """bf16 bits of x ~ N(0,1) [M, K]."""
+    return f32_to_bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+
+
 @dataclass
 class LayerWeights:
     gate_codes: np.ndarray   # [E, 32, 8, 32, 32]

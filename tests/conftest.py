@@ -40,6 +40,11 @@ def golden():
 
 
 @pytest.fixture(scope='session')
+def dense_golden():
+    return np.load(GOLDEN / 'dense_reference_outputs.npz')
+
+
+@pytest.fixture(scope='session')
 def tables():
     return np.load(GOLDEN / 'shared_math_tables.npz')
 

@@ -4,6 +4,11 @@
       The reference's pinned SiLU fp32 / sigmoid bf16 tables for every bf16
       bit pattern (native/shared_math_reference.safetensors), copied after
       checking the sha256 recorded in native/shared_math_reference.json.
+  dense_reference_outputs.npz
+      Outputs of the reference's own dense library (kernels/dense_n32/,
+      compiled for the CPU) on the seeded DENSE_CASES: the A8 projection from
+      N16 banks (every geometry), from the N32 shadow, and the bf16 prefill
+      preparation.  Inputs are regenerated from their seeds, as below.
   routed_reference_outputs.npz
       Outputs of the reference's own routed library (kernels/routed_storage/,
       compiled for the CPU by oracle/build_ref.py) on seeded synthetic cases.
@@ -11,7 +16,7 @@
       synthetic generator, and the sha256 of the regenerated inputs is stored
       so that generator drift is detected.
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/reference]
+Usage: python tests/golden/make_golden.py [--reference /path/to/reference] [--only dense]
 """
 import argparse
 import hashlib
@@ -71,6 +76,38 @@ def make_case(S, layer, case_seed, T, pad, hot, special):
     return x, w, ids
 
 
+# (name, seed, M, N, K, entry, geometry, special); entry 'n16', 'n32' or 'prepare'
+DENSE_CASES = [
+    ('d_m1_n32', 31, 1, 64, 2048, 'n32', 2, ''),
+    ('d_m1_n16', 32, 1, 96, 2048, 'n16', 2, ''),
+    ('d_m3_g1_n48', 33, 3, 48, 512, 'n16', 1, ''),
+    ('d_m16_g0', 34, 16, 128, 768, 'n16', 0, ''),
+    ('d_m37_g0', 35, 37, 64, 256, 'n16', 0, ''),
+    ('d_m7_n32_k8192', 36, 7, 32, 8192, 'n32', 2, ''),
+    ('d_m5_edges', 37, 5, 64, 512, 'n16', 2, 'edges'),
+    ('d_prep_m5', 38, 5, 48, 512, 'prepare', 0, 'edges'),
+]
+
+
+def make_dense_case(S, seed, M, N, K, special):
+    """Rows and an N16 bank.  Draw order: bank (make_dense_bank), then rows."""
+    rng = np.random.default_rng(seed)
+    codes, meta = S.make_dense_bank(rng, N, K)
+    x = S.make_rows(rng, M, K)
+    if special == 'edges':
+        # row 0 all zero (zero groups -> scale 1); row 1 a NaN element; row 2
+        # an element of 3e4 saturating its group; row 3 every element at the
+        # bf16 maximum (the Hadamard overflows: flags 1 and 2); column 3 of
+        # tile 1 has an infinite offset in group 0 (flags 4 and 8)
+        x[0, :] = 0
+        x[1, 5] = 0x7FC0
+        x[2, 7] = S.f32_to_bf16_bits(np.array([3.0e4], np.float32))[0]
+        x[3, :] = 0x7F7F
+        meta = meta.copy()
+        meta[1, 0, 3] = (meta[1, 0, 3] & 0xFFFF) | (0x7C00 << 16)
+    return x, codes, meta
+
+
 def digest(*arrays):
     h = hashlib.sha256()
     for a in arrays:
@@ -81,8 +118,12 @@ def digest(*arrays):
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument('--reference', default='/root/reference')
+    parser.add_argument('--only', choices=['dense'], default=None)
     args = parser.parse_args()
     ref = Path(args.reference)
+    write_dense()
+    if args.only == 'dense':
+        return
     import torch
     from safetensors.torch import load_file
 
@@ -140,6 +181,34 @@ def main():
         store[f'config1/flags_{key}'] = np.array(flags, np.uint32)
     np.savez_compressed(OUT / 'routed_reference_outputs.npz', **store)
     print('wrote', OUT / 'routed_reference_outputs.npz')
+
+
+def write_dense():
+    S = _synthetic()
+    store = {}
+    for name, seed, M, N, K, entry, geometry, special in DENSE_CASES:
+        x, codes, meta = make_dense_case(S, seed, M, N, K, special)
+        store[f'{name}/inputs_sha256'] = np.array(digest(x, codes, meta))
+        if entry == 'prepare':
+            xt, w, flags, st = O.ref_dense_prepare_bf16(x, codes, meta, N, K)
+            assert st == 0, (name, st)
+            store[f'{name}/transformed'] = xt
+            store[f'{name}/weights'] = w
+        else:
+            if entry == 'n32':
+                codes, meta = O.repack_n16_to_n32(codes[None], meta[None], N, K)
+                codes, meta = codes[0], meta[0]
+                fn = 'ornith_dense_g256_launch_n32'
+            else:
+                fn = 'ornith_dense_g256_launch'
+            out, proj, flags, st = O.ref_dense(x, codes, meta, N, K, entry=fn, geometry=geometry)
+            assert st == 0, (name, st)
+            store[f'{name}/out'] = out
+            store[f'{name}/projection'] = proj
+        store[f'{name}/flags'] = np.array(flags, np.uint32)
+        print(name, 'flags', flags)
+    np.savez_compressed(OUT / 'dense_reference_outputs.npz', **store)
+    print('wrote', OUT / 'dense_reference_outputs.npz')
 
 
 if __name__ == '__main__':
