@@ -70,6 +70,11 @@ CONFIGS = {
                         name='dense G256 A8 projection N12288 x K2048, 1 row, 40 banks'),
     'dense_qkvz16': dict(T=16, layers=40, N=12288, K=2048, dense=True,
                          name='dense G256 A8 projection N12288 x K2048, 16 rows, 40 banks'),
+    # W8 LM head: the 248,320 x 2048 int8 bank (508 MB, four times L2) per decode step
+    'head_vocab1': dict(T=1, layers=1, N=248320, K=2048, head=True,
+                        name='W8 LM head, vocabulary 248320 x 2048 int8, 1 row'),
+    'head_vocab8': dict(T=8, layers=1, N=248320, K=2048, head=True,
+                        name='W8 LM head, vocabulary 248320 x 2048 int8, 8 rows'),
 }
 
 
@@ -402,6 +407,93 @@ def run_dense(args):
     }), flush=True)
 
 
+def run_head(args):
+    """W8 LM head (ornith_b200::head_out): one step = the step's rows through
+    the full-vocabulary bank, captured as a CUDA graph.  Roofline: algorithmic
+    bytes of one launch (int8 codes N*K, fp16 scales N*32, bf16 rows in, bf16
+    logits and the fp32 diagnostic out) over its CUDA-event time."""
+    import torch
+    cfg = dict(CONFIGS[args.config])
+    dev = torch.device('cuda', 0)
+    torch.cuda.set_device(dev)
+    graft.load_package()
+    import importlib
+    native = importlib.import_module('ornith_b200.native')
+    lib = native.lib()
+    M, N, K = cfg['T'], cfg['N'], cfg['K']
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(555)
+    codes = torch.randint(-127, 128, (N // 16, K // 16, 4, 16, 4), dtype=torch.int8, device=dev, generator=gen)
+    words = codes.view(torch.int32).view(N // 16, K // 16, 4, 16).view(torch.uint32)
+    scales = (0.01 * torch.randn((N, K // 128), device=dev, generator=gen).abs()).to(torch.float16).clamp_min(2 ** -14)
+    x = torch.randn((M, K), device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(native.head_get_layout(native.HEAD_ROWS, N).workspace_bytes, dtype=torch.uint8, device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def step():
+        native.head_out(x, words, scales, ws, out, flags, 2)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    launches = launches_per_step(lib, step) * args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    algo = N * K + N * (K // 128) * 2 + M * K * 2 + M * N * 2 + M * N * 4
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    peak = peaks.get('hbm_gbs', 6650.0)
+    launch_ms = ms / args.steps
+    achieved = algo / (launch_ms * 1e-3) / 1e9
+    pin_x = x.cpu().pin_memory()
+    pin_out = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        x.copy_(pin_x, non_blocking=True)
+        graph.replay()
+        pin_out.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    print(json.dumps({
+        'metric': 'W8 LM head rows/s & % of HBM roofline', 'value': round(M * args.steps / (ms / 1e3), 3),
+        'unit': 'rows/s', 'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': round(launch_ms, 4), 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+        'dtype': 'int8', 'data': 'synthetic (seeded random int8 bank)',
+        'config': {'workload': cfg['name'], 'rows': M, 'N': N, 'K': K,
+                   'l2': f'inputs larger than L2: {algo / 1e6:.0f} MB per step'},
+        'e2e': {'value': round(M * args.steps / (e2e_ms / 1e3), 3), 'unit': 'rows/s',
+                'h2d_bytes_per_step': M * K * 2, 'd2h_bytes_per_step': M * N * 2},
+        'gpu_launches': int(launches),
+        'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
+                     'frac': round(achieved / peak, 4), 'traffic': None,
+                     'kernel': 'one head launch (head_quant_kernel + head_project_kernel)',
+                     'algorithmic_bytes_per_launch': algo, 'launch_ms': round(launch_ms, 5),
+                     'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'},
+        'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': True,
+    }), flush=True)
+
+
 def launches_per_step(lib, step_fn):
     """Kernels one step enqueues: counted by running the step eagerly once."""
     import torch
@@ -694,6 +786,10 @@ def run_reference(args):
         return
     if cfg.get('dense'):
         return run_reference_dense(args, cfg, O)
+    if cfg.get('head'):
+        print(json.dumps({'impl': 'reference', 'unavailable': 'the head bench line has no CPU reference arm; '
+                          'tests compare the reference head source compiled for the CPU on sampled columns'}))
+        return
     S, layer = _cpu_layer()
     tab = np.load(ROOT / 'tests' / 'golden' / 'shared_math_tables.npz')
     rng = np.random.default_rng(10)
@@ -778,5 +874,7 @@ if __name__ == '__main__':
         run_ep(a)
     elif CONFIGS[a.config].get('dense'):
         run_dense(a)
+    elif CONFIGS[a.config].get('head'):
+        run_head(a)
     else:
         run(a)

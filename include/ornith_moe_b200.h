@@ -308,6 +308,48 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_dense_g256_prepare_bf16(
     const void* input_bf16, const void* codes, const void* metadata,
     void* transformed_bf16, void* weights_bf16, void* flags_u32, int M, int N, int K, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * W8 LM head: drop-in for the reference's head library (kernels/head/
+ * head_i8_tile_api.h, head_i8_tile_consumer.cpp), same symbols, arguments and
+ * return codes.  K = 2048 in 16 groups of 128; N in {256, 1024, 4096, 65536,
+ * 248320}; 0 <= M <= Mcap <= 64; geometry 0, 1 or 2 (identical results).
+ * weights UINT32[N/16][K/16][4][16]: four signed int8 codes per word, lowest
+ * k first (word kw of column n at ((n/16*128 + kw/4)*4 + kw%4)*16 + n%16);
+ * scales fp16 [N][16], positive, >= 2^-14.  Per row: H128 per group, A8 per
+ * 128-group, exact int32 dots, value += w_scale*(sa*dot) over ascending
+ * groups without FMA, bf16 RNE.  Flags as the dense library (1, 2, 4, 8).
+ * group_dots (optional, int32 [M][N][16]) receives the raw group dots;
+ * null iff group_dots_bytes == 0.  Alignment: input 16 B (the reference asks
+ * 2), workspace 256 B, weights, group_dots and flags 4 B, scales and output
+ * 2 B; workspace, output, group_dots and flags overlap nothing.
+ * ------------------------------------------------------------------------ */
+
+/* Same 5 size_t fields as the reference (head_i8_tile_api.h:13-15,
+ * native.py:23-25): activation_words UINT32[Mcap][512] in the reference's
+ * format, activation_scales fp16 [Mcap][16], projection the fp32 diagnostic
+ * [Mcap][N]; transformed holds SIZE_MAX. */
+typedef struct OrnithHeadI8Layout {
+    size_t workspace_bytes, transformed, activation_words, activation_scales, projection;
+} OrnithHeadI8Layout;
+
+/* Replaces ornith_head_i8_tile_abi_version (head_i8_tile_api.h:42).  Returns 1. */
+ORNITH_MOE_B200_EXPORT uint32_t ornith_head_i8_tile_abi_version(void);
+
+/* Replaces ornith_head_i8_tile_get_layout (head_i8_tile_api.h:43,
+ * head_i8_tile_consumer.cpp:242-250). */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_head_i8_tile_get_layout(int Mcap, int N, OrnithHeadI8Layout* out);
+
+/* Replaces ornith_head_i8_tile_launch (head_i8_tile_api.h:44-48,
+ * head_i8_tile_consumer.cpp:251-291): input bf16 [M,2048] -> output bf16 [M,N]. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_head_i8_tile_launch(
+    const void* input_bf16, const void* weights_i8, const void* scales_f16,
+    void* workspace, size_t workspace_bytes, void* output_bf16,
+    void* group_dots_i32, size_t group_dots_bytes, void* flags_u32,
+    int M, int Mcap, int N, int geometry, cudaStream_t stream);
+
+/* Replaces ornith_head_i8_tile_shortlist (head_i8_tile_consumer.cpp:293): 1. */
+ORNITH_MOE_B200_EXPORT int ornith_head_i8_tile_shortlist(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,7 +16,8 @@ shared libraries under oracle/_ref/ so that their outputs pin the C oracle:
 Outputs (git-ignored, never committed):
   oracle/_ref/libref_routed_storage_n32.so   kernels/routed_storage/ (production library)
   oracle/_ref/libref_routed_direct_n16.so    kernels/routed/ (N16 checkpoint layout)
-  oracle/_ref/libref_dense_n32.so            kernels/dense_n32/ (shared-expert dense path)
+  oracle/_ref/libref_dense_n32.so            kernels/dense_n32/ (dense G256 projections)
+  oracle/_ref/libref_head_i8.so              kernels/head/ (W8 LM head)
 
 Usage: python oracle/build_ref.py [--reference DIR]
 The reference checkout exists only in the build container; on other machines
@@ -43,6 +44,9 @@ LIBS = {
     'dense_n32': ('kernels/dense_n32',
                   ['dense_g256_consumer.cpp', 'dense_g256_api.h'],
                   'dense_g256_consumer.cpp'),
+    'head_i8': ('kernels/head',
+                ['head_i8_tile_consumer.cpp', 'head_i8_tile_api.h'],
+                'head_i8_tile_consumer.cpp'),
 }
 LAUNCH = re.compile(r'(\b[A-Za-z_]\w*(?:<[^<>;()]*>)?)\s*<<<(.*?)>>>\s*\(')
 

@@ -18,6 +18,10 @@
 //       16x16x16 integer MMA; lane l holds row l%16 of A and column l%16 of B
 //       as 16 nibbles in two dwords (k = 8*dword + nibble); D element (m, n) is
 //       in lane n + 16*(m&1), dword m>>1;
+//   __builtin_amdgcn_sudot4(sa, a, sb, b, c, clamp): c + sum of 4 products of
+//       8-bit lanes (byte i = bits 8i..8i+7), each operand signed or unsigned;
+//   __builtin_amdgcn_wmma_i32_16x16x16_iu8_w32(sa, A, sb, B, C, clamp): as the
+//       iu4 form with 16 bytes per lane in four dwords (k = 4*dword + byte);
 //   __builtin_amdgcn_readfirstlane(v): lane 0's value.
 #pragma once
 #include <math.h>
@@ -65,7 +69,7 @@ struct Block {
     const std::function<void()>* body = nullptr;
     // per-warp exchange buffers
     std::vector<uint32_t> xch;
-    std::vector<int32_t> wa, wb;  // WMMA operands: 32 lanes x 2 dwords each
+    std::vector<int32_t> wa, wb;  // WMMA operands: 32 lanes x up to 4 dwords each
 };
 
 inline thread_local Block* g_block = nullptr;
@@ -110,8 +114,8 @@ inline void run_block(const std::function<void()>& body, unsigned nthreads) {
     blk.fibers.resize(nthreads);
     blk.live = (int)nthreads;
     blk.xch.assign(nthreads + 32, 0);
-    blk.wa.assign((nthreads + 32) * 2, 0);
-    blk.wb.assign((nthreads + 32) * 2, 0);
+    blk.wa.assign((nthreads + 32) * 4, 0);
+    blk.wb.assign((nthreads + 32) * 4, 0);
     Block* saved = g_block;
     g_block = &blk;
     for (unsigned t = 0; t < nthreads; ++t) {
@@ -181,6 +185,11 @@ inline int nib(uint32_t word, int i, bool is_signed) {
     return (is_signed && v >= 8) ? v - 16 : v;
 }
 
+inline int byte8(uint32_t word, int i, bool is_signed) {
+    int v = (int)((word >> (8 * i)) & 255u);
+    return (is_signed && v >= 128) ? v - 256 : v;
+}
+
 }  // namespace hipshim
 
 #define threadIdx (::hipshim::current_tid())
@@ -243,6 +252,40 @@ inline hipshim_i32x8 hipshim_wmma_iu4(bool sa, hipshim_i32x2 A, bool sb, hipshim
     return D;
 }
 #define __builtin_amdgcn_wmma_i32_16x16x16_iu4_w32 hipshim_wmma_iu4
+
+inline int hipshim_sudot4(bool sa, int a, bool sb, int b, int c, bool) {
+    int acc = c;
+    for (int i = 0; i < 4; ++i) acc += ::hipshim::byte8((uint32_t)a, i, sa) * ::hipshim::byte8((uint32_t)b, i, sb);
+    return acc;
+}
+#define __builtin_amdgcn_sudot4 hipshim_sudot4
+
+typedef int32_t hipshim_i32x4 __attribute__((vector_size(16)));
+inline hipshim_i32x8 hipshim_wmma_iu8(bool sa, hipshim_i32x4 A, bool sb, hipshim_i32x4 B, hipshim_i32x8 C, bool) {
+    using namespace ::hipshim;
+    Block* blk = g_block;
+    unsigned lane = lane_id(), base = warp_base();
+    for (int d = 0; d < 4; ++d) {
+        blk->wa[4 * (base + lane) + d] = A[d];
+        blk->wb[4 * (base + lane) + d] = B[d];
+    }
+    barrier();
+    hipshim_i32x8 D = C;
+    unsigned n = lane & 15u, half = lane >> 4;
+    for (int v = 0; v < 8; ++v) {
+        unsigned m = 2u * (unsigned)v + half;
+        int acc = 0;
+        for (int k = 0; k < 16; ++k) {
+            uint32_t aw = (uint32_t)blk->wa[4 * (base + m) + k / 4];
+            uint32_t bw = (uint32_t)blk->wb[4 * (base + n) + k / 4];
+            acc += byte8(aw, k % 4, sa) * byte8(bw, k % 4, sb);
+        }
+        D[v] += acc;
+    }
+    barrier();
+    return D;
+}
+#define __builtin_amdgcn_wmma_i32_16x16x16_iu8_w32 hipshim_wmma_iu8
 
 inline hipError_t hipMemsetAsync(void* p, int v, size_t n, hipStream_t) { memset(p, v, n); return hipSuccess; }
 inline hipError_t hipGetLastError() { return hipSuccess; }

@@ -331,3 +331,60 @@ def ref_dense_prepare_bf16(x_bits, codes16, meta16, N, K):
     st = fn(_p(x_bits), _p(_c(codes16, np.uint32)), _p(_c(meta16, np.uint32)), _p(xt), _p(w), _p(flags),
             C.c_int(M), C.c_int(N), C.c_int(K), None)
     return xt, w, int(flags[0]), st
+
+
+# ---------------------------------------------------------------------------
+# W8 LM head (kernels/head/, head_i8_tile_api.h:21-41)
+# ---------------------------------------------------------------------------
+
+HEAD_K, HEAD_GROUPS = 2048, 16
+
+
+def head_project(x_bits, words, scales_bits, N, group_dots=False):
+    """x bf16 bits [M,2048] by the int8 head bank (words uint32 [N/16,128,4,16],
+    scales fp16 bits [N,16]).  Returns (out bf16 bits, fp32 values, flags[, dots])."""
+    x_bits = _c(x_bits, np.uint16).reshape(-1, HEAD_K)
+    M = x_bits.shape[0]
+    out = np.zeros((M, N), np.uint16)
+    diag = np.zeros((M, N), np.float32)
+    dots = np.zeros((M, N, HEAD_GROUPS), np.int32) if group_dots else None
+    flags = np.zeros(1, np.uint32)
+    lib().orc_head_project(_p(x_bits), C.c_int(M), C.c_int(N), _p(_c(words, np.uint32)),
+                           _p(_c(scales_bits, np.uint16)), _p(out), _p(diag), _p(dots) if dots is not None else None,
+                           _p(flags))
+    res = (out, diag, int(flags[0]))
+    return res + (dots,) if group_dots else res
+
+
+class HeadLayout(C.Structure):
+    """OrnithHeadI8Layout, kernels/head/head_i8_tile_api.h:13-15."""
+    _fields_ = [(n, C.c_size_t) for n in
+                ('workspace_bytes', 'transformed', 'activation_words', 'activation_scales', 'projection')]
+
+
+def ref_head(x_bits, words, scales_bits, N, geometry=2, Mcap=None, group_dots=False):
+    """ornith_head_i8_tile_launch of the compiled reference.
+    Returns (out, fp32 projection, flags, status[, dots])."""
+    L = ref_lib('head_i8')
+    x_bits = _c(x_bits, np.uint16).reshape(-1, HEAD_K)
+    M = x_bits.shape[0]
+    Mcap = M if Mcap is None else Mcap
+    layout = HeadLayout()
+    L.ornith_head_i8_tile_get_layout.restype = C.c_int
+    st = L.ornith_head_i8_tile_get_layout(C.c_int(Mcap), C.c_int(N), C.byref(layout))
+    if st:
+        return (None, None, None, st) + ((None,) if group_dots else ())
+    ws = _aligned_bytes(max(layout.workspace_bytes, 256))
+    out = np.zeros((max(M, 1), N), np.uint16)
+    dots = np.zeros((max(M, 1), N, HEAD_GROUPS), np.int32) if group_dots else None
+    flags = np.zeros(1, np.uint32)
+    fn = L.ornith_head_i8_tile_launch
+    fn.restype = C.c_int
+    st = fn(_p(x_bits), _p(_c(words, np.uint32)), _p(_c(scales_bits, np.uint16)), _p(ws), C.c_size_t(ws.size),
+            _p(out), _p(dots) if group_dots else None, C.c_size_t(dots.nbytes if group_dots else 0), _p(flags),
+            C.c_int(M), C.c_int(Mcap), C.c_int(N), C.c_int(geometry), None)
+    proj = None
+    if st == 0:
+        proj = ws[layout.projection:layout.projection + M * N * 4].view(np.float32).reshape(M, N).copy()
+    res = (out[:M], proj, int(flags[0]), st)
+    return res + (dots[:M] if group_dots else None,) if group_dots else res

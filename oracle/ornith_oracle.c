@@ -779,6 +779,79 @@ void orc_dense_prepare_bf16(const uint16_t* x, int M, int N, int K,
     *flags |= f;
 }
 
+/* ------------------------------------------------------------------------
+ * W8 LM head (kernels/head/head_i8_tile_api.h:21-41, head_i8_tile_consumer.cpp).
+ * K = 2048 in 16 groups of 128.  Weights: signed int8 codes in words
+ * UINT32[N/16][K/16][4][16] (word kw = k/4 of column n at
+ * ((n/16*(K/16) + kw/4)*4 + kw%4)*16 + n%16, byte k%4 = bits 8(k%4)..),
+ * fp16 scales [N][16], no offset.  Per row: H128 per group (flag 1), A8 per
+ * 128-group (quantisation as the routed path, over 128 elements, flag 2),
+ * exact int32 group dots, then over groups g = 0..15
+ *   value = value + w_scale[n][g]*(sa[g]*float(dot))
+ * (compact_projection :87-116 and the WMMA forms compute this sequence),
+ * stored through dense_store (flags 4 and 8).  group_dots (may be NULL)
+ * receives the raw dots [M][N][16]. */
+void orc_head_project(const uint16_t* x, int M, int N, const uint32_t* words, const uint16_t* scales,
+                      uint16_t* out, float* diag, int32_t* group_dots, uint32_t* flags) {
+    enum { HK = 2048, HG = 128, HGROUPS = 16 };
+    int8_t* q = (int8_t*)malloc((size_t)M * HK);
+    float* sa = (float*)malloc(sizeof(float) * (size_t)M * HGROUPS);
+    uint32_t f = 0;
+    for (int r = 0; r < M; ++r)
+        for (int g = 0; g < HGROUPS; ++g) {
+            float in[HG], t[HG], v[HG], absmax = 0.f;
+            for (int l = 0; l < HG; ++l) {
+                in[l] = orc_bf16_to_f32(x[(size_t)r * HK + g * HG + l]);
+                if (!isfinite(in[l])) f |= ORC_FLAG_NONFINITE_INPUT;
+            }
+            orc_wht128(in, t);
+            for (int l = 0; l < HG; ++l) {
+                if (!isfinite(t[l])) f |= ORC_FLAG_NONFINITE_INPUT;
+                int finite = isfinite(t[l]);
+                if (!finite) f |= ORC_FLAG_INVALID_ACT;
+                v[l] = finite ? t[l] : 0.f;
+                absmax = fmaxf(absmax, fabsf(v[l]));
+            }
+            float raw = absmax / 127.f;
+            int valid = isfinite(raw) && raw <= 65504.f;
+            if (!valid) f |= ORC_FLAG_INVALID_ACT;
+            uint16_t scale = orc_f32_to_half_rne(absmax == 0.f || !valid ? 1.f : fmaxf(raw, 0x1p-14f));
+            float sf = orc_half_to_f32(scale);
+            for (int l = 0; l < HG; ++l) {
+                int qi = (absmax == 0.f || !valid) ? 0 : (int)nearbyintf(v[l] / sf);
+                q[(size_t)r * HK + g * HG + l] = (int8_t)(qi < -127 ? -127 : (qi > 127 ? 127 : qi));
+            }
+            sa[(size_t)r * HGROUPS + g] = sf;
+        }
+#pragma omp parallel for reduction(| : f) schedule(static)
+    for (int n = 0; n < N; ++n) {
+        int8_t wc[HK];
+        for (int k = 0; k < HK; k += 4) {
+            int kw = k / 4;
+            uint32_t w = words[(((size_t)(n / 16) * (HK / 16) + kw / 4) * 4 + kw % 4) * 16 + n % 16];
+            for (int b = 0; b < 4; ++b) wc[k + b] = (int8_t)((w >> (8 * b)) & 255u);
+        }
+        for (int r = 0; r < M; ++r) {
+            float value = 0.f;
+            for (int g = 0; g < HGROUPS; ++g) {
+                int32_t dot = 0;
+                for (int l = 0; l < HG; ++l) dot += (int32_t)wc[g * HG + l] * (int32_t)q[(size_t)r * HK + g * HG + l];
+                if (group_dots) group_dots[((size_t)r * N + n) * HGROUPS + g] = dot;
+                float scaled = sa[(size_t)r * HGROUPS + g] * (float)dot;
+                float term = orc_half_to_f32(scales[(size_t)n * HGROUPS + g]) * scaled;
+                value = value + term;
+            }
+            uint32_t lf = 0;
+            out[(size_t)r * N + n] = dense_store(value, &lf);
+            if (diag) diag[(size_t)r * N + n] = value;
+            f |= lf;
+        }
+    }
+    *flags |= f;
+    free(q);
+    free(sa);
+}
+
 int orc_set_threads(int n) {
 #ifdef _OPENMP
     if (n > 0) omp_set_num_threads(n);

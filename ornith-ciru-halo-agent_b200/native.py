@@ -13,7 +13,9 @@ Mirrors the reference plugin's binding (plugin-site/ornith_g256/native.py):
     states + router logits -> combined hidden states);
   * `ornith_b200::dense_out` has the arguments and the A8 / bf16-prefill
     split of `ornith_g256::dense_out` (native.py:121-153), and
-    `dense_n32_out` is the one-row N32 shadow launch of dense_n32.py:45-53.
+    `dense_n32_out` is the one-row N32 shadow launch of dense_n32.py:45-53;
+  * `ornith_b200::head_out` is the W8 LM head launch of
+    `ornith_g256::head_out` (native.py:205-212).
 All launches go to the caller's current CUDA stream.  There is no CPU
 fallback: every operator raises if the CUDA library is missing.
 """
@@ -42,6 +44,12 @@ class DenseLayout(C.Structure):
     """OrnithDenseG256Layout (include/ornith_moe_b200.h; reference native.py:11-13)."""
     _fields_ = [(n, C.c_size_t) for n in
                 ('workspace_bytes', 'transformed', 'low', 'high', 'scales', 'sums', 'projection')]
+
+
+class HeadLayout(C.Structure):
+    """OrnithHeadI8Layout (include/ornith_moe_b200.h; reference native.py:23-25)."""
+    _fields_ = [(n, C.c_size_t) for n in
+                ('workspace_bytes', 'transformed', 'activation_words', 'activation_scales', 'projection')]
 
 
 _DENSE_ARGS = [C.c_void_p] * 4 + [C.c_size_t] + [C.c_void_p] * 2 + [C.c_int] * 7 + [C.c_void_p]
@@ -80,6 +88,11 @@ SIGNATURES = {
     'ornith_dense_g256_launch_n32': (_DENSE_ARGS, C.c_int),
     'ornith_dense_g256_n32_rows': ([], C.c_int),
     'ornith_dense_g256_prepare_bf16': ([C.c_void_p] * 6 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
+    'ornith_head_i8_tile_abi_version': ([], C.c_uint32),
+    'ornith_head_i8_tile_get_layout': ([C.c_int, C.c_int, C.POINTER(HeadLayout)], C.c_int),
+    'ornith_head_i8_tile_launch': ([C.c_void_p] * 4 + [C.c_size_t] + [C.c_void_p] * 2 + [C.c_size_t]
+                                   + [C.c_void_p] + [C.c_int] * 4 + [C.c_void_p], C.c_int),
+    'ornith_head_i8_tile_shortlist': ([], C.c_int),
 }
 
 
@@ -437,3 +450,41 @@ def dense_n32_shadow(codes, metadata, n, k):
     codes32, meta32 = repack_n16_to_n32(codes.reshape(1, n // 16, k // 256, 32, 16),
                                         metadata.reshape(1, n // 16, k // 256, 16), n, k)
     return codes32[0], meta32[0]
+
+
+# ---------------------------------------------------------------------------
+# W8 LM head (reference native.py:205-212)
+# ---------------------------------------------------------------------------
+HEAD_VOCAB, HEAD_ROWS = 248320, 64
+
+
+def head_get_layout(capacity, n=HEAD_VOCAB):
+    layout = HeadLayout()
+    check(lib().ornith_head_i8_tile_get_layout(capacity, n, C.byref(layout)), 'head layout')
+    return layout
+
+
+@torch.library.custom_op('ornith_b200::head_out', mutates_args={'workspace', 'out', 'flags'}, device_types='cuda')
+def head_out(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor,
+             workspace: torch.Tensor, out: torch.Tensor, flags: torch.Tensor, geometry: int) -> None:
+    """Logits bf16 [M, 248320] of up to 64 rows x bf16 [M, 2048] through the
+    int8 head bank (codes uint32 [15520, 128, 4, 16], scales fp16 [248320, 16])."""
+    validate(x, out, HEAD_ROWS, 2048)
+    check(lib().ornith_head_i8_tile_launch(ptr(x), ptr(codes), ptr(scales), ptr(workspace), workspace.numel(),
+                                           ptr(out), None, 0, ptr(flags), x.shape[0], HEAD_ROWS, out.shape[1],
+                                           geometry, stream(x)), 'W8 head')
+
+
+@head_out.register_fake
+def _head_fake(x, codes, scales, workspace, out, flags, geometry):
+    return None
+
+
+def head_launch(x, codes, scales, workspace, out, flags, n, capacity=HEAD_ROWS, geometry=2, group_dots=None):
+    """The head launch for any supported vocabulary size n, optionally storing
+    the raw group dots int32 [M, n, 16]."""
+    validate(x, out, capacity, 2048)
+    nbytes = group_dots.numel() * group_dots.element_size() if group_dots is not None else 0
+    check(lib().ornith_head_i8_tile_launch(ptr(x), ptr(codes), ptr(scales), ptr(workspace), workspace.numel(),
+                                           ptr(out), ptr(group_dots) if group_dots is not None else None, nbytes,
+                                           ptr(flags), x.shape[0], capacity, n, geometry, stream(x)), 'W8 head')

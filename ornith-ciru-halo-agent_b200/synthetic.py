@@ -64,6 +64,19 @@ def make_dense_bank(rng, N, K):
     return codes, meta
 
 
+def make_head_bank(rng, N, K=2048):
+    """An int8 head bank in the reference's physical layout (head_i8_tile_api.h:1-2,
+    :21-26): words uint32 [N/16, K/16, 4, 16], four signed codes per word
+    (lowest k first) uniform over [-127, 127], and fp16 scales [N, 16] (one per
+    128-group) = 0.01*|N(0,1)| floored at 2^-14, as uint16 bits.
+    Draw order: codes, then scales."""
+    codes = rng.integers(-127, 128, size=(N // 16, K // 16, 4, 16, 4), dtype=np.int8)
+    words = np.ascontiguousarray(codes).view(np.uint32).reshape(N // 16, K // 16, 4, 16)
+    z = rng.standard_normal((N, K // 128), dtype=np.float32)
+    scales = np.maximum((np.float32(0.01) * np.abs(z)).astype(np.float16), np.float16(2 ** -14))
+    return words, scales.view(np.uint16)
+
+
 def make_rows(rng, M, K):
     """bf16 bits of x ~ N(0,1) [M, K]."""
     return f32_to_bf16_bits(rng.standard_normal((M, K), dtype=np.float32))

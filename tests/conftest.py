@@ -45,6 +45,11 @@ def dense_golden():
 
 
 @pytest.fixture(scope='session')
+def head_golden():
+    return np.load(GOLDEN / 'head_reference_outputs.npz')
+
+
+@pytest.fixture(scope='session')
 def tables():
     return np.load(GOLDEN / 'shared_math_tables.npz')
 

@@ -9,6 +9,10 @@
       compiled for the CPU) on the seeded DENSE_CASES: the A8 projection from
       N16 banks (every geometry), from the N32 shadow, and the bf16 prefill
       preparation.  Inputs are regenerated from their seeds, as below.
+  head_reference_outputs.npz
+      Outputs of the reference's own W8 head library (kernels/head/, compiled
+      for the CPU) on the seeded HEAD_CASES: logits, fp32 projections, raw
+      group dots and flags.
   routed_reference_outputs.npz
       Outputs of the reference's own routed library (kernels/routed_storage/,
       compiled for the CPU by oracle/build_ref.py) on seeded synthetic cases.
@@ -16,7 +20,7 @@
       synthetic generator, and the sha256 of the regenerated inputs is stored
       so that generator drift is detected.
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/reference] [--only dense]
+Usage: python tests/golden/make_golden.py [--reference /path/to/reference] [--only dense|head]
 """
 import argparse
 import hashlib
@@ -89,6 +93,34 @@ DENSE_CASES = [
 ]
 
 
+# (name, seed, M, N, geometry, special)
+HEAD_CASES = [
+    ('h_m1_n1024', 41, 1, 1024, 2, ''),
+    ('h_m3_n256_compact', 42, 3, 256, 1, ''),
+    ('h_m16_n1024_wmma', 43, 16, 1024, 0, ''),
+    ('h_m64_n256_shared64', 44, 64, 256, 2, ''),
+    ('h_m5_edges', 45, 5, 256, 2, 'edges'),
+]
+
+
+def make_head_case(S, seed, M, N, special):
+    """Rows and an int8 head bank.  Draw order: bank (make_head_bank), then rows."""
+    rng = np.random.default_rng(seed)
+    words, scales = S.make_head_bank(rng, N)
+    x = S.make_rows(rng, M, 2048)
+    if special == 'edges':
+        # row 0 all zero; row 1 a NaN element; row 2 a saturating 3e4; row 3 at
+        # the bf16 maximum (the Hadamard overflows: flags 1 and 2); column 5
+        # has an infinite scale in group 3 (flags 4 and 8)
+        x[0, :] = 0
+        x[1, 300] = 0x7FC0
+        x[2, 1000] = S.f32_to_bf16_bits(np.array([3.0e4], np.float32))[0]
+        x[3, :] = 0x7F7F
+        scales = scales.copy()
+        scales[5, 3] = 0x7C00
+    return x, words, scales
+
+
 def make_dense_case(S, seed, M, N, K, special):
     """Rows and an N16 bank.  Draw order: bank (make_dense_bank), then rows."""
     rng = np.random.default_rng(seed)
@@ -118,11 +150,14 @@ def digest(*arrays):
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument('--reference', default='/root/reference')
-    parser.add_argument('--only', choices=['dense'], default=None)
+    parser.add_argument('--only', choices=['dense', 'head'], default=None)
     args = parser.parse_args()
     ref = Path(args.reference)
-    write_dense()
-    if args.only == 'dense':
+    if args.only != 'head':
+        write_dense()
+    if args.only != 'dense':
+        write_head()
+    if args.only:
         return
     import torch
     from safetensors.torch import load_file
@@ -181,6 +216,24 @@ def main():
         store[f'config1/flags_{key}'] = np.array(flags, np.uint32)
     np.savez_compressed(OUT / 'routed_reference_outputs.npz', **store)
     print('wrote', OUT / 'routed_reference_outputs.npz')
+
+
+def write_head():
+    S = _synthetic()
+    store = {}
+    for name, seed, M, N, geometry, special in HEAD_CASES:
+        x, words, scales = make_head_case(S, seed, M, N, special)
+        store[f'{name}/inputs_sha256'] = np.array(digest(x, words, scales))
+        out, proj, flags, st, dots = O.ref_head(x, words, scales, N, geometry=geometry, group_dots=True)
+        assert st == 0, (name, st)
+        store[f'{name}/out'] = out
+        store[f'{name}/projection'] = proj
+        if M * N <= 4096:  # raw dots only for the small cases (fixture size)
+            store[f'{name}/group_dots'] = dots
+        store[f'{name}/flags'] = np.array(flags, np.uint32)
+        print(name, 'flags', flags)
+    np.savez_compressed(OUT / 'head_reference_outputs.npz', **store)
+    print('wrote', OUT / 'head_reference_outputs.npz')
 
 
 def write_dense():
