@@ -9,6 +9,24 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device('cuda:0')
 
 
+def assert_bits_equal(got, want, err_msg=''):
+    """Bit equality, except that a NaN matches any NaN: the bits of a NaN made
+    by arithmetic (inf*0 from an infinite weight scale or offset) are the
+    hardware's default NaN (0x7FFFFFFF on NVIDIA GPUs, 0xFFC00000 on x86,
+    where the reference's source was compiled for the golden vectors), and
+    x86 passes an input NaN's bits through arithmetic where NVIDIA GPUs
+    return their default NaN."""
+    got, want = np.asarray(got), np.asarray(want)
+    if got.dtype == np.uint16:
+        nan = lambda b: ((b & 0x7F80) == 0x7F80) & ((b & 0x7F) != 0)  # noqa: E731
+    else:
+        got, want = got.view(np.uint32), want.view(np.uint32)
+        nan = lambda b: ((b & 0x7F800000) == 0x7F800000) & ((b & 0x7FFFFF) != 0)  # noqa: E731
+    np.testing.assert_array_equal(nan(got), nan(want), err_msg=err_msg)
+    keep = ~nan(want)
+    np.testing.assert_array_equal(got[keep], want[keep], err_msg=err_msg)
+
+
 def _u32(a):
     return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).to(DEV).view(torch.uint32)
 
@@ -41,9 +59,8 @@ def test_head_golden_cases(native, head_golden, make_golden, S):
         x, words, scales = make_golden.make_head_case(S, seed, M, N, special)
         has_dots = f'{name}/group_dots' in head_golden
         out, proj, flags, dots = run_head(native, x, words, scales, N, geometry, dots=has_dots)
-        np.testing.assert_array_equal(out, head_golden[f'{name}/out'], err_msg=name)
-        np.testing.assert_array_equal(proj.view(np.uint32), head_golden[f'{name}/projection'].view(np.uint32),
-                                      err_msg=name)
+        assert_bits_equal(out, head_golden[f'{name}/out'], err_msg=name)
+        assert_bits_equal(proj, head_golden[f'{name}/projection'], err_msg=name)
         if has_dots:
             np.testing.assert_array_equal(dots, head_golden[f'{name}/group_dots'], err_msg=name)
         assert flags == int(head_golden[f'{name}/flags']), name
