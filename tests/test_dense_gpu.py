@@ -65,11 +65,13 @@ def run_dense(native, x_bits, codes, meta, N, K, entry='n16', geometry=2, Mcap=N
 def run_prepare(native, x_bits, codes, meta, N, K):
     lib = native.lib()
     M = x_bits.shape[0]
-    x = _bf16(x_bits)
+    # device copies held in locals until the kernels have run (a temporary
+    # freed after ptr() would hand its memory to the next allocation)
+    x, c, m = _bf16(x_bits), _u32(codes), _u32(meta)
     xt = torch.empty((M, K), dtype=torch.bfloat16, device=DEV)
     w = torch.empty((N, K), dtype=torch.bfloat16, device=DEV)
     flags = torch.zeros(1, dtype=torch.int32, device=DEV)
-    st = lib.ornith_dense_g256_prepare_bf16(native.ptr(x), native.ptr(_u32(codes)), native.ptr(_u32(meta)),
+    st = lib.ornith_dense_g256_prepare_bf16(native.ptr(x), native.ptr(c), native.ptr(m),
                                             native.ptr(xt), native.ptr(w), native.ptr(flags), M, N, K,
                                             native.stream(x))
     torch.cuda.synchronize()
