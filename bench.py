@@ -298,9 +298,9 @@ def run_ep(args):
 def run_dense(args):
     """Dense G256 projections (ornith_dense_g256_launch, N16 banks): one step =
     the step's rows through 40 independent banks, captured as one CUDA graph.
-    Roofline: the algorithmic bytes of one launch (codes N*K/2, metadata
-    N*K/64, bf16 rows in and out, the fp32 diagnostic row out) over its
-    CUDA-event time."""
+    Roofline: the algorithmic bytes of one call (codes N*K/2, metadata N*K/64,
+    bf16 rows in and out, the fp32 diagnostic row out) over its share of the
+    step's CUDA-event time."""
     import torch
     cfg = dict(CONFIGS[args.config])
     if args.layers:
@@ -360,17 +360,9 @@ def run_dense(args):
         end.record()
         torch.cuda.synchronize()
     ms = start.elapsed_time(end)
-    # one launch (quantisation + projection) timed alone, banks in sequence
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
-    per = []
-    for _ in range(3):
-        for l in range(L):
-            ev[l][0].record()
-            call(l)
-            ev[l][1].record()
-        torch.cuda.synchronize()
-        per += [a.elapsed_time(b) for a, b in ev]
-    launch_ms = statistics.mean(per)
+    # one launch = one bank's call inside the captured step (the step's device
+    # time over its L calls; eager calls would add host launch gaps)
+    launch_ms = ms / args.steps / L
     algo = N * K // 2 + N * (K // 256) * 4 + M * K * 2 + M * N * 2 + M * N * 4
     peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
     peak = peaks.get('hbm_gbs', 6650.0)
@@ -400,7 +392,8 @@ def run_dense(args):
         'gpu_launches': int(launches),
         'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
                      'frac': round(achieved / peak, 4), 'traffic': None,
-                     'kernel': 'one dense launch (dense_quant_kernel + dense_project_kernel<16>)',
+                     'kernel': ('one dense call: dense_fused_kernel<16>' if M <= 4 else
+                                'one dense call: dense_quant_kernel + dense_project_kernel<16>'),
                      'algorithmic_bytes_per_launch': algo, 'launch_ms': round(launch_ms, 5),
                      'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'},
         'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': True,

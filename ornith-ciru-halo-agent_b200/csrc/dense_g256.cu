@@ -29,6 +29,9 @@
 //                          terms are summed in ascending group order.  At
 //                          decode sizes (M <= 16) every weight byte is read
 //                          once and the kernel is bound by HBM;
+//   dense_fused_kernel     decode rows (M <= 4): the quantisation of the
+//                          projection kernel's own groups inside it, so one
+//                          launch per call;
 //   dense_transform_bf16_kernel, dense_dequant_bf16_kernel
 //                          the prefill preparation (one warp per row group;
 //                          one CTA per 16-column tile and group, transposed
@@ -195,6 +198,74 @@ __global__ __launch_bounds__(256) void dense_project_kernel(const uint32_t* code
     flag_or(flags, f);
 }
 
+// Decode rows (M <= 4, the reference's compact crossover, geometry 2): the
+// quantisation runs inside the projection, one launch per call.  Warp w first
+// issues the weight loads of its group, then transforms and quantises that
+// group of every row into its own shared-memory slot (each CTA repeats this
+// for the groups it needs, a few hundred instructions per warp, hidden
+// behind the weight stream), and dots from there.  Every CTA computes the
+// same activations, so the flags it raises are those of the two-kernel path.
+// The activation fields of the workspace are not written on this path.
+constexpr int kFusedRows = 4;
+template <int W>
+__global__ __launch_bounds__(256) void dense_fused_kernel(const uint16_t* x, const uint32_t* codes,
+                                                          const uint32_t* meta, int M, int N, int K, float* diag,
+                                                          uint16_t* out, uint32_t* flags) {
+    extern __shared__ float terms[];  // [groups][kFusedRows][32]
+    __shared__ __align__(16) uint8_t act[kWarps][kFusedRows][kG];
+    __shared__ __half asc[kWarps][kFusedRows];
+    __shared__ int32_t asum[kWarps][kFusedRows];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int groups = K / kG;
+    const int n = blockIdx.x * 32 + lane;
+    const bool live = n < N;
+    const size_t tile_groups = size_t(n / W) * groups;
+    const int c = n % W;
+    uint32_t f = 0;
+    for (int g = warp; g < groups; g += kWarps) {
+        uint32_t w[32];
+        const uint32_t* blk = codes + (tile_groups + g) * 32 * W + c;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) w[j] = live ? __ldcs(blk + j * W) : 0u;
+        const uint32_t mt = live ? __ldg(meta + (tile_groups + g) * W + c) : 0u;
+        for (int m = 0; m < M; ++m) {
+            float e[8];
+            uint32_t qf = load_transform(x + size_t(m) * K + size_t(g) * kG, lane, e);
+            quantize_group_warp<127>(e, lane, reinterpret_cast<uint2*>(act[warp][m]), &asc[warp][m],
+                                     &asum[warp][m], qf);
+            f |= qf;
+        }
+        __syncwarp();
+        for (int m = 0; m < M; ++m) {
+            const uint4* a4 = reinterpret_cast<const uint4*>(act[warp][m]);
+            int dot = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint4 a = a4[j];
+                dot = dot8(w[2 * j], make_uint2(a.x, a.y), dot);
+                dot = dot8(w[2 * j + 1], make_uint2(a.z, a.w), dot);
+            }
+            terms[(g * kFusedRows + m) * 32 + lane] =
+                group_term(__half2float(asc[warp][m]), dot, asum[warp][m], mt);
+        }
+        __syncwarp();  // the slot is rewritten for the warp's next group
+    }
+    __syncthreads();
+    for (int m = warp; m < M; m += kWarps) {
+        float v = 0.f;
+        for (int g = 0; g < groups; ++g) v = __fadd_rn(v, terms[(g * kFusedRows + m) * 32 + lane]);
+        if (live) {
+            if (!isfinite(v)) f |= kNonfiniteProjection;
+            const uint16_t b = bf16_rne(v);
+            if ((b & 0x7f80u) == 0x7f80u) f |= kNonfiniteBf16;
+            const size_t idx = size_t(m) * N + n;
+            diag[idx] = v;
+            out[idx] = b;
+        }
+    }
+    flag_or(flags, f);
+}
+
 // bf16(H128(x)), one warp per (row, 256-group) (transform_bf16,
 // dense_g256_consumer.cpp:192-205): flag 1 on a non-finite input or fp32
 // result, flag 8 on a bf16 whose exponent is all ones.
@@ -313,6 +384,17 @@ cudaError_t project(const uint32_t* codes, const uint32_t* meta, uint8_t* ws, co
     return cudaGetLastError();
 }
 
+template <int W>
+cudaError_t project_fused(const uint16_t* x, const uint32_t* codes, const uint32_t* meta, uint8_t* ws,
+                          const OrnithDenseG256Layout& l, uint16_t* out, uint32_t* flags, int M, int N, int K,
+                          cudaStream_t stream) {
+    count_launches(1);
+    const size_t smem = size_t(K / kG) * kFusedRows * 32 * sizeof(float);
+    dense_fused_kernel<W><<<(N + 31) / 32, kWarps * 32, smem, stream>>>(
+        x, codes, meta, M, N, K, reinterpret_cast<float*>(ws + l.projection), out, flags);
+    return cudaGetLastError();
+}
+
 cudaError_t quantize(const uint16_t* x, uint8_t* ws, const OrnithDenseG256Layout& l, uint32_t* flags, int M, int K,
                      cudaStream_t stream) {
     count_launches(1);
@@ -353,6 +435,10 @@ extern "C" cudaError_t ornith_dense_g256_launch(const void* input, const void* c
     if (!dense::buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
+    if (M <= dense::kFusedRows)
+        return dense::project_fused<16>(static_cast<const uint16_t*>(input), static_cast<const uint32_t*>(codes),
+                                        static_cast<const uint32_t*>(metadata), ws, l,
+                                        static_cast<uint16_t*>(output), fl, M, N, K, stream);
     cudaError_t st = dense::quantize(static_cast<const uint16_t*>(input), ws, l, fl, M, K, stream);
     if (st != cudaSuccess) return st;
     return dense::project<16>(static_cast<const uint32_t*>(codes), static_cast<const uint32_t*>(metadata), ws, l,
@@ -375,6 +461,10 @@ extern "C" cudaError_t ornith_dense_g256_launch_n32(const void* input, const voi
     if (!dense::buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
+    if (M <= dense::kFusedRows)
+        return dense::project_fused<32>(static_cast<const uint16_t*>(input), static_cast<const uint32_t*>(codes),
+                                        static_cast<const uint32_t*>(metadata), ws, l,
+                                        static_cast<uint16_t*>(output), fl, M, N, K, stream);
     cudaError_t st = dense::quantize(static_cast<const uint16_t*>(input), ws, l, fl, M, K, stream);
     if (st != cudaSuccess) return st;
     return dense::project<32>(static_cast<const uint32_t*>(codes), static_cast<const uint32_t*>(metadata), ws, l,
