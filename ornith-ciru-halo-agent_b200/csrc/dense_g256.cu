@@ -208,7 +208,7 @@ __global__ __launch_bounds__(256) void dense_project_kernel(const uint32_t* code
 // The activation fields of the workspace are not written on this path.
 constexpr int kFusedRows = 4;
 template <int W>
-__global__ __launch_bounds__(256) void dense_fused_kernel(const uint16_t* x, const uint32_t* codes,
+__global__ __launch_bounds__(256, 3) void dense_fused_kernel(const uint16_t* x, const uint32_t* codes,
                                                           const uint32_t* meta, int M, int N, int K, float* diag,
                                                           uint16_t* out, uint32_t* flags) {
     extern __shared__ float terms[];  // [groups][kFusedRows][32]
