@@ -1,7 +1,12 @@
-"""Routed-expert weights and the MoE method the reference plugin drives.
+"""Packed-weight methods the reference plugin drives: routed experts, dense
+G256 linears and the W8 head.
 
-Mirrors, without vLLM, the reference plugin's routed method and its strict
-checkpoint loader:
+Mirrors, without vLLM, the reference plugin's methods and its strict
+checkpoint loaders:
+  * `register_packed`, `G256LinearMethod`, `W8HeadMethod`
+    (plugin-site/ornith_g256/method.py:11-91): packed parameters that accept
+    one load each of their exact shape and dtype, sealed after loading, and
+    `apply` through `ornith_b200::dense_out` / `ornith_b200::head_out`;
   * `G256MoEMethod` (plugin-site/ornith_g256/method.py:101-184):
     `create_weights` registers the four N16 tile banks of a routed layer,
     `process_weights_after_loading` seals them, `prepare_n32_weights` reorders
@@ -76,6 +81,95 @@ def require_complete_tilebank_load(layer):
     """Call from process_weights_after_loading, before binding (loader.py:52-54)."""
     if getattr(layer, '_tilebank_loaded_fields', set()) != set(FIELDS):
         raise ValueError('Incomplete tilebank packed-bank checkpoint coverage')
+
+
+def register_packed(layer, specs):
+    """Register packed parameters (name, shape, dtype) whose weight_loader
+    accepts one copy each of exactly that shape and dtype, before the layer
+    is sealed (method.py:11-27)."""
+    layer._g256_loaded = set()
+    layer._g256_ready = False
+    for name, shape, dtype in specs:
+        param = torch.nn.Parameter(torch.empty(shape, dtype=dtype, device=getattr(layer, '_g256_device', None)),
+                                   requires_grad=False)
+        layer.register_parameter(name, param)
+
+        def load(destination, value, *shard_args, name=name, param=param):
+            if layer._g256_ready or name in layer._g256_loaded or destination is not param:
+                raise ValueError(f'Duplicate or late packed load: {name}')
+            if value.shape != param.shape or value.dtype != param.dtype:
+                raise ValueError(f'Packed shape/dtype mismatch: {name}: {value.shape}/{value.dtype}')
+            with torch.no_grad():
+                param.copy_(value)
+            layer._g256_loaded.add(name)
+        param.weight_loader = load
+
+
+class G256LinearMethod:
+    """A dense G256 linear (method.py:30-62): codes uint32 [N/16, K/256, 32, 16]
+    and metadata uint32 [N/16, K/256, 16]; apply(x [..., K]) -> bf16 [..., N]."""
+    fields = ('g256_codes', 'g256_metadata')
+
+    def __init__(self, prefix=''):
+        self.prefix, self.runtime, self.slot = prefix, None, None
+
+    def create_weights(self, layer, input_size_per_partition, output_partition_sizes, input_size, output_size,
+                       params_dtype, **attrs):
+        self.k, self.n = input_size, output_size
+        if (input_size_per_partition != input_size or sum(output_partition_sizes) != output_size
+                or getattr(layer, 'tp_size', 1) != 1 or params_dtype != torch.bfloat16
+                or getattr(layer, 'has_bias', False) or not 0 < self.n <= 12288
+                or self.n % 16 or not 0 < self.k <= 8192 or self.k % 256):
+            raise ValueError(f'Unsupported G256 linear geometry: {self.prefix}: N{self.n}/K{self.k}')
+        layer._g256_device = attrs.get('device')
+        register_packed(layer, [(self.fields[0], (self.n // 16, self.k // 256, 32, 16), torch.uint32),
+                                (self.fields[1], (self.n // 16, self.k // 256, 16), torch.uint32)])
+
+    def process_weights_after_loading(self, layer):
+        if layer._g256_loaded != set(self.fields):
+            raise ValueError(f'Incomplete packed weights: {self.prefix}')
+        layer._g256_ready = True
+
+    def bind(self, runtime, slot):
+        self.runtime, self.slot = runtime, slot
+
+    def apply(self, layer, x, bias=None):
+        if self.runtime is None or not layer._g256_ready or bias is not None:
+            raise RuntimeError('G256 requires loaded weights and a bound worker')
+        shape = x.shape[:-1]
+        x = x.reshape(-1, self.k).contiguous()
+        out = torch.empty((x.shape[0], self.n), dtype=x.dtype, device=x.device)
+        native.dense_out(x, layer.g256_codes, layer.g256_metadata, self.runtime.workspace, out,
+                         self.runtime.slots[self.slot], self.runtime.capacity, self.n, self.k,
+                         self.runtime.dense_geometry, self.runtime.dense_a8_max_rows)
+        return out.view(*shape, self.n)
+
+
+class W8HeadMethod(G256LinearMethod):
+    """The W8 LM head (method.py:65-91): codes uint32 [15520, 128, 4, 16] and
+    scales fp16 [248320, 16]; apply runs 64-row slices through head_out."""
+    fields = ('head_tilebank_codes', 'head_scales')
+
+    def create_weights(self, layer, input_size_per_partition, output_partition_sizes, input_size, output_size,
+                       params_dtype, **attrs):
+        self.k, self.n = input_size, output_size
+        if (input_size_per_partition, input_size, output_size, params_dtype,
+                getattr(layer, 'tp_size', 1)) != (2048, 2048, native.HEAD_VOCAB, torch.bfloat16, 1):
+            raise ValueError('W8 head requires the full TP1 Ornith vocabulary')
+        layer._g256_device = attrs.get('device')
+        register_packed(layer, [(self.fields[0], (native.HEAD_VOCAB // 16, 128, 4, 16), torch.uint32),
+                                (self.fields[1], (native.HEAD_VOCAB, 16), torch.float16)])
+
+    def apply(self, layer, x, bias=None):
+        if self.runtime is None or not layer._g256_ready or bias is not None:
+            raise RuntimeError('W8 head requires loaded weights and a bound worker')
+        x = x.reshape(-1, self.k).contiguous()
+        out = torch.empty((x.shape[0], self.n), dtype=x.dtype, device=x.device)
+        for start in range(0, x.shape[0], native.HEAD_ROWS):
+            native.head_out(x[start:start + native.HEAD_ROWS], layer.head_tilebank_codes, layer.head_scales,
+                            self.runtime.workspace, out[start:start + native.HEAD_ROWS],
+                            self.runtime.slots[self.slot], self.runtime.head_geometry)
+        return out
 
 
 class G256MoEMethod:

@@ -16,10 +16,29 @@ NUMERIC_MASK = 59
 
 
 class Runtime:
-    def __init__(self, layers, capacity, device, settings=None):
+    """`layers` names the layers that own a flag slot (in slot order);
+    `dense_shapes` lists the (N, K) of the dense G256 layers sharing the arena
+    and `head` says whether the W8 head does (runtime.py:36-40 sizes the arena
+    the same way).  Settings: the routed activation bits of native.configure,
+    dense_geometry / head_geometry (0, 1 or 2) and dense_a8_max_rows (32 or
+    64, the row count up to which dense calls take the A8 projection)."""
+
+    def __init__(self, layers, capacity, device, settings=None, dense_shapes=(), head=False):
+        settings = settings or {}
         self.capacity = int(capacity)
         self.device = torch.device(device)
-        size = native.configure(settings or {}, self.capacity)
+        self.dense_geometry = settings.get('dense_geometry', 2)
+        self.dense_a8_max_rows = settings.get('dense_a8_max_rows', 32)
+        if self.dense_a8_max_rows not in (32, 64):
+            raise ValueError('G256 dense A8 crossover must be 32 or 64 rows')
+        self.head_geometry = settings.get('head_geometry', 2)
+        if self.dense_geometry not in (0, 1, 2) or self.head_geometry not in (0, 1, 2):
+            raise ValueError('Native geometry must be 0, 1, or 2')
+        size = native.configure(settings, self.capacity)
+        if dense_shapes:
+            size = max(size, native.dense_workspace_bytes(self.capacity, sorted(set(dense_shapes))))
+        if head:
+            size = max(size, native.head_get_layout(native.HEAD_ROWS).workspace_bytes)
         self.workspace = torch.empty(size, dtype=torch.uint8, device=self.device)
         self.error_flags = torch.zeros(len(layers), dtype=torch.int32, device=self.device)
         self.slots = tuple(self.error_flags[i:i + 1] for i in range(len(layers)))

@@ -118,3 +118,58 @@ def test_method_needs_binding_and_gpu_banks(M):
         m2.prepare_n32_weights(torch.nn.Module())
     with pytest.raises(RuntimeError, match='loaded, unbound'):
         m2.prepare_n32_weights(unloaded)
+
+
+def test_dense_linear_registration_and_loader(M):
+    layer = torch.nn.Module()
+    method = M.G256LinearMethod('model.layers.0.linear_attn.in_proj_qkvz')
+    method.create_weights(layer, 2048, [12288], 2048, 12288, torch.bfloat16)
+    assert layer.g256_codes.shape == (768, 8, 32, 16) and layer.g256_metadata.shape == (768, 8, 16)
+    for bad in [dict(input_size_per_partition=1024), dict(output_size=12304), dict(input_size=2100),
+                dict(params_dtype=torch.float16)]:
+        args = dict(input_size_per_partition=2048, output_partition_sizes=[12288], input_size=2048,
+                    output_size=12288, params_dtype=torch.bfloat16)
+        args.update(bad)
+        if 'input_size' in bad:
+            args['input_size_per_partition'] = bad['input_size']
+        if 'output_size' in bad:
+            args['output_partition_sizes'] = [bad['output_size']]
+        with pytest.raises(ValueError, match='Unsupported G256 linear geometry'):
+            M.G256LinearMethod('x').create_weights(torch.nn.Module(), **args)
+    codes = torch.zeros(layer.g256_codes.shape, dtype=torch.uint32)
+    with pytest.raises(ValueError, match='mismatch'):
+        layer.g256_codes.weight_loader(layer.g256_codes, codes[:1])
+    with pytest.raises(ValueError, match='Duplicate or late'):
+        layer.g256_codes.weight_loader(layer.g256_metadata, codes)       # wrong destination
+    layer.g256_codes.weight_loader(layer.g256_codes, codes)
+    with pytest.raises(ValueError, match='Duplicate or late'):
+        layer.g256_codes.weight_loader(layer.g256_codes, codes)
+    with pytest.raises(ValueError, match='Incomplete packed weights'):
+        method.process_weights_after_loading(layer)
+    layer.g256_metadata.weight_loader(layer.g256_metadata, _valid(layer.g256_metadata.shape))
+    method.process_weights_after_loading(layer)
+    with pytest.raises(ValueError, match='Duplicate or late'):
+        layer.g256_metadata.weight_loader(layer.g256_metadata, _valid(layer.g256_metadata.shape))
+    with pytest.raises(RuntimeError, match='bound worker'):
+        method.apply(layer, torch.zeros((1, 2048), dtype=torch.bfloat16))
+
+
+def test_w8_head_registration(M):
+    layer = torch.nn.Module()
+    M.W8HeadMethod('lm_head').create_weights(layer, 2048, [248320], 2048, 248320, torch.bfloat16, device='meta')
+    assert layer.head_tilebank_codes.shape == (15520, 128, 4, 16) and layer.head_tilebank_codes.dtype == torch.uint32
+    assert layer.head_scales.shape == (248320, 16) and layer.head_scales.dtype == torch.float16
+    with pytest.raises(ValueError, match='full TP1 Ornith vocabulary'):
+        M.W8HeadMethod('lm_head').create_weights(torch.nn.Module(), 2048, [151936], 2048, 151936, torch.bfloat16)
+
+
+def test_runtime_settings_are_checked():
+    R = importlib.import_module('ornith_b200.runtime')
+    with pytest.raises(ValueError, match='32 or 64'):
+        R.Runtime(['a'], 8, 'cpu', {'dense_a8_max_rows': 16})
+    with pytest.raises(ValueError, match='geometry'):
+        R.Runtime(['a'], 8, 'cpu', {'head_geometry': 3})
+    rt = R.Runtime(['a', 'b'], 8, 'cpu', dense_shapes=[(12288, 2048), (2048, 4096)])
+    native = importlib.import_module('ornith_b200.native')
+    assert rt.workspace.numel() >= native.dense_workspace_bytes(8, [(12288, 2048), (2048, 4096)])
+    assert rt.dense_geometry == 2 and rt.dense_a8_max_rows == 32 and len(rt.slots) == 2

@@ -59,3 +59,71 @@ def test_loaded_layer_matches_oracle(S, O, replace):
     ref, _, ref_flags = O.routed_layer(x, w, ids, lw.gate_codes, lw.gate_meta, lw.down_codes, lw.down_meta)
     np.testing.assert_array_equal(out.view(torch.int16).cpu().numpy().view(np.uint16), ref)
     assert runtime.check_error_flags() == [ref_flags] == [0]
+
+
+def test_dense_linear_method_apply(S, O):
+    """G256LinearMethod: packed loads, seal, apply on [..., K] rows through
+    dense_out (A8 up to dense_a8_max_rows rows, bit for bit; the bf16 prefill
+    path beyond, within one bf16 ulp of the exact product of its operands)."""
+    M = importlib.import_module('ornith_b200.method')
+    runtime_mod = importlib.import_module('ornith_b200.runtime')
+    N, K = 1024, 2048
+    rng = np.random.default_rng(17)
+    codes, meta = S.make_dense_bank(rng, N, K)
+    layer = torch.nn.Module()
+    method = M.G256LinearMethod('model.layers.3.mlp.gate_up_proj')
+    method.create_weights(layer, K, [N], K, N, torch.bfloat16, device='cuda')
+    layer.g256_codes.weight_loader(layer.g256_codes, _u32(codes))
+    layer.g256_metadata.weight_loader(layer.g256_metadata, _u32(meta))
+    method.process_weights_after_loading(layer)
+    runtime = runtime_mod.Runtime(['model.layers.3.mlp.gate_up_proj'], 64, 'cuda', dense_shapes=[(N, K)])
+    method.bind(runtime, 0)
+    dev = torch.device('cuda')
+    x = S.make_rows(rng, 6, K)
+    out = method.apply(layer, torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16).view(2, 3, K))
+    torch.cuda.synchronize()
+    assert out.shape == (2, 3, N)
+    ref, _, ref_flags = O.dense_project(x, codes, meta, N, K, 16)
+    np.testing.assert_array_equal(out.reshape(6, N).view(torch.int16).cpu().numpy().view(np.uint16), ref)
+    x = S.make_rows(rng, 40, K)   # above dense_a8_max_rows = 32: the bf16 prefill path
+    out = method.apply(layer, torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16))
+    torch.cuda.synchronize()
+    xt, w, _ = O.dense_prepare_bf16(x, codes, meta, N, K)
+    exact = S.bf16_bits_to_f32(xt).astype(np.float64) @ S.bf16_bits_to_f32(w).astype(np.float64).T
+    want = S.bf16_bits_to_f32(S.f32_to_bf16_bits(exact.astype(np.float32)))
+    got = S.bf16_bits_to_f32(out.view(torch.int16).cpu().numpy().view(np.uint16))
+    assert np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -7 + 1e-6)
+    assert runtime.check_error_flags() == [ref_flags] == [0]
+
+
+def test_w8_head_method_apply_in_64_row_slices(S, O):
+    """W8HeadMethod over the full vocabulary with 70 rows (slices of 64 and 6),
+    sampled tiles bit for bit against the oracle."""
+    M = importlib.import_module('ornith_b200.method')
+    runtime_mod = importlib.import_module('ornith_b200.runtime')
+    native = importlib.import_module('ornith_b200.native')
+    N = native.HEAD_VOCAB
+    dev = torch.device('cuda')
+    layer = torch.nn.Module()
+    method = M.W8HeadMethod('lm_head')
+    method.create_weights(layer, 2048, [N], 2048, N, torch.bfloat16, device='cuda')
+    gen = torch.Generator(device=dev).manual_seed(21)
+    codes = torch.randint(-127, 128, (N // 16, 128, 4, 16, 4), dtype=torch.int8, device=dev, generator=gen)
+    words = codes.view(torch.int32).view(N // 16, 128, 4, 16).view(torch.uint32)
+    scales = (0.01 * torch.randn((N, 16), device=dev, generator=gen).abs()).to(torch.float16).clamp_min(2 ** -14)
+    layer.head_tilebank_codes.weight_loader(layer.head_tilebank_codes, words)
+    layer.head_scales.weight_loader(layer.head_scales, scales)
+    method.process_weights_after_loading(layer)
+    del codes, words
+    runtime = runtime_mod.Runtime(['lm_head'], 64, 'cuda', head=True)
+    method.bind(runtime, 0)
+    x = S.make_rows(np.random.default_rng(22), 70, 2048)
+    out = method.apply(layer, torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16))
+    torch.cuda.synchronize()
+    got = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    w_np = layer.head_tilebank_codes.view(torch.int32).cpu().numpy().view(np.uint32)
+    s_np = layer.head_scales.view(torch.int16).cpu().numpy().view(np.uint16)
+    for t in (0, 9999, N // 16 - 1):
+        ref, _, _ = O.head_project(x, w_np[t:t + 1], s_np[16 * t:16 * t + 16], 16)
+        np.testing.assert_array_equal(got[:, 16 * t:16 * t + 16], ref)
+    assert runtime.check_error_flags() == [0]
