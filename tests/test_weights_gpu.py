@@ -64,7 +64,8 @@ def test_loaded_layer_matches_oracle(S, O, replace):
 def test_dense_linear_method_apply(S, O):
     """G256LinearMethod: packed loads, seal, apply on [..., K] rows through
     dense_out (A8 up to dense_a8_max_rows rows, bit for bit; the bf16 prefill
-    path beyond, within one bf16 ulp of the exact product of its operands)."""
+    path beyond, within one bf16 ulp plus an fp32 summation error bound of the
+    exact product of its operands, and relative L2 <= 1e-3)."""
     M = importlib.import_module('ornith_b200.method')
     runtime_mod = importlib.import_module('ornith_b200.runtime')
     N, K = 1024, 2048
@@ -89,10 +90,14 @@ def test_dense_linear_method_apply(S, O):
     out = method.apply(layer, torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16))
     torch.cuda.synchronize()
     xt, w, _ = O.dense_prepare_bf16(x, codes, meta, N, K)
-    exact = S.bf16_bits_to_f32(xt).astype(np.float64) @ S.bf16_bits_to_f32(w).astype(np.float64).T
+    xa, wa = S.bf16_bits_to_f32(xt).astype(np.float64), S.bf16_bits_to_f32(w).astype(np.float64)
+    exact = xa @ wa.T
+    magnitude = np.abs(xa) @ np.abs(wa).T   # sum of |products|: scale of the fp32 summation error
     want = S.bf16_bits_to_f32(S.f32_to_bf16_bits(exact.astype(np.float32)))
     got = S.bf16_bits_to_f32(out.view(torch.int16).cpu().numpy().view(np.uint16))
-    assert np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -7 + 1e-6)
+    # one bf16 ulp of the result plus an fp32 summation error bound over K terms
+    assert np.all(np.abs(got - want) <= np.abs(want) * 2.0 ** -7 + magnitude * 2.0 ** -16)
+    assert np.linalg.norm(got - want) <= 1e-3 * np.linalg.norm(want)
     assert runtime.check_error_flags() == [ref_flags] == [0]
 
 
