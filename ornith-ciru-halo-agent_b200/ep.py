@@ -11,8 +11,10 @@ compact (any batch; ranks may hold different token counts):
   1. dispatch plan: for every destination rank d, the local tokens with at
      least one expert on d (deduplicated per (token, rank)), with their eight
      ids rewritten to d's local expert numbers (-1 for slots owned elsewhere);
-  2. exchange: counts, then token rows (bf16 pairs carried as int32) and local
-     ids (all_to_all_single with variable splits; NCCL on GPUs, gloo on CPU);
+  2. exchange: one all_to_all of (tokens sent, slots to come back) per rank
+     pair and a single host synchronisation for every split size of the
+     layer, then token rows (bf16 pairs carried as int32) and local ids
+     (all_to_all_single with variable splits; NCCL on GPUs, gloo on CPU);
   3. expert compute on the received rows with the local banks; the fp32
      down projections of the valid slots are gathered in (token, slot) order;
   4. return exchange of those rows, one per (token, slot) owned by d;
@@ -100,51 +102,68 @@ class DispatchPlan:
     token_index: torch.Tensor  # [sum(send_counts)] local token of each sent row, grouped by rank
     local_ids: torch.Tensor    # [sum(send_counts), 8] ids in the destination's numbering, -1 elsewhere
     slot_mask: torch.Tensor    # [sum(send_counts), 8] True where the slot is owned by the destination
+    dest: torch.Tensor = None  # [sum(send_counts)] destination rank of each sent row
+
+
+def _owner_mask(ids, world, placement):
+    """Device half of the dispatch plan: (mask [world, T, 8] of the slots each
+    rank owns, local ids, int64 [world, 2] = (tokens sent, slots to come back)
+    per destination).  No host synchronisation."""
+    placement = placement or contiguous_placement(world, ids.device)
+    owner, lid = map_ids(ids, placement)
+    dest = torch.arange(world, device=ids.device).view(-1, 1, 1)
+    mask = owner.unsqueeze(0) == dest                      # [world, T, 8]
+    counts = torch.stack([mask.any(dim=2).sum(dim=1), mask.sum(dim=(1, 2))], dim=1).to(torch.int64)
+    return mask, lid, counts.contiguous()
+
+
+def _plan_from_mask(mask, lid, ids, send_counts, home_counts):
+    """Host-sized half of the plan: the (destination, token) pairs, grouped by
+    destination and ascending in token; nonzero_static with the known total
+    needs no host synchronisation."""
+    sent = torch.nonzero_static(mask.any(dim=2), size=sum(send_counts))   # (d, t)
+    d, tok = sent[:, 0], sent[:, 1]
+    slot_mask = mask[d, tok]
+    local = torch.where(slot_mask, lid[tok], torch.full_like(slot_mask, -1, dtype=ids.dtype))
+    return DispatchPlan(send_counts, home_counts, tok, local.to(torch.int32).contiguous(), slot_mask, d)
 
 
 def build_dispatch(ids, world, placement=None):
     """Group each token's slots by owning rank (pure tensor logic, any device;
     one host synchronisation for the split sizes)."""
-    placement = placement or contiguous_placement(world, ids.device)
-    owner, lid = map_ids(ids, placement)
-    dest = torch.arange(world, device=ids.device).view(-1, 1, 1)
-    mask = owner.unsqueeze(0) == dest                      # [world, T, 8]
-    sent = mask.any(dim=2).nonzero()                       # (d, t), grouped by d, t ascending
-    d, tok = sent[:, 0], sent[:, 1]
-    slot_mask = mask[d, tok]
-    local = torch.where(slot_mask, lid[tok], torch.full_like(slot_mask, -1, dtype=ids.dtype))
-    counts = torch.stack([torch.bincount(d, minlength=world),
-                          torch.zeros(world, dtype=torch.int64, device=ids.device).index_add_(
-                              0, d, slot_mask.sum(dim=1))]).tolist()
-    return DispatchPlan(counts[0], counts[1], tok, local.to(torch.int32).contiguous(), slot_mask)
+    mask, lid, counts = _owner_mask(ids, world, placement)
+    host = counts.tolist()
+    return _plan_from_mask(mask, lid, ids, [int(r[0]) for r in host], [int(r[1]) for r in host])
+
+
+def dispatch_with_counts(group, world, ids, placement=None):
+    """The dispatch plan plus what every peer sends here: one all_to_all of
+    the (tokens sent, slots to come back) pairs and the layer's single host
+    synchronisation, for all four split lists.  Returns (plan, recv_counts:
+    token rows arriving from each rank, back_counts: (token, slot) rows this
+    rank returns to each rank)."""
+    mask, lid, counts = _owner_mask(ids, world, placement)
+    got = torch.empty_like(counts)
+    _a2a(group, got, counts, [1] * world, [1] * world)
+    both = torch.cat([counts, got], dim=1).tolist()          # the single host synchronisation
+    plan = _plan_from_mask(mask, lid, ids, [int(r[0]) for r in both], [int(r[1]) for r in both])
+    return plan, [int(r[2]) for r in both], [int(r[3]) for r in both]
 
 
 def _a2a(group, out, inp, out_splits, in_splits):
     dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
 
 
-def exchange_rows(group, world, plan, x):
-    """Send each rank its token rows and local ids; returns (x_recv, ids_recv, recv_counts)."""
+def exchange_rows(group, world, plan, x, recv_counts):
+    """Send each rank its token rows and local ids; returns (x_recv, ids_recv)."""
     dev = x.device
-    send = torch.tensor(plan.send_counts, dtype=torch.int64, device=dev)
-    recv = torch.empty_like(send)
-    _a2a(group, recv, send, [1] * world, [1] * world)
-    recv_counts = [int(v) for v in recv.tolist()]
     n_in = sum(recv_counts)
     x_words = x.contiguous().view(torch.int32)[plan.token_index].contiguous()   # [n, 1024]
     x_recv = torch.empty((n_in, H // 2), dtype=torch.int32, device=dev)
     _a2a(group, x_recv, x_words, recv_counts, plan.send_counts)
     ids_recv = torch.empty((n_in, TOP), dtype=torch.int32, device=dev)
     _a2a(group, ids_recv, plan.local_ids, recv_counts, plan.send_counts)
-    return x_recv.view(x.dtype), ids_recv, recv_counts
-
-
-def valid_counts(ids_recv, recv_counts):
-    """(token, slot) rows with a valid local id, per source rank (host ints)."""
-    src = torch.repeat_interleave(torch.arange(len(recv_counts), device=ids_recv.device),
-                                  torch.tensor(recv_counts, device=ids_recv.device), output_size=ids_recv.shape[0])
-    per = torch.zeros(len(recv_counts), dtype=torch.int64, device=ids_recv.device)
-    return per.index_add_(0, src, (ids_recv >= 0).sum(dim=1)).tolist()
+    return x_recv.view(x.dtype), ids_recv
 
 
 def return_rows(group, world, plan, back_counts, out_rows):
@@ -175,14 +194,14 @@ def route_row_index(T, plan, device):
 def ep_layer(group, world, x, ids, weights, compute, combine, placement=None):
     """One expert-parallel layer call, compact exchange.
 
-    compute(x_recv, ids_recv) -> fp32 [n_valid, 2048]: the rows of the received
-    slots with a valid id, in (token, slot) order; combine(rows [n, 2048],
-    row_index [T, 8], weights, ids) -> output.  Both are injected so that the
-    host logic also runs on CPU ranks."""
-    plan = build_dispatch(ids, world, placement)
-    x_recv, ids_recv, recv_counts = exchange_rows(group, world, plan, x)
-    back_counts = valid_counts(ids_recv, recv_counts)
-    out_rows = compute(x_recv, ids_recv)
+    compute(x_recv, ids_recv, n_valid) -> fp32 [n_valid, 2048]: the rows of the
+    received slots with a valid id, in (token, slot) order (n_valid, known on
+    the host, is their count); combine(rows [n, 2048], row_index [T, 8],
+    weights, ids) -> output.  Both are injected so that the host logic also
+    runs on CPU ranks."""
+    plan, recv_counts, back_counts = dispatch_with_counts(group, world, ids, placement)
+    x_recv, ids_recv = exchange_rows(group, world, plan, x, recv_counts)
+    out_rows = compute(x_recv, ids_recv, sum(back_counts))
     got = return_rows(group, world, plan, back_counts, out_rows)
     return combine(got, route_row_index(x.shape[0], plan, got.device), weights, ids)
 
@@ -212,17 +231,16 @@ def ep_layer_partial(group, world, x, ids, weights, compute_partial, combine, pl
     compute_partial(x_recv, ids_recv, w_recv) -> fp32 [n_recv, 2048]: per
     received token, its routing weights times this rank's projections summed
     in slot order."""
-    plan = build_dispatch(ids, world, placement)
-    x_recv, ids_recv, recv_counts = exchange_rows(group, world, plan, x)
+    plan, recv_counts, _ = dispatch_with_counts(group, world, ids, placement)
+    x_recv, ids_recv = exchange_rows(group, world, plan, x, recv_counts)
     w_send = torch.where(plan.slot_mask, weights[plan.token_index], torch.zeros_like(weights[plan.token_index]))
     w_recv = torch.empty((sum(recv_counts), TOP), dtype=torch.float32, device=x.device)
     _a2a(group, w_recv, w_send.contiguous(), recv_counts, plan.send_counts)
     part = compute_partial(x_recv, ids_recv, w_recv)
     got = torch.empty((plan.token_index.numel(), H), dtype=torch.float32, device=x.device)
     _a2a(group, got, part.contiguous(), plan.send_counts, recv_counts)
-    dest = torch.repeat_interleave(torch.arange(world, device=x.device),
-                                   torch.tensor(plan.send_counts, device=x.device), output_size=got.shape[0])
-    return rank_sum(combine, got, partial_row_index(x.shape[0], world, plan.token_index, dest, x.device), weights)
+    return rank_sum(combine, got, partial_row_index(x.shape[0], world, plan.token_index, plan.dest, x.device),
+                    weights)
 
 
 def ep_layer_fixed(group, world, x, ids, weights, compute_block, combine, placement=None):
@@ -327,9 +345,12 @@ class ExpertParallelMoE:
                             self.capacity, native.stream(x_recv)), 'expert-parallel compute')
         return n
 
-    def compute(self, x_recv, ids_recv):
+    def compute(self, x_recv, ids_recv, n_valid=None):
         n = self._layer(x_recv, ids_recv)
-        sel = (ids_recv >= 0).view(-1).nonzero().flatten().to(torch.int32)  # (token, slot) order
+        valid = (ids_recv >= 0).view(-1)
+        # (token, slot) order; with the count known no host synchronisation
+        sel = (valid.nonzero() if n_valid is None else torch.nonzero_static(valid, size=n_valid))
+        sel = sel.flatten().to(torch.int32)
         rows = torch.empty((sel.numel(), H), dtype=torch.float32, device=x_recv.device)
         self.native.gather_route_rows(self.workspace, n, self.capacity, sel, rows, self.flags)
         return rows

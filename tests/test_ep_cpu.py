@@ -105,7 +105,8 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
             placement = ep.contiguous_placement(world)
         table = torch.tensor(placement.experts_of(rank))
 
-        def compute(xr, ir):
+        def compute(xr, ir, n_valid):
+            assert n_valid == int((ir >= 0).sum())      # the host count the exchange delivered
             return fake_rows(xr, ir, table)[ir >= 0] if xr.shape[0] else torch.zeros((0, H))
 
         def compute_block(xa, ia):
