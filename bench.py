@@ -380,7 +380,7 @@ def run_dense(args):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    print(json.dumps({
+    line = {
         'metric': 'dense G256 projection rows/s (40-bank step) & % of HBM roofline', 'value': round(
             M * L * args.steps / (ms / 1e3), 3), 'unit': 'row-projections/s', 'n_gpus': 1, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(ms / args.steps, 4), 'higher_is_better': True,
@@ -397,7 +397,10 @@ def run_dense(args):
                      'algorithmic_bytes_per_launch': algo, 'launch_ms': round(launch_ms, 5),
                      'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'},
         'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': True,
-    }), flush=True)
+    }
+    if not args.no_cpu_baseline:
+        line['cpu_baseline'] = cpu_baseline_projection(cfg, min(args.cpu_seconds, 5.0))
+    print(json.dumps(line), flush=True)
 
 
 def run_head(args):
@@ -468,7 +471,7 @@ def run_head(args):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    print(json.dumps({
+    line = {
         'metric': 'W8 LM head rows/s & % of HBM roofline', 'value': round(M * args.steps / (ms / 1e3), 3),
         'unit': 'rows/s', 'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup,
         'ms_per_step': round(launch_ms, 4), 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
@@ -484,7 +487,10 @@ def run_head(args):
                      'algorithmic_bytes_per_launch': algo, 'launch_ms': round(launch_ms, 5),
                      'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'},
         'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': True,
-    }), flush=True)
+    }
+    if not args.no_cpu_baseline:
+        line['cpu_baseline'] = cpu_baseline_projection(cfg, min(args.cpu_seconds, 5.0))
+    print(json.dumps(line), flush=True)
 
 
 def launches_per_step(lib, step_fn):
@@ -780,9 +786,7 @@ def run_reference(args):
     if cfg.get('dense'):
         return run_reference_dense(args, cfg, O)
     if cfg.get('head'):
-        print(json.dumps({'impl': 'reference', 'unavailable': 'the head bench line has no CPU reference arm; '
-                          'tests compare the reference head source compiled for the CPU on sampled columns'}))
-        return
+        return run_reference_head(args, cfg, O)
     S, layer = _cpu_layer()
     tab = np.load(ROOT / 'tests' / 'golden' / 'shared_math_tables.npz')
     rng = np.random.default_rng(10)
@@ -857,6 +861,69 @@ def run_reference_dense(args, cfg, O):
         'e2e': {'value': round(value, 4), 'unit': 'row-projections/s', 'h2d_bytes_per_step': 0,
                 'd2h_bytes_per_step': 0},
     }), flush=True)
+
+
+def _synthetic_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('ornith_synthetic', ROOT / 'ornith-ciru-halo-agent_b200' / 'synthetic.py')
+    S = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(S)
+    return S
+
+
+def run_reference_head(args, cfg, O):
+    """The reference's head library compiled for the CPU (oracle/_ref) on a
+    65,536-column slice of the vocabulary (a size it supports), scaled to the
+    full 248,320 columns."""
+    S = _synthetic_module()
+    rng = np.random.default_rng(10)
+    M, N, slice_n = cfg['T'], cfg['N'], 65536
+    words, scales = S.make_head_bank(rng, slice_n)
+    x = S.make_rows(rng, M, 2048)
+    for _ in range(args.warmup):
+        O.ref_head(x, words, scales, slice_n)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.ref_head(x, words, scales, slice_n)
+    call_s = (time.perf_counter() - t0) / args.steps * (N / slice_n)
+    value = M / call_s
+    sample = (f'{args.steps} calls of a {slice_n}-column slice, {M} rows (reference head source compiled for '
+              f'the CPU), scaled to {N} columns')
+    print(json.dumps({
+        'impl': 'reference', 'metric': 'W8 LM head rows/s & % of HBM roofline', 'value': round(value, 4),
+        'unit': 'rows/s', 'n_gpus': 0, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': round(call_s * 1e3, 3), 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+        'dtype': 'int8', 'data': 'synthetic', 'config': {'workload': cfg['name'], 'rows': M},
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'rows/s', 'cores': os.cpu_count() or 1,
+                         'kind': 'reference', 'sample': sample},
+        'e2e': {'value': round(value, 4), 'unit': 'rows/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }), flush=True)
+
+
+def cpu_baseline_projection(cfg, seconds):
+    """The oracle port (C, OpenMP on every host core) on the dense or head
+    workload: repeated single-bank calls for about `seconds`, as rows (or row
+    projections) per second."""
+    from oracle import oracle as O
+    S = _synthetic_module()
+    rng = np.random.default_rng(11)
+    M, N, K = cfg['T'], cfg['N'], cfg['K']
+    if cfg.get('head'):
+        words, scales = S.make_head_bank(rng, N)
+        call = lambda x: O.head_project(x, words, scales, N)  # noqa: E731
+    else:
+        codes, meta = S.make_dense_bank(rng, N, K)
+        call = lambda x: O.dense_project(x, codes, meta, N, K, 16)  # noqa: E731
+    x = S.make_rows(rng, M, K)
+    call(x)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n == 0:
+        call(x)
+        n += 1
+    per_call = (time.perf_counter() - t0) / n
+    return {'value': round(M / per_call, 4), 'unit': 'rows/s' if cfg.get('head') else 'row-projections/s',
+            'cores': O.set_threads(0), 'kind': 'port',
+            'sample': f'{n} calls of one {N}x{K} bank with {M} rows (oracle C port, OpenMP)'}
 
 
 if __name__ == '__main__':
