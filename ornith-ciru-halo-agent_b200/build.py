@@ -28,9 +28,14 @@ def stale():
 
 
 def build(force=False, verbose=False):
+    """Compile the library.  ORNITH_MOE_B200_NVCC_FLAGS adds nvcc flags, for
+    the build-time options of the kernels (-DORNITH_PREFILL_F32X2=1,
+    -DORNITH_DECODE_L2_PREFETCH=1, the trace builds); the default build sets
+    none of them."""
     if not force and not stale():
         return LIB
-    cmd = [NVCC, *FLAGS, *[str(CSRC / s) for s in SOURCES], '-o', str(LIB)]
+    extra = os.environ.get('ORNITH_MOE_B200_NVCC_FLAGS', '').split()
+    cmd = [NVCC, *FLAGS, *extra, *[str(CSRC / s) for s in SOURCES], '-o', str(LIB)]
     if verbose:
         cmd.insert(1, '-Xptxas=-v')
     subprocess.run(cmd, check=True)

@@ -916,6 +916,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         // its parity is exact.  Every issued stage is recorded per slot for
         // the drain at exit.
         volatile int* misc = s.misc;
+#if ORNITH_DECODE_L2_PREFETCH
+        // Warm L2 with this CTA's down blocks while its gate stages stream, so
+        // that the down stages, issued only after the gate stages landed, read
+        // from L2.  A prefetch changes no result.  Built with
+        // -DORNITH_DECODE_L2_PREFETCH=1 (not the default build yet: it has not
+        // been run on a GPU).
+        for (int d2 = lane; d2 < 2 * nd; d2 += 32) {
+            const int dj = thr ? dj0 + d2 / 2 : jstart + (d2 / 2) * G;
+            const int e = s.act_e[dj / 64], tile = dj % 64, g = d2 % 2;
+            const int groups = kI / kG;
+            const uint32_t* codes = e == kE ? a.sdown_codes : a.down_codes + size_t(e) * kH * (kI / 8);
+            const uint32_t* meta = e == kE ? a.sdown_meta : a.down_meta + size_t(e) * kH * groups;
+            codes += (size_t(tile) * groups + g) * 1024;
+            meta += (size_t(tile) * groups + g) * 32;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(codes), "r"(4096u) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(meta), "r"(128u) : "memory");
+        }
+#endif
         int st0 = 0;
         while (st0 < total_stages) {
             if (st0 == 16 * ng && ng > 0) {

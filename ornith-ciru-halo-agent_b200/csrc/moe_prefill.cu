@@ -145,6 +145,40 @@ __device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t v) {
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): two independent IEEE
+// round-to-nearest operations per instruction, the low half first.  Results
+// are those of the scalar __f*_rn forms lane for lane.  Used by the epilogue
+// built with -DORNITH_PREFILL_F32X2=1 (not the default build yet: it has not
+// been run on a GPU).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_pack_bits(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Named barrier that also ANDs a predicate across the participating threads,
@@ -477,12 +511,29 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 const int ssumi = reinterpret_cast<const int32_t*>(mslot + kNT * 4 + kMT * 4)[row];
                 const float ssum = __fmul_rn(sa, float(ssumi));
                 const uint32_t base = tmem + lane_base + uint32_t(b * kNT);
+#if ORNITH_PREFILL_F32X2
+                const uint64_t sa2 = f2_pack(sa, sa), ssum2 = f2_pack(ssum, ssum);
+                const uint64_t magic2 = f2_pack_bits(kMagic, kMagic);
+#endif
 #pragma unroll
                 for (int part = 0; part < 4; ++part) {
                     const int col = (part < 2 ? c0 : c1) + 16 * (part & 1);
                     uint32_t r[16];
                     tmem_ld16(base + col, r);
                     tmem_wait_ld();
+#if ORNITH_PREFILL_F32X2
+                    // the same six operations per accumulator on column pairs
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const uint64_t sw2 = *reinterpret_cast<const uint64_t*>(swf + col + 2 * q);
+                        const uint64_t of2 = *reinterpret_cast<const uint64_t*>(offf + col + 2 * q);
+                        const uint64_t fd2 = f2_sub(f2_pack_bits(r[2 * q], r[2 * q + 1]), magic2);
+                        const uint64_t term2 = f2_add(f2_mul(sw2, f2_mul(sa2, fd2)), f2_mul(of2, ssum2));
+                        float& a0 = acc[part * 16 + 2 * q];
+                        float& a1 = acc[part * 16 + 2 * q + 1];
+                        f2_unpack(f2_add(f2_pack(a0, a1), term2), a0, a1);
+                    }
+#else
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float4 sw4 = *reinterpret_cast<const float4*>(swf + col + 4 * q);
@@ -497,6 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                             acc[part * 16 + i] = __fadd_rn(acc[part * 16 + i], term);
                         }
                     }
+#endif
                     tmem_st16_const(base + col, kMagic);
                 }
                 tmem_wait_st();
