@@ -146,6 +146,7 @@ __device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t v) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+#if ORNITH_PREFILL_F32X2
 // Packed fp32 pairs (sm_100 f32x2 arithmetic): two independent IEEE
 // round-to-nearest operations per instruction, the low half first.  Results
 // are those of the scalar __f*_rn forms lane for lane.  Used by the epilogue
@@ -179,6 +180,7 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+#endif
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Named barrier that also ANDs a predicate across the participating threads,
