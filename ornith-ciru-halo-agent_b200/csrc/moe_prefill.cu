@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 const uint32_t base = tmem + lane_base + uint32_t(b * kNT);
 #if ORNITH_PREFILL_F32X2
                 const uint64_t sa2 = f2_pack(sa, sa), ssum2 = f2_pack(ssum, ssum);
-                const uint64_t magic2 = f2_pack_bits(kMagic, kMagic);
+                const uint64_t magic2 = f2_pack(kMagicF, kMagicF);
 #endif
 #pragma unroll
                 for (int part = 0; part < 4; ++part) {
