@@ -13,6 +13,10 @@
       Outputs of the reference's own W8 head library (kernels/head/, compiled
       for the CPU) on the seeded HEAD_CASES: logits, fp32 projections, raw
       group dots and flags.
+  routed_reference_digests.npz
+      sha256 digests of the reference routed library's outputs (and its flags)
+      on the larger DIGEST_CASES (T = 32, 64, 1120), whose outputs are too big
+      to commit.
   routed_reference_outputs.npz
       Outputs of the reference's own routed library (kernels/routed_storage/,
       compiled for the CPU by oracle/build_ref.py) on seeded synthetic cases.
@@ -20,7 +24,7 @@
       synthetic generator, and the sha256 of the regenerated inputs is stored
       so that generator drift is detected.
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/reference] [--only dense|head]
+Usage: python tests/golden/make_golden.py [--reference /path/to/reference] [--only dense|head|digests]
 """
 import argparse
 import hashlib
@@ -150,13 +154,15 @@ def digest(*arrays):
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument('--reference', default='/root/reference')
-    parser.add_argument('--only', choices=['dense', 'head'], default=None)
+    parser.add_argument('--only', choices=['dense', 'head', 'digests'], default=None)
     args = parser.parse_args()
     ref = Path(args.reference)
-    if args.only != 'head':
+    if args.only in (None, 'dense'):
         write_dense()
-    if args.only != 'dense':
+    if args.only in (None, 'head'):
         write_head()
+    if args.only in (None, 'digests'):
+        write_digests()
     if args.only:
         return
     import torch
@@ -216,6 +222,31 @@ def main():
         store[f'config1/flags_{key}'] = np.array(flags, np.uint32)
     np.savez_compressed(OUT / 'routed_reference_outputs.npz', **store)
     print('wrote', OUT / 'routed_reference_outputs.npz')
+
+
+# (name, case seed, T, pad fraction, entry) on the seed-1 layer
+DIGEST_CASES = [
+    ('t32_a8', 51, 32, 0.05, 'ornith_routed_direct_launch'),
+    ('t64_a4', 52, 64, 0.05, 'ornith_routed_direct_launch_a4'),
+    ('t1120_a4prefill', 53, 1120, 0.05, 'ornith_routed_direct_launch_a4_prefill'),
+]
+
+
+def write_digests():
+    S = _synthetic()
+    layer = S.make_layer(np.random.default_rng(1))
+    banks = (layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta)
+    store = {}
+    for name, case_seed, T, pad, entry in DIGEST_CASES:
+        x, w, ids = make_case(S, layer, case_seed, T, pad, 0, '')
+        out, _, flags, st = O.ref_routed(x, w, ids, *banks, entry=entry)
+        assert st == 0, (name, st)
+        store[f'{name}/inputs_sha256'] = np.array(digest(x, w, ids))
+        store[f'{name}/out_sha256'] = np.array(digest(out))
+        store[f'{name}/flags'] = np.array(flags, np.uint32)
+        print(name, 'flags', flags)
+    np.savez_compressed(OUT / 'routed_reference_digests.npz', **store)
+    print('wrote', OUT / 'routed_reference_digests.npz')
 
 
 def write_head():

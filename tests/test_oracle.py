@@ -1,6 +1,7 @@
 """CPU: the oracle against the golden vectors and known-answer checks."""
 import hashlib
 import math
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -177,3 +178,18 @@ def test_repack_n16_roundtrip(O):
     r_c, r_m = O.repack_n16_to_n32(np.ascontiguousarray(c16), np.ascontiguousarray(m16), N, K)
     np.testing.assert_array_equal(r_c, c32)
     np.testing.assert_array_equal(r_m, m32)
+
+
+def test_oracle_matches_reference_digests_at_larger_batches(layer1, make_golden, S, O):
+    """T = 32 (A8), 64 (A4) and 1120 (A4 prefill): the oracle's outputs hash to
+    the digests of the compiled reference's outputs (tests/golden/
+    routed_reference_digests.npz; the outputs themselves are too big to keep)."""
+    digests = np.load(Path(__file__).resolve().parent / 'golden' / 'routed_reference_digests.npz')
+    banks = (layer1.gate_codes, layer1.gate_meta, layer1.down_codes, layer1.down_meta)
+    for name, seed, T, pad, entry in make_golden.DIGEST_CASES:
+        x, w, ids = make_golden.make_case(S, layer1, seed, T, pad, 0, '')
+        assert make_golden.digest(x, w, ids) == str(digests[f'{name}/inputs_sha256']), name
+        a8 = entry == 'ornith_routed_direct_launch' or (entry.endswith('_a4_prefill') and T <= 64)
+        out, _, flags = O.routed_layer(x, w, ids, *banks, a8=a8)
+        assert make_golden.digest(out) == str(digests[f'{name}/out_sha256']), name
+        assert flags == int(digests[f'{name}/flags']), name
