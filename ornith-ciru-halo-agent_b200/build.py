@@ -23,7 +23,7 @@ def stale():
     if not LIB.exists():
         return True
     t = LIB.stat().st_mtime
-    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob('*.cuh')) + list((HERE.parent / 'include').glob('*.h'))
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob('*.cuh')) + list(CSRC.glob('*.h')) + list((HERE.parent / 'include').glob('*.h'))
     return any(d.stat().st_mtime > t for d in deps)
 
 

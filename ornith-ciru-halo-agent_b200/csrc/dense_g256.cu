@@ -44,6 +44,7 @@
 #include <cstring>
 
 #include "../../include/ornith_moe_b200.h"
+#include "abi_check.h"
 #include "moe_common.cuh"
 
 namespace ornith {
@@ -332,30 +333,6 @@ __global__ __launch_bounds__(256) void dense_dequant_bf16_kernel(const uint32_t*
     flag_or(flags, f);
 }
 
-struct Range {
-    uintptr_t lo, hi;
-};
-bool range_of(const void* p, size_t n, Range& out) {
-    const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
-    if (!p || n > UINTPTR_MAX - lo) return false;
-    out = {lo, lo + n};
-    return true;
-}
-// Null, misaligned or wrapping pointers, and any overlap between a written
-// buffer (indices >= first_written) and any other buffer, are invalid
-// (dense_g256_consumer.cpp:178-181).
-template <int NB>
-bool buffers_ok(const void* const (&ptr)[NB], const size_t (&bytes)[NB], const uintptr_t (&align)[NB],
-                int first_written) {
-    Range r[NB];
-    for (int i = 0; i < NB; ++i)
-        if (reinterpret_cast<uintptr_t>(ptr[i]) % align[i] || !range_of(ptr[i], bytes[i], r[i])) return false;
-    for (int i = first_written; i < NB; ++i)
-        for (int j = 0; j < NB; ++j)
-            if (i != j && r[i].lo < r[j].hi && r[j].lo < r[i].hi) return false;
-    return true;
-}
-
 std::atomic<bool> g_smem_attr[2][64];
 
 template <int W>
@@ -432,7 +409,7 @@ extern "C" cudaError_t ornith_dense_g256_launch(const void* input, const void* c
     const size_t size[6] = {size_t(M) * K * 2, size_t(N) * K / 2, size_t(N) * (K / kG) * 4, bytes,
                             size_t(M) * N * 2, 4};
     const uintptr_t align[6] = {16, 4, 4, 256, 2, 4};
-    if (!dense::buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
+    if (!buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
     if (M <= dense::kFusedRows)
@@ -458,7 +435,7 @@ extern "C" cudaError_t ornith_dense_g256_launch_n32(const void* input, const voi
     const size_t size[6] = {size_t(M) * K * 2, size_t(N) * K / 2, size_t(N) * (K / kG) * 4, bytes,
                             size_t(M) * N * 2, 4};
     const uintptr_t align[6] = {16, 4, 4, 256, 2, 4};
-    if (!dense::buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
+    if (!buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
     if (M <= dense::kFusedRows)
@@ -482,7 +459,7 @@ extern "C" cudaError_t ornith_dense_g256_prepare_bf16(const void* input, const v
     const size_t size[6] = {size_t(M) * K * 2, size_t(N) * K / 2, size_t(N) * (K / kG) * 4, size_t(M) * K * 2,
                             size_t(N) * K * 2, 4};
     const uintptr_t align[6] = {16, 16, 4, 16, 16, 4};
-    if (!dense::buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
+    if (!buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
     auto* fl = static_cast<uint32_t*>(flags);
     count_launches(2);
     const size_t warps = size_t(M) * (K / kG);

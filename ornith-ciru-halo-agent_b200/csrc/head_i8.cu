@@ -30,6 +30,7 @@
 #include <climits>
 
 #include "../../include/ornith_moe_b200.h"
+#include "abi_check.h"
 #include "moe_common.cuh"
 
 namespace ornith {
@@ -169,16 +170,6 @@ __global__ __launch_bounds__(256) void head_project_kernel(const uint32_t* codes
     flag_or(flags, f);
 }
 
-struct Range {
-    uintptr_t lo, hi;
-};
-bool range_of(const void* p, size_t n, Range& out) {
-    const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
-    if (!p || n > UINTPTR_MAX - lo) return false;
-    out = {lo, lo + n};
-    return true;
-}
-
 std::atomic<bool> g_smem_attr[2][64];
 
 }  // namespace head
@@ -213,17 +204,7 @@ extern "C" cudaError_t ornith_head_i8_tile_launch(const void* input, const void*
     const size_t size[7] = {size_t(M) * kK * 2, size_t(N) * kK, size_t(N) * kGroups * 2, workspace_bytes,
                             size_t(M) * N * 2, group_dots_bytes, 4};
     const uintptr_t align[7] = {16, 4, 2, 256, 2, 4, 4};
-    Range r[7]{};
-    for (int i = 0; i < 7; ++i) {
-        if (i == 5 && !group_dots) continue;
-        if (reinterpret_cast<uintptr_t>(ptr[i]) % align[i] || !range_of(ptr[i], size[i], r[i]))
-            return cudaErrorInvalidValue;
-    }
-    for (int i = 3; i < 7; ++i)
-        for (int j = 0; j < 7; ++j) {
-            if (i == j || (!group_dots && (i == 5 || j == 5))) continue;
-            if (r[i].lo < r[j].hi && r[j].lo < r[i].hi) return cudaErrorInvalidValue;
-        }
+    if (!buffers_ok(ptr, size, align, 3, 5)) return cudaErrorInvalidValue;  // group_dots may be null
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
     auto* words = reinterpret_cast<uint32_t*>(ws + l.activation_words);
