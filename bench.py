@@ -49,6 +49,9 @@ NCU_TRAFFIC = {
     'decode1': {'kernel': 'decode_layer_kernel<127>', 'bytes': 14_737_152},
     'decode32': {'kernel': 'decode_layer_kernel<127>', 'bytes': 214_940_160 + 5_720_320},
     'prefill8192': {'kernel': 'mma_kernel<8,1> (gate/up)', 'bytes': 454_199_552 + 119_388_928},
+    # profiles/dense_fused_kernel_dense_qkvz1.md, profiles/head_project_kernel_head_vocab1.md
+    'dense_qkvz1': {'kernel': 'dense_fused_kernel<16>', 'bytes': 13_006_336 + 0},
+    'head_vocab1': {'kernel': 'head_project_kernel<0>', 'bytes': 516_537_856 + 3_437_824},
 }
 # int8 multiply-accumulates per valid route of one layer: gate/up 1024x2048 + down 2048x512
 MACS_PER_ROUTE = 3_145_728
@@ -391,7 +394,8 @@ def run_dense(args):
                 'h2d_bytes_per_step': M * K * 2, 'd2h_bytes_per_step': M * N * 2},
         'gpu_launches': int(launches),
         'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
-                     'frac': round(achieved / peak, 4), 'traffic': None,
+                     'frac': round(achieved / peak, 4),
+                     'traffic': NCU_TRAFFIC[args.config]['bytes'] if args.config in NCU_TRAFFIC else None,
                      'kernel': ('one dense call: dense_fused_kernel<16>' if M <= 4 else
                                 'one dense call: dense_quant_kernel + dense_project_kernel<16>'),
                      'algorithmic_bytes_per_launch': algo, 'launch_ms': round(launch_ms, 5),
@@ -482,7 +486,8 @@ def run_head(args):
                 'h2d_bytes_per_step': M * K * 2, 'd2h_bytes_per_step': M * N * 2},
         'gpu_launches': int(launches),
         'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
-                     'frac': round(achieved / peak, 4), 'traffic': None,
+                     'frac': round(achieved / peak, 4),
+                     'traffic': NCU_TRAFFIC[args.config]['bytes'] if args.config in NCU_TRAFFIC else None,
                      'kernel': 'one head launch (head_quant_kernel + head_project_kernel)',
                      'algorithmic_bytes_per_launch': algo, 'launch_ms': round(launch_ms, 5),
                      'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'},
