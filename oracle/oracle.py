@@ -388,3 +388,41 @@ def ref_head(x_bits, words, scales_bits, N, geometry=2, Mcap=None, group_dots=Fa
         proj = ws[layout.projection:layout.projection + M * N * 4].view(np.float32).reshape(M, N).copy()
     res = (out[:M], proj, int(flags[0]), st)
     return res + (dots[:M] if group_dots else None,) if group_dots else res
+
+
+def _bf16_bits(a):
+    b = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    nan = (b & 0x7FFFFFFF) > 0x7F800000
+    r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    return np.where(nan, ((b >> 16) | 0x40).astype(np.uint16), r)
+
+
+def _bf16_f32(bits):
+    return (np.ascontiguousarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def shared_dense(x_bits, sgate_codes, sgate_meta, sdown_codes, sdown_meta, gate_w_bits):
+    """The shared expert in the reference's dense decode form
+    (plugin-site/ornith_g256/iu4_correctness/shared_kernel.py:33-62): the two
+    dense A8 projections restated above (dense_g256_consumer.cpp), vLLM's
+    silu_and_mul (silu in fp32 rounded to bf16, times up rounded to bf16) and
+    bf16(sigmoid(bf16(fp32 sum x*w))) * down.  The elementwise functions and the
+    logit sum are not pinned by the reference (third-party code, unspecified
+    order): numpy's float32 exp and a double sum stand in for them, so callers
+    compare within a tolerance.  Banks in N32 storage with one expert.
+    Returns (out bf16 bits [M, 2048], gate/up flags, down flags)."""
+    x_bits = _c(x_bits, np.uint16).reshape(-1, H)
+    gu, _, gate_flags = dense_project(x_bits, np.asarray(sgate_codes).reshape(-1), np.asarray(sgate_meta).reshape(-1),
+                                      2 * I, H, 32)
+    g, u = _bf16_f32(gu[:, :I]), _bf16_f32(gu[:, I:])
+    with np.errstate(over='ignore'):
+        silu = _bf16_bits(g / (np.float32(1) + np.exp(-g)))
+    act = _bf16_bits(_bf16_f32(silu) * u)
+    down, _, down_flags = dense_project(act, np.asarray(sdown_codes).reshape(-1), np.asarray(sdown_meta).reshape(-1),
+                                        H, I, 32)
+    logit = _bf16_bits((_bf16_f32(x_bits).astype(np.float64) @ _bf16_f32(gate_w_bits).astype(np.float64))
+                       .astype(np.float32))
+    with np.errstate(over='ignore'):
+        sig = _bf16_bits(np.float32(1) / (np.float32(1) + np.exp(-_bf16_f32(logit))))
+    out = _bf16_bits(_bf16_f32(sig)[:, None] * _bf16_f32(down))
+    return out, gate_flags, down_flags

@@ -488,3 +488,53 @@ def head_launch(x, codes, scales, workspace, out, flags, n, capacity=HEAD_ROWS, 
     check(lib().ornith_head_i8_tile_launch(ptr(x), ptr(codes), ptr(scales), ptr(workspace), workspace.numel(),
                                            ptr(out), ptr(group_dots) if group_dots is not None else None, nbytes,
                                            ptr(flags), x.shape[0], capacity, n, geometry, stream(x)), 'W8 head')
+
+
+# ---------------------------------------------------------------------------
+# Shared expert in the reference's dense decode form
+# (plugin-site/ornith_g256/iu4_correctness/shared_kernel.py:33-62, `fixed8`)
+# ---------------------------------------------------------------------------
+SHARED_DENSE_ROWS = 16  # rows per dense N32 launch (ornith_dense_g256_n32_rows)
+
+
+def shared_dense_workspace_bytes():
+    """Workspace for shared_dense_out: the dense N32 launches of 16 rows."""
+    return max(dense_get_layout(SHARED_DENSE_ROWS, 1024, 2048).workspace_bytes,
+               dense_get_layout(SHARED_DENSE_ROWS, 2048, 512).workspace_bytes)
+
+
+def shared_dense_out(x, gate_codes, gate_meta, down_codes, down_meta, gate_weight, workspace, gate_flags,
+                     down_flags):
+    """The shared expert as the reference's production decode computes it
+    (shared_kernel.py:33-62, which overwrites the fused ninth slot's decode
+    rows, shared_live.py:125-137): gate/up = the dense A8 projection of x by
+    the shared expert's N32 gate/up bank (bf16 [M, 1024]); act =
+    bf16(bf16(silu(gate)) * up) in the arithmetic of vLLM's silu_and_mul;
+    down = the dense A8 projection of act by the N32 down bank (bf16
+    [M, 2048]); out = bf16(sigmoid(bf16(sum_k x*w_gate)) * down), the gate
+    logit summed in fp32.  The projections are this library's dense N32
+    launches (16 rows at a time: rows are independent, so the reference's
+    padding to 8 rows changes nothing); the elementwise tail and the logit are
+    torch operations, as the reference's are vLLM and torch operations.
+    gate_flags / down_flags receive the dense flag bits of the two launches."""
+    if (x.ndim != 2 or x.shape[1] != 2048 or x.dtype != torch.bfloat16 or x.device.type != 'cuda'
+            or not x.is_contiguous()):
+        raise ValueError('shared_dense_out requires contiguous CUDA BF16 rows [M, 2048]')
+    if gate_weight.dtype != torch.bfloat16 or gate_weight.numel() != 2048:
+        raise ValueError('shared_dense_out requires a BF16 shared gate weight of 2048 values')
+    result = torch.empty_like(x)
+    M = x.shape[0]
+    if M == 0:
+        return result
+    logit = (x.float() @ gate_weight.reshape(2048, 1).float()).to(torch.bfloat16)   # [M, 1]
+    gate = torch.sigmoid(logit)
+    for first in range(0, M, SHARED_DENSE_ROWS):
+        chunk = x[first:first + SHARED_DENSE_ROWS]
+        m = chunk.shape[0]
+        gu = torch.empty((m, 1024), dtype=torch.bfloat16, device=x.device)
+        dense_n32_out(chunk, gate_codes, gate_meta, workspace, gu, gate_flags, SHARED_DENSE_ROWS, 1024, 2048)
+        act = torch.nn.functional.silu(gu[:, :512].float()).to(torch.bfloat16) * gu[:, 512:]
+        down = torch.empty((m, 2048), dtype=torch.bfloat16, device=x.device)
+        dense_n32_out(act, down_codes, down_meta, workspace, down, down_flags, SHARED_DENSE_ROWS, 2048, 512)
+        result[first:first + m] = gate[first:first + m] * down
+    return result

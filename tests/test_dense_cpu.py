@@ -136,3 +136,30 @@ def test_dense_workspace_bytes_cover_both_paths(native):
     for N, K in shapes:
         assert n >= native.dense_get_layout(64, N, K).workspace_bytes
         assert n >= (64 * K + N * K) * 2
+
+
+def test_shared_dense_oracle_uses_the_reference_projections(layer1, S, O):
+    """The shared expert's dense decode form (shared_kernel.py:33-62): with
+    both projections taken from the reference's dense N32 launch compiled for
+    the CPU, the oracle composition gives the same output bit for bit."""
+    if not O.reference_available('dense_n32'):
+        pytest.skip('oracle/_ref/libref_dense_n32.so not built')
+    x = S.make_tokens(np.random.default_rng(61), 9)
+    out, gf, df = O.shared_dense(x, layer1.sgate_codes, layer1.sgate_meta, layer1.sdown_codes, layer1.sdown_meta,
+                                 layer1.shared_gate_w)
+    entry = 'ornith_dense_g256_launch_n32'
+    gu, _, rgf, st = O.ref_dense(x, layer1.sgate_codes[0], layer1.sgate_meta[0], 1024, 2048, entry=entry)
+    assert st == 0
+    g, u = S.bf16_bits_to_f32(gu[:, :512]), S.bf16_bits_to_f32(gu[:, 512:])
+    with np.errstate(over='ignore'):
+        silu = S.f32_to_bf16_bits(g / (np.float32(1) + np.exp(-g)))
+    act = S.f32_to_bf16_bits(S.bf16_bits_to_f32(silu) * u)
+    down, _, rdf, st = O.ref_dense(act, layer1.sdown_codes[0], layer1.sdown_meta[0], 2048, 512, entry=entry)
+    assert st == 0
+    logit = S.f32_to_bf16_bits((S.bf16_bits_to_f32(x).astype(np.float64)
+                                @ S.bf16_bits_to_f32(layer1.shared_gate_w).astype(np.float64)).astype(np.float32))
+    with np.errstate(over='ignore'):
+        sig = S.f32_to_bf16_bits(np.float32(1) / (np.float32(1) + np.exp(-S.bf16_bits_to_f32(logit))))
+    want = S.f32_to_bf16_bits(S.bf16_bits_to_f32(sig)[:, None] * S.bf16_bits_to_f32(down))
+    np.testing.assert_array_equal(out, want)
+    assert (gf, df) == (rgf, rdf) == (0, 0)
