@@ -711,6 +711,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     }
     __syncthreads();
     if (tid == 0) DECODE_TRACE(12);
+#if ORNITH_DECODE_EARLY_PREFETCH
+    // Latency mode: every CTA knows every route here, so the CTAs share an L2
+    // prefetch of the selected experts' banks (four contiguous ranges each:
+    // gate codes 1 MiB, gate metadata 32 KiB, down codes 512 KiB, down
+    // metadata 16 KiB; CTA b takes slice b of every range) that overlaps the
+    // plan; the ring's bulk copies then find the weights in L2.  A prefetch
+    // changes no result.  Built with -DORNITH_DECODE_EARLY_PREFETCH=1 (not the
+    // default build yet: it has not been run on a GPU).
+    if (small && tid <= R) {
+        int e = -1;
+        if (tid < R) {
+            e = s.ids[tid];
+            if (!id_valid(e)) e = -1;
+            for (int r = 0; r < tid && e >= 0; ++r)
+                if (s.ids[r] == e) e = -1;  // the first route of an expert prefetches it
+        } else if (a.shared) {
+            e = kE;
+        }
+        if (e >= 0) {
+            const bool sh = e == kE;
+            const char* base[4] = {
+                reinterpret_cast<const char*>(sh ? a.sgate_codes : a.gate_codes + size_t(e) * (2 * kI) * (kH / 8)),
+                reinterpret_cast<const char*>(sh ? a.sgate_meta : a.gate_meta + size_t(e) * (2 * kI) * (kH / kG)),
+                reinterpret_cast<const char*>(sh ? a.sdown_codes : a.down_codes + size_t(e) * kH * (kI / 8)),
+                reinterpret_cast<const char*>(sh ? a.sdown_meta : a.down_meta + size_t(e) * kH * (kI / kG))};
+            const uint32_t bytes[4] = {2u * kI * kH / 2, 2u * kI * (kH / kG) * 4, uint32_t(kH) * kI / 2,
+                                       uint32_t(kH) * (kI / kG) * 4};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t chunk = ((bytes[i] + uint32_t(G) - 1) / uint32_t(G) + 15u) & ~15u;
+                const uint32_t start = uint32_t(b) * chunk;
+                if (start < bytes[i]) {
+                    const uint32_t n = min(chunk, bytes[i] - start);
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base[i] + start), "r"(n)
+                                 : "memory");
+                }
+            }
+        }
+    }
+#endif
     if (small) {
         // ---- plan for R <= 32 routes: warp 0 sorts (expert, route) keys -----
         if (warp == 0) {
