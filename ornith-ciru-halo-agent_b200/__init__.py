@@ -4,6 +4,9 @@ routed path of ciru-ai/ornith-ciru-halo-agent).
 Modules:
   native     ctypes binding of libornith_moe_b200.so and the torch custom ops
   runtime    workspace arena and per-layer sticky error flags
+  lifecycle  per-step flag snapshots and worker poisoning (failure detection)
+  method     packed-weight methods and strict checkpoint loaders
+  ep         expert parallelism over torch.distributed
   synthetic  seeded inputs with the benchmark configurations' shapes
   build      nvcc build of the in-tree CUDA library
 
