@@ -46,6 +46,7 @@
 #include "../../include/ornith_moe_b200.h"
 #include "abi_check.h"
 #include "moe_common.cuh"
+#include "nvtx_range.h"
 
 namespace ornith {
 void count_launches(int n);
@@ -410,6 +411,7 @@ extern "C" cudaError_t ornith_dense_g256_launch(const void* input, const void* c
                             size_t(M) * N * 2, 4};
     const uintptr_t align[6] = {16, 4, 4, 256, 2, 4};
     if (!buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
+    NvtxRange range("ornith.dense.a8");
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
     if (M <= dense::kFusedRows)
@@ -436,6 +438,7 @@ extern "C" cudaError_t ornith_dense_g256_launch_n32(const void* input, const voi
                             size_t(M) * N * 2, 4};
     const uintptr_t align[6] = {16, 4, 4, 256, 2, 4};
     if (!buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
+    NvtxRange range("ornith.dense.a8_n32");
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
     if (M <= dense::kFusedRows)
@@ -460,6 +463,7 @@ extern "C" cudaError_t ornith_dense_g256_prepare_bf16(const void* input, const v
                             size_t(N) * K * 2, 4};
     const uintptr_t align[6] = {16, 16, 4, 16, 16, 4};
     if (!buffers_ok(ptr, size, align, 3)) return cudaErrorInvalidValue;
+    NvtxRange range("ornith.dense.prepare_bf16");
     auto* fl = static_cast<uint32_t*>(flags);
     count_launches(2);
     const size_t warps = size_t(M) * (K / kG);

@@ -32,6 +32,7 @@
 #include "../../include/ornith_moe_b200.h"
 #include "abi_check.h"
 #include "moe_common.cuh"
+#include "nvtx_range.h"
 
 namespace ornith {
 void count_launches(int n);
@@ -205,6 +206,7 @@ extern "C" cudaError_t ornith_head_i8_tile_launch(const void* input, const void*
                             size_t(M) * N * 2, group_dots_bytes, 4};
     const uintptr_t align[7] = {16, 4, 2, 256, 2, 4, 4};
     if (!buffers_ok(ptr, size, align, 3, 5)) return cudaErrorInvalidValue;  // group_dots may be null
+    NvtxRange range("ornith.head");
     auto* ws = static_cast<uint8_t*>(workspace);
     auto* fl = static_cast<uint32_t*>(flags);
     auto* words = reinterpret_cast<uint32_t*>(ws + l.activation_words);

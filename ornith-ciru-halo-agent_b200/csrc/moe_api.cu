@@ -13,6 +13,7 @@
 
 #include "../../include/ornith_moe_b200.h"
 #include "moe_layer.cuh"
+#include "nvtx_range.h"
 
 using namespace ornith;
 
@@ -232,8 +233,15 @@ bool force_generic() { return generic_forced(); }
 bool uses_decode(int T) { return !force_generic() && decode_supported(T); }
 
 cudaError_t run_layer(const LayerArgs& a, cudaStream_t stream) {
-    if (uses_decode(a.T)) return launch_decode(a, stream);
-    if (rows_by_position(a.T)) return launch_prefill(a, stream);
+    if (uses_decode(a.T)) {
+        NvtxRange r("ornith.layer.decode");
+        return launch_decode(a, stream);
+    }
+    if (rows_by_position(a.T)) {
+        NvtxRange r("ornith.layer.prefill");
+        return launch_prefill(a, stream);
+    }
+    NvtxRange r("ornith.layer.generic");
     return launch_generic(a, stream);
 }
 

@@ -39,6 +39,7 @@
 // so unpacking a packed code word is two masks, with no byte shuffles.
 // No TMA or bulk load uses cluster multicast.  Every wait is bounded.
 #include "moe_layer.cuh"
+#include "nvtx_range.h"
 
 namespace ornith {
 namespace {
@@ -956,15 +957,21 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     const int T = a.T, R = T * kTop, rows = R + (a.shared ? T : 0);
     const int nblk = min(kPlanBlocks, max(1, (R + 255) / 256));
     count_launches(7);  // plan x3, gather, gate, middle, down; quantisation and combine count their own
-    prefill_count_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
-    prefill_scan_kernel<<<1, 1024, 0, stream>>>(a, nblk);
-    prefill_place_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
-    if ((st = cudaGetLastError()) != cudaSuccess) return st;
-    if ((st = launch_quant_tokens(a, stream)) != cudaSuccess) return st;
+    {
+        NvtxRange r("ornith.prefill.plan");
+        prefill_count_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
+        prefill_scan_kernel<<<1, 1024, 0, stream>>>(a, nblk);
+        prefill_place_kernel<<<nblk, 256, 0, stream>>>(a, nblk);
+        if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    }
     // upper bound of M-tiles (the kernels read the device-side count)
     const int max_tiles = (rows + kMT - 1) / kMT + (kE + 1);
-    pack_gather_kernel<<<max_tiles * 8, 256, 0, stream>>>(a);
-    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    {
+        NvtxRange r("ornith.prefill.pack_tokens");
+        if ((st = launch_quant_tokens(a, stream)) != cudaSuccess) return st;
+        pack_gather_kernel<<<max_tiles * 8, 256, 0, stream>>>(a);
+        if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    }
     MmaArgs g{};
     g.atiles = ws_at<uint8_t>(a, a.L.agate);
     g.asa = ws_at<float>(a, a.L.agate_sa);
@@ -978,11 +985,17 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     g.out = ws_at<float>(a, a.L.middle);
     g.silu_table = a.silu_table;
     g.flags = a.flags;
-    gate<<<min(ds.sms, max_tiles * 4), kThreads, kMmaSmem, stream>>>(g);
-    if ((st = cudaGetLastError()) != cudaSuccess) return st;
-    if (a.a8) pack_middle_kernel<127><<<max_tiles * 32, 256, 0, stream>>>(a);
-    else pack_middle_kernel<7><<<max_tiles * 32, 256, 0, stream>>>(a);
-    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    {
+        NvtxRange r("ornith.prefill.gate_up");
+        gate<<<min(ds.sms, max_tiles * 4), kThreads, kMmaSmem, stream>>>(g);
+        if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    }
+    {
+        NvtxRange r("ornith.prefill.pack_middle");
+        if (a.a8) pack_middle_kernel<127><<<max_tiles * 32, 256, 0, stream>>>(a);
+        else pack_middle_kernel<7><<<max_tiles * 32, 256, 0, stream>>>(a);
+        if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    }
     MmaArgs d = g;
     d.atiles = ws_at<uint8_t>(a, a.L.adown);
     d.asa = ws_at<float>(a, a.L.adown_sa);
@@ -992,8 +1005,12 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     d.scodes = a.sdown_codes;
     d.smeta = a.sdown_meta;
     d.out = ws_at<float>(a, a.L.route_out);
-    down<<<min(ds.sms, max_tiles * 8), kThreads, kMmaSmem, stream>>>(d);
-    if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    {
+        NvtxRange r("ornith.prefill.down");
+        down<<<min(ds.sms, max_tiles * 8), kThreads, kMmaSmem, stream>>>(d);
+        if ((st = cudaGetLastError()) != cudaSuccess) return st;
+    }
+    NvtxRange r("ornith.prefill.combine");
     return launch_combine(a, stream, true);
 }
 
