@@ -27,21 +27,30 @@ def stale():
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(force=False, verbose=False):
-    """Compile the library.  ORNITH_MOE_B200_NVCC_FLAGS adds nvcc flags, for
-    the build-time options of the kernels (-DORNITH_PREFILL_F32X2=1,
-    -DORNITH_DECODE_L2_PREFETCH=1, the trace builds); the default build sets
-    none of them."""
-    if not force and not stale():
+def build(force=False, verbose=False, flags=(), out=None):
+    """Compile the library.  Extra nvcc flags (the kernels' build-time
+    options: -DORNITH_PREFILL_F32X2=1, -DORNITH_DECODE_L2_PREFETCH=1,
+    -DORNITH_DECODE_EARLY_PREFETCH=1, the trace builds) come from `flags` and
+    from ORNITH_MOE_B200_NVCC_FLAGS; the default build sets none of them.
+    `out` writes a variant library elsewhere (always rebuilt), which
+    ORNITH_MOE_B200_LIB then selects at run time, so that a default and a
+    variant build can be measured side by side."""
+    target = Path(out) if out else LIB
+    if not out and not force and not stale():
         return LIB
-    extra = os.environ.get('ORNITH_MOE_B200_NVCC_FLAGS', '').split()
-    cmd = [NVCC, *FLAGS, *extra, *[str(CSRC / s) for s in SOURCES], '-o', str(LIB)]
+    extra = [*flags, *os.environ.get('ORNITH_MOE_B200_NVCC_FLAGS', '').split()]
+    cmd = [NVCC, *FLAGS, *extra, *[str(CSRC / s) for s in SOURCES], '-o', str(target)]
     if verbose:
         cmd.insert(1, '-Xptxas=-v')
     subprocess.run(cmd, check=True)
-    return LIB
+    return target
 
 
 if __name__ == '__main__':
-    build(force=True, verbose='-v' in sys.argv)
-    print(LIB)
+    import argparse
+    p = argparse.ArgumentParser(description='build libornith_moe_b200.so for sm_100a')
+    p.add_argument('-v', '--verbose', action='store_true', help='print ptxas register and spill counts')
+    p.add_argument('--out', default=None, help='write a variant library to this path')
+    p.add_argument('--flag', action='append', default=[], help='extra nvcc flag, e.g. --flag=-DORNITH_PREFILL_F32X2=1')
+    a = p.parse_args()
+    print(build(force=True, verbose=a.verbose, flags=a.flag, out=a.out))

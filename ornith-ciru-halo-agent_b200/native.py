@@ -20,12 +20,15 @@ All launches go to the caller's current CUDA stream.  There is no CPU
 fallback: every operator raises if the CUDA library is missing.
 """
 import ctypes as C
+import os
 from pathlib import Path
 
 import torch
 
 HERE = Path(__file__).resolve().parent
-LIB_PATH = HERE / 'libornith_moe_b200.so'
+# ORNITH_MOE_B200_LIB selects another build of the library (a variant written
+# by build.py --out; relative paths are taken from this package's directory)
+LIB_PATH = HERE / os.environ.get('ORNITH_MOE_B200_LIB', 'libornith_moe_b200.so')
 
 _lib = None
 _PHASE_SEGMENTS = ()

@@ -99,3 +99,16 @@ def test_operators_fail_loudly_without_library(native, monkeypatch, tmp_path):
     monkeypatch.setattr(native, 'LIB_PATH', tmp_path / 'missing.so')
     with pytest.raises(RuntimeError, match='no CPU fallback'):
         native.lib()
+
+
+def test_variant_library_is_selected_by_environment(tmp_path):
+    """ORNITH_MOE_B200_LIB points the binding at another build; a missing one
+    fails loudly instead of falling back."""
+    import subprocess
+    import sys
+    code = ('import sys; sys.path.insert(0, %r); import __graft_entry__ as g; g.load_package(); '
+            'from ornith_b200 import native; print(native.LIB_PATH); native.lib()') % str(ROOT)
+    env = dict(__import__('os').environ, ORNITH_MOE_B200_LIB=str(tmp_path / 'variant.so'))
+    out = subprocess.run([sys.executable, '-c', code], env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode != 0 and 'no CPU fallback' in out.stderr
+    assert str(tmp_path / 'variant.so') in out.stdout
