@@ -181,6 +181,74 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_splat(float v) { return f2_pack(v, v); }
+// sign flip of both halves, exact (what the scalar form's unary minus does)
+__device__ __forceinline__ uint64_t f2_neg(uint64_t v) { return v ^ 0x8000000080000000ull; }
+
+// The confirmation of div_rn_ge1 for one lane (moe_common.cuh), on the
+// quotient q1 and remainder r1 computed in packed form.
+__device__ __forceinline__ float div_confirm(float g, float d, float q1, float r1, bool& ok) {
+    const uint32_t qb = __float_as_uint(q1);
+    const float half_ulp = __uint_as_float((qb & 0x7f800000u) - (24u << 23));
+    ok = d < 16777216.f && fabsf(g) < 0x1p64f && fabsf(q1) >= 0x1p-100f && (qb & 0x7fffffu) != 0u &&
+         fabsf(r1) < __fmul_rn(d, half_ulp);
+    const bool zero = g == 0.f && d < 16777216.f;
+    ok = ok || zero;
+    return zero ? g : q1;
+}
+
+// silu_quotient_fast (moe_common.cuh) on two values at once, operation for
+// operation on packed pairs; the reciprocal estimate and the exactness checks
+// stay per lane.  Same results as two scalar calls.
+__device__ __forceinline__ void silu_quotient_fast2(float g0, float g1, float& q0, float& q1, bool& ok0, bool& ok1) {
+    const uint64_t g2 = f2_pack(g0, g1);
+    const uint64_t x2 = f2_neg(g2);
+    const uint64_t magic = f2_splat(12582912.f);
+    const uint64_t shifted = f2_add(f2_mul(x2, f2_splat(0x1.715476p+0f)), magic);
+    const uint64_t n_float = f2_sub(shifted, magic);
+    float s0, s1;
+    f2_unpack(shifted, s0, s1);
+    const int n0 = __float_as_int(s0) - 0x4B400000, n1 = __float_as_int(s1) - 0x4B400000;
+    const uint64_t high = f2_mul(n_float, f2_splat(0x1.62e400p-1f));
+    const uint64_t low = f2_mul(n_float, f2_splat(0x1.7f7d1cp-20f));
+    const uint64_t r = f2_sub(f2_sub(x2, high), low);
+    uint64_t p = f2_splat(0x1.a01a02p-16f);
+    p = f2_add(f2_mul(p, r), f2_splat(0x1.a01a02p-13f));
+    p = f2_add(f2_mul(p, r), f2_splat(0x1.6c16c2p-10f));
+    p = f2_add(f2_mul(p, r), f2_splat(0x1.111112p-7f));
+    p = f2_add(f2_mul(p, r), f2_splat(0x1.555556p-5f));
+    p = f2_add(f2_mul(p, r), f2_splat(0x1.555556p-3f));
+    p = f2_add(f2_mul(p, r), f2_splat(0x1p-1f));
+    p = f2_add(f2_mul(p, r), f2_splat(0x1p+0f));
+    p = f2_add(f2_mul(p, r), f2_splat(0x1p+0f));
+    const uint64_t e = f2_mul(p, f2_pack(__int_as_float((n0 + 127) << 23), __int_as_float((n1 + 127) << 23)));
+    const uint64_t d = f2_add(f2_splat(1.f), e);
+    // div_rn_ge1 on the pair
+    float d0, d1, y00, y01;
+    f2_unpack(d, d0, d1);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y00) : "f"(d0));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y01) : "f"(d1));
+    const uint64_t y0 = f2_pack(y00, y01), nd = f2_neg(d);
+    const uint64_t e1 = f2_fma(nd, y0, f2_splat(1.f));
+    const uint64_t y1 = f2_fma(y0, e1, y0);
+    const uint64_t qa = f2_mul(g2, y1);
+    const uint64_t ra = f2_fma(nd, qa, g2);
+    const uint64_t qb = f2_fma(ra, y1, qa);
+    const uint64_t rb = f2_fma(nd, qb, g2);
+    float qb0, qb1, rb0, rb1;
+    f2_unpack(qb, qb0, qb1);
+    f2_unpack(rb, rb0, rb1);
+    bool dok0, dok1;
+    q0 = div_confirm(g0, d0, qb0, rb0, dok0);
+    q1 = div_confirm(g1, d1, qb1, rb1, dok1);
+    ok0 = dok0 && fabsf(g0) < 80.f;
+    ok1 = dok1 && fabsf(g1) < 80.f;
+}
 #endif
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -599,8 +667,14 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         bool ok[8];
 #pragma unroll
                         for (int j = 0; j < 8; ++j) gs[j] = valid ? acc[i + j] : 1.f;
+#if ORNITH_PREFILL_F32X2
+#pragma unroll
+                        for (int j = 0; j < 8; j += 2)
+                            silu_quotient_fast2(gs[j], gs[j + 1], q[j], q[j + 1], ok[j], ok[j + 1]);
+#else
 #pragma unroll
                         for (int j = 0; j < 8; ++j) q[j] = silu_quotient_fast(gs[j], ok[j]);
+#endif
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
                             if (!ok[j]) q[j] = __fdiv_rn(gs[j], __fadd_rn(1.f, portable_exp(-gs[j])));
