@@ -78,6 +78,20 @@ def run_prepare(native, x_bits, codes, meta, N, K):
     return st, _bits(xt), _bits(w), int(flags.item())
 
 
+def _fp32_reduced_gemm(fn):
+    """Run fn with cuBLAS told to keep split-K reductions in fp32: by default
+    torch lets bf16 GEMMs reduce partial sums in bf16, whose error the fp32
+    summation bound of these checks does not cover."""
+    flag = torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    try:
+        result = fn()
+        torch.cuda.synchronize()
+        return result
+    finally:
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = flag
+
+
 def test_dense_golden_cases(native, dense_golden, make_golden, S, O):
     """Every golden case of the compiled reference, bit for bit (out, fp32
     projection, flags), on the GPU."""
@@ -172,8 +186,7 @@ def test_dense_out_operator_both_paths(native, S, O):
     # bf16 prefill rows
     x = S.make_rows(rng, 48, K)
     out = torch.empty((48, N), dtype=torch.bfloat16, device=DEV)
-    native.dense_out(_bf16(x), c, m, ws, out, flags, capacity, N, K, 2, 16)
-    torch.cuda.synchronize()
+    _fp32_reduced_gemm(lambda: native.dense_out(_bf16(x), c, m, ws, out, flags, capacity, N, K, 2, 16))
     xt, w, pf = O.dense_prepare_bf16(x, codes, meta, N, K)
     xa, wa = S.bf16_bits_to_f32(xt).astype(np.float64), S.bf16_bits_to_f32(w).astype(np.float64)
     exact = xa @ wa.T

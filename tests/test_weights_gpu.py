@@ -61,6 +61,20 @@ def test_loaded_layer_matches_oracle(S, O, replace):
     assert runtime.check_error_flags() == [ref_flags] == [0]
 
 
+def _fp32_reduced_gemm(fn):
+    """Run fn with cuBLAS told to keep split-K reductions in fp32: by default
+    torch lets bf16 GEMMs reduce partial sums in bf16, whose error the fp32
+    summation bound of these checks does not cover."""
+    flag = torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    try:
+        result = fn()
+        torch.cuda.synchronize()
+        return result
+    finally:
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = flag
+
+
 def test_dense_linear_method_apply(S, O):
     """G256LinearMethod: packed loads, seal, apply on [..., K] rows through
     dense_out (A8 up to dense_a8_max_rows rows, bit for bit; the bf16 prefill
@@ -87,8 +101,8 @@ def test_dense_linear_method_apply(S, O):
     ref, _, ref_flags = O.dense_project(x, codes, meta, N, K, 16)
     np.testing.assert_array_equal(out.reshape(6, N).view(torch.int16).cpu().numpy().view(np.uint16), ref)
     x = S.make_rows(rng, 40, K)   # above dense_a8_max_rows = 32: the bf16 prefill path
-    out = method.apply(layer, torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16))
-    torch.cuda.synchronize()
+    out = _fp32_reduced_gemm(lambda: method.apply(layer, torch.from_numpy(x.view(np.int16)).to(dev)
+                                                  .view(torch.bfloat16)))
     xt, w, _ = O.dense_prepare_bf16(x, codes, meta, N, K)
     xa, wa = S.bf16_bits_to_f32(xt).astype(np.float64), S.bf16_bits_to_f32(w).astype(np.float64)
     exact = xa @ wa.T
