@@ -44,7 +44,7 @@ def test_loaded_layer_matches_oracle(S, O, replace):
     method.process_weights_after_loading(layer)
     size = method.prepare_n32_weights(layer, replace=replace)
     assert size == (256 * 1024 * 2048 // 2 + 256 * 1024 * 8 * 4 + 256 * 2048 * 512 // 2 + 256 * 2048 * 2 * 4)
-    with pytest.raises(RuntimeError, match='prepared once'):
+    with pytest.raises(RuntimeError, match='already prepared'):
         method.prepare_n32_weights(layer, replace=replace)
 
     T = 6
