@@ -162,6 +162,20 @@ def set_phase_segments(segments):
     _PHASE_SEGMENTS = tuple((int(a), int(b), bool(p)) for a, b, p in segments)
 
 
+def _phase_plan(rows):
+    """Row ranges (lo, hi, prefill) of a mixed prefill/decode batch: the
+    configured segments, then any rows past them as prefill; None when the
+    batch is not segmented (no segments, or fewer rows than they cover).
+    The rule of the plugin's phase dispatch (native.py:124-135,162-168)."""
+    if not _PHASE_SEGMENTS or rows < _PHASE_SEGMENTS[-1][1]:
+        return None
+    plan = list(_PHASE_SEGMENTS)
+    covered = plan[-1][1]
+    if covered < rows:
+        plan.append((covered, rows, True))
+    return plan
+
+
 def validate(x, out, capacity, k):
     if (x.ndim != 2 or x.shape[1] != k or not 0 <= x.shape[0] <= capacity
             or x.dtype != torch.bfloat16 or x.device.type != 'cuda'
@@ -190,17 +204,15 @@ def _routed_launch(symbol, x, routes, ids, gate, gate_meta, down, down_meta, wor
 def routed_out(x: torch.Tensor, routes: torch.Tensor, ids: torch.Tensor,
                gate: torch.Tensor, gate_meta: torch.Tensor, down: torch.Tensor, down_meta: torch.Tensor,
                workspace: torch.Tensor, out: torch.Tensor, flags: torch.Tensor, capacity: int) -> None:
-    if _PHASE_SEGMENTS and x.shape[0] >= _PHASE_SEGMENTS[-1][1]:
-        segments = list(_PHASE_SEGMENTS)
-        if segments[-1][1] < x.shape[0]:
-            segments.append((segments[-1][1], x.shape[0], True))
-        for start, end, prefill in segments:
-            symbol = 'ornith_routed_direct_launch_a4' if prefill else 'ornith_routed_direct_launch'
-            _routed_launch(symbol, x[start:end], routes[start:end], ids[start:end], gate, gate_meta, down,
-                           down_meta, workspace, out[start:end], flags, capacity)
+    plan = _phase_plan(x.shape[0])
+    if plan is None:
+        _routed_launch(_SETTINGS['launch'], x, routes, ids, gate, gate_meta, down, down_meta, workspace, out, flags,
+                       capacity)
         return
-    _routed_launch(_SETTINGS['launch'], x, routes, ids, gate, gate_meta, down, down_meta, workspace, out, flags,
-                   capacity)
+    for lo, hi, prefill in plan:
+        symbol = 'ornith_routed_direct_launch_a4' if prefill else 'ornith_routed_direct_launch'
+        _routed_launch(symbol, x[lo:hi], routes[lo:hi], ids[lo:hi], gate, gate_meta, down, down_meta, workspace,
+                       out[lo:hi], flags, capacity)
 
 
 @routed_out.register_fake
@@ -396,25 +408,33 @@ def dense_workspace_bytes(capacity, shapes):
     return max(sizes)
 
 
+def _bf16_prefill_views(workspace, capacity, m, n, k):
+    """The arena as the bf16 prefill path uses it (the plugin sizes it for
+    this, native.py:87-91): bf16 H128(x) [m, k] from byte 0, the dequantised
+    bf16 weights [n, k] from byte capacity*k*2."""
+    w0 = capacity * k * 2
+    if workspace.numel() < w0 + n * k * 2:
+        raise ValueError('G256 dense workspace too small for the bf16 prefill path')
+    xt = workspace[:m * k * 2].view(torch.bfloat16).view(m, k)
+    w = workspace[w0:w0 + n * k * 2].view(torch.bfloat16).view(n, k)
+    return xt, w
+
+
 def _dense_impl(x, codes, metadata, workspace, out, flags, capacity, n, k, geometry, a8_max_rows):
     validate(x, out, capacity, k)
-    if out.shape != (x.shape[0], n):
+    m = x.shape[0]
+    if out.shape != (m, n):
         raise ValueError('Native G256 dense output must be [M, N]')
-    if x.shape[0] > a8_max_rows:
-        # bf16 prefill: transformed x and dequantised W in the arena, then a bf16 GEMM
-        weight_offset = capacity * k * 2
-        if workspace.numel() < weight_offset + n * k * 2:
-            raise ValueError('G256 dense workspace too small for the bf16 prefill path')
-        transformed = workspace[:x.shape[0] * k * 2].view(torch.bfloat16).view(x.shape[0], k)
-        weight = workspace[weight_offset:weight_offset + n * k * 2].view(torch.bfloat16).view(n, k)
-        check(lib().ornith_dense_g256_prepare_bf16(ptr(x), ptr(codes), ptr(metadata), ptr(transformed),
-                                                    ptr(weight), ptr(flags), x.shape[0], n, k, stream(x)),
-              'G256 BF16 prefill preparation')
-        torch.mm(transformed, weight.t(), out=out)
+    if m <= a8_max_rows:
+        check(lib().ornith_dense_g256_launch(ptr(x), ptr(codes), ptr(metadata), ptr(workspace), workspace.numel(),
+                                             ptr(out), ptr(flags), m, capacity, n, k, 8, 128, geometry, stream(x)),
+              'G256 dense')
         return
-    check(lib().ornith_dense_g256_launch(ptr(x), ptr(codes), ptr(metadata), ptr(workspace), workspace.numel(),
-                                         ptr(out), ptr(flags), x.shape[0], capacity, n, k, 8, 128, geometry,
-                                         stream(x)), 'G256 dense')
+    # longer batches: bf16 operands prepared in the arena, then a bf16 GEMM
+    xt, w = _bf16_prefill_views(workspace, capacity, m, n, k)
+    check(lib().ornith_dense_g256_prepare_bf16(ptr(x), ptr(codes), ptr(metadata), ptr(xt), ptr(w), ptr(flags), m,
+                                                n, k, stream(x)), 'G256 BF16 prefill preparation')
+    torch.mm(xt, w.t(), out=out)
 
 
 @torch.library.custom_op('ornith_b200::dense_out', mutates_args={'workspace', 'out', 'flags'}, device_types='cuda')
@@ -422,16 +442,15 @@ def dense_out(x: torch.Tensor, codes: torch.Tensor, metadata: torch.Tensor,
               workspace: torch.Tensor, out: torch.Tensor, flags: torch.Tensor,
               capacity: int, n: int, k: int, geometry: int, a8_max_rows: int) -> None:
     """out[M,n] = x[M,k] projected by an N16 G256 bank: A8 for M <= a8_max_rows,
-    else the bf16 prefill path; mixed batches follow the phase segments."""
-    if _PHASE_SEGMENTS and x.shape[0] >= _PHASE_SEGMENTS[-1][1]:
-        for start, end, prefill in _PHASE_SEGMENTS:
-            _dense_impl(x[start:end], codes, metadata, workspace, out[start:end], flags,
-                        capacity, n, k, geometry, 0 if prefill else capacity)
-        end = _PHASE_SEGMENTS[-1][1]
-        if end < x.shape[0]:
-            _dense_impl(x[end:], codes, metadata, workspace, out[end:], flags, capacity, n, k, geometry, 0)
+    else the bf16 prefill path; a mixed batch follows the phase segments
+    (decode rows A8, prefill rows bf16)."""
+    plan = _phase_plan(x.shape[0])
+    if plan is None:
+        _dense_impl(x, codes, metadata, workspace, out, flags, capacity, n, k, geometry, a8_max_rows)
         return
-    _dense_impl(x, codes, metadata, workspace, out, flags, capacity, n, k, geometry, a8_max_rows)
+    for lo, hi, prefill in plan:
+        _dense_impl(x[lo:hi], codes, metadata, workspace, out[lo:hi], flags, capacity, n, k, geometry,
+                    0 if prefill else capacity)
 
 
 @dense_out.register_fake

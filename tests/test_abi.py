@@ -112,3 +112,18 @@ def test_variant_library_is_selected_by_environment(tmp_path):
     out = subprocess.run([sys.executable, '-c', code], env=env, capture_output=True, text=True, timeout=120)
     assert out.returncode != 0 and 'no CPU fallback' in out.stderr
     assert str(tmp_path / 'variant.so') in out.stdout
+
+
+def test_phase_plan_of_mixed_batches(native):
+    """Mixed prefill/decode batches (the plugin's phase dispatch): the
+    configured segments, then any rows past them as prefill; an unsegmented
+    batch when no segments are set or the batch is shorter than they cover."""
+    try:
+        native.set_phase_segments(())
+        assert native._phase_plan(40) is None
+        native.set_phase_segments([(0, 8, False), (8, 24, True)])
+        assert native._phase_plan(20) is None
+        assert native._phase_plan(24) == [(0, 8, False), (8, 24, True)]
+        assert native._phase_plan(30) == [(0, 8, False), (8, 24, True), (24, 30, True)]
+    finally:
+        native.set_phase_segments(())
