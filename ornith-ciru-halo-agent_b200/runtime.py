@@ -30,10 +30,10 @@ class Runtime:
         self.dense_geometry = settings.get('dense_geometry', 2)
         self.dense_a8_max_rows = settings.get('dense_a8_max_rows', 32)
         if self.dense_a8_max_rows not in (32, 64):
-            raise ValueError('G256 dense A8 crossover must be 32 or 64 rows')
+            raise ValueError(f'dense_a8_max_rows is {self.dense_a8_max_rows}; it must be 32 or 64')
         self.head_geometry = settings.get('head_geometry', 2)
         if self.dense_geometry not in (0, 1, 2) or self.head_geometry not in (0, 1, 2):
-            raise ValueError('Native geometry must be 0, 1, or 2')
+            raise ValueError('dense_geometry and head_geometry take 0, 1 or 2')
         size = native.configure(settings, self.capacity)
         if dense_shapes:
             size = max(size, native.dense_workspace_bytes(self.capacity, sorted(set(dense_shapes))))
@@ -46,11 +46,12 @@ class Runtime:
 
     def reset_error_flags(self):
         if torch.cuda.is_current_stream_capturing():
-            raise RuntimeError('Reset native error flags outside graph capture')
+            raise RuntimeError('error flags are reset outside CUDA graph capture only')
         self.error_flags.zero_()
 
     def check_error_flags(self):
         flags = self.error_flags.cpu().tolist()
         if any(flags):
-            raise RuntimeError(str({name: code for name, code in zip(self.layer_prefixes, flags) if code}))
+            raise RuntimeError(f'native error flags set: '
+                               f'{ {name: code for name, code in zip(self.layer_prefixes, flags) if code} }')
         return flags
