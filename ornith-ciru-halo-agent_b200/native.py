@@ -111,7 +111,7 @@ def lib():
             fn = getattr(handle, name)
             fn.argtypes, fn.restype = args, res
         if handle.ornith_routed_storage_n32() != 32:
-            raise RuntimeError('Sole N32 storage requires the full N32 consumer')
+            raise RuntimeError(f'{LIB_PATH} does not report N32 expert storage (marker 32)')
         _lib = handle
     return _lib
 
@@ -147,9 +147,9 @@ def configure(settings, capacity):
     bits = settings.get('routed_activation_bits', 8)
     prefill_bits = settings.get('routed_prefill_activation_bits', 8)
     if bits not in (4, 8) or prefill_bits not in (4, 8):
-        raise ValueError('G256 routed activation bits must be 4 or 8')
+        raise ValueError('routed_activation_bits and routed_prefill_activation_bits take 4 or 8')
     if bits == prefill_bits == 4:
-        raise ValueError('Choose either global routed A4 or prefill-only routed A4')
+        raise ValueError('A4 everywhere and A4 for prefill only are exclusive: set one of the two to 8')
     suffix = '_a4' if bits == 4 else '_a4_prefill' if prefill_bits == 4 else ''
     _SETTINGS['launch'] = 'ornith_routed_direct_launch' + suffix
     return workspace_bytes(capacity)
@@ -181,7 +181,8 @@ def validate(x, out, capacity, k):
             or x.dtype != torch.bfloat16 or x.device.type != 'cuda'
             or out.dtype != x.dtype or out.device != x.device
             or not x.is_contiguous() or not out.is_contiguous()):
-        raise ValueError('Native G256 requires contiguous BF16 input/output within capacity')
+        raise ValueError(f'expected contiguous CUDA bf16 rows [M <= {capacity}, {k}] '
+                         'and a bf16 output on the same device')
 
 
 def _validate_routes(x, routes, ids):
@@ -189,7 +190,7 @@ def _validate_routes(x, routes, ids):
             or routes.shape != (x.shape[0], 8) or ids.shape != routes.shape
             or routes.device != x.device or ids.device != x.device
             or not routes.is_contiguous() or not ids.is_contiguous()):
-        raise ValueError('G256 routed input requires FP32 weights and INT32 IDs [T,8]')
+        raise ValueError('routing weights must be contiguous fp32 [T, 8] and ids int32 [T, 8] on the input device')
 
 
 def _routed_launch(symbol, x, routes, ids, gate, gate_meta, down, down_meta, workspace, out, flags, capacity):
