@@ -7,7 +7,8 @@ shared libraries under oracle/_ref/ so that their outputs pin the C oracle:
   1. copy each needed source and header into oracle/_ref/src/<library>/,
      rewriting only the CUDA/HIP launch syntax `kernel<<<grid,block,smem,stream>>>(args)`
      into `::hipshim::Launch(grid,block,smem,stream)(kernel,args)` because g++
-     cannot parse triple chevrons; nothing else in the text changes;
+     cannot parse triple chevrons; nothing else in the text changes; the
+     copies are deleted once the library is compiled;
   2. compile with g++ against oracle/hipshim (a CPU SIMT shim written for this
      repository) using the reference's numerics flags (-O2 -ffp-contract=off,
      correctly rounded division, -DORNITH_PREFILL_OUTPUT32=1 as in
@@ -26,6 +27,7 @@ the prebuilt libraries travel with the repository snapshot.
 import argparse
 import os
 import re
+import shutil
 import subprocess
 import sys
 from pathlib import Path
@@ -71,8 +73,14 @@ def build(reference, names=None):
         cmd = ['g++', '-std=c++20', '-O2', '-ffp-contract=off', '-fopenmp', '-fPIC', '-shared',
                '-w', '-Wno-psabi', '-DORNITH_PREFILL_OUTPUT32=1', f'-I{HERE / "hipshim"}', f'-I{src_dir}',
                str(src_dir / main), '-o', str(lib)]
-        subprocess.run(cmd, check=True)
+        try:
+            subprocess.run(cmd, check=True)
+        finally:
+            # only the compiled library stays: no copy of the reference's
+            # sources remains in the repository tree
+            shutil.rmtree(src_dir, ignore_errors=True)
         built.append(lib)
+    shutil.rmtree(OUT / 'src', ignore_errors=True)
     return built
 
 
