@@ -622,6 +622,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         DECODE_CLOCK(23);
     }
 
+#if ORNITH_DECODE_EARLY_PREFETCH
+    // the shared expert's banks do not depend on routing: CTA b prefetches
+    // slice b of each into L2 before routing starts (see the routed experts'
+    // prefetch after routing below)
+    if (a.shared && tid < 4) {
+        // thread i takes range i: gate codes, gate metadata, down codes, down metadata
+        const uint32_t* range = tid == 0 ? a.sgate_codes : tid == 1 ? a.sgate_meta : tid == 2 ? a.sdown_codes
+                                                                                              : a.sdown_meta;
+        const uint32_t bytes = tid == 0 ? 2u * kI * kH / 2
+                             : tid == 1 ? 2u * kI * (kH / kG) * 4
+                             : tid == 2 ? uint32_t(kH) * kI / 2
+                                        : uint32_t(kH) * (kI / kG) * 4;
+        const uint32_t chunk = ((bytes + uint32_t(G) - 1) / uint32_t(G) + 15u) & ~15u;
+        const uint32_t start = uint32_t(b) * chunk;
+        if (start < bytes)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                             reinterpret_cast<const char*>(range) + start),
+                         "r"(min(chunk, bytes - start))
+                         : "memory");
+    }
+#endif
     // ---- routing (every CTA, identical) -----------------------------------
     if (tid == 0) {
         for (int i = 0; i < nst; ++i) {
@@ -719,16 +740,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     // plan; the ring's bulk copies then find the weights in L2.  A prefetch
     // changes no result.  Built with -DORNITH_DECODE_EARLY_PREFETCH=1 (not the
     // default build yet: it has not been run on a GPU).
-    if (small && tid <= R) {
+    if (small && tid < R) {
         int e = -1;
         if (tid < R) {
             e = s.ids[tid];
             if (!id_valid(e)) e = -1;
             for (int r = 0; r < tid && e >= 0; ++r)
                 if (s.ids[r] == e) e = -1;  // the first route of an expert prefetches it
-        } else if (a.shared) {
-            e = kE;
-        }
+        }  // the shared expert was prefetched at entry
         if (e >= 0) {
             const bool sh = e == kE;
             const char* base[4] = {
