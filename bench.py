@@ -95,6 +95,8 @@ def parse():
                    help='expert placement of the expert-parallel configs')
     p.add_argument('--combine', choices=['exact', 'partial'], default='exact',
                    help='expert-parallel return: per-slot rows (bit-exact) or per-rank fp32 partial sums')
+    p.add_argument('--ep-chunks', type=int, default=1,
+                   help='compact expert-parallel exchange in this many pipelined token chunks (exact combine)')
     p.add_argument('--layers', type=int, default=None,
                    help='override the layer count (small cases for profiler captures)')
     return p.parse_args()
@@ -225,7 +227,8 @@ def run_ep(args):
         d = device_bank(torch, gen, dev, epr, 2048, 512)
         layers.append(ep.ExpertParallelMoE(None, world, (g[0], g[1], d[0], d[1]), capacity=min(T * world, 8192),
                                            act_bits=bits, exchange=cfg['exchange'], placement=placement,
-                                           combine=args.combine))
+                                           combine=args.combine,
+                                           chunks=args.ep_chunks if cfg['exchange'] == 'compact' else 1))
     logits = torch.randn((L, T, 256), device=dev, generator=gen) + bias
     x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
     w = torch.empty((L, T, 8), dtype=torch.float32, device=dev)
@@ -286,7 +289,8 @@ def run_ep(args):
                                'per-rank fp32 partial sums, equal to one GPU within fp32 rounding'),
                    'exchange': ('NCCL all_gather of token rows + equal-block all_to_all of fp32 per-slot rows '
                                 '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
-                                'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)')},
+                                'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)'),
+                   'chunks': args.ep_chunks if cfg['exchange'] == 'compact' else 1},
         'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': graph is not None,
     }
     dist.barrier()

@@ -191,6 +191,61 @@ def route_row_index(T, plan, device):
     return idx.scatter_reduce_(0, plan.token_index.view(-1, 1).expand(-1, TOP), dense, 'amax')
 
 
+def dispatch_chunks(group, world, ids, placement, bounds):
+    """dispatch_with_counts for the token ranges `bounds` of this rank at
+    once: one all_to_all of every chunk's (tokens sent, slots to come back)
+    pairs and one host synchronisation.  Returns [(plan, recv_counts,
+    back_counts)] per chunk."""
+    parts = [_owner_mask(ids[lo:hi], world, placement) for lo, hi in bounds]
+    counts = torch.stack([c for _, _, c in parts], dim=1).contiguous()       # [world, chunks, 2]
+    got = torch.empty_like(counts)
+    n = len(bounds) * 2
+    _a2a(group, got.view(world, n), counts.view(world, n), [1] * world, [1] * world)
+    both = torch.cat([counts, got], dim=2).tolist()                         # the single host synchronisation
+    out = []
+    for c, ((lo, hi), (mask, lid, _)) in enumerate(zip(bounds, parts)):
+        rows = [both[d][c] for d in range(world)]
+        plan = _plan_from_mask(mask, lid, ids[lo:hi], [int(r[0]) for r in rows], [int(r[1]) for r in rows])
+        out.append((plan, [int(r[2]) for r in rows], [int(r[3]) for r in rows]))
+    return out
+
+
+def ep_layer_chunked(group, world, x, ids, weights, compute, combine, placement=None, chunks=2):
+    """ep_layer over `chunks` contiguous token ranges, pipelined so that the
+    return exchange of chunk c overlaps the expert compute of chunk c + 1:
+    per chunk the row exchange of the next chunk is issued before this
+    chunk's return, which is asynchronous (collectives of one group run in
+    issue order, so the other order would serialise them).  Every rank must
+    use the same chunk count.  Tokens are independent, so the output equals
+    ep_layer's bit for bit."""
+    T = x.shape[0]
+    bounds = [(T * c // chunks, T * (c + 1) // chunks) for c in range(chunks)]
+    plans = dispatch_chunks(group, world, ids, placement, bounds)
+
+    def send(c):
+        lo, hi = bounds[c]
+        plan, recv_counts, _ = plans[c]
+        return exchange_rows(group, world, plan, x[lo:hi], recv_counts)
+
+    pending = []
+    nxt = send(0)
+    for c in range(chunks):
+        x_recv, ids_recv = nxt
+        plan, _, back_counts = plans[c]
+        rows = compute(x_recv, ids_recv, sum(back_counts))
+        if c + 1 < chunks:
+            nxt = send(c + 1)
+        got = torch.empty((sum(plan.home_counts), H), dtype=torch.float32, device=rows.device)
+        work = dist.all_to_all_single(got, rows, plan.home_counts, back_counts, group=group, async_op=True)
+        pending.append((work, got, rows))
+    outs = []
+    for c, (work, got, _) in enumerate(pending):
+        work.wait()
+        lo, hi = bounds[c]
+        outs.append(combine(got, route_row_index(hi - lo, plans[c][0], got.device), weights[lo:hi], ids[lo:hi]))
+    return torch.cat(outs)
+
+
 def ep_layer(group, world, x, ids, weights, compute, combine, placement=None):
     """One expert-parallel layer call, compact exchange.
 
@@ -308,7 +363,7 @@ class ExpertParallelMoE:
     every rank; contiguous ranges by default."""
 
     def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact', placement=None,
-                 combine='exact'):
+                 combine='exact', chunks=1):
         from . import native
         if exchange not in ('compact', 'fixed'):
             raise ValueError(f'unknown exchange mode {exchange!r}')
@@ -316,6 +371,9 @@ class ExpertParallelMoE:
             raise ValueError(f'unknown combine mode {combine!r}')
         if combine == 'partial' and world > TOP:
             raise ValueError('the rank-partial combine supports at most 8 ranks')
+        if not isinstance(chunks, int) or chunks < 1 or (chunks > 1 and (exchange, combine) != ('compact', 'exact')):
+            raise ValueError('chunks > 1 applies to the compact exchange with the exact combine')
+        self.chunks = chunks
         self.combine_mode = combine
         self.native = native
         self.group, self.world = group, world
@@ -378,4 +436,7 @@ class ExpertParallelMoE:
         if self.exchange == 'fixed':
             return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine,
                                   self.placement)
+        if self.chunks > 1:
+            return ep_layer_chunked(self.group, self.world, x, ids, weights, self.compute, self.combine,
+                                    self.placement, self.chunks)
         return ep_layer(self.group, self.world, x, ids, weights, self.compute, self.combine, self.placement)

@@ -119,6 +119,10 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
             out = ep.ep_layer_fixed(None, world, x, ids, weights, compute_block, fake_combine_gathered, placement)
         elif mode == 'compact':
             out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered, placement)
+        elif mode == 'chunked':   # pipelined chunks; T + 1 chunks leaves one chunk empty
+            chunks = 3 if world == 2 else T + 1
+            out = ep.ep_layer_chunked(None, world, x, ids, weights, compute, fake_combine_gathered, placement,
+                                      chunks)
         elif mode == 'fixed_partial':
             out = ep.ep_layer_fixed_partial(None, world, x, ids, weights, compute_partial, fake_combine_gathered,
                                             placement)
@@ -137,7 +141,7 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
 
 
 @pytest.mark.parametrize('balanced', [False, True])
-@pytest.mark.parametrize('mode', ['compact', 'fixed', 'compact_partial', 'fixed_partial'])
+@pytest.mark.parametrize('mode', ['compact', 'chunked', 'fixed', 'compact_partial', 'fixed_partial'])
 @pytest.mark.parametrize('world,T', [(2, 16), (4, 9)])
 def test_ep_dispatch_combine_matches_single_rank(world, T, mode, balanced):
     ctx = mp.get_context('spawn')
