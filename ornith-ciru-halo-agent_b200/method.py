@@ -207,7 +207,7 @@ class W8HeadMethod(G256LinearMethod):
         for first in range(0, rows.shape[0], step):
             native.head_out(rows[first:first + step], layer.head_tilebank_codes, layer.head_scales, rt.workspace,
                             out[first:first + step], rt.slots[self.slot], rt.head_geometry)
-        return out
+        return out.view(*x.shape[:-1], self.n)
 
 
 class G256MoEMethod:
