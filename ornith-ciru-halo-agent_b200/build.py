@@ -6,7 +6,6 @@ reference's fixed-order arithmetic un-contracted.
 """
 import os
 import subprocess
-import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent

@@ -1,10 +1,8 @@
 """CPU: the oracle against the golden vectors and known-answer checks."""
-import hashlib
 import math
 from pathlib import Path
 
 import numpy as np
-import pytest
 
 
 def test_shared_tables_match_reference_receipt(tables):
@@ -19,9 +17,6 @@ def test_golden_layer_regenerates(golden, layer1, make_golden):
     banks = (layer1.gate_codes, layer1.gate_meta, layer1.down_codes, layer1.down_meta,
              layer1.sgate_codes, layer1.sgate_meta, layer1.sdown_codes, layer1.sdown_meta, layer1.shared_gate_w)
     assert make_golden.digest(*banks) == str(golden['layer_sha256'])
-
-
-
 
 
 

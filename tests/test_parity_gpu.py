@@ -1,7 +1,6 @@
 """GPU parity: the CUDA path through the C ABI against the golden vectors
 (outputs of the reference's own routed source) and the CPU oracle.
 Bit-exact for outputs, fp32 diagnostics, ids, routing weights and flags."""
-import ctypes as C
 
 import numpy as np
 import pytest

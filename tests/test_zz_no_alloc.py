@@ -8,7 +8,6 @@ and it builds its own inputs so that it also passes alone in a fresh process.
 """
 import ctypes as C
 
-import numpy as np
 import pytest
 import torch
 
