@@ -127,3 +127,65 @@ def test_phase_plan_of_mixed_batches(native):
         assert native._phase_plan(30) == [(0, 8, False), (8, 24, True), (24, 30, True)]
     finally:
         native.set_phase_segments(())
+
+
+def _routed_fn(lib, name, n_ptrs):
+    fn = getattr(lib, name)
+    fn.restype = C.c_int
+    fn.argtypes = [C.c_void_p] * n_ptrs + [C.c_size_t] + [C.c_void_p] * (3 if n_ptrs == 15 else 2) + \
+        [C.c_int, C.c_int, C.c_void_p]
+    return fn
+
+
+def test_routed_reference_status_codes_match_ours(native, O):
+    """Where the compiled reference (routed_storage_n32_consumer.cpp:309-324,
+    :383-386) answers without device work, this library gives the same
+    status: layout capacities, T outside [0, Tcap], a short workspace, T == 0
+    with null pointers, and each of the ten pointers null."""
+    if not O.reference_available('routed_storage_n32'):
+        pytest.skip('oracle/_ref/libref_routed_storage_n32.so not built')
+    ref = C.CDLL(str(O.REF_DIR / 'libref_routed_storage_n32.so'))   # own handle: own argtypes
+    ours = native.lib()
+    for get in ('ornith_routed_direct_get_layout', 'ornith_routed_shared_get_layout'):
+        f_ref, f_ours = getattr(ref, get), getattr(ours, get)
+        f_ref.restype = C.c_int
+        for tcap in (-1, 0, 1, 8, 9, 16, 17, 64, 8192, 8193):
+            a, b = native.RoutedLayout(), native.RoutedLayout()
+            assert f_ref(tcap, C.byref(a)) == f_ours(tcap, C.byref(b)), (get, tcap)
+        assert f_ref(4, None) == f_ours(4, None) == INVALID
+    big = 1 << 40                      # a size only; never dereferenced
+    fake = 1 << 20
+    for name in ('ornith_routed_direct_launch', 'ornith_routed_direct_launch_a4',
+                 'ornith_routed_direct_launch_a4_prefill'):
+        f_ref, f_ours = _routed_fn(ref, name, 8), _routed_fn(ours, name, 8)
+        need = native.get_layout(64).workspace_bytes
+        cases = [([None] * 8, big, None, None, 0, 64),          # T == 0: success before any pointer check
+                 ([fake] * 8, big, fake, fake, 65, 64),          # T > Tcap
+                 ([fake] * 8, big, fake, fake, -1, 64),          # T < 0
+                 ([fake] * 8, big, fake, fake, 1, 8193),         # Tcap too large
+                 ([fake] * 8, big, fake, fake, 1, -1)]           # Tcap negative
+        for i in range(10):                                      # each pointer null in turn
+            ptrs, out, flags = [fake] * 8, fake, fake
+            if i < 8:
+                ptrs[i] = None
+            elif i == 8:
+                out = None
+            else:
+                flags = None
+            cases.append((ptrs, big, out, flags, 3, 64))
+        for ptrs, nbytes, out, flags, T, tcap in cases:
+            want = f_ref(*ptrs, nbytes, out, flags, T, tcap, None)
+            assert want in (0, INVALID), (name, T, tcap, want)
+            assert f_ours(*ptrs, nbytes, out, flags, T, tcap, None) == want, (name, T, tcap)
+        # a workspace one byte short of each library's own layout
+        ref_need = native.RoutedLayout()
+        getattr(ref, 'ornith_routed_direct_get_layout')(64, C.byref(ref_need))
+        assert f_ref(*[fake] * 8, ref_need.workspace_bytes - 1, fake, fake, 1, 64, None) == INVALID
+        assert f_ours(*[fake] * 8, need - 1, fake, fake, 1, 64, None) == INVALID
+    f_ref = _routed_fn(ref, 'ornith_routed_direct_launch_shared_tables', 15)
+    f_ours = _routed_fn(ours, 'ornith_routed_direct_launch_shared_tables', 15)
+    # the reference's shared entry checks no pointer, so only the scalar cases
+    for T, tcap in ((0, 16), (17, 16), (-1, 16), (1, 17), (1, -1)):
+        ptrs = [None] * 15 if T == 0 else [fake] * 15
+        want = f_ref(*ptrs, big, fake, fake, fake, T, tcap, None)
+        assert f_ours(*ptrs, big, fake, fake, fake, T, tcap, None) == want, (T, tcap)
