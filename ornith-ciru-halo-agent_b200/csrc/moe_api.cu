@@ -66,7 +66,9 @@ __global__ __launch_bounds__(256) void combine_gathered_kernel(const float* rows
 #pragma unroll
         for (int s = 0; s < kTop; ++s) {
             const int r = t * kTop + s;
-            if (!id_valid(ids[r])) continue;
+            const int id = ids[r];
+            if (id >= kE || id < -1) f |= kFlagInvalidId;  // -1 is padding
+            if (!id_valid(id)) continue;
             const int row = row_index[r];
             if (row < 0 || row >= n) {
                 f |= kFlagInvalidId;

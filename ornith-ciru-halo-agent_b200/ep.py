@@ -87,9 +87,11 @@ def balanced_placement(counts, world, device=None):
 
 
 def map_ids(ids, placement):
-    """(owning rank, index in the owner's banks) of every slot; -1 for padding."""
-    valid = ids >= 0
-    e = ids.clamp(min=0).long()
+    """(owning rank, index in the owner's banks) of every slot; -1 for padding
+    and for ids outside 0..255, which no rank owns (the home rank's combine
+    raises flag 4 for the latter, as the single-GPU layer does)."""
+    valid = (ids >= 0) & (ids < E)
+    e = torch.where(valid, ids, torch.zeros_like(ids)).long()
     neg = torch.full_like(ids, -1)
     return (torch.where(valid, placement.rank[e].to(ids.dtype), neg),
             torch.where(valid, placement.local[e].to(ids.dtype), neg))
@@ -431,6 +433,9 @@ class ExpertParallelMoE:
 
     def __call__(self, x, ids, weights):
         if self.combine_mode == 'partial':
+            # the partial rows reach the combine without the ids: ids outside
+            # -1..255 (flag 4 on one GPU) are flagged here, on the device
+            self.flags.bitwise_or_(((ids >= E) | (ids < -1)).any().to(self.flags.dtype) * 4)
             run = ep_layer_fixed_partial if self.exchange == 'fixed' else ep_layer_partial
             return run(self.group, self.world, x, ids, weights, self.compute_partial, self.combine, self.placement)
         if self.exchange == 'fixed':

@@ -25,12 +25,17 @@ def fake_rows(x, ids_local, table):
     return (xf.unsqueeze(1) * (g.unsqueeze(2) * 0.01 + 1.0) + g.unsqueeze(2) * 0.5).contiguous()
 
 
+def valid_ids(ids):
+    """Slots that name an expert: -1 is padding, ids outside 0..255 are invalid."""
+    return (ids >= 0) & (ids < E)
+
+
 def fake_combine(rows, weights, ids):
     T = ids.shape[0]
     r = rows.view(T, TOP, H)
     out = torch.zeros((T, H), dtype=torch.float32)
     for s in range(TOP):
-        valid = (ids[:, s] >= 0).unsqueeze(1)
+        valid = valid_ids(ids[:, s]).unsqueeze(1)
         out = torch.where(valid, out + r[:, s] * weights[:, s:s + 1], out)
     return out
 
@@ -41,7 +46,7 @@ def fake_combine_gathered(rows, row_index, weights, ids):
     dense = torch.zeros((T, TOP, H), dtype=torch.float32)
     have = row_index >= 0
     dense[have] = rows[row_index[have].long()]
-    assert bool(((ids >= 0) <= have).all()), 'a valid slot came back without a row'
+    assert bool((valid_ids(ids) <= have).all()), 'a valid slot came back without a row'
     return fake_combine(dense.view(T * TOP, H), weights, ids)
 
 
@@ -84,6 +89,8 @@ def _inputs(rank, T, seed):
     ids = torch.topk(logits, TOP, dim=1).indices.to(torch.int32)
     ids[::5, 3] = -1                   # padding slots
     ids[1, :] = -1                     # a token with no expert at all
+    ids[4, 2] = 300                    # invalid ids: no rank owns them, the slot is skipped
+    ids[6, 7] = -5
     weights = torch.softmax(torch.randn((T, TOP), generator=gen), dim=1)
     return x, ids, weights
 
@@ -132,7 +139,8 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
         if mode.endswith('partial'):
             ref = rank_partial_reference(x, ids, weights, placement, world)
         else:
-            ref = fake_combine(fake_rows(x, ids, torch.arange(E)).view(T * TOP, H), weights, ids)
+            clean = torch.where(valid_ids(ids), ids, torch.full_like(ids, -1))
+            ref = fake_combine(fake_rows(x, clean, torch.arange(E)).view(T * TOP, H), weights, ids)
         q.put((rank, bool(torch.equal(out, ref)), ''))
         dist.barrier()
         dist.destroy_process_group()
