@@ -164,8 +164,9 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine(
 
 /* The same combine from gathered rows: rows fp32 [n][2048] holds only the
  * per-slot rows that exist, and row_index int32 [T,8] gives the row of slot s
- * of token t (ignored where the id is -1 padding; a valid id whose index is
- * outside [0, n) raises flag 4 and contributes nothing).  Saves the expert-
+ * of token t (ignored where the id is -1 padding; an id outside -1..255, or
+ * a valid id whose index is outside [0, n), raises flag 4 and contributes
+ * nothing).  Saves the expert-
  * parallel home rank from scattering the returned rows into a dense
  * [T*8][2048] buffer.  No counterpart in the reference. */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_combine_gathered(
@@ -191,6 +192,24 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_gather_route_rows(
  * reference. */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_scatter_route_rows(
     const void* workspace, size_t bytes, int T, int Tcap, void* rows_f32, cudaStream_t stream);
+
+/* Dispatch plan of one expert-parallel layer call, in one launch: for T
+ * tokens' ids int32 [T,8] and a placement (owner_i32 [256]: rank of each
+ * expert, local_i32 [256]: its index in that rank's banks) over world ranks
+ * (1..8), writes counts int64 [world][2] (tokens sent to each rank, (token,
+ * slot) rows it returns), and for the n = sum of tokens sent: token_index
+ * int64 [n] (grouped by destination, tokens ascending), dest int64 [n],
+ * local_ids int32 [n][8] (the destination's bank numbering, -1 elsewhere),
+ * slot_mask uint8 [n][8], and row_index int32 [T][8] (the row of each slot
+ * among the rows that come back, -1 where no rank owns it).  The n-sized
+ * buffers must hold T*world rows.  Ids -1 and outside 0..255 belong to no
+ * rank.  T == 0 writes zero counts and touches nothing else.  No counterpart
+ * in the reference, which runs one rank (plugin-site/ornith_g256/
+ * moe_base.py:34-39). */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_plan(
+    const void* ids_i32, int T, const void* owner_i32, const void* local_i32, int world, void* counts_i64,
+    void* token_index_i64, void* dest_i64, void* local_ids_i32, void* slot_mask_u8, void* row_index_i32,
+    cudaStream_t stream);
 
 /* Router logits, the router linear ahead of the operator
  * (iu4_correctness/gates_projection.py:17-25): input bf16 [T,2048],

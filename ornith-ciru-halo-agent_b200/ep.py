@@ -11,6 +11,8 @@ compact (any batch; ranks may hold different token counts):
   1. dispatch plan: for every destination rank d, the local tokens with at
      least one expert on d (deduplicated per (token, rank)), with their eight
      ids rewritten to d's local expert numbers (-1 for slots owned elsewhere);
+     on GPUs one launch of ornith_moe_b200_ep_plan (NativePlanner), on any
+     device the equivalent torch operations (TorchPlanner);
   2. exchange: one all_to_all of (tokens sent, slots to come back) per rank
      pair and a single host synchronisation for every split size of the
      layer, then token rows (bf16 pairs carried as int32) and local ids
@@ -105,6 +107,7 @@ class DispatchPlan:
     local_ids: torch.Tensor    # [sum(send_counts), 8] ids in the destination's numbering, -1 elsewhere
     slot_mask: torch.Tensor    # [sum(send_counts), 8] True where the slot is owned by the destination
     dest: torch.Tensor = None  # [sum(send_counts)] destination rank of each sent row
+    row_index: torch.Tensor = None  # [T, 8] row of each slot among the returned rows, when the planner made it
 
 
 def _owner_mask(ids, world, placement):
@@ -138,17 +141,57 @@ def build_dispatch(ids, world, placement=None):
     return _plan_from_mask(mask, lid, ids, [int(r[0]) for r in host], [int(r[1]) for r in host])
 
 
-def dispatch_with_counts(group, world, ids, placement=None):
+class TorchPlanner:
+    """The dispatch plan from torch operations on any device (the CPU ranks
+    of the tests use it): start(ids) -> (state, counts int64 [world, 2]) with
+    no host synchronisation; finish(state, ids, send_counts, home_counts) ->
+    DispatchPlan once the split sizes are known on the host."""
+
+    def __init__(self, world, placement=None):
+        self.world, self.placement = world, placement
+
+    def start(self, ids):
+        mask, lid, counts = _owner_mask(ids, self.world, self.placement)
+        return (mask, lid), counts
+
+    def finish(self, state, ids, send_counts, home_counts):
+        mask, lid = state
+        return _plan_from_mask(mask, lid, ids, send_counts, home_counts)
+
+
+class NativePlanner:
+    """The same plan from one launch of ornith_moe_b200_ep_plan (CUDA ids),
+    row index included; its outputs equal TorchPlanner's."""
+
+    def __init__(self, world, placement, device):
+        from . import native
+        self.native, self.world = native, world
+        self.owner = placement.rank.to(device=device, dtype=torch.int32).contiguous()
+        self.local = placement.local.to(device=device, dtype=torch.int32).contiguous()
+
+    def start(self, ids):
+        out = self.native.ep_plan(ids.contiguous(), self.owner, self.local, self.world)
+        return out, out[0]
+
+    def finish(self, state, ids, send_counts, home_counts):
+        _, token_index, dest, local_ids, slot_mask, row_index = state
+        n = sum(send_counts)
+        return DispatchPlan(send_counts, home_counts, token_index[:n], local_ids[:n], slot_mask[:n], dest[:n],
+                            row_index)
+
+
+def dispatch_with_counts(group, world, ids, placement=None, planner=None):
     """The dispatch plan plus what every peer sends here: one all_to_all of
     the (tokens sent, slots to come back) pairs and the layer's single host
     synchronisation, for all four split lists.  Returns (plan, recv_counts:
     token rows arriving from each rank, back_counts: (token, slot) rows this
     rank returns to each rank)."""
-    mask, lid, counts = _owner_mask(ids, world, placement)
+    planner = planner or TorchPlanner(world, placement)
+    state, counts = planner.start(ids)
     got = torch.empty_like(counts)
     _a2a(group, got, counts, [1] * world, [1] * world)
     both = torch.cat([counts, got], dim=1).tolist()          # the single host synchronisation
-    plan = _plan_from_mask(mask, lid, ids, [int(r[0]) for r in both], [int(r[1]) for r in both])
+    plan = planner.finish(state, ids, [int(r[0]) for r in both], [int(r[1]) for r in both])
     return plan, [int(r[2]) for r in both], [int(r[3]) for r in both]
 
 
@@ -185,7 +228,10 @@ def route_row_index(T, plan, device):
     -1 for slots no rank returned (padding ids).  No host synchronisation:
     rows arrive in slot_mask order, so the row of a masked entry is the count
     of masked entries before it; each slot has one owner, so the per-token
-    maximum over destinations picks it."""
+    maximum over destinations picks it.  A plan that carries its row index
+    (NativePlanner) returns that."""
+    if plan.row_index is not None:
+        return plan.row_index
     flat = plan.slot_mask.reshape(-1).to(torch.int32)
     dense = torch.where(plan.slot_mask, (torch.cumsum(flat, 0, dtype=torch.int32) - 1).view_as(plan.slot_mask),
                         torch.full_like(plan.slot_mask, -1, dtype=torch.int32))
@@ -193,26 +239,27 @@ def route_row_index(T, plan, device):
     return idx.scatter_reduce_(0, plan.token_index.view(-1, 1).expand(-1, TOP), dense, 'amax')
 
 
-def dispatch_chunks(group, world, ids, placement, bounds):
+def dispatch_chunks(group, world, ids, placement, bounds, planner=None):
     """dispatch_with_counts for the token ranges `bounds` of this rank at
     once: one all_to_all of every chunk's (tokens sent, slots to come back)
     pairs and one host synchronisation.  Returns [(plan, recv_counts,
     back_counts)] per chunk."""
-    parts = [_owner_mask(ids[lo:hi], world, placement) for lo, hi in bounds]
-    counts = torch.stack([c for _, _, c in parts], dim=1).contiguous()       # [world, chunks, 2]
+    planner = planner or TorchPlanner(world, placement)
+    parts = [planner.start(ids[lo:hi]) for lo, hi in bounds]
+    counts = torch.stack([c for _, c in parts], dim=1).contiguous()          # [world, chunks, 2]
     got = torch.empty_like(counts)
     n = len(bounds) * 2
     _a2a(group, got.view(world, n), counts.view(world, n), [1] * world, [1] * world)
     both = torch.cat([counts, got], dim=2).tolist()                         # the single host synchronisation
     out = []
-    for c, ((lo, hi), (mask, lid, _)) in enumerate(zip(bounds, parts)):
+    for c, ((lo, hi), (state, _)) in enumerate(zip(bounds, parts)):
         rows = [both[d][c] for d in range(world)]
-        plan = _plan_from_mask(mask, lid, ids[lo:hi], [int(r[0]) for r in rows], [int(r[1]) for r in rows])
+        plan = planner.finish(state, ids[lo:hi], [int(r[0]) for r in rows], [int(r[1]) for r in rows])
         out.append((plan, [int(r[2]) for r in rows], [int(r[3]) for r in rows]))
     return out
 
 
-def ep_layer_chunked(group, world, x, ids, weights, compute, combine, placement=None, chunks=2):
+def ep_layer_chunked(group, world, x, ids, weights, compute, combine, placement=None, chunks=2, planner=None):
     """ep_layer over `chunks` contiguous token ranges, pipelined so that the
     return exchange of chunk c overlaps the expert compute of chunk c + 1:
     per chunk the row exchange of the next chunk is issued before this
@@ -222,7 +269,7 @@ def ep_layer_chunked(group, world, x, ids, weights, compute, combine, placement=
     ep_layer's bit for bit."""
     T = x.shape[0]
     bounds = [(T * c // chunks, T * (c + 1) // chunks) for c in range(chunks)]
-    plans = dispatch_chunks(group, world, ids, placement, bounds)
+    plans = dispatch_chunks(group, world, ids, placement, bounds, planner)
 
     def send(c):
         lo, hi = bounds[c]
@@ -248,15 +295,16 @@ def ep_layer_chunked(group, world, x, ids, weights, compute, combine, placement=
     return torch.cat(outs)
 
 
-def ep_layer(group, world, x, ids, weights, compute, combine, placement=None):
+def ep_layer(group, world, x, ids, weights, compute, combine, placement=None, planner=None):
     """One expert-parallel layer call, compact exchange.
 
     compute(x_recv, ids_recv, n_valid) -> fp32 [n_valid, 2048]: the rows of the
     received slots with a valid id, in (token, slot) order (n_valid, known on
     the host, is their count); combine(rows [n, 2048], row_index [T, 8],
     weights, ids) -> output.  Both are injected so that the host logic also
-    runs on CPU ranks."""
-    plan, recv_counts, back_counts = dispatch_with_counts(group, world, ids, placement)
+    runs on CPU ranks.  planner: how the dispatch plan is made (TorchPlanner
+    by default)."""
+    plan, recv_counts, back_counts = dispatch_with_counts(group, world, ids, placement, planner)
     x_recv, ids_recv = exchange_rows(group, world, plan, x, recv_counts)
     out_rows = compute(x_recv, ids_recv, sum(back_counts))
     got = return_rows(group, world, plan, back_counts, out_rows)
@@ -282,13 +330,13 @@ def rank_sum(combine, got, row_index, like_weights):
     return combine(got, row_index, ones, ids)
 
 
-def ep_layer_partial(group, world, x, ids, weights, compute_partial, combine, placement=None):
+def ep_layer_partial(group, world, x, ids, weights, compute_partial, combine, placement=None, planner=None):
     """Compact exchange with the rank-partial combine.
 
     compute_partial(x_recv, ids_recv, w_recv) -> fp32 [n_recv, 2048]: per
     received token, its routing weights times this rank's projections summed
     in slot order."""
-    plan, recv_counts, _ = dispatch_with_counts(group, world, ids, placement)
+    plan, recv_counts, _ = dispatch_with_counts(group, world, ids, placement, planner)
     x_recv, ids_recv = exchange_rows(group, world, plan, x, recv_counts)
     w_send = torch.where(plan.slot_mask, weights[plan.token_index], torch.zeros_like(weights[plan.token_index]))
     w_recv = torch.empty((sum(recv_counts), TOP), dtype=torch.float32, device=x.device)
@@ -383,6 +431,7 @@ class ExpertParallelMoE:
         self.capacity = int(capacity)
         self.exchange = exchange
         self.placement = placement or contiguous_placement(world, banks[0].device)
+        self.planner = NativePlanner(world, self.placement, banks[0].device)
         self.symbol = 'ornith_routed_direct_launch' if act_bits == 8 else 'ornith_routed_direct_launch_a4'
         dev = banks[0].device
         self.layout = native.get_layout(self.capacity)
@@ -436,12 +485,16 @@ class ExpertParallelMoE:
             # the partial rows reach the combine without the ids: ids outside
             # -1..255 (flag 4 on one GPU) are flagged here, on the device
             self.flags.bitwise_or_(((ids >= E) | (ids < -1)).any().to(self.flags.dtype) * 4)
-            run = ep_layer_fixed_partial if self.exchange == 'fixed' else ep_layer_partial
-            return run(self.group, self.world, x, ids, weights, self.compute_partial, self.combine, self.placement)
+            if self.exchange == 'fixed':
+                return ep_layer_fixed_partial(self.group, self.world, x, ids, weights, self.compute_partial,
+                                              self.combine, self.placement)
+            return ep_layer_partial(self.group, self.world, x, ids, weights, self.compute_partial, self.combine,
+                                    self.placement, self.planner)
         if self.exchange == 'fixed':
             return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine,
                                   self.placement)
         if self.chunks > 1:
             return ep_layer_chunked(self.group, self.world, x, ids, weights, self.compute, self.combine,
-                                    self.placement, self.chunks)
-        return ep_layer(self.group, self.world, x, ids, weights, self.compute, self.combine, self.placement)
+                                    self.placement, self.chunks, self.planner)
+        return ep_layer(self.group, self.world, x, ids, weights, self.compute, self.combine, self.placement,
+                        self.planner)

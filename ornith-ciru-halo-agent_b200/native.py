@@ -84,6 +84,7 @@ SIGNATURES = {
     'ornith_moe_b200_scatter_route_rows': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_void_p],
                                            C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_plan': ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int] + [C.c_void_p] * 7, C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
     'ornith_dense_g256_abi_version': ([], C.c_uint32),
     'ornith_dense_g256_get_layout': ([C.c_int] * 4 + [C.POINTER(DenseLayout)], C.c_int),
@@ -367,6 +368,33 @@ def gather_route_rows(workspace, T, capacity, route_index, rows, flags):
         raise ValueError('gather_route_rows requires INT32 route indices [n] and FP32 rows [n,2048]')
     check(lib().ornith_moe_b200_gather_route_rows(ptr(workspace), workspace.numel(), T, capacity, ptr(route_index), n,
                                                   ptr(rows), ptr(flags), stream(rows)), 'gather_route_rows')
+
+
+def ep_plan(ids, owner, local, world):
+    """The expert-parallel dispatch plan of ids int32 [T, 8] in one launch
+    (owner, local: int32 [256] placement tables).  Returns device tensors
+    (counts int64 [world, 2], token_index int64, dest int64, local_ids int32
+    [., 8], slot_mask bool [., 8], row_index int32 [T, 8]); the row buffers
+    hold T * world rows, of which the first counts[:, 0].sum() are the plan."""
+    T = ids.shape[0]
+    dev = ids.device
+    if (ids.dtype != torch.int32 or ids.dim() != 2 or ids.shape[1] != 8 or not ids.is_contiguous()
+            or dev.type != 'cuda' or not 1 <= world <= 8 or T > 8192):
+        raise ValueError('ep_plan takes contiguous CUDA int32 ids [T <= 8192, 8] and 1..8 ranks')
+    for t in (owner, local):
+        if t.dtype != torch.int32 or t.shape != (256,) or not t.is_contiguous() or t.device != dev:
+            raise ValueError('ep_plan takes int32 [256] placement tables on the ids device')
+    n = T * world
+    counts = torch.empty((world, 2), dtype=torch.int64, device=dev)
+    token_index = torch.empty(n, dtype=torch.int64, device=dev)
+    dest = torch.empty(n, dtype=torch.int64, device=dev)
+    local_ids = torch.empty((n, 8), dtype=torch.int32, device=dev)
+    slot_mask = torch.empty((n, 8), dtype=torch.bool, device=dev)
+    row_index = torch.empty((T, 8), dtype=torch.int32, device=dev)
+    check(lib().ornith_moe_b200_ep_plan(ptr(ids), T, ptr(owner), ptr(local), world, ptr(counts), ptr(token_index),
+                                        ptr(dest), ptr(local_ids), ptr(slot_mask), ptr(row_index), stream(ids)),
+          'expert-parallel dispatch plan')
+    return counts, token_index, dest, local_ids, slot_mask, row_index
 
 
 def scatter_route_rows(workspace, T, capacity, rows):

@@ -18,6 +18,15 @@ def pytest_configure(config):
     config.addinivalue_line('markers', 'gpu: needs a CUDA device (B200)')
 
 
+def pytest_collection_modifyitems(config, items):
+    """The routed parity suite runs first and the allocation-free entry last,
+    so that a run stopped at its first failure has always checked parity."""
+    def rank(item):
+        name = item.path.name
+        return 0 if name == 'test_parity_gpu.py' else 2 if name == 'test_zz_no_alloc.py' else 1
+    items.sort(key=rank)   # stable: file order otherwise
+
+
 @pytest.fixture(scope='session')
 def S():
     return importlib.import_module('ornith_b200.synthetic')
