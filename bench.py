@@ -95,6 +95,9 @@ def parse():
                    help='expert placement of the expert-parallel configs')
     p.add_argument('--combine', choices=['exact', 'partial'], default='exact',
                    help='expert-parallel return: per-slot rows (bit-exact) or per-rank fp32 partial sums')
+    p.add_argument('--ep-return', choices=['nccl', 'p2p'], default='nccl',
+                   help='compact expert-parallel return: NCCL all_to_all, or stores into the home ranks\' buffers '
+                        'over NVLink peer memory (exact combine, one chunk)')
     p.add_argument('--ep-chunks', type=int, default=1,
                    help='compact expert-parallel exchange in this many pipelined token chunks (exact combine)')
     p.add_argument('--layers', type=int, default=None,
@@ -228,7 +231,8 @@ def run_ep(args):
         layers.append(ep.ExpertParallelMoE(None, world, (g[0], g[1], d[0], d[1]), capacity=min(T * world, 8192),
                                            act_bits=bits, exchange=cfg['exchange'], placement=placement,
                                            combine=args.combine,
-                                           chunks=args.ep_chunks if cfg['exchange'] == 'compact' else 1))
+                                           chunks=args.ep_chunks if cfg['exchange'] == 'compact' else 1,
+                                           return_path=args.ep_return if cfg['exchange'] == 'compact' else 'nccl'))
     logits = torch.randn((L, T, 256), device=dev, generator=gen) + bias
     x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
     w = torch.empty((L, T, 8), dtype=torch.float32, device=dev)
@@ -290,13 +294,17 @@ def run_ep(args):
                    'exchange': ('NCCL all_gather of token rows + equal-block all_to_all of fp32 per-slot rows '
                                 '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
                                 'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)'),
-                   'chunks': args.ep_chunks if cfg['exchange'] == 'compact' else 1},
+                   'chunks': args.ep_chunks if cfg['exchange'] == 'compact' else 1,
+                   'return': (('NVLink peer stores' if args.ep_return == 'p2p' else 'NCCL all_to_all')
+                              if cfg['exchange'] == 'compact' else 'NCCL all_to_all')},
         'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': graph is not None,
     }
     dist.barrier()
     step = None
     graph = None  # a graph holding NCCL calls is released before the process group
     torch.cuda.synchronize()
+    for layer in layers:
+        layer.close()   # peer-memory buffers, collectively
     dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)

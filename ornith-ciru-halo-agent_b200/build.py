@@ -12,7 +12,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / 'csrc'
 LIB = HERE / 'libornith_moe_b200.so'
 SOURCES = ['moe_api.cu', 'moe_generic.cu', 'moe_decode.cu', 'moe_prefill.cu', 'moe_noalloc.cu', 'dense_g256.cu', 'head_i8.cu',
-           'ep_plan.cu']
+           'ep_plan.cu', 'ep_p2p.cu']
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-lineinfo', '-O3', '-std=c++17',
          '-fmad=false', '-Xcompiler', '-fPIC,-fvisibility=hidden', '-shared', '-rdc=false',

@@ -1,0 +1,229 @@
+// Expert-parallel return over NVLink peer memory (declared in
+// include/ornith_moe_b200.h): the expert rank gathers the fp32 down
+// projections of the (token, slot) rows it computed and stores each one
+// straight into its home rank's receive buffer, then raises a flag there;
+// the home rank waits for the flags of the other ranks (bounded) before its
+// combine reads the buffer.  This replaces the row gather plus the NCCL
+// all_to_all of the compact exchange with one kernel per side.
+//
+// Receive buffers are plain device allocations shared by CUDA IPC handles.
+// Only ordinary stores reach peer memory: no TMA, no bulk copies, no
+// multicast.  The launcher checks every destination range against the
+// buffer's capacity on the host before the launch, and the kernel checks each
+// row again, so no store can leave a peer's buffer.  Every wait has a time
+// limit (flag 64 when it runs out).
+//
+// Ordering.  Each thread fences at system scope after its stores, the CTA
+// meets at a barrier and counts itself done on a device counter; the last CTA
+// fences again and publishes `epoch` into slot `me` of every other rank's
+// flag array with a system-scope release store.  The home rank's wait reads
+// the flags with system-scope acquire loads; its combine is the next kernel
+// on the same stream.  A receive buffer is written again only after the next
+// layer call's count exchange, which every rank enters after its combine was
+// issued on its stream, so a block is never overwritten while it is read.
+#include <stdint.h>
+
+#include <cstring>
+
+#include "../../include/ornith_moe_b200.h"
+#include "moe_layer.cuh"
+#include "nvtx_range.h"
+
+namespace ornith {
+namespace {
+
+constexpr int kP2PMaxWorld = 8;
+constexpr uint64_t kP2PTimeoutNs = 1000000000ull;
+
+struct ReturnArgs {
+    const float* route_out;
+    const int32_t* rowpos;  // route -> row of route_out on the tensor-core path, else null
+    const int32_t* route_index;
+    int R, rows, n;
+    int seg[kP2PMaxWorld + 1];         // rows [seg[h], seg[h+1]) of route_index go home to rank h
+    float* dst[kP2PMaxWorld];          // receive rows of each home rank (this rank's own buffer for h == me)
+    long long off[kP2PMaxWorld];       // first row of this rank's block in home h's buffer
+    long long cap;                     // rows of every receive buffer
+    uint32_t* sig[kP2PMaxWorld];       // flag array of each home rank
+    int world, me;
+    uint32_t epoch;
+    uint32_t* counter;                 // CTAs done; zero between calls
+    uint32_t* flags;
+};
+
+bool p2p_aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+__device__ __forceinline__ uint64_t p2p_now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__global__ __launch_bounds__(256) void ep_return_p2p_kernel(const ReturnArgs a) {
+    uint32_t f = 0;
+    for (int i = blockIdx.x; i < a.n; i += gridDim.x) {
+        int h = 0;
+#pragma unroll
+        for (int k = 1; k < kP2PMaxWorld; ++k)
+            if (k < a.world && i >= a.seg[k]) h = k;
+        const long long drow = a.off[h] + (i - a.seg[h]);
+        if (drow < 0 || drow >= a.cap) {  // never true after the launcher's checks
+            f |= kFlagInvalidId;
+            continue;
+        }
+        float4* d = reinterpret_cast<float4*>(a.dst[h] + size_t(drow) * kH) + threadIdx.x * 2;
+        const int r = a.route_index[i];
+        int row = -1;
+        if (r >= 0 && r < a.R) row = a.rowpos ? a.rowpos[r] : r;
+        if (row < 0 || row >= a.rows) {
+            d[0] = d[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            f |= kFlagInvalidId;
+            continue;
+        }
+        const float4* src = reinterpret_cast<const float4*>(a.route_out + size_t(row) * kH) + threadIdx.x * 2;
+        const float4 v0 = __ldcs(src), v1 = __ldcs(src + 1);
+        d[0] = v0;
+        d[1] = v1;
+    }
+    if (f && threadIdx.x == 0) atomicOr(a.flags, f);
+    __threadfence_system();  // this thread's stores, before the CTA counts itself done
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t done = atomicAdd(a.counter, 1u);
+        if (done == gridDim.x - 1) {  // the last CTA: every row of this call is stored
+            __threadfence_system();
+            for (int h = 0; h < a.world; ++h) {
+                if (h == a.me) continue;
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[h] + a.me), "r"(a.epoch) : "memory");
+            }
+            *a.counter = 0u;  // ready for the next call on this stream
+        }
+    }
+}
+
+// Lane d waits until rank d's flag in this rank's array reaches `epoch`
+// (wrap-around safe), for at most about a second.
+__global__ __launch_bounds__(32) void ep_wait_signals_kernel(const uint32_t* sig, int world, int me, uint32_t epoch,
+                                                             uint32_t* flags) {
+    const int d = threadIdx.x;
+    if (d >= world || d == me) return;
+    const uint64_t t0 = p2p_now_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sig + d) : "memory");
+        if (int32_t(v - epoch) >= 0) return;
+        if (p2p_now_ns() - t0 > kP2PTimeoutNs) {
+            atomicOr(flags, uint32_t(kFlagWaitTimeout));
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
+}  // namespace
+}  // namespace ornith
+
+using namespace ornith;
+
+extern "C" cudaError_t ornith_moe_b200_ep_buffer_alloc(size_t bytes, void** ptr) {
+    if (!ptr || !bytes) return cudaErrorInvalidValue;
+    *ptr = nullptr;
+    void* p = nullptr;
+    cudaError_t st = cudaMalloc(&p, bytes);
+    if (st != cudaSuccess) return st;
+    if ((st = cudaMemset(p, 0, bytes)) != cudaSuccess) {
+        cudaFree(p);
+        return st;
+    }
+    *ptr = p;
+    return cudaSuccess;
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_buffer_free(void* ptr) { return ptr ? cudaFree(ptr) : cudaSuccess; }
+
+extern "C" cudaError_t ornith_moe_b200_ep_ipc_handle(const void* base, void* handle_out) {
+    if (!base || !handle_out) return cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h;
+    const cudaError_t st = cudaIpcGetMemHandle(&h, const_cast<void*>(base));
+    if (st == cudaSuccess) memcpy(handle_out, &h, sizeof(h));
+    return st;
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_ipc_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return cudaErrorInvalidValue;
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_ipc_close(void* ptr) {
+    return ptr ? cudaIpcCloseMemHandle(ptr) : cudaSuccess;
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_return_p2p(const void* workspace, size_t bytes, int T, int Tcap,
+                                                     const void* route_index_i32, int n, const int32_t* seg,
+                                                     void* const* dst_rows, const int64_t* dst_offset,
+                                                     int64_t dst_capacity_rows, void* const* signals, int world,
+                                                     int me, uint32_t epoch, void* counter_u32, void* flags,
+                                                     cudaStream_t stream) {
+    if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap || n < 0 || world < 1 || world > kP2PMaxWorld || me < 0 ||
+        me >= world || dst_capacity_rows < 0)
+        return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes) return cudaErrorInvalidValue;
+    if (!workspace || (n && !route_index_i32) || !seg || !dst_rows || !dst_offset || !signals || !counter_u32 ||
+        !flags || !p2p_aligned(workspace, 256) || !p2p_aligned(route_index_i32, 4) || !p2p_aligned(counter_u32, 4) ||
+        !p2p_aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    ReturnArgs a{};
+    if (seg[0] != 0 || seg[world] != n) return cudaErrorInvalidValue;
+    for (int h = 0; h < world; ++h) {
+        const int rows_h = seg[h + 1] - seg[h];
+        // every destination range inside its buffer, checked before any store is issued
+        if (rows_h < 0 || dst_offset[h] < 0 || dst_offset[h] + rows_h > dst_capacity_rows) return cudaErrorInvalidValue;
+        if ((rows_h && !dst_rows[h]) || !p2p_aligned(dst_rows[h], 16)) return cudaErrorInvalidValue;
+        if (h != me && (!signals[h] || !p2p_aligned(signals[h], 4))) return cudaErrorInvalidValue;
+        a.seg[h] = seg[h];
+        a.dst[h] = static_cast<float*>(dst_rows[h]);
+        a.off[h] = dst_offset[h];
+        a.sig[h] = static_cast<uint32_t*>(signals[h]);
+    }
+    a.seg[world] = n;
+    const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+    a.route_out = reinterpret_cast<const float*>(ws + w.route_out);
+    a.rowpos = rows_by_position(T) ? reinterpret_cast<const int32_t*>(ws + w.rowpos) : nullptr;
+    a.route_index = static_cast<const int32_t*>(route_index_i32);
+    a.R = T * kTop;
+    a.rows = T * (kTop + 1);
+    a.n = n;
+    a.cap = dst_capacity_rows;
+    a.world = world;
+    a.me = me;
+    a.epoch = epoch;
+    a.counter = static_cast<uint32_t*>(counter_u32);
+    a.flags = static_cast<uint32_t*>(flags);
+    NvtxRange range("ornith.ep.return_p2p");
+    int device = 0, sms = 0;
+    cudaError_t st = cudaGetDevice(&device);
+    if (st != cudaSuccess) return st;
+    if ((st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return st;
+    // at least one CTA: with no rows the call still raises the flags
+    const int grid = n < 2 * sms ? (n > 0 ? n : 1) : 2 * sms;
+    count_launches(1);
+    ep_return_p2p_kernel<<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_wait_signals(const void* signals_u32, int world, int me, uint32_t epoch,
+                                                       void* flags, cudaStream_t stream) {
+    if (world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || !signals_u32 || !flags ||
+        !p2p_aligned(signals_u32, 4) || !p2p_aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    if (world == 1) return cudaSuccess;
+    NvtxRange range("ornith.ep.wait");
+    count_launches(1);
+    ep_wait_signals_kernel<<<1, 32, 0, stream>>>(static_cast<const uint32_t*>(signals_u32), world, me, epoch,
+                                                 static_cast<uint32_t*>(flags));
+    return cudaGetLastError();
+}

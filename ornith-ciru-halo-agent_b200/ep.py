@@ -44,6 +44,7 @@ tolerance) rather than bit for bit, for up to 8x less return traffic.
 These collectives are the layer's only exchange.  Every rank takes the same
 collective steps in the same order, zero-sized messages included.
 """
+import ctypes as C
 from dataclasses import dataclass
 
 import torch
@@ -193,6 +194,36 @@ def dispatch_with_counts(group, world, ids, placement=None, planner=None):
     both = torch.cat([counts, got], dim=1).tolist()          # the single host synchronisation
     plan = planner.finish(state, ids, [int(r[0]) for r in both], [int(r[1]) for r in both])
     return plan, [int(r[2]) for r in both], [int(r[3]) for r in both]
+
+
+def peer_offsets(matrix, me):
+    """From the gathered count matrix (matrix[src][d] = (tokens src sends to
+    d, (token, slot) rows d returns to src)) the split lists of rank `me` and,
+    for the return over peer memory, the first row of its block in every home
+    rank's receive buffer: home h holds the blocks of ranks 0, 1, ... in rank
+    order, so rank me's block starts after the rows h gets from ranks below me.
+    Returns (send_counts, home_counts, recv_counts, back_counts, offsets)."""
+    world = len(matrix)
+    send = [int(matrix[me][d][0]) for d in range(world)]
+    home = [int(matrix[me][d][1]) for d in range(world)]
+    recv = [int(matrix[src][me][0]) for src in range(world)]
+    back = [int(matrix[src][me][1]) for src in range(world)]
+    offsets = [sum(int(matrix[h][d][1]) for d in range(me)) for h in range(world)]
+    return send, home, recv, back, offsets
+
+
+def dispatch_with_matrix(group, world, me, ids, placement=None, planner=None):
+    """dispatch_with_counts with an all_gather of every rank's counts instead
+    of the all_to_all, so that this rank also learns where its returned rows
+    go in each home rank's buffer; still one host synchronisation.  Returns
+    (plan, recv_counts, back_counts, offsets)."""
+    planner = planner or TorchPlanner(world, placement)
+    state, counts = planner.start(ids)
+    parts = [torch.empty_like(counts) for _ in range(world)]
+    dist.all_gather(parts, counts.contiguous(), group=group)
+    matrix = torch.stack(parts).tolist()                   # the single host synchronisation
+    send, home, recv, back, offsets = peer_offsets(matrix, me)
+    return planner.finish(state, ids, send, home), recv, back, offsets
 
 
 def _a2a(group, out, inp, out_splits, in_splits):
@@ -399,6 +430,82 @@ def ep_layer_fixed_partial(group, world, x, ids, weights, compute_partial, combi
     return rank_sum(combine, got.view(world * T, H), row_index.contiguous(), weights)
 
 
+class _DeviceArray:
+    """A device range described by __cuda_array_interface__ (v3), so that
+    torch.as_tensor can view memory this module allocated itself."""
+
+    def __init__(self, address, shape, typestr):
+        self.__cuda_array_interface__ = {'shape': tuple(shape), 'typestr': typestr, 'data': (int(address), False),
+                                         'strides': None, 'version': 3}
+
+
+class PeerReturn:
+    """This rank's receive buffer for the return over NVLink peer memory,
+    shared with the other ranks of the node: fp32 rows [cap, 2048], then one
+    uint32 flag per rank.  Made collectively (every rank at once); close()
+    collectively before the process group goes away.  send() stores this
+    rank's computed rows into their home ranks' buffers and raises its flag
+    there (ornith_moe_b200_ep_return_p2p); wait() waits, bounded, for the
+    other ranks' flags of the same call (ornith_moe_b200_ep_wait_signals)."""
+
+    def __init__(self, group, world, me, cap_rows, device):
+        from . import native
+        if not 1 <= world <= 8:
+            raise ValueError('the peer-memory return serves 1..8 ranks of one node')
+        self.native, self.group, self.world, self.me, self.cap = native, group, world, me, int(cap_rows)
+        self.flag_offset = (self.cap * H * 4 + 255) // 256 * 256
+        self.base = native.ep_buffer_alloc(self.flag_offset + 256)
+        self.peers = {}
+        try:
+            handles = [None] * world
+            dist.all_gather_object(handles, native.ep_ipc_handle(self.base), group=group)
+            for r in range(world):
+                if r != me:
+                    self.peers[r] = native.ep_ipc_open(handles[r])
+        except BaseException:
+            self._release()
+            raise
+        bases = [self.base if r == me else self.peers[r] for r in range(world)]
+        self.dst = (C.c_void_p * world)(*bases)
+        self.signals = (C.c_void_p * world)(*[b + self.flag_offset for b in bases])
+        self.rows = torch.as_tensor(_DeviceArray(self.base, (self.cap, H), '<f4'), device=device)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.epoch = 0
+
+    def send(self, workspace, T, capacity, route_index, back_counts, offsets, flags):
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        seg = [0]
+        for c in back_counts:
+            seg.append(seg[-1] + int(c))
+        self.native.ep_return_p2p(workspace, T, capacity, route_index, seg, self.dst, offsets, self.cap,
+                                  self.signals, self.world, self.me, self.epoch, self.counter, flags)
+
+    def wait(self, flags):
+        self.native.ep_wait_signals(self.base + self.flag_offset, self.world, self.me, self.epoch, flags)
+
+    def _release(self):
+        for ptr in self.peers.values():
+            self.native.ep_ipc_close(ptr)
+        self.peers = {}
+        if self.base:
+            self.native.ep_buffer_free(self.base)
+            self.base = 0
+
+    def close(self):
+        """Collective: no rank unmaps or frees before every rank has finished."""
+        if not self.base:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.rows = None
+        for ptr in self.peers.values():
+            self.native.ep_ipc_close(ptr)
+        self.peers = {}
+        dist.barrier(group=self.group)
+        self.native.ep_buffer_free(self.base)
+        self.base = 0
+
+
 class ExpertParallelMoE:
     """GPU expert-parallel layer over NCCL with this library's kernels.
 
@@ -413,7 +520,7 @@ class ExpertParallelMoE:
     every rank; contiguous ranges by default."""
 
     def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact', placement=None,
-                 combine='exact', chunks=1):
+                 combine='exact', chunks=1, return_path='nccl'):
         from . import native
         if exchange not in ('compact', 'fixed'):
             raise ValueError(f'unknown exchange mode {exchange!r}')
@@ -423,6 +530,10 @@ class ExpertParallelMoE:
             raise ValueError('the rank-partial combine supports at most 8 ranks')
         if not isinstance(chunks, int) or chunks < 1 or (chunks > 1 and (exchange, combine) != ('compact', 'exact')):
             raise ValueError('chunks > 1 applies to the compact exchange with the exact combine')
+        if return_path not in ('nccl', 'p2p') or (return_path == 'p2p' and (
+                (exchange, combine, chunks) != ('compact', 'exact', 1) or not 1 <= world <= 8)):
+            raise ValueError("return_path 'p2p' applies to the compact exchange with the exact combine, one chunk, "
+                             "on 1..8 ranks of one node")
         self.chunks = chunks
         self.combine_mode = combine
         self.native = native
@@ -432,6 +543,10 @@ class ExpertParallelMoE:
         self.exchange = exchange
         self.placement = placement or contiguous_placement(world, banks[0].device)
         self.planner = NativePlanner(world, self.placement, banks[0].device)
+        self.me = dist.get_rank(group)
+        # a home rank receives at most one row per (token, slot): 8 per local token
+        self.peer = PeerReturn(group, world, self.me, TOP * self.capacity, banks[0].device) \
+            if return_path == 'p2p' else None
         self.symbol = 'ornith_routed_direct_launch' if act_bits == 8 else 'ornith_routed_direct_launch_a4'
         dev = banks[0].device
         self.layout = native.get_layout(self.capacity)
@@ -480,6 +595,27 @@ class ExpertParallelMoE:
         self.native.combine_gathered(rows, row_index, weights, ids, out, self.flags)
         return out
 
+    def _layer_p2p(self, x, ids, weights):
+        """Compact exchange whose return goes straight into the home ranks'
+        receive buffers over NVLink (PeerReturn) instead of an all_to_all."""
+        plan, recv_counts, back_counts, offsets = dispatch_with_matrix(self.group, self.world, self.me, ids,
+                                                                        self.placement, self.planner)
+        x_recv, ids_recv = exchange_rows(self.group, self.world, plan, x, recv_counts)
+        n = self._layer(x_recv, ids_recv)
+        valid = (ids_recv >= 0).view(-1)
+        sel = torch.nonzero_static(valid, size=sum(back_counts)).flatten().to(torch.int32)
+        self.peer.send(self.workspace, n, self.capacity, sel, back_counts, offsets, self.flags)
+        self.peer.wait(self.flags)
+        got = self.peer.rows[:sum(plan.home_counts)]
+        return self.combine(got, route_row_index(x.shape[0], plan, x.device), weights, ids)
+
+    def close(self):
+        """Release the peer-memory buffers (collective; before the process
+        group is destroyed)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
     def __call__(self, x, ids, weights):
         if self.combine_mode == 'partial':
             # the partial rows reach the combine without the ids: ids outside
@@ -493,6 +629,8 @@ class ExpertParallelMoE:
         if self.exchange == 'fixed':
             return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine,
                                   self.placement)
+        if self.peer is not None:
+            return self._layer_p2p(x, ids, weights)
         if self.chunks > 1:
             return ep_layer_chunked(self.group, self.world, x, ids, weights, self.compute, self.combine,
                                     self.placement, self.chunks, self.planner)

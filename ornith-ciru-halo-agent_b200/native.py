@@ -85,6 +85,16 @@ SIGNATURES = {
                                            C.c_int),
     'ornith_moe_b200_repack_n16_to_n32': ([C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_void_p], C.c_int),
     'ornith_moe_b200_ep_plan': ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int] + [C.c_void_p] * 7, C.c_int),
+    'ornith_moe_b200_ep_buffer_alloc': ([C.c_size_t, C.POINTER(C.c_void_p)], C.c_int),
+    'ornith_moe_b200_ep_buffer_free': ([C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_ipc_handle': ([C.c_void_p, C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_ipc_open': ([C.c_void_p, C.POINTER(C.c_void_p)], C.c_int),
+    'ornith_moe_b200_ep_ipc_close': ([C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_return_p2p': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                       C.POINTER(C.c_int32), C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int64,
+                                       C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p,
+                                       C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_wait_signals': ([C.c_void_p, C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
     'ornith_dense_g256_abi_version': ([], C.c_uint32),
     'ornith_dense_g256_get_layout': ([C.c_int] * 4 + [C.POINTER(DenseLayout)], C.c_int),
@@ -395,6 +405,60 @@ def ep_plan(ids, owner, local, world):
                                         ptr(dest), ptr(local_ids), ptr(slot_mask), ptr(row_index), stream(ids)),
           'expert-parallel dispatch plan')
     return counts, token_index, dest, local_ids, slot_mask, row_index
+
+
+def ep_buffer_alloc(nbytes):
+    """A zeroed device allocation for a peer-memory receive buffer; its address."""
+    p = C.c_void_p()
+    check(lib().ornith_moe_b200_ep_buffer_alloc(int(nbytes), C.byref(p)), 'expert-parallel buffer allocation')
+    return int(p.value)
+
+
+def ep_buffer_free(address):
+    check(lib().ornith_moe_b200_ep_buffer_free(C.c_void_p(address)), 'expert-parallel buffer release')
+
+
+def ep_ipc_handle(address):
+    """The 64-byte CUDA IPC handle of an ep_buffer_alloc allocation."""
+    h = (C.c_uint8 * 64)()
+    check(lib().ornith_moe_b200_ep_ipc_handle(C.c_void_p(address), h), 'IPC handle')
+    return bytes(h)
+
+
+def ep_ipc_open(handle):
+    """Map another rank's buffer from its IPC handle; the local address."""
+    if len(handle) != 64:
+        raise ValueError('an IPC handle has 64 bytes')
+    h = (C.c_uint8 * 64).from_buffer_copy(handle)
+    p = C.c_void_p()
+    check(lib().ornith_moe_b200_ep_ipc_open(h, C.byref(p)), 'IPC open')
+    return int(p.value)
+
+
+def ep_ipc_close(address):
+    check(lib().ornith_moe_b200_ep_ipc_close(C.c_void_p(address)), 'IPC close')
+
+
+def ep_return_p2p(workspace, T, capacity, route_index, seg, dst, offsets, cap_rows, signals, world, me, epoch,
+                  counter, flags):
+    """Store the fp32 down projections of route_index (rows [seg[h], seg[h+1])
+    to home rank h) into the home ranks' receive buffers (dst: ctypes array of
+    world addresses) at rows offsets[h]..., then raise `epoch` in their flag
+    arrays (signals)."""
+    n = route_index.numel()
+    if (route_index.dtype != torch.int32 or not route_index.is_contiguous() or len(seg) != world + 1
+            or len(offsets) != world or len(dst) != world or len(signals) != world):
+        raise ValueError('ep_return_p2p takes INT32 route indices and per-rank segments, offsets and addresses')
+    seg_a = (C.c_int32 * (world + 1))(*seg)
+    off_a = (C.c_int64 * world)(*offsets)
+    check(lib().ornith_moe_b200_ep_return_p2p(ptr(workspace), workspace.numel(), T, capacity, ptr(route_index), n,
+                                              seg_a, dst, off_a, cap_rows, signals, world, me, epoch, ptr(counter),
+                                              ptr(flags), stream(workspace)), 'expert-parallel peer return')
+
+
+def ep_wait_signals(signals_address, world, me, epoch, flags):
+    check(lib().ornith_moe_b200_ep_wait_signals(C.c_void_p(signals_address), world, me, epoch, ptr(flags),
+                                                stream(flags)), 'expert-parallel peer wait')
 
 
 def scatter_route_rows(workspace, T, capacity, rows):

@@ -126,6 +126,22 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
             out = ep.ep_layer_fixed(None, world, x, ids, weights, compute_block, fake_combine_gathered, placement)
         elif mode == 'compact':
             out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered, placement)
+        elif mode == 'peer':      # the return over peer memory, its stores emulated on the host
+            me = dist.get_rank()
+            plan, recv_counts, back_counts, offsets = ep.dispatch_with_matrix(None, world, me, ids, placement)
+            plan2, recv2, back2 = ep.dispatch_with_counts(None, world, ids, placement)
+            assert (recv_counts, back_counts) == (recv2, back2)
+            assert (plan.send_counts, plan.home_counts) == (plan2.send_counts, plan2.home_counts)
+            x_recv, ids_recv = ep.exchange_rows(None, world, plan, x, recv_counts)
+            rows = compute(x_recv, ids_recv, sum(back_counts))
+            gathered = [None] * world
+            dist.all_gather_object(gathered, (rows, back_counts, offsets))
+            got = torch.full((sum(plan.home_counts), H), float('nan'))   # an unwritten row would show
+            for rows_d, back_d, off_d in gathered:
+                lo, k = sum(back_d[:me]), back_d[me]
+                assert 0 <= off_d[me] and off_d[me] + k <= got.shape[0]
+                got[off_d[me]:off_d[me] + k] = rows_d[lo:lo + k]
+            out = fake_combine_gathered(got, ep.route_row_index(T, plan, got.device), weights, ids)
         elif mode == 'chunked':   # pipelined chunks; T + 1 chunks leaves one chunk empty
             chunks = 3 if world == 2 else T + 1
             out = ep.ep_layer_chunked(None, world, x, ids, weights, compute, fake_combine_gathered, placement,
@@ -149,7 +165,7 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
 
 
 @pytest.mark.parametrize('balanced', [False, True])
-@pytest.mark.parametrize('mode', ['compact', 'chunked', 'fixed', 'compact_partial', 'fixed_partial'])
+@pytest.mark.parametrize('mode', ['compact', 'chunked', 'peer', 'fixed', 'compact_partial', 'fixed_partial'])
 @pytest.mark.parametrize('world,T', [(2, 16), (4, 9)])
 def test_ep_dispatch_combine_matches_single_rank(world, T, mode, balanced):
     ctx = mp.get_context('spawn')

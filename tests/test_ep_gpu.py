@@ -31,9 +31,11 @@ def _bank(gen, experts, N, K, dev):
     return codes, meta.view(torch.uint32)
 
 
-CASES = [  # (exchange, balanced placement, combine)
-    ('compact', False, 'exact'), ('compact', True, 'exact'), ('fixed', False, 'exact'), ('fixed', True, 'exact'),
-    ('compact', True, 'partial'), ('fixed', True, 'partial'),
+CASES = [  # (exchange, balanced placement, combine, further ExpertParallelMoE options)
+    ('compact', False, 'exact', {}), ('compact', True, 'exact', {}), ('fixed', False, 'exact', {}),
+    ('fixed', True, 'exact', {}), ('compact', True, 'partial', {}), ('fixed', True, 'partial', {}),
+    ('compact', True, 'exact', {'chunks': 3}),
+    ('compact', False, 'exact', {'return_path': 'p2p'}), ('compact', True, 'exact', {'return_path': 'p2p'}),
 ]
 
 
@@ -78,7 +80,7 @@ def _worker(rank, world, port, T, q):
             *[native.ptr(t) for t in (x, w, ids, gc, gm, dc, dm, ws)], ws.numel(), native.ptr(ref),
             native.ptr(flags), T, T, native.stream(x)), 'reference layer')
         results = []
-        for mode, balanced, combine in CASES:
+        for mode, balanced, combine, options in CASES:
             if balanced:  # any placement must give the same result; use a skewed-load one
                 placement = ep.balanced_placement(torch.arange(256, dtype=torch.float64).flip(0) ** 2, world, dev)
             else:
@@ -89,12 +91,15 @@ def _worker(rank, world, port, T, q):
                 return bank.view(torch.int32)[sl].contiguous().view(torch.uint32)
 
             layer = ep.ExpertParallelMoE(None, world, (pick(gc), pick(gm), pick(dc), pick(dm)), capacity=T * world,
-                                         exchange=mode, placement=placement, combine=combine)
-            out = layer(x, ids, w)
-            torch.cuda.synchronize()
-            ok = (bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))) if combine == 'exact'
-                  else _close(out, ref))
-            results.append(((mode, balanced, combine), ok, int(layer.flags.item())))
+                                         exchange=mode, placement=placement, combine=combine, **options)
+            ok = True
+            for _ in range(2):   # twice: the second call reuses the exchange buffers
+                out = layer(x, ids, w)
+                torch.cuda.synchronize()
+                ok = ok and (bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))) if combine == 'exact'
+                             else _close(out, ref))
+            results.append(((mode, balanced, combine, tuple(options.items())), ok, int(layer.flags.item())))
+            layer.close()
             dist.barrier()
         q.put((rank, results, int(flags.item()), ''))
         dist.barrier()

@@ -165,3 +165,51 @@ def test_ep_plan_validation_without_device_work(native):
         assert call(**{name: None}) == INVALID, name
     assert call(tok=C.c_void_p(base + (4 << 24) + 4)) == INVALID
     assert call(rows=C.c_void_p(base + (8 << 24) + 2)) == INVALID
+
+
+def test_peer_return_validation_without_device_work(native):
+    """The peer-memory return's entry points reject bad arguments before any
+    device work; every destination range is checked against the capacity."""
+    lib = native.lib()
+    p = C.c_void_p()
+    assert lib.ornith_moe_b200_ep_buffer_alloc(0, C.byref(p)) == INVALID
+    assert lib.ornith_moe_b200_ep_buffer_alloc(256, None) == INVALID
+    assert lib.ornith_moe_b200_ep_buffer_free(None) == 0
+    assert lib.ornith_moe_b200_ep_ipc_close(None) == 0
+    h = (C.c_uint8 * 64)()
+    assert lib.ornith_moe_b200_ep_ipc_handle(None, h) == INVALID
+    assert lib.ornith_moe_b200_ep_ipc_open(None, C.byref(p)) == INVALID
+    sig = C.c_void_p(1 << 30)
+    assert lib.ornith_moe_b200_ep_wait_signals(sig, 0, 0, 1, sig, None) == INVALID
+    assert lib.ornith_moe_b200_ep_wait_signals(sig, 9, 0, 1, sig, None) == INVALID
+    assert lib.ornith_moe_b200_ep_wait_signals(sig, 2, 2, 1, sig, None) == INVALID
+    assert lib.ornith_moe_b200_ep_wait_signals(None, 2, 0, 1, sig, None) == INVALID
+    assert lib.ornith_moe_b200_ep_wait_signals(sig, 1, 0, 1, sig, None) == 0     # one rank: nothing to wait for
+
+    fn = lib.ornith_moe_b200_ep_return_p2p
+    nb = native.get_layout(16).workspace_bytes
+    base = 1 << 32
+    ws, ri, counter, flags = (C.c_void_p(base + (i << 28)) for i in range(4))
+    world = 2
+    dst = (C.c_void_p * world)(base + (5 << 28), base + (6 << 28))
+    sigs = (C.c_void_p * world)(base + (7 << 28), base + (8 << 28))
+
+    def call(seg=(0, 3, 5), off=(0, 4), cap=8, n=5, me=0, T=16, Tcap=16, nbytes=nb, w=world, d=dst, s=sigs):
+        seg_a = (C.c_int32 * len(seg))(*seg)
+        off_a = (C.c_int64 * len(off))(*off)
+        return fn(ws, nbytes, T, Tcap, ri, n, seg_a, d, off_a, cap, s, w, me, 1, counter, flags, None)
+
+    assert call(T=17) == INVALID
+    assert call(nbytes=nb - 1) == INVALID
+    assert call(w=0) == INVALID
+    assert call(me=2) == INVALID
+    assert call(seg=(1, 3, 5)) == INVALID           # segments start at 0
+    assert call(seg=(0, 3, 4)) == INVALID           # and end at n
+    assert call(seg=(0, 4, 3), n=3) == INVALID      # and never go down
+    assert call(off=(6, 0)) == INVALID              # rank 0's 3 rows at 6..8 of an 8-row buffer
+    assert call(off=(0, 7)) == INVALID              # rank 1's 2 rows at 7..8
+    assert call(off=(-1, 0)) == INVALID
+    assert call(cap=-1) == INVALID
+    assert call(d=(C.c_void_p * world)(base + (5 << 28), None)) == INVALID
+    assert call(d=(C.c_void_p * world)(base + (5 << 28) + 4, base + (6 << 28))) == INVALID   # 16-byte rows
+    assert call(s=(C.c_void_p * world)(base + (7 << 28), None)) == INVALID                 # a peer's flags
