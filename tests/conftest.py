@@ -19,11 +19,16 @@ def pytest_configure(config):
 
 
 def pytest_collection_modifyitems(config, items):
-    """The routed parity suite runs first and the allocation-free entry last,
-    so that a run stopped at its first failure has always checked parity."""
+    """Order: the routed parity suite, the other single-GPU files, the
+    expert-parallel files, and the allocation-free entry last, so that a run
+    stopped at its first failure has always checked the single-GPU paths."""
     def rank(item):
         name = item.path.name
-        return 0 if name == 'test_parity_gpu.py' else 2 if name == 'test_zz_no_alloc.py' else 1
+        if name == 'test_parity_gpu.py':
+            return 0
+        if name == 'test_zz_no_alloc.py':
+            return 3
+        return 2 if name.startswith('test_ep_') and name.endswith('_gpu.py') else 1
     items.sort(key=rank)   # stable: file order otherwise
 
 
