@@ -211,21 +211,22 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_plan(
     void* token_index_i64, void* dest_i64, void* local_ids_i32, void* slot_mask_u8, void* row_index_i32,
     cudaStream_t stream);
 
-/* Expert-parallel return over NVLink peer memory.  Each rank owns one
- * receive buffer (fp32 rows [cap][2048] followed by a uint32 flag per rank),
- * made by ep_buffer_alloc (zeroed) and shared with the other ranks of the node
- * through a CUDA IPC handle (ep_ipc_handle: 64 bytes; ep_ipc_open/_close on
- * the peers).  ep_return_p2p: after a layer call of T tokens on `workspace`,
- * rows [seg[h], seg[h+1]) of route_index (the routes whose down projections
- * go home to rank h, seg a host array of world+1 entries) are copied to rows
- * dst_offset[h]... of dst_rows[h] (host arrays of world entries; dst_rows[me]
- * is this rank's own buffer), then `epoch` is stored into slot `me` of every
- * other rank's flag array (signals[h]).  Every destination range must lie
- * inside dst_capacity_rows, which is checked before the launch.  counter_u32
- * is a zeroed device word per stream.  ep_wait_signals: waits until every
- * other rank's flag in this rank's array has reached `epoch`, for at most
- * about a second (then flag 64).  Plain stores and loads only (no TMA, no
- * multicast).  No counterpart in the reference, which runs one rank. */
+/* Expert-parallel exchanges over NVLink peer memory.  Each rank owns a
+ * receive buffer made by ep_buffer_alloc (zeroed device memory), shared with
+ * the other ranks of the node through a CUDA IPC handle (ep_ipc_handle: 64
+ * bytes; ep_ipc_open/_close on the peers); the caller lays out rows and flag
+ * arrays (one uint32 per rank) inside it.  ep_return_p2p: after a layer call
+ * of T tokens on `workspace`, rows [seg[h], seg[h+1]) of route_index (the
+ * routes whose down projections go home to rank h; seg a host array of
+ * world+1 entries) are copied to rows dst_offset[h]... of dst_rows[h] (host
+ * arrays of world entries; entry `me` is this rank's own buffer), then
+ * `epoch` is stored into slot `me` of every other rank's flag array
+ * (signals[h]).  Every destination range must lie inside dst_capacity_rows,
+ * which is checked before the launch.  counter_u32 is a zeroed device word
+ * per stream.  ep_wait_signals: waits until every other rank's flag in this
+ * rank's array has reached `epoch`, for at most about a second (then flag
+ * 64).  Plain stores and loads only (no TMA, no multicast).  No counterpart
+ * in the reference, which runs one rank. */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_buffer_alloc(size_t bytes, void** ptr);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_buffer_free(void* ptr);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_ipc_handle(const void* base, void* handle_out);
@@ -235,6 +236,16 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_return_p2p(
     const void* workspace, size_t bytes, int T, int Tcap, const void* route_index_i32, int n, const int32_t* seg,
     void* const* dst_rows, const int64_t* dst_offset, int64_t dst_capacity_rows, void* const* signals, int world,
     int me, uint32_t epoch, void* counter_u32, void* flags_u32, cudaStream_t stream);
+/* The dispatch direction: sent row i of a dispatch plan (token_index int64,
+ * local_ids int32 [n][8], rows [seg[d], seg[d+1]) to expert rank d) is stored
+ * as token row x[token_index[i]] (bf16 [T][2048]) and its ids at row
+ * dst_offset[d] + i - seg[d] of expert rank d's buffers (dst_x, dst_ids), then
+ * `epoch` goes into slot `me` of the other ranks' dispatch flag arrays. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_dispatch_p2p(
+    const void* x_bf16, int T, const void* token_index_i64, const void* local_ids_i32, int n, const int32_t* seg,
+    void* const* dst_x, void* const* dst_ids, const int64_t* dst_offset, int64_t dst_capacity_rows,
+    void* const* signals, int world, int me, uint32_t epoch, void* counter_u32, void* flags_u32,
+    cudaStream_t stream);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_wait_signals(
     const void* signals_u32, int world, int me, uint32_t epoch, void* flags_u32, cudaStream_t stream);
 

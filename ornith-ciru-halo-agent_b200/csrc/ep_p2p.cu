@@ -1,10 +1,13 @@
-// Expert-parallel return over NVLink peer memory (declared in
-// include/ornith_moe_b200.h): the expert rank gathers the fp32 down
-// projections of the (token, slot) rows it computed and stores each one
-// straight into its home rank's receive buffer, then raises a flag there;
-// the home rank waits for the flags of the other ranks (bounded) before its
-// combine reads the buffer.  This replaces the row gather plus the NCCL
-// all_to_all of the compact exchange with one kernel per side.
+// Expert-parallel exchanges over NVLink peer memory (declared in
+// include/ornith_moe_b200.h).  Dispatch: the home rank stores each token row
+// it sends (bf16, 4 KB) and its local ids straight into the expert rank's
+// receive buffer.  Return: the expert rank gathers the fp32 down projections
+// of the (token, slot) rows it computed and stores each one straight into its
+// home rank's receive buffer.  Each direction then raises a flag in the
+// receiving ranks' flag arrays, and the receiver waits for the flags of the
+// other ranks (bounded) before it reads its buffer.  This replaces the
+// gathers and the NCCL all_to_alls of the compact exchange with one kernel
+// per direction and side.
 //
 // Receive buffers are plain device allocations shared by CUDA IPC handles.
 // Only ordinary stores reach peer memory: no TMA, no bulk copies, no
@@ -97,6 +100,65 @@ __global__ __launch_bounds__(256) void ep_return_p2p_kernel(const ReturnArgs a) 
                 asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[h] + a.me), "r"(a.epoch) : "memory");
             }
             *a.counter = 0u;  // ready for the next call on this stream
+        }
+    }
+}
+
+struct DispatchArgs {
+    const uint16_t* x;                 // bf16 token rows [T][2048] of this (home) rank
+    const long long* token_index;      // plan: token of sent row i
+    const int32_t* local_ids;          // plan: [n][8] ids in the destination's numbering
+    int T, n;
+    int seg[kP2PMaxWorld + 1];         // sent rows [seg[d], seg[d+1]) go to expert rank d
+    uint16_t* dst_x[kP2PMaxWorld];     // token rows of each expert rank's receive buffer
+    int32_t* dst_ids[kP2PMaxWorld];    // local ids of each expert rank's receive buffer
+    long long off[kP2PMaxWorld];       // first row of this rank's block at expert rank d
+    long long cap;                     // rows of every token receive buffer
+    uint32_t* sig[kP2PMaxWorld];       // dispatch flag array of each expert rank
+    int world, me;
+    uint32_t epoch;
+    uint32_t* counter;
+    uint32_t* flags;
+};
+
+// Home side of the dispatch: sent row i (token token_index[i], the local ids
+// of plan row i) is stored at row off[d] + i - seg[d] of expert rank d.
+// 256 threads copy one 4 KB token row (one 16-byte store each) and threads
+// 0..1 the 32 bytes of ids.  Completion is published as in the return.
+__global__ __launch_bounds__(256) void ep_dispatch_p2p_kernel(const DispatchArgs a) {
+    uint32_t f = 0;
+    for (int i = blockIdx.x; i < a.n; i += gridDim.x) {
+        int d = 0;
+#pragma unroll
+        for (int k = 1; k < kP2PMaxWorld; ++k)
+            if (k < a.world && i >= a.seg[k]) d = k;
+        const long long drow = a.off[d] + (i - a.seg[d]);
+        const long long t = a.token_index[i];
+        if (drow < 0 || drow >= a.cap || t < 0 || t >= a.T) {  // never true after the launcher's checks
+            f |= kFlagInvalidId;
+            continue;
+        }
+        const uint4* src = reinterpret_cast<const uint4*>(a.x + size_t(t) * kH);
+        uint4* dx = reinterpret_cast<uint4*>(a.dst_x[d] + size_t(drow) * kH);
+        dx[threadIdx.x] = __ldg(src + threadIdx.x);
+        if (threadIdx.x < 2) {
+            const uint4* si = reinterpret_cast<const uint4*>(a.local_ids + size_t(i) * kTop);
+            uint4* di = reinterpret_cast<uint4*>(a.dst_ids[d] + size_t(drow) * kTop);
+            di[threadIdx.x] = __ldg(si + threadIdx.x);
+        }
+    }
+    if (f && threadIdx.x == 0) atomicOr(a.flags, f);
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t done = atomicAdd(a.counter, 1u);
+        if (done == gridDim.x - 1) {
+            __threadfence_system();
+            for (int d = 0; d < a.world; ++d) {
+                if (d == a.me) continue;
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[d] + a.me), "r"(a.epoch) : "memory");
+            }
+            *a.counter = 0u;
         }
     }
 }
@@ -212,6 +274,56 @@ extern "C" cudaError_t ornith_moe_b200_ep_return_p2p(const void* workspace, size
     const int grid = n < 2 * sms ? (n > 0 ? n : 1) : 2 * sms;
     count_launches(1);
     ep_return_p2p_kernel<<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_dispatch_p2p(const void* x_bf16, int T, const void* token_index_i64,
+                                                       const void* local_ids_i32, int n, const int32_t* seg,
+                                                       void* const* dst_x, void* const* dst_ids,
+                                                       const int64_t* dst_offset, int64_t dst_capacity_rows,
+                                                       void* const* signals, int world, int me, uint32_t epoch,
+                                                       void* counter_u32, void* flags, cudaStream_t stream) {
+    if (T < 0 || T > kTcapMax || n < 0 || n > T * world || world < 1 || world > kP2PMaxWorld || me < 0 ||
+        me >= world || dst_capacity_rows < 0)
+        return cudaErrorInvalidValue;
+    if ((n && (!x_bf16 || !token_index_i64 || !local_ids_i32)) || !seg || !dst_x || !dst_ids || !dst_offset ||
+        !signals || !counter_u32 || !flags || !p2p_aligned(x_bf16, 16) || !p2p_aligned(token_index_i64, 8) ||
+        !p2p_aligned(local_ids_i32, 16) || !p2p_aligned(counter_u32, 4) || !p2p_aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    DispatchArgs a{};
+    if (seg[0] != 0 || seg[world] != n) return cudaErrorInvalidValue;
+    for (int d = 0; d < world; ++d) {
+        const int rows_d = seg[d + 1] - seg[d];
+        if (rows_d < 0 || dst_offset[d] < 0 || dst_offset[d] + rows_d > dst_capacity_rows) return cudaErrorInvalidValue;
+        if ((rows_d && (!dst_x[d] || !dst_ids[d])) || !p2p_aligned(dst_x[d], 16) || !p2p_aligned(dst_ids[d], 16))
+            return cudaErrorInvalidValue;
+        if (d != me && (!signals[d] || !p2p_aligned(signals[d], 4))) return cudaErrorInvalidValue;
+        a.seg[d] = seg[d];
+        a.dst_x[d] = static_cast<uint16_t*>(dst_x[d]);
+        a.dst_ids[d] = static_cast<int32_t*>(dst_ids[d]);
+        a.off[d] = dst_offset[d];
+        a.sig[d] = static_cast<uint32_t*>(signals[d]);
+    }
+    a.seg[world] = n;
+    a.x = static_cast<const uint16_t*>(x_bf16);
+    a.token_index = static_cast<const long long*>(token_index_i64);
+    a.local_ids = static_cast<const int32_t*>(local_ids_i32);
+    a.T = T;
+    a.n = n;
+    a.cap = dst_capacity_rows;
+    a.world = world;
+    a.me = me;
+    a.epoch = epoch;
+    a.counter = static_cast<uint32_t*>(counter_u32);
+    a.flags = static_cast<uint32_t*>(flags);
+    NvtxRange range("ornith.ep.dispatch_p2p");
+    int device = 0, sms = 0;
+    cudaError_t st = cudaGetDevice(&device);
+    if (st != cudaSuccess) return st;
+    if ((st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return st;
+    const int grid = n < 2 * sms ? (n > 0 ? n : 1) : 2 * sms;
+    count_launches(1);
+    ep_dispatch_p2p_kernel<<<grid, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

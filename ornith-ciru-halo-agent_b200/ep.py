@@ -212,18 +212,26 @@ def peer_offsets(matrix, me):
     return send, home, recv, back, offsets
 
 
+def dispatch_offsets(matrix, me):
+    """For the dispatch over peer memory: the first row of this rank's block
+    of token rows in every expert rank's receive buffer (after the rows that
+    expert rank d gets from lower ranks)."""
+    world = len(matrix)
+    return [sum(int(matrix[h][d][0]) for h in range(me)) for d in range(world)]
+
+
 def dispatch_with_matrix(group, world, me, ids, placement=None, planner=None):
     """dispatch_with_counts with an all_gather of every rank's counts instead
     of the all_to_all, so that this rank also learns where its returned rows
     go in each home rank's buffer; still one host synchronisation.  Returns
-    (plan, recv_counts, back_counts, offsets)."""
+    (plan, recv_counts, back_counts, return offsets, dispatch offsets)."""
     planner = planner or TorchPlanner(world, placement)
     state, counts = planner.start(ids)
     parts = [torch.empty_like(counts) for _ in range(world)]
     dist.all_gather(parts, counts.contiguous(), group=group)
     matrix = torch.stack(parts).tolist()                   # the single host synchronisation
     send, home, recv, back, offsets = peer_offsets(matrix, me)
-    return planner.finish(state, ids, send, home), recv, back, offsets
+    return planner.finish(state, ids, send, home), recv, back, offsets, dispatch_offsets(matrix, me)
 
 
 def _a2a(group, out, inp, out_splits, in_splits):
@@ -439,21 +447,33 @@ class _DeviceArray:
                                          'strides': None, 'version': 3}
 
 
-class PeerReturn:
-    """This rank's receive buffer for the return over NVLink peer memory,
-    shared with the other ranks of the node: fp32 rows [cap, 2048], then one
-    uint32 flag per rank.  Made collectively (every rank at once); close()
-    collectively before the process group goes away.  send() stores this
-    rank's computed rows into their home ranks' buffers and raises its flag
-    there (ornith_moe_b200_ep_return_p2p); wait() waits, bounded, for the
+class PeerExchange:
+    """This rank's receive buffers for the exchanges over NVLink peer memory,
+    shared with the other ranks of the node through CUDA IPC: token rows bf16
+    [cap_tokens, 2048] and their local ids int32 [cap_tokens, 8] (dispatch),
+    fp32 result rows [cap_rows, 2048] (return), then two flag arrays of one
+    uint32 per rank (return, dispatch).  Made collectively (every rank at
+    once); close() collectively before the process group goes away.
+
+    dispatch() stores this rank's sent token rows into the expert ranks'
+    buffers (ornith_moe_b200_ep_dispatch_p2p), ret() stores its computed rows
+    into the home ranks' buffers (ornith_moe_b200_ep_return_p2p); each raises
+    this rank's flag at the receivers, and wait_*() waits, bounded, for the
     other ranks' flags of the same call (ornith_moe_b200_ep_wait_signals)."""
 
-    def __init__(self, group, world, me, cap_rows, device):
+    def __init__(self, group, world, me, cap_tokens, cap_rows, device):
         from . import native
         if not 1 <= world <= 8:
-            raise ValueError('the peer-memory return serves 1..8 ranks of one node')
-        self.native, self.group, self.world, self.me, self.cap = native, group, world, me, int(cap_rows)
-        self.flag_offset = (self.cap * H * 4 + 255) // 256 * 256
+            raise ValueError('the peer-memory exchange serves 1..8 ranks of one node')
+        self.native, self.group, self.world, self.me = native, group, world, me
+        self.cap_tokens, self.cap_rows = int(cap_tokens), int(cap_rows)
+
+        def up(n):
+            return (n + 255) // 256 * 256
+        self.x_offset = 0
+        self.ids_offset = up(self.cap_tokens * H * 2)
+        self.rows_offset = self.ids_offset + up(self.cap_tokens * TOP * 4)
+        self.flag_offset = self.rows_offset + up(self.cap_rows * H * 4)
         self.base = native.ep_buffer_alloc(self.flag_offset + 256)
         self.peers = {}
         try:
@@ -466,21 +486,45 @@ class PeerReturn:
             self._release()
             raise
         bases = [self.base if r == me else self.peers[r] for r in range(world)]
-        self.dst = (C.c_void_p * world)(*bases)
-        self.signals = (C.c_void_p * world)(*[b + self.flag_offset for b in bases])
-        self.rows = torch.as_tensor(_DeviceArray(self.base, (self.cap, H), '<f4'), device=device)
-        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+
+        def table(offset):
+            return (C.c_void_p * world)(*[b + offset for b in bases])
+        self.dst_x, self.dst_ids, self.dst_rows = table(self.x_offset), table(self.ids_offset), table(self.rows_offset)
+        self.return_flags, self.dispatch_flags = table(self.flag_offset), table(self.flag_offset + 4 * world)
+        self.x = torch.as_tensor(_DeviceArray(self.base + self.x_offset, (self.cap_tokens, H), '<i2'),
+                                 device=device).view(torch.bfloat16)
+        self.ids = torch.as_tensor(_DeviceArray(self.base + self.ids_offset, (self.cap_tokens, TOP), '<i4'),
+                                   device=device)
+        self.rows = torch.as_tensor(_DeviceArray(self.base + self.rows_offset, (self.cap_rows, H), '<f4'),
+                                    device=device)
+        self.counters = torch.zeros(2, dtype=torch.int32, device=device)
         self.epoch = 0
 
-    def send(self, workspace, T, capacity, route_index, back_counts, offsets, flags):
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+    @staticmethod
+    def _segments(counts):
         seg = [0]
-        for c in back_counts:
+        for c in counts:
             seg.append(seg[-1] + int(c))
-        self.native.ep_return_p2p(workspace, T, capacity, route_index, seg, self.dst, offsets, self.cap,
-                                  self.signals, self.world, self.me, self.epoch, self.counter, flags)
+        return seg
 
-    def wait(self, flags):
+    def dispatch(self, x, plan, offsets, flags):
+        """Home side: the plan's sent rows into the expert ranks' token buffers."""
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        self.native.ep_dispatch_p2p(x, plan.token_index, plan.local_ids, self._segments(plan.send_counts),
+                                    self.dst_x, self.dst_ids, offsets, self.cap_tokens, self.dispatch_flags,
+                                    self.world, self.me, self.epoch, self.counters[0:1], flags)
+
+    def wait_dispatch(self, flags):
+        self.native.ep_wait_signals(self.base + self.flag_offset + 4 * self.world, self.world, self.me, self.epoch,
+                                    flags)
+
+    def ret(self, workspace, T, capacity, route_index, back_counts, offsets, flags):
+        """Expert side: the computed rows into the home ranks' result buffers."""
+        self.native.ep_return_p2p(workspace, T, capacity, route_index, self._segments(back_counts), self.dst_rows,
+                                  offsets, self.cap_rows, self.return_flags, self.world, self.me, self.epoch,
+                                  self.counters[1:2], flags)
+
+    def wait_return(self, flags):
         self.native.ep_wait_signals(self.base + self.flag_offset, self.world, self.me, self.epoch, flags)
 
     def _release(self):
@@ -497,7 +541,7 @@ class PeerReturn:
             return
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
-        self.rows = None
+        self.x = self.ids = self.rows = None
         for ptr in self.peers.values():
             self.native.ep_ipc_close(ptr)
         self.peers = {}
@@ -520,7 +564,7 @@ class ExpertParallelMoE:
     every rank; contiguous ranges by default."""
 
     def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact', placement=None,
-                 combine='exact', chunks=1, return_path='nccl'):
+                 combine='exact', chunks=1, transport='nccl'):
         from . import native
         if exchange not in ('compact', 'fixed'):
             raise ValueError(f'unknown exchange mode {exchange!r}')
@@ -530,9 +574,9 @@ class ExpertParallelMoE:
             raise ValueError('the rank-partial combine supports at most 8 ranks')
         if not isinstance(chunks, int) or chunks < 1 or (chunks > 1 and (exchange, combine) != ('compact', 'exact')):
             raise ValueError('chunks > 1 applies to the compact exchange with the exact combine')
-        if return_path not in ('nccl', 'p2p') or (return_path == 'p2p' and (
+        if transport not in ('nccl', 'p2p') or (transport == 'p2p' and (
                 (exchange, combine, chunks) != ('compact', 'exact', 1) or not 1 <= world <= 8)):
-            raise ValueError("return_path 'p2p' applies to the compact exchange with the exact combine, one chunk, "
+            raise ValueError("transport 'p2p' applies to the compact exchange with the exact combine, one chunk, "
                              "on 1..8 ranks of one node")
         self.chunks = chunks
         self.combine_mode = combine
@@ -544,9 +588,10 @@ class ExpertParallelMoE:
         self.placement = placement or contiguous_placement(world, banks[0].device)
         self.planner = NativePlanner(world, self.placement, banks[0].device)
         self.me = dist.get_rank(group)
-        # a home rank receives at most one row per (token, slot): 8 per local token
-        self.peer = PeerReturn(group, world, self.me, TOP * self.capacity, banks[0].device) \
-            if return_path == 'p2p' else None
+        # an expert rank receives at most `capacity` token rows; a home rank gets
+        # back at most one row per (token, slot), 8 per local token
+        self.peer = PeerExchange(group, world, self.me, self.capacity, TOP * self.capacity, banks[0].device) \
+            if transport == 'p2p' else None
         self.symbol = 'ornith_routed_direct_launch' if act_bits == 8 else 'ornith_routed_direct_launch_a4'
         dev = banks[0].device
         self.layout = native.get_layout(self.capacity)
@@ -596,16 +641,22 @@ class ExpertParallelMoE:
         return out
 
     def _layer_p2p(self, x, ids, weights):
-        """Compact exchange whose return goes straight into the home ranks'
-        receive buffers over NVLink (PeerReturn) instead of an all_to_all."""
-        plan, recv_counts, back_counts, offsets = dispatch_with_matrix(self.group, self.world, self.me, ids,
-                                                                        self.placement, self.planner)
-        x_recv, ids_recv = exchange_rows(self.group, self.world, plan, x, recv_counts)
-        n = self._layer(x_recv, ids_recv)
+        """Compact exchange over NVLink peer memory (PeerExchange): token rows
+        go straight into the expert ranks' buffers and results straight into
+        the home ranks' buffers; the count all_gather stays on NCCL."""
+        plan, recv_counts, back_counts, offsets, x_offsets = dispatch_with_matrix(
+            self.group, self.world, self.me, ids, self.placement, self.planner)
+        n = sum(recv_counts)
+        if n > self.capacity:
+            raise ValueError(f'expert-parallel receive of {n} rows exceeds capacity {self.capacity}')
+        self.peer.dispatch(x.contiguous(), plan, x_offsets, self.flags)
+        self.peer.wait_dispatch(self.flags)
+        x_recv, ids_recv = self.peer.x[:n], self.peer.ids[:n]
+        self._layer(x_recv, ids_recv)
         valid = (ids_recv >= 0).view(-1)
         sel = torch.nonzero_static(valid, size=sum(back_counts)).flatten().to(torch.int32)
-        self.peer.send(self.workspace, n, self.capacity, sel, back_counts, offsets, self.flags)
-        self.peer.wait(self.flags)
+        self.peer.ret(self.workspace, n, self.capacity, sel, back_counts, offsets, self.flags)
+        self.peer.wait_return(self.flags)
         got = self.peer.rows[:sum(plan.home_counts)]
         return self.combine(got, route_row_index(x.shape[0], plan, x.device), weights, ids)
 

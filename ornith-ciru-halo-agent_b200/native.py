@@ -94,6 +94,10 @@ SIGNATURES = {
                                        C.POINTER(C.c_int32), C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int64,
                                        C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p,
                                        C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_dispatch_p2p': ([C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_int32),
+                                         C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int64,
+                                         C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p,
+                                         C.c_void_p], C.c_int),
     'ornith_moe_b200_ep_wait_signals': ([C.c_void_p, C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
     'ornith_dense_g256_abi_version': ([], C.c_uint32),
@@ -454,6 +458,25 @@ def ep_return_p2p(workspace, T, capacity, route_index, seg, dst, offsets, cap_ro
     check(lib().ornith_moe_b200_ep_return_p2p(ptr(workspace), workspace.numel(), T, capacity, ptr(route_index), n,
                                               seg_a, dst, off_a, cap_rows, signals, world, me, epoch, ptr(counter),
                                               ptr(flags), stream(workspace)), 'expert-parallel peer return')
+
+
+def ep_dispatch_p2p(x, token_index, local_ids, seg, dst_x, dst_ids, offsets, cap_tokens, signals, world, me, epoch,
+                    counter, flags):
+    """Store the sent token rows (x[token_index[i]], local_ids[i]; rows
+    [seg[d], seg[d+1]) to expert rank d) into the expert ranks' receive
+    buffers (dst_x, dst_ids: ctypes arrays of world addresses) at rows
+    offsets[d]..., then raise `epoch` in their dispatch flag arrays."""
+    n = token_index.numel()
+    if (x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != 2048 or not x.is_contiguous()
+            or token_index.dtype != torch.int64 or not token_index.is_contiguous()
+            or local_ids.dtype != torch.int32 or local_ids.shape != (n, 8) or not local_ids.is_contiguous()
+            or len(seg) != world + 1 or len(offsets) != world):
+        raise ValueError('ep_dispatch_p2p takes bf16 rows [T, 2048], INT64 token indices and INT32 local ids [n, 8]')
+    seg_a = (C.c_int32 * (world + 1))(*seg)
+    off_a = (C.c_int64 * world)(*offsets)
+    check(lib().ornith_moe_b200_ep_dispatch_p2p(ptr(x), x.shape[0], ptr(token_index), ptr(local_ids), n, seg_a, dst_x,
+                                                dst_ids, off_a, cap_tokens, signals, world, me, epoch, ptr(counter),
+                                                ptr(flags), stream(x)), 'expert-parallel peer dispatch')
 
 
 def ep_wait_signals(signals_address, world, me, epoch, flags):

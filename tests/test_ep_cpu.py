@@ -128,11 +128,23 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
             out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered, placement)
         elif mode == 'peer':      # the return over peer memory, its stores emulated on the host
             me = dist.get_rank()
-            plan, recv_counts, back_counts, offsets = ep.dispatch_with_matrix(None, world, me, ids, placement)
+            plan, recv_counts, back_counts, offsets, x_offsets = ep.dispatch_with_matrix(None, world, me, ids,
+                                                                                        placement)
             plan2, recv2, back2 = ep.dispatch_with_counts(None, world, ids, placement)
             assert (recv_counts, back_counts) == (recv2, back2)
             assert (plan.send_counts, plan.home_counts) == (plan2.send_counts, plan2.home_counts)
             x_recv, ids_recv = ep.exchange_rows(None, world, plan, x, recv_counts)
+            # emulated dispatch stores: each home's sent rows at its offset in this rank's token buffer
+            sent = [None] * world
+            dist.all_gather_object(sent, (x[plan.token_index], plan.local_ids, plan.send_counts, x_offsets))
+            x_buf = torch.full((sum(recv_counts), H), float('nan')).to(torch.bfloat16)
+            ids_buf = torch.full((sum(recv_counts), TOP), -77, dtype=torch.int32)
+            for x_h, ids_h, send_h, off_h in sent:
+                lo, k = sum(send_h[:me]), send_h[me]
+                assert 0 <= off_h[me] and off_h[me] + k <= x_buf.shape[0]
+                x_buf[off_h[me]:off_h[me] + k] = x_h[lo:lo + k]
+                ids_buf[off_h[me]:off_h[me] + k] = ids_h[lo:lo + k]
+            assert torch.equal(x_buf.view(torch.int16), x_recv.view(torch.int16)) and torch.equal(ids_buf, ids_recv)
             rows = compute(x_recv, ids_recv, sum(back_counts))
             gathered = [None] * world
             dist.all_gather_object(gathered, (rows, back_counts, offsets))

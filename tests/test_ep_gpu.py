@@ -35,7 +35,7 @@ CASES = [  # (exchange, balanced placement, combine, further ExpertParallelMoE o
     ('compact', False, 'exact', {}), ('compact', True, 'exact', {}), ('fixed', False, 'exact', {}),
     ('fixed', True, 'exact', {}), ('compact', True, 'partial', {}), ('fixed', True, 'partial', {}),
     ('compact', True, 'exact', {'chunks': 3}),
-    ('compact', False, 'exact', {'return_path': 'p2p'}), ('compact', True, 'exact', {'return_path': 'p2p'}),
+    ('compact', False, 'exact', {'transport': 'p2p'}), ('compact', True, 'exact', {'transport': 'p2p'}),
 ]
 
 

@@ -213,3 +213,29 @@ def test_peer_return_validation_without_device_work(native):
     assert call(d=(C.c_void_p * world)(base + (5 << 28), None)) == INVALID
     assert call(d=(C.c_void_p * world)(base + (5 << 28) + 4, base + (6 << 28))) == INVALID   # 16-byte rows
     assert call(s=(C.c_void_p * world)(base + (7 << 28), None)) == INVALID                 # a peer's flags
+
+
+def test_peer_dispatch_validation_without_device_work(native):
+    fn = native.lib().ornith_moe_b200_ep_dispatch_p2p
+    base = 1 << 32
+    x, tok, lids, counter, flags = (C.c_void_p(base + (i << 28)) for i in range(5))
+    world = 2
+    dx = (C.c_void_p * world)(base + (5 << 28), base + (6 << 28))
+    di = (C.c_void_p * world)(base + (7 << 28), base + (8 << 28))
+    sigs = (C.c_void_p * world)(base + (9 << 28), base + (10 << 28))
+
+    def call(seg=(0, 3, 5), off=(0, 4), cap=8, n=5, T=4, me=1, X=x, ids=lids, d=dx, s=sigs):
+        seg_a = (C.c_int32 * len(seg))(*seg)
+        off_a = (C.c_int64 * len(off))(*off)
+        return fn(X, T, tok, ids, n, seg_a, d, di, off_a, cap, s, world, me, 1, counter, flags, None)
+
+    assert call(n=9, seg=(0, 4, 9)) == INVALID         # more rows than T * world
+    assert call(T=8193) == INVALID
+    assert call(me=2) == INVALID
+    assert call(seg=(0, 3, 4)) == INVALID
+    assert call(off=(6, 0)) == INVALID                 # 3 rows at 6..8 of an 8-row buffer
+    assert call(off=(0, 7)) == INVALID
+    assert call(X=C.c_void_p(base + 8)) == INVALID     # 16-byte token rows
+    assert call(ids=C.c_void_p(base + (2 << 28) + 4)) == INVALID
+    assert call(d=(C.c_void_p * world)(base + (5 << 28), None)) == INVALID
+    assert call(s=(C.c_void_p * world)(None, base + (10 << 28))) == INVALID   # rank 0's flags (this is rank 1)
