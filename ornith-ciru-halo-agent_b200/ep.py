@@ -220,16 +220,23 @@ def dispatch_offsets(matrix, me):
     return [sum(int(matrix[h][d][0]) for h in range(me)) for d in range(world)]
 
 
-def dispatch_with_matrix(group, world, me, ids, placement=None, planner=None):
+def dispatch_with_matrix(group, world, me, ids, placement=None, planner=None, capacity=None):
     """dispatch_with_counts with an all_gather of every rank's counts instead
     of the all_to_all, so that this rank also learns where its returned rows
     go in each home rank's buffer; still one host synchronisation.  Returns
-    (plan, recv_counts, back_counts, return offsets, dispatch offsets)."""
+    (plan, recv_counts, back_counts, return offsets, dispatch offsets).  With
+    `capacity`, every rank raises ValueError when any rank would receive more
+    token rows than that."""
     planner = planner or TorchPlanner(world, placement)
     state, counts = planner.start(ids)
     parts = [torch.empty_like(counts) for _ in range(world)]
     dist.all_gather(parts, counts.contiguous(), group=group)
     matrix = torch.stack(parts).tolist()                   # the single host synchronisation
+    if capacity is not None:
+        # every rank sees the same matrix, so all ranks refuse together
+        most = max(sum(int(matrix[h][d][0]) for h in range(world)) for d in range(world))
+        if most > capacity:
+            raise ValueError(f'expert-parallel receive of {most} rows on one rank exceeds capacity {capacity}')
     send, home, recv, back, offsets = peer_offsets(matrix, me)
     return planner.finish(state, ids, send, home), recv, back, offsets, dispatch_offsets(matrix, me)
 
@@ -645,10 +652,8 @@ class ExpertParallelMoE:
         go straight into the expert ranks' buffers and results straight into
         the home ranks' buffers; the count all_gather stays on NCCL."""
         plan, recv_counts, back_counts, offsets, x_offsets = dispatch_with_matrix(
-            self.group, self.world, self.me, ids, self.placement, self.planner)
+            self.group, self.world, self.me, ids, self.placement, self.planner, self.capacity)
         n = sum(recv_counts)
-        if n > self.capacity:
-            raise ValueError(f'expert-parallel receive of {n} rows exceeds capacity {self.capacity}')
         self.peer.dispatch(x.contiguous(), plan, x_offsets, self.flags)
         self.peer.wait_dispatch(self.flags)
         x_recv, ids_recv = self.peer.x[:n], self.peer.ids[:n]

@@ -128,6 +128,11 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
             out = ep.ep_layer(None, world, x, ids, weights, compute, fake_combine_gathered, placement)
         elif mode == 'peer':      # the return over peer memory, its stores emulated on the host
             me = dist.get_rank()
+            try:                  # too small a capacity: every rank refuses, after the same collective
+                ep.dispatch_with_matrix(None, world, me, ids, placement, capacity=1)
+                raise AssertionError('capacity 1 was accepted')
+            except ValueError:
+                pass
             plan, recv_counts, back_counts, offsets, x_offsets = ep.dispatch_with_matrix(None, world, me, ids,
                                                                                         placement)
             plan2, recv2, back2 = ep.dispatch_with_counts(None, world, ids, placement)
