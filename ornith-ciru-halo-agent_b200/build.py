@@ -11,6 +11,10 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / 'csrc'
 LIB = HERE / 'libornith_moe_b200.so'
+# the same library with the debug bounds checks (-DORNITH_DEBUG_BOUNDS=1): data-
+# dependent indices outside their buffers raise flag 128 instead of faulting
+DEBUG_LIB = HERE / 'libornith_moe_b200_debug.so'
+DEBUG_FLAGS = ('-DORNITH_DEBUG_BOUNDS=1',)
 SOURCES = ['moe_api.cu', 'moe_generic.cu', 'moe_decode.cu', 'moe_prefill.cu', 'moe_noalloc.cu', 'dense_g256.cu', 'head_i8.cu',
            'ep_plan.cu', 'ep_p2p.cu']
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
@@ -31,7 +35,8 @@ def build(force=False, verbose=False, flags=(), out=None):
     """Compile the library.  Extra nvcc flags (the kernels' build-time
     options: -DORNITH_PREFILL_F32X2=1, -DORNITH_DECODE_L2_PREFETCH=1,
     -DORNITH_DECODE_EARLY_PREFETCH=1, the trace builds) come from `flags` and
-    from ORNITH_MOE_B200_NVCC_FLAGS; the default build sets none of them.
+    from ORNITH_MOE_B200_NVCC_FLAGS; the default build sets none of them
+    (DEBUG_FLAGS make the debug-bounds library).
     `out` writes a variant library elsewhere (always rebuilt), which
     ORNITH_MOE_B200_LIB then selects at run time, so that a default and a
     variant build can be measured side by side."""

@@ -38,7 +38,44 @@ enum : uint32_t {
     kFlagNonfiniteMiddle = 16,
     kFlagNonfiniteOutput = 32,
     kFlagWaitTimeout = 64,  // a bounded device wait gave up; results are incomplete
+    kFlagDebugBounds = 128, // debug builds: a data-dependent index was out of range (access redirected)
 };
+
+// Debug builds (-DORNITH_DEBUG_BOUNDS=1) pass the data-dependent indices of
+// the hot kernels (plan positions, route and token numbers read back from
+// plans, expert slots that select a bank) through checked(): an index outside
+// [0, limit) raises flag 128 and is replaced by 0, so the access stays inside
+// its buffer and nothing traps.  It stands in for a device sanitizer, which
+// the shared GPUs do not offer.  In the default build checked() is the index.
+#ifndef ORNITH_DEBUG_BOUNDS
+#define ORNITH_DEBUG_BOUNDS 0
+#endif
+__device__ __forceinline__ int checked(int idx, int limit, uint32_t* flags) {
+#if ORNITH_DEBUG_BOUNDS
+    if (idx < 0 || idx >= limit) {
+        atomicOr(flags, uint32_t(kFlagDebugBounds));
+        return 0;
+    }
+#endif
+    (void)limit;
+    (void)flags;
+    return idx;
+}
+// The same for the rows [first, first + count) of a tile, which must lie in
+// [0, limit); an out-of-range tile is moved to row 0 (count <= limit on every
+// path that uses it).
+__device__ __forceinline__ int checked_range(int first, int count, int limit, uint32_t* flags) {
+#if ORNITH_DEBUG_BOUNDS
+    if (first < 0 || count < 0 || first + count > limit) {
+        atomicOr(flags, uint32_t(kFlagDebugBounds));
+        return 0;
+    }
+#endif
+    (void)count;
+    (void)limit;
+    (void)flags;
+    return first;
+}
 
 __device__ __forceinline__ uint16_t bf16_rne(float value) {
     uint32_t bits = __float_as_uint(value);

@@ -122,6 +122,13 @@ struct Smem {
     int* misc;        // [0] abort, [1] final issued count, [2] nact, [3] NA, [4] issued so far, [5] tasks posted,
                       // [6..9] this CTA's gate and down item ranges (throughput mode)
 };
+// Route number at plan position i; debug builds check the position and the
+// route against the plan's 9T rows (8T routes, then T shared-slot rows).
+__device__ __forceinline__ int route_at(const LayerArgs& a, const Smem& s, int i) {
+    const int rows = a.T * (kTop + 1);
+    return checked(s.routes[checked(i, rows, a.flags)], rows, a.flags);
+}
+
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 static_assert((2 * (kE + 4) + 2 * (kMaxSlots + 2)) * 4 + 8 * kRedundantX * 4 <= kNCW * 2 * kChunk * 32 * 4,
@@ -457,7 +464,7 @@ __device__ __forceinline__ void deferred_quant_tasks(const LayerArgs& a, Smem& s
     for (int t = 0; t < nt; ++t) {
         const int task = s.tasks[t], kk = task >> 1, hh = task & 1;
         const int nr2 = s.act_cnt[kk], roff2 = s.act_off[kk];
-        for (int q = cw; q < nr2; q += kNCW + kEW) quant_middle_group<QMAX>(a, s.routes[roff2 + q], hh, lane, f);
+        for (int q = cw; q < nr2; q += kNCW + kEW) quant_middle_group<QMAX>(a, route_at(a, s, roff2 + q), hh, lane, f);
         named_barrier(kBarDotE, kDotEThreads);
         if (cw == 0 && lane == 0) red_release_add(ctrl + kCtrlReady + kk, 1u);
     }
@@ -545,7 +552,7 @@ __device__ __forceinline__ void epilogue_warps(const LayerArgs& a, Smem& s, uint
                         value = silu_mul(gv, uv);
                     }
                     if (!isfinite(value)) f |= kFlagNonfiniteMiddle;
-                    middle[size_t(s.routes[roff + c * kTChunk + r]) * kI + p * 32 + lane] = value;
+                    middle[size_t(route_at(a, s, roff + c * kTChunk + r)) * kI + p * 32 + lane] = value;
                 }
             }
             named_barrier_arrive(kBarTermsFree + buf, kDotEThreads);
@@ -572,7 +579,7 @@ __device__ __forceinline__ void epilogue_warps(const LayerArgs& a, Smem& s, uint
         if (task >= 0 && !misc[0]) {
             const int kk = task >> 1, hh = task & 1;
             const int nr2 = s.act_cnt[kk], roff2 = s.act_off[kk];
-            for (int q = e; q < nr2; q += kEW) quant_middle_group<QMAX>(a, s.routes[roff2 + q], hh, lane, f);
+            for (int q = e; q < nr2; q += kEW) quant_middle_group<QMAX>(a, route_at(a, s, roff2 + q), hh, lane, f);
             named_barrier(kBarE, kEW * 32);
             if (e == 0 && lane == 0) red_release_add(ctrl + kCtrlReady + kk, 1u);
         }
@@ -897,7 +904,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                 const bool valid = id_valid(e);
                 const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : -2 - lane);
                 const int rank = __popc(peers & ((1u << lane) - 1u));
-                if (valid) s.routes[s.off[e] + s.cnt[e] + rank] = r;
+                if (valid) s.routes[checked(s.off[e] + s.cnt[e] + rank, R + T, a.flags)] = r;
                 __syncwarp();
                 if (valid && lane == 31 - __clz(peers)) s.cnt[e] += __popc(peers);
                 __syncwarp();
@@ -983,7 +990,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         // been run on a GPU).
         for (int d2 = lane; d2 < 2 * nd; d2 += 32) {
             const int dj = thr ? dj0 + d2 / 2 : jstart + (d2 / 2) * G;
-            const int e = s.act_e[dj / 64], tile = dj % 64, g = d2 % 2;
+            const int e = checked(s.act_e[dj / 64], kE + 1, a.flags), tile = dj % 64, g = d2 % 2;
             const int groups = kI / kG;
             const uint32_t* codes = e == kE ? a.sdown_codes : a.down_codes + size_t(e) * kH * (kI / 8);
             const uint32_t* meta = e == kE ? a.sdown_meta : a.down_meta + size_t(e) * kH * groups;
@@ -1048,7 +1055,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     g = (st - 16 * ng) % 2;
                     gate = false;
                 }
-                const int e = s.act_e[k];
+                const int e = checked(s.act_e[k], kE + 1, a.flags);
                 const uint32_t *codes, *meta;
                 if (gate) {
                     const int groups = kH / kG;
@@ -1167,7 +1174,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     int sm[kChunk];
 #pragma unroll
                     for (int i = 0; i < kChunk; ++i) {
-                        const int tok = token_of(s.routes[roff + c * kChunk + (i < n ? i : n - 1)], R);
+                        const int tok = checked(token_of(route_at(a, s, roff + c * kChunk + (i < n ? i : n - 1)), R), T, a.flags);
                         act[i] = reinterpret_cast<const uint4*>(s.xq + size_t(tok) * kH + warp * kG);
                         sa[i] = __half2float(s.xs[tok * 8 + warp]);
                         sm[i] = s.xsum[tok * 8 + warp];
@@ -1214,7 +1221,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                         value = silu_mul(gv, uv);
                     }
                     if (!isfinite(value)) f |= kFlagNonfiniteMiddle;
-                    middle[size_t(s.routes[roff + c * kChunk + warp]) * kI + p * 32 + lane] = value;
+                    middle[size_t(route_at(a, s, roff + c * kChunk + warp)) * kI + p * 32 + lane] = value;
                 }
                 if (c + 1 < nchunks) named_barrier(kBarConsumers, kNCW * 32);  // tbuf is rewritten next
             }
@@ -1248,7 +1255,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
             for (; tasks_done < posted; ++tasks_done) {
                 const int task = s.tasks[tasks_done], kk = task >> 1, hh = task & 1;
                 const int nr2 = s.act_cnt[kk], roff2 = s.act_off[kk];
-                for (int q = warp; q < nr2; q += kNCW) quant_middle_group<QMAX>(a, s.routes[roff2 + q], hh, lane, f);
+                for (int q = warp; q < nr2; q += kNCW) quant_middle_group<QMAX>(a, route_at(a, s, roff2 + q), hh, lane, f);
                 __syncwarp();
                 if (lane == 0) red_release_add(ctrl + kCtrlReady + kk, 1u);
                 if (lane == 0 && warp == 0) DECODE_TRACE(6);
@@ -1279,7 +1286,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                         int sm[kChunk];
 #pragma unroll
                         for (int i = 0; i < kChunk; ++i) {
-                            const int tok = token_of(s.routes[roff + c * kTChunk + (i < n ? i : n - 1)], R);
+                            const int tok = checked(token_of(route_at(a, s, roff + c * kTChunk + (i < n ? i : n - 1)), R), T, a.flags);
                             act[i] = reinterpret_cast<const uint4*>(s.xq + size_t(tok) * kH + warp * kG);
                             sa[i] = __half2float(s.xs[tok * 8 + warp]);
                             sm[i] = s.xsum[tok * 8 + warp];
@@ -1350,7 +1357,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                         float4 v[kSelfQuantMax][2];
 #pragma unroll
                         for (int i = 0; i < kSelfQuantMax; ++i)
-                            if (i < n) load_middle(a, s.routes[roff + i], g, lane, v[i][0], v[i][1]);
+                            if (i < n) load_middle(a, route_at(a, s, roff + i), g, lane, v[i][0], v[i][1]);
 #pragma unroll
                         for (int i = 0; i < kSelfQuantMax; ++i)
                             if (i < n)
@@ -1360,13 +1367,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     } else if (ok) {
                         for (int i = lane; i < n * 16; i += 32) {
                             const int ri = i / 16, part = i % 16;
-                            const int route = s.routes[roff + c * kChunk + ri];
+                            const int route = route_at(a, s, roff + c * kChunk + ri);
                             reinterpret_cast<uint4*>(dact + ri * kG)[part] = __ldcg(
                                 reinterpret_cast<const uint4*>(ws_at<uint8_t>(a, a.L.mq) + size_t(route) * kI + g * kG) +
                                 part);
                         }
                         if (lane < n) {
-                            const int route = s.routes[roff + c * kChunk + lane];
+                            const int route = route_at(a, s, roff + c * kChunk + lane);
                             dsc[lane] = __ldcg(ws_at<__half>(a, a.L.ms) + route * 2 + g);
                             dsm[lane] = __ldcg(ws_at<int32_t>(a, a.L.msum) + route * 2 + g);
                         }
@@ -1404,7 +1411,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                                 float v = __fadd_rn(__fadd_rn(0.f, term[i]), pb[i * 32 + lane]);
                                 if (shared) v = bf16_round_f32(v);
                                 if (!isfinite(v)) f |= kFlagNonfiniteProjection;
-                                route_out[size_t(s.routes[roff + c * kChunk + i]) * kH + tile * 32 + lane] = v;
+                                route_out[size_t(route_at(a, s, roff + c * kChunk + i)) * kH + tile * 32 + lane] = v;
                             }
                         }
                     }
@@ -1471,10 +1478,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                     for (int i = tid; i < nr * 32; i += kNCW * 32) {
                         const int ri = i / 32, part = i % 32;
                         reinterpret_cast<uint4*>(sact + ri * kI)[part] = __ldcg(
-                            reinterpret_cast<const uint4*>(ws_at<uint8_t>(a, a.L.mq) + size_t(s.routes[roff + ri]) * kI) + part);
+                            reinterpret_cast<const uint4*>(ws_at<uint8_t>(a, a.L.mq) + size_t(route_at(a, s, roff + ri)) * kI) + part);
                     }
                     for (int i = tid; i < nr * 2; i += kNCW * 32) {
-                        const int route = s.routes[roff + i / 2];
+                        const int route = route_at(a, s, roff + i / 2);
                         s.dscale[i] = __ldcg(ws_at<__half>(a, a.L.ms) + route * 2 + i % 2);
                         s.dsum[i] = __ldcg(ws_at<int32_t>(a, a.L.msum) + route * 2 + i % 2);
                     }
@@ -1511,7 +1518,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                                 __syncwarp();  // earlier reads of dact are done
                                 for (int i = lane; i < n * 16; i += 32) {
                                     const int ri = i / 16, part = i % 16;
-                                    const int route = s.routes[roff + c * kChunk + ri];
+                                    const int route = route_at(a, s, roff + c * kChunk + ri);
                                     reinterpret_cast<uint4*>(dact + ri * kG)[part] = __ldcg(
                                         reinterpret_cast<const uint4*>(ws_at<uint8_t>(a, a.L.mq) + size_t(route) * kI + g * kG) +
                                         part);
@@ -1520,7 +1527,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
 #pragma unroll
                                 for (int i = 0; i < kChunk; ++i) {
                                     const int ri = i < n ? i : n - 1;
-                                    const int route = s.routes[roff + c * kChunk + ri];
+                                    const int route = route_at(a, s, roff + c * kChunk + ri);
                                     act[i] = reinterpret_cast<const uint4*>(dact + ri * kG);
                                     sa[i] = __half2float(__ldcg(ws_at<__half>(a, a.L.ms) + route * 2 + g));
                                     sm[i] = __ldcg(ws_at<int32_t>(a, a.L.msum) + route * 2 + g);
@@ -1538,7 +1545,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
                                         float v = __fadd_rn(__fadd_rn(0.f, term0[i]), group_term(sa[i], dot[i], sm[i], mw1));
                                         if (shared) v = bf16_round_f32(v);
                                         if (!isfinite(v)) f |= kFlagNonfiniteProjection;
-                                        route_out[size_t(s.routes[roff + c * kChunk + i]) * kH + tile * 32 + lane] = v;
+                                        route_out[size_t(route_at(a, s, roff + c * kChunk + i)) * kH + tile * 32 + lane] = v;
                                     }
                                 }
                             }

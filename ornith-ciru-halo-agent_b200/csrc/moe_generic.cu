@@ -105,7 +105,7 @@ __global__ __launch_bounds__(1024) void plan_kernel(LayerArgs a) {
         int e = a.ids[r];
         if (id_valid(e)) {
             int slot = atomicAdd(reinterpret_cast<int*>(&counts[e]), -1) - 1;  // descending fill
-            g_routes[offsets[e] + slot] = r;
+            g_routes[checked(offsets[e] + slot, R + a.T, a.flags)] = r;
         }
     }
     if (a.shared)
@@ -177,8 +177,8 @@ __global__ __launch_bounds__(256) void gate_kernel(LayerArgs a) {
     float* middle = ws_at<float>(a, a.L.middle);
     uint32_t f = 0;
     for (int i = warp; i < nr; i += nwarps) {
-        const int route = routes[i];
-        const int token = route >= R ? route - R : route / kTop;
+        const int route = checked(routes[i], R + a.T, a.flags);
+        const int token = checked(route >= R ? route - R : route / kTop, a.T, a.flags);
         float acc[2] = {0.f, 0.f};
         for (int g = 0; g < groups; ++g) {
             const uint2* act = xq + (size_t(token) * kH + g * kG) / 8;
@@ -256,7 +256,7 @@ __global__ __launch_bounds__(256) void down_kernel(LayerArgs a) {
     float* route_out = ws_at<float>(a, a.L.route_out);
     uint32_t f = 0;
     for (int i = warp; i < nr; i += nwarps) {
-        const int route = routes[i];
+        const int route = checked(routes[i], a.T * (kTop + 1), a.flags);
         float acc = 0.f;
         for (int g = 0; g < groups; ++g) {
             const uint2* act = mq + (size_t(route) * kI + g * kG) / 8;
@@ -285,7 +285,8 @@ __global__ __launch_bounds__(256) void combine_kernel(LayerArgs a) {
     const float* route_out = ws_at<float>(a, a.L.route_out);
     const int32_t* rowpos = BY_POSITION ? ws_at<int32_t>(a, a.L.rowpos) : nullptr;
     auto row_ptr = [&](int r) {
-        return reinterpret_cast<const float4*>(route_out + size_t(BY_POSITION ? rowpos[r] : r) * kH + c);
+        const int row = BY_POSITION ? checked(rowpos[r], a.T * (kTop + 1), a.flags) : r;
+        return reinterpret_cast<const float4*>(route_out + size_t(row) * kH + c);
     };
     uint32_t f = 0;
     float sum[8];

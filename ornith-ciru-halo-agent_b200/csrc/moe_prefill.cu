@@ -329,6 +329,7 @@ struct MmaArgs {
     float* out;              // gate: middle [positions][512]; down: route_out [positions][2048]
     const float* silu_table;
     uint32_t* flags;
+    int rows;                // positions of the plan (8T routes + T shared rows), for debug checks
 };
 
 template <int KG, bool GATE>
@@ -383,9 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
 
     auto unit_bank = [&](int unit, const uint32_t*& codes, const uint32_t*& meta) {
         const int4 mt = p.mtiles[unit / NUPT];
-        const bool shared = mt.x == kE;
-        codes = shared ? p.scodes : p.codes + size_t(mt.x) * BANK_CODES;
-        meta = shared ? p.smeta : p.meta + size_t(mt.x) * BANK_META;
+        const int e = checked(mt.x, kE + 1, p.flags);  // the slot's expert selects the bank
+        const bool shared = e == kE;
+        codes = shared ? p.scodes : p.codes + size_t(e) * BANK_CODES;
+        meta = shared ? p.smeta : p.meta + size_t(e) * BANK_META;
     };
     // 32-column bank tile feeding B-tile rows 32i..32i+31 of N-tile nt
     auto n32_of = [&](int nt, int i) { return GATE ? (i < 4 ? 4 * nt + i : 16 + 4 * nt + (i - 4)) : 8 * nt + i; };
@@ -692,7 +694,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 if (ew == 0 && lane == 0) PREFILL_TRACE(9, 3 + 4 * un);
                 transpose8(c, lane);
                 if (ew == 0 && lane == 0) PREFILL_TRACE(9, 4 + 4 * un);
-                float* dst = p.out + size_t(mt.y + rbase) * kI + kMT * nt + 32 * wg + 4 * jc;
+                float* dst = p.out + size_t(checked_range(mt.y, mt.z, p.rows, p.flags) + rbase) * kI + kMT * nt +
+                             32 * wg + 4 * jc;
 #pragma unroll
                 for (int m = 0; m < 8; ++m)
                     if (rbase + m < mt.z) *reinterpret_cast<float4*>(dst + size_t(m) * kI) = c[m];
@@ -712,7 +715,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                     if (ew == 0 && lane == 0 && h == 0) PREFILL_TRACE(9, 3 + 4 * un);
                     transpose8(c, lane);
                     if (ew == 0 && lane == 0 && h == 0) PREFILL_TRACE(9, 4 + 4 * un);
-                    float* dst = p.out + size_t(mt.y + rbase) * kH + kNT * nt + 64 * wg + 32 * h + 4 * jc;
+                    float* dst = p.out + size_t(checked_range(mt.y, mt.z, p.rows, p.flags) + rbase) * kH + kNT * nt +
+                                 64 * wg + 32 * h + 4 * jc;
 #pragma unroll
                     for (int m = 0; m < 8; ++m)
                         if (rbase + m < mt.z) *reinterpret_cast<float4*>(dst + size_t(m) * kH) = c[m];
@@ -861,7 +865,7 @@ __global__ __launch_bounds__(256) void prefill_place_kernel(LayerArgs a, int nbl
     for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
         const int e = a.ids[r];
         if (id_valid(e)) {
-            const int pos = atomicAdd(&base[e], 1);
+            const int pos = checked(atomicAdd(&base[e], 1), R + a.T, a.flags);
             routes[pos] = r;
             rowpos[r] = pos;
         }
@@ -902,7 +906,7 @@ __global__ __launch_bounds__(256) void pack_gather_kernel(LayerArgs a) {
     if (tile >= *ws_at<int32_t>(a, a.L.n_mtiles)) return;
     const int4 mt = ws_at<int4>(a, a.L.mtiles)[tile];
     const int R = a.T * kTop;
-    const int32_t* routes = ws_at<int32_t>(a, a.L.routes) + mt.y;
+    const int32_t* routes = ws_at<int32_t>(a, a.L.routes) + checked_range(mt.y, mt.z, a.T * (kTop + 1), a.flags);
     const uint8_t* xq = ws_at<uint8_t>(a, a.L.xq) + g * kG;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -911,7 +915,7 @@ __global__ __launch_bounds__(256) void pack_gather_kernel(LayerArgs a) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (row < mt.z) {
             const int route = routes[row];
-            const int t = route >= R ? route - R : route / kTop;
+            const int t = checked(route >= R ? route - R : route / kTop, a.T, a.flags);
             v = __ldcg(reinterpret_cast<const uint4*>(xq + size_t(t) * kH) + chunk);
         }
         *reinterpret_cast<uint4*>(img + tile_slot(chunk, row)) = v;
@@ -922,7 +926,7 @@ __global__ __launch_bounds__(256) void pack_gather_kernel(LayerArgs a) {
         int32_t sum = 0;
         if (row < mt.z) {
             const int route = routes[row];
-            const int t = route >= R ? route - R : route / kTop;
+            const int t = checked(route >= R ? route - R : route / kTop, a.T, a.flags);
             sa = __half2float(ws_at<__half>(a, a.L.xs)[t * (kH / kG) + g]);
             sum = ws_at<int32_t>(a, a.L.xsum)[t * (kH / kG) + g];
         }
@@ -953,7 +957,9 @@ __global__ __launch_bounds__(256) void pack_middle_kernel(LayerArgs a) {
     uint32_t f = 0;
     if (row < mt.z) {
         const float4* src =
-            reinterpret_cast<const float4*>(ws_at<float>(a, a.L.middle) + size_t(mt.y + row) * kI + g * kG + lane * 8);
+            reinterpret_cast<const float4*>(ws_at<float>(a, a.L.middle) +
+                                            size_t(checked(mt.y + row, a.T * (kTop + 1), a.flags)) * kI + g * kG +
+                                            lane * 8);
         const float4 v0 = __ldcs(src), v1 = __ldcs(src + 1);
         float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
@@ -1059,6 +1065,7 @@ cudaError_t launch_prefill(const LayerArgs& a, cudaStream_t stream) {
     g.out = ws_at<float>(a, a.L.middle);
     g.silu_table = a.silu_table;
     g.flags = a.flags;
+    g.rows = T * (kTop + 1);
     {
         NvtxRange r("ornith.prefill.gate_up");
         gate<<<min(ds.sms, max_tiles * 4), kThreads, kMmaSmem, stream>>>(g);

@@ -114,20 +114,27 @@ SIGNATURES = {
 }
 
 
+def load(path):
+    """A ctypes handle of a build of the library at `path`, with the
+    signatures of every exported entry point set."""
+    path = Path(path)
+    if not path.exists():
+        raise RuntimeError(f'{path} is missing: build it with `python {HERE / "build.py"}` '
+                           '(or __graft_entry__.build()); the MoE operators have no CPU fallback')
+    handle = C.CDLL(str(path))
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.argtypes, fn.restype = args, res
+    if handle.ornith_routed_storage_n32() != 32:
+        raise RuntimeError(f'{path} does not report N32 expert storage (marker 32)')
+    return handle
+
+
 def lib():
     """Load the CUDA library (raises if it was not built: there is no fallback)."""
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
-            raise RuntimeError(f'{LIB_PATH} is missing: build it with `python {HERE / "build.py"}` '
-                               '(or __graft_entry__.build()); the MoE operators have no CPU fallback')
-        handle = C.CDLL(str(LIB_PATH))
-        for name, (args, res) in SIGNATURES.items():
-            fn = getattr(handle, name)
-            fn.argtypes, fn.restype = args, res
-        if handle.ornith_routed_storage_n32() != 32:
-            raise RuntimeError(f'{LIB_PATH} does not report N32 expert storage (marker 32)')
-        _lib = handle
+        _lib = load(LIB_PATH)
     return _lib
 
 

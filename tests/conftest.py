@@ -18,17 +18,22 @@ def pytest_configure(config):
     config.addinivalue_line('markers', 'gpu: needs a CUDA device (B200)')
 
 
+# GPU files in run order: the routed parity suite first, then the other
+# single-GPU files that have passed on a B200, then files not yet run on one,
+# the expert-parallel ones (two GPUs) and the allocation-free entry last, so
+# that a run stopped at its first failure has always checked what came before.
+GPU_ORDER = ['test_parity_gpu.py', 'test_dense_gpu.py', 'test_head_gpu.py', 'test_shared_dense_gpu.py',
+             'test_weights_gpu.py', 'test_debug_bounds_gpu.py', 'test_ep_plan_gpu.py', 'test_ep_gpu.py',
+             'test_zz_no_alloc.py']
+
+
 def pytest_collection_modifyitems(config, items):
-    """Order: the routed parity suite, the other single-GPU files, the
-    expert-parallel files, and the allocation-free entry last, so that a run
-    stopped at its first failure has always checked the single-GPU paths."""
     def rank(item):
         name = item.path.name
-        if name == 'test_parity_gpu.py':
-            return 0
-        if name == 'test_zz_no_alloc.py':
-            return 3
-        return 2 if name.startswith('test_ep_') and name.endswith('_gpu.py') else 1
+        if name in GPU_ORDER:
+            return GPU_ORDER.index(name)
+        # an unlisted GPU file runs just before the allocation-free entry; CPU files keep their place
+        return len(GPU_ORDER) - 1.5 if name.endswith('_gpu.py') else -1
     items.sort(key=rank)   # stable: file order otherwise
 
 

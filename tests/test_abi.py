@@ -189,3 +189,15 @@ def test_routed_reference_status_codes_match_ours(native, O):
         ptrs = [None] * 15 if T == 0 else [fake] * 15
         want = f_ref(*ptrs, big, fake, fake, fake, T, tcap, None)
         assert f_ours(*ptrs, big, fake, fake, fake, T, tcap, None) == want, (T, tcap)
+
+
+def test_debug_bounds_library_exports_every_declared_symbol(native):
+    """The debug-bounds build (-DORNITH_DEBUG_BOUNDS=1) is a drop-in copy of the
+    library: same symbols, same signatures, loadable through native.load."""
+    path = native.HERE / 'libornith_moe_b200_debug.so'
+    if not path.exists():
+        pytest.skip(f'{path} not built (__graft_entry__.build() makes it)')
+    dbg = native.load(path)
+    for n in declared_symbols():
+        assert hasattr(dbg, n), n
+    assert dbg.ornith_moe_b200_abi_version() == native.lib().ornith_moe_b200_abi_version()
