@@ -19,7 +19,8 @@
  * Contract (routed_storage_n32_consumer.cpp:319-351 and the dense contract
  * kernels/dense_n32/dense_g256_api.h:32-44):
  *   - every launch is enqueued on `stream`; no allocation, no synchronisation,
- *     no host reads of device data;
+ *     no host reads of device data (the expert-parallel buffer and IPC calls
+ *     at the end are set-up functions outside this rule);
  *   - the caller owns every buffer; the workspace (size from get_layout) is not
  *     re-entrant: calls that share it must be ordered on one stream;
  *   - T == 0 returns success without touching any pointer; bad Tcap/T/bytes,
@@ -29,7 +30,8 @@
  *     (never cleared by the library): 1 non-finite input/transform,
  *     2 invalid activation quantisation, 4 expert id outside [-1, 256),
  *     8 non-finite projection, 16 non-finite SiLU*up, 32 non-finite or
- *     overflowing output, 64 a bounded device wait gave up (results incomplete);
+ *     overflowing output, 64 a bounded device wait gave up (results incomplete),
+ *     128 (debug-bounds builds only) an index outside its buffer was redirected;
  *   - ids of -1 are padding and skip their slot.
  * Alignment: workspace 256 B; input, output, codes and metadata 16 B;
  * route weights, ids and flags 4 B.

@@ -6,7 +6,8 @@ on one stream), each layer owns one uint32 flag slot that the library ORs
 into, flags are reset only outside CUDA-graph capture, and a check raises on
 any non-zero slot.  Bit 4 (invalid expert id) is fatal; bits 1/2/8/16/32 are
 numerical (worker.py:189-197, mask 59); bit 64 means a bounded device wait
-gave up.
+gave up, and bit 128 (debug-bounds builds only) that an index outside its
+buffer was redirected.
 """
 import torch
 
