@@ -568,7 +568,13 @@ class ExpertParallelMoE:
     synchronisation; every rank must call with the same token count).
     combine: 'exact' (per-slot rows, bit-identical to one GPU) or 'partial'
     (per-rank partial sums, fp32-rounding agreement).  placement: the same on
-    every rank; contiguous ranges by default."""
+    every rank; contiguous ranges by default.  chunks: compact exchange in
+    that many pipelined token ranges (exact combine).  transport: 'nccl'
+    (all_to_all) or 'p2p' (token rows and results stored straight into the
+    receiving ranks' buffers over NVLink peer memory; compact exchange, exact
+    combine, one chunk).  The dispatch plan of the compact exchange comes from
+    one device launch (NativePlanner).  close() releases the peer buffers,
+    collectively, before the process group is destroyed."""
 
     def __init__(self, group, world, banks, capacity, act_bits=8, exchange='compact', placement=None,
                  combine='exact', chunks=1, transport='nccl'):
