@@ -58,7 +58,13 @@ constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarps = 16;
 constexpr int kEpiFirst = 8;    // epilogue warps 8..23 (warpgroups 2..5)
-constexpr int kConvWarps = 4;   // converter warps 2..5, one per scheduler
+// Converter warps 2..5, one per scheduler; built with -DORNITH_PREFILL_CONV6=1
+// (not the default build yet: it has not been run on a GPU) warps 2..7, the
+// two otherwise idle warps of the second setup warpgroup included.
+#ifndef ORNITH_PREFILL_CONV6
+#define ORNITH_PREFILL_CONV6 0
+#endif
+constexpr int kConvWarps = ORNITH_PREFILL_CONV6 ? 6 : 4;
 // Register split (setmaxnreg, per warpgroup): the two setup warpgroups drop to
 // kRegsSetup, the four epilogue warpgroups rise to kRegsEpi.  The sum must not
 // exceed what the CTA was launched with (kThreads x kRegsLaunch), which the
@@ -479,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
             }
         } else if (warp < 2 + kConvWarps) {
             // ---------------- converters ----------------
-            const int cw = warp - 2;  // converter warp 0..3
+            const int cw = warp - 2;  // converter warp 0..kConvWarps-1
             int st = 0;
             for (int unit = blockIdx.x; unit < n_units && !*abort; unit += gridDim.x) {
                 for (int g = 0; g < KG && !*abort; ++g) {
@@ -487,6 +493,23 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         const int s = st % kStages;
                         if (!bwait(&full[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
                         if (warp == 2 && lane == 0) PREFILL_TRACE(2, st);
+#if ORNITH_PREFILL_CONV6
+                        // The same 64 (tile i, pair q) items per lane as below, dealt
+                        // over six warps: item p = cw + 6m is tile p / 8, pair p % 8.
+                        {
+                            const uint32_t* bp0 =
+                                reinterpret_cast<const uint32_t*>(stages + size_t(s) * kStageBytes + kABytes) + lane;
+                            uint8_t* bu0 = stages + size_t(s) * kStageBytes + kABytes + kBpBytes + (lane >> 3) * 128 +
+                                           (lane & 7) * 16;
+                            for (int it = cw; it < 64; it += kConvWarps) {
+                                const int i = it >> 3, q = it & 7;
+                                const uint32_t w0 = bp0[i * 512 + (2 * q) * 32], w1 = bp0[i * 512 + (2 * q + 1) * 32];
+                                *reinterpret_cast<uint4*>(bu0 + q * 4096 + i * 512) =
+                                    make_uint4(w0 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu,
+                                               (w1 >> 4) & 0x0f0f0f0fu);
+                            }
+                        }
+#else
                         // Work item (i, q, c): 32-column tile i (8), word pair q (8),
                         // column c = lane; converter warp cw takes the pairs
                         // q = cw + 4*qq.  Packed word j of column c of tile i is
@@ -512,6 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                                     make_uint4(w[2 * qq] & 0x0f0f0f0fu, (w[2 * qq] >> 4) & 0x0f0f0f0fu,
                                                w[2 * qq + 1] & 0x0f0f0f0fu, (w[2 * qq + 1] >> 4) & 0x0f0f0f0fu);
                         }
+#endif
                         fence_proxy_async();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&conv[s]);
