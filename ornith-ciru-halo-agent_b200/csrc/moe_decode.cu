@@ -423,8 +423,18 @@ __device__ __forceinline__ void quant_middle_group(const LayerArgs& a, int route
 // groups and long runs of one slot's down tiles.  Relative cost of an item of
 // a slot with nr routes: a gate item streams 66 KB and runs 2 x 16 x 8 dp4a
 // per route and lane, a down item streams 8 KB with a fixed per-tile overhead.
-__host__ __device__ inline int gate_cost(int nr) { return 3 + nr; }
-__host__ __device__ inline int down_cost(int nr) { return 4 + nr; }
+// The fixed parts are build-time settings (-DORNITH_DECODE_GATE_COST=…,
+// -DORNITH_DECODE_DOWN_COST=…) so that variant builds can measure other
+// balances between weight bytes and per-route work; the default is 3 and 4.
+#ifndef ORNITH_DECODE_GATE_COST
+#define ORNITH_DECODE_GATE_COST 3
+#endif
+#ifndef ORNITH_DECODE_DOWN_COST
+#define ORNITH_DECODE_DOWN_COST 4
+#endif
+static_assert(ORNITH_DECODE_GATE_COST >= 1 && ORNITH_DECODE_DOWN_COST >= 1, "item costs are positive");
+__host__ __device__ inline int gate_cost(int nr) { return ORNITH_DECODE_GATE_COST + nr; }
+__host__ __device__ inline int down_cost(int nr) { return ORNITH_DECODE_DOWN_COST + nr; }
 // First item (slot-major index, per_slot items per slot) whose cost prefix is
 // at least `target`; W[k] = cost of all items of slots < k, W[NA] = total.
 __device__ __forceinline__ int first_item(const int* W, int NA, int per_slot, int target) {
