@@ -99,8 +99,8 @@ def parse():
     p.add_argument('--combine', choices=['exact', 'partial'], default='exact',
                    help='expert-parallel return: per-slot rows (bit-exact) or per-rank fp32 partial sums')
     p.add_argument('--ep-transport', choices=['nccl', 'p2p'], default='nccl',
-                   help='compact expert-parallel token dispatch and return: NCCL all_to_all, or stores into the '
-                        'receiving ranks\' buffers over NVLink peer memory (exact combine, one chunk)')
+                   help='expert-parallel token dispatch and return: NCCL, or stores into the receiving ranks\' '
+                        'buffers over NVLink peer memory (exact combine, one chunk)')
     p.add_argument('--ep-chunks', type=int, default=1,
                    help='compact expert-parallel exchange in this many pipelined token chunks (exact combine)')
     p.add_argument('--layers', type=int, default=None,
@@ -235,7 +235,7 @@ def run_ep(args):
                                            act_bits=bits, exchange=cfg['exchange'], placement=placement,
                                            combine=args.combine,
                                            chunks=args.ep_chunks if cfg['exchange'] == 'compact' else 1,
-                                           transport=args.ep_transport if cfg['exchange'] == 'compact' else 'nccl'))
+                                           transport=args.ep_transport))
     logits = torch.randn((L, T, 256), device=dev, generator=gen) + bias
     x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
     w = torch.empty((L, T, 8), dtype=torch.float32, device=dev)
@@ -298,8 +298,7 @@ def run_ep(args):
                                 '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
                                 'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)'),
                    'chunks': args.ep_chunks if cfg['exchange'] == 'compact' else 1,
-                   'transport': (('NVLink peer stores' if args.ep_transport == 'p2p' else 'NCCL all_to_all')
-                                 if cfg['exchange'] == 'compact' else 'NCCL')},
+                   'transport': 'NVLink peer stores' if args.ep_transport == 'p2p' else 'NCCL'},
         'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': graph is not None,
     }
     dist.barrier()

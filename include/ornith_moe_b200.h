@@ -248,6 +248,28 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_dispatch_p2p(
     void* const* dst_x, void* const* dst_ids, const int64_t* dst_offset, int64_t dst_capacity_rows,
     void* const* signals, int world, int me, uint32_t epoch, void* counter_u32, void* flags_u32,
     cudaStream_t stream);
+/* The fixed-size exchange over peer memory (every rank T tokens; no host
+ * value changes between calls, so a step can be captured in a CUDA graph).
+ * Receive buffers come in two sets, used by calls of odd and even number; the
+ * call number is a uint32 in device memory (epoch_u32, zero at first).
+ * ep_fixed_dispatch: row me*T + t of every rank d's token buffer (dst_x, host
+ * array [2][world]) receives x[t] (bf16 [T][2048]) and its ids buffer
+ * (dst_ids) local_ids[d][t] (int32 [world][T][8]); then the call number goes
+ * into slot `me` of the others' dispatch flags and into *epoch_u32.
+ * ep_fixed_return: after the layer call on the world*T received rows (ids
+ * int32 [world*T][8], capacity Tcap), each slot with a valid local id of row
+ * h*T + t goes to row t*8 + s of home h's result buffer (dst_rows, [2][world]),
+ * then the call number into the others' return flags.  ep_wait_epoch: waits,
+ * bounded (flag 64), until every other rank's flag reaches *epoch_u32. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_fixed_dispatch(
+    const void* x_bf16, const void* local_ids_i32, int T, void* const* dst_x, void* const* dst_ids,
+    void* const* signals, int world, int me, void* epoch_u32, void* counter_u32, cudaStream_t stream);
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_fixed_return(
+    const void* workspace, size_t bytes, int T, int Tcap, const void* ids_i32, void* const* dst_rows,
+    void* const* signals, int world, int me, const void* epoch_u32, void* counter_u32, void* flags_u32,
+    cudaStream_t stream);
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_wait_epoch(
+    const void* signals_u32, int world, int me, const void* epoch_u32, void* flags_u32, cudaStream_t stream);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_wait_signals(
     const void* signals_u32, int world, int me, uint32_t epoch, void* flags_u32, cudaStream_t stream);
 

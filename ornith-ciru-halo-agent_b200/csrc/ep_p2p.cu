@@ -163,6 +163,117 @@ __global__ __launch_bounds__(256) void ep_dispatch_p2p_kernel(const DispatchArgs
     }
 }
 
+// ---- fixed-size exchange (every rank the same T tokens; graph-capturable) ----
+// Each rank's receive buffers come in two sets, chosen by the parity of the
+// call; the call number lives in device memory (`epoch`: the dispatch kernel
+// of call k reads k - 1 and its last CTA stores k), so no host value changes
+// between calls.  A rank writes into a peer's set k % 2 only after it has
+// seen the peer's dispatch flags of call k - 1, i.e. after the peer finished
+// every kernel of call k - 2, the last reader of that set.
+struct FixedArgs {
+    const uint16_t* x;                 // this rank's token rows [T][2048]
+    const int32_t* local_ids;          // [world][T][8]: ids of this rank's tokens in rank d's numbering
+    int T, world, me;
+    uint16_t* dst_x[2][kP2PMaxWorld];  // per set: token rows [world][T][2048] of rank d
+    int32_t* dst_ids[2][kP2PMaxWorld]; // per set: ids [world][T][8] of rank d
+    uint32_t* sig[kP2PMaxWorld];       // dispatch flag array of each rank
+    uint32_t* epoch;                   // this rank's call counter
+    uint32_t* counter;
+};
+
+// Dispatch: block `me` of every rank's token buffer receives this rank's T
+// rows, and its ids buffer the ids in that rank's numbering.  Item i is
+// (rank d = i / T, token t = i % T).
+__global__ __launch_bounds__(256) void ep_fixed_dispatch_kernel(const FixedArgs a) {
+    const uint32_t call = *a.epoch + 1u;   // stored by the last CTA only, after every CTA read it
+    const int set = int(call & 1u);
+    for (int i = blockIdx.x; i < a.T * a.world; i += gridDim.x) {
+        const int d = i / a.T, t = i % a.T;
+        const size_t row = size_t(a.me) * a.T + t;
+        reinterpret_cast<uint4*>(a.dst_x[set][d] + row * kH)[threadIdx.x] =
+            __ldg(reinterpret_cast<const uint4*>(a.x + size_t(t) * kH) + threadIdx.x);
+        if (threadIdx.x < 2)
+            reinterpret_cast<uint4*>(a.dst_ids[set][d] + row * kTop)[threadIdx.x] =
+                __ldg(reinterpret_cast<const uint4*>(a.local_ids + (size_t(d) * a.T + t) * kTop) + threadIdx.x);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
+        __threadfence_system();
+        for (int d = 0; d < a.world; ++d)
+            if (d != a.me)
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[d] + a.me), "r"(call) : "memory");
+        *a.counter = 0u;
+        *a.epoch = call;
+    }
+}
+
+struct FixedReturnArgs {
+    const float* route_out;
+    const int32_t* rowpos;             // route -> row of route_out on the tensor-core path, else null
+    const int32_t* ids;                // [world * T][8] the local ids the layer call used
+    int T, world, me;
+    float* dst_rows[2][kP2PMaxWorld];  // per set: result rows [T * 8][2048] of home rank h
+    uint32_t* sig[kP2PMaxWorld];       // return flag array of each rank
+    const uint32_t* epoch;
+    uint32_t* counter;
+    uint32_t* flags;
+};
+
+// Return: received row r = h * T + t computed the slots s whose local id is
+// valid here; each goes to row t * 8 + s of home h's result buffer (every
+// slot has one owner, so the rows of different ranks never collide).
+__global__ __launch_bounds__(256) void ep_fixed_return_kernel(const FixedReturnArgs a) {
+    const uint32_t call = *a.epoch;
+    const int set = int(call & 1u);
+    const int R = a.T * a.world * kTop;
+    uint32_t f = 0;
+    for (int i = blockIdx.x; i < R; i += gridDim.x) {
+        if (a.ids[i] < 0) continue;   // padding, or a slot another rank owns
+        const int r = i / kTop, s = i % kTop, h = r / a.T, t = r % a.T;
+        const int row = a.rowpos ? a.rowpos[i] : i;
+        float4* d = reinterpret_cast<float4*>(a.dst_rows[set][h] + (size_t(t) * kTop + s) * kH) + threadIdx.x * 2;
+        if (row < 0 || row >= R + a.T * a.world) {
+            d[0] = d[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            f |= kFlagInvalidId;
+            continue;
+        }
+        const float4* src = reinterpret_cast<const float4*>(a.route_out + size_t(row) * kH) + threadIdx.x * 2;
+        const float4 v0 = __ldcs(src), v1 = __ldcs(src + 1);
+        d[0] = v0;
+        d[1] = v1;
+    }
+    if (f && threadIdx.x == 0) atomicOr(a.flags, f);
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
+        __threadfence_system();
+        for (int h = 0; h < a.world; ++h)
+            if (h != a.me)
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[h] + a.me), "r"(call) : "memory");
+        *a.counter = 0u;
+    }
+}
+
+// Waits as ep_wait_signals_kernel does, for the call number in device memory.
+__global__ __launch_bounds__(32) void ep_wait_epoch_kernel(const uint32_t* sig, int world, int me,
+                                                           const uint32_t* epoch, uint32_t* flags) {
+    const int d = threadIdx.x;
+    if (d >= world || d == me) return;
+    const uint32_t call = *epoch;
+    const uint64_t t0 = p2p_now_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sig + d) : "memory");
+        if (int32_t(v - call) >= 0) return;
+        if (p2p_now_ns() - t0 > kP2PTimeoutNs) {
+            atomicOr(flags, uint32_t(kFlagWaitTimeout));
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
 // Lane d waits until rank d's flag in this rank's array reaches `epoch`
 // (wrap-around safe), for at most about a second.
 __global__ __launch_bounds__(32) void ep_wait_signals_kernel(const uint32_t* sig, int world, int me, uint32_t epoch,
@@ -324,6 +435,107 @@ extern "C" cudaError_t ornith_moe_b200_ep_dispatch_p2p(const void* x_bf16, int T
     const int grid = n < 2 * sms ? (n > 0 ? n : 1) : 2 * sms;
     count_launches(1);
     ep_dispatch_p2p_kernel<<<grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, const void* local_ids_i32, int T,
+                                                         void* const* dst_x, void* const* dst_ids,
+                                                         void* const* signals, int world, int me, void* epoch_u32,
+                                                         void* counter_u32, cudaStream_t stream) {
+    if (T < 1 || T > kTcapMax || world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || !x_bf16 ||
+        !local_ids_i32 || !dst_x || !dst_ids || !signals || !epoch_u32 || !counter_u32 ||
+        !p2p_aligned(x_bf16, 16) || !p2p_aligned(local_ids_i32, 16) || !p2p_aligned(epoch_u32, 4) ||
+        !p2p_aligned(counter_u32, 4) || size_t(T) * world > size_t(kTcapMax))
+        return cudaErrorInvalidValue;
+    FixedArgs a{};
+    for (int set = 0; set < 2; ++set)
+        for (int d = 0; d < world; ++d) {
+            void* px = dst_x[set * world + d];
+            void* pi = dst_ids[set * world + d];
+            if (!px || !pi || !p2p_aligned(px, 16) || !p2p_aligned(pi, 16)) return cudaErrorInvalidValue;
+            a.dst_x[set][d] = static_cast<uint16_t*>(px);
+            a.dst_ids[set][d] = static_cast<int32_t*>(pi);
+        }
+    for (int d = 0; d < world; ++d) {
+        if (d != me && (!signals[d] || !p2p_aligned(signals[d], 4))) return cudaErrorInvalidValue;
+        a.sig[d] = static_cast<uint32_t*>(signals[d]);
+    }
+    a.x = static_cast<const uint16_t*>(x_bf16);
+    a.local_ids = static_cast<const int32_t*>(local_ids_i32);
+    a.T = T;
+    a.world = world;
+    a.me = me;
+    a.epoch = static_cast<uint32_t*>(epoch_u32);
+    a.counter = static_cast<uint32_t*>(counter_u32);
+    NvtxRange range("ornith.ep.fixed_dispatch");
+    int device = 0, sms = 0;
+    cudaError_t st = cudaGetDevice(&device);
+    if (st != cudaSuccess) return st;
+    if ((st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return st;
+    const int items = T * world;
+    count_launches(1);
+    ep_fixed_dispatch_kernel<<<items < 2 * sms ? items : 2 * sms, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_fixed_return(const void* workspace, size_t bytes, int T, int Tcap,
+                                                       const void* ids_i32, void* const* dst_rows,
+                                                       void* const* signals, int world, int me,
+                                                       const void* epoch_u32, void* counter_u32, void* flags,
+                                                       cudaStream_t stream) {
+    // T: tokens per rank; the layer call ran on world * T rows with capacity Tcap
+    if (T < 1 || world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || Tcap < 0 || Tcap > kTcapMax ||
+        T * world > Tcap)
+        return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes || !workspace || !ids_i32 || !dst_rows || !signals || !epoch_u32 || !counter_u32 ||
+        !flags || !p2p_aligned(workspace, 256) || !p2p_aligned(ids_i32, 4) || !p2p_aligned(epoch_u32, 4) ||
+        !p2p_aligned(counter_u32, 4) || !p2p_aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    FixedReturnArgs a{};
+    for (int set = 0; set < 2; ++set)
+        for (int h = 0; h < world; ++h) {
+            void* p = dst_rows[set * world + h];
+            if (!p || !p2p_aligned(p, 16)) return cudaErrorInvalidValue;
+            a.dst_rows[set][h] = static_cast<float*>(p);
+        }
+    for (int h = 0; h < world; ++h) {
+        if (h != me && (!signals[h] || !p2p_aligned(signals[h], 4))) return cudaErrorInvalidValue;
+        a.sig[h] = static_cast<uint32_t*>(signals[h]);
+    }
+    const int rows_in = T * world;
+    const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+    a.route_out = reinterpret_cast<const float*>(ws + w.route_out);
+    a.rowpos = rows_by_position(rows_in) ? reinterpret_cast<const int32_t*>(ws + w.rowpos) : nullptr;
+    a.ids = static_cast<const int32_t*>(ids_i32);
+    a.T = T;
+    a.world = world;
+    a.me = me;
+    a.epoch = static_cast<const uint32_t*>(epoch_u32);
+    a.counter = static_cast<uint32_t*>(counter_u32);
+    a.flags = static_cast<uint32_t*>(flags);
+    NvtxRange range("ornith.ep.fixed_return");
+    int device = 0, sms = 0;
+    cudaError_t st = cudaGetDevice(&device);
+    if (st != cudaSuccess) return st;
+    if ((st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return st;
+    const int items = rows_in * kTop;
+    count_launches(1);
+    ep_fixed_return_kernel<<<items < 2 * sms ? items : 2 * sms, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_wait_epoch(const void* signals_u32, int world, int me,
+                                                     const void* epoch_u32, void* flags, cudaStream_t stream) {
+    if (world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || !signals_u32 || !epoch_u32 || !flags ||
+        !p2p_aligned(signals_u32, 4) || !p2p_aligned(epoch_u32, 4) || !p2p_aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    if (world == 1) return cudaSuccess;
+    NvtxRange range("ornith.ep.wait");
+    count_launches(1);
+    ep_wait_epoch_kernel<<<1, 32, 0, stream>>>(static_cast<const uint32_t*>(signals_u32), world, me,
+                                               static_cast<const uint32_t*>(epoch_u32),
+                                               static_cast<uint32_t*>(flags));
     return cudaGetLastError();
 }
 

@@ -449,9 +449,9 @@ class _DeviceArray:
     """A device range described by __cuda_array_interface__ (v3), so that
     torch.as_tensor can view memory this module allocated itself."""
 
-    def __init__(self, address, shape, typestr):
+    def __init__(self, address, shape, typestr, strides=None):
         self.__cuda_array_interface__ = {'shape': tuple(shape), 'typestr': typestr, 'data': (int(address), False),
-                                         'strides': None, 'version': 3}
+                                         'strides': None if strides is None else tuple(strides), 'version': 3}
 
 
 class PeerExchange:
@@ -557,6 +557,99 @@ class PeerExchange:
         self.base = 0
 
 
+class PeerFixedExchange:
+    """Receive buffers of the fixed-size exchange over NVLink peer memory
+    (every rank T tokens), in two sets used by odd and even calls: token rows
+    bf16 [2][world*T][2048] and their local ids int32 [2][world*T][8], result
+    rows fp32 [2][T*8][2048], then dispatch and return flags (one uint32 per
+    rank).  The call number is an int32 on the device, so a step holds no
+    host value that changes between calls and can be captured in a CUDA
+    graph.  Made and closed collectively, like PeerExchange."""
+
+    def __init__(self, group, world, me, T, device):
+        from . import native
+        if not 1 <= world <= 8:
+            raise ValueError('the peer-memory exchange serves 1..8 ranks of one node')
+        self.native, self.group, self.world, self.me, self.T = native, group, world, me, int(T)
+        rows_in, rows_out = world * self.T, self.T * TOP
+
+        def up(n):
+            return (n + 255) // 256 * 256
+        self.x_offset, self.x_set = 0, up(rows_in * H * 2)
+        self.ids_offset, self.ids_set = 2 * self.x_set, up(rows_in * TOP * 4)
+        self.rows_offset, self.rows_set = self.ids_offset + 2 * self.ids_set, rows_out * H * 4
+        self.flag_offset = up(self.rows_offset + 2 * self.rows_set)
+        self.base = native.ep_buffer_alloc(self.flag_offset + 256)
+        self.peers = {}
+        try:
+            handles = [None] * world
+            dist.all_gather_object(handles, native.ep_ipc_handle(self.base), group=group)
+            for r in range(world):
+                if r != me:
+                    self.peers[r] = native.ep_ipc_open(handles[r])
+        except BaseException:
+            PeerExchange._release(self)
+            raise
+        bases = [self.base if r == me else self.peers[r] for r in range(world)]
+
+        def sets(offset, stride):
+            return (C.c_void_p * (2 * world))(*[b + offset + k * stride for k in range(2) for b in bases])
+        self.dst_x, self.dst_ids = sets(self.x_offset, self.x_set), sets(self.ids_offset, self.ids_set)
+        self.dst_rows = sets(self.rows_offset, self.rows_set)
+        self.dispatch_flags = (C.c_void_p * world)(*[b + self.flag_offset for b in bases])
+        self.return_flags = (C.c_void_p * world)(*[b + self.flag_offset + 4 * world for b in bases])
+        def view(offset, shape, typestr, strides=None):
+            return torch.as_tensor(_DeviceArray(self.base + offset, shape, typestr, strides), device=device)
+        # both sets of a buffer as one [2, ...] view (byte strides), so that a
+        # device-side index picks a set without touching the other
+        self.x2 = view(self.x_offset, (2, rows_in, H), '<i2', (self.x_set, H * 2, 2)).view(torch.bfloat16)
+        self.ids2 = view(self.ids_offset, (2, rows_in, TOP), '<i4', (self.ids_set, TOP * 4, 4))
+        self.rows = view(self.rows_offset, (2 * rows_out, H), '<f4')   # both result sets, one array
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.counters = torch.zeros(2, dtype=torch.int32, device=device)
+        self._slot_rows = torch.arange(rows_out, dtype=torch.int32, device=device).view(self.T, TOP)
+
+    def parity(self):
+        """0 or 1: the set of the current call, as a device tensor."""
+        return (self.epoch & 1).long()
+
+    def dispatch(self, x, local_ids_per_rank):
+        self.native.ep_fixed_dispatch(x, local_ids_per_rank, self.dst_x, self.dst_ids, self.dispatch_flags,
+                                      self.world, self.me, self.epoch, self.counters[0:1])
+
+    def wait_dispatch(self, flags):
+        self.native.ep_wait_epoch(self.base + self.flag_offset, self.world, self.me, self.epoch, flags)
+
+    def received(self):
+        """(token rows [world*T, 2048], local ids [world*T, 8]) of this call's
+        set, copied out by a device-side choice of the set (index_select reads
+        only the chosen one)."""
+        k = self.parity()
+        x = torch.index_select(self.x2, 0, k)[0]
+        ids = torch.index_select(self.ids2, 0, k)[0]
+        return x.contiguous(), ids.contiguous()
+
+    def ret(self, workspace, capacity, ids_all, flags):
+        self.native.ep_fixed_return(workspace, self.T, capacity, ids_all, self.dst_rows, self.return_flags,
+                                    self.world, self.me, self.epoch, self.counters[1:2], flags)
+
+    def wait_return(self, flags):
+        self.native.ep_wait_epoch(self.base + self.flag_offset + 4 * self.world, self.world, self.me, self.epoch,
+                                  flags)
+
+    def result_index(self, ids):
+        """int32 [T, 8]: row of self.rows holding slot s of token t in this
+        call's set, -1 for padding and invalid ids."""
+        valid = (ids >= 0) & (ids < E)
+        rows = self._slot_rows + (self.parity() * (self.T * TOP)).to(torch.int32)
+        return torch.where(valid, rows, torch.full_like(rows, -1)).contiguous()
+
+    def close(self):
+        """Collective, like PeerExchange.close; the views go first."""
+        self.x2 = self.ids2 = None
+        PeerExchange.close(self)
+
+
 class ExpertParallelMoE:
     """GPU expert-parallel layer over NCCL with this library's kernels.
 
@@ -588,9 +681,9 @@ class ExpertParallelMoE:
         if not isinstance(chunks, int) or chunks < 1 or (chunks > 1 and (exchange, combine) != ('compact', 'exact')):
             raise ValueError('chunks > 1 applies to the compact exchange with the exact combine')
         if transport not in ('nccl', 'p2p') or (transport == 'p2p' and (
-                (exchange, combine, chunks) != ('compact', 'exact', 1) or not 1 <= world <= 8)):
-            raise ValueError("transport 'p2p' applies to the compact exchange with the exact combine, one chunk, "
-                             "on 1..8 ranks of one node")
+                (combine, chunks) != ('exact', 1) or not 1 <= world <= 8)):
+            raise ValueError("transport 'p2p' applies to the exact combine with one chunk, on 1..8 ranks of one node")
+        self.transport = transport
         self.chunks = chunks
         self.combine_mode = combine
         self.native = native
@@ -604,7 +697,8 @@ class ExpertParallelMoE:
         # an expert rank receives at most `capacity` token rows; a home rank gets
         # back at most one row per (token, slot), 8 per local token
         self.peer = PeerExchange(group, world, self.me, self.capacity, TOP * self.capacity, banks[0].device) \
-            if transport == 'p2p' else None
+            if (transport, exchange) == ('p2p', 'compact') else None
+        self.peer_fixed = None   # fixed exchange over peer memory: made at the first call (it needs T)
         self.symbol = 'ornith_routed_direct_launch' if act_bits == 8 else 'ornith_routed_direct_launch_a4'
         dev = banks[0].device
         self.layout = native.get_layout(self.capacity)
@@ -671,12 +765,38 @@ class ExpertParallelMoE:
         got = self.peer.rows[:sum(plan.home_counts)]
         return self.combine(got, route_row_index(x.shape[0], plan, x.device), weights, ids)
 
+    def _layer_fixed_p2p(self, x, ids, weights):
+        """Fixed exchange over NVLink peer memory (PeerFixedExchange): every
+        rank's token rows go to every rank, the computed slots straight to
+        their home ranks; no collective and no host value that changes
+        between calls, so the step can be captured in a CUDA graph.  Every
+        call must have the token count of the first."""
+        T = x.shape[0]
+        if self.peer_fixed is None:
+            self.peer_fixed = PeerFixedExchange(self.group, self.world, self.me, T, x.device)   # collective
+        elif self.peer_fixed.T != T:
+            raise ValueError(f'the fixed peer-memory exchange was made for {self.peer_fixed.T} tokens, got {T}')
+        if self.world * T > self.capacity:
+            raise ValueError(f'expert-parallel receive of {self.world * T} rows exceeds capacity {self.capacity}')
+        owner, lid = map_ids(ids, self.placement)
+        dest = torch.arange(self.world, device=ids.device, dtype=owner.dtype).view(-1, 1, 1)
+        local = torch.where(owner.unsqueeze(0) == dest, lid.unsqueeze(0), torch.full_like(lid, -1).unsqueeze(0))
+        pf = self.peer_fixed
+        pf.dispatch(x.contiguous(), local.to(torch.int32).contiguous())
+        pf.wait_dispatch(self.flags)
+        x_all, ids_all = pf.received()
+        self._layer(x_all, ids_all)
+        pf.ret(self.workspace, self.capacity, ids_all, self.flags)
+        pf.wait_return(self.flags)
+        return self.combine(pf.rows, pf.result_index(ids), weights, ids)
+
     def close(self):
         """Release the peer-memory buffers (collective; before the process
         group is destroyed)."""
-        if self.peer is not None:
-            self.peer.close()
-            self.peer = None
+        for name in ('peer', 'peer_fixed'):
+            if getattr(self, name) is not None:
+                getattr(self, name).close()
+                setattr(self, name, None)
 
     def __call__(self, x, ids, weights):
         if self.combine_mode == 'partial':
@@ -688,6 +808,8 @@ class ExpertParallelMoE:
                                               self.combine, self.placement)
             return ep_layer_partial(self.group, self.world, x, ids, weights, self.compute_partial, self.combine,
                                     self.placement, self.planner)
+        if self.exchange == 'fixed' and self.transport == 'p2p':
+            return self._layer_fixed_p2p(x, ids, weights)
         if self.exchange == 'fixed':
             return ep_layer_fixed(self.group, self.world, x, ids, weights, self.compute_block, self.combine,
                                   self.placement)

@@ -98,6 +98,12 @@ SIGNATURES = {
                                          C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int64,
                                          C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p,
                                          C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_fixed_dispatch': ([C.c_void_p, C.c_void_p, C.c_int] + [C.POINTER(C.c_void_p)] * 3
+                                          + [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_fixed_return': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p]
+                                        + [C.POINTER(C.c_void_p)] * 2 + [C.c_int, C.c_int] + [C.c_void_p] * 4,
+                                        C.c_int),
+    'ornith_moe_b200_ep_wait_epoch': ([C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
     'ornith_moe_b200_ep_wait_signals': ([C.c_void_p, C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
     'ornith_dense_g256_abi_version': ([], C.c_uint32),
@@ -484,6 +490,33 @@ def ep_dispatch_p2p(x, token_index, local_ids, seg, dst_x, dst_ids, offsets, cap
     check(lib().ornith_moe_b200_ep_dispatch_p2p(ptr(x), x.shape[0], ptr(token_index), ptr(local_ids), n, seg_a, dst_x,
                                                 dst_ids, off_a, cap_tokens, signals, world, me, epoch, ptr(counter),
                                                 ptr(flags), stream(x)), 'expert-parallel peer dispatch')
+
+
+def ep_fixed_dispatch(x, local_ids, dst_x, dst_ids, signals, world, me, epoch, counter):
+    """Fixed-size dispatch over peer memory: x bf16 [T, 2048] and local_ids
+    int32 [world, T, 8] into every rank's receive set of this call (dst_x,
+    dst_ids: ctypes arrays [2 * world]); epoch: the int32 call counter."""
+    T = x.shape[0]
+    if (x.dtype != torch.bfloat16 or x.shape != (T, 2048) or not x.is_contiguous() or local_ids.dtype != torch.int32
+            or local_ids.shape != (world, T, 8) or not local_ids.is_contiguous()):
+        raise ValueError('ep_fixed_dispatch takes bf16 rows [T, 2048] and INT32 ids [world, T, 8]')
+    check(lib().ornith_moe_b200_ep_fixed_dispatch(ptr(x), ptr(local_ids), T, dst_x, dst_ids, signals, world, me,
+                                                  ptr(epoch), ptr(counter), stream(x)), 'expert-parallel fixed dispatch')
+
+
+def ep_fixed_return(workspace, T, capacity, ids, dst_rows, signals, world, me, epoch, counter, flags):
+    """Fixed-size return over peer memory after a layer call on ids int32
+    [world * T, 8] (local ids; -1 where another rank owns the slot)."""
+    if ids.dtype != torch.int32 or ids.shape != (world * T, 8) or not ids.is_contiguous():
+        raise ValueError('ep_fixed_return takes the INT32 local ids [world * T, 8] of the layer call')
+    check(lib().ornith_moe_b200_ep_fixed_return(ptr(workspace), workspace.numel(), T, capacity, ptr(ids), dst_rows,
+                                                signals, world, me, ptr(epoch), ptr(counter), ptr(flags),
+                                                stream(ids)), 'expert-parallel fixed return')
+
+
+def ep_wait_epoch(signals_address, world, me, epoch, flags):
+    check(lib().ornith_moe_b200_ep_wait_epoch(C.c_void_p(signals_address), world, me, ptr(epoch), ptr(flags),
+                                              stream(flags)), 'expert-parallel peer wait')
 
 
 def ep_wait_signals(signals_address, world, me, epoch, flags):

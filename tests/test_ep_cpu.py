@@ -159,6 +159,29 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
                 assert 0 <= off_d[me] and off_d[me] + k <= got.shape[0]
                 got[off_d[me]:off_d[me] + k] = rows_d[lo:lo + k]
             out = fake_combine_gathered(got, ep.route_row_index(T, plan, got.device), weights, ids)
+        elif mode == 'fixed_peer':   # the fixed exchange over peer memory, its stores emulated on the host
+            me = dist.get_rank()
+            owner, lid = ep.map_ids(ids, placement)
+            dest = torch.arange(world).view(-1, 1, 1)
+            local = torch.where(owner.unsqueeze(0) == dest, lid.unsqueeze(0),
+                                torch.full_like(lid, -1).unsqueeze(0)).to(torch.int32)
+            sent = [None] * world        # dispatch: rank d's row h*T + t holds token t of rank h
+            dist.all_gather_object(sent, (x, local))
+            x_all = torch.cat([x_h for x_h, _ in sent])
+            ids_all = torch.cat([local_h[me] for _, local_h in sent])
+            rows = fake_rows(x_all, ids_all, table)                     # [world*T, 8, H]
+            back = [None] * world        # return: home h's row t*8 + s from the slot's owner
+            dist.all_gather_object(back, (rows, ids_all))
+            res = torch.full((T * TOP, H), float('nan'))
+            for rows_d, ids_d in back:
+                for t in range(T):
+                    for s_ in range(TOP):
+                        if ids_d[me * T + t, s_] >= 0:
+                            assert bool(torch.isnan(res[t * TOP + s_]).all()), 'two owners stored one slot'
+                            res[t * TOP + s_] = rows_d[me * T + t, s_]
+            row_index = torch.where((ids >= 0) & (ids < E), torch.arange(T * TOP, dtype=torch.int32).view(T, TOP),
+                                    torch.full((T, TOP), -1, dtype=torch.int32))
+            out = fake_combine_gathered(res, row_index, weights, ids)
         elif mode == 'chunked':   # pipelined chunks; T + 1 chunks leaves one chunk empty
             chunks = 3 if world == 2 else T + 1
             out = ep.ep_layer_chunked(None, world, x, ids, weights, compute, fake_combine_gathered, placement,
@@ -182,7 +205,8 @@ def _worker(rank, world, port, T, seed, q, mode, balanced):
 
 
 @pytest.mark.parametrize('balanced', [False, True])
-@pytest.mark.parametrize('mode', ['compact', 'chunked', 'peer', 'fixed', 'compact_partial', 'fixed_partial'])
+@pytest.mark.parametrize('mode', ['compact', 'chunked', 'peer', 'fixed', 'fixed_peer', 'compact_partial',
+                                  'fixed_partial'])
 @pytest.mark.parametrize('world,T', [(2, 16), (4, 9)])
 def test_ep_dispatch_combine_matches_single_rank(world, T, mode, balanced):
     ctx = mp.get_context('spawn')

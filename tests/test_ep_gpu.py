@@ -36,6 +36,7 @@ CASES = [  # (exchange, balanced placement, combine, further ExpertParallelMoE o
     ('fixed', True, 'exact', {}), ('compact', True, 'partial', {}), ('fixed', True, 'partial', {}),
     ('compact', True, 'exact', {'chunks': 3}),
     ('compact', False, 'exact', {'transport': 'p2p'}), ('compact', True, 'exact', {'transport': 'p2p'}),
+    ('fixed', False, 'exact', {'transport': 'p2p'}), ('fixed', True, 'exact', {'transport': 'p2p'}),
 ]
 
 
@@ -93,7 +94,7 @@ def _worker(rank, world, port, T, q):
             layer = ep.ExpertParallelMoE(None, world, (pick(gc), pick(gm), pick(dc), pick(dm)), capacity=T * world,
                                          exchange=mode, placement=placement, combine=combine, **options)
             ok = True
-            for _ in range(2):   # twice: the second call reuses the exchange buffers
+            for _ in range(3):   # three calls: both buffer sets of the fixed peer exchange, then the first again
                 out = layer(x, ids, w)
                 torch.cuda.synchronize()
                 ok = ok and (bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))) if combine == 'exact'
