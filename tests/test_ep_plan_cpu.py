@@ -239,3 +239,30 @@ def test_peer_dispatch_validation_without_device_work(native):
     assert call(ids=C.c_void_p(base + (2 << 28) + 4)) == INVALID
     assert call(d=(C.c_void_p * world)(base + (5 << 28), None)) == INVALID
     assert call(s=(C.c_void_p * world)(None, base + (10 << 28))) == INVALID   # rank 0's flags (this is rank 1)
+
+
+def test_fixed_peer_exchange_validation_without_device_work(native):
+    lib = native.lib()
+    base = 1 << 32
+    x, lids, epoch, counter, flags, ws = (C.c_void_p(base + (i << 28)) for i in range(6))
+    world = 2
+    sets = (C.c_void_p * (2 * world))(*[base + ((8 + i) << 28) for i in range(2 * world)])
+    sigs = (C.c_void_p * world)(base + (14 << 28), base + (15 << 28))
+    d = lib.ornith_moe_b200_ep_fixed_dispatch
+    assert d(x, lids, 0, sets, sets, sigs, world, 0, epoch, counter, None) == INVALID        # T >= 1
+    assert d(x, lids, 4097, sets, sets, sigs, world, 0, epoch, counter, None) == INVALID     # world*T <= 8192
+    assert d(x, lids, 4, sets, sets, sigs, world, 2, epoch, counter, None) == INVALID        # me < world
+    assert d(C.c_void_p(base + 8), lids, 4, sets, sets, sigs, world, 0, epoch, counter, None) == INVALID
+    bad = (C.c_void_p * (2 * world))(*[base + ((8 + i) << 28) for i in range(2 * world - 1)], None)
+    assert d(x, lids, 4, bad, sets, sigs, world, 0, epoch, counter, None) == INVALID          # every set, every rank
+    r = lib.ornith_moe_b200_ep_fixed_return
+    nb = native.get_layout(16).workspace_bytes
+    assert r(ws, nb, 9, 16, lids, sets, sigs, world, 0, epoch, counter, flags, None) == INVALID   # world*T > Tcap
+    assert r(ws, nb - 1, 8, 16, lids, sets, sigs, world, 0, epoch, counter, flags, None) == INVALID
+    assert r(ws, nb, 8, 16, lids, bad, sigs, world, 0, epoch, counter, flags, None) == INVALID
+    assert r(ws, nb, 8, 16, lids, sets, (C.c_void_p * world)(base, None), world, 0, epoch, counter, flags,
+             None) == INVALID                                                               # a peer's flags
+    w = lib.ornith_moe_b200_ep_wait_epoch
+    assert w(sigs[0], 9, 0, epoch, flags, None) == INVALID
+    assert w(None, 2, 0, epoch, flags, None) == INVALID
+    assert w(sigs[0], 1, 0, epoch, flags, None) == 0          # one rank: nothing to wait for
