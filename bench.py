@@ -294,9 +294,15 @@ def run_ep(args):
                                  if args.placement == 'balanced' else 'contiguous ranges'),
                    'combine': ('per-slot fp32 rows, bit-identical to one GPU' if args.combine == 'exact' else
                                'per-rank fp32 partial sums, equal to one GPU within fp32 rounding'),
-                   'exchange': ('NCCL all_gather of token rows + equal-block all_to_all of fp32 per-slot rows '
-                                '(no host synchronisation)' if cfg['exchange'] == 'fixed' else
-                                'NCCL all_to_all_single dispatch + fp32 per-slot return (variable splits)'),
+                   'exchange': ({('fixed', 'nccl'): 'NCCL all_gather of token rows + equal-block all_to_all of '
+                                                   'fp32 per-slot rows (no host synchronisation)',
+                                 ('compact', 'nccl'): 'NCCL all_to_all_single dispatch + fp32 per-slot return '
+                                                      '(variable splits)',
+                                 ('fixed', 'p2p'): 'token rows to every rank and owned fp32 slots to their home '
+                                                   'as NVLink peer stores (double-buffered, no collective)',
+                                 ('compact', 'p2p'): 'NCCL count all_gather, then token rows and fp32 per-slot '
+                                                     'rows as NVLink peer stores'}[(cfg['exchange'],
+                                                                                    args.ep_transport)]),
                    'chunks': args.ep_chunks if cfg['exchange'] == 'compact' else 1,
                    'transport': 'NVLink peer stores' if args.ep_transport == 'p2p' else 'NCCL'},
         'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': graph is not None,
