@@ -35,7 +35,8 @@ def build(force=False, verbose=False, flags=(), out=None):
     """Compile the library.  Extra nvcc flags (the kernels' build-time
     options: -DORNITH_PREFILL_F32X2=1, -DORNITH_PREFILL_CONV6=1,
     -DORNITH_DECODE_L2_PREFETCH=1, -DORNITH_DECODE_EARLY_PREFETCH=1,
-    -DORNITH_DENSE_HOISTED_NIBBLES=1, the trace builds) come from `flags` and
+    -DORNITH_DENSE_HOISTED_NIBBLES=1, -DORNITH_DECODE_GATE_COST=…,
+    -DORNITH_DECODE_DOWN_COST=…, the trace builds) come from `flags` and
     from ORNITH_MOE_B200_NVCC_FLAGS; the default build sets none of them
     (DEBUG_FLAGS make the debug-bounds library).
     `out` writes a variant library elsewhere (always rebuilt), which
