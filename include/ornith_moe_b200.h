@@ -217,7 +217,10 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_plan(
  * receive buffer made by ep_buffer_alloc (zeroed device memory), shared with
  * the other ranks of the node through a CUDA IPC handle (ep_ipc_handle: 64
  * bytes; ep_ipc_open/_close on the peers); the caller lays out rows and flag
- * arrays (one uint32 per rank) inside it.  ep_return_p2p: after a layer call
+ * arrays inside it.  A flag array holds 2*world uint32 words: the epoch each
+ * other rank raised, then that rank's status word (its flag-64 bit, stored
+ * before the epoch), so that a rank whose own wait ran out makes every rank
+ * it sends to report flag 64 too.  ep_return_p2p: after a layer call
  * of T tokens on `workspace`, rows [seg[h], seg[h+1]) of route_index (the
  * routes whose down projections go home to rank h; seg a host array of
  * world+1 entries) are copied to rows dst_offset[h]... of dst_rows[h] (host
@@ -225,10 +228,11 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_plan(
  * `epoch` is stored into slot `me` of every other rank's flag array
  * (signals[h]).  Every destination range must lie inside dst_capacity_rows,
  * which is checked before the launch.  counter_u32 is a zeroed device word
- * per stream.  ep_wait_signals: waits until every other rank's flag in this
- * rank's array has reached `epoch`, for at most about a second (then flag
- * 64).  Plain stores and loads only (no TMA, no multicast).  No counterpart
- * in the reference, which runs one rank. */
+ * per stream.  ep_wait_signals: waits until every other rank's epoch in this
+ * rank's array has reached `epoch`, for at most the peer wait limit (then
+ * flag 64), and ORs their status bits into flags_u32.  Plain stores and loads
+ * only (no TMA, no multicast).  No counterpart in the reference, which runs
+ * one rank. */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_buffer_alloc(size_t bytes, void** ptr);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_buffer_free(void* ptr);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_ipc_handle(const void* base, void* handle_out);
@@ -253,25 +257,38 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_dispatch_p2p(
  * Receive buffers come in two sets, used by calls of odd and even number; the
  * call number is a uint32 in device memory (epoch_u32, zero at first).
  * ep_fixed_dispatch: row me*T + t of every rank d's token buffer (dst_x, host
- * array [2][world]) receives x[t] (bf16 [T][2048]) and its ids buffer
- * (dst_ids) local_ids[d][t] (int32 [world][T][8]); then the call number goes
- * into slot `me` of the others' dispatch flags and into *epoch_u32.
- * ep_fixed_return: after the layer call on the world*T received rows (ids
- * int32 [world*T][8], capacity Tcap), each slot with a valid local id of row
- * h*T + t goes to row t*8 + s of home h's result buffer (dst_rows, [2][world]),
- * then the call number into the others' return flags.  ep_wait_epoch: waits,
- * bounded (flag 64), until every other rank's flag reaches *epoch_u32. */
+ * array [2][world], each set dst_capacity_rows >= world*T rows) receives x[t]
+ * (bf16 [T][2048]) and its ids buffer (dst_ids) local_ids[d][t] (int32
+ * [world][T][8]); then the call number goes into slot `me` of the others'
+ * dispatch flags (with this rank's flag-64 bit from flags_u32 as its status
+ * word) and into *epoch_u32.  ep_fixed_return: after the layer call on the
+ * world*T received rows (ids int32 [world*T][8], capacity Tcap), each slot
+ * with a valid local id of row h*T + t goes to row t*8 + s of home h's result
+ * buffer (dst_rows, [2][world], each set dst_capacity_rows >= T*8 rows), then
+ * the call number into the others' return flags.  Capacities too small for
+ * those rows are refused before the launch.  ep_wait_epoch: waits, bounded
+ * (flag 64), until every other rank's epoch reaches *epoch_u32, and ORs their
+ * status bits into flags_u32. */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_fixed_dispatch(
     const void* x_bf16, const void* local_ids_i32, int T, void* const* dst_x, void* const* dst_ids,
-    void* const* signals, int world, int me, void* epoch_u32, void* counter_u32, cudaStream_t stream);
+    int64_t dst_capacity_rows, void* const* signals, int world, int me, void* epoch_u32, void* counter_u32,
+    const void* flags_u32, cudaStream_t stream);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_fixed_return(
     const void* workspace, size_t bytes, int T, int Tcap, const void* ids_i32, void* const* dst_rows,
-    void* const* signals, int world, int me, const void* epoch_u32, void* counter_u32, void* flags_u32,
-    cudaStream_t stream);
+    int64_t dst_capacity_rows, void* const* signals, int world, int me, const void* epoch_u32, void* counter_u32,
+    void* flags_u32, cudaStream_t stream);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_wait_epoch(
     const void* signals_u32, int world, int me, const void* epoch_u32, void* flags_u32, cudaStream_t stream);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_wait_signals(
     const void* signals_u32, int world, int me, uint32_t epoch, void* flags_u32, cudaStream_t stream);
+/* The limit of every wait on another rank (ep_wait_signals, ep_wait_epoch), in
+ * nanoseconds of the GPU's global timer: 1 s by default, 1 us to 60 s
+ * accepted (cudaErrorInvalidValue otherwise).  Process-wide; read when a wait
+ * is launched, so a captured graph keeps the value of its capture.  Waits
+ * inside one kernel on its own copies and CTAs keep a fixed 1 s limit.  No
+ * counterpart in the reference. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_set_peer_wait_limit_ns(uint64_t limit_ns);
+ORNITH_MOE_B200_EXPORT uint64_t ornith_moe_b200_peer_wait_limit_ns(void);
 
 /* Router logits, the router linear ahead of the operator
  * (iu4_correctness/gates_projection.py:17-25): input bf16 [T,2048],
@@ -305,8 +322,12 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_get_layout(int Tcap, size_t* 
  * exit; it limits a call to T <= 8 tokens (larger T: cudaErrorInvalidValue).
  * Every call on a device shares that array, so calls that can overlap on the
  * GPU race: order them on one stream.  The first call on a device looks up the
- * array's address and should come before any stream capture.  The library
- * calls no allocator.  Arguments and results otherwise as
+ * array's address and should come before any stream capture; that address is
+ * kept for the life of the process, so calls after cudaDeviceReset (or after
+ * the device's primary context was destroyed and made again) are not
+ * supported.  The library calls no allocator.  It always runs the fused decode
+ * kernel: ORNITH_MOE_B200_PATH=generic and the NVTX layer range of the
+ * workspace entry do not apply to it.  Arguments and results otherwise as
  * ornith_routed_direct_launch. */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_routed_direct_launch_noalloc(
     const void* input_bf16, const void* route_weights_f32, const void* ids_i32,

@@ -20,7 +20,8 @@ Outputs (git-ignored, never committed):
   oracle/_ref/libref_dense_n32.so            kernels/dense_n32/ (dense G256 projections)
   oracle/_ref/libref_head_i8.so              kernels/head/ (W8 LM head)
 
-Usage: python oracle/build_ref.py [--reference DIR]
+Usage: python oracle/build_ref.py [--reference DIR]   (default: ORNITH_REFERENCE, else
+BASELINE.json's reference_path)
 The reference checkout exists only in the build container; on other machines
 the prebuilt libraries travel with the repository snapshot.
 """
@@ -50,6 +51,26 @@ LIBS = {
                 ['head_i8_tile_consumer.cpp', 'head_i8_tile_api.h'],
                 'head_i8_tile_consumer.cpp'),
 }
+ROOT = HERE.parent
+
+
+def reference_root():
+    """The reference checkout: the ORNITH_REFERENCE environment variable, else
+    the `reference_path` that BASELINE.json at the repository root records;
+    None when neither names an existing checkout (as on the GPU boxes, where
+    the prebuilt libraries travel with the repository instead)."""
+    path = os.environ.get('ORNITH_REFERENCE')
+    if not path:
+        try:
+            import json
+            path = json.loads((ROOT / 'BASELINE.json').read_text()).get('reference_path')
+        except (OSError, ValueError):
+            path = None
+    if path and Path(path, 'kernels').is_dir():
+        return Path(path)
+    return None
+
+
 LAUNCH = re.compile(r'(\b[A-Za-z_]\w*(?:<[^<>;()]*>)?)\s*<<<(.*?)>>>\s*\(')
 
 
@@ -86,9 +107,11 @@ def build(reference, names=None):
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument('--reference', default=os.environ.get('ORNITH_REFERENCE', '/root/reference'))
+    parser.add_argument('--reference', default=None,
+                        help='reference checkout (default: ORNITH_REFERENCE, else BASELINE.json reference_path)')
     args = parser.parse_args()
-    if not Path(args.reference, 'kernels').is_dir():
+    args.reference = args.reference or reference_root()
+    if args.reference is None or not Path(args.reference, 'kernels').is_dir():
         print(f'reference checkout not found at {args.reference}; nothing built', file=sys.stderr)
         return 1
     for lib in build(args.reference):

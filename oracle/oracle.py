@@ -31,8 +31,8 @@ def build():
     """Compile liboracle.so (and the reference libraries when the reference checkout exists)."""
     subprocess.run(['make', '-s', '-C', str(HERE)], check=True)
     from . import build_ref  # noqa: WPS433
-    ref = Path(build_ref.os.environ.get('ORNITH_REFERENCE', '/root/reference'))
-    if (ref / 'kernels').is_dir():
+    ref = build_ref.reference_root()
+    if ref is not None:
         build_ref.build(ref)
 
 

@@ -46,10 +46,24 @@ def build(force=False, verbose=False, flags=(), out=None):
     if not out and not force and not stale():
         return LIB
     extra = [*flags, *os.environ.get('ORNITH_MOE_B200_NVCC_FLAGS', '').split()]
-    cmd = [NVCC, *FLAGS, *extra, *[str(CSRC / s) for s in SOURCES], '-o', str(target)]
-    if verbose:
-        cmd.insert(1, '-Xptxas=-v')
-    subprocess.run(cmd, check=True)
+    # one object per source, compiled in parallel, then one link step
+    objdir = HERE.parent / '_build' / target.stem
+    objdir.mkdir(parents=True, exist_ok=True)
+    compile_flags = [f for f in FLAGS if f != '-shared']
+
+    def compile_one(src):
+        obj = objdir / (Path(src).stem + '.o')
+        cmd = [NVCC, *compile_flags, *extra, '-c', str(CSRC / src), '-o', str(obj)]
+        if verbose:
+            cmd.insert(1, '-Xptxas=-v')
+        subprocess.run(cmd, check=True)
+        return obj
+
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 1)) as pool:
+        objs = list(pool.map(compile_one, SOURCES))
+    subprocess.run([NVCC, '-gencode', 'arch=compute_100a,code=sm_100a', '-shared', *map(str, objs),
+                    '-o', str(target)], check=True)
     return target
 
 

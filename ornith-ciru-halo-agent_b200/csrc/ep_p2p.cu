@@ -16,6 +16,20 @@
 // row again, so no store can leave a peer's buffer.  Every wait has a time
 // limit (flag 64 when it runs out).
 //
+// Flag arrays.  Every receiving rank has one array per direction of 2*world
+// uint32 words: the call numbers (epochs) that each sender raised, then one
+// status word per sender.  A sender stores its own timeout bit (flag 64: one
+// of its bounded waits gave up) into its status word before it publishes the
+// epoch, and the receiver's wait ORs that bit into its own flags after it has
+// seen the epoch.  A rank that went on with stale rows after a wait ran out
+// therefore makes every rank it sends to report flag 64 as well, instead of
+// handing over wrong rows under clean flags.
+//
+// Wait limit.  The waits on other ranks give up after a limit that is a
+// library setting (ornith_moe_b200_set_peer_wait_limit_ns, 1 s by default),
+// read when the wait is launched (a captured graph keeps the value it was
+// captured with).
+//
 // Ordering.  Each thread fences at system scope after its stores, the CTA
 // meets at a barrier and counts itself done on a device counter; the last CTA
 // fences again and publishes `epoch` into slot `me` of every other rank's
@@ -26,6 +40,7 @@
 // issued on its stream, so a block is never overwritten while it is read.
 #include <stdint.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "../../include/ornith_moe_b200.h"
@@ -36,7 +51,10 @@ namespace ornith {
 namespace {
 
 constexpr int kP2PMaxWorld = 8;
-constexpr uint64_t kP2PTimeoutNs = 1000000000ull;
+constexpr uint64_t kP2PDefaultWaitNs = 1000000000ull;
+constexpr uint64_t kP2PMinWaitNs = 1000ull;            // 1 us
+constexpr uint64_t kP2PMaxWaitNs = 60000000000ull;     // 60 s
+std::atomic<uint64_t> g_peer_wait_ns{kP2PDefaultWaitNs};
 
 struct ReturnArgs {
     const float* route_out;
@@ -60,6 +78,19 @@ __device__ __forceinline__ uint64_t p2p_now_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// Last CTA of a sending kernel: for every other rank h, this rank's timeout
+// bit into its status word of h's array, then the epoch (release, system
+// scope, so the status store is visible before the epoch is).
+__device__ __forceinline__ void publish_epoch(uint32_t* const* sig, int world, int me, uint32_t epoch,
+                                              const uint32_t* flags) {
+    const uint32_t status = flags ? (*reinterpret_cast<const volatile uint32_t*>(flags) & kFlagWaitTimeout) : 0u;
+    for (int h = 0; h < world; ++h) {
+        if (h == me) continue;
+        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(sig[h] + world + me), "r"(status) : "memory");
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(sig[h] + me), "r"(epoch) : "memory");
+    }
 }
 
 __global__ __launch_bounds__(256) void ep_return_p2p_kernel(const ReturnArgs a) {
@@ -95,10 +126,7 @@ __global__ __launch_bounds__(256) void ep_return_p2p_kernel(const ReturnArgs a) 
         const uint32_t done = atomicAdd(a.counter, 1u);
         if (done == gridDim.x - 1) {  // the last CTA: every row of this call is stored
             __threadfence_system();
-            for (int h = 0; h < a.world; ++h) {
-                if (h == a.me) continue;
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[h] + a.me), "r"(a.epoch) : "memory");
-            }
+            publish_epoch(a.sig, a.world, a.me, a.epoch, a.flags);
             *a.counter = 0u;  // ready for the next call on this stream
         }
     }
@@ -154,10 +182,7 @@ __global__ __launch_bounds__(256) void ep_dispatch_p2p_kernel(const DispatchArgs
         const uint32_t done = atomicAdd(a.counter, 1u);
         if (done == gridDim.x - 1) {
             __threadfence_system();
-            for (int d = 0; d < a.world; ++d) {
-                if (d == a.me) continue;
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[d] + a.me), "r"(a.epoch) : "memory");
-            }
+            publish_epoch(a.sig, a.world, a.me, a.epoch, a.flags);
             *a.counter = 0u;
         }
     }
@@ -179,6 +204,7 @@ struct FixedArgs {
     uint32_t* sig[kP2PMaxWorld];       // dispatch flag array of each rank
     uint32_t* epoch;                   // this rank's call counter
     uint32_t* counter;
+    const uint32_t* flags;             // this rank's flags (its timeout bit travels with the epoch)
 };
 
 // Dispatch: block `me` of every rank's token buffer receives this rank's T
@@ -200,9 +226,7 @@ __global__ __launch_bounds__(256) void ep_fixed_dispatch_kernel(const FixedArgs 
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
         __threadfence_system();
-        for (int d = 0; d < a.world; ++d)
-            if (d != a.me)
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[d] + a.me), "r"(call) : "memory");
+        publish_epoch(a.sig, a.world, a.me, call, a.flags);
         *a.counter = 0u;
         *a.epoch = call;
     }
@@ -248,49 +272,47 @@ __global__ __launch_bounds__(256) void ep_fixed_return_kernel(const FixedReturnA
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
         __threadfence_system();
-        for (int h = 0; h < a.world; ++h)
-            if (h != a.me)
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig[h] + a.me), "r"(call) : "memory");
+        publish_epoch(a.sig, a.world, a.me, call, a.flags);
         *a.counter = 0u;
     }
 }
 
-// Waits as ep_wait_signals_kernel does, for the call number in device memory.
-__global__ __launch_bounds__(32) void ep_wait_epoch_kernel(const uint32_t* sig, int world, int me,
-                                                           const uint32_t* epoch, uint32_t* flags) {
-    const int d = threadIdx.x;
-    if (d >= world || d == me) return;
-    const uint32_t call = *epoch;
+// Lane d waits until rank d's epoch in this rank's array reaches `epoch`
+// (wrap-around safe), for at most limit_ns of %globaltimer; then ORs rank d's
+// timeout bit (its status word) into this rank's flags.  A wait that runs out
+// raises flag 64 and returns.
+__device__ __forceinline__ void wait_peer_epoch(const uint32_t* sig, int world, int d, uint32_t epoch,
+                                                uint64_t limit_ns, uint32_t* flags) {
     const uint64_t t0 = p2p_now_ns();
     for (;;) {
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sig + d) : "memory");
-        if (int32_t(v - call) >= 0) return;
-        if (p2p_now_ns() - t0 > kP2PTimeoutNs) {
+        if (int32_t(v - epoch) >= 0) break;
+        if (p2p_now_ns() - t0 > limit_ns) {
             atomicOr(flags, uint32_t(kFlagWaitTimeout));
             return;
         }
         __nanosleep(200);
     }
+    uint32_t status;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(status) : "l"(sig + world + d) : "memory");
+    if (status & kFlagWaitTimeout) atomicOr(flags, uint32_t(kFlagWaitTimeout));
 }
 
-// Lane d waits until rank d's flag in this rank's array reaches `epoch`
-// (wrap-around safe), for at most about a second.
-__global__ __launch_bounds__(32) void ep_wait_signals_kernel(const uint32_t* sig, int world, int me, uint32_t epoch,
-                                                             uint32_t* flags) {
+// Waits as ep_wait_signals_kernel does, for the call number in device memory.
+__global__ __launch_bounds__(32) void ep_wait_epoch_kernel(const uint32_t* sig, int world, int me,
+                                                           const uint32_t* epoch, uint64_t limit_ns,
+                                                           uint32_t* flags) {
     const int d = threadIdx.x;
     if (d >= world || d == me) return;
-    const uint64_t t0 = p2p_now_ns();
-    for (;;) {
-        uint32_t v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sig + d) : "memory");
-        if (int32_t(v - epoch) >= 0) return;
-        if (p2p_now_ns() - t0 > kP2PTimeoutNs) {
-            atomicOr(flags, uint32_t(kFlagWaitTimeout));
-            return;
-        }
-        __nanosleep(200);
-    }
+    wait_peer_epoch(sig, world, d, *epoch, limit_ns, flags);
+}
+
+__global__ __launch_bounds__(32) void ep_wait_signals_kernel(const uint32_t* sig, int world, int me, uint32_t epoch,
+                                                             uint64_t limit_ns, uint32_t* flags) {
+    const int d = threadIdx.x;
+    if (d >= world || d == me) return;
+    wait_peer_epoch(sig, world, d, epoch, limit_ns, flags);
 }
 
 }  // namespace
@@ -440,13 +462,16 @@ extern "C" cudaError_t ornith_moe_b200_ep_dispatch_p2p(const void* x_bf16, int T
 
 extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, const void* local_ids_i32, int T,
                                                          void* const* dst_x, void* const* dst_ids,
-                                                         void* const* signals, int world, int me, void* epoch_u32,
-                                                         void* counter_u32, cudaStream_t stream) {
+                                                         int64_t dst_capacity_rows, void* const* signals, int world,
+                                                         int me, void* epoch_u32, void* counter_u32,
+                                                         const void* flags_u32, cudaStream_t stream) {
     if (T < 1 || T > kTcapMax || world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || !x_bf16 ||
-        !local_ids_i32 || !dst_x || !dst_ids || !signals || !epoch_u32 || !counter_u32 ||
+        !local_ids_i32 || !dst_x || !dst_ids || !signals || !epoch_u32 || !counter_u32 || !flags_u32 ||
         !p2p_aligned(x_bf16, 16) || !p2p_aligned(local_ids_i32, 16) || !p2p_aligned(epoch_u32, 4) ||
-        !p2p_aligned(counter_u32, 4) || size_t(T) * world > size_t(kTcapMax))
+        !p2p_aligned(counter_u32, 4) || !p2p_aligned(flags_u32, 4) || size_t(T) * world > size_t(kTcapMax))
         return cudaErrorInvalidValue;
+    // every set of every rank's token buffer holds the world*T rows this exchange writes
+    if (dst_capacity_rows < int64_t(T) * world) return cudaErrorInvalidValue;
     FixedArgs a{};
     for (int set = 0; set < 2; ++set)
         for (int d = 0; d < world; ++d) {
@@ -467,6 +492,7 @@ extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, con
     a.me = me;
     a.epoch = static_cast<uint32_t*>(epoch_u32);
     a.counter = static_cast<uint32_t*>(counter_u32);
+    a.flags = static_cast<const uint32_t*>(flags_u32);
     NvtxRange range("ornith.ep.fixed_dispatch");
     int device = 0, sms = 0;
     cudaError_t st = cudaGetDevice(&device);
@@ -480,13 +506,15 @@ extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, con
 
 extern "C" cudaError_t ornith_moe_b200_ep_fixed_return(const void* workspace, size_t bytes, int T, int Tcap,
                                                        const void* ids_i32, void* const* dst_rows,
-                                                       void* const* signals, int world, int me,
-                                                       const void* epoch_u32, void* counter_u32, void* flags,
+                                                       int64_t dst_capacity_rows, void* const* signals, int world,
+                                                       int me, const void* epoch_u32, void* counter_u32, void* flags,
                                                        cudaStream_t stream) {
     // T: tokens per rank; the layer call ran on world * T rows with capacity Tcap
     if (T < 1 || world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || Tcap < 0 || Tcap > kTcapMax ||
         T * world > Tcap)
         return cudaErrorInvalidValue;
+    // every set of every home rank's result buffer holds the T*8 slot rows
+    if (dst_capacity_rows < int64_t(T) * kTop) return cudaErrorInvalidValue;
     const Workspace w = workspace_layout(Tcap);
     if (bytes < w.bytes || !workspace || !ids_i32 || !dst_rows || !signals || !epoch_u32 || !counter_u32 ||
         !flags || !p2p_aligned(workspace, 256) || !p2p_aligned(ids_i32, 4) || !p2p_aligned(epoch_u32, 4) ||
@@ -534,7 +562,7 @@ extern "C" cudaError_t ornith_moe_b200_ep_wait_epoch(const void* signals_u32, in
     NvtxRange range("ornith.ep.wait");
     count_launches(1);
     ep_wait_epoch_kernel<<<1, 32, 0, stream>>>(static_cast<const uint32_t*>(signals_u32), world, me,
-                                               static_cast<const uint32_t*>(epoch_u32),
+                                               static_cast<const uint32_t*>(epoch_u32), g_peer_wait_ns.load(),
                                                static_cast<uint32_t*>(flags));
     return cudaGetLastError();
 }
@@ -548,6 +576,14 @@ extern "C" cudaError_t ornith_moe_b200_ep_wait_signals(const void* signals_u32, 
     NvtxRange range("ornith.ep.wait");
     count_launches(1);
     ep_wait_signals_kernel<<<1, 32, 0, stream>>>(static_cast<const uint32_t*>(signals_u32), world, me, epoch,
-                                                 static_cast<uint32_t*>(flags));
+                                                 g_peer_wait_ns.load(), static_cast<uint32_t*>(flags));
     return cudaGetLastError();
 }
+
+extern "C" cudaError_t ornith_moe_b200_set_peer_wait_limit_ns(uint64_t limit_ns) {
+    if (limit_ns < kP2PMinWaitNs || limit_ns > kP2PMaxWaitNs) return cudaErrorInvalidValue;
+    g_peer_wait_ns.store(limit_ns);
+    return cudaSuccess;
+}
+
+extern "C" uint64_t ornith_moe_b200_peer_wait_limit_ns(void) { return g_peer_wait_ns.load(); }

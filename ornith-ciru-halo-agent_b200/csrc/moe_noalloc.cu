@@ -22,9 +22,14 @@
 //     callers must order them, for example on one stream;
 //   * the first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress (once per device, with that device current), so
-//     that first call should come before any stream capture.
-// The arithmetic is that of ornith_routed_direct_launch (A8) through the same
-// kernels; only the place of the scratch differs.
+//     that first call should come before any stream capture;
+//   * that address is kept for the life of the process: calls after
+//     cudaDeviceReset, or after the device's primary context was destroyed and
+//     made again, are not supported.
+// The arithmetic is that of ornith_routed_direct_launch (A8) through the
+// fused decode kernel, which this entry always runs (the environment setting
+// that forces the multi-kernel path, and the NVTX layer range, belong to the
+// workspace entry only); only the place of the scratch differs.
 #include <mutex>
 
 #include "../../include/ornith_moe_b200.h"

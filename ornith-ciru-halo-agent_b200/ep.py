@@ -458,8 +458,9 @@ class PeerExchange:
     """This rank's receive buffers for the exchanges over NVLink peer memory,
     shared with the other ranks of the node through CUDA IPC: token rows bf16
     [cap_tokens, 2048] and their local ids int32 [cap_tokens, 8] (dispatch),
-    fp32 result rows [cap_rows, 2048] (return), then two flag arrays of one
-    uint32 per rank (return, dispatch).  Made collectively (every rank at
+    fp32 result rows [cap_rows, 2048] (return), then two flag arrays (return,
+    dispatch) of 2*world uint32 words each: the epoch every rank raised, then
+    its status word (its flag-64 bit).  Made collectively (every rank at
     once); close() collectively before the process group goes away.
 
     dispatch() stores this rank's sent token rows into the expert ranks'
@@ -497,7 +498,7 @@ class PeerExchange:
         def table(offset):
             return (C.c_void_p * world)(*[b + offset for b in bases])
         self.dst_x, self.dst_ids, self.dst_rows = table(self.x_offset), table(self.ids_offset), table(self.rows_offset)
-        self.return_flags, self.dispatch_flags = table(self.flag_offset), table(self.flag_offset + 4 * world)
+        self.return_flags, self.dispatch_flags = table(self.flag_offset), table(self.flag_offset + 8 * world)
         self.x = torch.as_tensor(_DeviceArray(self.base + self.x_offset, (self.cap_tokens, H), '<i2'),
                                  device=device).view(torch.bfloat16)
         self.ids = torch.as_tensor(_DeviceArray(self.base + self.ids_offset, (self.cap_tokens, TOP), '<i4'),
@@ -522,7 +523,7 @@ class PeerExchange:
                                     self.world, self.me, self.epoch, self.counters[0:1], flags)
 
     def wait_dispatch(self, flags):
-        self.native.ep_wait_signals(self.base + self.flag_offset + 4 * self.world, self.world, self.me, self.epoch,
+        self.native.ep_wait_signals(self.base + self.flag_offset + 8 * self.world, self.world, self.me, self.epoch,
                                     flags)
 
     def ret(self, workspace, T, capacity, route_index, back_counts, offsets, flags):
@@ -561,8 +562,9 @@ class PeerFixedExchange:
     """Receive buffers of the fixed-size exchange over NVLink peer memory
     (every rank T tokens), in two sets used by odd and even calls: token rows
     bf16 [2][world*T][2048] and their local ids int32 [2][world*T][8], result
-    rows fp32 [2][T*8][2048], then dispatch and return flags (one uint32 per
-    rank).  The call number is an int32 on the device, so a step holds no
+    rows fp32 [2][T*8][2048], then dispatch and return flag arrays (2*world
+    uint32 words each: epochs, then status words carrying each sender's
+    flag-64 bit).  The call number is an int32 on the device, so a step holds no
     host value that changes between calls and can be captured in a CUDA
     graph.  Made and closed collectively, like PeerExchange."""
 
@@ -597,7 +599,7 @@ class PeerFixedExchange:
         self.dst_x, self.dst_ids = sets(self.x_offset, self.x_set), sets(self.ids_offset, self.ids_set)
         self.dst_rows = sets(self.rows_offset, self.rows_set)
         self.dispatch_flags = (C.c_void_p * world)(*[b + self.flag_offset for b in bases])
-        self.return_flags = (C.c_void_p * world)(*[b + self.flag_offset + 4 * world for b in bases])
+        self.return_flags = (C.c_void_p * world)(*[b + self.flag_offset + 8 * world for b in bases])
         def view(offset, shape, typestr, strides=None):
             return torch.as_tensor(_DeviceArray(self.base + offset, shape, typestr, strides), device=device)
         # both sets of a buffer as one [2, ...] view (byte strides), so that a
@@ -613,9 +615,9 @@ class PeerFixedExchange:
         """0 or 1: the set of the current call, as a device tensor."""
         return (self.epoch & 1).long()
 
-    def dispatch(self, x, local_ids_per_rank):
-        self.native.ep_fixed_dispatch(x, local_ids_per_rank, self.dst_x, self.dst_ids, self.dispatch_flags,
-                                      self.world, self.me, self.epoch, self.counters[0:1])
+    def dispatch(self, x, local_ids_per_rank, flags):
+        self.native.ep_fixed_dispatch(x, local_ids_per_rank, self.dst_x, self.dst_ids, self.world * self.T,
+                                      self.dispatch_flags, self.world, self.me, self.epoch, self.counters[0:1], flags)
 
     def wait_dispatch(self, flags):
         self.native.ep_wait_epoch(self.base + self.flag_offset, self.world, self.me, self.epoch, flags)
@@ -630,11 +632,11 @@ class PeerFixedExchange:
         return x.contiguous(), ids.contiguous()
 
     def ret(self, workspace, capacity, ids_all, flags):
-        self.native.ep_fixed_return(workspace, self.T, capacity, ids_all, self.dst_rows, self.return_flags,
-                                    self.world, self.me, self.epoch, self.counters[1:2], flags)
+        self.native.ep_fixed_return(workspace, self.T, capacity, ids_all, self.dst_rows, self.T * TOP,
+                                    self.return_flags, self.world, self.me, self.epoch, self.counters[1:2], flags)
 
     def wait_return(self, flags):
-        self.native.ep_wait_epoch(self.base + self.flag_offset + 4 * self.world, self.world, self.me, self.epoch,
+        self.native.ep_wait_epoch(self.base + self.flag_offset + 8 * self.world, self.world, self.me, self.epoch,
                                   flags)
 
     def result_index(self, ids):
@@ -782,7 +784,7 @@ class ExpertParallelMoE:
         dest = torch.arange(self.world, device=ids.device, dtype=owner.dtype).view(-1, 1, 1)
         local = torch.where(owner.unsqueeze(0) == dest, lid.unsqueeze(0), torch.full_like(lid, -1).unsqueeze(0))
         pf = self.peer_fixed
-        pf.dispatch(x.contiguous(), local.to(torch.int32).contiguous())
+        pf.dispatch(x.contiguous(), local.to(torch.int32).contiguous(), self.flags)
         pf.wait_dispatch(self.flags)
         x_all, ids_all = pf.received()
         self._layer(x_all, ids_all)

@@ -98,11 +98,14 @@ SIGNATURES = {
                                          C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int64,
                                          C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p,
                                          C.c_void_p], C.c_int),
-    'ornith_moe_b200_ep_fixed_dispatch': ([C.c_void_p, C.c_void_p, C.c_int] + [C.POINTER(C.c_void_p)] * 3
-                                          + [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
+    'ornith_moe_b200_ep_fixed_dispatch': ([C.c_void_p, C.c_void_p, C.c_int] + [C.POINTER(C.c_void_p)] * 2
+                                          + [C.c_int64, C.POINTER(C.c_void_p)]
+                                          + [C.c_int, C.c_int] + [C.c_void_p] * 4, C.c_int),
     'ornith_moe_b200_ep_fixed_return': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p]
-                                        + [C.POINTER(C.c_void_p)] * 2 + [C.c_int, C.c_int] + [C.c_void_p] * 4,
-                                        C.c_int),
+                                        + [C.POINTER(C.c_void_p), C.c_int64, C.POINTER(C.c_void_p)]
+                                        + [C.c_int, C.c_int] + [C.c_void_p] * 4, C.c_int),
+    'ornith_moe_b200_set_peer_wait_limit_ns': ([C.c_uint64], C.c_int),
+    'ornith_moe_b200_peer_wait_limit_ns': ([], C.c_uint64),
     'ornith_moe_b200_ep_wait_epoch': ([C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
     'ornith_moe_b200_ep_wait_signals': ([C.c_void_p, C.c_int, C.c_int, C.c_uint32, C.c_void_p, C.c_void_p], C.c_int),
     'ornith_routed_direct_launch_noalloc': ([C.c_void_p] * 9 + [C.c_int, C.c_void_p], C.c_int),
@@ -492,26 +495,39 @@ def ep_dispatch_p2p(x, token_index, local_ids, seg, dst_x, dst_ids, offsets, cap
                                                 ptr(flags), stream(x)), 'expert-parallel peer dispatch')
 
 
-def ep_fixed_dispatch(x, local_ids, dst_x, dst_ids, signals, world, me, epoch, counter):
+def ep_fixed_dispatch(x, local_ids, dst_x, dst_ids, cap_rows, signals, world, me, epoch, counter, flags):
     """Fixed-size dispatch over peer memory: x bf16 [T, 2048] and local_ids
     int32 [world, T, 8] into every rank's receive set of this call (dst_x,
-    dst_ids: ctypes arrays [2 * world]); epoch: the int32 call counter."""
+    dst_ids: ctypes arrays [2 * world], cap_rows rows per set); epoch: the
+    int32 call counter; flags: this rank's flag word, whose timeout bit goes
+    with the epoch."""
     T = x.shape[0]
     if (x.dtype != torch.bfloat16 or x.shape != (T, 2048) or not x.is_contiguous() or local_ids.dtype != torch.int32
             or local_ids.shape != (world, T, 8) or not local_ids.is_contiguous()):
         raise ValueError('ep_fixed_dispatch takes bf16 rows [T, 2048] and INT32 ids [world, T, 8]')
-    check(lib().ornith_moe_b200_ep_fixed_dispatch(ptr(x), ptr(local_ids), T, dst_x, dst_ids, signals, world, me,
-                                                  ptr(epoch), ptr(counter), stream(x)), 'expert-parallel fixed dispatch')
+    check(lib().ornith_moe_b200_ep_fixed_dispatch(ptr(x), ptr(local_ids), T, dst_x, dst_ids, cap_rows, signals,
+                                                  world, me, ptr(epoch), ptr(counter), ptr(flags), stream(x)),
+          'expert-parallel fixed dispatch')
 
 
-def ep_fixed_return(workspace, T, capacity, ids, dst_rows, signals, world, me, epoch, counter, flags):
+def ep_fixed_return(workspace, T, capacity, ids, dst_rows, cap_rows, signals, world, me, epoch, counter, flags):
     """Fixed-size return over peer memory after a layer call on ids int32
-    [world * T, 8] (local ids; -1 where another rank owns the slot)."""
+    [world * T, 8] (local ids; -1 where another rank owns the slot); every
+    set of dst_rows holds cap_rows rows."""
     if ids.dtype != torch.int32 or ids.shape != (world * T, 8) or not ids.is_contiguous():
         raise ValueError('ep_fixed_return takes the INT32 local ids [world * T, 8] of the layer call')
     check(lib().ornith_moe_b200_ep_fixed_return(ptr(workspace), workspace.numel(), T, capacity, ptr(ids), dst_rows,
-                                                signals, world, me, ptr(epoch), ptr(counter), ptr(flags),
+                                                cap_rows, signals, world, me, ptr(epoch), ptr(counter), ptr(flags),
                                                 stream(ids)), 'expert-parallel fixed return')
+
+
+def set_peer_wait_limit_ns(limit_ns):
+    """Limit of the bounded waits on other ranks (ns; 1 s by default)."""
+    check(lib().ornith_moe_b200_set_peer_wait_limit_ns(int(limit_ns)), 'peer wait limit')
+
+
+def peer_wait_limit_ns():
+    return int(lib().ornith_moe_b200_peer_wait_limit_ns())
 
 
 def ep_wait_epoch(signals_address, world, me, epoch, flags):

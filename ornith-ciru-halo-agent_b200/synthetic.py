@@ -144,6 +144,31 @@ def random_routes(rng, T, pad_fraction=0.0, experts=E, bias=None):
     return np.ascontiguousarray(w), np.ascontiguousarray(ids)
 
 
+def hot_routes(rng, T, counts, pad_fraction=0.0, experts=E):
+    """Routes in which chosen experts receive exactly the given numbers of
+    routes (`counts`: {expert: routes}), so that an expert's rows span several
+    128-row tiles of the grouped projection, end one short of, exactly at or
+    one past a tile, or take more routes than there are tokens (the same
+    expert in several slots of one token, which the reference treats as
+    independent routes).  The other slots get random top-8 routes over the
+    remaining experts.  Draw order: random_routes (logits, padding mask), then
+    one permutation of the T*8 (token, slot) positions, whose leading runs go
+    to the hot experts in the order of `counts`."""
+    total = sum(counts.values())
+    if total > T * TOP:
+        raise ValueError(f'{total} hot routes do not fit in {T} tokens x {TOP} slots')
+    bias = np.zeros(experts, np.float32)
+    bias[list(counts)] = -np.inf          # hot experts only where placed below
+    w, ids = random_routes(rng, T, pad_fraction=pad_fraction, experts=experts, bias=bias)
+    flat = ids.reshape(-1)
+    pos = rng.permutation(T * TOP)
+    at = 0
+    for e, c in counts.items():
+        flat[pos[at:at + c]] = e
+        at += c
+    return w, np.ascontiguousarray(flat.reshape(T, TOP))
+
+
 def zipf_bias(rng, experts=E, s=1.2):
     """Per-expert logit bias giving a Zipf(s) load skew: a seeded permutation
     ranks the experts, bias_e = -s*ln(rank_e)."""

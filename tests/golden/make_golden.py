@@ -24,7 +24,8 @@
       synthetic generator, and the sha256 of the regenerated inputs is stored
       so that generator drift is detected.
 
-Usage: python tests/golden/make_golden.py [--reference /path/to/reference] [--only dense|head|digests]
+Usage: python tests/golden/make_golden.py [--reference DIR] [--only dense|head|digests]
+(default reference: ORNITH_REFERENCE, else BASELINE.json's reference_path)
 """
 import argparse
 import hashlib
@@ -153,10 +154,14 @@ def digest(*arrays):
 
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument('--reference', default='/root/reference')
+    parser.add_argument('--reference', default=None,
+                        help='reference checkout (default: ORNITH_REFERENCE, else BASELINE.json reference_path)')
     parser.add_argument('--only', choices=['dense', 'head', 'digests'], default=None)
     args = parser.parse_args()
-    ref = Path(args.reference)
+    from oracle import build_ref
+    ref = Path(args.reference) if args.reference else build_ref.reference_root()
+    if ref is None:
+        raise SystemExit('reference checkout not found: pass --reference or set ORNITH_REFERENCE')
     if args.only in (None, 'dense'):
         write_dense()
     if args.only in (None, 'head'):
@@ -231,6 +236,27 @@ DIGEST_CASES = [
     ('t1120_a4prefill', 53, 1120, 0.05, 'ornith_routed_direct_launch_a4_prefill'),
 ]
 
+# Experts with exactly these route counts: one short of, exactly at and one
+# past a 128-row tile, two tiles, two tiles plus one, and more routes than
+# tokens (duplicates inside tokens).  The grouped projection of the reference
+# splits each expert into 16-row jobs (routed_storage_n32_prefill.h:19-42);
+# the tensor-core path here into 128-row tiles.
+HOT_COUNTS = {3: 127, 40: 128, 77: 129, 128: 256, 200: 257, 255: 1100}
+
+# (name, case seed, T, pad fraction, entry, hot counts) on the seed-1 layer
+HOT_DIGEST_CASES = [
+    ('t300_hot_a8', 54, 300, 0.02, 'ornith_routed_direct_launch', HOT_COUNTS),
+    ('t300_hot_a4', 55, 300, 0.02, 'ornith_routed_direct_launch_a4', HOT_COUNTS),
+]
+
+
+def make_hot_case(S, case_seed, T, pad, counts):
+    """Tokens, then hot routes (synthetic.hot_routes), from one generator."""
+    rng = np.random.default_rng(case_seed)
+    x = S.make_tokens(rng, T)
+    w, ids = S.hot_routes(rng, T, counts, pad_fraction=pad)
+    return x, w, ids
+
 
 def write_digests():
     S = _synthetic()
@@ -239,6 +265,14 @@ def write_digests():
     store = {}
     for name, case_seed, T, pad, entry in DIGEST_CASES:
         x, w, ids = make_case(S, layer, case_seed, T, pad, 0, '')
+        out, _, flags, st = O.ref_routed(x, w, ids, *banks, entry=entry)
+        assert st == 0, (name, st)
+        store[f'{name}/inputs_sha256'] = np.array(digest(x, w, ids))
+        store[f'{name}/out_sha256'] = np.array(digest(out))
+        store[f'{name}/flags'] = np.array(flags, np.uint32)
+        print(name, 'flags', flags)
+    for name, case_seed, T, pad, entry, counts in HOT_DIGEST_CASES:
+        x, w, ids = make_hot_case(S, case_seed, T, pad, counts)
         out, _, flags, st = O.ref_routed(x, w, ids, *banks, entry=entry)
         assert st == 0, (name, st)
         store[f'{name}/inputs_sha256'] = np.array(digest(x, w, ids))

@@ -249,20 +249,40 @@ def test_fixed_peer_exchange_validation_without_device_work(native):
     sets = (C.c_void_p * (2 * world))(*[base + ((8 + i) << 28) for i in range(2 * world)])
     sigs = (C.c_void_p * world)(base + (14 << 28), base + (15 << 28))
     d = lib.ornith_moe_b200_ep_fixed_dispatch
-    assert d(x, lids, 0, sets, sets, sigs, world, 0, epoch, counter, None) == INVALID        # T >= 1
-    assert d(x, lids, 4097, sets, sets, sigs, world, 0, epoch, counter, None) == INVALID     # world*T <= 8192
-    assert d(x, lids, 4, sets, sets, sigs, world, 2, epoch, counter, None) == INVALID        # me < world
-    assert d(C.c_void_p(base + 8), lids, 4, sets, sets, sigs, world, 0, epoch, counter, None) == INVALID
+    cap = 8192
+    assert d(x, lids, 0, sets, sets, cap, sigs, world, 0, epoch, counter, flags, None) == INVALID     # T >= 1
+    assert d(x, lids, 4097, sets, sets, cap, sigs, world, 0, epoch, counter, flags, None) == INVALID  # world*T <= 8192
+    assert d(x, lids, 4, sets, sets, cap, sigs, world, 2, epoch, counter, flags, None) == INVALID     # me < world
+    assert d(C.c_void_p(base + 8), lids, 4, sets, sets, cap, sigs, world, 0, epoch, counter, flags,
+             None) == INVALID
     bad = (C.c_void_p * (2 * world))(*[base + ((8 + i) << 28) for i in range(2 * world - 1)], None)
-    assert d(x, lids, 4, bad, sets, sigs, world, 0, epoch, counter, None) == INVALID          # every set, every rank
+    assert d(x, lids, 4, bad, sets, cap, sigs, world, 0, epoch, counter, flags, None) == INVALID  # every set, rank
+    assert d(x, lids, 4, sets, sets, 7, sigs, world, 0, epoch, counter, flags, None) == INVALID   # 8 rows, 7 fit
+    assert d(x, lids, 4, sets, sets, cap, sigs, world, 0, epoch, counter, None, None) == INVALID  # flags needed
     r = lib.ornith_moe_b200_ep_fixed_return
     nb = native.get_layout(16).workspace_bytes
-    assert r(ws, nb, 9, 16, lids, sets, sigs, world, 0, epoch, counter, flags, None) == INVALID   # world*T > Tcap
-    assert r(ws, nb - 1, 8, 16, lids, sets, sigs, world, 0, epoch, counter, flags, None) == INVALID
-    assert r(ws, nb, 8, 16, lids, bad, sigs, world, 0, epoch, counter, flags, None) == INVALID
-    assert r(ws, nb, 8, 16, lids, sets, (C.c_void_p * world)(base, None), world, 0, epoch, counter, flags,
+    assert r(ws, nb, 9, 16, lids, sets, cap, sigs, world, 0, epoch, counter, flags, None) == INVALID  # world*T > Tcap
+    assert r(ws, nb - 1, 8, 16, lids, sets, cap, sigs, world, 0, epoch, counter, flags, None) == INVALID
+    assert r(ws, nb, 8, 16, lids, bad, cap, sigs, world, 0, epoch, counter, flags, None) == INVALID
+    assert r(ws, nb, 8, 16, lids, sets, 63, sigs, world, 0, epoch, counter, flags, None) == INVALID  # 64 slot rows
+    assert r(ws, nb, 8, 16, lids, sets, cap, (C.c_void_p * world)(base, None), world, 0, epoch, counter, flags,
              None) == INVALID                                                               # a peer's flags
     w = lib.ornith_moe_b200_ep_wait_epoch
     assert w(sigs[0], 9, 0, epoch, flags, None) == INVALID
     assert w(None, 2, 0, epoch, flags, None) == INVALID
     assert w(sigs[0], 1, 0, epoch, flags, None) == 0          # one rank: nothing to wait for
+
+
+def test_peer_wait_limit_setting(native):
+    """The limit of the waits on other ranks is a library setting: 1 s by
+    default, 1 us .. 60 s accepted, anything else refused unchanged."""
+    assert native.peer_wait_limit_ns() == 1_000_000_000
+    lib = native.lib()
+    try:
+        assert lib.ornith_moe_b200_set_peer_wait_limit_ns(999) == INVALID
+        assert lib.ornith_moe_b200_set_peer_wait_limit_ns(60_000_000_001) == INVALID
+        assert native.peer_wait_limit_ns() == 1_000_000_000
+        native.set_peer_wait_limit_ns(5_000_000)
+        assert native.peer_wait_limit_ns() == 5_000_000
+    finally:
+        native.set_peer_wait_limit_ns(1_000_000_000)

@@ -188,3 +188,19 @@ def test_oracle_matches_reference_digests_at_larger_batches(layer1, make_golden,
         out, _, flags = O.routed_layer(x, w, ids, *banks, a8=a8)
         assert make_golden.digest(out) == str(digests[f'{name}/out_sha256']), name
         assert flags == int(digests[f'{name}/flags']), name
+
+
+def test_oracle_matches_reference_digests_with_hot_experts(layer1, make_golden, S, O):
+    """T = 300 with experts that hold 127, 128, 129, 256, 257 and 1,100 routes
+    (the reference's grouped projection splits them into 16-row jobs): the
+    oracle's outputs hash to the compiled reference's, A8 and A4."""
+    digests = np.load(Path(__file__).resolve().parent / 'golden' / 'routed_reference_digests.npz')
+    banks = (layer1.gate_codes, layer1.gate_meta, layer1.down_codes, layer1.down_meta)
+    for name, seed, T, pad, entry, counts in make_golden.HOT_DIGEST_CASES:
+        x, w, ids = make_golden.make_hot_case(S, seed, T, pad, counts)
+        assert make_golden.digest(x, w, ids) == str(digests[f'{name}/inputs_sha256']), name
+        for e, c in counts.items():
+            assert int((ids == e).sum()) == c
+        out, _, flags = O.routed_layer(x, w, ids, *banks, a8=entry == 'ornith_routed_direct_launch')
+        assert make_golden.digest(out) == str(digests[f'{name}/out_sha256']), name
+        assert flags == int(digests[f'{name}/flags']), name

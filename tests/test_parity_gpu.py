@@ -472,3 +472,97 @@ def test_config1_from_hidden(native, golden, S):
     got_top = np.argsort(-got, axis=1, kind='stable')[:, :8]
     np.testing.assert_array_equal(np.sort(got_top, axis=1), np.sort(ref_top, axis=1))
     np.testing.assert_array_equal(host_bits(out_h), host_bits(out_l))
+
+
+# Route counts per chosen expert for the multi-tile cases: one short of, at
+# and one past a 128-row tile, two tiles and two tiles plus one, more routes
+# than tokens at T = 300 (duplicates inside tokens), and at 8192 an expert
+# with 16 tiles and one with a single route.
+HOT_BY_T = {
+    300: None,   # make_golden.HOT_COUNTS, pinned by a reference digest below
+    1120: {3: 127, 40: 128, 77: 129, 128: 256, 200: 257, 255: 1100, 9: 1},
+    8192: {3: 127, 40: 128, 77: 129, 128: 256, 200: 257, 255: 1100, 17: 2048, 9: 1},
+}
+
+
+def hot_token_sample(rng, ids, counts, per_expert=24, extra=48):
+    """Tokens to check against the oracle: for each hot expert its first and
+    last token and up to `per_expert` others, plus `extra` random tokens."""
+    T = ids.shape[0]
+    pick = set(rng.choice(T, min(extra, T), replace=False).tolist())
+    for e in counts:
+        toks = np.flatnonzero((ids == e).any(axis=1))
+        pick.update([int(toks[0]), int(toks[-1])])
+        pick.update(rng.choice(toks, min(per_expert, toks.size), replace=False).tolist())
+    return np.array(sorted(pick))
+
+
+@pytest.mark.parametrize('T', [300, 1120, 8192])
+@pytest.mark.parametrize('a8', [True, False])
+def test_hot_experts_span_several_tiles(native, layer1, bank1, S, O, make_golden, T, a8):
+    """Experts whose routes fill several 128-row tiles of the tensor-core path
+    (tile tails, the per-expert tile lists and the row positions past the
+    first tile): the sampled tokens, every hot expert's first and last token
+    among them, equal the oracle bit for bit.  At T = 300 every token is
+    checked."""
+    counts = HOT_BY_T[T] or make_golden.HOT_COUNTS
+    rng = np.random.default_rng(8000 + T + (1 if a8 else 0))
+    x = S.make_tokens(rng, T)
+    w, ids = S.hot_routes(rng, T, counts, pad_fraction=0.02)
+    for e, c in counts.items():
+        assert int((ids == e).sum()) == c
+    symbol = 'ornith_routed_direct_launch' if a8 else 'ornith_routed_direct_launch_a4'
+    out, _, flags = run_entry(native, symbol, x, w, ids, bank1)
+    pick = np.arange(T) if T <= 300 else hot_token_sample(rng, ids, counts)
+    ref, _, ref_flags = O.routed_layer(x[pick], w[pick], ids[pick], *bank1.np_routed, a8=a8)
+    np.testing.assert_array_equal(out[pick], ref)
+    assert flags == ref_flags == 0
+
+
+@pytest.mark.parametrize('entry_name', ['digest', 'hot_digest'])
+def test_larger_batches_match_reference_digests(native, layer1, bank1, S, make_golden, entry_name):
+    """The CUDA outputs hash to the digests of the compiled reference's own
+    outputs: T = 32 (A8), 64 (A4), 1120 (A4 prefill) and the two T = 300
+    hot-expert cases whose experts span one to nine 128-row tiles."""
+    from pathlib import Path
+    digests = np.load(Path(__file__).resolve().parent / 'golden' / 'routed_reference_digests.npz')
+    if entry_name == 'digest':
+        cases = [(name, make_golden.make_case(S, layer1, seed, T, pad, 0, ''), entry)
+                 for name, seed, T, pad, entry in make_golden.DIGEST_CASES]
+    else:
+        cases = [(name, make_golden.make_hot_case(S, seed, T, pad, counts), entry)
+                 for name, seed, T, pad, entry, counts in make_golden.HOT_DIGEST_CASES]
+    for name, (x, w, ids), entry in cases:
+        assert make_golden.digest(x, w, ids) == str(digests[f'{name}/inputs_sha256']), name
+        out, _, flags = run_entry(native, entry, x, w, ids, bank1)
+        assert make_golden.digest(out) == str(digests[f'{name}/out_sha256']), name
+        assert flags == int(digests[f'{name}/flags']), name
+
+
+@pytest.mark.parametrize('path', ['a4_prefill', 'from_logits'])
+def test_prefill_8192_sampled_tokens(native, layer1, bank1, S, O, path):
+    """The headline prefill size: 8192 tokens (about 256 routes per expert, so
+    every expert spans two or more 128-row tiles), A4, through the reference's
+    A4-prefill entry and through the from-logits operator the benchmark
+    calls (device top-8 included); 64 sampled tokens against the oracle."""
+    rng = np.random.default_rng(8192)
+    T = 8192
+    x = S.make_tokens(rng, T)
+    logits = rng.standard_normal((T, 256)).astype(np.float32)
+    w, ids = O.route_topk(logits)
+    if path == 'a4_prefill':
+        out, _, flags = run_entry(native, 'ornith_routed_direct_launch_a4_prefill', x, w, ids, bank1)
+    else:
+        ws = torch.empty(native.workspace_bytes(T), dtype=torch.uint8, device=DEV)
+        o = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+        fl = torch.zeros(1, dtype=torch.int32, device=DEV)
+        native.routed_from_logits(dev(x), dev(logits), *bank1.routed, None, None, None, None, None, None, None,
+                                  ws, o, None, fl, T, 4)
+        torch.cuda.synchronize()
+        out, flags = host_bits(o), int(fl.item())
+        del ws
+    assert np.bincount(ids.reshape(-1), minlength=256).min() > 128
+    pick = np.sort(rng.choice(T, 64, replace=False))
+    ref, _, ref_flags = O.routed_layer(x[pick], w[pick], ids[pick], *bank1.np_routed, a8=False)
+    np.testing.assert_array_equal(out[pick], ref)
+    assert flags == 0 == ref_flags
