@@ -55,6 +55,8 @@ NCU_TRAFFIC = {
 }
 # int8 multiply-accumulates per valid route of one layer: gate/up 1024x2048 + down 2048x512
 MACS_PER_ROUTE = 3_145_728
+# workloads measured in the same process as the default decode B=1 line
+SUB_CONFIGS = {'decode1': ['decode32', 'prefill1120', 'prefill8192']}
 
 CONFIGS = {
     'decode1': dict(T=1, layers=40, bias=0.0, act_bits=8, shared=True, name='decode B=1, 40-layer stack (configs[1])'),
@@ -87,7 +89,12 @@ def parse():
     p.add_argument('--steps', type=int, default=20)
     p.add_argument('--warmup', type=int, default=5)
     p.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    p.add_argument('--config', default='decode1', choices=sorted(CONFIGS))
+    p.add_argument('--config', default=None, choices=sorted(CONFIGS),
+                   help='workload (default: decode1 as a plain process; ep_prefill8192 under torch.distributed.run, '
+                        'any world size)')
+    p.add_argument('--no-sub', action='store_true',
+                   help='only the named workload (the decode1 line otherwise also measures decode32, prefill1120 '
+                        'and prefill8192 as sub_results)')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--cpu-seconds', type=float, default=12.0)
     p.add_argument('--no-graph', action='store_true', help='time eager launches instead of a captured step')
@@ -105,7 +112,15 @@ def parse():
                    help='compact expert-parallel exchange in this many pipelined token chunks (exact combine)')
     p.add_argument('--layers', type=int, default=None,
                    help='override the layer count (small cases for profiler captures)')
-    return p.parse_args()
+    args = p.parse_args()
+    if args.config is None:
+        args.config = 'ep_prefill8192' if under_torchrun() else 'decode1'
+    return args
+
+
+def under_torchrun():
+    """True when torch.distributed.run (torchrun) launched this process."""
+    return 'TORCHELASTIC_RUN_ID' in os.environ or 'LOCAL_WORLD_SIZE' in os.environ
 
 
 # ---------------------------------------------------------------------------
@@ -191,9 +206,12 @@ class Stack:
 
 
 def run_ep(args):
-    """Expert-parallel step: every rank routes its share of the tokens and runs
-    each layer through ornith_b200.ep (NCCL all-to-all dispatch, local experts,
-    return of the fp32 per-slot rows, slot-ordered combine)."""
+    """Expert-parallel step: the total token count is
+    fixed and split over the ranks; every rank routes its tokens (device
+    top-8 from its router logits) and runs each layer through ornith_b200.ep
+    (dispatch to the expert ranks, local experts, return, slot-ordered
+    combine on the home rank).  Under torch.distributed.run this is the
+    default workload at every world size, one included."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -214,6 +232,7 @@ def run_ep(args):
     native = importlib.import_module('ornith_b200.native')
     ep = importlib.import_module('ornith_b200.ep')
     S = importlib.import_module('ornith_b200.synthetic')
+    lib = native.lib()
     T_total, L, bits = cfg['T'], cfg['layers'], cfg['act_bits']
     T = T_total // world
     epr = 256 // world
@@ -240,14 +259,33 @@ def run_ep(args):
     x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
     w = torch.empty((L, T, 8), dtype=torch.float32, device=dev)
     ids = torch.empty((L, T, 8), dtype=torch.int32, device=dev)
-    flags = torch.zeros(1, dtype=torch.int32, device=dev)
-    for l in range(L):
-        native.route_topk(logits[l], w[l], ids[l], flags)
+    rflags = torch.zeros(1, dtype=torch.int32, device=dev)
+    outs = [None]
 
     def step():
         for l in range(L):
-            layers[l](x, ids[l], w[l])
+            native.route_topk(logits[l], w[l], ids[l], rflags)   # routing is part of the layer
+            outs[0] = layers[l](x, ids[l], w[l])
 
+    # NVLink bytes this rank sends per step: a token row (4,096 B) per (token,
+    # remote expert rank), an fp32 result row (8,192 B) per (token, slot) whose
+    # expert lives on another rank; summed over the ranks
+    step()
+    torch.cuda.synchronize()
+    owner = placement.rank[ids.clamp_min(0).long()]
+    valid = ids >= 0
+    home = torch.full_like(owner, rank)
+    remote_slot = valid & (owner != home)
+    remote_rank_tok = torch.zeros((L, T, world), dtype=torch.bool, device=dev)
+    remote_rank_tok.scatter_(2, owner.masked_fill(~remote_slot, rank), remote_slot)
+    remote_rank_tok[:, :, rank] = False
+    nv = torch.tensor([float(remote_rank_tok.sum()) * 4096 + float(remote_slot.sum()) * 8192,
+                       float(valid.sum())], device=dev, dtype=torch.float64)
+    nv_max = nv.clone()
+    if world > 1:
+        dist.all_reduce(nv, op=dist.ReduceOp.SUM)
+        dist.all_reduce(nv_max, op=dist.ReduceOp.MAX)
+    nvlink_step, routes_step, nvlink_rank_max = float(nv[0]), float(nv[1]), float(nv_max[0])
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -269,23 +307,75 @@ def run_ep(args):
         dist.barrier()
         graph.replay()
         torch.cuda.synchronize()
-        step = graph.replay
+    run_step = graph.replay if graph is not None else step
+    n0 = lib.ornith_moe_b200_kernel_launches()
     dist.barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record()
         for _ in range(args.steps):
-            step()
+            run_step()
         e1.record()
         torch.cuda.synchronize()
+    launches = lib.ornith_moe_b200_kernel_launches() - n0
+    if graph is not None:
+        launches = launches_per_step(lib, step) * args.steps
     ms = e0.elapsed_time(e1)
-    t = torch.tensor([ms], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX) if world > 1 else None
-    ms = float(t.item())
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = max_over_ranks(ms)
+    ms_step = ms / args.steps
     value = T_total * args.steps / (ms / 1e3)
+    # end to end: each rank's token rows and router logits copied in from
+    # pinned host memory, the last layer's output copied out, every step
+    pin_x = x.cpu().pin_memory()
+    pin_logits = logits.cpu().pin_memory()
+    pin_out = torch.empty((T, 2048), dtype=torch.bfloat16).pin_memory()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        x.copy_(pin_x, non_blocking=True)
+        logits.copy_(pin_logits, non_blocking=True)
+        run_step()
+        pin_out.copy_(outs[0], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    flags_max = int(max_over_ranks(float(max(rflags.item(), max(int(ly.flags.item()) for ly in layers)))))
+    ops_step = 2.0 * routes_step * MACS_PER_ROUTE
+    bytes_step = L * 256 * EXPERT_BYTES + 2 * L * T_total * 4096
+    tops = ops_step / (ms_step * 1e-3) / 1e12
+    hbm_gbs = bytes_step / (ms_step * 1e-3) / 1e9
+    if cfg['T'] > 64:
+        dense = measure_dense_peaks(torch, dev, seconds=1.0) if rank == 0 else {}
+        tpeak = max(dense.get('int8_tops', 0.0), dense.get('fp8_tflops', 0.0)) or 2 * peaks.get('bf16_tflops', 1590.0)
+        roofline = {'bound': 'tensor', 'achieved': round(tops, 1), 'peak': round(tpeak * world, 1), 'unit': 'TOP/s',
+                    'frac': round(tops / (tpeak * world), 4), 'algorithmic_ops_per_step': ops_step,
+                    'peak_source': 'world x rank 0 int8/fp8 dense burst, measured in line (of measured)',
+                    'dense_tensor_peaks_rank0': dense}
+    else:
+        hpeak = peaks.get('hbm_gbs', 6650.0)
+        roofline = {'bound': 'hbm', 'achieved': round(hbm_gbs, 1), 'peak': round(hpeak * world, 1), 'unit': 'GB/s',
+                    'frac': round(hbm_gbs / (hpeak * world), 4), 'algorithmic_bytes_per_step': bytes_step,
+                    'peak_source': 'world x MEASURED_PEAKS.json hbm_gbs (of measured)'}
+    roofline.update({
+        'traffic': None, 'kernel': 'whole expert-parallel step, max over ranks',
+        'nvlink': {'bytes_per_layer_all_ranks': round(nvlink_step / L), 'bytes_per_layer_max_rank':
+                   round(nvlink_rank_max / L), 'peak_gbs_per_rank': 770.0,
+                   'bound_ms_per_step': round(nvlink_rank_max / 770e9 * 1e3, 4),
+                   'peak_source': 'measured peer copy 770 GB/s per direction per GPU (profiling recipe)'}})
     result = {
         'metric': METRIC, 'value': round(value, 3), 'unit': 'tokens/s', 'n_gpus': world, 'steps': args.steps,
-        'warmup': args.warmup, 'ms_per_step': round(ms / args.steps, 4), 'higher_is_better': True,
+        'warmup': args.warmup, 'ms_per_step': round(ms_step, 4), 'higher_is_better': True,
         'scaling': 'strong', 'vs_baseline': None, 'dtype': 'int8',
         'data': 'synthetic (seeded random-init weights and logits of the configured shapes)',
         'config': {'workload': cfg['name'], 'tokens_per_step': T_total, 'tokens_per_rank': T, 'layers': L,
@@ -304,16 +394,25 @@ def run_ep(args):
                                                      'rows as NVLink peer stores'}[(cfg['exchange'],
                                                                                     args.ep_transport)]),
                    'chunks': args.ep_chunks if cfg['exchange'] == 'compact' else 1,
-                   'transport': 'NVLink peer stores' if args.ep_transport == 'p2p' else 'NCCL'},
-        'flags': int(flags.item()), 'clocks': clk.summary(), 'cuda_graph': graph is not None,
+                   'transport': 'NVLink peer stores' if args.ep_transport == 'p2p' else 'NCCL',
+                   'routing': 'device top-8 of each rank\'s router logits inside the step',
+                   'single_gpu_line_differs': 'the plain-process line (BASELINE run) is decode B=1; '
+                                             'this expert-parallel workload is what torchrun runs at every N'},
+        'e2e': {'value': round(T_total * args.steps / (e2e_ms / 1e3), 3), 'unit': 'tokens/s',
+                'h2d_bytes_per_step': T * 4096 + L * T * 1024, 'd2h_bytes_per_step': T * 4096,
+                'per': 'rank (every rank copies its own rows; time = max over ranks)'},
+        'gpu_launches': int(launches), 'roofline': roofline,
+        'flags_max': flags_max, 'clocks': clk.summary(), 'cuda_graph': graph is not None,
     }
     dist.barrier()
-    step = None
+    step = run_step = None
     graph = None  # a graph holding NCCL calls is released before the process group
     torch.cuda.synchronize()
     for layer in layers:
         layer.close()   # peer-memory buffers, collectively
     dist.destroy_process_group()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result['cpu_baseline'] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -582,28 +681,69 @@ def e2e_pipelined(torch, steps, pin_x, pin_logits, x_static, static_logits, out_
     torch.cuda.synchronize()   # the staging buffers are released when this returns
 
 
-def run(args):
-    import torch
-    import torch.distributed as dist
-    cfg = dict(CONFIGS[args.config])
-    if args.layers:
-        cfg['layers'] = args.layers
-    world = int(os.environ.get('WORLD_SIZE', '1'))
-    rank = int(os.environ.get('RANK', '0'))
-    local = int(os.environ.get('LOCAL_RANK', '0'))
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group('nccl', timeout=__import__('datetime').timedelta(seconds=120))
-    dev = torch.device('cuda', local)
-    torch.cuda.set_device(dev)
-    graft.load_package()
-    import importlib
-    native = importlib.import_module('ornith_b200.native')
-    lib = native.lib()
+def measure_dense_peaks(torch, dev, seconds=2.0):
+    """Dense int8 and fp8 tensor-core rates of this GPU, measured in line:
+    torch._int_mm (int8 x int8 -> int32) and torch._scaled_mm (fp8 e4m3 ->
+    bf16), both 8192^3 (2 * 8192^3 operations per call), as the best of ten
+    calls (burst) and over `seconds` of back-to-back calls (sustained).  The
+    prefill roofline uses the higher of the two burst figures as its peak."""
+    n = 8192
+    out = {}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+
+    def rate(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        best = float('inf')
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        calls = max(1, int(seconds / (best * 1e-3)))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(calls):
+            fn()
+        e1.record()
+        e1.synchronize()
+        ops = 2.0 * n ** 3
+        return round(ops / (best * 1e-3) / 1e12, 1), round(ops * calls / (e0.elapsed_time(e1) * 1e-3) / 1e12, 1)
+
+    try:
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=gen)
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev, generator=gen).t()
+        out['int8_tops'], out['int8_tops_sustained'] = rate(lambda: torch._int_mm(a, b))
+        del a, b
+    except Exception as exc:  # no int8 GEMM on this build: the fp8 figure stands alone
+        out['int8_error'] = repr(exc)[:120]
+    try:
+        a = torch.randn((n, n), device=dev, generator=gen).to(torch.float8_e4m3fn)
+        b = torch.randn((n, n), device=dev, generator=gen).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=dev)
+        out['fp8_tflops'], out['fp8_tflops_sustained'] = rate(
+            lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16))
+        del a, b
+    except Exception as exc:
+        out['fp8_error'] = repr(exc)[:120]
+    torch.cuda.empty_cache()
+    out['how'] = ('torch._int_mm int8 and torch._scaled_mm fp8 e4m3, 8192^3: best of 10 calls (burst), '
+                  f'{seconds:.0f} s back to back (sustained)')
+    return out
+
+
+def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense_peaks):
+    """One workload (a CONFIGS entry) on the resident 40-layer stack: W
+    warm-up steps, K timed steps of a captured CUDA graph (router logits of
+    each step copied in first), then the same steps end to end with pinned
+    host inputs copied in and the output copied out inside the timed region.
+    Returns the workload's part of the JSON line."""
     T, L, bits = cfg['T'], cfg['layers'], cfg['act_bits']
-    stack = Stack(torch, cfg, dev, seed=1234 + rank)
     steps_total = args.warmup + args.steps
-    # router logits per (step, layer): N(0,1) (+ per-layer per-expert bias)
     bias = (cfg['bias'] * torch.randn((L, 256), device=dev, generator=stack.gen)) if cfg['bias'] else None
     n_logit_sets = steps_total if T <= 64 else 1
     logits = torch.randn((n_logit_sets, L, T, 256), device=dev, generator=stack.gen)
@@ -614,9 +754,10 @@ def run(args):
     outs = [torch.empty((T, 2048), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     shared_out = torch.empty((T, 2048), dtype=torch.bfloat16, device=dev) if cfg['shared'] else None
     flags = torch.zeros(L, dtype=torch.int32, device=dev)
+    L_stack = len(stack.layers)
 
     def layer_call(l, x, lg, out):
-        (gc, gm), (dc, dm), (sgc, sgm), (sdc, sdm), gw = stack.layers[l]
+        (gc, gm), (dc, dm), (sgc, sgm), (sdc, sdm), gw = stack.layers[l % L_stack]
         if cfg['shared']:
             native.routed_from_logits(x, lg, gc, gm, dc, dm, sgc, sgm, sdc, sdm, gw, stack.silu, stack.sigmoid,
                                       ws, out, shared_out, flags[l:l + 1], T, bits)
@@ -624,7 +765,6 @@ def run(args):
             native.routed_from_logits(x, lg, gc, gm, dc, dm, None, None, None, None, None, None, None,
                                       ws, out, None, flags[l:l + 1], T, bits)
 
-    # static inputs: a step reads its token rows and router logits from these
     static_logits = logits[0].clone()
     x_static = x0
 
@@ -643,6 +783,7 @@ def run(args):
         for l in range(L):
             d += int(torch.unique(ids[s, l]).numel()) + (1 if cfg['shared'] else 0)
         distinct.append(d)
+    del ids
     act_bytes = L * (2 * T * 4096 + T * 1024)
 
     def step_bytes(s):
@@ -652,12 +793,7 @@ def run(args):
         stage_inputs(s)
         step_static()
     torch.cuda.synchronize()
-
-    # Decode steps are captured once as a CUDA graph and replayed (the way a
-    # serving engine runs decode); the layer calls inside are the same C-ABI
-    # launches.  Each replay is preceded by a device copy of that step's logits.
     graph, graph_error = None, None
-    layer_graphs = []
     if not args.no_graph:
         try:
             side = torch.cuda.Stream()
@@ -669,14 +805,9 @@ def run(args):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 step_static()
-            for l in range(L):
-                g1 = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g1):
-                    layer_call(l, x_static, static_logits[l], outs[l % 2])
-                layer_graphs.append(g1)
             torch.cuda.synchronize()
         except Exception as exc:  # capture unsupported: time the eager launches instead
-            graph, layer_graphs, graph_error = None, [], repr(exc)[:200]
+            graph, graph_error = None, repr(exc)[:200]
             torch.cuda.synchronize()
 
     def run_step(s):
@@ -689,74 +820,47 @@ def run(args):
     for s in range(args.warmup):
         run_step(s)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     launches0 = lib.ornith_moe_b200_kernel_launches()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev.index) as clk:
         start.record()
         for s in range(args.warmup, steps_total):
             run_step(s)
         end.record()
         torch.cuda.synchronize()
-    # kernels of this library enqueued per step (graph replays re-run the captured launches)
-    launches = (lib.ornith_moe_b200_kernel_launches() - launches0) if graph is None else \
-        launches_per_step(lib, step_static) * args.steps
+    per_step_launches = launches_per_step(lib, step_static)
+    launches = (lib.ornith_moe_b200_kernel_launches() - launches0) if graph is None else per_step_launches * args.steps
     ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
     ms_step = ms / args.steps
-    value = world * T * args.steps / (ms / 1e3)
-    bytes_timed = sum(step_bytes(s) for s in range(args.warmup, steps_total)) / args.steps
-
-    # per-layer timing: each layer call (routing + fused layer kernel) replayed
-    # as its own graph between events, layers in sequence so that weights stream
-    # from HBM as in a step
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
-    per_layer = []
-    for rep in range(3):
-        stage_inputs(args.warmup + rep)
-        for l in range(L):
-            ev[l][0].record()
-            if layer_graphs:
-                layer_graphs[l].replay()
-            else:
-                layer_call(l, x_static, static_logits[l], outs[l % 2])
-            ev[l][1].record()
-        torch.cuda.synchronize()
-        per_layer += [a.elapsed_time(b) for a, b in ev]
-    layer_ms = statistics.mean(per_layer)
-    layer_bytes = bytes_timed / L
-    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
-    peak = peaks.get('hbm_gbs', 6650.0)
-    achieved = layer_bytes / (layer_ms * 1e-3) / 1e9
-    traffic = NCU_TRAFFIC.get(args.config)
-    hbm_roofline = {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
-                    'frac': round(achieved / peak, 4), 'traffic': traffic['bytes'] if traffic else None,
-                    'kernel': 'one routed_from_logits layer call (all its kernels)',
-                    'algorithmic_bytes_per_launch': int(layer_bytes), 'launch_ms': round(layer_ms, 5),
-                    'peak_source': 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s'}
+    value = T * args.steps / (ms / 1e3)
+    bytes_step = sum(step_bytes(s) for s in range(args.warmup, steps_total)) / args.steps
+    hbm_peak = peaks.get('hbm_gbs', 6650.0)
+    peak_src = 'MEASURED_PEAKS.json hbm_gbs (of measured)' if peaks else 'fallback 6650 GB/s (of fallback)'
+    gbs = bytes_step / (ms_step * 1e-3) / 1e9
+    per_layer_launches = per_step_launches / L
+    hbm = {'bound': 'hbm', 'achieved': round(gbs, 1), 'peak': hbm_peak, 'unit': 'GB/s',
+           'frac': round(gbs / hbm_peak, 4), 'algorithmic_bytes_per_step': int(bytes_step),
+           'kernel': ('the layer kernels back to back in one captured step: '
+                      f'{per_layer_launches:g} launch(es) per layer, {L} layers; achieved = algorithmic bytes '
+                      'of the timed steps over their CUDA-event time'),
+           'launch_ms': round(ms_step / L, 5), 'peak_source': peak_src}
+    traffic = NCU_TRAFFIC.get(cfg['key'])
     if T > 64:
-        # prefill: the grouped int8 GEMMs bound the layer; int8 dense tensor rate is
-        # twice bf16 on B200, and only the bf16 rate is measured on this pool
-        ops = 2.0 * T * 8 * MACS_PER_ROUTE
-        bf16 = peaks.get('bf16_tflops', 1590.0)
-        tops = ops / (layer_ms * 1e-3) / 1e12
-        roofline = {'bound': 'tensor', 'achieved': round(tops, 1), 'peak': round(2 * bf16, 1), 'unit': 'TOP/s',
-                    'frac': round(tops / (2 * bf16), 4), 'traffic': traffic['bytes'] if traffic else None,
-                    'kernel': 'one routed_from_logits layer call (all its kernels)',
-                    'algorithmic_ops_per_launch': ops, 'launch_ms': round(layer_ms, 5),
-                    'peak_source': ('2 x MEASURED_PEAKS.json bf16_tflops (of measured; int8 = 2 x bf16 dense)'
-                                    if peaks else '2 x fallback 1590 TFLOP/s'),
-                    'frac_of_bf16_peak': round(tops / bf16, 4),
-                    'hbm': hbm_roofline}
+        ops_step = 2.0 * L * T * 8 * MACS_PER_ROUTE
+        tops = ops_step / (ms_step * 1e-3) / 1e12
+        tpeak = max(dense_peaks.get('int8_tops', 0.0), dense_peaks.get('fp8_tflops', 0.0))
+        src = 'measured in line: max of int8 / fp8 dense burst (of measured)'
+        if not tpeak:
+            tpeak, src = 2 * peaks.get('bf16_tflops', 1590.0), '2 x bf16 (of measured bf16; no int8/fp8 figure)'
+        roofline = {'bound': 'tensor', 'achieved': round(tops, 1), 'peak': tpeak, 'unit': 'TOP/s',
+                    'frac': round(tops / tpeak, 4), 'algorithmic_ops_per_step': ops_step,
+                    'kernel': hbm['kernel'], 'launch_ms': hbm['launch_ms'], 'peak_source': src,
+                    'hbm': hbm}
     else:
-        roofline = hbm_roofline
+        roofline = hbm
+    roofline['traffic'] = traffic['bytes'] if traffic else None
     if traffic:
-        roofline['traffic_kernel'] = traffic['kernel']
+        roofline['traffic_kernel'] = traffic['kernel'] + ' (per launch, ncu)'
 
     # end to end through the public operator: pinned host inputs copied in, the
     # step (graph of the operator's launches) run, the last output copied out
@@ -764,8 +868,6 @@ def run(args):
     pin_logits = logits[: min(n_logit_sets, 4)].cpu().pin_memory()
     pin_out = torch.empty((T, 2048), dtype=torch.bfloat16).pin_memory()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     replay = graph.replay if graph is not None else step_static
     if args.e2e_overlap:
@@ -781,44 +883,75 @@ def run(args):
         e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
-    flag_any = int(flags.max().item())
-
-    result = {
-        'metric': METRIC, 'value': round(value, 3), 'unit': 'tokens/s', 'n_gpus': world,
-        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms_step, 4),
-        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8',
-        'data': 'synthetic (seeded random-init weights and logits of the configured shapes)',
+    part = {
+        'value': round(value, 3), 'unit': 'tokens/s', 'ms_per_step': round(ms_step, 4),
         'config': {'workload': cfg['name'], 'tokens_per_step': T, 'layers': L, 'experts': 256, 'top_k': 8,
                    'hidden': 2048, 'intermediate': 512, 'shared_expert': cfg['shared'],
                    'weights': 'affine-u4 G256 (scale, offset=-8*scale), N32 storage',
                    'activations': f'A{bits} per 256-group after H128', 'arith': 'u4 x s8 -> int32 dot, fp32 epilogue',
-                   'parallelism': f'replicas x{world}' if world > 1 else 'single GPU',
-                   'l2': f'inputs larger than L2: {bytes_timed / 1e6:.0f} MB of weights read per step'},
-        'e2e': {'value': round(e2e_value, 3), 'unit': 'tokens/s', 'h2d_bytes_per_step': T * 4096 + L * T * 1024,
-                'd2h_bytes_per_step': T * 4096,
+                   'l2': f'inputs larger than L2: {bytes_step / 1e6:.0f} MB of weights read per step'},
+        'e2e': {'value': round(T * args.steps / (e2e_ms / 1e3), 3), 'unit': 'tokens/s',
+                'h2d_bytes_per_step': T * 4096 + L * T * 1024, 'd2h_bytes_per_step': T * 4096,
                 'copies': ('pipelined on copy streams, inside the timed region' if args.e2e_overlap
                            else 'in line with the steps')},
         'gpu_launches': int(launches),
         'roofline': roofline,
-        'step_roofline_frac': round(bytes_timed / (ms_step * 1e-3) / 1e9 / peak, 4),
-        'flags_max': flag_any,
+        'flags_max': int(flags.max().item()),
         'cuda_graph': graph is not None,
         'clocks': clk.summary(),
     }
     if graph_error:
-        result['cuda_graph_error'] = graph_error
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        part['cuda_graph_error'] = graph_error
+    graph = None
+    del ws, logits
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return part
+
+
+def run(args):
+    """Single-GPU workloads of the routed layer: the named config as the line,
+    and (for the default decode B=1 line) decode B=32, prefill 1120 and
+    prefill 8192 measured in the same process on the same resident weights
+    as `sub_results`, each with its own timing, roofline and clocks."""
+    import torch
+    cfg = dict(CONFIGS[args.config], key=args.config)
+    if args.layers:
+        cfg['layers'] = args.layers
+    dev = torch.device('cuda', 0)
+    torch.cuda.set_device(dev)
+    graft.load_package()
+    import importlib
+    native = importlib.import_module('ornith_b200.native')
+    lib = native.lib()
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    subs = [] if (args.no_sub or args.layers) else list(SUB_CONFIGS.get(args.config, []))
+    need_tensor = cfg['T'] > 64 or any(CONFIGS[k]['T'] > 64 for k in subs)
+    dense_peaks = measure_dense_peaks(torch, dev) if need_tensor else {}
+    stack = Stack(torch, cfg, dev, seed=1234)
+    main = measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense_peaks)
+    result = {
+        'metric': METRIC, 'value': main['value'], 'unit': 'tokens/s', 'n_gpus': 1,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': main['ms_per_step'],
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8',
+        'data': 'synthetic (seeded random-init weights and logits of the configured shapes)',
+        'config': dict(main['config'], parallelism='single GPU'),
+        'e2e': main['e2e'], 'gpu_launches': main['gpu_launches'], 'roofline': main['roofline'],
+        'flags_max': main['flags_max'], 'cuda_graph': main['cuda_graph'], 'clocks': main['clocks'],
+    }
+    if 'cuda_graph_error' in main:
+        result['cuda_graph_error'] = main['cuda_graph_error']
+    if subs:
+        result['sub_results'] = {}
+        for key in subs:
+            sub_cfg = dict(CONFIGS[key], key=key)
+            result['sub_results'][key] = measure_layer_config(torch, native, lib, stack, sub_cfg, args, dev, peaks,
+                                                              dense_peaks)
+    if dense_peaks:
+        result['dense_tensor_peaks'] = dense_peaks
+    if not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(cfg, args.cpu_seconds)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(result), flush=True)
+    print(json.dumps(result), flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -876,18 +1009,25 @@ def run_reference(args):
     rng = np.random.default_rng(10)
     T = min(cfg['T'], 16 if cfg['shared'] else 64)
     layers_per_step = 2
+    # inputs drawn before any timing: the timed loop runs only the reference's layer calls
+    pool = []
+    for _ in range(4 * layers_per_step):
+        x = S.make_tokens(rng, T)
+        w, ids = O.route_topk(rng.standard_normal((T, 256)).astype(np.float32))
+        logit = S.f32_to_bf16_bits(rng.standard_normal(T).astype(np.float32))
+        pool.append((x, w, ids, logit))
+    entry = 'ornith_routed_direct_launch' if cfg['act_bits'] == 8 else 'ornith_routed_direct_launch_a4'
+    calls = [0]
 
     def one():
         for _ in range(layers_per_step):
-            x = S.make_tokens(rng, T)
-            w, ids = O.route_topk(rng.standard_normal((T, 256)).astype(np.float32))
+            x, w, ids, logit = pool[calls[0] % len(pool)]
+            calls[0] += 1
             if cfg['shared']:
-                logit = S.f32_to_bf16_bits(rng.standard_normal(T).astype(np.float32))
                 O.ref_routed_shared(x, w, ids, layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta,
                                     layer.sgate_codes, layer.sgate_meta, layer.sdown_codes, layer.sdown_meta, logit,
                                     tab['silu_fp32'], tab['sigmoid_bf16'])
             else:
-                entry = 'ornith_routed_direct_launch' if cfg['act_bits'] == 8 else 'ornith_routed_direct_launch_a4'
                 O.ref_routed(x, w, ids, layer.gate_codes, layer.gate_meta, layer.down_codes, layer.down_meta,
                              entry=entry)
 
@@ -1021,4 +1161,7 @@ if __name__ == '__main__':
     elif CONFIGS[a.config].get('head'):
         run_head(a)
     else:
+        if int(os.environ.get('WORLD_SIZE', '1')) > 1:
+            raise SystemExit(f'--config {a.config} runs on one GPU; the multi-GPU workloads are ep_prefill8192 '
+                             'and ep_decode256')
         run(a)

@@ -40,3 +40,19 @@ def test_reference_arm_line(config, library):
 
 def test_reference_arm_other_ranks_print_nothing():
     assert _run(['--impl', 'reference', '--steps', '1', '--warmup', '0'], {'RANK': '1', 'WORLD_SIZE': '2'}) == []
+
+
+def test_default_workload_follows_the_launcher():
+    """A plain process measures decode B=1; under
+    torch.distributed.run, at any world size, the expert-parallel prefill
+    (configs[4]) is the default, so a scaling run compares one workload."""
+    if not (REF / 'libref_routed_storage_n32.so').exists():
+        pytest.skip('oracle/_ref/libref_routed_storage_n32.so not built')
+    sys.path.insert(0, str(ROOT))
+    import bench
+    plain = json.loads(_run(['--impl', 'reference', '--steps', '1', '--warmup', '0'])[0])
+    assert plain['config']['workload'] == bench.CONFIGS['decode1']['name']
+    launched = json.loads(_run(['--impl', 'reference', '--steps', '1', '--warmup', '0'],
+                               {'TORCHELASTIC_RUN_ID': 'test', 'LOCAL_WORLD_SIZE': '1', 'RANK': '0',
+                                'WORLD_SIZE': '1'})[0])
+    assert launched['config']['workload'] == bench.CONFIGS['ep_prefill8192']['name']
