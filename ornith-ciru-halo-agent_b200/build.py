@@ -15,7 +15,7 @@ LIB = HERE / 'libornith_moe_b200.so'
 # dependent indices outside their buffers raise flag 128 instead of faulting
 DEBUG_LIB = HERE / 'libornith_moe_b200_debug.so'
 DEBUG_FLAGS = ('-DORNITH_DEBUG_BOUNDS=1',)
-SOURCES = ['moe_api.cu', 'moe_generic.cu', 'moe_decode.cu', 'moe_prefill.cu', 'moe_noalloc.cu', 'dense_g256.cu', 'head_i8.cu',
+SOURCES = ['moe_api.cu', 'moe_generic.cu', 'moe_decode.cu', 'moe_decode1.cu', 'moe_prefill.cu', 'moe_noalloc.cu', 'dense_g256.cu', 'head_i8.cu',
            'ep_plan.cu', 'ep_p2p.cu']
 NVCC = os.environ.get('NVCC', '/usr/local/cuda/bin/nvcc')
 FLAGS = ['-gencode', 'arch=compute_100a,code=sm_100a', '-lineinfo', '-O3', '-std=c++17',
@@ -33,10 +33,8 @@ def stale():
 
 def build(force=False, verbose=False, flags=(), out=None):
     """Compile the library.  Extra nvcc flags (the kernels' build-time
-    options: -DORNITH_PREFILL_F32X2=1, -DORNITH_PREFILL_CONV6=1,
-    -DORNITH_DECODE_L2_PREFETCH=1, -DORNITH_DECODE_EARLY_PREFETCH=1,
-    -DORNITH_DENSE_HOISTED_NIBBLES=1, -DORNITH_DECODE_GATE_COST=…,
-    -DORNITH_DECODE_DOWN_COST=…, the trace builds) come from `flags` and
+    options: -DORNITH_DECODE_GATE_COST=…, -DORNITH_DECODE_DOWN_COST=…, the
+    trace builds -DORNITH_DECODE_TRACE / -DORNITH_PREFILL_TRACE) come from `flags` and
     from ORNITH_MOE_B200_NVCC_FLAGS; the default build sets none of them
     (DEBUG_FLAGS make the debug-bounds library).
     `out` writes a variant library elsewhere (always rebuilt), which
@@ -72,6 +70,6 @@ if __name__ == '__main__':
     p = argparse.ArgumentParser(description='build libornith_moe_b200.so for sm_100a')
     p.add_argument('-v', '--verbose', action='store_true', help='print ptxas register and spill counts')
     p.add_argument('--out', default=None, help='write a variant library to this path')
-    p.add_argument('--flag', action='append', default=[], help='extra nvcc flag, e.g. --flag=-DORNITH_PREFILL_F32X2=1')
+    p.add_argument('--flag', action='append', default=[], help='extra nvcc flag, e.g. --flag=-DORNITH_DECODE_GATE_COST=4')
     a = p.parse_args()
     print(build(force=True, verbose=a.verbose, flags=a.flag, out=a.out))

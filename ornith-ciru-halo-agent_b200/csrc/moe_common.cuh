@@ -281,6 +281,28 @@ __device__ __forceinline__ void quantize_group_warp(const float (&t)[8], int lan
     }
 }
 
+// Hadamard + quantise one 256-group held by the warp (lane l: elements
+// 8l..8l+7, as scalars so that nothing goes through local memory).  Writes
+// the permuted int8 codes to q and, from lane 0, the scale and code sum;
+// returns the flags (non-finite values before or after the transform, invalid
+// scale).  Out of line: every activation group of the layer goes through
+// this one copy.
+template <int QMAX>
+__device__ __noinline__ uint32_t wht_quant(float e0, float e1, float e2, float e3, float e4, float e5, float e6,
+                                           float e7, int lane, uint2* q, __half* scale, int32_t* sum) {
+    float e[8] = {e0, e1, e2, e3, e4, e5, e6, e7};
+    uint32_t f = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (!isfinite(e[i])) f |= kFlagNonfiniteInput;
+    wht128_halfwarp(e, lane);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (!isfinite(e[i])) f |= kFlagNonfiniteInput;
+    quantize_group_warp<QMAX>(e, lane, q, scale, sum, f);
+    return f;
+}
+
 // Counter updates between CTAs.  red_release_add publishes the caller's
 // earlier writes (and, after a warp or CTA barrier, those of the threads it
 // synchronised with) without waiting for the update to land;

@@ -354,28 +354,6 @@ __device__ __forceinline__ void stage_dots1_n(int n, const uint32_t* blk, const 
     else stage_dots1<8>(blk, act, lane, dot);
 }
 
-// Hadamard + quantise one 256-group held by the warp (lane l: elements
-// 8l..8l+7, as scalars so that nothing goes through local memory).  Writes
-// the permuted int8 codes to q and, from lane 0, the scale and code sum;
-// returns the flags (non-finite values before or after the transform, invalid
-// scale).  Out of line: every activation group of the layer goes through
-// this one copy.
-template <int QMAX>
-__device__ __noinline__ uint32_t wht_quant(float e0, float e1, float e2, float e3, float e4, float e5, float e6,
-                                           float e7, int lane, uint2* q, __half* scale, int32_t* sum) {
-    float e[8] = {e0, e1, e2, e3, e4, e5, e6, e7};
-    uint32_t f = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        if (!isfinite(e[i])) f |= kFlagNonfiniteInput;
-    wht128_halfwarp(e, lane);
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        if (!isfinite(e[i])) f |= kFlagNonfiniteInput;
-    quantize_group_warp<QMAX>(e, lane, q, scale, sum, f);
-    return f;
-}
-
 // Transform + quantise one 256-group of one token (a dead token's group is
 // all zeros and reports no flags).
 template <int QMAX>
@@ -639,27 +617,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         DECODE_CLOCK(23);
     }
 
-#if ORNITH_DECODE_EARLY_PREFETCH
-    // the shared expert's banks do not depend on routing: CTA b prefetches
-    // slice b of each into L2 before routing starts (see the routed experts'
-    // prefetch after routing below)
-    if (a.shared && tid < 4) {
-        // thread i takes range i: gate codes, gate metadata, down codes, down metadata
-        const uint32_t* range = tid == 0 ? a.sgate_codes : tid == 1 ? a.sgate_meta : tid == 2 ? a.sdown_codes
-                                                                                              : a.sdown_meta;
-        const uint32_t bytes = tid == 0 ? 2u * kI * kH / 2
-                             : tid == 1 ? 2u * kI * (kH / kG) * 4
-                             : tid == 2 ? uint32_t(kH) * kI / 2
-                                        : uint32_t(kH) * (kI / kG) * 4;
-        const uint32_t chunk = ((bytes + uint32_t(G) - 1) / uint32_t(G) + 15u) & ~15u;
-        const uint32_t start = uint32_t(b) * chunk;
-        if (start < bytes)
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
-                             reinterpret_cast<const char*>(range) + start),
-                         "r"(min(chunk, bytes - start))
-                         : "memory");
-    }
-#endif
     // ---- routing (every CTA, identical) -----------------------------------
     if (tid == 0) {
         for (int i = 0; i < nst; ++i) {
@@ -749,44 +706,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
     }
     __syncthreads();
     if (tid == 0) DECODE_TRACE(12);
-#if ORNITH_DECODE_EARLY_PREFETCH
-    // Latency mode: every CTA knows every route here, so the CTAs share an L2
-    // prefetch of the selected experts' banks (four contiguous ranges each:
-    // gate codes 1 MiB, gate metadata 32 KiB, down codes 512 KiB, down
-    // metadata 16 KiB; CTA b takes slice b of every range) that overlaps the
-    // plan; the ring's bulk copies then find the weights in L2.  A prefetch
-    // changes no result.  Built with -DORNITH_DECODE_EARLY_PREFETCH=1 (not the
-    // default build yet: it has not been run on a GPU).
-    if (small && tid < R) {
-        int e = -1;
-        if (tid < R) {
-            e = s.ids[tid];
-            if (!id_valid(e)) e = -1;
-            for (int r = 0; r < tid && e >= 0; ++r)
-                if (s.ids[r] == e) e = -1;  // the first route of an expert prefetches it
-        }  // the shared expert was prefetched at entry
-        if (e >= 0) {
-            const bool sh = e == kE;
-            const char* base[4] = {
-                reinterpret_cast<const char*>(sh ? a.sgate_codes : a.gate_codes + size_t(e) * (2 * kI) * (kH / 8)),
-                reinterpret_cast<const char*>(sh ? a.sgate_meta : a.gate_meta + size_t(e) * (2 * kI) * (kH / kG)),
-                reinterpret_cast<const char*>(sh ? a.sdown_codes : a.down_codes + size_t(e) * kH * (kI / 8)),
-                reinterpret_cast<const char*>(sh ? a.sdown_meta : a.down_meta + size_t(e) * kH * (kI / kG))};
-            const uint32_t bytes[4] = {2u * kI * kH / 2, 2u * kI * (kH / kG) * 4, uint32_t(kH) * kI / 2,
-                                       uint32_t(kH) * (kI / kG) * 4};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t chunk = ((bytes[i] + uint32_t(G) - 1) / uint32_t(G) + 15u) & ~15u;
-                const uint32_t start = uint32_t(b) * chunk;
-                if (start < bytes[i]) {
-                    const uint32_t n = min(chunk, bytes[i] - start);
-                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base[i] + start), "r"(n)
-                                 : "memory");
-                }
-            }
-        }
-    }
-#endif
     if (small) {
         // ---- plan for R <= 32 routes: warp 0 sorts (expert, route) keys -----
         if (warp == 0) {
@@ -992,24 +911,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layer_kernel(const LayerAr
         // its parity is exact.  Every issued stage is recorded per slot for
         // the drain at exit.
         volatile int* misc = s.misc;
-#if ORNITH_DECODE_L2_PREFETCH
-        // Warm L2 with this CTA's down blocks while its gate stages stream, so
-        // that the down stages, issued only after the gate stages landed, read
-        // from L2.  A prefetch changes no result.  Built with
-        // -DORNITH_DECODE_L2_PREFETCH=1 (not the default build yet: it has not
-        // been run on a GPU).
-        for (int d2 = lane; d2 < 2 * nd; d2 += 32) {
-            const int dj = thr ? dj0 + d2 / 2 : jstart + (d2 / 2) * G;
-            const int e = checked(s.act_e[dj / 64], kE + 1, a.flags), tile = dj % 64, g = d2 % 2;
-            const int groups = kI / kG;
-            const uint32_t* codes = e == kE ? a.sdown_codes : a.down_codes + size_t(e) * kH * (kI / 8);
-            const uint32_t* meta = e == kE ? a.sdown_meta : a.down_meta + size_t(e) * kH * groups;
-            codes += (size_t(tile) * groups + g) * 1024;
-            meta += (size_t(tile) * groups + g) * 32;
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(codes), "r"(4096u) : "memory");
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(meta), "r"(128u) : "memory");
-        }
-#endif
         int st0 = 0;
         while (st0 < total_stages) {
             if (st0 == 16 * ng && ng > 0) {
@@ -1633,6 +1534,10 @@ extern "C" __attribute__((visibility("default"))) int ornith_moe_b200_decode_tra
 bool decode_supported(int T) { return T >= 1 && T <= kDecodeMaxT; }
 
 cudaError_t launch_decode(const LayerArgs& a, cudaStream_t stream) {
+    if (a.T == 1) {  // the single-token kernel where the device fits it
+        const cudaError_t s1 = launch_decode_single(a, stream);
+        if (s1 != cudaErrorNotSupported) return s1;
+    }
     int device = 0;
     cudaError_t st = cudaGetDevice(&device);
     if (st != cudaSuccess) return st;

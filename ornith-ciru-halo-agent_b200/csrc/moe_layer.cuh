@@ -43,6 +43,15 @@ constexpr int kCtrlAbort = 1056;       // any CTA gave up a bounded wait
 // 3 = global counter (x = ctrl word, y = target, observed = last value)
 constexpr int kCtrlGiveUp = 1060;
 constexpr int kCtrlClearWords = 1072;  // words zeroed before every fused launch
+// Words of the single-token decode kernel, never cleared: every launch tags
+// its flags with a call number (epoch) read from kCtrlD1Epoch, so stale words
+// of earlier calls never match the current one.  Beyond kCtrlClearWords so
+// that the multi-token kernel's clear does not touch them.
+constexpr int kCtrlD1Epoch = 1088;     // call number of the last completed launch
+constexpr int kCtrlD1Seen = 1104;      // [kD1MaxCtas] a CTA read the epoch of this launch
+constexpr int kD1MaxCtas = 256;
+constexpr int kCtrlD1Gate = kCtrlD1Seen + kD1MaxCtas;  // [9 slots x 16 tile pairs] middle columns stored
+static_assert(kCtrlD1Gate + 9 * 16 <= kCtrlWords, "single-token decode words fit the control block");
 
 Workspace workspace_layout(int Tcap);
 
@@ -184,5 +193,9 @@ constexpr int kDecodeMaxT = 32;
 constexpr int kPlanBlocks = 256;  // most blocks of the prefill routing plan
 bool decode_supported(int T);
 cudaError_t launch_decode(const LayerArgs& a, cudaStream_t stream);
+// Single-token decode kernel (T == 1); returns cudaErrorNotSupported when
+// this device or call does not fit it (the caller then runs launch_decode's
+// multi-token kernel).
+cudaError_t launch_decode_single(const LayerArgs& a, cudaStream_t stream);
 
 }  // namespace ornith

@@ -58,13 +58,10 @@ constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
 constexpr int kEpiWarps = 16;
 constexpr int kEpiFirst = 8;    // epilogue warps 8..23 (warpgroups 2..5)
-// Converter warps 2..5, one per scheduler; built with -DORNITH_PREFILL_CONV6=1
-// (not the default build yet: it has not been run on a GPU) warps 2..7, the
-// two otherwise idle warps of the second setup warpgroup included.
-#ifndef ORNITH_PREFILL_CONV6
-#define ORNITH_PREFILL_CONV6 0
-#endif
-constexpr int kConvWarps = ORNITH_PREFILL_CONV6 ? 6 : 4;
+// Converter warps 2..5, one per scheduler.  Dealing the conversion over warps
+// 2..7 instead was measured slower on a B200 (46.3 against 45.8 ms per
+// 40-layer prefill-8192 step), so the converters are not latency-bound.
+constexpr int kConvWarps = 4;
 // Register split (setmaxnreg, per warpgroup): the two setup warpgroups drop to
 // kRegsSetup, the four epilogue warpgroups rise to kRegsEpi.  The sum must not
 // exceed what the CTA was launched with (kThreads x kRegsLaunch), which the
@@ -153,109 +150,6 @@ __device__ __forceinline__ void tmem_st16_const(uint32_t taddr, uint32_t v) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-#if ORNITH_PREFILL_F32X2
-// Packed fp32 pairs (sm_100 f32x2 arithmetic): two independent IEEE
-// round-to-nearest operations per instruction, the low half first.  Results
-// are those of the scalar __f*_rn forms lane for lane.  Used by the epilogue
-// built with -DORNITH_PREFILL_F32X2=1 (not the default build yet: it has not
-// been run on a GPU).
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_pack_bits(uint32_t lo, uint32_t hi) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_splat(float v) { return f2_pack(v, v); }
-// sign flip of both halves, exact (what the scalar form's unary minus does)
-__device__ __forceinline__ uint64_t f2_neg(uint64_t v) { return v ^ 0x8000000080000000ull; }
-
-// The confirmation of div_rn_ge1 for one lane (moe_common.cuh), on the
-// quotient q1 and remainder r1 computed in packed form.
-__device__ __forceinline__ float div_confirm(float g, float d, float q1, float r1, bool& ok) {
-    const uint32_t qb = __float_as_uint(q1);
-    const float half_ulp = __uint_as_float((qb & 0x7f800000u) - (24u << 23));
-    ok = d < 16777216.f && fabsf(g) < 0x1p64f && fabsf(q1) >= 0x1p-100f && (qb & 0x7fffffu) != 0u &&
-         fabsf(r1) < __fmul_rn(d, half_ulp);
-    const bool zero = g == 0.f && d < 16777216.f;
-    ok = ok || zero;
-    return zero ? g : q1;
-}
-
-// silu_quotient_fast (moe_common.cuh) on two values at once, operation for
-// operation on packed pairs; the reciprocal estimate and the exactness checks
-// stay per lane.  Same results as two scalar calls.
-__device__ __forceinline__ void silu_quotient_fast2(float g0, float g1, float& q0, float& q1, bool& ok0, bool& ok1) {
-    const uint64_t g2 = f2_pack(g0, g1);
-    const uint64_t x2 = f2_neg(g2);
-    const uint64_t magic = f2_splat(12582912.f);
-    const uint64_t shifted = f2_add(f2_mul(x2, f2_splat(0x1.715476p+0f)), magic);
-    const uint64_t n_float = f2_sub(shifted, magic);
-    float s0, s1;
-    f2_unpack(shifted, s0, s1);
-    const int n0 = __float_as_int(s0) - 0x4B400000, n1 = __float_as_int(s1) - 0x4B400000;
-    const uint64_t high = f2_mul(n_float, f2_splat(0x1.62e400p-1f));
-    const uint64_t low = f2_mul(n_float, f2_splat(0x1.7f7d1cp-20f));
-    const uint64_t r = f2_sub(f2_sub(x2, high), low);
-    uint64_t p = f2_splat(0x1.a01a02p-16f);
-    p = f2_add(f2_mul(p, r), f2_splat(0x1.a01a02p-13f));
-    p = f2_add(f2_mul(p, r), f2_splat(0x1.6c16c2p-10f));
-    p = f2_add(f2_mul(p, r), f2_splat(0x1.111112p-7f));
-    p = f2_add(f2_mul(p, r), f2_splat(0x1.555556p-5f));
-    p = f2_add(f2_mul(p, r), f2_splat(0x1.555556p-3f));
-    p = f2_add(f2_mul(p, r), f2_splat(0x1p-1f));
-    p = f2_add(f2_mul(p, r), f2_splat(0x1p+0f));
-    p = f2_add(f2_mul(p, r), f2_splat(0x1p+0f));
-    const uint64_t e = f2_mul(p, f2_pack(__int_as_float((n0 + 127) << 23), __int_as_float((n1 + 127) << 23)));
-    const uint64_t d = f2_add(f2_splat(1.f), e);
-    // div_rn_ge1 on the pair
-    float d0, d1, y00, y01;
-    f2_unpack(d, d0, d1);
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y00) : "f"(d0));
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y01) : "f"(d1));
-    const uint64_t y0 = f2_pack(y00, y01), nd = f2_neg(d);
-    const uint64_t e1 = f2_fma(nd, y0, f2_splat(1.f));
-    const uint64_t y1 = f2_fma(y0, e1, y0);
-    const uint64_t qa = f2_mul(g2, y1);
-    const uint64_t ra = f2_fma(nd, qa, g2);
-    const uint64_t qb = f2_fma(ra, y1, qa);
-    const uint64_t rb = f2_fma(nd, qb, g2);
-    float qb0, qb1, rb0, rb1;
-    f2_unpack(qb, qb0, qb1);
-    f2_unpack(rb, rb0, rb1);
-    bool dok0, dok1;
-    q0 = div_confirm(g0, d0, qb0, rb0, dok0);
-    q1 = div_confirm(g1, d1, qb1, rb1, dok1);
-    ok0 = dok0 && fabsf(g0) < 80.f;
-    ok1 = dok1 && fabsf(g1) < 80.f;
-}
-#endif
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Named barrier that also ANDs a predicate across the participating threads,
@@ -493,23 +387,6 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         const int s = st % kStages;
                         if (!bwait(&full[s], uint32_t(st / kStages) & 1u, abort, p.flags)) break;
                         if (warp == 2 && lane == 0) PREFILL_TRACE(2, st);
-#if ORNITH_PREFILL_CONV6
-                        // The same 64 (tile i, pair q) items per lane as below, dealt
-                        // over six warps: item p = cw + 6m is tile p / 8, pair p % 8.
-                        {
-                            const uint32_t* bp0 =
-                                reinterpret_cast<const uint32_t*>(stages + size_t(s) * kStageBytes + kABytes) + lane;
-                            uint8_t* bu0 = stages + size_t(s) * kStageBytes + kABytes + kBpBytes + (lane >> 3) * 128 +
-                                           (lane & 7) * 16;
-                            for (int it = cw; it < 64; it += kConvWarps) {
-                                const int i = it >> 3, q = it & 7;
-                                const uint32_t w0 = bp0[i * 512 + (2 * q) * 32], w1 = bp0[i * 512 + (2 * q + 1) * 32];
-                                *reinterpret_cast<uint4*>(bu0 + q * 4096 + i * 512) =
-                                    make_uint4(w0 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu,
-                                               (w1 >> 4) & 0x0f0f0f0fu);
-                            }
-                        }
-#else
                         // Work item (i, q, c): 32-column tile i (8), word pair q (8),
                         // column c = lane; converter warp cw takes the pairs
                         // q = cw + 4*qq.  Packed word j of column c of tile i is
@@ -535,7 +412,6 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                                     make_uint4(w[2 * qq] & 0x0f0f0f0fu, (w[2 * qq] >> 4) & 0x0f0f0f0fu,
                                                w[2 * qq + 1] & 0x0f0f0f0fu, (w[2 * qq + 1] >> 4) & 0x0f0f0f0fu);
                         }
-#endif
                         fence_proxy_async();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&conv[s]);
@@ -608,29 +484,12 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 const int ssumi = reinterpret_cast<const int32_t*>(mslot + kNT * 4 + kMT * 4)[row];
                 const float ssum = __fmul_rn(sa, float(ssumi));
                 const uint32_t base = tmem + lane_base + uint32_t(b * kNT);
-#if ORNITH_PREFILL_F32X2
-                const uint64_t sa2 = f2_pack(sa, sa), ssum2 = f2_pack(ssum, ssum);
-                const uint64_t magic2 = f2_pack(kMagicF, kMagicF);
-#endif
 #pragma unroll
                 for (int part = 0; part < 4; ++part) {
                     const int col = (part < 2 ? c0 : c1) + 16 * (part & 1);
                     uint32_t r[16];
                     tmem_ld16(base + col, r);
                     tmem_wait_ld();
-#if ORNITH_PREFILL_F32X2
-                    // the same six operations per accumulator on column pairs
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const uint64_t sw2 = *reinterpret_cast<const uint64_t*>(swf + col + 2 * q);
-                        const uint64_t of2 = *reinterpret_cast<const uint64_t*>(offf + col + 2 * q);
-                        const uint64_t fd2 = f2_sub(f2_pack_bits(r[2 * q], r[2 * q + 1]), magic2);
-                        const uint64_t term2 = f2_add(f2_mul(sw2, f2_mul(sa2, fd2)), f2_mul(of2, ssum2));
-                        float& a0 = acc[part * 16 + 2 * q];
-                        float& a1 = acc[part * 16 + 2 * q + 1];
-                        f2_unpack(f2_add(f2_pack(a0, a1), term2), a0, a1);
-                    }
-#else
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const float4 sw4 = *reinterpret_cast<const float4*>(swf + col + 4 * q);
@@ -645,7 +504,6 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                             acc[part * 16 + i] = __fadd_rn(acc[part * 16 + i], term);
                         }
                     }
-#endif
                     tmem_st16_const(base + col, kMagic);
                 }
                 tmem_wait_st();
@@ -693,14 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         bool ok[8];
 #pragma unroll
                         for (int j = 0; j < 8; ++j) gs[j] = valid ? acc[i + j] : 1.f;
-#if ORNITH_PREFILL_F32X2
-#pragma unroll
-                        for (int j = 0; j < 8; j += 2)
-                            silu_quotient_fast2(gs[j], gs[j + 1], q[j], q[j + 1], ok[j], ok[j + 1]);
-#else
 #pragma unroll
                         for (int j = 0; j < 8; ++j) q[j] = silu_quotient_fast(gs[j], ok[j]);
-#endif
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
                             if (!ok[j]) q[j] = __fdiv_rn(gs[j], __fadd_rn(1.f, portable_exp(-gs[j])));

@@ -566,3 +566,116 @@ def test_prefill_8192_sampled_tokens(native, layer1, bank1, S, O, path):
     ref, _, ref_flags = O.routed_layer(x[pick], w[pick], ids[pick], *bank1.np_routed, a8=False)
     np.testing.assert_array_equal(out[pick], ref)
     assert flags == 0 == ref_flags
+
+
+def single_token_cases(S, rng, n=10):
+    """T = 1 routes: random, padded, duplicated, invalid ids and non-finite
+    inputs (one of each kind per case index)."""
+    cases = []
+    for i in range(n):
+        x = S.make_tokens(rng, 1)
+        w, ids = S.random_routes(rng, 1, pad_fraction=0.15 if i % 3 == 0 else 0.0)
+        if i % 4 == 1:
+            ids[0, 5] = ids[0, 2]             # an expert named by two slots
+        if i % 5 == 2:
+            ids[0, 3] = 300                   # invalid id: flag 4
+        if i % 7 == 3:
+            x[0, 11] = 0x7F80                 # +inf input: flag 1
+        if i == n - 1:
+            ids[0, :] = -1                    # every slot padded
+        cases.append((x, w, ids))
+    return cases
+
+
+@pytest.mark.parametrize('a8', [True, False])
+def test_single_token_kernel_matches_multi_token_kernel(native, layer1, bank1, S, O, a8, monkeypatch):
+    """T = 1 runs the single-token kernel; the multi-token kernel (selected
+    with ORNITH_MOE_B200_DECODE1=0) and the oracle give the same bits, fp32
+    diagnostic and flags on padding, duplicate and invalid ids and non-finite
+    inputs."""
+    symbol = 'ornith_routed_direct_launch' if a8 else 'ornith_routed_direct_launch_a4'
+    for x, w, ids in single_token_cases(S, np.random.default_rng(4242 + a8)):
+        monkeypatch.delenv('ORNITH_MOE_B200_DECODE1', raising=False)
+        one = run_entry(native, symbol, x, w, ids, bank1)
+        monkeypatch.setenv('ORNITH_MOE_B200_DECODE1', '0')
+        multi = run_entry(native, symbol, x, w, ids, bank1)
+        ref, ref_f32, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=a8)
+        np.testing.assert_array_equal(one[0], ref)
+        np.testing.assert_array_equal(one[1].view(np.uint32), ref_f32.view(np.uint32))
+        np.testing.assert_array_equal(multi[0], one[0])
+        assert one[2] == multi[2] == ref_flags
+
+
+def test_single_token_kernel_shared_expert_and_from_logits(native, layer1, bank1, S, O, tables, monkeypatch):
+    """The single-token kernel with the shared expert: the caller's logit and
+    tables (shared-slot entry) and the from-logits operator (device top-8 and
+    shared logit), against the oracle and the multi-token kernel."""
+    silu, sigmoid = dev(tables['silu_fp32']), dev(tables['sigmoid_bf16'])
+    rng = np.random.default_rng(77)
+    for i, (x, w, ids) in enumerate(single_token_cases(S, rng, 6)):
+        logit = S.f32_to_bf16_bits(rng.standard_normal(1).astype(np.float32))
+        ref, ref_sh, _, ref_flags = O.routed_layer_shared(x, w, ids, *bank1.np_routed, *bank1.np_shared, logit,
+                                                          tables['silu_fp32'], tables['sigmoid_bf16'])
+        got = []
+        for env in (None, '0'):
+            if env is None:
+                monkeypatch.delenv('ORNITH_MOE_B200_DECODE1', raising=False)
+            else:
+                monkeypatch.setenv('ORNITH_MOE_B200_DECODE1', env)
+            ws = torch.empty(native.get_layout(16).workspace_bytes, dtype=torch.uint8, device=DEV)
+            out = torch.empty((1, 2048), dtype=torch.bfloat16, device=DEV)
+            shared = torch.empty((1, 2048), dtype=torch.bfloat16, device=DEV)
+            flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+            native.routed_shared_out(dev(x), dev(w), dev(ids), *bank1.routed, *bank1.shared, dev(logit), silu,
+                                     sigmoid, ws, out, shared, flags, 16)
+            torch.cuda.synchronize()
+            got.append((host_bits(out), host_bits(shared), int(flags.item())))
+        for o, sh, fl in got:
+            np.testing.assert_array_equal(o, ref)
+            np.testing.assert_array_equal(sh, ref_sh)
+            assert fl == ref_flags
+    monkeypatch.delenv('ORNITH_MOE_B200_DECODE1', raising=False)
+    for seed in range(4):
+        r2 = np.random.default_rng(600 + seed)
+        x = S.make_tokens(r2, 1)
+        logits = r2.standard_normal((1, 256)).astype(np.float32)
+        if seed == 3:
+            logits[0, 40] = np.nan
+        w, ids = O.route_topk(logits)
+        lg = shared_logit_like_device(x, bank1.gate_w)
+        ref, ref_sh, _, ref_flags = O.routed_layer_shared(x, w, ids, *bank1.np_routed, *bank1.np_shared, lg,
+                                                          tables['silu_fp32'], tables['sigmoid_bf16'])
+        ws = torch.empty(native.workspace_bytes(1), dtype=torch.uint8, device=DEV)
+        out = torch.empty((1, 2048), dtype=torch.bfloat16, device=DEV)
+        shared = torch.empty((1, 2048), dtype=torch.bfloat16, device=DEV)
+        flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+        native.routed_from_logits(dev(x), dev(logits), *bank1.routed, *bank1.shared, dev(bank1.gate_w), silu,
+                                  sigmoid, ws, out, shared, flags, 1, 0)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(host_bits(out), ref)
+        np.testing.assert_array_equal(host_bits(shared), ref_sh)
+        assert int(flags.item()) == ref_flags | (1 if seed == 3 else 0)
+
+
+def test_single_token_kernel_call_numbers(native, layer1, bank1, S, O):
+    """The single-token kernel tags its flags with call numbers kept in the
+    workspace instead of clearing them: a workspace that starts as all-ones
+    bytes, many calls in a row, and calls of the multi-token kernel (T = 3)
+    on the same workspace in between all give the oracle's bits."""
+    rng = np.random.default_rng(31)
+    cases = [(S.make_tokens(rng, T), *S.random_routes(rng, T, pad_fraction=0.1)) for T in (1, 1, 3, 1, 3, 1)]
+    refs = [O.routed_layer(x, w, ids, *bank1.np_routed, a8=True) for x, w, ids in cases]
+    ws = torch.full((native.get_layout(8).workspace_bytes,), 255, dtype=torch.uint8, device=DEV)
+    out = torch.empty((3, 2048), dtype=torch.bfloat16, device=DEV)
+    fn = native.lib().ornith_routed_direct_launch
+    for rep in range(40):
+        i = rep % len(cases)
+        x, w, ids = cases[i]
+        T = x.shape[0]
+        flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+        st = fn(*[native.ptr(t) for t in (dev(x), dev(w), dev(ids), *bank1.routed, ws)], ws.numel(),
+                native.ptr(out), native.ptr(flags), T, 8, native.stream(out))
+        assert st == 0
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(host_bits(out)[:T], refs[i][0], err_msg=f'call {rep}')
+        assert int(flags.item()) == refs[i][2], f'call {rep}'
