@@ -11,29 +11,30 @@
 // projection epilogue, :168-175 SiLU*up, :176-185 combine, :187-306 shared
 // slot), operation for operation, as in the multi-token kernel.
 //
-// One cooperative launch of one CTA per SM (148 on B200), 9 warps:
+// One cooperative launch of one CTA per SM (148 on B200), 19 warps:
 //  * every CTA routes the token itself (top-8 of the logits, or the caller's
 //    ids) and builds the same plan: slot 0 is the shared expert when present,
 //    then the distinct routed experts in slot order (an expert named by
 //    several slots is one plan slot whose routes share every value, since
 //    they see the same token);
 //  * gate item (slot k, tile pair p) -> CTA 16k + p: gate tile p and up tile
-//    p + 16 over the 8 K-groups (66 KB), warp g takes K-group g; warp 0 sums
-//    the eight group terms in order, applies SiLU*up and stores the slot's 32
-//    middle columns, then raises the item's flag;
-//  * output tile t (32 columns) -> CTA G-1-t, for every slot (the down
-//    blocks of all slots, up to 76 KB): the CTA waits for every gate item's
-//    flag, transforms and quantises each slot's middle row itself, computes
-//    the tile's down projection of every slot and performs the slot-ordered
-//    combine of the tile locally;
+//    p + 16 over the 8 K-groups (66 KB, four bulk copies); warp 2g + r takes
+//    K-group g of tile r; warp 0 sums the eight group terms in order, applies
+//    SiLU*up and stores the slot's 32 middle columns as 64-bit words that
+//    carry the call number beside the fp32 value;
+//  * output tile t (32 columns) -> CTA G-1-t, for every slot (two bulk copies
+//    per slot, up to 76 KB): warp 2k + g polls the 256 middle words of slot k,
+//    K-group g until all carry this call's number (no separate flag, fence or
+//    second read), transforms and quantises them and computes that K-group's
+//    down term; the tile's per-slot rows and the slot-ordered combine follow
+//    in the same CTA;
 //  * the copy warp issues all of the CTA's weight blocks with cp.async.bulk
 //    right after routing (the shared expert's, which need no routing, before
-//    it), so at most one K-group's latency stands between the copies and the
-//    compute.  No cluster multicast.
-// Flags between CTAs carry a call number instead of being cleared: every CTA
-// reads the last completed call's number from the workspace and uses the next
-// one, and CTA 0 publishes it once every CTA has read it.  No separate clear
-// launch is needed and stale words of earlier calls never match.
+//    it).  No cluster multicast.
+// Call numbers instead of clears: every CTA reads the last completed call's
+// number from the workspace and uses the next one, and CTA 0 publishes it once
+// every CTA has read it.  No separate clear launch is needed and words of
+// earlier calls never match.
 // Every wait is bounded (about one second of %globaltimer), after which the
 // kernel raises flag 64, lets its issued copies land and returns.
 #include <cstdlib>
@@ -44,25 +45,28 @@
 namespace ornith {
 namespace {
 
-constexpr int kD1Warps = 9;                 // warps 0..7 compute, warp 8 routes and issues the copies
-constexpr int kD1Threads = kD1Warps * 32;
-constexpr int kD1Copier = 8;
-constexpr int kD1Compute = 8 * 32;          // threads of the compute warps (named barrier 1)
-constexpr int kBlkBytes = 4096 + 128;       // one (tile, 256-group) block: 32x32 code words + 32 metadata words
 constexpr int kD1Slots = kTop + 1;          // eight routed experts and the shared expert
+constexpr int kD1Compute = 2 * kD1Slots;    // compute warps: one per (slot, K-group) of the down tile
+constexpr int kD1Copier = kD1Compute;       // the warp that issues the copies
+constexpr int kD1Router = 16;               // routes the token (a compute warp idle until the down tile)
+constexpr int kD1Logit = 17;                // the shared expert's logit and gate value (idem)
+constexpr int kD1Warps = kD1Compute + 1;
+constexpr int kD1Threads = kD1Warps * 32;
 constexpr int kD1GateItems = kD1Slots * 16;
 constexpr int kD1DownCtas = kH / 32;        // one per 32-column output tile
 constexpr uint64_t kD1WaitNs = 1000000000ull;
-static_assert(kD1GateItems <= 9 * 16, "gate flags fit their control words");
+static_assert(kD1Compute >= 16, "a warp per (K-group, tile) of a gate item");
 
 struct __align__(128) D1Smem {
-    uint8_t gate[8][2][kBlkBytes];          // gate item: K-group g; [0] gate tile p, [1] up tile p + 16
-    uint8_t down[kD1Slots][2][kBlkBytes];   // this CTA's output tile of every slot, K-groups 0 and 1
+    uint8_t gate_codes[2][8][4096];         // gate item: [0] gate tile p, [1] up tile p + 16; K-group g
+    uint32_t gate_meta[2][8][32];
+    uint8_t down_codes[kD1Slots][2][4096];  // this CTA's output tile of every slot, K-groups 0 and 1
+    uint32_t down_meta[kD1Slots][2][32];
     uint8_t xq[kH];                         // the token's activations, permuted int8
     uint8_t mq[kD1Slots][2][kG];            // every slot's middle activations
     float terms[8][2][32];                  // gate item: group terms of gate and up
-    float sout[kD1Slots][32];               // this tile's down projection of every slot
-    uint64_t gbar[8];
+    float dterm[kD1Slots][2][32];           // down tile: group term of every slot and K-group
+    uint64_t gbar;
     uint64_t dbar[kD1Slots];
     __half xs[8];
     int32_t xsum[8];
@@ -75,9 +79,9 @@ struct __align__(128) D1Smem {
     int32_t act_e[kD1Slots];                // expert of each plan slot (kE: the shared expert)
     int32_t nslot;
     uint32_t tag;                           // this launch's call number
-    uint32_t issued;                        // bits 0..7: gate barriers issued, 8 + k: down barrier k issued
+    uint32_t issued;                        // bit 0: gate barrier issued, 1 + k: down barrier k issued
     int32_t abort;
-    uint16_t logit;
+    float shared_gate;                      // sigmoid of the shared expert's logit (bf16 table value)
 };
 
 __device__ __forceinline__ uint64_t d1_now() {
@@ -86,7 +90,29 @@ __device__ __forceinline__ uint64_t d1_now() {
     return t;
 }
 
-__device__ __forceinline__ void d1_barrier() { asm volatile("bar.sync 1, %0;" ::"r"(kD1Compute) : "memory"); }
+// Optional phase timestamps (%globaltimer ns) per CTA, for latency analysis
+// only: compiled in with -DORNITH_DECODE1_TRACE, absent from the default build.
+#ifdef ORNITH_DECODE1_TRACE
+constexpr int kD1TraceSlots = 16;
+__device__ unsigned long long g_d1_trace[kD1MaxCtas][kD1TraceSlots];
+#define D1_STAMP(i) (g_d1_trace[blockIdx.x][i] = d1_now())
+#else
+#define D1_STAMP(i) ((void)0)
+#endif
+
+__device__ __forceinline__ void d1_barrier() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kD1Compute * 32) : "memory");
+}
+
+// Programmatic dependent launch: let the next grid on the stream start
+// launching; wait until the previous grid has completed and its memory
+// operations are visible (a no-op when the launch did not ask for it).
+__device__ __forceinline__ void d1_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void d1_wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// The plan hand-off from the routing warp to the copy warp (named barrier 2).
+__device__ __forceinline__ void d1_plan_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
+__device__ __forceinline__ void d1_plan_arrive() { asm volatile("bar.arrive 2, 64;" ::: "memory"); }
 
 __device__ __forceinline__ void d1_flag_or(uint32_t* flags, uint32_t f) {
     f = __reduce_or_sync(0xffffffffu, f);
@@ -108,27 +134,50 @@ __device__ bool d1_wait_copies(uint64_t* bar, const volatile int32_t* abort) {
     return true;
 }
 
-__device__ __forceinline__ void copy_block(uint8_t* dst, const uint32_t* codes, const uint32_t* meta, uint64_t* bar) {
-    bulk_g2s(dst, codes, 4096, bar);
-    bulk_g2s(dst + 4096, meta, 128, bar);
+// Relaxed (single-copy atomic per 64-bit element) accesses of the exchange words.
+__device__ __forceinline__ void ld_relaxed_v2(const unsigned long long* p, unsigned long long& x,
+                                              unsigned long long& y) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(p) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Gate item of expert e (kE: shared), tile pair p, K-group g (the calling lane).
-__device__ __forceinline__ void issue_gate_group(const LayerArgs& a, D1Smem& S, int e, int p, int g) {
-    const uint32_t* codes = e == kE ? a.sgate_codes : a.gate_codes + size_t(e) * (2 * kI) * (kH / 8);
-    const uint32_t* meta = e == kE ? a.sgate_meta : a.gate_meta + size_t(e) * (2 * kI) * (kH / kG);
-    mbar_arrive_expect_tx(&S.gbar[g], 2 * kBlkBytes);
-    copy_block(S.gate[g][0], codes + size_t(p * 8 + g) * 1024, meta + size_t(p * 8 + g) * 32, &S.gbar[g]);
-    copy_block(S.gate[g][1], codes + size_t((p + 16) * 8 + g) * 1024, meta + size_t((p + 16) * 8 + g) * 32, &S.gbar[g]);
-}
-
-// Down blocks of expert e for output tile `tile` into plan slot k.
-__device__ __forceinline__ void issue_down_slot(const LayerArgs& a, D1Smem& S, int e, int k, int tile) {
-    const uint32_t* codes = e == kE ? a.sdown_codes : a.down_codes + size_t(e) * kH * (kI / 8);
-    const uint32_t* meta = e == kE ? a.sdown_meta : a.down_meta + size_t(e) * kH * (kI / kG);
-    mbar_arrive_expect_tx(&S.dbar[k], 2 * kBlkBytes);
-    copy_block(S.down[k][0], codes + size_t(tile * 2) * 1024, meta + size_t(tile * 2) * 32, &S.dbar[k]);
-    copy_block(S.down[k][1], codes + size_t(tile * 2 + 1) * 1024, meta + size_t(tile * 2 + 1) * 32, &S.dbar[k]);
+// The copies of one CTA, one per lane.  Copy i: the gate item's four (gate
+// and up tile codes, 32 KB each, and metadata, 1 KB each) when `gate_item`,
+// then two per down slot k in [k0, k1) (8 KB of codes and 256 B of metadata
+// of output tile `tile`).  mbarrier expect-tx is registered for every barrier
+// (lane 0: the gate barrier, lane 1 + k: down slot k) before any copy starts.
+__device__ __forceinline__ void issue_copies(const LayerArgs& a, D1Smem& S, int lane, bool gate_item, int ge, int gp,
+                                             int k0, int k1, int tile) {
+    if (gate_item && lane == 0) mbar_arrive_expect_tx(&S.gbar, 2 * (32768 + 1024));
+    if (lane >= 1 + k0 && lane < 1 + k1) mbar_arrive_expect_tx(&S.dbar[lane - 1], 8192 + 256);
+    __syncwarp();
+    int i = lane;
+    if (gate_item) {
+        if (i < 4) {
+            const int r = i >> 1, tile_g = gp + 16 * r;
+            const uint32_t* codes = ge == kE ? a.sgate_codes : a.gate_codes + size_t(ge) * (2 * kI) * (kH / 8);
+            const uint32_t* meta = ge == kE ? a.sgate_meta : a.gate_meta + size_t(ge) * (2 * kI) * (kH / kG);
+            if ((i & 1) == 0) bulk_g2s(S.gate_codes[r], codes + size_t(tile_g) * 8 * 1024, 32768, &S.gbar);
+            else bulk_g2s(S.gate_meta[r], meta + size_t(tile_g) * 8 * 32, 1024, &S.gbar);
+            return;
+        }
+        i -= 4;
+    }
+    const int k = k0 + (i >> 1);
+    if (i < 0 || k >= k1) return;
+    const int e = checked(S.act_e[k], kE + 1, a.flags);
+    if ((i & 1) == 0) {
+        const uint32_t* codes = e == kE ? a.sdown_codes : a.down_codes + size_t(e) * kH * (kI / 8);
+        bulk_g2s(S.down_codes[k], codes + size_t(tile) * 2 * 1024, 8192, &S.dbar[k]);
+    } else {
+        const uint32_t* meta = e == kE ? a.sdown_meta : a.down_meta + size_t(e) * kH * (kI / kG);
+        bulk_g2s(S.down_meta[k], meta + size_t(tile) * 2 * 32, 256, &S.dbar[k]);
+    }
 }
 
 // Exact integer dot of one column (lane) of a 256-group block with one
@@ -149,6 +198,13 @@ __device__ __forceinline__ int block_dot(const uint32_t* blk, const uint4* act, 
     return (c0 + c1) + (c2 + c3);
 }
 
+// The down projection value of slot k for this lane's column: (0 + group-0
+// term) + group-1 term, bf16-rounded for the shared expert.
+__device__ __forceinline__ float down_value(const D1Smem& S, int k, int lane) {
+    float v = __fadd_rn(__fadd_rn(0.f, S.dterm[k][0][lane]), S.dterm[k][1][lane]);
+    return S.act_e[k] == kE ? bf16_round_f32(v) : v;
+}
+
 template <int QMAX>
 __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const LayerArgs a) {
     extern __shared__ __align__(128) uint8_t d1_raw[];
@@ -156,29 +212,58 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.x, G = gridDim.x;
     uint32_t* ctrl = ws_at<uint32_t>(a, a.L.ctrl);
+    unsigned long long* const xchg = ws_at<unsigned long long>(a, a.L.xchg);
     const bool is_down = b >= G - kD1DownCtas;
     const int tile = G - 1 - b;  // output tile of a down CTA
     uint32_t f = 0;
-
-    if (tid == 0) {
-        for (int i = 0; i < 8; ++i) mbar_init(&S.gbar[i], 1);
-        for (int i = 0; i < kD1Slots; ++i) mbar_init(&S.dbar[i], 1);
-        fence_barrier_init();
-        S.abort = 0;
-        S.issued = 0;
-        uint32_t tag = *reinterpret_cast<const volatile uint32_t*>(ctrl + kCtrlD1Epoch) + 1u;
-        if (tag == 0u) tag = 1u;  // 0 never tags a call, so never-written words never match
-        S.tag = tag;
-        st_release(ctrl + kCtrlD1Seen + b, tag);  // after the read above: the epoch may advance
-    }
-    __syncthreads();
+    // The next layer's launch may begin now: its CTAs take SMs as ours leave
+    // them, and run only their prologue (barriers, the shared expert's weight
+    // copies) until this grid has completed (programmatic dependent launch).
+    d1_launch_dependents();
 
     if (warp == kD1Copier) {
-        // the shared expert's blocks need no routing: issued first
-        if (a.shared) {
-            if (b < 16 && lane < 8) issue_gate_group(a, S, kE, b, lane);
-            if (is_down && lane == 8) issue_down_slot(a, S, kE, 0, tile);
+        if (lane == 0) {
+            D1_STAMP(0);
+            mbar_init(&S.gbar, 1);
+            for (int i = 0; i < kD1Slots; ++i) mbar_init(&S.dbar[i], 1);
+            fence_barrier_init();
+            if (a.shared) S.act_e[0] = kE;  // plan slot 0, before its copies are issued
+            S.abort = 0;
         }
+        __syncwarp();
+        // the shared expert's blocks: constant weights, independent of routing
+        // and of the previous grid, so issued before waiting for it
+        if (a.shared) issue_copies(a, S, lane, b < 16, kE, b, 0, is_down ? 1 : 0, tile);
+        d1_wait_prior_grid();  // everything below may read what the previous grid wrote
+        uint32_t tag = 0;
+        if (lane == 0) {
+            tag = *reinterpret_cast<const volatile uint32_t*>(ctrl + kCtrlD1Epoch) + 1u;
+            if (tag == 0u) tag = 1u;  // 0 never tags a call, so never-written words never match
+            // seen: the stored value depends on the epoch read, so the read has
+            // completed when any CTA observes it.  Relaxed rather than release:
+            // a release here would also wait for this thread's bulk copies.
+            st_relaxed_u32(ctrl + kCtrlD1Seen + b, tag);
+        }
+        __syncwarp();
+        d1_plan_sync();  // the routing warp's plan
+        if (lane == 0) D1_STAMP(3);
+        const int NA = S.nslot, base = a.shared ? 1 : 0, gk = b / 16;
+        const bool has_gate = b < NA * 16;
+        const bool routed_gate = has_gate && !(a.shared && gk == 0);
+        // the routed gate item first; a CTA that also owns a down tile issues
+        // its routed down blocks once the gate item has landed (below), so
+        // that the gate bytes, needed first, are not slowed by them
+        const bool down_now = is_down && !has_gate;
+        issue_copies(a, S, lane, routed_gate, routed_gate ? S.act_e[gk] : 0, b % 16, base, down_now ? NA : base,
+                     tile);
+        if (lane == 0) {
+            S.tag = tag;
+            S.issued = (has_gate ? 1u : 0u) | (is_down ? 1u << 1 : 0u) * (a.shared ? 1u : 0u) |
+                       (down_now ? ((1u << NA) - 1u) << 1 : 0u);
+            D1_STAMP(4);
+        }
+    } else if (warp == kD1Router) {
+        d1_wait_prior_grid();
         // router top-8 (from logits) or the caller's ids, then the plan
         uint32_t rf = 0;
         if (a.logits) {
@@ -188,6 +273,7 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
             S.wts[lane] = a.weights[lane];
         }
         __syncwarp();
+        if (lane == 0) D1_STAMP(2);
         const int e = lane < kTop ? S.ids[lane] : -1;
         const bool valid = lane < kTop && id_valid(e);
         if (lane < kTop && !valid && e != -1) rf |= kFlagInvalidId;
@@ -202,12 +288,12 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         const int slot = base + __popc(heads & ((1u << leader) - 1u));
         if (lane < kTop) S.slot_of[lane] = valid ? slot : -1;
         if (valid && leader == lane) S.act_e[slot] = e;
-        if (lane == 0) {
-            if (a.shared) S.act_e[0] = kE;
-            S.nslot = base + __popc(heads);
-        }
+        if (lane == 0) S.nslot = base + __popc(heads);
+        d1_plan_arrive();  // hands the plan to the copy warp
+        if (lane == 0) D1_STAMP(1);
         if (b == 0) d1_flag_or(a.flags, rf);  // routing and id flags, once
-    } else {
+    } else if (warp < 8) {
+        d1_wait_prior_grid();
         // the token's 256-groups: warp g transforms and quantises group g
         const uint4 raw = *reinterpret_cast<const uint4*>(a.x + warp * kG + lane * 8);
         uint32_t qf = wht_quant<QMAX>(
@@ -217,6 +303,21 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
             reinterpret_cast<uint2*>(S.xq + warp * kG), S.xs + warp, S.xsum + warp);
         qf = __reduce_or_sync(0xffffffffu, qf);
         if (lane == 0) S.xflag[warp] = qf;
+        if (tid == 0) D1_STAMP(5);
+    } else if (warp == kD1Logit && a.shared && is_down) {
+        d1_wait_prior_grid();
+        // the shared expert's output gate, sigmoid(logit) from the caller's
+        // table, needed by the combine: fetched now, off the critical path
+        uint16_t v;
+        if (a.shared_gate_weight) {
+            v = shared_logit_warp(a.x, a.shared_gate_weight, lane);
+            if (lane == 0 && tile == 0) a.logit_out[0] = v;
+        } else {
+            v = a.shared_logit[0];
+        }
+        if (lane == 0) S.shared_gate = bf16_to_f32(a.sigmoid_table[v]);
+    } else {
+        d1_wait_prior_grid();
     }
     __syncthreads();
 
@@ -234,39 +335,45 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
     }
 
     if (warp == kD1Copier) {
-        // the routed experts' blocks of this CTA
-        if (has_gate && !(a.shared && gk == 0) && lane < 8)
-            issue_gate_group(a, S, checked(S.act_e[gk], kE + 1, a.flags), gp, lane);
+        // a CTA with a gate item and a down tile: its routed down blocks once
+        // the gate item has landed
         const int base = a.shared ? 1 : 0;
-        if (is_down && lane >= 8 + base && lane < 8 + NA)
-            issue_down_slot(a, S, checked(S.act_e[lane - 8], kE + 1, a.flags), lane - 8, tile);
-        if (lane == 0) S.issued = (has_gate ? 0xffu : 0u) | (is_down ? ((1u << NA) - 1u) << 8 : 0u);
+        if (is_down && has_gate && NA > base) {
+            bool landed = true;
+            if (lane == 0) landed = d1_wait_copies(&S.gbar, &S.abort);
+            landed = __shfl_sync(0xffffffffu, int(landed), 0) != 0;
+            if (landed) {
+                issue_copies(a, S, lane, false, 0, 0, base, NA, tile);
+                if (lane == 0) atomicOr(&S.issued, ((1u << NA) - 1u) << 1);
+            } else if (lane == 0) {
+                d1_give_up(S, a.flags);
+            }
+        }
     } else if (NA == 0) {
         // every slot padded and no shared expert: the output is zero
         if (b == 0)
-            for (int i = tid; i < kH; i += kD1Compute) {
+            for (int i = tid; i < kH; i += kD1Compute * 32) {
                 a.out[i] = 0;
                 ws_at<float>(a, a.L.final_f32)[i] = 0.f;
             }
     } else {
-        float* const middle = ws_at<float>(a, a.L.middle);
-        // ---- gate item (slot gk, tile pair gp): warp g = K-group g ----------
+        // ---- gate item (slot gk, tile pair gp): warp 2g + r = K-group g of tile r
         if (has_gate) {
-            const int g = warp;
-            if (d1_wait_copies(&S.gbar[g], &S.abort)) {
-                const uint32_t* bg = reinterpret_cast<const uint32_t*>(S.gate[g][0]);
-                const uint32_t* bu = reinterpret_cast<const uint32_t*>(S.gate[g][1]);
-                const uint4* act = reinterpret_cast<const uint4*>(S.xq + g * kG);
-                const int dg = block_dot(bg, act, lane), du = block_dot(bu, act, lane);
-                const float sa = __half2float(S.xs[g]);
-                const int sm = S.xsum[g];
-                S.terms[g][0][lane] = group_term(sa, dg, sm, bg[1024 + lane]);
-                S.terms[g][1][lane] = group_term(sa, du, sm, bu[1024 + lane]);
-            } else if (lane == 0) {
-                d1_give_up(S, a.flags);
+            if (warp < 16) {
+                const int g = warp >> 1, r = warp & 1;
+                if (d1_wait_copies(&S.gbar, &S.abort)) {
+                    if (lane == 0 && warp == 0) D1_STAMP(6);
+                    const uint32_t* blk = reinterpret_cast<const uint32_t*>(S.gate_codes[r][g]);
+                    const int dot = block_dot(blk, reinterpret_cast<const uint4*>(S.xq + g * kG), lane);
+                    S.terms[g][r][lane] = group_term(__half2float(S.xs[g]), dot, S.xsum[g], S.gate_meta[r][g][lane]);
+                    if (lane == 0 && warp == 0) D1_STAMP(7);
+                } else if (lane == 0) {
+                    d1_give_up(S, a.flags);
+                }
             }
             d1_barrier();
-            if (warp == 0 && !S.abort) {
+            if (tid == 0) D1_STAMP(8);
+            if (warp == 0 && !*reinterpret_cast<const volatile int32_t*>(&S.abort)) {
                 float gv = 0.f, uv = 0.f;
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
@@ -284,91 +391,93 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
                     value = silu_mul(gv, uv);
                 }
                 if (!isfinite(value)) f |= kFlagNonfiniteMiddle;
-                middle[size_t(gk) * kI + gp * 32 + lane] = value;
-                __syncwarp();
-                if (lane == 0) st_release(ctrl + kCtrlD1Gate + b, tag);  // the slot's 32 middle columns are out
+                // the slot's 32 middle columns, each word tagged with this call's number
+                st_relaxed_u64(xchg + size_t(gk) * kI + gp * 32 + lane,
+                               (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(value));
+                if (lane == 0) D1_STAMP(9);
             }
         }
-        // ---- output tile: every slot's down projection, then the combine ----
+        // ---- output tile: warp 2k + g = slot k, K-group g ----------------------
         if (is_down) {
-            if (a.shared && a.shared_gate_weight && warp == 7) {
-                const uint16_t v = shared_logit_warp(a.x, a.shared_gate_weight, lane);
-                if (lane == 0) {
-                    S.logit = v;
-                    if (tile == 0) a.logit_out[0] = v;
-                }
-            }
-            if (warp == 0) {
-                // every gate item's middle columns (bounded wait)
-                const int n = NA * 16;
+            const int k = warp >> 1, g = warp & 1;
+            bool ok = k < NA;
+            if (ok) {
+                // poll the 256 middle words of (k, g) until all carry this call's number
+                const unsigned long long* src = xchg + size_t(k) * kI + g * kG + lane * 8;
+                unsigned long long w[8];
                 const uint64_t t0 = d1_now();
                 for (;;) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) ld_relaxed_v2(src + 2 * i, w[2 * i], w[2 * i + 1]);
                     bool mine = true;
-                    for (int i = lane; i < n; i += 32) mine &= ld_acquire(ctrl + kCtrlD1Gate + i) == tag;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) mine &= uint32_t(w[i] >> 32) == tag;
                     if (__all_sync(0xffffffffu, mine)) break;
-                    const bool stop = __shfl_sync(0xffffffffu, int(S.abort != 0 || d1_now() - t0 > kD1WaitNs), 0);
+                    const int stop = __shfl_sync(
+                        0xffffffffu, int(*reinterpret_cast<const volatile int32_t*>(&S.abort) != 0 ||
+                                         d1_now() - t0 > kD1WaitNs), 0);
                     if (stop) {
                         if (lane == 0) d1_give_up(S, a.flags);
+                        ok = false;
                         break;
                     }
-                    __nanosleep(64);
+                    __nanosleep(32);
                 }
-            }
-            d1_barrier();  // orders every warp's reads after warp 0's acquires
-            const bool alive = !*reinterpret_cast<const volatile int32_t*>(&S.abort);
-            if (alive) {
-                // transform + quantise each slot's middle row (one 256-group per task)
-                for (int j = warp; j < NA * 2; j += 8) {
-                    const int k = j >> 1, g = j & 1;
-                    const float4* src = reinterpret_cast<const float4*>(middle + size_t(k) * kI + g * kG + lane * 8);
-                    const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
-                    f |= wht_quant<QMAX>(v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w, lane,
+                if (ok) {
+                    if (lane == 0 && warp == 0) D1_STAMP(10);
+                    f |= wht_quant<QMAX>(__uint_as_float(uint32_t(w[0])), __uint_as_float(uint32_t(w[1])),
+                                         __uint_as_float(uint32_t(w[2])), __uint_as_float(uint32_t(w[3])),
+                                         __uint_as_float(uint32_t(w[4])), __uint_as_float(uint32_t(w[5])),
+                                         __uint_as_float(uint32_t(w[6])), __uint_as_float(uint32_t(w[7])), lane,
                                          reinterpret_cast<uint2*>(S.mq[k][g]), &S.ms[k][g], &S.msum[k][g]);
+                    __syncwarp();
+                    if (lane == 0 && warp == 0) D1_STAMP(11);
+                    if (d1_wait_copies(&S.dbar[k], &S.abort)) {
+                        if (lane == 0 && warp == 0) D1_STAMP(12);
+                        const uint32_t* blk = reinterpret_cast<const uint32_t*>(S.down_codes[k][g]);
+                        const int dot = block_dot(blk, reinterpret_cast<const uint4*>(S.mq[k][g]), lane);
+                        S.dterm[k][g][lane] =
+                            group_term(__half2float(S.ms[k][g]), dot, S.msum[k][g], S.down_meta[k][g][lane]);
+                        if (lane == 0 && warp == 0) D1_STAMP(13);
+                    } else if (lane == 0) {
+                        d1_give_up(S, a.flags);
+                    }
                 }
             }
             d1_barrier();
-            for (int k = warp; alive && k < NA; k += 8) {
-                if (!d1_wait_copies(&S.dbar[k], &S.abort)) {
-                    if (lane == 0) d1_give_up(S, a.flags);
-                    break;
-                }
-                float v = 0.f;  // (0 + group 0 term) + group 1 term
-#pragma unroll
-                for (int g = 0; g < 2; ++g) {
-                    const uint32_t* blk = reinterpret_cast<const uint32_t*>(S.down[k][g]);
-                    const int dot = block_dot(blk, reinterpret_cast<const uint4*>(S.mq[k][g]), lane);
-                    v = __fadd_rn(v, group_term(__half2float(S.ms[k][g]), dot, S.msum[k][g], blk[1024 + lane]));
-                }
-                if (S.act_e[k] == kE) v = bf16_round_f32(v);
-                if (!isfinite(v)) f |= kFlagNonfiniteProjection;
-                S.sout[k][lane] = v;
-            }
-            d1_barrier();
+            if (tid == 0) D1_STAMP(14);
             if (!*reinterpret_cast<const volatile int32_t*>(&S.abort)) {
                 const int col = tile * 32 + lane;
                 float* const route_out = ws_at<float>(a, a.L.route_out);
                 if (warp < kTop) {
-                    const int k = S.slot_of[warp];
-                    if (k >= 0) route_out[size_t(warp) * kH + col] = S.sout[k][lane];
-                }
-                if (warp == 0 && a.shared) route_out[size_t(kTop) * kH + col] = S.sout[0][lane];
-                if (warp == 1) {
+                    // per-route rows (route order), as the other paths leave them
+                    const int kk = S.slot_of[warp];
+                    if (kk >= 0) {
+                        const float v = down_value(S, kk, lane);
+                        if (!isfinite(v)) f |= kFlagNonfiniteProjection;
+                        route_out[size_t(warp) * kH + col] = v;
+                    }
+                } else if (warp == kTop && a.shared) {
+                    const float v = down_value(S, 0, lane);
+                    if (!isfinite(v)) f |= kFlagNonfiniteProjection;
+                    route_out[size_t(kTop) * kH + col] = v;
+                } else if (warp == kTop + 1) {
                     // slot-ordered combine of the token (reduce_slots :176-185)
                     float sum = 0.f;
 #pragma unroll
                     for (int sl = 0; sl < kTop; ++sl)
-                        if (id_valid(S.ids[sl])) sum = __fadd_rn(sum, __fmul_rn(S.sout[S.slot_of[sl]][lane], S.wts[sl]));
+                        if (id_valid(S.ids[sl]))
+                            sum = __fadd_rn(sum, __fmul_rn(down_value(S, S.slot_of[sl], lane), S.wts[sl]));
                     const uint16_t res = bf16_rne(sum);
                     ws_at<float>(a, a.L.final_f32)[col] = sum;
                     a.out[col] = res;
                     if (!isfinite(sum) || (res & 0x7f80u) == 0x7f80u) f |= kFlagNonfiniteOutput;
                     if (a.shared) {
-                        const uint16_t lg = a.shared_gate_weight ? S.logit : a.shared_logit[0];
-                        const float gate = bf16_to_f32(a.sigmoid_table[lg]);
-                        const float sh = __fmul_rn(S.sout[0][lane], gate);
+                        const float sh = __fmul_rn(down_value(S, 0, lane), S.shared_gate);
                         a.shared_out[col] = bf16_rne(sh);
                         if (!isfinite(sh)) f |= kFlagNonfiniteOutput;
                     }
+                    if (lane == 0) D1_STAMP(15);
                 }
             }
         }
@@ -396,9 +505,9 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
     __syncthreads();
     if (tid == 0 && S.abort) {
         const uint64_t t0 = d1_now();
-        for (int i = 0; i < 8 + kD1Slots; ++i) {
+        for (int i = 0; i < 1 + kD1Slots; ++i) {
             if (!(S.issued >> i & 1u)) continue;
-            uint64_t* bar = i < 8 ? &S.gbar[i] : &S.dbar[i - 8];
+            uint64_t* bar = i == 0 ? &S.gbar : &S.dbar[i - 1];
             while (!mbar_try_wait(bar, 0) && d1_now() - t0 < kD1WaitNs) {
             }
         }
@@ -409,6 +518,7 @@ struct D1Device {
     int sms = 0;
     int max_smem = 0;
     bool attr_set[2] = {false, false};
+    int pdl = -1;  // -1: not yet known whether the device takes the launch with programmatic serialization
 };
 D1Device g_d1[64];
 
@@ -416,6 +526,11 @@ D1Device g_d1[64];
 // kernel instead (the tests compare the two).
 bool single_disabled() {
     const char* v = getenv("ORNITH_MOE_B200_DECODE1");
+    return v && strcmp(v, "0") == 0;
+}
+// ORNITH_MOE_B200_PDL=0 launches without programmatic dependent launch.
+bool pdl_disabled() {
+    const char* v = getenv("ORNITH_MOE_B200_PDL");
     return v && strcmp(v, "0") == 0;
 }
 
@@ -448,13 +563,40 @@ cudaError_t launch_decode_single(const LayerArgs& a, cudaStream_t stream) {
     cfg.blockDim = dim3(kD1Threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if ((st = cudaStreamIsCapturing(stream, &capturing)) != cudaSuccess) return st;
+    // programmatic serialization where the device takes it together with the
+    // cooperative launch; the first launch outside a stream capture finds out
+    const bool try_pdl = !pdl_disabled() && (d.pdl == 1 || (d.pdl < 0 && capturing == cudaStreamCaptureStatusNone));
+    cfg.numAttrs = try_pdl ? 2 : 1;
     count_launches(1);
-    return cudaLaunchKernelEx(&cfg, kernel, a);
+    st = cudaLaunchKernelEx(&cfg, kernel, a);
+    if (try_pdl && d.pdl < 0) {
+        d.pdl = st == cudaSuccess ? 1 : 0;
+        if (st != cudaSuccess) {
+            (void)cudaGetLastError();  // the refused launch left no work behind: launch without it
+            cfg.numAttrs = 1;
+            st = cudaLaunchKernelEx(&cfg, kernel, a);
+        }
+    }
+    return st;
 }
+
+#ifdef ORNITH_DECODE1_TRACE
+// Copies the phase timestamps of the last single-token launch (256 x 16 u64)
+// and clears them.
+extern "C" __attribute__((visibility("default"))) int ornith_moe_b200_decode1_trace(void* dst) {
+    cudaError_t st = cudaMemcpyFromSymbol(dst, g_d1_trace, sizeof(g_d1_trace));
+    if (st != cudaSuccess) return int(st);
+    static unsigned long long zeros[kD1MaxCtas][kD1TraceSlots];
+    return int(cudaMemcpyToSymbol(g_d1_trace, zeros, sizeof(zeros)));
+}
+#endif
 
 }  // namespace ornith

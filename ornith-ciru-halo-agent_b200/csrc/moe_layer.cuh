@@ -20,6 +20,7 @@ struct Workspace {
     size_t counts, offsets, routes, cursors, active;  // routing plan
     size_t ctrl;                  // counters of the fused kernels
     size_t topk_w, topk_ids, logit;  // router outputs of the from-logits entry point
+    size_t xchg;                  // single-token decode: middle rows as (call number, fp32) words [9][512] u64
     // tensor-core prefill path (only when Tcap > kDecodeMaxT)
     size_t rowpos, slot_tiles, mtiles, n_mtiles;
     size_t pblock;                // per-block expert counts, then bases [kPlanBlocks][E+1] (x2)
@@ -50,8 +51,7 @@ constexpr int kCtrlClearWords = 1072;  // words zeroed before every fused launch
 constexpr int kCtrlD1Epoch = 1088;     // call number of the last completed launch
 constexpr int kCtrlD1Seen = 1104;      // [kD1MaxCtas] a CTA read the epoch of this launch
 constexpr int kD1MaxCtas = 256;
-constexpr int kCtrlD1Gate = kCtrlD1Seen + kD1MaxCtas;  // [9 slots x 16 tile pairs] middle columns stored
-static_assert(kCtrlD1Gate + 9 * 16 <= kCtrlWords, "single-token decode words fit the control block");
+static_assert(kCtrlD1Seen + kD1MaxCtas <= kCtrlWords, "single-token decode words fit the control block");
 
 Workspace workspace_layout(int Tcap);
 
