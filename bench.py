@@ -65,8 +65,14 @@ CONFIGS = {
     'prefill8192': dict(T=8192, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 8192 (configs[3])'),
     # expert-parallel sweep: total tokens fixed, experts sharded over the ranks
     'ep_decode256': dict(T=256, layers=40, bias=0.0, act_bits=8, shared=False, ep=True, exchange='fixed',
+                         combine='exact', transport='p2p',
                          name='expert-parallel decode B=256, 40 layers, Zipf(1.2) expert skew (configs[4])'),
-    'ep_prefill8192': dict(T=8192, layers=4, bias=0.0, act_bits=4, shared=False, ep=True, exchange='compact',
+    # prefill: equal blocks (token rows gathered on every rank, no host
+    # synchronisation, one CUDA graph) and per-rank fp32 partial sums coming
+    # home (within the north-star tolerance of the single-GPU layer); measured
+    # fastest of the exchange modes on 2 B200s
+    'ep_prefill8192': dict(T=8192, layers=4, bias=0.0, act_bits=4, shared=False, ep=True, exchange='fixed',
+                           combine='partial', transport='nccl',
                            name='expert-parallel prefill 8192 tokens, Zipf(1.2) expert skew (configs[4]); '
                                 '4 weight sets cycled'),
     # dense G256 projection (the next row after the MoE layer): QKVZ-shaped
@@ -103,11 +109,15 @@ def parse():
                         'streams while step s runs (every copy still inside the timed region)')
     p.add_argument('--placement', choices=['balanced', 'contiguous'], default='balanced',
                    help='expert placement of the expert-parallel configs')
-    p.add_argument('--combine', choices=['exact', 'partial'], default='exact',
-                   help='expert-parallel return: per-slot rows (bit-exact) or per-rank fp32 partial sums')
-    p.add_argument('--ep-transport', choices=['nccl', 'p2p'], default='nccl',
+    p.add_argument('--combine', choices=['exact', 'partial'], default=None,
+                   help='expert-parallel return (default: the config\'s): per-slot rows (bit-exact) or per-rank '
+                        'fp32 partial sums')
+    p.add_argument('--ep-transport', choices=['nccl', 'p2p'], default=None,
                    help='expert-parallel token dispatch and return: NCCL, or stores into the receiving ranks\' '
                         'buffers over NVLink peer memory (exact combine, one chunk)')
+    p.add_argument('--ep-exchange', choices=['compact', 'fixed'], default=None,
+                   help='expert-parallel exchange (default: the config\'s): variable-size compact blocks, or '
+                        'equal blocks with no host synchronisation')
     p.add_argument('--ep-chunks', type=int, default=1,
                    help='compact expert-parallel exchange in this many pipelined token chunks (exact combine)')
     p.add_argument('--layers', type=int, default=None,
@@ -218,6 +228,12 @@ def run_ep(args):
     cfg = dict(CONFIGS[args.config])
     if args.layers:
         cfg['layers'] = args.layers
+    if args.ep_exchange:
+        cfg['exchange'] = args.ep_exchange
+    args.combine = args.combine or cfg['combine']
+    args.ep_transport = args.ep_transport or cfg['transport']
+    if args.combine == 'partial':
+        args.ep_transport = 'nccl'   # the peer-memory transport carries the exact per-slot rows only
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
@@ -305,7 +321,8 @@ def run_ep(args):
             step()
         torch.cuda.synchronize()
         dist.barrier()
-        graph.replay()
+        for _ in range(max(3, args.warmup)):   # the captured collectives warmed up on every rank
+            graph.replay()
         torch.cuda.synchronize()
     run_step = graph.replay if graph is not None else step
     n0 = lib.ornith_moe_b200_kernel_launches()
@@ -384,7 +401,7 @@ def run_ep(args):
                                  if args.placement == 'balanced' else 'contiguous ranges'),
                    'combine': ('per-slot fp32 rows, bit-identical to one GPU' if args.combine == 'exact' else
                                'per-rank fp32 partial sums, equal to one GPU within fp32 rounding'),
-                   'exchange': ({('fixed', 'nccl'): 'NCCL all_gather of token rows + equal-block all_to_all of '
+                   'exchange': 'none: one rank holds all 256 experts' if world == 1 else ({('fixed', 'nccl'): 'NCCL all_gather of token rows + equal-block all_to_all of '
                                                    'fp32 per-slot rows (no host synchronisation)',
                                  ('compact', 'nccl'): 'NCCL all_to_all_single dispatch + fp32 per-slot return '
                                                       '(variable splits)',

@@ -213,13 +213,17 @@ __device__ __forceinline__ void wht128_halfwarp(float (&e)[8], int lane) {
 #pragma unroll
         for (int s = 0; s < 8; ++s) e[s] = n[s];
     }
+    // across lanes: the upper lane of each pair computes other - e, which is
+    // the IEEE sum (-e) + other, so every lane adds, after flipping its own
+    // value's sign where it is the upper lane (the same results as choosing
+    // between the subtraction and the addition)
 #pragma unroll
     for (int lstep = 1; lstep < 16; lstep *= 2) {
-        const bool upper = (lane & lstep) != 0;
+        const uint32_t flip = (lane & lstep) != 0 ? 0x80000000u : 0u;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-            float other = __shfl_xor_sync(0xffffffffu, e[s], lstep);
-            e[s] = upper ? __fsub_rn(other, e[s]) : __fadd_rn(e[s], other);
+            const float other = __shfl_xor_sync(0xffffffffu, e[s], lstep);
+            e[s] = __fadd_rn(__uint_as_float(__float_as_uint(e[s]) ^ flip), other);
         }
     }
 #pragma unroll
@@ -292,9 +296,10 @@ __device__ __noinline__ uint32_t wht_quant(float e0, float e1, float e2, float e
                                            float e7, int lane, uint2* q, __half* scale, int32_t* sum) {
     float e[8] = {e0, e1, e2, e3, e4, e5, e6, e7};
     uint32_t f = 0;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        if (!isfinite(e[i])) f |= kFlagNonfiniteInput;
+    // A non-finite input makes every output of its 128-block non-finite (each
+    // output is a signed sum of all 128 inputs), and the lane holds outputs of
+    // its own block, so testing the outputs alone raises the same flag as
+    // testing inputs and outputs.
     wht128_halfwarp(e, lane);
 #pragma unroll
     for (int i = 0; i < 8; ++i)

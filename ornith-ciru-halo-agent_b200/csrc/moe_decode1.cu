@@ -49,7 +49,7 @@ constexpr int kD1Slots = kTop + 1;          // eight routed experts and the shar
 constexpr int kD1Compute = 2 * kD1Slots;    // compute warps: one per (slot, K-group) of the down tile
 constexpr int kD1Copier = kD1Compute;       // the warp that issues the copies
 constexpr int kD1Router = 16;               // routes the token (a compute warp idle until the down tile)
-constexpr int kD1Logit = 17;                // the shared expert's logit and gate value (idem)
+constexpr int kD1Combine = kTop + 1;        // the combine of a down tile (warps 0..8 store the per-route rows)
 constexpr int kD1Warps = kD1Compute + 1;
 constexpr int kD1Threads = kD1Warps * 32;
 constexpr int kD1GateItems = kD1Slots * 16;
@@ -63,10 +63,12 @@ struct __align__(128) D1Smem {
     uint8_t down_codes[kD1Slots][2][4096];  // this CTA's output tile of every slot, K-groups 0 and 1
     uint32_t down_meta[kD1Slots][2][32];
     uint8_t xq[kH];                         // the token's activations, permuted int8
+    uint16_t xraw[kH];                      // the token row as given (bf16)
     uint8_t mq[kD1Slots][2][kG];            // every slot's middle activations
     float terms[8][2][32];                  // gate item: group terms of gate and up
     float dterm[kD1Slots][2][32];           // down tile: group term of every slot and K-group
-    uint64_t gbar;
+    uint64_t gbar[8];                       // gate item: K-group g of both tiles
+    uint64_t gmbar;                         // gate item: metadata of both tiles
     uint64_t dbar[kD1Slots];
     __half xs[8];
     int32_t xsum[8];
@@ -79,7 +81,7 @@ struct __align__(128) D1Smem {
     int32_t act_e[kD1Slots];                // expert of each plan slot (kE: the shared expert)
     int32_t nslot;
     uint32_t tag;                           // this launch's call number
-    uint32_t issued;                        // bit 0: gate barrier issued, 1 + k: down barrier k issued
+    uint32_t issued;                        // bits 0..7: gate K-group barriers, 8: gate metadata, 9 + k: down slot k
     int32_t abort;
     float shared_gate;                      // sigmoid of the shared expert's logit (bf16 table value)
 };
@@ -113,6 +115,26 @@ __device__ __forceinline__ void d1_wait_prior_grid() { asm volatile("griddepcont
 // The plan hand-off from the routing warp to the copy warp (named barrier 2).
 __device__ __forceinline__ void d1_plan_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
 __device__ __forceinline__ void d1_plan_arrive() { asm volatile("bar.arrive 2, 64;" ::: "memory"); }
+// The gate item's end from warp 0 to the copy warp (named barrier 3).
+__device__ __forceinline__ void d1_gate_done_sync() { asm volatile("bar.sync 3, 64;" ::: "memory"); }
+__device__ __forceinline__ void d1_gate_done_arrive() { asm volatile("bar.arrive 3, 64;" ::: "memory"); }
+
+// The shared expert's gate logit of the token: fp32 products summed per lane
+// in k order (k = lane + 32i), then an xor tree across lanes, rounded to bf16
+// (the order of shared_logit_warp), with the token row read from shared
+// memory and the 64 weights of each lane loaded before the sum, so that the
+// warp waits for one round trip to memory instead of one per step.
+__device__ __forceinline__ uint16_t shared_logit_staged(const uint16_t* xs, const uint16_t* w, int lane) {
+    uint16_t wv[kH / 32];
+#pragma unroll
+    for (int i = 0; i < kH / 32; ++i) wv[i] = w[lane + 32 * i];
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < kH / 32; ++i) acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(xs[lane + 32 * i]), bf16_to_f32(wv[i])));
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    return bf16_rne(acc);
+}
 
 __device__ __forceinline__ void d1_flag_or(uint32_t* flags, uint32_t f) {
     f = __reduce_or_sync(0xffffffffu, f);
@@ -153,20 +175,29 @@ __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned l
 // (lane 0: the gate barrier, lane 1 + k: down slot k) before any copy starts.
 __device__ __forceinline__ void issue_copies(const LayerArgs& a, D1Smem& S, int lane, bool gate_item, int ge, int gp,
                                              int k0, int k1, int tile) {
-    if (gate_item && lane == 0) mbar_arrive_expect_tx(&S.gbar, 2 * (32768 + 1024));
-    if (lane >= 1 + k0 && lane < 1 + k1) mbar_arrive_expect_tx(&S.dbar[lane - 1], 8192 + 256);
+    // expect-tx first: lane 0 the gate metadata, lane 1 + g the gate item's
+    // K-group g, lane 9 + k down slot k
+    if (gate_item && lane == 0) mbar_arrive_expect_tx(&S.gmbar, 2 * 1024);
+    if (gate_item && lane >= 1 && lane < 9) mbar_arrive_expect_tx(&S.gbar[lane - 1], 2 * 4096);
+    if (lane >= 9 + k0 && lane < 9 + k1) mbar_arrive_expect_tx(&S.dbar[lane - 9], 8192 + 256);
     __syncwarp();
     int i = lane;
     if (gate_item) {
-        if (i < 4) {
-            const int r = i >> 1, tile_g = gp + 16 * r;
+        // copy 0..1: metadata of the gate and up tiles (1 KB each, all
+        // K-groups); copy 2 + 2g + r: K-group g of tile r (4 KB), one barrier
+        // per K-group so that its two warps start as soon as it has landed
+        if (i < 18) {
             const uint32_t* codes = ge == kE ? a.sgate_codes : a.gate_codes + size_t(ge) * (2 * kI) * (kH / 8);
             const uint32_t* meta = ge == kE ? a.sgate_meta : a.gate_meta + size_t(ge) * (2 * kI) * (kH / kG);
-            if ((i & 1) == 0) bulk_g2s(S.gate_codes[r], codes + size_t(tile_g) * 8 * 1024, 32768, &S.gbar);
-            else bulk_g2s(S.gate_meta[r], meta + size_t(tile_g) * 8 * 32, 1024, &S.gbar);
+            if (i < 2) {
+                bulk_g2s(S.gate_meta[i], meta + size_t(gp + 16 * i) * 8 * 32, 1024, &S.gmbar);
+            } else {
+                const int g = (i - 2) >> 1, r = (i - 2) & 1;
+                bulk_g2s(S.gate_codes[r][g], codes + (size_t(gp + 16 * r) * 8 + g) * 1024, 4096, &S.gbar[g]);
+            }
             return;
         }
-        i -= 4;
+        i -= 18;
     }
     const int k = k0 + (i >> 1);
     if (i < 0 || k >= k1) return;
@@ -224,7 +255,8 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
     if (warp == kD1Copier) {
         if (lane == 0) {
             D1_STAMP(0);
-            mbar_init(&S.gbar, 1);
+            for (int g = 0; g < 8; ++g) mbar_init(&S.gbar[g], 1);
+            mbar_init(&S.gmbar, 1);
             for (int i = 0; i < kD1Slots; ++i) mbar_init(&S.dbar[i], 1);
             fence_barrier_init();
             if (a.shared) S.act_e[0] = kE;  // plan slot 0, before its copies are issued
@@ -258,8 +290,8 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
                      tile);
         if (lane == 0) {
             S.tag = tag;
-            S.issued = (has_gate ? 1u : 0u) | (is_down ? 1u << 1 : 0u) * (a.shared ? 1u : 0u) |
-                       (down_now ? ((1u << NA) - 1u) << 1 : 0u);
+            S.issued = (has_gate ? 0x1ffu : 0u) | (is_down ? 1u << 9 : 0u) * (a.shared ? 1u : 0u) |
+                       (down_now ? ((1u << NA) - 1u) << 9 : 0u);
             D1_STAMP(4);
         }
     } else if (warp == kD1Router) {
@@ -296,6 +328,7 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         d1_wait_prior_grid();
         // the token's 256-groups: warp g transforms and quantises group g
         const uint4 raw = *reinterpret_cast<const uint4*>(a.x + warp * kG + lane * 8);
+        reinterpret_cast<uint4*>(S.xraw)[warp * 32 + lane] = raw;  // for the shared expert's logit
         uint32_t qf = wht_quant<QMAX>(
             __uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u), __uint_as_float(raw.y << 16),
             __uint_as_float(raw.y & 0xffff0000u), __uint_as_float(raw.z << 16), __uint_as_float(raw.z & 0xffff0000u),
@@ -304,18 +337,6 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         qf = __reduce_or_sync(0xffffffffu, qf);
         if (lane == 0) S.xflag[warp] = qf;
         if (tid == 0) D1_STAMP(5);
-    } else if (warp == kD1Logit && a.shared && is_down) {
-        d1_wait_prior_grid();
-        // the shared expert's output gate, sigmoid(logit) from the caller's
-        // table, needed by the combine: fetched now, off the critical path
-        uint16_t v;
-        if (a.shared_gate_weight) {
-            v = shared_logit_warp(a.x, a.shared_gate_weight, lane);
-            if (lane == 0 && tile == 0) a.logit_out[0] = v;
-        } else {
-            v = a.shared_logit[0];
-        }
-        if (lane == 0) S.shared_gate = bf16_to_f32(a.sigmoid_table[v]);
     } else {
         d1_wait_prior_grid();
     }
@@ -336,17 +357,16 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
 
     if (warp == kD1Copier) {
         // a CTA with a gate item and a down tile: its routed down blocks once
-        // the gate item has landed
+        // the gate item is computed (barrier 3 from warp 0), so that neither
+        // the gate bytes nor the gate arithmetic share the CTA's copy engine
+        // and shared-memory port with them; they are needed only after the
+        // middle rows of every CTA are in
         const int base = a.shared ? 1 : 0;
         if (is_down && has_gate && NA > base) {
-            bool landed = true;
-            if (lane == 0) landed = d1_wait_copies(&S.gbar, &S.abort);
-            landed = __shfl_sync(0xffffffffu, int(landed), 0) != 0;
-            if (landed) {
+            d1_gate_done_sync();
+            if (!*reinterpret_cast<const volatile int32_t*>(&S.abort)) {
                 issue_copies(a, S, lane, false, 0, 0, base, NA, tile);
-                if (lane == 0) atomicOr(&S.issued, ((1u << NA) - 1u) << 1);
-            } else if (lane == 0) {
-                d1_give_up(S, a.flags);
+                if (lane == 0) atomicOr(&S.issued, ((1u << NA) - 1u) << 9);
             }
         }
     } else if (NA == 0) {
@@ -361,7 +381,7 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         if (has_gate) {
             if (warp < 16) {
                 const int g = warp >> 1, r = warp & 1;
-                if (d1_wait_copies(&S.gbar, &S.abort)) {
+                if (d1_wait_copies(&S.gbar[g], &S.abort) && d1_wait_copies(&S.gmbar, &S.abort)) {
                     if (lane == 0 && warp == 0) D1_STAMP(6);
                     const uint32_t* blk = reinterpret_cast<const uint32_t*>(S.gate_codes[r][g]);
                     const int dot = block_dot(blk, reinterpret_cast<const uint4*>(S.xq + g * kG), lane);
@@ -396,9 +416,19 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
                                (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(value));
                 if (lane == 0) D1_STAMP(9);
             }
+            if (warp == 0 && is_down && NA > (a.shared ? 1 : 0)) d1_gate_done_arrive();  // the copy warp's down blocks
         }
         // ---- output tile: warp 2k + g = slot k, K-group g ----------------------
         if (is_down) {
+            if (warp == kD1Combine && a.shared) {
+                // the shared expert's output gate, sigmoid(logit) from the
+                // caller's table, while the middle rows are still being made
+                const uint16_t v = a.shared_gate_weight ? shared_logit_staged(S.xraw, a.shared_gate_weight, lane)
+                                                        : a.shared_logit[0];
+                if (a.shared_gate_weight && lane == 0 && tile == 0) a.logit_out[0] = v;
+                const float gate = bf16_to_f32(a.sigmoid_table[v]);
+                if (lane == 0) S.shared_gate = gate;
+            }
             const int k = warp >> 1, g = warp & 1;
             bool ok = k < NA;
             if (ok) {
@@ -461,7 +491,7 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
                     const float v = down_value(S, 0, lane);
                     if (!isfinite(v)) f |= kFlagNonfiniteProjection;
                     route_out[size_t(kTop) * kH + col] = v;
-                } else if (warp == kTop + 1) {
+                } else if (warp == kD1Combine) {
                     // slot-ordered combine of the token (reduce_slots :176-185)
                     float sum = 0.f;
 #pragma unroll
@@ -505,9 +535,9 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
     __syncthreads();
     if (tid == 0 && S.abort) {
         const uint64_t t0 = d1_now();
-        for (int i = 0; i < 1 + kD1Slots; ++i) {
+        for (int i = 0; i < 9 + kD1Slots; ++i) {
             if (!(S.issued >> i & 1u)) continue;
-            uint64_t* bar = i == 0 ? &S.gbar : &S.dbar[i - 1];
+            uint64_t* bar = i < 8 ? &S.gbar[i] : i == 8 ? &S.gmbar : &S.dbar[i - 9];
             while (!mbar_try_wait(bar, 0) && d1_now() - t0 < kD1WaitNs) {
             }
         }

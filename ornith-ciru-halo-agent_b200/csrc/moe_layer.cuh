@@ -146,9 +146,14 @@ __device__ __forceinline__ void route_topk_warp(const float* l, int lane, int32_
     const int top_i = __shfl_sync(0xffffffffu, my_i, 0);
     const float mx = top_i >= 0 ? top : 0.f;
     const float ex = (lane < kTop && my_i >= 0) ? portable_exp(__fsub_rn(my_v, mx)) : 0.f;
+    // every lane gathers the eight terms first (independent shuffles), then
+    // adds them in slot order
+    float exs[kTop];
+#pragma unroll
+    for (int s = 0; s < kTop; ++s) exs[s] = __shfl_sync(0xffffffffu, ex, s);
     float sum = 0.f;
-#pragma unroll 1
-    for (int s = 0; s < kTop; ++s) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, s));
+#pragma unroll
+    for (int s = 0; s < kTop; ++s) sum = __fadd_rn(sum, exs[s]);
     if (lane < kTop) {
         ids[lane] = my_i;
         weights[lane] = my_i >= 0 ? __fdiv_rn(ex, sum) : 0.f;

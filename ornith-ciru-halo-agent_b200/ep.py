@@ -800,7 +800,25 @@ class ExpertParallelMoE:
                 getattr(self, name).close()
                 setattr(self, name, None)
 
+    def _single(self, x, ids, weights):
+        """One rank holds every expert: the layer itself, no exchange (the
+        single-GPU layer's result, bit for bit)."""
+        T = x.shape[0]
+        if T > self.capacity:
+            raise ValueError(f'{T} tokens exceed capacity {self.capacity}')
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+        if T:
+            native = self.native
+            fn = getattr(native.lib(), self.symbol)
+            native.check(fn(*[native.ptr(t) for t in (x.contiguous(), weights.contiguous(), ids.contiguous(),
+                                                      *self.banks, self.workspace)],
+                            self.workspace.numel(), native.ptr(out), native.ptr(self.flags), T, self.capacity,
+                            native.stream(x)), 'expert-parallel compute')
+        return out
+
     def __call__(self, x, ids, weights):
+        if self.world == 1:
+            return self._single(x, ids, weights)
         if self.combine_mode == 'partial':
             # the partial rows reach the combine without the ids: ids outside
             # -1..255 (flag 4 on one GPU) are flagged here, on the device
