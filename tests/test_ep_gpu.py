@@ -128,3 +128,69 @@ def test_expert_parallel_matches_single_gpu(T):
         assert cases is not None and flags == 0, (rank, flags, err)
         for case, ok, case_flags in cases:
             assert ok and case_flags == 0, (rank, case, case_flags)
+
+
+def _timeout_worker(rank, world, port, q):
+    """Fixed exchange over peer memory with a 50 ms wait limit; rank 1 sleeps
+    on the host before its layer call (no kernel of it in flight), so rank 0's
+    wait for rank 1's token rows runs out.  Rank 0 carries on and its flag-64
+    bit travels with its returned rows, so rank 1 reports flag 64 as well."""
+    try:
+        import datetime
+        import time
+        import torch.distributed as dist
+        os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), NCCL_NVLS_ENABLE='0')
+        torch.cuda.set_device(rank)
+        dev = torch.device('cuda', rank)
+        dist.init_process_group('nccl', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        sys.path.insert(0, str(ROOT))
+        import __graft_entry__ as g
+        g.load_package()
+        from ornith_b200 import ep, native
+        native.set_peer_wait_limit_ns(50_000_000)
+        T = 4
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        gc, gm = _bank(gen, 256 // world, 1024, 2048, dev)
+        dc, dm = _bank(gen, 256 // world, 2048, 512, dev)
+        x = torch.randn((T, 2048), device=dev, generator=gen).to(torch.bfloat16)
+        logits = torch.randn((T, 256), device=dev, generator=gen)
+        w = torch.empty((T, 8), dtype=torch.float32, device=dev)
+        ids = torch.empty((T, 8), dtype=torch.int32, device=dev)
+        rflags = torch.zeros(1, dtype=torch.int32, device=dev)
+        native.route_topk(logits, w, ids, rflags)
+        layer = ep.ExpertParallelMoE(None, world, (gc, gm, dc, dm), capacity=T * world, exchange='fixed',
+                                     transport='p2p')
+        layer.peer_fixed = ep.PeerFixedExchange(None, world, rank, T, dev)   # made collectively, before the sleep
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 1:
+            time.sleep(0.5)
+        layer(x, ids, w)
+        torch.cuda.synchronize()
+        flags = int(layer.flags.item())
+        dist.barrier()
+        layer.close()
+        q.put((rank, flags, ''))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:
+        q.put((rank, -1, repr(exc)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason='needs 2 GPUs')
+def test_fixed_peer_timeout_reaches_every_rank():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_timeout_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict((rank, (flags, err)) for rank, flags, err in (q.get(timeout=300) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    for rank in (0, 1):
+        flags, err = results[rank]
+        assert flags >= 0, err
+        assert flags & 64, (rank, flags)
