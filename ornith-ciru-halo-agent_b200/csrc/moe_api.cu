@@ -279,6 +279,14 @@ cudaError_t routed_launch(int act_bits, const void* input, const void* weights, 
     return run_layer(a, stream);
 }
 
+cudaError_t layer_from_logits(const void* input, const void* logits, const void* router_weight,
+                              const void* gate_codes, const void* gate_meta, const void* down_codes,
+                              const void* down_meta, const void* shared_gate_codes, const void* shared_gate_meta,
+                              const void* shared_down_codes, const void* shared_down_meta,
+                              const void* shared_gate_weight, const void* shared_silu, const void* shared_sigmoid,
+                              void* workspace, size_t bytes, void* output, void* shared_output, void* flags, int T,
+                              int Tcap, int act_bits, cudaStream_t stream);
+
 }  // namespace
 
 extern "C" {
@@ -478,6 +486,18 @@ cudaError_t ornith_moe_b200_launch_from_hidden(
     const void* shared_silu, const void* shared_sigmoid, void* workspace, size_t bytes, void* output,
     void* shared_output, void* flags, int T, int Tcap, int act_bits, cudaStream_t stream) {
     if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap) return cudaErrorInvalidValue;
+    // one token on the fused decode path: the single-token kernel computes the
+    // router logits itself (one launch per layer); it refuses devices it does
+    // not fit, and the separate router launch runs then
+    if (T == 1 && uses_decode(T)) {
+        if (!router_weight || !aligned(router_weight, 16)) return cudaErrorInvalidValue;
+        const cudaError_t st =
+            layer_from_logits(input, logits, router_weight, gate_codes, gate_meta, down_codes, down_meta,
+                              shared_gate_codes, shared_gate_meta, shared_down_codes, shared_down_meta,
+                              shared_gate_weight, shared_silu, shared_sigmoid, workspace, bytes, output,
+                              shared_output, flags, T, Tcap, act_bits, stream);
+        if (st != cudaErrorNotSupported) return st;
+    }
     cudaError_t st = ornith_moe_b200_router_logits(input, router_weight, T, logits, stream);
     if (st != cudaSuccess) return st;
     return ornith_moe_b200_launch_from_logits(input, logits, gate_codes, gate_meta, down_codes, down_meta,
@@ -499,6 +519,27 @@ cudaError_t ornith_moe_b200_launch_from_logits(
     const void* shared_down_meta, const void* shared_gate_weight, const void* shared_silu, const void* shared_sigmoid,
     void* workspace, size_t bytes, void* output, void* shared_output, void* flags, int T, int Tcap, int act_bits,
     cudaStream_t stream) {
+    return layer_from_logits(input, logits, nullptr, gate_codes, gate_meta, down_codes, down_meta, shared_gate_codes,
+                             shared_gate_meta, shared_down_codes, shared_down_meta, shared_gate_weight, shared_silu,
+                             shared_sigmoid, workspace, bytes, output, shared_output, flags, T, Tcap, act_bits,
+                             stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// The routed layer from router logits.  With router_weight (the from-hidden
+// entry at T = 1 on the fused decode path) the single-token kernel writes the
+// logits into `logits` itself, or the call returns cudaErrorNotSupported
+// having launched nothing.
+cudaError_t layer_from_logits(const void* input, const void* logits, const void* router_weight,
+                              const void* gate_codes, const void* gate_meta, const void* down_codes,
+                              const void* down_meta, const void* shared_gate_codes, const void* shared_gate_meta,
+                              const void* shared_down_codes, const void* shared_down_meta,
+                              const void* shared_gate_weight, const void* shared_silu, const void* shared_sigmoid,
+                              void* workspace, size_t bytes, void* output, void* shared_output, void* flags, int T,
+                              int Tcap, int act_bits, cudaStream_t stream) {
     if (Tcap < 0 || Tcap > kTcapMax || T < 0 || T > Tcap) return cudaErrorInvalidValue;
     if (act_bits != 0 && act_bits != 4 && act_bits != 8) return cudaErrorInvalidValue;
     const Workspace w = workspace_layout(Tcap);
@@ -527,6 +568,7 @@ cudaError_t ornith_moe_b200_launch_from_logits(
     // decode batches: the fused kernel routes and computes the shared logits
     // itself (one launch per layer); otherwise two small kernels run first
     const bool fused = uses_decode(T);
+    if (router_weight && (!fused || T != 1)) return cudaErrorNotSupported;
     cudaError_t s = cudaSuccess;
     if (!fused) {
         count_launches(1);
@@ -540,6 +582,10 @@ cudaError_t ornith_moe_b200_launch_from_logits(
         a.logits = static_cast<const float*>(logits);
         a.ids_out = tid;
         a.weights_out = tw;
+    }
+    if (router_weight) {
+        a.router_weight = static_cast<const uint16_t*>(router_weight);
+        a.logits_out = static_cast<float*>(const_cast<void*>(logits));
     }
     a.x = static_cast<const uint16_t*>(input);
     a.weights = tw;
@@ -576,8 +622,13 @@ cudaError_t ornith_moe_b200_launch_from_logits(
         a.shared = 1;
         a.shared_all_live = 1;
     }
+    if (router_weight) return launch_decode_single(a, stream);
     return run_layer(a, stream);
 }
+
+}  // namespace
+
+extern "C" {
 
 cudaError_t ornith_moe_b200_repack_n16_to_n32(const void* codes_n16, const void* meta_n16, void* codes_n32,
                                               void* meta_n32, int experts, int N, int K, cudaStream_t stream) {

@@ -84,6 +84,7 @@ struct __align__(128) D1Smem {
     uint32_t issued;                        // bits 0..7: gate K-group barriers, 8: gate metadata, 9 + k: down slot k
     int32_t abort;
     float shared_gate;                      // sigmoid of the shared expert's logit (bf16 table value)
+    float rlogits[kE];                      // router logits gathered from every CTA (from-hidden entry)
 };
 
 __device__ __forceinline__ uint64_t d1_now() {
@@ -95,7 +96,7 @@ __device__ __forceinline__ uint64_t d1_now() {
 // Optional phase timestamps (%globaltimer ns) per CTA, for latency analysis
 // only: compiled in with -DORNITH_DECODE1_TRACE, absent from the default build.
 #ifdef ORNITH_DECODE1_TRACE
-constexpr int kD1TraceSlots = 16;
+constexpr int kD1TraceSlots = 20;
 __device__ unsigned long long g_d1_trace[kD1MaxCtas][kD1TraceSlots];
 #define D1_STAMP(i) (g_d1_trace[blockIdx.x][i] = d1_now())
 #else
@@ -115,6 +116,41 @@ __device__ __forceinline__ void d1_wait_prior_grid() { asm volatile("griddepcont
 // The plan hand-off from the routing warp to the copy warp (named barrier 2).
 __device__ __forceinline__ void d1_plan_sync() { asm volatile("bar.sync 2, 64;" ::: "memory"); }
 __device__ __forceinline__ void d1_plan_arrive() { asm volatile("bar.arrive 2, 64;" ::: "memory"); }
+// The call number from the copy warp to the router-logit warps and the
+// routing warp (named barrier 4, from-hidden entry only).
+constexpr int kD1TagThreads = 4 * 32;
+__device__ __forceinline__ void d1_tag_sync() { asm volatile("bar.sync 4, %0;" ::"r"(kD1TagThreads) : "memory"); }
+__device__ __forceinline__ void d1_tag_arrive() { asm volatile("bar.arrive 4, %0;" ::"r"(kD1TagThreads) : "memory"); }
+
+// One router logit (gates_projection.py:17-25) by one warp, in the order of
+// router_logits_kernel: lane l holds k = 256j + 8l .. 8l+7 for j = 0..7, FMA
+// in j then element order, then an xor tree across lanes; every lane returns
+// the sum.  The same bits as the separate router launch.
+// The weight row is constant, so the caller loads it (router_row_load)
+// before waiting for the previous grid; x may come from that grid.
+__device__ __forceinline__ void router_row_load(const uint16_t* w_row, int lane, uint4 (&wr)[8]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wr[j] = __ldg(reinterpret_cast<const uint4*>(w_row + j * 256 + lane * 8));
+}
+__device__ __forceinline__ float router_logit_warp(const uint16_t* x, const uint4 (&wr)[8], int lane) {
+    uint4 xr[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr[j] = *reinterpret_cast<const uint4*>(x + j * 256 + lane * 8);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t xv[4] = {xr[j].x, xr[j].y, xr[j].z, xr[j].w}, wv[4] = {wr[j].x, wr[j].y, wr[j].z, wr[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            acc = __fmaf_rn(__uint_as_float(xv[i] << 16), __uint_as_float(wv[i] << 16), acc);
+            acc = __fmaf_rn(__uint_as_float(xv[i] & 0xffff0000u), __uint_as_float(wv[i] & 0xffff0000u), acc);
+        }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    return acc;
+}
+
 // The gate item's end from warp 0 to the copy warp (named barrier 3).
 __device__ __forceinline__ void d1_gate_done_sync() { asm volatile("bar.sync 3, 64;" ::: "memory"); }
 __device__ __forceinline__ void d1_gate_done_arrive() { asm volatile("bar.arrive 3, 64;" ::: "memory"); }
@@ -271,12 +307,14 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         if (lane == 0) {
             tag = *reinterpret_cast<const volatile uint32_t*>(ctrl + kCtrlD1Epoch) + 1u;
             if (tag == 0u) tag = 1u;  // 0 never tags a call, so never-written words never match
+            S.tag = tag;
             // seen: the stored value depends on the epoch read, so the read has
             // completed when any CTA observes it.  Relaxed rather than release:
             // a release here would also wait for this thread's bulk copies.
             st_relaxed_u32(ctrl + kCtrlD1Seen + b, tag);
         }
         __syncwarp();
+        if (a.router_weight) d1_tag_arrive();  // the router-logit and routing warps need the call number
         d1_plan_sync();  // the routing warp's plan
         if (lane == 0) D1_STAMP(3);
         const int NA = S.nslot, base = a.shared ? 1 : 0, gk = b / 16;
@@ -289,7 +327,6 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         issue_copies(a, S, lane, routed_gate, routed_gate ? S.act_e[gk] : 0, b % 16, base, down_now ? NA : base,
                      tile);
         if (lane == 0) {
-            S.tag = tag;
             S.issued = (has_gate ? 0x1ffu : 0u) | (is_down ? 1u << 9 : 0u) * (a.shared ? 1u : 0u) |
                        (down_now ? ((1u << NA) - 1u) << 9 : 0u);
             D1_STAMP(4);
@@ -298,7 +335,39 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         d1_wait_prior_grid();
         // router top-8 (from logits) or the caller's ids, then the plan
         uint32_t rf = 0;
-        if (a.logits) {
+        if (a.router_weight) {
+            // the logits come from every CTA's router warps as call-numbered
+            // words; a wait that runs out routes nothing (ids -1, flag 64)
+            d1_tag_sync();
+            const uint32_t tag = S.tag;
+            // this CTA's copy of the words; a warp load covers 512 contiguous bytes
+            const unsigned long long* src =
+                ws_at<unsigned long long>(a, a.L.xlogit) + (b % kD1LogitCopies) * kE + 2 * lane;
+            unsigned long long wv[8];
+            const uint64_t t0 = d1_now();
+            bool got = true;
+            for (;;) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) ld_relaxed_v2(src + 64 * i, wv[2 * i], wv[2 * i + 1]);
+                bool mine = true;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mine &= uint32_t(wv[i] >> 32) == tag;
+                if (__all_sync(0xffffffffu, mine)) break;
+                if (__shfl_sync(0xffffffffu, int(d1_now() - t0 > kD1WaitNs), 0)) {
+                    got = false;
+                    break;
+                }
+                __nanosleep(32);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                S.rlogits[64 * (i / 2) + 2 * lane + i % 2] =
+                    got ? __uint_as_float(uint32_t(wv[i])) : __uint_as_float(0x7fc00000u);
+            if (!got && lane == 0) d1_give_up(S, a.flags);
+            if (lane == 0) D1_STAMP(19);
+            __syncwarp();
+            route_topk_warp(S.rlogits, lane, S.ids, S.wts, rf);
+        } else if (a.logits) {
             route_topk_warp(a.logits, lane, S.ids, S.wts, rf);
         } else if (lane < kTop) {
             S.ids[lane] = a.ids[lane];
@@ -337,6 +406,25 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
         qf = __reduce_or_sync(0xffffffffu, qf);
         if (lane == 0) S.xflag[warp] = qf;
         if (tid == 0) D1_STAMP(5);
+    } else if (a.router_weight && (warp == 8 || warp == 9)) {
+        // router logits of experts b and b + G (gates_projection.py:17-25):
+        // into the caller's logits and, tagged with the call number, into the
+        // exchange words every CTA's routing warp reads
+        const int e = b + (warp - 8) * G;
+        uint4 wr[8];
+        if (e < kE) router_row_load(a.router_weight + size_t(e) * kH, lane, wr);
+        d1_wait_prior_grid();
+        if (lane == 0 && warp == 8) D1_STAMP(16);
+        float v = 0.f;
+        if (e < kE) v = router_logit_warp(a.x, wr, lane);
+        if (lane == 0 && warp == 8) D1_STAMP(17);
+        d1_tag_sync();
+        if (e < kE && lane < kD1LogitCopies) {
+            if (lane == 0) a.logits_out[e] = v;
+            st_relaxed_u64(ws_at<unsigned long long>(a, a.L.xlogit) + lane * kE + e,
+                           (static_cast<unsigned long long>(S.tag) << 32) | __float_as_uint(v));
+        }
+        if (lane == 0 && warp == 8) D1_STAMP(18);
     } else {
         d1_wait_prior_grid();
     }
@@ -581,6 +669,7 @@ cudaError_t launch_decode_single(const LayerArgs& a, cudaStream_t stream) {
     const size_t smem = sizeof(D1Smem);
     // one CTA per gate item and per output tile, at most kD1MaxCtas seen-words
     if (d.sms < kD1GateItems || d.sms > kD1MaxCtas || size_t(d.max_smem) < smem) return cudaErrorNotSupported;
+    if (a.router_weight && 2 * d.sms < kE) return cudaErrorNotSupported;  // two router logits per CTA at most
     const int which = a.a8 ? 0 : 1;
     auto kernel = a.a8 ? decode_single_kernel<127> : decode_single_kernel<7>;
     if (!d.attr_set[which]) {
@@ -619,7 +708,7 @@ cudaError_t launch_decode_single(const LayerArgs& a, cudaStream_t stream) {
 }
 
 #ifdef ORNITH_DECODE1_TRACE
-// Copies the phase timestamps of the last single-token launch (256 x 16 u64)
+// Copies the phase timestamps of the last single-token launch (256 x 20 u64)
 // and clears them.
 extern "C" __attribute__((visibility("default"))) int ornith_moe_b200_decode1_trace(void* dst) {
     cudaError_t st = cudaMemcpyFromSymbol(dst, g_d1_trace, sizeof(g_d1_trace));

@@ -37,6 +37,7 @@ Workspace workspace_layout(int Tcap) {
     add(w.topk_ids, t * kTop * 4);
     add(w.logit, t * 2);
     add(w.xchg, size_t(kTop + 1) * kI * 8);
+    add(w.xlogit, size_t(kD1LogitCopies) * kE * 8);
     if (Tcap > kDecodeMaxT) {
         const size_t mt = (rows + 127) / 128 + (kE + 1);
         add(w.rowpos, rows * 4);

@@ -21,6 +21,7 @@ struct Workspace {
     size_t ctrl;                  // counters of the fused kernels
     size_t topk_w, topk_ids, logit;  // router outputs of the from-logits entry point
     size_t xchg;                  // single-token decode: middle rows as (call number, fp32) words [9][512] u64
+    size_t xlogit;                // single-token decode from hidden: router logits as (call number, fp32) words [kD1LogitCopies][256]
     // tensor-core prefill path (only when Tcap > kDecodeMaxT)
     size_t rowpos, slot_tiles, mtiles, n_mtiles;
     size_t pblock;                // per-block expert counts, then bases [kPlanBlocks][E+1] (x2)
@@ -50,6 +51,11 @@ constexpr int kCtrlClearWords = 1072;  // words zeroed before every fused launch
 // that the multi-token kernel's clear does not touch them.
 constexpr int kCtrlD1Epoch = 1088;     // call number of the last completed launch
 constexpr int kCtrlD1Seen = 1104;      // [kD1MaxCtas] a CTA read the epoch of this launch
+// Copies of the single-token kernel's router-logit words: every CTA polls
+// one of them, so that no line of the exchange is read by more than
+// ceil(CTAs / copies) CTAs at once (polls of every CTA on one copy were
+// found to serialise on its lines).
+constexpr int kD1LogitCopies = 16;
 constexpr int kD1MaxCtas = 256;
 static_assert(kCtrlD1Seen + kD1MaxCtas <= kCtrlWords, "single-token decode words fit the control block");
 
@@ -84,6 +90,10 @@ struct LayerArgs {
     int32_t* ids_out;
     float* weights_out;
     uint16_t* logit_out;
+    // router linear inside the single-token kernel (from-hidden entry, T = 1):
+    // logits = x . router_weight^T, written to logits_out and routed from
+    const uint16_t* router_weight;  // bf16 [256][2048]
+    float* logits_out;              // fp32 [256]
     Workspace L;
     int T;
     int a8;

@@ -679,3 +679,81 @@ def test_single_token_kernel_call_numbers(native, layer1, bank1, S, O):
         torch.cuda.synchronize()
         np.testing.assert_array_equal(host_bits(out)[:T], refs[i][0], err_msg=f'call {rep}')
         assert int(flags.item()) == refs[i][2], f'call {rep}'
+
+
+def run_from_hidden(native, x, router, bank, shared_args, Tcap, ws=None):
+    """One routed_from_hidden call; returns (logits bits, out bits, shared bits, flags)."""
+    T = x.shape[0]
+    if ws is None:
+        ws = torch.empty(native.workspace_bytes(Tcap), dtype=torch.uint8, device=DEV)
+    logits = torch.full((T, 256), float('nan'), dtype=torch.float32, device=DEV)
+    out = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV)
+    shared = torch.empty((T, 2048), dtype=torch.bfloat16, device=DEV) if shared_args[0] is not None else None
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    native.routed_from_hidden(dev(x), router, logits, *bank.routed, *shared_args, ws, out, shared, flags, Tcap, 0)
+    torch.cuda.synchronize()
+    return (logits.cpu().numpy().view(np.uint32), host_bits(out),
+            None if shared is None else host_bits(shared), int(flags.item()))
+
+
+@pytest.mark.parametrize('with_shared', [False, True])
+def test_single_token_from_hidden_router_in_kernel(native, layer1, bank1, S, O, tables, with_shared, monkeypatch):
+    """T = 1 from hidden states: the single-token kernel computes the router
+    linear itself.  Its logits equal the router launch's bit for bit, and its
+    outputs and flags equal the from-logits entry fed those logits, the
+    two-launch path (ORNITH_MOE_B200_DECODE1=0) and the oracle routed from
+    the same logits; one case has a +inf input (non-finite logits, flag 1)."""
+    silu, sigmoid = dev(tables['silu_fp32']), dev(tables['sigmoid_bf16'])
+    shared_args = ((*bank1.shared, dev(bank1.gate_w), silu, sigmoid) if with_shared else (None,) * 7)
+    rng = np.random.default_rng(900 + with_shared)
+    router = dev(S.make_router(rng))
+    for case in range(5):
+        x = S.make_tokens(rng, 1)
+        if case == 4:
+            x[0, 100] = 0x7F80
+        monkeypatch.delenv('ORNITH_MOE_B200_DECODE1', raising=False)
+        lg, out, sh, fl = run_from_hidden(native, x, router, bank1, shared_args, 1)
+        sep = torch.empty((1, 256), dtype=torch.float32, device=DEV)
+        native.router_logits(dev(x), router, sep)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(lg, sep.cpu().numpy().view(np.uint32))
+        monkeypatch.setenv('ORNITH_MOE_B200_DECODE1', '0')
+        lg2, out2, sh2, fl2 = run_from_hidden(native, x, router, bank1, shared_args, 1)
+        monkeypatch.delenv('ORNITH_MOE_B200_DECODE1', raising=False)
+        np.testing.assert_array_equal(lg2, lg)
+        np.testing.assert_array_equal(out2, out)
+        assert fl2 == fl
+        logits = sep.cpu().numpy()
+        w, ids = O.route_topk(logits)
+        if with_shared:
+            lgs = shared_logit_like_device(x, bank1.gate_w)
+            ref, ref_sh, _, ref_flags = O.routed_layer_shared(x, w, ids, *bank1.np_routed, *bank1.np_shared, lgs,
+                                                              tables['silu_fp32'], tables['sigmoid_bf16'])
+            np.testing.assert_array_equal(sh, ref_sh)
+            np.testing.assert_array_equal(sh2, sh)
+        else:
+            ref, _, ref_flags = O.routed_layer(x, w, ids, *bank1.np_routed, a8=True)
+        np.testing.assert_array_equal(out, ref)
+        nonfinite = 1 if not np.all(np.isfinite(logits)) else 0
+        assert fl == ref_flags | nonfinite
+
+
+def test_single_token_from_hidden_call_numbers(native, layer1, bank1, S):
+    """The router words the single-token kernel exchanges carry call numbers:
+    one workspace that starts as all-ones bytes, T = 1 and T = 3 calls
+    alternating, every T = 1 call equal to its first run."""
+    rng = np.random.default_rng(61)
+    router = dev(S.make_router(rng))
+    xs = [S.make_tokens(rng, T) for T in (1, 3, 1, 1, 3)]
+    ws = torch.full((native.workspace_bytes(8),), 255, dtype=torch.uint8, device=DEV)
+    none = (None,) * 7
+    first = {}
+    for rep in range(25):
+        i = rep % len(xs)
+        got = run_from_hidden(native, xs[i], router, bank1, none, 8, ws)
+        if i in first:
+            for a, b in zip(got[:2], first[i][:2]):
+                np.testing.assert_array_equal(a, b, err_msg=f'call {rep}')
+            assert got[3] == first[i][3] == 0
+        else:
+            first[i] = got
