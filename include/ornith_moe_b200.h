@@ -300,7 +300,11 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_router_logits(
 
 /* The router linear followed by ornith_moe_b200_launch_from_logits: the
  * logits are written to logits_f32 [T,256] (caller memory) and routed from
- * there.  Same workspace, outputs and flags as the from-logits entry. */
+ * there.  Same workspace, outputs and flags as the from-logits entry.  At
+ * T = 1 on the fused decode path one launch does both: the single-token
+ * kernel computes the logits (the same bits as ornith_moe_b200_router_logits),
+ * writes them to logits_f32 and routes from its own copy; where that kernel
+ * does not fit the device the two launches run instead. */
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_launch_from_hidden(
     const void* input_bf16, const void* router_weight_bf16, void* logits_f32,
     const void* gate_codes, const void* gate_meta, const void* down_codes, const void* down_meta,
