@@ -562,6 +562,19 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
                     }
                 }
             }
+            // the combine's per-slot plan into registers before the barrier, so
+            // that after it only the down terms are read
+            int cslot[kTop];
+            float cwt[kTop];
+            bool cround[kTop];
+            if (warp == kD1Combine) {
+#pragma unroll
+                for (int sl = 0; sl < kTop; ++sl) {
+                    cslot[sl] = id_valid(S.ids[sl]) ? S.slot_of[sl] : -1;
+                    cwt[sl] = S.wts[sl];
+                    cround[sl] = cslot[sl] >= 0 && S.act_e[cslot[sl]] == kE;
+                }
+            }
             d1_barrier();
             if (tid == 0) D1_STAMP(14);
             if (!*reinterpret_cast<const volatile int32_t*>(&S.abort)) {
@@ -581,11 +594,17 @@ __global__ void __launch_bounds__(kD1Threads, 1) decode_single_kernel(const Laye
                     route_out[size_t(kTop) * kH + col] = v;
                 } else if (warp == kD1Combine) {
                     // slot-ordered combine of the token (reduce_slots :176-185)
+                    float dv[kTop];
+#pragma unroll
+                    for (int sl = 0; sl < kTop; ++sl) {
+                        const int kk = cslot[sl] < 0 ? 0 : cslot[sl];
+                        const float v = __fadd_rn(__fadd_rn(0.f, S.dterm[kk][0][lane]), S.dterm[kk][1][lane]);
+                        dv[sl] = cround[sl] ? bf16_round_f32(v) : v;  // as down_value
+                    }
                     float sum = 0.f;
 #pragma unroll
                     for (int sl = 0; sl < kTop; ++sl)
-                        if (id_valid(S.ids[sl]))
-                            sum = __fadd_rn(sum, __fmul_rn(down_value(S, S.slot_of[sl], lane), S.wts[sl]));
+                        if (cslot[sl] >= 0) sum = __fadd_rn(sum, __fmul_rn(dv[sl], cwt[sl]));
                     const uint16_t res = bf16_rne(sum);
                     ws_at<float>(a, a.L.final_f32)[col] = sum;
                     a.out[col] = res;
