@@ -213,17 +213,17 @@ __device__ __forceinline__ void wht128_halfwarp(float (&e)[8], int lane) {
 #pragma unroll
         for (int s = 0; s < 8; ++s) e[s] = n[s];
     }
-    // across lanes: the upper lane of each pair computes other - e, which is
-    // the IEEE sum (-e) + other, so every lane adds, after flipping its own
-    // value's sign where it is the upper lane (the same results as choosing
-    // between the subtraction and the addition)
+    // across lanes: the upper lane of each pair computes other - e, the IEEE
+    // sum (-e) + other, and the lower one e + other.  fma(sign, e, other) with
+    // sign = -1 or +1 is that sum in one instruction: the product is exact and
+    // the single rounding is the addition's, signed zeros included.
 #pragma unroll
     for (int lstep = 1; lstep < 16; lstep *= 2) {
-        const uint32_t flip = (lane & lstep) != 0 ? 0x80000000u : 0u;
+        const float sign = (lane & lstep) != 0 ? -1.f : 1.f;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
             const float other = __shfl_xor_sync(0xffffffffu, e[s], lstep);
-            e[s] = __fadd_rn(__uint_as_float(__float_as_uint(e[s]) ^ flip), other);
+            e[s] = __fmaf_rn(sign, e[s], other);
         }
     }
 #pragma unroll

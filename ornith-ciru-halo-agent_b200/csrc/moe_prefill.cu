@@ -454,9 +454,13 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
             if (!named_and(1, kEpiWarps * 32, !*abort)) break;
             const int4 mt = p.mtiles[unit / NUPT];
             const int nt = unit % NUPT;
-            float acc[64];
+            // 64 accumulators as 32 packed pairs (columns 2i, 2i + 1): the
+            // per-group sequence runs on f32x2 arithmetic, two IEEE
+            // round-to-nearest results per instruction, each the scalar one
+            float2 acc2[32];
 #pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+            for (int i = 0; i < 32; ++i) acc2[i] = make_float2(0.f, 0.f);
+            auto acc = [&](int i) -> float { return (i & 1) ? acc2[i >> 1].y : acc2[i >> 1].x; };
             bool ok = true;
             for (int g = 0; g < KG; ++g, ++gg) {
                 const int b = gg & 1;
@@ -483,6 +487,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 const float sa = reinterpret_cast<const float*>(mslot + kNT * 4)[row];
                 const int ssumi = reinterpret_cast<const int32_t*>(mslot + kNT * 4 + kMT * 4)[row];
                 const float ssum = __fmul_rn(sa, float(ssumi));
+                const float2 sa2 = make_float2(sa, sa), ssum2 = make_float2(ssum, ssum);
+                const float2 nmagic2 = make_float2(-kMagicF, -kMagicF);
                 const uint32_t base = tmem + lane_base + uint32_t(b * kNT);
 #pragma unroll
                 for (int part = 0; part < 4; ++part) {
@@ -494,14 +500,23 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                     for (int q = 0; q < 4; ++q) {
                         const float4 sw4 = *reinterpret_cast<const float4*>(swf + col + 4 * q);
                         const float4 of4 = *reinterpret_cast<const float4*>(offf + col + 4 * q);
-                        const float sw[4] = {sw4.x, sw4.y, sw4.z, sw4.w}, of[4] = {of4.x, of4.y, of4.z, of4.w};
 #pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            const int i = 4 * q + h;
-                            const float fd = __fsub_rn(__uint_as_float(r[i]), kMagicF);
-                            const float scaled_dot = __fmul_rn(sa, fd);
-                            const float term = __fadd_rn(__fmul_rn(sw[h], scaled_dot), __fmul_rn(of[h], ssum));
-                            acc[part * 16 + i] = __fadd_rn(acc[part * 16 + i], term);
+                        for (int hp = 0; hp < 2; ++hp) {
+                            const int i = 4 * q + 2 * hp;
+                            const float2 sw2 = hp ? make_float2(sw4.z, sw4.w) : make_float2(sw4.x, sw4.y);
+                            const float2 of2 = hp ? make_float2(of4.z, of4.w) : make_float2(of4.x, of4.y);
+                            // fd = dot exactly (r - 1.5*2^23), then sw*(sa*fd) + of*ssum:
+                            // packed products, scalar sums of products.  A packed
+                            // sum with a packed product among its operands was
+                            // found contracted into a fused multiply-add on sm_100a
+                            // despite .rn and -fmad=false, changing the rounding.
+                            const float2 fd2 =
+                                __fadd2_rn(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), nmagic2);
+                            const float2 p1 = __fmul2_rn(sw2, __fmul2_rn(sa2, fd2));
+                            const float2 p2 = __fmul2_rn(of2, ssum2);
+                            const float2 term2 = make_float2(__fadd_rn(p1.x, p2.x), __fadd_rn(p1.y, p2.y));
+                            float2& a2 = acc2[(part * 16 + i) >> 1];
+                            a2 = __fadd2_rn(a2, term2);
                         }
                     }
                     tmem_st16_const(base + col, kMagic);
@@ -532,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         float v[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            const float gv = bf16_round_f32(acc[4 * k + j]), uv = bf16_round_f32(acc[32 + 4 * k + j]);
+                            const float gv = bf16_round_f32(acc(4 * k + j)), uv = bf16_round_f32(acc(32 + 4 * k + j));
                             if (valid && (!isfinite(gv) || !isfinite(uv))) f |= kFlagNonfiniteProjection;
                             v[j] = bf16_round_f32(__fmul_rn(p.silu_table[__float_as_uint(gv) >> 16], uv));
                             if (valid && !isfinite(v[j])) f |= kFlagNonfiniteMiddle;
@@ -550,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         float gs[8], q[8], v[8];
                         bool ok[8];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) gs[j] = valid ? acc[i + j] : 1.f;
+                        for (int j = 0; j < 8; ++j) gs[j] = valid ? acc(i + j) : 1.f;
 #pragma unroll
                         for (int j = 0; j < 8; ++j) q[j] = silu_quotient_fast(gs[j], ok[j]);
 #pragma unroll
@@ -558,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                             if (!ok[j]) q[j] = __fdiv_rn(gs[j], __fadd_rn(1.f, portable_exp(-gs[j])));
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
-                            const float gv = acc[i + j], uv = acc[32 + i + j];
+                            const float gv = acc(i + j), uv = acc(32 + i + j);
                             if (valid && (!isfinite(gv) || !isfinite(uv))) f |= kFlagNonfiniteProjection;
                             v[j] = __fmul_rn(q[j], uv);
                             if (valid && !isfinite(v[j])) f |= kFlagNonfiniteMiddle;
@@ -583,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         float v[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            v[j] = shared ? bf16_round_f32(acc[32 * h + 4 * k + j]) : acc[32 * h + 4 * k + j];
+                            v[j] = shared ? bf16_round_f32(acc(32 * h + 4 * k + j)) : acc(32 * h + 4 * k + j);
                             if (valid && !isfinite(v[j])) f |= kFlagNonfiniteProjection;
                         }
                         c[k] = make_float4(v[0], v[1], v[2], v[3]);
