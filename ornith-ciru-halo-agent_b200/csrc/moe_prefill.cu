@@ -52,11 +52,13 @@ constexpr int kBpBytes = kNT * 128 / 2;   // packed codes half-tile
 constexpr int kBuBytes = kNT * 128;       // unpacked codes half-tile
 constexpr int kStageBytes = kABytes + kBpBytes + kBuBytes;
 constexpr int kMetaBytes = kNT * 4 + kMT * 4 + kMT * 4;  // B meta, A scale, A sum
-constexpr int kMetaFBytes = kNT * 4 * 2;                   // fp32 column scales then offsets
+constexpr int kEpiWarps = 16;
+// fp32 column scales then offsets of one epilogue warp's 64 columns, one copy per warp
+constexpr int kMetaFWarpFloats = 2 * 64;
+constexpr int kMetaFBytes = kEpiWarps * kMetaFWarpFloats * 4;
 constexpr int kMetaSlots = 4;  // metadata ring: the producer runs up to 4 groups ahead of the epilogue
 constexpr int kWarps = 24;
 constexpr int kThreads = kWarps * 32;
-constexpr int kEpiWarps = 16;
 constexpr int kEpiFirst = 8;    // epilogue warps 8..23 (warpgroups 2..5)
 // Converter warps 2..5, one per scheduler.  Dealing the conversion over warps
 // 2..7 instead was measured slower on a B200 (46.3 against 45.8 ms per
@@ -242,8 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* stages = smem;
     uint8_t* metabuf = smem + kStages * kStageBytes;  // [kMetaSlots][kMetaBytes]
-    float* metaf = reinterpret_cast<float*>(metabuf + kMetaSlots * kMetaBytes);  // [2][scales 256 | offsets 256]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(metabuf + kMetaSlots * kMetaBytes + 2 * kMetaFBytes);
+    float* metaf = reinterpret_cast<float*>(metabuf + kMetaSlots * kMetaBytes);  // [epilogue warp][scales 64 | offsets 64]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(metabuf + kMetaSlots * kMetaBytes + kMetaFBytes);
     uint64_t* full = bars;                       // [kStages] producer -> converters
     uint64_t* conv = bars + kStages;             // [kStages] converters -> MMA
     uint64_t* empty = bars + 2 * kStages;        // [kStages] MMA -> producer
@@ -447,9 +449,11 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
         uint32_t f = 0;
         int gg = 0;
         int un = 0;  // units done (trace index)
-        const int et = tid - kEpiFirst * 32;  // 0..511 within the epilogue warps
-        // Every exit from these loops is a collective decision (named_and), so the
-        // 16 warps always pass the same sequence of barrier 1.
+        float* const wmeta = metaf + ew * kMetaFWarpFloats;  // this warp's converted column metadata
+        // The only barrier of the epilogue warps is the vote at each unit's
+        // start (named_and), which every warp reaches once per unit: a warp
+        // whose wait fails skips the rest of its unit, and the next vote ends
+        // the loop for all of them (the failed wait has raised the abort state).
         for (int unit = blockIdx.x; unit < n_units; unit += gridDim.x) {
             if (!named_and(1, kEpiWarps * 32, !*abort)) break;
             const int4 mt = p.mtiles[unit / NUPT];
@@ -466,24 +470,30 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 const int b = gg & 1;
                 const int ms = gg % kMetaSlots;
                 const uint8_t* mslot = metabuf + ms * kMetaBytes;
-                const bool mine = ok && bwait(&meta_full[ms], uint32_t(gg / kMetaSlots) & 1u, abort, p.flags);
-                // the group's column metadata, converted once for all rows
-                if (mine && et < kNT) {
-                    const uint32_t mw = reinterpret_cast<const uint32_t*>(mslot)[et];
-                    metaf[b * 2 * kNT + et] = __half2float(__ushort_as_half(uint16_t(mw & 0xffffu)));
-                    metaf[b * 2 * kNT + kNT + et] = __half2float(__ushort_as_half(uint16_t(mw >> 16)));
+                if (!ok || !bwait(&meta_full[ms], uint32_t(gg / kMetaSlots) & 1u, abort, p.flags)) {
+                    ok = false;  // the unit's remaining groups are skipped; the next vote ends the loop
+                    continue;
                 }
-                ok = named_and(1, kEpiWarps * 32, mine);
-                if (!ok) break;
+                // this warp's 64 columns of the group's metadata, in its own copy
+                // (the previous group's reads of it ended at that group's __syncwarp)
+                {
+                    const uint32_t m0 = reinterpret_cast<const uint32_t*>(mslot)[c0 + lane];
+                    const uint32_t m1 = reinterpret_cast<const uint32_t*>(mslot)[c1 + lane];
+                    wmeta[lane] = __half2float(__ushort_as_half(uint16_t(m0 & 0xffffu)));
+                    wmeta[32 + lane] = __half2float(__ushort_as_half(uint16_t(m1 & 0xffffu)));
+                    wmeta[64 + lane] = __half2float(__ushort_as_half(uint16_t(m0 >> 16)));
+                    wmeta[96 + lane] = __half2float(__ushort_as_half(uint16_t(m1 >> 16)));
+                    __syncwarp();
+                }
                 if (ew == 0 && lane == 0) PREFILL_TRACE(6, gg);
                 if (!bwait(&acc_full[b], uint32_t(gg / 2) & 1u, abort, p.flags)) {
-                    ok = false;  // voted at the next barrier
+                    ok = false;
                     continue;
                 }
                 tc_fence_after();
                 if (ew == 0 && lane == 0) PREFILL_TRACE(7, gg);
-                const float* swf = metaf + b * 2 * kNT;
-                const float* offf = swf + kNT;
+                const float* swf = wmeta;       // local column j: c0 + j (j < 32), c1 + j - 32
+                const float* offf = wmeta + 64;
                 const float sa = reinterpret_cast<const float*>(mslot + kNT * 4)[row];
                 const int ssumi = reinterpret_cast<const int32_t*>(mslot + kNT * 4 + kMT * 4)[row];
                 const float ssum = __fmul_rn(sa, float(ssumi));
@@ -493,13 +503,14 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
 #pragma unroll
                 for (int part = 0; part < 4; ++part) {
                     const int col = (part < 2 ? c0 : c1) + 16 * (part & 1);
+                    const int lcol = 16 * part;  // the same columns in the warp's metadata copy
                     uint32_t r[16];
                     tmem_ld16(base + col, r);
                     tmem_wait_ld();
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const float4 sw4 = *reinterpret_cast<const float4*>(swf + col + 4 * q);
-                        const float4 of4 = *reinterpret_cast<const float4*>(offf + col + 4 * q);
+                        const float4 sw4 = *reinterpret_cast<const float4*>(swf + lcol + 4 * q);
+                        const float4 of4 = *reinterpret_cast<const float4*>(offf + lcol + 4 * q);
 #pragma unroll
                         for (int hp = 0; hp < 2; ++hp) {
                             const int i = 4 * q + 2 * hp;
@@ -530,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                 }
                 if (ew == 0 && lane == 0) PREFILL_TRACE(8, gg);
             }
-            if (!ok) break;
+            if (!ok) continue;  // the next unit's vote ends the loop
             if (ew == 0 && lane == 0) PREFILL_TRACE(9, 2 + 4 * un);
             // Unit results, written as whole 128-byte lines: the eight float4
             // chunks of a lane are transposed across its group of eight lanes,
@@ -884,7 +895,7 @@ __global__ __launch_bounds__(256) void pack_middle_kernel(LayerArgs a) {
     }
 }
 
-constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + kMetaSlots * kMetaBytes + 2 * kMetaFBytes + 64 * 8 + 64;
+constexpr size_t kMmaSmem = size_t(kStages) * kStageBytes + kMetaSlots * kMetaBytes + kMetaFBytes + 64 * 8 + 64;
 
 struct DeviceState {
     int sms = 0;
