@@ -566,31 +566,38 @@ __global__ void __launch_bounds__(kThreads, 1) mma_kernel(const MmaArgs p) {
                         c[k] = make_float4(v[0], v[1], v[2], v[3]);
                     }
                 } else {
-                    // silu_mul in batches of 8: the eight quotients are
-                    // independent straight-line chains and interleave; the rare
-                    // ones the fast form cannot confirm take the general form
+                    // silu_mul in batches of 4: the four quotients are
+                    // independent straight-line chains and interleave (batches of
+                    // 8 ran slower: more registers live beside the 64
+                    // accumulators); the rare ones the fast form cannot confirm
+                    // take the general form, behind a warp vote so that the common
+                    // case never issues it.  Rows past the tile's end hold stale
+                    // sums: they take g = 1 so that they never reach the slow
+                    // division
 #pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        // rows past the tile's end hold stale sums: they take
-                        // g = 1 so that they never reach the slow division
-                        float gs[8], q[8], v[8];
-                        bool ok[8];
+                    for (int i = 0; i < 32; i += 4) {
+                        float gs[4], q[4], v[4];
+                        bool ok[4];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) gs[j] = valid ? acc(i + j) : 1.f;
+                        for (int j = 0; j < 4; ++j) gs[j] = valid ? acc(i + j) : 1.f;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) q[j] = silu_quotient_fast(gs[j], ok[j]);
+                        for (int j = 0; j < 4; ++j) q[j] = silu_quotient_fast(gs[j], ok[j]);
+                        bool all_ok = true;
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if (!ok[j]) q[j] = __fdiv_rn(gs[j], __fadd_rn(1.f, portable_exp(-gs[j])));
+                        for (int j = 0; j < 4; ++j) all_ok &= ok[j];
+                        if (!__all_sync(0xffffffffu, all_ok)) {
+#pragma unroll 1
+                            for (int j = 0; j < 4; ++j)
+                                if (!ok[j]) q[j] = __fdiv_rn(gs[j], __fadd_rn(1.f, portable_exp(-gs[j])));
+                        }
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
+                        for (int j = 0; j < 4; ++j) {
                             const float gv = acc(i + j), uv = acc(32 + i + j);
                             if (valid && (!isfinite(gv) || !isfinite(uv))) f |= kFlagNonfiniteProjection;
                             v[j] = __fmul_rn(q[j], uv);
                             if (valid && !isfinite(v[j])) f |= kFlagNonfiniteMiddle;
                         }
                         c[i / 4] = make_float4(v[0], v[1], v[2], v[3]);
-                        c[i / 4 + 1] = make_float4(v[4], v[5], v[6], v[7]);
                     }
                 }
                 if (ew == 0 && lane == 0) PREFILL_TRACE(9, 3 + 4 * un);
