@@ -259,6 +259,10 @@ __device__ __forceinline__ void quantize_group_warp(const float (&t)[8], int lan
     // rounded to fp16, or 2^-14 above it).  So y and RN(v/sf) round to the
     // same integer unless y lies within 2^-15 of a half-integer; only then is
     // the quotient computed with the IEEE division.
+    // The reference clamps q to [-QMAX, QMAX]; no clamp is needed here: sf is
+    // absmax / QMAX rounded to fp16 (relative error <= 2^-11) or 2^-14 above
+    // it, so |v / sf| <= QMAX * (1 + 2^-11) + 2^-16 < QMAX + 1/2 and every
+    // quotient rounds to at most QMAX in magnitude.
     const float rcp = __fdiv_rn(1.f, sf);
     int q[8], sum = 0;
 #pragma unroll
@@ -269,14 +273,14 @@ __device__ __forceinline__ void quantize_group_warp(const float (&t)[8], int lan
             const float k = rintf(y);
             qi = __fsub_rn(0.5f, fabsf(__fsub_rn(y, k))) > 0x1p-15f ? int(k) : __float2int_rn(__fdiv_rn(v[s], sf));
         }
-        qi = qi < -QMAX ? -QMAX : (qi > QMAX ? QMAX : qi);
         q[s] = qi;
         sum += qi;
     }
-    uint32_t even = (uint32_t(q[0]) & 0xffu) | ((uint32_t(q[2]) & 0xffu) << 8) |
-                    ((uint32_t(q[4]) & 0xffu) << 16) | ((uint32_t(q[6]) & 0xffu) << 24);
-    uint32_t odd = (uint32_t(q[1]) & 0xffu) | ((uint32_t(q[3]) & 0xffu) << 8) |
-                   ((uint32_t(q[5]) & 0xffu) << 16) | ((uint32_t(q[7]) & 0xffu) << 24);
+    // low bytes of q0 q2 q4 q6 and of q1 q3 q5 q7, three byte permutes each
+    const uint32_t even = __byte_perm(__byte_perm(uint32_t(q[0]), uint32_t(q[2]), 0x0040),
+                                      __byte_perm(uint32_t(q[4]), uint32_t(q[6]), 0x0040), 0x5410);
+    const uint32_t odd = __byte_perm(__byte_perm(uint32_t(q[1]), uint32_t(q[3]), 0x0040),
+                                     __byte_perm(uint32_t(q[5]), uint32_t(q[7]), 0x0040), 0x5410);
     q_out[lane] = make_uint2(even, odd);
     sum = int(__reduce_add_sync(0xffffffffu, uint32_t(sum)));
     if (lane == 0) {
