@@ -24,7 +24,7 @@ struct Workspace {
     size_t xlogit;                // single-token decode from hidden: router logits as (call number, fp32) words [kD1LogitCopies][256]
     // tensor-core prefill path (only when Tcap > kDecodeMaxT)
     size_t rowpos, slot_tiles, mtiles, n_mtiles;
-    size_t pblock;                // per-block expert counts, then bases [kPlanBlocks][E+1] (x2)
+    size_t pblock;                // per-block expert counts, then bases, both [E+1][kPlanBlocks]
     size_t agate, agate_sa, agate_sum;  // gate activation tiles [MT][8][32 KB] + per-row scale/sum
     size_t adown, adown_sa, adown_sum;  // down activation tiles [MT][2][32 KB]
     size_t bytes;

@@ -655,8 +655,10 @@ __global__ __launch_bounds__(256) void prefill_count_kernel(LayerArgs a, int nbl
     f = __reduce_or_sync(0xffffffffu, f);
     if (f && (threadIdx.x & 31) == 0) atomicOr(a.flags, f);
     __syncthreads();
-    int* bc = ws_at<int32_t>(a, a.L.pblock) + size_t(blockIdx.x) * (kE + 1);
-    for (int e = threadIdx.x; e <= kE; e += blockDim.x) bc[e] = hist[e];
+    // expert-major [E + 1][kPlanBlocks], so that the scan reads each expert's
+    // block counts as one contiguous run
+    int* bc = ws_at<int32_t>(a, a.L.pblock) + blockIdx.x;
+    for (int e = threadIdx.x; e <= kE; e += blockDim.x) bc[size_t(e) * kPlanBlocks] = hist[e];
 }
 
 __global__ __launch_bounds__(1024) void prefill_scan_kernel(LayerArgs a, int nblk) {
@@ -671,10 +673,14 @@ __global__ __launch_bounds__(1024) void prefill_scan_kernel(LayerArgs a, int nbl
     static_assert(kPlanBlocks == 256, "eight blocks per lane");
     for (int ex = w; ex < kE; ex += 32) {
         int v[8], run = 0;
+        {
+            // blocks 8l..8l+7 of expert ex: two 16-byte loads (entries past
+            // nblk were not written by this call and count as zero)
+            const int4* src = reinterpret_cast<const int4*>(bc + size_t(ex) * kPlanBlocks + 8 * lane);
+            const int4 lo = src[0], hi = src[1];
+            const int raw[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int blk = 8 * lane + k;
-            v[k] = blk < nblk ? bc[size_t(blk) * (kE + 1) + ex] : 0;
+            for (int k = 0; k < 8; ++k) v[k] = 8 * lane + k < nblk ? raw[k] : 0;
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -689,11 +695,11 @@ __global__ __launch_bounds__(1024) void prefill_scan_kernel(LayerArgs a, int nbl
             if (lane >= d) incl += u;
         }
         const int base = incl - run;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int blk = 8 * lane + k;
-            if (blk < nblk) bb[size_t(blk) * (kE + 1) + ex] = base + v[k];
-        }
+        // expert-major as well: each lane's eight bases are one 32-byte run
+        // (entries past nblk are written too and never read)
+        int4* dst = reinterpret_cast<int4*>(bb + size_t(ex) * kPlanBlocks + 8 * lane);
+        dst[0] = make_int4(base + v[0], base + v[1], base + v[2], base + v[3]);
+        dst[1] = make_int4(base + v[4], base + v[5], base + v[6], base + v[7]);
         if (lane == 31) total[ex] = incl;
     }
     __syncthreads();
@@ -752,8 +758,8 @@ __global__ __launch_bounds__(256) void prefill_place_kernel(LayerArgs a, int nbl
     const int R = a.T * kTop, chunk = plan_chunk(R, nblk);
     const int r0 = blockIdx.x * chunk, r1 = min(R, r0 + chunk);
     const int32_t* g_offsets = ws_at<int32_t>(a, a.L.offsets);
-    const int* bb = ws_at<int32_t>(a, a.L.pblock) + size_t(kPlanBlocks) * (kE + 1) + size_t(blockIdx.x) * (kE + 1);
-    for (int e = threadIdx.x; e < kE; e += blockDim.x) base[e] = g_offsets[e] + bb[e];
+    const int* bb = ws_at<int32_t>(a, a.L.pblock) + size_t(kPlanBlocks) * (kE + 1) + blockIdx.x;
+    for (int e = threadIdx.x; e < kE; e += blockDim.x) base[e] = g_offsets[e] + bb[size_t(e) * kPlanBlocks];
     __syncthreads();
     int32_t* routes = ws_at<int32_t>(a, a.L.routes);
     int32_t* rowpos = ws_at<int32_t>(a, a.L.rowpos);
