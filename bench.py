@@ -43,12 +43,12 @@ import __graft_entry__ as graft  # noqa: E402
 METRIC = 'MoE-layer tokens/s & % of HBM/tensor roofline (decode B=1/32, 8K prefill)'
 EXPERT_BYTES = 1_622_016          # w13 codes 1,048,576 + meta 32,768 + w2 codes 524,288 + meta 16,384
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu
-# capture of the same workload (profiles/decode_layer_kernel_decode1.md,
+# capture of the same workload (profiles/decode_single_kernel_decode1.md,
 # profiles/decode_layer_kernel_decode32.md, profiles/prefill_mma_kernel_prefill8192.md).
 NCU_TRAFFIC = {
-    'decode1': {'kernel': 'decode_layer_kernel<127>', 'bytes': 14_737_152},
+    'decode1': {'kernel': 'decode_single_kernel<127>', 'bytes': 14_712_832},
     'decode32': {'kernel': 'decode_layer_kernel<127>', 'bytes': 214_940_160 + 5_720_320},
-    'prefill8192': {'kernel': 'mma_kernel<8,1> (gate/up)', 'bytes': 454_199_552 + 119_388_928},
+    'prefill8192': {'kernel': 'mma_kernel<8,1> (gate/up)', 'bytes': 448_872_704 + 113_913_600},
     # profiles/dense_fused_kernel_dense_qkvz1.md, profiles/head_project_kernel_head_vocab1.md
     'dense_qkvz1': {'kernel': 'dense_fused_kernel<16>', 'bytes': 13_006_336 + 0},
     'head_vocab1': {'kernel': 'head_project_kernel<0>', 'bytes': 516_537_856 + 3_437_824},
