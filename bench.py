@@ -61,6 +61,10 @@ SUB_CONFIGS = {'decode1': ['decode32', 'prefill1120', 'prefill8192']}
 CONFIGS = {
     'decode1': dict(T=1, layers=40, bias=0.0, act_bits=8, shared=True, name='decode B=1, 40-layer stack (configs[1])'),
     'decode32': dict(T=32, layers=40, bias=0.5, act_bits=8, shared=True, name='decode B=32, 40-layer stack (configs[2])'),
+    # decode B=1 through the from-hidden entry: the router linear (bf16 [256, 2048]
+    # per layer) inside the operator, a fresh token row per step
+    'decode1_hidden': dict(T=1, layers=40, bias=0.0, act_bits=8, shared=True, entry='hidden',
+                           name='decode B=1 from hidden states (router linear in the operator), 40-layer stack'),
     'prefill1120': dict(T=1120, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 1120 (configs[3])'),
     'prefill8192': dict(T=8192, layers=40, bias=0.0, act_bits=4, shared=False, name='prefill chunk 8192 (configs[3])'),
     # expert-parallel sweep: total tokens fixed, experts sharded over the ranks
@@ -416,7 +420,7 @@ def run_ep(args):
                    'single_gpu_line_differs': 'the plain-process line (BASELINE run) is decode B=1; '
                                              'this expert-parallel workload is what torchrun runs at every N'},
         'e2e': {'value': round(T_total * args.steps / (e2e_ms / 1e3), 3), 'unit': 'tokens/s',
-                'h2d_bytes_per_step': T * 4096 + L * T * 1024, 'd2h_bytes_per_step': T * 4096,
+                'h2d_bytes_per_step': T * 4096 + (0 if hidden else L * T * 1024), 'd2h_bytes_per_step': T * 4096,
                 'per': 'rank (every rank copies its own rows; time = max over ranks)'},
         'gpu_launches': int(launches), 'roofline': roofline,
         'flags_max': flags_max, 'clocks': clk.summary(), 'cuda_graph': graph is not None,
@@ -767,6 +771,16 @@ def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense
     if bias is not None:
         logits += bias[None, :, None, :]
     x0 = torch.randn((T, 2048), device=dev, generator=stack.gen).to(torch.bfloat16)
+    hidden = cfg.get('entry') == 'hidden'
+    if hidden:
+        # the router computes the logits from a fresh token row every step
+        routers = [(0.02 * torch.randn((256, 2048), device=dev, generator=stack.gen)).to(torch.bfloat16)
+                   for _ in range(L)]
+        x_sets = torch.randn((n_logit_sets, T, 2048), device=dev, generator=stack.gen).to(torch.bfloat16)
+        logits_out = torch.empty((L, T, 256), device=dev)
+        logits = torch.stack([torch.stack([x_sets[s].float() @ routers[l].float().t() for l in range(L)])
+                              for s in range(n_logit_sets)])
+        x0 = x_sets[0]
     ws = torch.empty(native.workspace_bytes(T), dtype=torch.uint8, device=dev)
     outs = [torch.empty((T, 2048), dtype=torch.bfloat16, device=dev) for _ in range(2)]
     shared_out = torch.empty((T, 2048), dtype=torch.bfloat16, device=dev) if cfg['shared'] else None
@@ -775,7 +789,10 @@ def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense
 
     def layer_call(l, x, lg, out):
         (gc, gm), (dc, dm), (sgc, sgm), (sdc, sdm), gw = stack.layers[l % L_stack]
-        if cfg['shared']:
+        if hidden:
+            native.routed_from_hidden(x, routers[l], logits_out[l], gc, gm, dc, dm, sgc, sgm, sdc, sdm, gw,
+                                      stack.silu, stack.sigmoid, ws, out, shared_out, flags[l:l + 1], T, bits)
+        elif cfg['shared']:
             native.routed_from_logits(x, lg, gc, gm, dc, dm, sgc, sgm, sdc, sdm, gw, stack.silu, stack.sigmoid,
                                       ws, out, shared_out, flags[l:l + 1], T, bits)
         else:
@@ -783,14 +800,17 @@ def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense
                                       ws, out, None, flags[l:l + 1], T, bits)
 
     static_logits = logits[0].clone()
-    x_static = x0
+    x_static = x0.clone() if hidden else x0
 
     def step_static():
         for l in range(L):
             layer_call(l, x_static, static_logits[l], outs[l % 2])
 
     def stage_inputs(s):
-        static_logits.copy_(logits[s % n_logit_sets], non_blocking=True)
+        if hidden:
+            x_static.copy_(x_sets[s % n_logit_sets], non_blocking=True)
+        else:
+            static_logits.copy_(logits[s % n_logit_sets], non_blocking=True)
 
     # algorithmic bytes per step: (distinct experts + 1) * EXPERT_BYTES per layer + activations
     ids = torch.topk(logits, 8, dim=-1).indices  # [sets, L, T, 8]
@@ -801,7 +821,7 @@ def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense
             d += int(torch.unique(ids[s, l]).numel()) + (1 if cfg['shared'] else 0)
         distinct.append(d)
     del ids
-    act_bytes = L * (2 * T * 4096 + T * 1024)
+    act_bytes = L * (2 * T * 4096 + T * 1024) + (L * 256 * 2048 * 2 if hidden else 0)  # + router weights
 
     def step_bytes(s):
         return distinct[s % n_logit_sets] * EXPERT_BYTES + act_bytes
@@ -881,20 +901,23 @@ def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense
 
     # end to end through the public operator: pinned host inputs copied in, the
     # step (graph of the operator's launches) run, the last output copied out
-    pin_x = x0.cpu().pin_memory()
+    pin_x = (x_sets[: min(n_logit_sets, 4)] if hidden else x0).cpu().pin_memory()
     pin_logits = logits[: min(n_logit_sets, 4)].cpu().pin_memory()
     pin_out = torch.empty((T, 2048), dtype=torch.bfloat16).pin_memory()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     replay = graph.replay if graph is not None else step_static
-    if args.e2e_overlap:
+    if args.e2e_overlap and not hidden:
         e2e_pipelined(torch, args.steps, pin_x, pin_logits, x_static, static_logits, outs[(L - 1) % 2], pin_out,
                       replay, e0, e1)
     else:
         e0.record()
         for s in range(args.steps):
-            x_static.copy_(pin_x, non_blocking=True)
-            static_logits.copy_(pin_logits[s % pin_logits.shape[0]], non_blocking=True)
+            if hidden:
+                x_static.copy_(pin_x[s % pin_x.shape[0]], non_blocking=True)
+            else:
+                x_static.copy_(pin_x, non_blocking=True)
+                static_logits.copy_(pin_logits[s % pin_logits.shape[0]], non_blocking=True)
             replay()
             pin_out.copy_(outs[(L - 1) % 2], non_blocking=True)
         e1.record()
@@ -909,7 +932,7 @@ def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense
                    'l2': f'inputs larger than L2: {bytes_step / 1e6:.0f} MB of weights read per step'},
         'e2e': {'value': round(T * args.steps / (e2e_ms / 1e3), 3), 'unit': 'tokens/s',
                 'h2d_bytes_per_step': T * 4096 + L * T * 1024, 'd2h_bytes_per_step': T * 4096,
-                'copies': ('pipelined on copy streams, inside the timed region' if args.e2e_overlap
+                'copies': ('pipelined on copy streams, inside the timed region' if args.e2e_overlap and not hidden
                            else 'in line with the steps')},
         'gpu_launches': int(launches),
         'roofline': roofline,
