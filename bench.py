@@ -126,6 +126,9 @@ def parse():
                    help='compact expert-parallel exchange in this many pipelined token chunks (exact combine)')
     p.add_argument('--layers', type=int, default=None,
                    help='override the layer count (small cases for profiler captures)')
+    p.add_argument('--ep-phases', action='store_true',
+                   help='expert-parallel prefill (fixed exchange, partial combine): time each phase of one layer '
+                        'call eagerly with CUDA events (max over ranks) instead of the captured step')
     args = p.parse_args()
     if args.config is None:
         args.config = 'ep_prefill8192' if under_torchrun() else 'decode1'
@@ -219,6 +222,66 @@ class Stack:
         self.gen = gen
 
 
+def ep_phase_times(torch, dist, ep, native, layer, placement, x, logits, w, ids, rflags, world, rank, dev, T, args):
+    """The phases of one fixed-exchange, rank-partial layer call (the steps of
+    ep.ep_layer_fixed_partial), each between CUDA events on the compute
+    stream, eagerly (not captured), averaged over the timed repetitions;
+    rank 0 prints the per-phase maximum over ranks as one JSON line."""
+    if (layer.exchange, layer.combine_mode) != ('fixed', 'partial'):
+        raise SystemExit('--ep-phases times the fixed exchange with the partial combine')
+    H, TOP = 2048, 8
+    native.route_topk(logits, w, ids, rflags)
+    names = ['plan', 'all_gather_tokens', 'all_to_all_ids_weights', 'layer', 'all_to_all_partials', 'rank_sum']
+    acc = np.zeros(len(names))
+    reps = args.warmup + args.steps
+    ids_all = None
+    for it in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+        dist.barrier()
+        torch.cuda.synchronize()
+        ev[0].record()
+        owner, lid = ep.map_ids(ids, placement)
+        dest = torch.arange(world, device=dev).view(-1, 1, 1)
+        mine = owner.unsqueeze(0) == dest
+        local_ids = torch.where(mine, lid.unsqueeze(0), torch.full_like(owner.unsqueeze(0), -1)).to(torch.int32)
+        local_ids = local_ids.contiguous()
+        w_local = torch.where(mine, w.unsqueeze(0), torch.zeros_like(w).unsqueeze(0)).contiguous()
+        ev[1].record()
+        x_all = torch.empty((world * T, H // 2), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(x_all, x.contiguous().view(torch.int32))
+        ev[2].record()
+        ids_all = torch.empty_like(local_ids)
+        dist.all_to_all_single(ids_all, local_ids)
+        w_all = torch.empty_like(w_local)
+        dist.all_to_all_single(w_all, w_local)
+        ev[3].record()
+        part = layer.compute_partial(x_all.view(torch.bfloat16), ids_all.view(world * T, TOP),
+                                     w_all.view(world * T, TOP))
+        ev[4].record()
+        got = torch.empty_like(part)
+        dist.all_to_all_single(got, part.contiguous())
+        ev[5].record()
+        t = torch.arange(T, device=dev, dtype=torch.int32).view(-1, 1)
+        d = torch.arange(TOP, device=dev, dtype=torch.int32).view(1, -1)
+        has = (mine.any(dim=2).t() if world == TOP else
+               torch.cat([mine.any(dim=2).t(), torch.zeros((T, TOP - world), dtype=torch.bool, device=dev)], 1))
+        row_index = torch.where(has, d * T + t, torch.full_like(has, -1, dtype=torch.int32))
+        ep.rank_sum(layer.combine, got.view(world * T, H), row_index.contiguous(), w)
+        ev[6].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            acc += np.array([ev[i].elapsed_time(ev[i + 1]) for i in range(len(names))])
+    acc /= max(1, args.steps)
+    tm = torch.tensor(acc, device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        print(json.dumps({'ep_phases_ms': dict(zip(names, [round(v, 4) for v in tm.tolist()])),
+                          'world': world, 'tokens_total': T * world, 'layer_calls_timed': args.steps,
+                          'how': 'one layer call, eager launches, CUDA events per phase on the compute stream, '
+                                 'mean over the timed calls, max over ranks'}), flush=True)
+
+
 def run_ep(args):
     """Expert-parallel step: the total token count is
     fixed and split over the ranks; every rank routes its tokens (device
@@ -236,8 +299,8 @@ def run_ep(args):
         cfg['exchange'] = args.ep_exchange
     args.combine = args.combine or cfg['combine']
     args.ep_transport = args.ep_transport or cfg['transport']
-    if args.combine == 'partial':
-        args.ep_transport = 'nccl'   # the peer-memory transport carries the exact per-slot rows only
+    if args.combine == 'partial' and cfg['exchange'] != 'fixed':
+        args.ep_transport = 'nccl'   # the rank-partial sums travel over peer memory in the fixed exchange only
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
@@ -286,6 +349,12 @@ def run_ep(args):
         for l in range(L):
             native.route_topk(logits[l], w[l], ids[l], rflags)   # routing is part of the layer
             outs[0] = layers[l](x, ids[l], w[l])
+
+    if args.ep_phases:
+        ep_phase_times(torch, dist, ep, native, layers[0], placement, x, logits[0], w[0], ids[0], rflags, world,
+                       rank, dev, T, args)
+        dist.destroy_process_group()
+        return
 
     # NVLink bytes this rank sends per step: a token row (4,096 B) per (token,
     # remote expert rank), an fp32 result row (8,192 B) per (token, slot) whose
@@ -420,7 +489,7 @@ def run_ep(args):
                    'single_gpu_line_differs': 'the plain-process line (BASELINE run) is decode B=1; '
                                              'this expert-parallel workload is what torchrun runs at every N'},
         'e2e': {'value': round(T_total * args.steps / (e2e_ms / 1e3), 3), 'unit': 'tokens/s',
-                'h2d_bytes_per_step': T * 4096 + (0 if hidden else L * T * 1024), 'd2h_bytes_per_step': T * 4096,
+                'h2d_bytes_per_step': T * 4096 + L * T * 1024, 'd2h_bytes_per_step': T * 4096,
                 'per': 'rank (every rank copies its own rows; time = max over ranks)'},
         'gpu_launches': int(launches), 'roofline': roofline,
         'flags_max': flags_max, 'clocks': clk.summary(), 'cuda_graph': graph is not None,
@@ -931,7 +1000,7 @@ def measure_layer_config(torch, native, lib, stack, cfg, args, dev, peaks, dense
                    'activations': f'A{bits} per 256-group after H128', 'arith': 'u4 x s8 -> int32 dot, fp32 epilogue',
                    'l2': f'inputs larger than L2: {bytes_step / 1e6:.0f} MB of weights read per step'},
         'e2e': {'value': round(T * args.steps / (e2e_ms / 1e3), 3), 'unit': 'tokens/s',
-                'h2d_bytes_per_step': T * 4096 + L * T * 1024, 'd2h_bytes_per_step': T * 4096,
+                'h2d_bytes_per_step': T * 4096 + (0 if hidden else L * T * 1024), 'd2h_bytes_per_step': T * 4096,
                 'copies': ('pipelined on copy streams, inside the timed region' if args.e2e_overlap and not hidden
                            else 'in line with the steps')},
         'gpu_launches': int(launches),

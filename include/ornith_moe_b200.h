@@ -277,6 +277,24 @@ ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_fixed_return(
     const void* workspace, size_t bytes, int T, int Tcap, const void* ids_i32, void* const* dst_rows,
     int64_t dst_capacity_rows, void* const* signals, int world, int me, const void* epoch_u32, void* counter_u32,
     void* flags_u32, cudaStream_t stream);
+/* The fixed exchange with the rank-partial combine.  ep_fixed_dispatch_weights:
+ * ep_fixed_dispatch that also stores local_w[d][t] (fp32 [world][T][8], the
+ * weights of rank d's slots, 0 elsewhere) into rank d's weight buffer
+ * (dst_w, [2][world], each set world*T rows of 8).  ep_fixed_return_partial:
+ * after the layer call on the world*T received rows with those weights, row
+ * h*T + t of the layer's fp32 sums (the workspace's final_f32, this rank's
+ * partial over its slots of token t of home rank h) goes to row me*T + t of
+ * home h's partial buffer (dst_part, [2][world], each set dst_capacity_rows
+ * >= world*T rows of 2048 fp32) when the token has a slot here, then the call
+ * number into the others' return flags. */
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_fixed_dispatch_weights(
+    const void* x_bf16, const void* local_ids_i32, const void* local_w_f32, int T, void* const* dst_x,
+    void* const* dst_ids, void* const* dst_w, int64_t dst_capacity_rows, void* const* signals, int world, int me,
+    void* epoch_u32, void* counter_u32, const void* flags_u32, cudaStream_t stream);
+ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_fixed_return_partial(
+    const void* workspace, size_t bytes, int T, int Tcap, const void* ids_i32, void* const* dst_part,
+    int64_t dst_capacity_rows, void* const* signals, int world, int me, const void* epoch_u32, void* counter_u32,
+    void* flags_u32, cudaStream_t stream);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_wait_epoch(
     const void* signals_u32, int world, int me, const void* epoch_u32, void* flags_u32, cudaStream_t stream);
 ORNITH_MOE_B200_EXPORT cudaError_t ornith_moe_b200_ep_wait_signals(

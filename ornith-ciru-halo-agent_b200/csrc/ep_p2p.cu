@@ -198,9 +198,11 @@ __global__ __launch_bounds__(256) void ep_dispatch_p2p_kernel(const DispatchArgs
 struct FixedArgs {
     const uint16_t* x;                 // this rank's token rows [T][2048]
     const int32_t* local_ids;          // [world][T][8]: ids of this rank's tokens in rank d's numbering
+    const float* local_w;              // [world][T][8]: their weights (rank-partial combine), or null
     int T, world, me;
     uint16_t* dst_x[2][kP2PMaxWorld];  // per set: token rows [world][T][2048] of rank d
     int32_t* dst_ids[2][kP2PMaxWorld]; // per set: ids [world][T][8] of rank d
+    float* dst_w[2][kP2PMaxWorld];     // per set: weights [world][T][8] of rank d (with local_w)
     uint32_t* sig[kP2PMaxWorld];       // dispatch flag array of each rank
     uint32_t* epoch;                   // this rank's call counter
     uint32_t* counter;
@@ -221,6 +223,9 @@ __global__ __launch_bounds__(256) void ep_fixed_dispatch_kernel(const FixedArgs 
         if (threadIdx.x < 2)
             reinterpret_cast<uint4*>(a.dst_ids[set][d] + row * kTop)[threadIdx.x] =
                 __ldg(reinterpret_cast<const uint4*>(a.local_ids + (size_t(d) * a.T + t) * kTop) + threadIdx.x);
+        else if (threadIdx.x < 4 && a.local_w)
+            reinterpret_cast<uint4*>(a.dst_w[set][d] + row * kTop)[threadIdx.x - 2] =
+                __ldg(reinterpret_cast<const uint4*>(a.local_w + (size_t(d) * a.T + t) * kTop) + threadIdx.x - 2);
     }
     __threadfence_system();
     __syncthreads();
@@ -268,6 +273,45 @@ __global__ __launch_bounds__(256) void ep_fixed_return_kernel(const FixedReturnA
         d[1] = v1;
     }
     if (f && threadIdx.x == 0) atomicOr(a.flags, f);
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
+        __threadfence_system();
+        publish_epoch(a.sig, a.world, a.me, call, a.flags);
+        *a.counter = 0u;
+    }
+}
+
+struct FixedPartialArgs {
+    const float* partial;              // the layer call's fp32 sums [world * T][2048] (final_f32)
+    const int32_t* ids;                // [world * T][8] the local ids the layer call used
+    int T, world, me;
+    float* dst_part[2][kP2PMaxWorld];  // per set: partial rows [world][T][2048] of home rank h
+    uint32_t* sig[kP2PMaxWorld];       // return flag array of each rank
+    const uint32_t* epoch;
+    uint32_t* counter;
+    uint32_t* flags;
+};
+
+// Rank-partial return: received row r = h * T + t, if any of its slots has a
+// valid local id here, goes to row me * T + t of home h's partial buffer (its
+// sum over this rank's slots); rows with no slot here are not sent (the home
+// rank reads only the rows of ranks that own one of the token's slots).
+__global__ __launch_bounds__(256) void ep_fixed_return_partial_kernel(const FixedPartialArgs a) {
+    const uint32_t call = *a.epoch;
+    const int set = int(call & 1u);
+    for (int r = blockIdx.x; r < a.T * a.world; r += gridDim.x) {
+        const int4 i0 = __ldg(reinterpret_cast<const int4*>(a.ids + size_t(r) * kTop));
+        const int4 i1 = __ldg(reinterpret_cast<const int4*>(a.ids + size_t(r) * kTop) + 1);
+        const int top = max(max(max(i0.x, i0.y), max(i0.z, i0.w)), max(max(i1.x, i1.y), max(i1.z, i1.w)));
+        if (top < 0) continue;  // no slot of this token here
+        const int h = r / a.T, t = r % a.T;
+        const float4* src = reinterpret_cast<const float4*>(a.partial + size_t(r) * kH) + threadIdx.x * 2;
+        float4* d = reinterpret_cast<float4*>(a.dst_part[set][h] + (size_t(a.me) * a.T + t) * kH) + threadIdx.x * 2;
+        const float4 v0 = __ldcs(src), v1 = __ldcs(src + 1);
+        d[0] = v0;
+        d[1] = v1;
+    }
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(a.counter, 1u) == gridDim.x - 1) {
@@ -460,11 +504,12 @@ extern "C" cudaError_t ornith_moe_b200_ep_dispatch_p2p(const void* x_bf16, int T
     return cudaGetLastError();
 }
 
-extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, const void* local_ids_i32, int T,
-                                                         void* const* dst_x, void* const* dst_ids,
-                                                         int64_t dst_capacity_rows, void* const* signals, int world,
-                                                         int me, void* epoch_u32, void* counter_u32,
-                                                         const void* flags_u32, cudaStream_t stream) {
+namespace {
+cudaError_t fixed_dispatch(const void* x_bf16, const void* local_ids_i32, const void* local_w_f32, int T,
+                           void* const* dst_x, void* const* dst_ids, void* const* dst_w, int64_t dst_capacity_rows,
+                           void* const* signals, int world, int me, void* epoch_u32, void* counter_u32,
+                           const void* flags_u32, cudaStream_t stream) {
+    if (local_w_f32 && (!dst_w || !p2p_aligned(local_w_f32, 16))) return cudaErrorInvalidValue;
     if (T < 1 || T > kTcapMax || world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || !x_bf16 ||
         !local_ids_i32 || !dst_x || !dst_ids || !signals || !epoch_u32 || !counter_u32 || !flags_u32 ||
         !p2p_aligned(x_bf16, 16) || !p2p_aligned(local_ids_i32, 16) || !p2p_aligned(epoch_u32, 4) ||
@@ -480,7 +525,13 @@ extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, con
             if (!px || !pi || !p2p_aligned(px, 16) || !p2p_aligned(pi, 16)) return cudaErrorInvalidValue;
             a.dst_x[set][d] = static_cast<uint16_t*>(px);
             a.dst_ids[set][d] = static_cast<int32_t*>(pi);
+            if (local_w_f32) {
+                void* pw = dst_w[set * world + d];
+                if (!pw || !p2p_aligned(pw, 16)) return cudaErrorInvalidValue;
+                a.dst_w[set][d] = static_cast<float*>(pw);
+            }
         }
+    a.local_w = static_cast<const float*>(local_w_f32);
     for (int d = 0; d < world; ++d) {
         if (d != me && (!signals[d] || !p2p_aligned(signals[d], 4))) return cudaErrorInvalidValue;
         a.sig[d] = static_cast<uint32_t*>(signals[d]);
@@ -501,6 +552,71 @@ extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, con
     const int items = T * world;
     count_launches(1);
     ep_fixed_dispatch_kernel<<<items < 2 * sms ? items : 2 * sms, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+}  // namespace
+
+extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch(const void* x_bf16, const void* local_ids_i32, int T,
+                                                         void* const* dst_x, void* const* dst_ids,
+                                                         int64_t dst_capacity_rows, void* const* signals, int world,
+                                                         int me, void* epoch_u32, void* counter_u32,
+                                                         const void* flags_u32, cudaStream_t stream) {
+    return fixed_dispatch(x_bf16, local_ids_i32, nullptr, T, dst_x, dst_ids, nullptr, dst_capacity_rows, signals,
+                          world, me, epoch_u32, counter_u32, flags_u32, stream);
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_fixed_dispatch_weights(
+    const void* x_bf16, const void* local_ids_i32, const void* local_w_f32, int T, void* const* dst_x,
+    void* const* dst_ids, void* const* dst_w, int64_t dst_capacity_rows, void* const* signals, int world, int me,
+    void* epoch_u32, void* counter_u32, const void* flags_u32, cudaStream_t stream) {
+    if (!local_w_f32) return cudaErrorInvalidValue;
+    return fixed_dispatch(x_bf16, local_ids_i32, local_w_f32, T, dst_x, dst_ids, dst_w, dst_capacity_rows, signals,
+                          world, me, epoch_u32, counter_u32, flags_u32, stream);
+}
+
+extern "C" cudaError_t ornith_moe_b200_ep_fixed_return_partial(const void* workspace, size_t bytes, int T,
+                                                               int Tcap, const void* ids_i32, void* const* dst_part,
+                                                               int64_t dst_capacity_rows, void* const* signals,
+                                                               int world, int me, const void* epoch_u32,
+                                                               void* counter_u32, void* flags, cudaStream_t stream) {
+    // T: tokens per rank; the layer call ran on world * T rows with capacity Tcap
+    if (T < 1 || world < 1 || world > kP2PMaxWorld || me < 0 || me >= world || Tcap < 0 || Tcap > kTcapMax ||
+        T * world > Tcap)
+        return cudaErrorInvalidValue;
+    // every set of every home rank's partial buffer holds world*T rows
+    if (dst_capacity_rows < int64_t(T) * world) return cudaErrorInvalidValue;
+    const Workspace w = workspace_layout(Tcap);
+    if (bytes < w.bytes || !workspace || !ids_i32 || !dst_part || !signals || !epoch_u32 || !counter_u32 ||
+        !flags || !p2p_aligned(workspace, 256) || !p2p_aligned(ids_i32, 16) || !p2p_aligned(epoch_u32, 4) ||
+        !p2p_aligned(counter_u32, 4) || !p2p_aligned(flags, 4))
+        return cudaErrorInvalidValue;
+    FixedPartialArgs a{};
+    for (int set = 0; set < 2; ++set)
+        for (int h = 0; h < world; ++h) {
+            void* p = dst_part[set * world + h];
+            if (!p || !p2p_aligned(p, 16)) return cudaErrorInvalidValue;
+            a.dst_part[set][h] = static_cast<float*>(p);
+        }
+    for (int h = 0; h < world; ++h) {
+        if (h != me && (!signals[h] || !p2p_aligned(signals[h], 4))) return cudaErrorInvalidValue;
+        a.sig[h] = static_cast<uint32_t*>(signals[h]);
+    }
+    a.partial = reinterpret_cast<const float*>(static_cast<const uint8_t*>(workspace) + w.final_f32);
+    a.ids = static_cast<const int32_t*>(ids_i32);
+    a.T = T;
+    a.world = world;
+    a.me = me;
+    a.epoch = static_cast<const uint32_t*>(epoch_u32);
+    a.counter = static_cast<uint32_t*>(counter_u32);
+    a.flags = static_cast<uint32_t*>(flags);
+    NvtxRange range("ornith.ep.fixed_return_partial");
+    int device = 0, sms = 0;
+    cudaError_t st = cudaGetDevice(&device);
+    if (st != cudaSuccess) return st;
+    if ((st = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess) return st;
+    const int items = T * world;
+    count_launches(1);
+    ep_fixed_return_partial_kernel<<<items < 2 * sms ? items : 2 * sms, 256, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -568,18 +568,24 @@ class PeerFixedExchange:
     host value that changes between calls and can be captured in a CUDA
     graph.  Made and closed collectively, like PeerExchange."""
 
-    def __init__(self, group, world, me, T, device):
+    def __init__(self, group, world, me, T, device, partial=False):
         from . import native
         if not 1 <= world <= 8:
             raise ValueError('the peer-memory exchange serves 1..8 ranks of one node')
         self.native, self.group, self.world, self.me, self.T = native, group, world, me, int(T)
-        rows_in, rows_out = world * self.T, self.T * TOP
+        self.partial = bool(partial)
+        rows_in = world * self.T
+        # result rows: the T*8 slot rows of this rank's tokens, or (rank-partial
+        # combine) one fp32 sum per (rank, token): world*T rows
+        rows_out = rows_in if self.partial else self.T * TOP
+        self.rows_out = rows_out
 
         def up(n):
             return (n + 255) // 256 * 256
         self.x_offset, self.x_set = 0, up(rows_in * H * 2)
         self.ids_offset, self.ids_set = 2 * self.x_set, up(rows_in * TOP * 4)
-        self.rows_offset, self.rows_set = self.ids_offset + 2 * self.ids_set, rows_out * H * 4
+        self.w_offset, self.w_set = self.ids_offset + 2 * self.ids_set, (up(rows_in * TOP * 4) if self.partial else 0)
+        self.rows_offset, self.rows_set = self.w_offset + 2 * self.w_set, up(rows_out * H * 4)
         self.flag_offset = up(self.rows_offset + 2 * self.rows_set)
         self.base = native.ep_buffer_alloc(self.flag_offset + 256)
         self.peers = {}
@@ -597,6 +603,7 @@ class PeerFixedExchange:
         def sets(offset, stride):
             return (C.c_void_p * (2 * world))(*[b + offset + k * stride for k in range(2) for b in bases])
         self.dst_x, self.dst_ids = sets(self.x_offset, self.x_set), sets(self.ids_offset, self.ids_set)
+        self.dst_w = sets(self.w_offset, self.w_set) if self.partial else None
         self.dst_rows = sets(self.rows_offset, self.rows_set)
         self.dispatch_flags = (C.c_void_p * world)(*[b + self.flag_offset for b in bases])
         self.return_flags = (C.c_void_p * world)(*[b + self.flag_offset + 8 * world for b in bases])
@@ -606,10 +613,12 @@ class PeerFixedExchange:
         # device-side index picks a set without touching the other
         self.x2 = view(self.x_offset, (2, rows_in, H), '<i2', (self.x_set, H * 2, 2)).view(torch.bfloat16)
         self.ids2 = view(self.ids_offset, (2, rows_in, TOP), '<i4', (self.ids_set, TOP * 4, 4))
-        self.rows = view(self.rows_offset, (2 * rows_out, H), '<f4')   # both result sets, one array
+        self.w2 = view(self.w_offset, (2, rows_in, TOP), '<f4', (self.w_set, TOP * 4, 4)) if self.partial else None
+        # both result sets as one array of rows (the set stride is whole rows)
+        self.rows = view(self.rows_offset, (2 * self.rows_set // (H * 4), H), '<f4')
         self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
         self.counters = torch.zeros(2, dtype=torch.int32, device=device)
-        self._slot_rows = torch.arange(rows_out, dtype=torch.int32, device=device).view(self.T, TOP)
+        self._slot_rows = torch.arange(self.T * TOP, dtype=torch.int32, device=device).view(self.T, TOP)
 
     def parity(self):
         """0 or 1: the set of the current call, as a device tensor."""
@@ -618,6 +627,37 @@ class PeerFixedExchange:
     def dispatch(self, x, local_ids_per_rank, flags):
         self.native.ep_fixed_dispatch(x, local_ids_per_rank, self.dst_x, self.dst_ids, self.world * self.T,
                                       self.dispatch_flags, self.world, self.me, self.epoch, self.counters[0:1], flags)
+
+    def dispatch_w(self, x, local_ids_per_rank, local_w_per_rank, flags):
+        self.native.ep_fixed_dispatch_weights(x, local_ids_per_rank, local_w_per_rank, self.dst_x, self.dst_ids,
+                                              self.dst_w, self.world * self.T, self.dispatch_flags, self.world,
+                                              self.me, self.epoch, self.counters[0:1], flags)
+
+    def received_w(self):
+        """received() plus the slot weights fp32 [world*T, 8] of this call's set."""
+        x, ids = self.received()
+        w = torch.index_select(self.w2, 0, self.parity())[0]
+        return x, ids, w.contiguous()
+
+    def ret_partial(self, workspace, capacity, ids_all, flags):
+        self.native.ep_fixed_return_partial(workspace, self.T, capacity, ids_all, self.dst_rows, self.rows_out,
+                                            self.return_flags, self.world, self.me, self.epoch,
+                                            self.counters[1:2], flags)
+
+    def partial_index(self, mine):
+        """int32 [T, 8] for the rank sum: column d holds the row of self.rows
+        with rank d's sum for token t in this call's set, -1 where rank d owns
+        none of the token's slots (and for columns d >= world).  mine: bool
+        [world, T, 8], slot s of token t belongs to rank d."""
+        T = self.T
+        has = mine.any(dim=2).t()                                                   # [T, world]
+        t = torch.arange(T, device=mine.device, dtype=torch.int32).view(-1, 1)
+        d = torch.arange(self.world, device=mine.device, dtype=torch.int32).view(1, -1)
+        base = (self.parity() * (self.rows_set // (H * 4))).to(torch.int32)
+        idx = torch.where(has, base + d * T + t, torch.full_like(t.expand(T, self.world), -1))
+        if self.world < TOP:
+            idx = torch.cat([idx, torch.full((T, TOP - self.world), -1, dtype=torch.int32, device=mine.device)], 1)
+        return idx.contiguous()
 
     def wait_dispatch(self, flags):
         self.native.ep_wait_epoch(self.base + self.flag_offset, self.world, self.me, self.epoch, flags)
@@ -648,7 +688,7 @@ class PeerFixedExchange:
 
     def close(self):
         """Collective, like PeerExchange.close; the views go first."""
-        self.x2 = self.ids2 = None
+        self.x2 = self.ids2 = self.w2 = self.rows = None
         PeerExchange.close(self)
 
 
@@ -683,8 +723,9 @@ class ExpertParallelMoE:
         if not isinstance(chunks, int) or chunks < 1 or (chunks > 1 and (exchange, combine) != ('compact', 'exact')):
             raise ValueError('chunks > 1 applies to the compact exchange with the exact combine')
         if transport not in ('nccl', 'p2p') or (transport == 'p2p' and (
-                (combine, chunks) != ('exact', 1) or not 1 <= world <= 8)):
-            raise ValueError("transport 'p2p' applies to the exact combine with one chunk, on 1..8 ranks of one node")
+                chunks != 1 or not 1 <= world <= 8 or (combine == 'partial' and exchange != 'fixed'))):
+            raise ValueError("transport 'p2p' applies to one chunk on 1..8 ranks of one node, and with the "
+                             "rank-partial combine to the fixed exchange")
         self.transport = transport
         self.chunks = chunks
         self.combine_mode = combine
@@ -792,6 +833,36 @@ class ExpertParallelMoE:
         pf.wait_return(self.flags)
         return self.combine(pf.rows, pf.result_index(ids), weights, ids)
 
+    def _layer_fixed_p2p_partial(self, x, ids, weights):
+        """Fixed exchange over NVLink peer memory with the rank-partial
+        combine: every rank's token rows, local ids and slot weights go to
+        every rank (one dispatch kernel); each rank's fp32 sums over its own
+        slots go straight to the tokens' home ranks (one return kernel, rows of
+        tokens with no slot there left out); the home rank adds the ranks'
+        sums in rank order.  No collective and no host value that changes
+        between calls, so the step can be captured in a CUDA graph.  Every call
+        must have the token count of the first."""
+        T = x.shape[0]
+        if self.peer_fixed is None:
+            self.peer_fixed = PeerFixedExchange(self.group, self.world, self.me, T, x.device, partial=True)
+        elif self.peer_fixed.T != T:
+            raise ValueError(f'the fixed peer-memory exchange was made for {self.peer_fixed.T} tokens, got {T}')
+        if self.world * T > self.capacity:
+            raise ValueError(f'expert-parallel receive of {self.world * T} rows exceeds capacity {self.capacity}')
+        owner, lid = map_ids(ids, self.placement)
+        dest = torch.arange(self.world, device=ids.device, dtype=owner.dtype).view(-1, 1, 1)
+        mine = owner.unsqueeze(0) == dest                                                  # [world, T, 8]
+        local = torch.where(mine, lid.unsqueeze(0), torch.full_like(lid, -1).unsqueeze(0)).to(torch.int32)
+        w_local = torch.where(mine, weights.unsqueeze(0), torch.zeros_like(weights).unsqueeze(0))
+        pf = self.peer_fixed
+        pf.dispatch_w(x.contiguous(), local.contiguous(), w_local.contiguous(), self.flags)
+        pf.wait_dispatch(self.flags)
+        x_all, ids_all, w_all = pf.received_w()
+        self._layer(x_all, ids_all, w_all)
+        pf.ret_partial(self.workspace, self.capacity, ids_all, self.flags)
+        pf.wait_return(self.flags)
+        return rank_sum(self.combine, pf.rows, pf.partial_index(mine), weights)
+
     def close(self):
         """Release the peer-memory buffers (collective; before the process
         group is destroyed)."""
@@ -823,6 +894,8 @@ class ExpertParallelMoE:
             # the partial rows reach the combine without the ids: ids outside
             # -1..255 (flag 4 on one GPU) are flagged here, on the device
             self.flags.bitwise_or_(((ids >= E) | (ids < -1)).any().to(self.flags.dtype) * 4)
+            if self.exchange == 'fixed' and self.transport == 'p2p':
+                return self._layer_fixed_p2p_partial(x, ids, weights)
             if self.exchange == 'fixed':
                 return ep_layer_fixed_partial(self.group, self.world, x, ids, weights, self.compute_partial,
                                               self.combine, self.placement)

@@ -104,6 +104,13 @@ SIGNATURES = {
     'ornith_moe_b200_ep_fixed_return': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p]
                                         + [C.POINTER(C.c_void_p), C.c_int64, C.POINTER(C.c_void_p)]
                                         + [C.c_int, C.c_int] + [C.c_void_p] * 4, C.c_int),
+    'ornith_moe_b200_ep_fixed_dispatch_weights': ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+                                                  + [C.POINTER(C.c_void_p)] * 3
+                                                  + [C.c_int64, C.POINTER(C.c_void_p)]
+                                                  + [C.c_int, C.c_int] + [C.c_void_p] * 4, C.c_int),
+    'ornith_moe_b200_ep_fixed_return_partial': ([C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p]
+                                                + [C.POINTER(C.c_void_p), C.c_int64, C.POINTER(C.c_void_p)]
+                                                + [C.c_int, C.c_int] + [C.c_void_p] * 4, C.c_int),
     'ornith_moe_b200_set_peer_wait_limit_ns': ([C.c_uint64], C.c_int),
     'ornith_moe_b200_peer_wait_limit_ns': ([], C.c_uint64),
     'ornith_moe_b200_ep_wait_epoch': ([C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
@@ -519,6 +526,36 @@ def ep_fixed_return(workspace, T, capacity, ids, dst_rows, cap_rows, signals, wo
     check(lib().ornith_moe_b200_ep_fixed_return(ptr(workspace), workspace.numel(), T, capacity, ptr(ids), dst_rows,
                                                 cap_rows, signals, world, me, ptr(epoch), ptr(counter), ptr(flags),
                                                 stream(ids)), 'expert-parallel fixed return')
+
+
+def ep_fixed_dispatch_weights(x, local_ids, local_w, dst_x, dst_ids, dst_w, cap_rows, signals, world, me, epoch,
+                              counter, flags):
+    """ep_fixed_dispatch that also carries local_w fp32 [world, T, 8] (the
+    weights of each rank's slots, 0 elsewhere) into dst_w, for the
+    rank-partial combine."""
+    T = x.shape[0]
+    if (x.dtype != torch.bfloat16 or x.shape != (T, 2048) or not x.is_contiguous() or local_ids.dtype != torch.int32
+            or local_ids.shape != (world, T, 8) or not local_ids.is_contiguous() or local_w.dtype != torch.float32
+            or local_w.shape != (world, T, 8) or not local_w.is_contiguous()):
+        raise ValueError('ep_fixed_dispatch_weights takes bf16 rows [T, 2048], INT32 ids and FP32 weights '
+                         '[world, T, 8]')
+    check(lib().ornith_moe_b200_ep_fixed_dispatch_weights(ptr(x), ptr(local_ids), ptr(local_w), T, dst_x, dst_ids,
+                                                          dst_w, cap_rows, signals, world, me, ptr(epoch),
+                                                          ptr(counter), ptr(flags), stream(x)),
+          'expert-parallel fixed dispatch with weights')
+
+
+def ep_fixed_return_partial(workspace, T, capacity, ids, dst_part, cap_rows, signals, world, me, epoch, counter,
+                            flags):
+    """Rank-partial return over peer memory after a layer call on ids int32
+    [world * T, 8]: each token's fp32 sum over this rank's slots goes to its
+    home rank's partial buffer (every set of dst_part holds cap_rows rows)."""
+    if ids.dtype != torch.int32 or ids.shape != (world * T, 8) or not ids.is_contiguous():
+        raise ValueError('ep_fixed_return_partial takes the INT32 local ids [world * T, 8] of the layer call')
+    check(lib().ornith_moe_b200_ep_fixed_return_partial(ptr(workspace), workspace.numel(), T, capacity, ptr(ids),
+                                                        dst_part, cap_rows, signals, world, me, ptr(epoch),
+                                                        ptr(counter), ptr(flags), stream(ids)),
+          'expert-parallel fixed partial return')
 
 
 def set_peer_wait_limit_ns(limit_ns):

@@ -37,6 +37,7 @@ CASES = [  # (exchange, balanced placement, combine, further ExpertParallelMoE o
     ('compact', True, 'exact', {'chunks': 3}),
     ('compact', False, 'exact', {'transport': 'p2p'}), ('compact', True, 'exact', {'transport': 'p2p'}),
     ('fixed', False, 'exact', {'transport': 'p2p'}), ('fixed', True, 'exact', {'transport': 'p2p'}),
+    ('fixed', True, 'partial', {'transport': 'p2p'}),   # bit-identical to the NCCL form of the same mode
 ]
 
 
@@ -81,6 +82,7 @@ def _worker(rank, world, port, T, q):
             *[native.ptr(t) for t in (x, w, ids, gc, gm, dc, dm, ws)], ws.numel(), native.ptr(ref),
             native.ptr(flags), T, T, native.stream(x)), 'reference layer')
         results = []
+        partial_outputs = {}   # (mode, balanced) -> output of the NCCL rank-partial form
         for mode, balanced, combine, options in CASES:
             if balanced:  # any placement must give the same result; use a skewed-load one
                 placement = ep.balanced_placement(torch.arange(256, dtype=torch.float64).flip(0) ** 2, world, dev)
@@ -99,6 +101,12 @@ def _worker(rank, world, port, T, q):
                 torch.cuda.synchronize()
                 ok = ok and (bool(torch.equal(out.view(torch.int16), ref.view(torch.int16))) if combine == 'exact'
                              else _close(out, ref))
+                if combine == 'partial' and mode == 'fixed':
+                    if options.get('transport') == 'p2p':   # the same sums, added in the same rank order
+                        nccl = partial_outputs.get((mode, balanced))
+                        ok = ok and nccl is not None and bool(torch.equal(out.view(torch.int16), nccl.view(torch.int16)))
+                    else:
+                        partial_outputs[(mode, balanced)] = out.clone()
             results.append(((mode, balanced, combine, tuple(options.items())), ok, int(layer.flags.item())))
             layer.close()
             dist.barrier()
