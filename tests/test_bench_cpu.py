@@ -1,6 +1,7 @@
 """CPU: the benchmark's reference arm (the reference's own source compiled for
 the CPU) prints one JSON line with the keys the benchmark contract names, and
-ranks other than 0 exit quietly."""
+ranks other than 0 exit quietly; the benchmark's and the package's GPU-only
+code reads no unbound name."""
 import json
 import os
 import subprocess
@@ -56,3 +57,37 @@ def test_default_workload_follows_the_launcher():
                                {'TORCHELASTIC_RUN_ID': 'test', 'LOCAL_WORLD_SIZE': '1', 'RANK': '0',
                                 'WORLD_SIZE': '1'})[0])
     assert launched['config']['workload'] == bench.CONFIGS['ep_prefill8192']['name']
+
+
+def _unbound_names(path):
+    """Names read inside the functions of a module that no scope binds: not a
+    parameter or local of the function or of an enclosing one, not a module
+    global, not a builtin.  The GPU-only legs of the benchmark (the
+    expert-parallel and layer measurements) never run on the CPU, so a
+    misspelt or misplaced name there would surface only on a GPU box."""
+    import builtins
+    import symtable
+    top = symtable.symtable(Path(path).read_text(), str(path), 'exec')
+    module_names = set(top.get_identifiers())
+    missing = []
+
+    def walk(table, enclosing):
+        bound = set(enclosing)
+        if table.get_type() == 'function':
+            bound |= {s.get_name() for s in table.get_symbols() if s.is_assigned() or s.is_parameter()
+                      or s.is_imported() or s.is_local()}
+            for s in table.get_symbols():
+                name = s.get_name()
+                if s.is_referenced() and not (name in bound or name in module_names or hasattr(builtins, name)):
+                    missing.append(f'{table.get_name()}:{table.get_lineno()}: {name}')
+        for child in table.get_children():
+            walk(child, bound if table.get_type() == 'function' else set())
+
+    walk(top, set())
+    return missing
+
+
+@pytest.mark.parametrize('path', ['bench.py', '__graft_entry__.py', 'ornith-ciru-halo-agent_b200/ep.py',
+                                  'ornith-ciru-halo-agent_b200/native.py', 'ornith-ciru-halo-agent_b200/method.py'])
+def test_functions_read_only_bound_names(path):
+    assert _unbound_names(ROOT / path) == []
